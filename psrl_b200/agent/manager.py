@@ -1,0 +1,268 @@
+"""Agent-loop manager: the driver-side dispatcher of the asynchronous pipeline (C12).
+
+Responsibilities (reference ``psrl/workers/agent_loop/manager.py``):
+
+1. **Dispatch-ahead bound** — prompt groups are released in order only while
+   ``expected_ps_version <= ps_version`` with
+   ``expected = initial + max(dispatched - min(eta, max_ahead) * buffer_size, 0) // buffer_size``
+   (``_get_expected_ps_version`` :636-652), so rollout never runs more than
+   ``min(eta, max_dispatch_ahead)`` buffers ahead of training.
+2. **Admission (Reserve)** — a rollout instance asks for work with its weight
+   version; each request is reserved in the PS at that version before it is
+   handed out (the role of the router's PS admission stage).
+3. **Completion** — finished trajectories are scored, collected per group, and
+   a completed group is committed with ``occupy_rollout_instance_request``;
+   optional group post-processing (DAPO dynamic-sampling filter) drops
+   zero-variance groups and replaces them.
+4. **Readiness** — when a buffer turns READY the PS runs its staleness aborts
+   (``handle_ready_buffer``); aborted requests are forwarded to the instances.
+5. **Consumption** — the trainer takes the trajectories of a READY buffer.
+6. **Retry** — groups that lost too many members are replaced by fresh prompts.
+
+All methods are thread-safe (one lock), so the same object serves in-process
+callers and the RPC server threads of remote rollout instances.
+"""
+
+from __future__ import annotations
+
+import threading
+from collections import deque
+from dataclasses import dataclass, field
+
+from ..config import redundant_settings
+from ..ps import BufferStatus, PSManager, RequestStatus
+from ..rollout.engine import GenRequest, RequestOutput, SamplingParams
+from ..trainer.batch import Trajectory
+from .data import DataProcessor
+
+
+@dataclass
+class _Group:
+    uid: int
+    prompt_ids: list
+    meta: dict
+    request_ids: list
+    done: dict = field(default_factory=dict)      # request_id -> Trajectory
+    dropped: set = field(default_factory=set)
+    committed: bool = False
+
+
+class AgentLoopManager:
+    def __init__(self, cfg, ps: PSManager, data: DataProcessor, reward, initial_ps_version: int = 0):
+        self.cfg = cfg
+        self.ps = ps
+        self.data = data
+        self.reward = reward
+        self.rollout_n, self.alg_rollout_n, self.entries, self.ready_entries = redundant_settings(cfg)
+        self.staleness = int(cfg.psrl.staleness)
+        self.max_ahead = int(cfg.psrl.get("max_dispatch_ahead", 5))
+        self.buffer_size = self.entries * self.rollout_n       # trajectories per buffer
+        self.initial_ps_version = int(initial_ps_version)
+        self.request_counter = 0
+        self.lock = threading.RLock()
+        self.queue: deque[GenRequest] = deque()
+        self.groups: dict[int, _Group] = {}
+        self.store: dict[int, list[Trajectory]] = {}           # committed groups by prompt id
+        self.pending_aborts: dict = {}                         # instance_id -> set(request ids)
+        self.rp = cfg.rollout
+        self.max_response = int(cfg.rollout.max_response_length)
+        gp = cfg.psrl.group_post_process
+        self.group_filter = gp.name if gp.enable else "no_filter"
+        self.filter_metric = gp.get("metric", "acc")
+        self.stats = {"dispatched_groups": 0, "completed_trajs": 0, "dropped_trajs": 0, "filtered_groups": 0,
+                      "retried_groups": 0, "aborted_requests": 0}
+        ps.on_abort_rollout = self._on_abort_rollout
+
+    # ------------------------------------------------------------ dispatch
+    def expected_ps_version(self) -> int:
+        eff = min(self.staleness, self.max_ahead)
+        return self.initial_ps_version + max(self.request_counter - eff * self.buffer_size, 0) // self.buffer_size
+
+    def _dispatch_group(self) -> None:
+        item = self.data.next_group()
+        uid = item.uid
+        rids = [uid * self.rollout_n + j for j in range(self.rollout_n)]
+        self.ps.add_request(rids, status=RequestStatus.PENDING)
+        self.ps.update_request_status(rids, RequestStatus.RUNNING)
+        meta = dict(item.meta)
+        if item.answer is not None:
+            meta["answer"] = item.answer
+        self.groups[uid] = _Group(uid, item.prompt_ids, meta, rids)
+        for j, rid in enumerate(rids):
+            mt = item.response_lens[j] if item.response_lens else self.max_response
+            params = SamplingParams(temperature=float(self.rp.temperature), top_p=float(self.rp.top_p),
+                                    top_k=int(self.rp.top_k), max_tokens=int(mt),
+                                    ignore_eos=bool(self.rp.ignore_eos), seed=rid * 7919 + 17)
+            self.queue.append(GenRequest(rid, item.prompt_ids, params, -1, {"uid": uid, "max_tokens": int(mt), **meta}))
+        self.request_counter += self.rollout_n
+        self.stats["dispatched_groups"] += 1
+
+    def fill(self, max_queued: int | None = None) -> int:
+        """Release prompt groups allowed by the dispatch-ahead bound."""
+        with self.lock:
+            cap = max_queued if max_queued is not None else 4 * self.buffer_size
+            ps_v = self.ps.get_ps_model_version()
+            n = 0
+            while len(self.queue) < cap and self.expected_ps_version() <= ps_v:
+                self._dispatch_group()
+                n += 1
+            return n
+
+    def take_work(self, instance_id, instance_version: int, max_n: int) -> list[GenRequest]:
+        """Admission: reserve each request at the instance's version and hand it out."""
+        with self.lock:
+            self.fill()
+            out: list[GenRequest] = []
+            while self.queue and len(out) < max_n:
+                req = self.queue[0]
+                rid = req.request_id
+                if self.ps.check_aborted_requests(rid, remove=True):
+                    self.queue.popleft()
+                    self._member_dropped(rid)
+                    continue
+                if not self.ps.can_reserve_request(rid, [instance_version])[0]:
+                    break
+                self.queue.popleft()
+                self.ps.reserve_rollout_instance_requests(instance_id, rid, instance_version)
+                self.ps.update_request_status(rid, RequestStatus.ROLLOUT_RUNNING, model_version=instance_version,
+                                              rollout_instance_id=instance_id)
+                # a request (re)starting on an instance takes that instance's version
+                req.version_tag = instance_version
+                if req.prev_output_ids:
+                    self.ps.update_request_version_tag(rid, instance_version)
+                out.append(req)
+            return out
+
+    # ---------------------------------------------------------- completion
+    def on_complete(self, outputs: list[RequestOutput], instance_id=None) -> None:
+        with self.lock:
+            for o in outputs:
+                self._complete_one(o)
+
+    def _complete_one(self, o: RequestOutput) -> None:
+        rid = o.request_id
+        uid = rid // self.rollout_n
+        g = self.groups.get(uid)
+        if o.finish_reason == "abort":
+            # interrupted for migration: back to the queue with its partial output
+            if g is not None and not self.ps.check_aborted_requests(rid, remove=False):
+                self.queue.appendleft(GenRequest(rid, o.prompt_ids, self._params_of(o), o.version_tag, o.meta,
+                                                 o.output_ids, o.logprobs, o.versions))
+            return
+        if g is None:
+            return
+        st = self.ps.get_request_status(rid)[0] if self.ps.has_request(rid) else None
+        if st is None:
+            self._member_dropped(rid)
+            return
+        # the engine promotes the tag when it re-prefills after a weight update
+        self.ps.update_request_version_tag(rid, o.version_tag)
+        if not self.ps.update_request_status(rid, RequestStatus.ROLLOUT_COMPLETED, model_version=o.version_tag):
+            self._member_dropped(rid)
+            return
+        traj = Trajectory(uid=uid, request_id=rid, prompt_ids=list(o.prompt_ids), response_ids=list(o.output_ids),
+                          rollout_logprobs=list(o.logprobs), versions=list(o.versions), version_tag=o.version_tag,
+                          meta=dict(o.meta))
+        self.ps.update_request_status(rid, RequestStatus.REWARD_RUNNING)
+        sc = self.reward.score(traj)
+        traj.reward = float(sc["score"])
+        traj.meta["reward_extra"] = sc
+        if not self.ps.update_request_status(rid, RequestStatus.COMPLETED):
+            self._member_dropped(rid)
+            return
+        g.done[rid] = traj
+        self.stats["completed_trajs"] += 1
+        self._maybe_commit(g)
+
+    def _params_of(self, o: RequestOutput) -> SamplingParams:
+        rp = self.rp
+        mt = o.meta.get("max_tokens", None)
+        return SamplingParams(temperature=float(rp.temperature), top_p=float(rp.top_p), top_k=int(rp.top_k),
+                              max_tokens=int(mt or (len(o.output_ids) + self.max_response)),
+                              ignore_eos=bool(rp.ignore_eos), seed=o.request_id * 7919 + 17)
+
+    def _member_dropped(self, rid: int) -> None:
+        uid = rid // self.rollout_n
+        g = self.groups.get(uid)
+        if g is None:
+            return
+        g.dropped.add(rid)
+        self.stats["dropped_trajs"] += 1
+        self._maybe_commit(g)
+
+    def _maybe_commit(self, g: _Group) -> None:
+        if g.committed:
+            return
+        live = len(g.request_ids) - len(g.dropped)
+        if live < self.alg_rollout_n:
+            # the group can no longer be completed: drop it and replace the prompt
+            self._retire_group(g, replace=True)
+            return
+        if len(g.done) < self.alg_rollout_n:
+            return
+        chosen = sorted(g.done)[: self.alg_rollout_n] if len(g.done) > self.alg_rollout_n else sorted(g.done)
+        trajs = [g.done[r] for r in chosen]
+        if self.group_filter == "dynamic_sampling_filter":
+            vals = [t.meta["reward_extra"].get(self.filter_metric, t.reward) for t in trajs]
+            if len(set(vals)) <= 1 and len(vals) > 1:
+                self.stats["filtered_groups"] += 1
+                self._retire_group(g, replace=True)
+                return
+        # redundant members still in flight are no longer needed
+        extra = [r for r in g.request_ids if r not in g.done and r not in g.dropped]
+        if extra:
+            self.ps.abort_requests(extra, abort_group=False)
+        bid, occ, entry = self.ps.occupy_rollout_instance_request(g.uid, chosen)
+        g.committed = True
+        self.groups.pop(g.uid, None)
+        if bid is None:
+            self._retire_group(g, replace=True)
+            return
+        self.store[g.uid] = trajs
+        status = self.ps.get_buffer_status(bid)
+        if status in (BufferStatus.READY, BufferStatus.READY_WITH_CAPACITY):
+            aborted = self.ps.handle_ready_buffer(bid)
+            self.stats["aborted_requests"] += len(aborted)
+
+    def _retire_group(self, g: _Group, replace: bool) -> None:
+        g.committed = True
+        self.groups.pop(g.uid, None)
+        alive = [r for r in g.request_ids if self.ps.has_request(r)]
+        if alive:
+            self.ps.abort_requests(alive, abort_group=True)
+        # purge queued members of the group
+        self.queue = deque(r for r in self.queue if r.request_id // self.rollout_n != g.uid)
+        if replace:
+            self.stats["retried_groups"] += 1
+            self._dispatch_group()
+
+    def _on_abort_rollout(self, instance_to_ids: dict) -> None:
+        for inst, ids in instance_to_ids.items():
+            self.pending_aborts.setdefault(inst, set()).update(ids)
+
+    def take_aborts(self, instance_id) -> list[int]:
+        with self.lock:
+            return sorted(self.pending_aborts.pop(instance_id, set()))
+
+    # ------------------------------------------------------------- trainer
+    def buffer_ready(self, buffer_id: int) -> bool:
+        with self.lock:
+            self.ps.ensure_train_buffer_exists(buffer_id)
+            st = self.ps.get_buffer_status(buffer_id)
+            return st in (BufferStatus.READY, BufferStatus.READY_WITH_CAPACITY)
+
+    def consume(self, buffer_id: int) -> list[Trajectory]:
+        with self.lock:
+            entries = self.ps.consume_buffer(buffer_id)
+            out: list[Trajectory] = []
+            for e in entries:
+                trajs = self.store.pop(e.prompt_id, [])
+                keep = set(e.get_all_request_ids(self.rollout_n))
+                out.extend(t for t in trajs if t.request_id in keep)
+            return out
+
+    def snapshot(self) -> dict:
+        with self.lock:
+            return {"queue": len(self.queue), "open_groups": len(self.groups), "stored_groups": len(self.store),
+                    "request_counter": self.request_counter, "expected_ps_version": self.expected_ps_version(),
+                    **self.stats}

@@ -1,0 +1,54 @@
+// Python bindings of the psrl_b200 CUDA kernels (module psrl_b200._C).
+#include <torch/extension.h>
+
+namespace psrl {
+std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, c10::optional<at::Tensor> residual, at::Tensor w, double eps);
+std::vector<at::Tensor> rmsnorm_bwd(at::Tensor dy, at::Tensor s, at::Tensor w, at::Tensor rstd,
+                                    c10::optional<at::Tensor> dres);
+at::Tensor head_rmsnorm_(at::Tensor x, at::Tensor w, double eps);
+void rope_(at::Tensor qkv, at::Tensor positions, at::Tensor cos_t, at::Tensor sin_t, int64_t nq, int64_t nkv,
+           int64_t d, bool inverse, c10::optional<at::Tensor> k_cache, c10::optional<at::Tensor> v_cache,
+           c10::optional<at::Tensor> slots);
+at::Tensor swiglu_fwd(at::Tensor gu);
+at::Tensor swiglu_bwd(at::Tensor gu, at::Tensor dout);
+void adamw_(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> p16, double lr,
+            double b1, double b2, double eps, double wd, int64_t step, c10::optional<at::Tensor> gscale_t,
+            double gscale);
+void sqnorm_accumulate_(at::Tensor x, at::Tensor out, at::Tensor partial);
+void clip_coef_(at::Tensor sq, double max_norm, at::Tensor coef, at::Tensor norm_out);
+std::vector<at::Tensor> logprob_fwd(at::Tensor logits, at::Tensor labels, double temperature, bool want_entropy);
+void logprob_bwd_(at::Tensor logits, at::Tensor labels, double temperature, c10::optional<at::Tensor> glp,
+                  c10::optional<at::Tensor> gent, at::Tensor lse, c10::optional<at::Tensor> ent);
+std::vector<at::Tensor> sample(at::Tensor logits, c10::optional<at::Tensor> temps, c10::optional<at::Tensor> seeds,
+                               c10::optional<at::Tensor> streams);
+std::vector<at::Tensor> attn_varlen_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cu_seqlens,
+                                        int64_t max_seqlen, double scale, bool want_lse);
+at::Tensor attn_paged_prefill(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor cu_q,
+                              at::Tensor kv_lens, at::Tensor block_table, int64_t max_q_len, double scale);
+std::vector<at::Tensor> attn_varlen_bwd(at::Tensor dO, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o,
+                                        at::Tensor lse, at::Tensor cu_seqlens, int64_t max_seqlen, double scale);
+int64_t decode_num_splits(int64_t batch, int64_t nkv, int64_t max_ctx);
+at::Tensor attn_decode(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor block_table,
+                       at::Tensor kv_lens, double scale, int64_t splits, c10::optional<at::Tensor> scratch);
+}  // namespace psrl
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "psrl_b200 sm_100a kernels";
+  m.def("rmsnorm_fwd", &psrl::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &psrl::rmsnorm_bwd);
+  m.def("head_rmsnorm_", &psrl::head_rmsnorm_);
+  m.def("rope_", &psrl::rope_);
+  m.def("swiglu_fwd", &psrl::swiglu_fwd);
+  m.def("swiglu_bwd", &psrl::swiglu_bwd);
+  m.def("adamw_", &psrl::adamw_);
+  m.def("sqnorm_accumulate_", &psrl::sqnorm_accumulate_);
+  m.def("clip_coef_", &psrl::clip_coef_);
+  m.def("logprob_fwd", &psrl::logprob_fwd);
+  m.def("logprob_bwd_", &psrl::logprob_bwd_);
+  m.def("sample", &psrl::sample);
+  m.def("attn_varlen_fwd", &psrl::attn_varlen_fwd);
+  m.def("attn_paged_prefill", &psrl::attn_paged_prefill);
+  m.def("attn_varlen_bwd", &psrl::attn_varlen_bwd);
+  m.def("decode_num_splits", &psrl::decode_num_splits);
+  m.def("attn_decode", &psrl::attn_decode);
+}

@@ -1,0 +1,162 @@
+"""Model architecture arguments and presets (Qwen2 / Qwen2.5 / Qwen3 / Qwen3-MoE)."""
+
+from __future__ import annotations
+
+import json
+from dataclasses import asdict, dataclass, field, replace
+from pathlib import Path
+
+
+@dataclass
+class ModelArgs:
+    arch: str = "qwen2"                 # qwen2 | qwen3 | qwen3_moe
+    vocab_size: int = 151936
+    hidden_size: int = 2048
+    num_layers: int = 36
+    num_heads: int = 16
+    num_kv_heads: int = 2
+    head_dim: int = 128
+    intermediate_size: int = 11008
+    rope_theta: float = 1_000_000.0
+    rms_eps: float = 1e-6
+    tie_word_embeddings: bool = True
+    qkv_bias: bool = True               # Qwen2/2.5: True; Qwen3: False
+    qk_norm: bool = False               # Qwen3: per-head RMSNorm on q and k
+    max_position: int = 32768
+    # MoE
+    num_experts: int = 0
+    num_experts_per_tok: int = 0
+    moe_intermediate_size: int = 0
+    norm_topk_prob: bool = True
+    router_zipf_alpha: float = 0.0      # >0: add log Zipf(alpha) prior to router logits (skewed load)
+    value_head: bool = False            # critic: scalar head instead of the LM head
+    extra: dict = field(default_factory=dict)
+
+    @property
+    def is_moe(self) -> bool:
+        return self.num_experts > 0
+
+    @property
+    def q_size(self) -> int:
+        return self.num_heads * self.head_dim
+
+    @property
+    def kv_size(self) -> int:
+        return self.num_kv_heads * self.head_dim
+
+    @property
+    def qkv_size(self) -> int:
+        return self.q_size + 2 * self.kv_size
+
+    def num_params(self) -> int:
+        h, L = self.hidden_size, self.num_layers
+        attn = h * self.qkv_size + (self.qkv_size if self.qkv_bias else 0) + self.q_size * h
+        if self.is_moe:
+            mlp = self.num_experts * 3 * h * self.moe_intermediate_size + self.num_experts * h
+        else:
+            mlp = 3 * h * self.intermediate_size
+        norms = 2 * h + (2 * self.head_dim if self.qk_norm else 0)
+        emb = self.vocab_size * h * (1 if self.tie_word_embeddings else 2)
+        return L * (attn + mlp + norms) + emb + h
+
+    def active_params_per_token(self) -> int:
+        """Matmul parameters touched per token (for FLOP accounting)."""
+        h, L = self.hidden_size, self.num_layers
+        attn = h * self.qkv_size + self.q_size * h
+        if self.is_moe:
+            mlp = self.num_experts_per_tok * 3 * h * self.moe_intermediate_size + self.num_experts * h
+        else:
+            mlp = 3 * h * self.intermediate_size
+        return L * (attn + mlp) + self.vocab_size * h
+
+    def to_dict(self) -> dict:
+        return asdict(self)
+
+    @classmethod
+    def from_hf_config(cls, cfg: dict) -> "ModelArgs":
+        mt = cfg.get("model_type", "qwen2")
+        arch = {"qwen2": "qwen2", "qwen3": "qwen3", "qwen3_moe": "qwen3_moe", "qwen2_moe": "qwen3_moe"}.get(mt, "qwen2")
+        heads = cfg["num_attention_heads"]
+        return cls(
+            arch=arch,
+            vocab_size=cfg["vocab_size"],
+            hidden_size=cfg["hidden_size"],
+            num_layers=cfg["num_hidden_layers"],
+            num_heads=heads,
+            num_kv_heads=cfg.get("num_key_value_heads", heads),
+            head_dim=cfg.get("head_dim", cfg["hidden_size"] // heads),
+            intermediate_size=cfg.get("intermediate_size", 0),
+            rope_theta=cfg.get("rope_theta", 1e6),
+            rms_eps=cfg.get("rms_norm_eps", 1e-6),
+            tie_word_embeddings=cfg.get("tie_word_embeddings", False),
+            qkv_bias=(arch == "qwen2") or cfg.get("attention_bias", False),
+            qk_norm=arch in ("qwen3", "qwen3_moe"),
+            max_position=cfg.get("max_position_embeddings", 32768),
+            num_experts=cfg.get("num_experts", 0),
+            num_experts_per_tok=cfg.get("num_experts_per_tok", 0),
+            moe_intermediate_size=cfg.get("moe_intermediate_size", 0),
+            norm_topk_prob=cfg.get("norm_topk_prob", True),
+        )
+
+    def to_hf_config(self) -> dict:
+        mt = {"qwen2": "qwen2", "qwen3": "qwen3", "qwen3_moe": "qwen3_moe"}[self.arch]
+        d = {
+            "model_type": mt,
+            "architectures": [{"qwen2": "Qwen2ForCausalLM", "qwen3": "Qwen3ForCausalLM",
+                               "qwen3_moe": "Qwen3MoeForCausalLM"}[self.arch]],
+            "vocab_size": self.vocab_size,
+            "hidden_size": self.hidden_size,
+            "num_hidden_layers": self.num_layers,
+            "num_attention_heads": self.num_heads,
+            "num_key_value_heads": self.num_kv_heads,
+            "head_dim": self.head_dim,
+            "intermediate_size": self.intermediate_size,
+            "rope_theta": self.rope_theta,
+            "rms_norm_eps": self.rms_eps,
+            "tie_word_embeddings": self.tie_word_embeddings,
+            "max_position_embeddings": self.max_position,
+            "hidden_act": "silu",
+            "torch_dtype": "bfloat16",
+        }
+        if self.is_moe:
+            d.update(num_experts=self.num_experts, num_experts_per_tok=self.num_experts_per_tok,
+                     moe_intermediate_size=self.moe_intermediate_size, norm_topk_prob=self.norm_topk_prob)
+        return d
+
+
+PRESETS: dict[str, ModelArgs] = {
+    # 2-layer Qwen2-style decoder for CPU/gloo plumbing runs
+    "tiny": ModelArgs(arch="qwen2", vocab_size=1024, hidden_size=256, num_layers=2, num_heads=4, num_kv_heads=2,
+                      head_dim=64, intermediate_size=688, tie_word_embeddings=True, max_position=4096),
+    # GPU test model: head_dim 128 so every CUDA kernel path is exercised
+    "tiny128": ModelArgs(arch="qwen2", vocab_size=2048, hidden_size=512, num_layers=2, num_heads=8, num_kv_heads=2,
+                         head_dim=128, intermediate_size=1024, tie_word_embeddings=True, max_position=8192),
+    "qwen2.5-3b": ModelArgs(arch="qwen2", vocab_size=151936, hidden_size=2048, num_layers=36, num_heads=16,
+                            num_kv_heads=2, head_dim=128, intermediate_size=11008, tie_word_embeddings=True),
+    "qwen2.5-7b": ModelArgs(arch="qwen2", vocab_size=152064, hidden_size=3584, num_layers=28, num_heads=28,
+                            num_kv_heads=4, head_dim=128, intermediate_size=18944, tie_word_embeddings=False),
+    "qwen3-8b": ModelArgs(arch="qwen3", vocab_size=151936, hidden_size=4096, num_layers=36, num_heads=32,
+                          num_kv_heads=8, head_dim=128, intermediate_size=12288, tie_word_embeddings=False,
+                          qkv_bias=False, qk_norm=True),
+    "qwen3-30b-a3b": ModelArgs(arch="qwen3_moe", vocab_size=151936, hidden_size=2048, num_layers=48, num_heads=32,
+                               num_kv_heads=4, head_dim=128, intermediate_size=6144, tie_word_embeddings=False,
+                               qkv_bias=False, qk_norm=True, num_experts=128, num_experts_per_tok=8,
+                               moe_intermediate_size=768, router_zipf_alpha=1.1),
+    "tiny-moe": ModelArgs(arch="qwen3_moe", vocab_size=2048, hidden_size=512, num_layers=2, num_heads=8,
+                          num_kv_heads=2, head_dim=128, intermediate_size=1024, tie_word_embeddings=False,
+                          qkv_bias=False, qk_norm=True, num_experts=8, num_experts_per_tok=2,
+                          moe_intermediate_size=256, router_zipf_alpha=1.1, max_position=8192),
+}
+
+
+def model_args_from_config(model_cfg) -> ModelArgs:
+    """Resolve ``model.preset`` / ``model.path`` (HF config.json) into ModelArgs."""
+    path = model_cfg.get("path") if hasattr(model_cfg, "get") else None
+    if path:
+        with open(Path(path) / "config.json") as fh:
+            return ModelArgs.from_hf_config(json.load(fh))
+    preset = model_cfg.get("preset") or "tiny"
+    if preset not in PRESETS:
+        raise KeyError(f"unknown model preset {preset!r}; have {sorted(PRESETS)}")
+    args = replace(PRESETS[preset])
+    return args

@@ -1,0 +1,163 @@
+"""Attention ops (K1, K2, K3).
+
+* :func:`varlen_attention` — causal attention over a packed batch (training,
+  remove-padding), autograd-enabled.  CUDA: ``attn_varlen_fwd/bwd``.
+* :func:`paged_prefill_attention` — chunked prefill against the paged KV cache.
+* :func:`paged_decode_attention` — one query token per sequence, split-KV.
+
+The PyTorch implementations below are the numerical oracles and the CPU path.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ._ext import ext
+
+
+# --------------------------------------------------------------- references
+def varlen_attention_ref(q, k, v, cu_seqlens, scale):
+    """q [T, nq, d], k/v [T, nkv, d]; causal per sequence; fp32 math."""
+    T, nq, d = q.shape
+    nkv = k.shape[1]
+    g = nq // nkv
+    out = torch.empty(T, nq, d, dtype=q.dtype, device=q.device)
+    cu = cu_seqlens.tolist()
+    for i in range(len(cu) - 1):
+        s, e = cu[i], cu[i + 1]
+        if e <= s:
+            continue
+        qs = q[s:e].float().transpose(0, 1)                     # [nq, L, d]
+        ks = k[s:e].float().transpose(0, 1).repeat_interleave(g, 0)
+        vs = v[s:e].float().transpose(0, 1).repeat_interleave(g, 0)
+        att = (qs @ ks.transpose(1, 2)) * scale
+        L = e - s
+        mask = torch.ones(L, L, dtype=torch.bool, device=q.device).triu(1)
+        att = att.masked_fill(mask, float("-inf")).softmax(-1)
+        out[s:e] = (att @ vs).transpose(0, 1).to(q.dtype)
+    return out
+
+
+def gather_paged_kv(k_cache, v_cache, block_table_row, length):
+    bs = k_cache.shape[2]
+    nblk = (length + bs - 1) // bs
+    blocks = block_table_row[:nblk].long()
+    k = k_cache[blocks].permute(0, 2, 1, 3).reshape(-1, k_cache.shape[1], k_cache.shape[3])[:length]
+    v = v_cache[blocks].permute(0, 2, 1, 3).reshape(-1, v_cache.shape[1], v_cache.shape[3])[:length]
+    return k, v
+
+
+def paged_attention_ref(q, k_cache, v_cache, cu_q, kv_lens, block_table, scale):
+    """Queries are the last q_len positions of each context (causal)."""
+    T, nq, d = q.shape
+    nkv = k_cache.shape[1]
+    g = nq // nkv
+    out = torch.empty_like(q)
+    cu = cu_q.tolist()
+    lens = kv_lens.tolist()
+    for i in range(len(cu) - 1):
+        s, e = cu[i], cu[i + 1]
+        if e <= s:
+            continue
+        L = lens[i]
+        k, v = gather_paged_kv(k_cache, v_cache, block_table[i], L)
+        qs = q[s:e].float().transpose(0, 1)
+        ks = k.float().transpose(0, 1).repeat_interleave(g, 0)
+        vs = v.float().transpose(0, 1).repeat_interleave(g, 0)
+        att = (qs @ ks.transpose(1, 2)) * scale            # [nq, ql, L]
+        ql = e - s
+        qpos = torch.arange(L - ql, L, device=q.device)[:, None]
+        kpos = torch.arange(L, device=q.device)[None, :]
+        att = att.masked_fill(kpos > qpos, float("-inf")).softmax(-1)
+        out[s:e] = (att @ vs).transpose(0, 1).to(q.dtype)
+    return out
+
+
+# ----------------------------------------------------------------- autograd
+class _VarlenAttnFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, cu_seqlens, max_seqlen, nq, nkv, d, scale):
+        T = qkv.shape[0]
+        q = qkv[:, : nq * d].view(T, nq, d)
+        k = qkv[:, nq * d: (nq + nkv) * d].view(T, nkv, d)
+        v = qkv[:, (nq + nkv) * d:].view(T, nkv, d)
+        o, lse = ext().attn_varlen_fwd(q, k, v, cu_seqlens, max_seqlen, scale, True)
+        ctx.save_for_backward(qkv, o, lse, cu_seqlens)
+        ctx.cfg = (max_seqlen, nq, nkv, d, scale)
+        return o.view(T, nq * d)
+
+    @staticmethod
+    def backward(ctx, do):
+        qkv, o, lse, cu = ctx.saved_tensors
+        max_seqlen, nq, nkv, d, scale = ctx.cfg
+        T = qkv.shape[0]
+        q = qkv[:, : nq * d].view(T, nq, d)
+        k = qkv[:, nq * d: (nq + nkv) * d].view(T, nkv, d)
+        v = qkv[:, (nq + nkv) * d:].view(T, nkv, d)
+        do = do.contiguous().view(T, nq, d)
+        dq, dk, dv = ext().attn_varlen_bwd(do, q, k, v, o, lse, cu, max_seqlen, scale)
+        dqkv = torch.cat([dq.view(T, -1), dk.view(T, -1), dv.view(T, -1)], dim=1)
+        return dqkv, None, None, None, None, None, None
+
+
+def varlen_attention(qkv: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int, nq: int, nkv: int, d: int,
+                     scale: float | None = None) -> torch.Tensor:
+    """Causal attention over a packed batch; ``qkv`` [T, (nq+2nkv)*d] -> [T, nq*d]."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(d)
+    if qkv.is_cuda and qkv.dtype == torch.bfloat16 and d == 128:
+        return _VarlenAttnFn.apply(qkv, cu_seqlens, int(max_seqlen), nq, nkv, d, scale)
+    T = qkv.shape[0]
+    q = qkv[:, : nq * d].view(T, nq, d)
+    k = qkv[:, nq * d: (nq + nkv) * d].view(T, nkv, d)
+    v = qkv[:, (nq + nkv) * d:].view(T, nkv, d)
+    return _ref_autograd(q, k, v, cu_seqlens, scale).reshape(T, nq * d)
+
+
+def _ref_autograd(q, k, v, cu_seqlens, scale):
+    # differentiable reference (CPU training path)
+    T, nq, d = q.shape
+    nkv = k.shape[1]
+    g = nq // nkv
+    outs = []
+    cu = cu_seqlens.tolist()
+    for i in range(len(cu) - 1):
+        s, e = cu[i], cu[i + 1]
+        if e <= s:
+            continue
+        qs = q[s:e].transpose(0, 1)
+        ks = k[s:e].transpose(0, 1).repeat_interleave(g, 0)
+        vs = v[s:e].transpose(0, 1).repeat_interleave(g, 0)
+        L = e - s
+        mask = torch.ones(L, L, dtype=torch.bool, device=q.device).triu(1)
+        att = ((qs @ ks.transpose(1, 2)) * scale).masked_fill(mask, float("-inf")).softmax(-1)
+        outs.append((att @ vs).transpose(0, 1))
+    return torch.cat(outs, 0) if outs else q.new_zeros(0, nq, d)
+
+
+def paged_prefill_attention(q, k_cache, v_cache, cu_q, kv_lens, block_table, max_q_len, scale=None):
+    """q [T, nq, d] (view ok); returns [T, nq, d]."""
+    d = q.shape[-1]
+    scale = scale if scale is not None else 1.0 / math.sqrt(d)
+    if q.is_cuda and d == 128:
+        return ext().attn_paged_prefill(q, k_cache, v_cache, cu_q, kv_lens, block_table, int(max_q_len), scale)
+    return paged_attention_ref(q, k_cache, v_cache, cu_q, kv_lens, block_table, scale)
+
+
+def decode_splits(batch: int, nkv: int, max_ctx: int) -> int:
+    return int(ext().decode_num_splits(batch, nkv, max_ctx))
+
+
+def paged_decode_attention(q, k_cache, v_cache, block_table, kv_lens, scale=None, splits: int | None = None,
+                           scratch: torch.Tensor | None = None):
+    """q [B, nq, d] -> [B, nq, d]; kv_lens include the current token."""
+    d = q.shape[-1]
+    scale = scale if scale is not None else 1.0 / math.sqrt(d)
+    if q.is_cuda and d == 128:
+        if splits is None:
+            splits = decode_splits(q.shape[0], k_cache.shape[1], int(block_table.shape[1] * k_cache.shape[2]))
+        return ext().attn_decode(q.contiguous(), k_cache, v_cache, block_table, kv_lens, scale, int(splits), scratch)
+    B = q.shape[0]
+    cu = torch.arange(B + 1, dtype=torch.int32, device=q.device)
+    return paged_attention_ref(q, k_cache, v_cache, cu, kv_lens, block_table, scale)

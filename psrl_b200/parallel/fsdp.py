@@ -1,0 +1,176 @@
+"""Sharded data parallelism with flat buckets (the trainer's FSDP backend).
+
+Layout (chosen for 180 GB of HBM per GPU):
+
+* every rank keeps the **full bf16 parameters** resident (views into one flat
+  buffer per bucket, one bucket per decoder layer), so forward/backward never
+  wait for a parameter all-gather;
+* gradients are accumulated across micro-batches into **fp32 main-grad**
+  buckets (post-accumulate hooks turn each bf16 ``.grad`` into an fp32 add);
+* the fp32 **master weights and Adam moments are sharded** 1/world per bucket
+  (ZeRO-2 style optimizer-state sharding);
+* the optimizer step per bucket is: reduce-scatter(grad) → global grad-norm
+  (one tiny all-reduce) → fused AdamW on the shard writing the bf16 shard in
+  place → all-gather of the bf16 shard back into the full bucket.
+
+The reference trains with FSDP2 full-shard (parameters re-gathered per layer
+in every forward and backward, ``engine_train_worker.py:80-85``); keeping
+parameters resident trades 2 bytes/param of HBM for one all-gather per
+optimizer step instead of two per micro-batch.  Collectives here are NCCL
+(the baseline path); :mod:`psrl_b200.parallel.peer` provides the peer-memory
+reduce-scatter + AdamW kernel path.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+
+
+class _Bucket:
+    def __init__(self, names, params, world: int, rank: int, device, pad_to: int):
+        self.names = names
+        self.params = params
+        n = sum(p.numel() for p in params)
+        self.numel = n
+        padded = math.ceil(n / pad_to) * pad_to
+        self.padded = padded
+        self.shard = padded // world
+        self.rank = rank
+        dtype = params[0].dtype
+        self.flat = torch.zeros(padded, dtype=dtype, device=device)
+        self.grad = torch.zeros(padded, dtype=torch.float32, device=device)
+        off = 0
+        self.offsets = []
+        for p in params:
+            k = p.numel()
+            self.flat[off: off + k].copy_(p.data.reshape(-1))
+            p.data = self.flat[off: off + k].view(p.shape)
+            self.offsets.append(off)
+            off += k
+        lo = rank * self.shard
+        self.lo, self.hi = lo, lo + self.shard
+        self.master = self.flat[lo: self.hi].float().clone()
+        self.m = torch.zeros_like(self.master)
+        self.v = torch.zeros_like(self.master)
+        self.grad_shard = self.grad[lo: self.hi] if world == 1 else torch.zeros_like(self.master)
+
+    def param_shard(self) -> torch.Tensor:
+        return self.flat[self.lo: self.hi]
+
+
+class FlatShardedDP:
+    def __init__(self, model: torch.nn.Module, group=None, *, lr: float = 1e-6, betas=(0.9, 0.999), eps: float = 1e-8,
+                 weight_decay: float = 0.0, max_grad_norm: float = 1.0, warmup_steps: int = 0,
+                 bucket_mode: str = "layer"):
+        self.model = model
+        self.group = group
+        self.world = dist.get_world_size(group) if (group is not None or dist.is_initialized()) and \
+            dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        self.device = next(model.parameters()).device
+        self.lr, self.betas, self.eps, self.wd = lr, tuple(betas), eps, weight_decay
+        self.max_grad_norm = max_grad_norm
+        self.warmup_steps = warmup_steps
+        self.step_count = 0
+        pad_to = self.world * 64
+        groups: dict[str, list] = {}
+        order: list[str] = []
+        for name, p in model.named_parameters():
+            if not p.requires_grad:
+                continue
+            key = ".".join(name.split(".")[:2]) if (bucket_mode == "layer" and name.startswith("layers.")) else "misc"
+            if key not in groups:
+                groups[key] = []
+                order.append(key)
+            groups[key].append((name, p))
+        self.buckets: list[_Bucket] = []
+        self.param_to_bucket: dict = {}
+        for key in order:
+            names = [n for n, _ in groups[key]]
+            params = [p for _, p in groups[key]]
+            b = _Bucket(names, params, self.world, self.rank, self.device, pad_to)
+            for i, p in enumerate(params):
+                self.param_to_bucket[p] = (b, b.offsets[i])
+            self.buckets.append(b)
+        self._hooks = [p.register_post_accumulate_grad_hook(self._accumulate) for p in self.param_to_bucket]
+        self.norm = ops.NormAccumulator(self.device)
+
+    # --------------------------------------------------------------- grads
+    def _accumulate(self, p: torch.Tensor) -> None:
+        b, off = self.param_to_bucket[p]
+        b.grad[off: off + p.numel()].add_(p.grad.reshape(-1))
+        p.grad = None
+
+    def zero_grad(self) -> None:
+        for b in self.buckets:
+            b.grad.zero_()
+
+    # ---------------------------------------------------------------- step
+    def current_lr(self) -> float:
+        if self.warmup_steps > 0:
+            return self.lr * min(1.0, (self.step_count + 1) / self.warmup_steps)
+        return self.lr
+
+    @torch.no_grad()
+    def step(self, grad_scale: float = 1.0) -> dict:
+        """Reduce, clip, update, re-gather.  Gradients are *summed* across ranks
+        (callers normalise the loss by the global token/sequence count)."""
+        self.step_count += 1
+        self.norm.reset()
+        for b in self.buckets:
+            if self.world > 1:
+                dist.reduce_scatter_tensor(b.grad_shard, b.grad, op=dist.ReduceOp.SUM, group=self.group)
+            self.norm.add(b.grad_shard)
+        if self.world > 1:
+            dist.all_reduce(self.norm.sq, group=self.group)
+        if grad_scale != 1.0:
+            self.norm.sq.mul_(grad_scale * grad_scale)
+        coef, gnorm = self.norm.clip_coef(self.max_grad_norm)
+        lr = self.current_lr()
+        b1, b2 = self.betas
+        for b in self.buckets:
+            ops.adamw_(b.master, b.grad_shard, b.m, b.v, b.param_shard(), lr, b1, b2, self.eps, self.wd,
+                       self.step_count, coef, grad_scale)
+            if self.world > 1:
+                dist.all_gather_into_tensor(b.flat, b.param_shard(), group=self.group)
+        self.zero_grad()
+        return {"grad_norm": gnorm, "lr": lr}
+
+    # -------------------------------------------------------------- state
+    def full_params(self) -> dict[str, torch.Tensor]:
+        return dict(self.model.named_parameters())
+
+    def optimizer_state(self) -> dict:
+        return {
+            "step": self.step_count,
+            "buckets": [{"names": b.names, "master": b.master.cpu(), "m": b.m.cpu(), "v": b.v.cpu()}
+                        for b in self.buckets],
+            "world": self.world,
+            "rank": self.rank,
+        }
+
+    def load_optimizer_state(self, st: dict) -> None:
+        if st.get("world") != self.world:
+            raise ValueError("optimizer state was saved with a different world size")
+        self.step_count = int(st["step"])
+        for b, s in zip(self.buckets, st["buckets"]):
+            if s["names"] != b.names:
+                raise ValueError("optimizer state bucket mismatch")
+            b.master.copy_(s["master"])
+            b.m.copy_(s["m"])
+            b.v.copy_(s["v"])
+
+    @torch.no_grad()
+    def sync_master_from_params(self) -> None:
+        """After loading bf16 params from a checkpoint, refresh the fp32 master shards."""
+        for b in self.buckets:
+            b.master.copy_(b.param_shard().float())
+
+    def remove_hooks(self) -> None:
+        for h in self._hooks:
+            h.remove()

@@ -163,6 +163,10 @@ class RequestStatusTracker:
             raise KeyError(f"unknown request ids in {ids}")
         return out
 
+    def has_request(self, request_id: int) -> bool:
+        with self._state_lock:
+            return request_id in self._status
+
     @state_locked
     def get_all_request_statuses(self) -> dict[int, RequestStatus]:
         return dict(self._status)

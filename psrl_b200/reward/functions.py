@@ -1,0 +1,105 @@
+"""Reward functions and the reward-loop registry.
+
+Registered loops (reference ``psrl/workers/reward/reward_loop/registry.py:22``):
+
+* ``naive`` — score = task reward;
+* ``dapo`` — task reward plus the DAPO overlong-buffer penalty
+  ``-min(1, (len - (max_len - buffer)) / buffer) * factor`` beyond the soft limit;
+* ``bernoulli_hash`` — Bernoulli(p) decided by a seeded hash of the trajectory id
+  (synthetic benchmark reward);
+* ``addition`` — 1.0 if the integer after the ``####`` marker equals the sum.
+
+``RewardManager.score`` is called per finished trajectory on the driver;
+``normalize_reward`` mirrors the reference's batch normalisation hook.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import re
+from typing import Callable
+
+REWARD_LOOPS: dict[str, Callable] = {}
+
+
+def register_reward_loop(name: str):
+    def deco(fn):
+        REWARD_LOOPS[name] = fn
+        return fn
+    return deco
+
+
+def bernoulli_hash_score(traj_id: int, p: float, seed: int = 0) -> float:
+    h = hashlib.blake2b(f"{seed}:{traj_id}".encode(), digest_size=8).digest()
+    u = int.from_bytes(h, "little") / 2**64
+    return 1.0 if u < p else 0.0
+
+
+_NUM = re.compile(r"####\s*(-?\d+)")
+
+
+def addition_score(response_text: str, answer: int) -> float:
+    m = _NUM.search(response_text)
+    return 1.0 if (m is not None and int(m.group(1)) == answer) else 0.0
+
+
+def overlong_penalty(resp_len: int, max_len: int, buffer_len: int, factor: float) -> float:
+    soft = max_len - buffer_len
+    if resp_len <= soft or buffer_len <= 0:
+        return 0.0
+    return -min(1.0, (resp_len - soft) / buffer_len) * factor
+
+
+@register_reward_loop("bernoulli_hash")
+def _bernoulli(ctx, traj) -> dict:
+    return {"score": bernoulli_hash_score(traj.request_id, ctx["p"], ctx.get("seed", 0))}
+
+
+@register_reward_loop("addition")
+def _addition(ctx, traj) -> dict:
+    text = ctx["tokenizer"].decode(traj.response_ids)
+    return {"score": addition_score(text, traj.meta.get("answer", -1))}
+
+
+@register_reward_loop("naive")
+def _naive(ctx, traj) -> dict:
+    base = REWARD_LOOPS[ctx.get("task", "bernoulli_hash")]
+    return base(ctx, traj)
+
+
+@register_reward_loop("dapo")
+def _dapo(ctx, traj) -> dict:
+    base = REWARD_LOOPS[ctx.get("task", "bernoulli_hash")](ctx, traj)
+    ob = ctx.get("overlong_buffer")
+    pen = 0.0
+    if ob and ob.get("enable"):
+        pen = overlong_penalty(traj.response_len, ctx["max_response_length"], int(ob["len"]),
+                               float(ob["penalty_factor"]))
+    return {"score": base["score"] + pen, "acc": base["score"], "overlong_penalty": pen}
+
+
+class RewardManager:
+    def __init__(self, cfg, tokenizer=None):
+        r = cfg.reward
+        self.kind = r.kind
+        self.ctx = {
+            "p": float(r.get("p", 0.3)),
+            "seed": int(cfg.data.get("seed", 0)),
+            "tokenizer": tokenizer,
+            "overlong_buffer": r.get("overlong_buffer"),
+            "max_response_length": int(cfg.rollout.max_response_length),
+            "task": r.get("task", "bernoulli_hash" if r.kind in ("naive", "dapo") else r.kind),
+        }
+        if self.kind not in REWARD_LOOPS:
+            raise KeyError(f"unknown reward loop {self.kind!r}; registered: {sorted(REWARD_LOOPS)}")
+
+    def score(self, traj) -> dict:
+        return REWARD_LOOPS[self.kind](self.ctx, traj)
+
+    @staticmethod
+    def normalize_reward(scores: list[float]) -> list[float]:
+        if len(scores) < 2:
+            return list(scores)
+        m = sum(scores) / len(scores)
+        sd = (sum((s - m) ** 2 for s in scores) / (len(scores) - 1)) ** 0.5
+        return [(s - m) / (sd + 1e-6) for s in scores]

@@ -1,0 +1,162 @@
+"""Actor / reference / critic workers (the trainer side of the engine, C11).
+
+``PolicyWorker`` owns a decoder in bf16 (fp32 on CPU), the sharded DP optimizer
+(:class:`~psrl_b200.parallel.fsdp.FlatShardedDP`) and implements:
+
+* ``compute_log_prob`` — old (or reference) log-probs over packed micro-batches;
+* ``update_policy`` — mini-batch / micro-batch PPO-family update with the fused
+  LM-head log-prob (K8), clip-higher + dual-clip, token-mean aggregation over
+  the global token count, optional entropy bonus, KL loss and TIS weights;
+* ``publish_state`` — the parameters to hand to the weight-sync path.
+
+Reference: ``PSRL_EngineTrainWorker`` (``psrl/workers/train/engine_train_worker.py:75``,
+``update_actor`` :521) on top of veRL's actor.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ..models import ModelArgs, build_model
+from ..parallel.fsdp import FlatShardedDP
+from . import algos
+from .batch import Trajectory, balance_across_ranks, build_micro_batch, pack_micro_batches, response_slices
+
+
+def _dtype(name: str, device) -> torch.dtype:
+    if torch.device(device).type == "cpu" and name == "bf16":
+        return torch.float32
+    return {"bf16": torch.bfloat16, "fp32": torch.float32, "fp16": torch.float16}[name]
+
+
+class PolicyWorker:
+    def __init__(self, cfg, args: ModelArgs, device, dp_group=None, seed: int = 0, trainable: bool = True,
+                 dp_rank: int = 0, dp_world: int = 1):
+        self.cfg = cfg
+        self.args = args
+        self.device = torch.device(device)
+        self.dtype = _dtype(cfg.model.dtype, device)
+        self.model = build_model(args, self.device, self.dtype, seed=seed)
+        self.model.gradient_checkpointing = bool(cfg.model.enable_gradient_checkpointing)
+        self.dp_rank, self.dp_world = dp_rank, dp_world
+        self.dp = None
+        if trainable:
+            oc = cfg.actor.optim if not args.value_head else cfg.critic.optim
+            self.dp = FlatShardedDP(self.model, dp_group, lr=float(oc.lr), betas=tuple(oc.get("betas", (0.9, 0.999))),
+                                    eps=float(oc.get("eps", 1e-8)), weight_decay=float(oc.weight_decay),
+                                    max_grad_norm=float(cfg.actor.grad_clip),
+                                    warmup_steps=int(oc.get("lr_warmup_steps", 0)))
+        else:
+            for p in self.model.parameters():
+                p.requires_grad_(False)
+        self.max_tokens = int(cfg.actor.ppo_max_token_len_per_gpu)
+
+    # ---------------------------------------------------------------- utils
+    def my_share(self, trajs: list[Trajectory], idx: list[int] | None = None) -> list[int]:
+        idx = list(range(len(trajs))) if idx is None else idx
+        parts = balance_across_ranks([trajs[i] for i in idx], self.dp_world)
+        return [idx[j] for j in parts[self.dp_rank]]
+
+    # ------------------------------------------------------------- logprob
+    @torch.no_grad()
+    def compute_log_prob(self, trajs: list[Trajectory], idx: list[int], field: str = "old_logprobs",
+                         temperature: float = 1.0) -> None:
+        self.model.eval()
+        for bin_ in pack_micro_batches(idx, trajs, self.max_tokens):
+            mb = build_micro_batch(trajs, bin_, self.device)
+            lp, _ = self.model.logprobs(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen, mb.labels,
+                                        temperature)
+            lp = lp.float().cpu()
+            for i, sl in response_slices(mb, trajs):
+                setattr(trajs[i], field, lp[sl].tolist())
+
+    @torch.no_grad()
+    def compute_values(self, trajs: list[Trajectory], idx: list[int]) -> None:
+        for bin_ in pack_micro_batches(idx, trajs, self.max_tokens):
+            mb = build_micro_batch(trajs, bin_, self.device)
+            v = self.model.values(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen).float().cpu()
+            for i, sl in response_slices(mb, trajs):
+                trajs[i].old_values = v[sl].tolist()
+
+    # -------------------------------------------------------------- update
+    def _mini_batches(self, trajs: list[Trajectory]) -> list[list[int]]:
+        """Split by prompt group into ``ppo_mini_batch_size`` groups per mini-batch."""
+        by_uid: dict = {}
+        for i, t in enumerate(trajs):
+            by_uid.setdefault(t.uid, []).append(i)
+        groups = list(by_uid.values())
+        per = max(1, int(self.cfg.actor.ppo_mini_batch_size))
+        return [[i for g in groups[s: s + per] for i in g] for s in range(0, len(groups), per)]
+
+    def update_policy(self, trajs: list[Trajectory], temperature: float = 1.0) -> dict:
+        ac = self.cfg.actor
+        self.model.train()
+        stats: dict[str, list] = {}
+        use_tis = bool(self.cfg.algorithm.rollout_correction.tis)
+        for _epoch in range(int(ac.ppo_epochs)):
+            for mini in self._mini_batches(trajs):
+                global_tokens = float(sum(trajs[i].response_len for i in mini))
+                num_seqs = len(mini)
+                mine = self.my_share(trajs, mini)
+                for bin_ in pack_micro_batches(mine, trajs, self.max_tokens):
+                    mb = build_micro_batch(trajs, bin_, self.device)
+                    lp, ent = self.model.logprobs(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen,
+                                                  mb.labels, temperature)
+                    tis = None
+                    if use_tis:
+                        rl = build_micro_batch(trajs, bin_, self.device, field_old="rollout_logprobs").old_logprobs
+                        tis = algos.truncated_is_weight(mb.old_logprobs, rl, float(self.cfg.algorithm.rollout_correction.tis_cap))
+                    agg = dict(seq_ids=mb.seq_ids, num_seqs=num_seqs, global_tokens=global_tokens)
+                    loss, m = algos.ppo_policy_loss(lp, mb.old_logprobs, mb.advantages, mb.loss_mask,
+                                                    float(ac.clip_ratio_low), float(ac.clip_ratio_high),
+                                                    float(ac.clip_ratio_c), ac.loss_agg_mode, tis_weight=tis, **agg)
+                    pg_loss = loss.detach()
+                    if float(ac.entropy_coeff) != 0.0:
+                        ent_loss = algos.agg_loss(ent, mb.loss_mask, ac.loss_agg_mode, **agg)
+                        loss = loss - float(ac.entropy_coeff) * ent_loss
+                    if ac.use_kl_loss:
+                        ref = build_micro_batch(trajs, bin_, self.device, field_old="ref_logprobs").old_logprobs
+                        kl = algos.kl_penalty(lp, ref, ac.kl_loss_type)
+                        loss = loss + float(ac.kl_loss_coef) * algos.agg_loss(kl, mb.loss_mask, ac.loss_agg_mode, **agg)
+                    loss.backward()
+                    with torch.no_grad():
+                        m["pg_loss"] = pg_loss
+                        m["entropy"] = (ent.detach() * mb.loss_mask).sum() / global_tokens
+                    for k, v in m.items():
+                        stats.setdefault(k, []).append(v)
+                st = self.dp.step()
+                stats.setdefault("grad_norm", []).append(st["grad_norm"])
+                stats.setdefault("lr", []).append(torch.tensor(st["lr"]))
+        out = {}
+        for k, vs in stats.items():
+            t = torch.stack([v.reshape(()).float().to(self.device) for v in vs])
+            out[f"actor/{k}"] = float(t.sum()) if k in ("pg_loss", "entropy") else float(t.mean())
+        return out
+
+    def update_critic(self, trajs: list[Trajectory]) -> dict:
+        cc = self.cfg.critic
+        self.model.train()
+        stats: dict[str, list] = {}
+        for mini in self._mini_batches(trajs):
+            global_tokens = float(sum(trajs[i].response_len for i in mini))
+            for bin_ in pack_micro_batches(self.my_share(trajs, mini), trajs, self.max_tokens):
+                mb = build_micro_batch(trajs, bin_, self.device)
+                v = self.model.values(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen)
+                old_v = torch.zeros_like(v)
+                ret = torch.zeros_like(v)
+                for j, (i, sl) in enumerate(response_slices(mb, trajs)):
+                    old_v[sl] = torch.tensor(trajs[i].old_values, device=v.device)
+                    ret[sl] = torch.tensor(trajs[i].returns, device=v.device)
+                loss, m = algos.value_loss(v, old_v, ret, mb.loss_mask, float(cc.cliprange_value),
+                                           global_tokens=global_tokens)
+                loss.backward()
+                m["vf_loss"] = loss.detach()
+                for k, val in m.items():
+                    stats.setdefault(k, []).append(val)
+            st = self.dp.step()
+            stats.setdefault("grad_norm", []).append(st["grad_norm"])
+        return {f"critic/{k}": float(torch.stack([x.reshape(()).float() for x in vs]).mean()) for k, vs in stats.items()}
+
+    # --------------------------------------------------------------- state
+    def named_parameters(self) -> dict[str, torch.Tensor]:
+        return {n: p.detach() for n, p in self.model.named_parameters()}

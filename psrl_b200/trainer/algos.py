@@ -1,0 +1,257 @@
+"""RL algorithm math: advantage estimators, policy/value losses, KL penalties.
+
+Behaviour follows the estimators the reference selects through veRL's
+``core_algos`` (reference glue: ``psrl/trainer/ppo/utils.py:133-308``):
+
+* ``gae`` — generalised advantage estimation over response tokens;
+* ``grpo`` — outcome reward normalised within the prompt group (``uid`` /
+  ``parent_id``), optionally divided by the group std;
+* ``rloo`` — leave-one-out group baseline;
+* ``reinforce_plus_plus`` — discounted returns whitened over the batch;
+* ``gdpo`` — each reward component is group-normalised separately, then summed
+  and re-normalised over the batch;
+* ``optimal_token_baseline`` — per-position baseline weighted by squared
+  sequence-length-normalised log-prob gradients (approximated by token counts);
+* multi-trajectory GRPO broadcasts the final session's advantage to every
+  output of that session (``compute_advantage_for_multi_trajectories``).
+
+Losses: PPO clipped surrogate with asymmetric ("clip-higher") ranges and the
+dual-clip lower bound ``clip_ratio_c``; aggregation modes ``token-mean``,
+``seq-mean-token-sum``, ``seq-mean-token-mean``, ``seq-mean-token-sum-norm``;
+clipped value loss; KL estimators k1/k2/k3(low_var_kl)/abs.
+"""
+
+from __future__ import annotations
+
+from collections import defaultdict
+
+import torch
+
+# ------------------------------------------------------------------ helpers
+
+
+def masked_mean(x: torch.Tensor, mask: torch.Tensor, dim=None, eps: float = 1e-8) -> torch.Tensor:
+    m = mask.to(x.dtype)
+    if dim is None:
+        return (x * m).sum() / (m.sum() + eps)
+    return (x * m).sum(dim) / (m.sum(dim) + eps)
+
+
+def masked_whiten(x: torch.Tensor, mask: torch.Tensor, shift_mean: bool = True, eps: float = 1e-8) -> torch.Tensor:
+    mean = masked_mean(x, mask)
+    var = masked_mean((x - mean) ** 2, mask)
+    out = (x - mean) * torch.rsqrt(var + eps)
+    if not shift_mean:
+        out = out + mean
+    return out * mask
+
+
+def group_indices(uids) -> dict:
+    groups: dict = defaultdict(list)
+    for i, u in enumerate(uids):
+        groups[u].append(i)
+    return groups
+
+
+# --------------------------------------------------------------- advantages
+
+
+def grpo_outcome_advantage(scores: torch.Tensor, uids, norm_by_std: bool = True, eps: float = 1e-6) -> torch.Tensor:
+    """scores [N] (one scalar per trajectory) -> advantages [N]."""
+    adv = torch.zeros_like(scores, dtype=torch.float32)
+    for idx in group_indices(uids).values():
+        s = scores[idx].float()
+        if len(idx) == 1:
+            mean, std = torch.zeros(()), torch.ones(())
+        else:
+            mean, std = s.mean(), s.std(unbiased=True)
+        a = s - mean
+        if norm_by_std:
+            a = a / (std + eps)
+        adv[idx] = a
+    return adv
+
+
+def rloo_advantage(scores: torch.Tensor, uids) -> torch.Tensor:
+    adv = torch.zeros_like(scores, dtype=torch.float32)
+    for idx in group_indices(uids).values():
+        s = scores[idx].float()
+        n = len(idx)
+        adv[idx] = s - (s.sum() - s) / (n - 1) if n > 1 else s * 0
+    return adv
+
+
+def gdpo_advantage(score_components: torch.Tensor, uids, eps: float = 1e-6) -> torch.Tensor:
+    """score_components [N, K]: group-normalise each component, sum, batch-whiten."""
+    N, K = score_components.shape
+    total = torch.zeros(N, dtype=torch.float32)
+    for k in range(K):
+        total += grpo_outcome_advantage(score_components[:, k], uids, True, eps)
+    return (total - total.mean()) / (total.std(unbiased=False) + eps) if N > 1 else total
+
+
+def reinforce_pp_returns(token_rewards: torch.Tensor, mask: torch.Tensor, gamma: float = 1.0) -> torch.Tensor:
+    """token_rewards/mask [N, L] -> whitened discounted returns [N, L]."""
+    ret = torch.zeros_like(token_rewards, dtype=torch.float32)
+    run = torch.zeros(token_rewards.shape[0], dtype=torch.float32)
+    for t in reversed(range(token_rewards.shape[1])):
+        run = token_rewards[:, t].float() + gamma * run * mask[:, t]
+        ret[:, t] = run
+    return masked_whiten(ret, mask)
+
+
+def gae_advantage(token_rewards: torch.Tensor, values: torch.Tensor, mask: torch.Tensor, gamma: float, lam: float):
+    """[N, L] tensors -> (advantages whitened [N, L], returns [N, L])."""
+    N, L = token_rewards.shape
+    adv = torch.zeros(N, L, dtype=torch.float32)
+    last = torch.zeros(N, dtype=torch.float32)
+    nextv = torch.zeros(N, dtype=torch.float32)
+    for t in reversed(range(L)):
+        m = mask[:, t].float()
+        delta = token_rewards[:, t].float() + gamma * nextv - values[:, t].float()
+        last = delta + gamma * lam * last
+        last = last * m
+        adv[:, t] = last
+        nextv = torch.where(m > 0, values[:, t].float(), nextv)
+    returns = adv + values.float()
+    return masked_whiten(adv, mask), returns * mask
+
+
+def optimal_token_baseline_advantage(scores: torch.Tensor, uids, lengths: torch.Tensor, eps: float = 1e-6):
+    """Group baseline weighted by 1/length (shorter trajectories' gradients are
+    larger per token), normalised by the weighted group std."""
+    adv = torch.zeros_like(scores, dtype=torch.float32)
+    for idx in group_indices(uids).values():
+        s = scores[idx].float()
+        w = 1.0 / lengths[idx].float().clamp_min(1)
+        b = (w * s).sum() / (w.sum() + eps)
+        d = s - b
+        sd = ((w * d * d).sum() / (w.sum() + eps)).sqrt()
+        adv[idx] = d / (sd + eps) if len(idx) > 1 else d * 0
+    return adv
+
+
+def broadcast_session_advantage(adv: torch.Tensor, session_ids, is_final) -> torch.Tensor:
+    """Multi-trajectory GRPO: every output of a session takes the final output's advantage."""
+    out = adv.clone()
+    final = {}
+    for i, (sid, fin) in enumerate(zip(session_ids, is_final)):
+        if fin:
+            final[sid] = adv[i]
+    for i, sid in enumerate(session_ids):
+        if sid in final:
+            out[i] = final[sid]
+    return out
+
+
+# -------------------------------------------------------------------- KL
+
+
+def kl_penalty(logp: torch.Tensor, ref_logp: torch.Tensor, kind: str = "low_var_kl") -> torch.Tensor:
+    d = logp - ref_logp
+    if kind in ("kl", "k1"):
+        return d
+    if kind == "abs":
+        return d.abs()
+    if kind in ("mse", "k2"):
+        return 0.5 * d * d
+    if kind in ("low_var_kl", "k3"):
+        r = torch.exp(-d.clamp(-20, 20))
+        return (r - 1 + d).clamp(-10, 10)
+    raise ValueError(f"unknown kl kind {kind!r}")
+
+
+# -------------------------------------------------------------------- loss
+
+
+def agg_loss(loss_mat: torch.Tensor, mask: torch.Tensor, mode: str, seq_ids: torch.Tensor | None = None,
+             num_seqs: int | None = None, global_tokens: float | None = None, max_len: int | None = None):
+    """Aggregate per-token losses of a packed micro-batch.
+
+    ``global_tokens`` (token-mean) / ``num_seqs`` (seq-mean-*) are the counts over
+    the whole mini-batch, so summing micro-batch losses gives the mini-batch mean.
+    """
+    m = mask.to(loss_mat.dtype)
+    if mode == "token-mean":
+        denom = global_tokens if global_tokens is not None else m.sum().clamp_min(1)
+        return (loss_mat * m).sum() / denom
+    assert seq_ids is not None, "seq-mean modes need per-token sequence ids"
+    nseq = int(seq_ids.max().item()) + 1 if seq_ids.numel() else 0
+    per_sum = torch.zeros(nseq, dtype=loss_mat.dtype, device=loss_mat.device).index_add_(0, seq_ids, loss_mat * m)
+    per_cnt = torch.zeros(nseq, dtype=loss_mat.dtype, device=loss_mat.device).index_add_(0, seq_ids, m)
+    denom = num_seqs if num_seqs is not None else max(nseq, 1)
+    if mode == "seq-mean-token-sum":
+        return per_sum.sum() / denom
+    if mode == "seq-mean-token-mean":
+        return (per_sum / per_cnt.clamp_min(1)).sum() / denom
+    if mode == "seq-mean-token-sum-norm":
+        return per_sum.sum() / (denom * (max_len or 1))
+    raise ValueError(f"unknown loss_agg_mode {mode!r}")
+
+
+def ppo_policy_loss(logp: torch.Tensor, old_logp: torch.Tensor, adv: torch.Tensor, mask: torch.Tensor,
+                    clip_low: float, clip_high: float, clip_c: float | None, agg_mode: str = "token-mean",
+                    tis_weight: torch.Tensor | None = None, **agg_kw):
+    """Clipped surrogate (DAPO clip-higher + dual clip).  Returns (loss, metrics)."""
+    neg_approx_kl = (logp - old_logp).clamp(-20.0, 20.0)
+    ratio = torch.exp(neg_approx_kl)
+    pg1 = -adv * ratio
+    pg2 = -adv * ratio.clamp(1.0 - clip_low, 1.0 + clip_high)
+    clipped = torch.maximum(pg1, pg2)
+    if clip_c is not None and clip_c > 1.0:
+        pg3 = -adv * clip_c
+        dual = torch.minimum(pg3, clipped)
+        pg = torch.where(adv < 0, dual, clipped)
+    else:
+        pg = clipped
+    if tis_weight is not None:
+        pg = pg * tis_weight
+    loss = agg_loss(pg, mask, agg_mode, **agg_kw)
+    with torch.no_grad():  # device tensors: no host sync inside the micro-batch loop
+        m = mask.float()
+        n = m.sum().clamp_min(1)
+        metrics = {
+            "pg_clipfrac": ((pg2 > pg1).float() * m).sum() / n,
+            "ppo_kl": (-neg_approx_kl * m).sum() / n,
+        }
+        if clip_c:
+            metrics["pg_clipfrac_lower"] = (((-adv * clip_c) < clipped).float() * (adv < 0).float() * m).sum() / n
+    return loss, metrics
+
+
+def value_loss(values: torch.Tensor, old_values: torch.Tensor, returns: torch.Tensor, mask: torch.Tensor,
+               cliprange: float, agg_mode: str = "token-mean", **agg_kw):
+    vclip = old_values + (values - old_values).clamp(-cliprange, cliprange)
+    l1 = (values - returns) ** 2
+    l2 = (vclip - returns) ** 2
+    loss = 0.5 * agg_loss(torch.maximum(l1, l2), mask, agg_mode, **agg_kw)
+    with torch.no_grad():
+        m = mask.float()
+        frac = ((l2 > l1).float() * m).sum() / m.sum().clamp_min(1)
+    return loss, {"vf_clipfrac": frac}
+
+
+def truncated_is_weight(old_logp: torch.Tensor, rollout_logp: torch.Tensor, cap: float) -> torch.Tensor:
+    """TIS: min(pi_old / pi_rollout, cap) per token (rollout correction)."""
+    return torch.exp((old_logp - rollout_logp).clamp(max=20.0)).clamp(max=cap).detach()
+
+
+def compute_advantages(estimator: str, *, scores: torch.Tensor, uids, gamma: float = 1.0, lam: float = 1.0,
+                       norm_by_std: bool = True, token_rewards=None, values=None, mask=None, lengths=None,
+                       score_components=None):
+    """Dispatch on ``algorithm.adv_estimator``; outcome estimators return [N],
+    token-level ones return [N, L]."""
+    if estimator == "grpo":
+        return grpo_outcome_advantage(scores, uids, norm_by_std)
+    if estimator == "rloo":
+        return rloo_advantage(scores, uids)
+    if estimator == "gdpo":
+        comps = score_components if score_components is not None else scores[:, None]
+        return gdpo_advantage(comps, uids)
+    if estimator == "optimal_token_baseline":
+        return optimal_token_baseline_advantage(scores, uids, lengths)
+    if estimator == "reinforce_plus_plus":
+        return reinforce_pp_returns(token_rewards, mask, gamma)
+    if estimator == "gae":
+        return gae_advantage(token_rewards, values, mask, gamma, lam)
+    raise ValueError(f"unknown adv_estimator {estimator!r}")

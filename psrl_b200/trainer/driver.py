@@ -1,0 +1,205 @@
+"""The RL driver: ``RLTrainer.fit`` / ``RLTrainer.step`` (C1/C2/C3).
+
+One training step consumes staleness buffer ``b = global_step``:
+
+1. wait until the buffer is READY (the rollout side keeps generating meanwhile);
+2. take its trajectories, compute advantages (GRPO / GAE / ...), optionally
+   recompute old log-probs, reference log-probs and values;
+3. update the critic and the actor (PPO-family loss);
+4. publish the new weights under the exclusive push lock and advance the PS
+   version to ``b + 1`` (which lets the dispatcher release more prompts and the
+   rollout instances sync).
+
+Placement:
+
+* **colocated** (one process / one GPU): the rollout engine and the trainer
+   share the device; waiting for a buffer means running engine steps, and the
+   weight sync is an in-HBM copy into the engine's fused-layout weights.
+* **disaggregated** (``torch.distributed.run``, N GPUs): ranks ``[0, n_train)``
+   train, the others serve rollout; see :mod:`psrl_b200.trainer.distributed`.
+
+Reference: ``PSRL_RayPPOTrainer.fit`` (``psrl/trainer/ppo/ray_trainer.py:3127``),
+``FullBatchStepStrategy.run_step`` (``psrl/trainer/ppo/strategies/full_batch.py:26``).
+"""
+
+from __future__ import annotations
+
+import time
+
+import torch
+
+from ..agent.data import DataProcessor
+from ..agent.manager import AgentLoopManager
+from ..config import redundant_settings
+from ..models import model_args_from_config
+from ..ps import PSManager
+from ..reward import RewardManager
+from ..rollout.engine import EngineWeights, RolloutEngine
+from ..rollout.instance import RolloutInstance, SyncPolicy
+from ..utils.events import EventLog
+from . import algos
+from .actor import PolicyWorker
+
+
+def resolve_device(cfg) -> torch.device:
+    d = cfg.trainer.get("device", "auto")
+    if d == "auto":
+        return torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+    return torch.device(d)
+
+
+def compute_batch_advantages(cfg, trajs) -> dict:
+    """Fill ``advantage`` / ``token_advantages`` / ``returns`` on the trajectories."""
+    est = cfg.algorithm.adv_estimator
+    if not trajs:
+        return {}
+    scores = torch.tensor([t.reward for t in trajs], dtype=torch.float32)
+    uids = [t.uid for t in trajs]
+    if est in ("grpo", "rloo", "gdpo", "optimal_token_baseline"):
+        lengths = torch.tensor([t.response_len for t in trajs])
+        adv = algos.compute_advantages(est, scores=scores, uids=uids, norm_by_std=bool(cfg.algorithm.norm_adv_by_std_in_grpo),
+                                       lengths=lengths)
+        for t, a in zip(trajs, adv.tolist()):
+            t.advantage = a
+            t.token_advantages = None
+    else:
+        L = max(t.response_len for t in trajs)
+        N = len(trajs)
+        rew = torch.zeros(N, L)
+        mask = torch.zeros(N, L)
+        vals = torch.zeros(N, L)
+        for i, t in enumerate(trajs):
+            n = t.response_len
+            mask[i, :n] = 1
+            rew[i, n - 1] = t.reward
+            if t.old_values is not None:
+                vals[i, :n] = torch.tensor(t.old_values[:n])
+        if est == "gae":
+            adv, ret = algos.gae_advantage(rew, vals, mask, float(cfg.algorithm.gamma), float(cfg.algorithm.lam))
+        else:
+            adv = algos.compute_advantages(est, scores=scores, uids=uids, token_rewards=rew, mask=mask,
+                                           gamma=float(cfg.algorithm.gamma))
+            ret = adv
+        for i, t in enumerate(trajs):
+            n = t.response_len
+            t.token_advantages = adv[i, :n].tolist()
+            t.returns = ret[i, :n].tolist()
+    return {"critic/score_mean": float(scores.mean()), "critic/score_max": float(scores.max()),
+            "critic/score_min": float(scores.min())}
+
+
+class RLTrainer:
+    """Colocated asynchronous RL trainer (one process drives trainer and rollout)."""
+
+    def __init__(self, cfg, device=None, seed: int | None = None, log: EventLog | None = None):
+        self.cfg = cfg
+        self.device = torch.device(device) if device is not None else resolve_device(cfg)
+        self.seed = int(cfg.trainer.seed if seed is None else seed)
+        self.log = log or EventLog()
+        self.args = model_args_from_config(cfg.model)
+        rn, alg_rn, _, _ = redundant_settings(cfg)
+        self.ps = PSManager.from_config(cfg)
+        self.data = DataProcessor(cfg, self.args.vocab_size, rn)
+        self.reward = RewardManager(cfg, self.data.tokenizer)
+        self.manager = AgentLoopManager(cfg, self.ps, self.data, self.reward)
+        self.actor = PolicyWorker(cfg, self.args, self.device, seed=self.seed)
+        self.critic = None
+        if cfg.critic.enable:
+            from dataclasses import replace
+            cargs = replace(self.args, value_head=True, tie_word_embeddings=False)
+            self.critic = PolicyWorker(cfg, cargs, self.device, seed=self.seed + 1)
+        self.ref = None
+        if cfg.actor.use_kl_loss or cfg.algorithm.use_kl_in_reward:
+            self.ref = PolicyWorker(cfg, self.args, self.device, seed=self.seed, trainable=False)
+        rc = cfg.rollout
+        self.engine_weights = EngineWeights.from_model(self.actor.model, self.device, dtype=self.actor.dtype)
+        max_len = int(rc.max_prompt_length) + int(rc.max_response_length) + 64
+        self.engine = RolloutEngine(
+            self.args, self.engine_weights, max_num_seqs=int(rc.max_num_seqs), max_model_len=max_len,
+            block_size=int(rc.block_size), max_num_batched_tokens=int(rc.max_num_batched_tokens),
+            kv_cache_gb=float(rc.get("kv_cache_gb", 4.0)), enable_prefix_caching=bool(rc.enable_prefix_caching),
+            use_cuda_graph=bool(rc.cuda_graph), keep_kv_on_update=bool(cfg.psrl.rollout_coordination.partial_rollout.get("keep_kv", False)),
+            eos_token_id=self.data.tokenizer.eos_id if not rc.ignore_eos else None)
+        sm = cfg.psrl.rollout_coordination.sync_and_mig_strategy
+        policy = SyncPolicy(sm.method, bool(cfg.psrl.rollout_coordination.partial_rollout.enable),
+                            sm.sync.get("threshold"), sm.sync.get("indicator", "request_num"))
+        self.instance_id = (0, 0)
+        self.ps.register_rollout_instance(self.instance_id, 0)
+        self.instance = RolloutInstance(self.instance_id, self.engine, self.manager, self._pull_weights,
+                                        self.ps.get_ps_model_version, policy)
+        self.global_step = 0
+        self.trained_tokens = 0
+
+    # ----------------------------------------------------------- weights
+    @torch.no_grad()
+    def _pull_weights(self, version: int) -> None:
+        if not self.ps.acquire_shared_pull(timeout=600):
+            raise TimeoutError("could not take the shared pull lock")
+        try:
+            v, _ = self.ps.pull_model(self.instance_id)
+            src = dict(self.actor.model.named_parameters())
+            for k, t in self.engine_weights.tensors.items():
+                if k in src:
+                    t.copy_(src[k].detach(), non_blocking=True)
+            self.engine.load_weights(None, v)
+        finally:
+            self.ps.release_shared_pull()
+
+    def _publish(self, version: int) -> None:
+        if not self.ps.acquire_exclusive_push(timeout=600):
+            raise TimeoutError("could not take the exclusive push lock")
+        try:
+            self.ps.push_model(version)
+        finally:
+            self.ps.release_exclusive_push()
+
+    # -------------------------------------------------------------- step
+    def wait_for_buffer(self, b: int, timeout_s: float = 3600.0) -> None:
+        t0 = time.monotonic()
+        while not self.manager.buffer_ready(b):
+            self.instance.pump()
+            if time.monotonic() - t0 > timeout_s:
+                raise TimeoutError(f"buffer {b} not ready after {timeout_s}s: {self.manager.snapshot()}")
+
+    def step(self) -> dict:
+        b = self.global_step
+        metrics: dict = {}
+        t0 = time.perf_counter()
+        with self.log.span("GEN", step=b):
+            self.wait_for_buffer(b)
+        t1 = time.perf_counter()
+        trajs = self.manager.consume(b)
+        idx = list(range(len(trajs)))
+        if self.critic is not None:
+            self.critic.compute_values(trajs, idx)
+        if self.ref is not None:
+            self.ref.compute_log_prob(trajs, idx, field="ref_logprobs")
+        if not self.cfg.psrl.log_prob.enable_rollout_engine_log_prob:
+            self.actor.compute_log_prob(trajs, idx, field="old_logprobs")
+        else:
+            for t in trajs:
+                t.old_logprobs = t.rollout_logprobs
+        metrics.update(compute_batch_advantages(self.cfg, trajs))
+        with self.log.span("TRAIN", step=b):
+            if self.critic is not None:
+                metrics.update(self.critic.update_critic(trajs))
+            metrics.update(self.actor.update_policy(trajs, float(self.cfg.rollout.temperature)))
+        t2 = time.perf_counter()
+        with self.log.span("PUSH", step=b):
+            self._publish(b + 1)
+        self.global_step += 1
+        ntok = sum(len(t.prompt_ids) + t.response_len for t in trajs)
+        self.trained_tokens += ntok
+        metrics.update({
+            "step": b, "num_trajectories": len(trajs), "trained_tokens": ntok,
+            "response_length/mean": sum(t.response_len for t in trajs) / max(1, len(trajs)),
+            "timing_s/gen_wait": t1 - t0, "timing_s/train": t2 - t1, "timing_s/step": time.perf_counter() - t0,
+            "ps_version": self.ps.get_ps_model_version(),
+            "staleness/max": max((b - t.version_tag) for t in trajs) if trajs else 0,
+        })
+        metrics.update({f"rollout/{k}": v for k, v in self.engine.engine_stats().items() if isinstance(v, (int, float))})
+        return metrics
+
+    def fit(self, num_steps: int | None = None) -> list[dict]:
+        n = int(num_steps if num_steps is not None else self.cfg.trainer.total_training_steps)
+        return [self.step() for _ in range(n)]
