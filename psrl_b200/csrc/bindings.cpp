@@ -30,6 +30,11 @@ std::vector<at::Tensor> attn_varlen_bwd(at::Tensor dO, at::Tensor q, at::Tensor 
 int64_t decode_num_splits(int64_t batch, int64_t nkv, int64_t max_ctx);
 at::Tensor attn_decode(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor block_table,
                        at::Tensor kv_lens, double scale, int64_t splits, c10::optional<at::Tensor> scratch);
+std::tuple<pybind11::bytes, int64_t> ipc_handle(at::Tensor t);
+at::Tensor ipc_open(pybind11::bytes handle, int64_t offset, int64_t numel, at::ScalarType dtype, int64_t src_device);
+void enable_peer_access(int64_t peer);
+void copy_segments(at::Tensor dst, std::vector<at::Tensor> srcs, std::vector<int64_t> dst_offsets_bytes,
+                   std::vector<int64_t> src_offsets_bytes, std::vector<int64_t> lengths_bytes);
 }  // namespace psrl
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -51,4 +56,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_varlen_bwd", &psrl::attn_varlen_bwd);
   m.def("decode_num_splits", &psrl::decode_num_splits);
   m.def("attn_decode", &psrl::attn_decode);
+  m.def("ipc_handle", &psrl::ipc_handle);
+  m.def("ipc_open", &psrl::ipc_open);
+  m.def("enable_peer_access", &psrl::enable_peer_access);
+  m.def("copy_segments", &psrl::copy_segments);
 }

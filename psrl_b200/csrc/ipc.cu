@@ -1,0 +1,142 @@
+// Peer-memory plumbing for the trainer -> rollout weight sync (K17).
+//
+//  ipc_handle / ipc_open : export a device allocation with cudaIpcGetMemHandle
+//    (the handle names the whole cudaMalloc'd range, so the tensor's offset
+//    inside it travels with the handle) and map it in another process with
+//    cudaIpcMemLazyEnablePeerAccess.  Mappings are cached per process.
+//  copy_segments : ONE kernel that gathers up to 16 byte ranges from local or
+//    peer device pointers into one destination buffer with 16-byte vector
+//    loads/stores; when a source is another GPU's memory the loads travel over
+//    NVLink (no copy engine, no staging, no TMA multicast).
+#include <cuda.h>
+#include <pybind11/pybind11.h>
+
+#include <map>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+
+namespace py = pybind11;
+
+namespace psrl {
+
+std::tuple<py::bytes, int64_t> ipc_handle(at::Tensor t) {
+  CHECK_CUDA_TENSOR(t);
+  at::cuda::CUDAGuard g(t.device());
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  CUresult r = cuMemGetAddressRange(&base, &size, (CUdeviceptr)t.data_ptr());
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuMemGetAddressRange failed (", (int)r, ")");
+  cudaIpcMemHandle_t h;
+  PSRL_CHECK_CUDA(cudaIpcGetMemHandle(&h, (void*)base));
+  const int64_t off = (int64_t)((CUdeviceptr)t.data_ptr() - base);
+  return {py::bytes(reinterpret_cast<const char*>(&h), sizeof(h)), off};
+}
+
+static std::mutex g_ipc_mu;
+static std::map<std::string, void*> g_ipc_open;
+
+at::Tensor ipc_open(py::bytes handle, int64_t offset, int64_t numel, at::ScalarType dtype, int64_t src_device) {
+  std::string key = handle;
+  TORCH_CHECK(key.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_ipc_mu);
+    auto it = g_ipc_open.find(key);
+    if (it != g_ipc_open.end()) {
+      base = it->second;
+    } else {
+      cudaIpcMemHandle_t h;
+      memcpy(&h, key.data(), sizeof(h));
+      PSRL_CHECK_CUDA(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+      g_ipc_open[key] = base;
+    }
+  }
+  // The mapping lives until process exit; the tensor only views it.  The tensor
+  // is tagged with the exporting device (pointer attributes resolve there).
+  auto opts = at::TensorOptions().dtype(dtype).device(at::kCUDA, src_device);
+  return at::from_blob(static_cast<char*>(base) + offset, {numel}, [](void*) {}, opts);
+}
+
+void enable_peer_access(int64_t peer) {
+  int dev;
+  cudaGetDevice(&dev);
+  if (dev == peer) return;
+  int can = 0;
+  cudaDeviceCanAccessPeer(&can, dev, (int)peer);
+  TORCH_CHECK(can, "device ", dev, " cannot access peer ", peer);
+  cudaError_t e = cudaDeviceEnablePeerAccess((int)peer, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();
+    return;
+  }
+  PSRL_CHECK_CUDA(e);
+}
+
+constexpr int MAX_SEG = 16;
+struct SegTable {
+  const uint4* src[MAX_SEG];
+  int64_t dst_off[MAX_SEG];  // in 16 B units
+  int64_t len[MAX_SEG];      // in 16 B units
+  int64_t start[MAX_SEG + 1];  // prefix sums of len
+  int n;
+};
+
+__global__ void __launch_bounds__(512) copy_segments_kernel(uint4* __restrict__ dst, SegTable t) {
+  const int64_t total = t.start[t.n];
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int seg = 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride * 4) {
+    uint4 v[4];
+    int64_t idx[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      idx[u] = i + u * stride;
+      if (idx[u] < total) {
+        while (seg + 1 < t.n && idx[u] >= t.start[seg + 1]) ++seg;
+        while (seg > 0 && idx[u] < t.start[seg]) --seg;
+        v[u] = t.src[seg][idx[u] - t.start[seg]];
+        idx[u] = t.dst_off[seg] + (idx[u] - t.start[seg]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (i + u * stride < total) dst[idx[u]] = v[u];
+  }
+}
+
+// dst: destination tensor (bytes are what matter); srcs: tensors (local or IPC-mapped peer views);
+// dst_offsets_bytes / lengths_bytes per source (multiples of 16).
+void copy_segments(at::Tensor dst, std::vector<at::Tensor> srcs, std::vector<int64_t> dst_offsets_bytes,
+                   std::vector<int64_t> src_offsets_bytes, std::vector<int64_t> lengths_bytes) {
+  CHECK_CUDA_TENSOR(dst);
+  const int n = srcs.size();
+  TORCH_CHECK(n <= MAX_SEG && n == (int)dst_offsets_bytes.size() && n == (int)lengths_bytes.size() &&
+                  n == (int)src_offsets_bytes.size(),
+              "bad segment lists");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(dst.data_ptr()) % 16 == 0, "dst must be 16-byte aligned");
+  SegTable t{};
+  t.n = n;
+  t.start[0] = 0;
+  const int64_t dst_bytes = dst.numel() * dst.element_size();
+  for (int i = 0; i < n; ++i) {
+    const char* sp = static_cast<const char*>(srcs[i].data_ptr()) + src_offsets_bytes[i];
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(sp) % 16 == 0, "source ", i, " not 16-byte aligned");
+    TORCH_CHECK(lengths_bytes[i] % 16 == 0 && dst_offsets_bytes[i] % 16 == 0, "lengths/offsets must be x16");
+    TORCH_CHECK(dst_offsets_bytes[i] + lengths_bytes[i] <= dst_bytes, "segment ", i, " overflows dst");
+    TORCH_CHECK(src_offsets_bytes[i] + lengths_bytes[i] <= srcs[i].numel() * srcs[i].element_size(),
+                "segment ", i, " overflows its source");
+    t.src[i] = reinterpret_cast<const uint4*>(sp);
+    t.dst_off[i] = dst_offsets_bytes[i] / 16;
+    t.len[i] = lengths_bytes[i] / 16;
+    t.start[i + 1] = t.start[i] + t.len[i];
+  }
+  if (t.start[n] == 0) return;
+  at::cuda::CUDAGuard g(dst.device());
+  const int grid = std::min<int64_t>(num_sms() * 4, (t.start[n] + 511) / 512);
+  copy_segments_kernel<<<grid, 512, 0, stream()>>>(reinterpret_cast<uint4*>(dst.data_ptr()), t);
+  PSRL_CHECK_LAUNCH();
+}
+
+}  // namespace psrl

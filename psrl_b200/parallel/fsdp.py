@@ -32,7 +32,8 @@ from .. import ops
 
 
 class _Bucket:
-    def __init__(self, names, params, world: int, rank: int, device, pad_to: int):
+    def __init__(self, names, params, world: int, rank: int, device, pad_to: int, flat: torch.Tensor,
+                 grad: torch.Tensor, base: int):
         self.names = names
         self.params = params
         n = sum(p.numel() for p in params)
@@ -41,9 +42,9 @@ class _Bucket:
         self.padded = padded
         self.shard = padded // world
         self.rank = rank
-        dtype = params[0].dtype
-        self.flat = torch.zeros(padded, dtype=dtype, device=device)
-        self.grad = torch.zeros(padded, dtype=torch.float32, device=device)
+        self.base = base                     # offset of this bucket in the model-wide flat buffer
+        self.flat = flat[base: base + padded]
+        self.grad = grad[base: base + padded]
         off = 0
         self.offsets = []
         for p in params:
@@ -90,10 +91,22 @@ class FlatShardedDP:
             groups[key].append((name, p))
         self.buckets: list[_Bucket] = []
         self.param_to_bucket: dict = {}
-        for key in order:
+        # one model-wide flat buffer (parameters) and one fp32 flat buffer (main grads);
+        # buckets are padded slices so every shard boundary is 64-element aligned
+        sizes = [math.ceil(sum(p.numel() for _, p in groups[k]) / pad_to) * pad_to for k in order]
+        self.total = sum(sizes)
+        dtype = next(model.parameters()).dtype
+        self.flat = torch.zeros(self.total, dtype=dtype, device=self.device)
+        self.flat_grad = torch.zeros(self.total, dtype=torch.float32, device=self.device)
+        base = 0
+        self.layout: list[tuple[str, tuple, int]] = []   # (name, shape, offset) in the flat buffer
+        for key, sz in zip(order, sizes):
             names = [n for n, _ in groups[key]]
             params = [p for _, p in groups[key]]
-            b = _Bucket(names, params, self.world, self.rank, self.device, pad_to)
+            b = _Bucket(names, params, self.world, self.rank, self.device, pad_to, self.flat, self.flat_grad, base)
+            for nm, p, off in zip(names, params, b.offsets):
+                self.layout.append((nm, tuple(p.shape), base + off))
+            base += sz
             for i, p in enumerate(params):
                 self.param_to_bucket[p] = (b, b.offsets[i])
             self.buckets.append(b)
@@ -107,8 +120,7 @@ class FlatShardedDP:
         p.grad = None
 
     def zero_grad(self) -> None:
-        for b in self.buckets:
-            b.grad.zero_()
+        self.flat_grad.zero_()
 
     # ---------------------------------------------------------------- step
     def current_lr(self) -> float:

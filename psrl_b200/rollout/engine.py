@@ -32,6 +32,7 @@ import torch
 import torch.nn.functional as F
 
 from .. import ops
+from ..utils import transfer
 from ..models.config import ModelArgs
 from .kv_cache import BlockManager, allocate_kv_tensors
 
@@ -171,6 +172,7 @@ class RolloutEngine:
         self.is_cuda = self.device.type == "cuda"
         self.use_cuda_graph = use_cuda_graph and self.is_cuda
         self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self._graph_launches: dict[int, int] = {}
         self._graph_pool = None
         self._alloc_static()
         # stats
@@ -383,6 +385,7 @@ class RolloutEngine:
         t_lens = torch.tensor(lens, dtype=torch.int32).to(dev, non_blocking=True)
         t_bt = torch.from_numpy(bt).to(dev, non_blocking=True)
         max_q = max(n for _, n in batch)
+        transfer.h2d(T * 16 + 8 * len(cu) + bt.nbytes)
         h = self._forward(t_ids, t_pos, t_slots, mode="prefill", cu_q=t_cu, kv_lens=t_lens, block_table=t_bt,
                           max_q=max_q)
         # sample for sequences whose prompt is now fully computed
@@ -404,6 +407,8 @@ class RolloutEngine:
             p0 = done_seqs[0].req.params
             tok, lp = ops.sample(logits, temps, seeds, streams, top_k=p0.top_k, top_p=p0.top_p)
             tok, lp = tok.tolist(), lp.tolist()
+            transfer.h2d(20 * len(done_seqs))
+            transfer.d2h(12 * len(done_seqs))
             for s, t, l in zip(done_seqs, tok, lp):
                 if self.enable_prefix_caching:
                     self.bm.register_full_blocks(s.blocks, s.tokens[: s.num_computed], s.registered_blocks)
@@ -479,17 +484,20 @@ class RolloutEngine:
             dst[:nb].copy_(src[:nb], non_blocking=True)
         mb = max(len(s.blocks) for s in self.running)
         self.s_bt[:nb, :mb].copy_(self.h_bt[:nb, :mb], non_blocking=True)
+        transfer.h2d(nb * (8 + 4 + 4 + 4 + 4 + 8 + 4 * mb))
         if self.use_cuda_graph:
             g = self._graphs.get(nb)
             if g is None:
                 g = self._capture(nb)
             g.replay()
+            ops._ext.add_launches(self._graph_launches[nb])
         else:
             self._decode_forward(nb)
         if self.is_cuda:
             self.h_out_tok[:nb].copy_(self.s_out_tok[:nb], non_blocking=True)
             self.h_out_lp[:nb].copy_(self.s_out_lp[:nb], non_blocking=True)
             torch.cuda.current_stream().synchronize()
+            transfer.d2h(nb * 12)
             tok = self.h_out_tok.numpy()[:B].tolist()
             lp = self.h_out_lp.numpy()[:B].tolist()
         else:
@@ -525,8 +533,10 @@ class RolloutEngine:
         g = torch.cuda.CUDAGraph()
         if self._graph_pool is None:
             self._graph_pool = torch.cuda.graph_pool_handle()
+        before = ops._ext.launches()
         with torch.cuda.graph(g, pool=self._graph_pool):
             self._decode_forward(nb)
+        self._graph_launches[nb] = ops._ext.launches() - before
         self._graphs[nb] = g
         return g
 

@@ -15,6 +15,8 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
+from ..utils import transfer
+
 
 @dataclass
 class Trajectory:
@@ -121,10 +123,16 @@ def build_micro_batch(trajs: list[Trajectory], idx: list[int], device, field_old
         seq.append(np.full(n, j, dtype=np.int64))
         cu.append(cu[-1] + n)
 
+    on_gpu = torch.device(device).type == "cuda"
+
     def cat(xs, dtype):
-        return torch.from_numpy(np.concatenate(xs)).to(device=device, dtype=dtype, non_blocking=True)
+        t = torch.from_numpy(np.concatenate(xs)).to(dtype)
+        if on_gpu:
+            t = t.pin_memory()
+        return t.to(device=device, non_blocking=True)
 
     lens = [cu[k + 1] - cu[k] for k in range(len(idx))]
+    transfer.h2d(cu[-1] * 40 + 4 * len(cu))
     return MicroBatch(
         input_ids=cat(ids, torch.long), positions=cat(pos, torch.int32),
         cu_seqlens=torch.tensor(cu, dtype=torch.int32).to(device), max_seqlen=max(lens) if lens else 0,
