@@ -130,7 +130,9 @@ __global__ void __launch_bounds__(LP_THREADS)
   const int64_t row = blockIdx.x;
   T* z = logits + row * ld;
   const float L = lse[row];
-  const float gl = glp ? glp[row] : 0.f;
+  const int64_t lab0 = labels[row];
+  // rows without a label contribute no log-prob term (forward wrote lp = 0)
+  const float gl = (glp && lab0 >= 0 && lab0 < V) ? glp[row] : 0.f;
   const float ge = gent ? gent[row] : 0.f;
   const float H = (gent && ent) ? ent[row] : 0.f;
   const int64_t lab = labels[row];

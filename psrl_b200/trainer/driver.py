@@ -202,4 +202,34 @@ class RLTrainer:
 
     def fit(self, num_steps: int | None = None) -> list[dict]:
         n = int(num_steps if num_steps is not None else self.cfg.trainer.total_training_steps)
-        return [self.step() for _ in range(n)]
+        if self.cfg.trainer.resume_mode != "disable" and self.global_step == 0:
+            self.resume()
+        out = []
+        for _ in range(n):
+            out.append(self.step())
+            freq = int(self.cfg.trainer.save_freq)
+            if freq > 0 and self.global_step % freq == 0:
+                self.save_checkpoint()
+        return out
+
+    # -------------------------------------------------------- checkpoints
+    def save_checkpoint(self) -> str:
+        from ..utils.checkpoint import save_checkpoint
+        return save_checkpoint(self.cfg.trainer.default_local_dir, self.global_step, self.actor, self.data,
+                               self.critic, self.ps.get_ps_model_version(),
+                               use_dcp=bool(self.cfg.psrl.checkpoint.use_dcp_save))
+
+    def resume(self, step: int | None = None) -> int:
+        """Load weights/optimizer/data cursor and re-seat the PS at that version."""
+        from ..utils.checkpoint import find_latest, load_checkpoint
+        root = self.cfg.trainer.get("resume_from_path") or self.cfg.trainer.default_local_dir
+        if step is None and find_latest(root) is None:
+            return 0
+        step = load_checkpoint(root, self.actor, self.data, self.critic, step,
+                               use_dcp=bool(self.cfg.psrl.checkpoint.use_dcp_save))
+        self.global_step = step
+        self.ps.init_model_version_for_resume(step + 1)
+        self.manager.initial_ps_version = step
+        self.manager.request_counter = 0
+        self._pull_weights(self.ps.get_ps_model_version())
+        return step

@@ -1,0 +1,94 @@
+"""Checkpoint / resume (reference: ``ray_trainer.py:2413-2560``, C36).
+
+Layout under ``trainer.default_local_dir``::
+
+    global_step_{N}/actor/config.json, model*.safetensors   (HF format, rank 0)
+    global_step_{N}/actor/dcp/                             (torch DCP, when use_dcp_save)
+    global_step_{N}/actor/optim_rank{r}.pt                  (per-rank optimizer shard)
+    global_step_{N}/critic/...                              (same, if a critic exists)
+    global_step_{N}/data.pt                                 (data cursor, PS version)
+    latest_checkpointed_iteration.txt
+
+The optimizer state is saved per rank (the reference's per-rank Megatron save
+avoids DCP's collective object gathers); model weights are saved in HF format
+and, optionally, as a torch Distributed Checkpoint.  Resuming at step N sets the
+PS version to N (the version after N trainer steps).
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+
+from ..models.hf_io import load_hf_into, save_hf
+
+LATEST = "latest_checkpointed_iteration.txt"
+
+
+def step_dir(root: str, step: int) -> str:
+    return os.path.join(os.path.expanduser(root), f"global_step_{step}")
+
+
+def save_worker(worker, path: str, rank: int = 0, use_dcp: bool = False) -> None:
+    os.makedirs(path, exist_ok=True)
+    if rank == 0:
+        save_hf(worker.model, path)
+    if use_dcp:
+        import torch.distributed.checkpoint as dcp
+        sd = {k: v.detach() for k, v in worker.model.state_dict().items()}
+        dcp.save(sd, checkpoint_id=os.path.join(path, "dcp"))
+    if worker.dp is not None:
+        torch.save(worker.dp.optimizer_state(), os.path.join(path, f"optim_rank{rank}.pt"))
+
+
+def load_worker(worker, path: str, rank: int = 0, use_dcp: bool = False) -> None:
+    if use_dcp and os.path.isdir(os.path.join(path, "dcp")):
+        import torch.distributed.checkpoint as dcp
+        sd = {k: v.detach() for k, v in worker.model.state_dict().items()}
+        dcp.load(sd, checkpoint_id=os.path.join(path, "dcp"))
+    else:
+        load_hf_into(worker.model, path)
+    opt = os.path.join(path, f"optim_rank{rank}.pt")
+    if worker.dp is not None:
+        if os.path.exists(opt):
+            worker.dp.load_optimizer_state(torch.load(opt, map_location="cpu", weights_only=False))
+        else:
+            worker.dp.sync_master_from_params()
+
+
+def save_checkpoint(root: str, step: int, actor, data=None, critic=None, ps_version: int | None = None,
+                    rank: int = 0, use_dcp: bool = False) -> str:
+    d = step_dir(root, step)
+    save_worker(actor, os.path.join(d, "actor"), rank, use_dcp)
+    if critic is not None:
+        save_worker(critic, os.path.join(d, "critic"), rank, use_dcp)
+    if rank == 0:
+        torch.save({"data": data.state_dict() if data is not None else None, "ps_version": ps_version,
+                    "global_step": step}, os.path.join(d, "data.pt"))
+        with open(os.path.join(os.path.expanduser(root), LATEST), "w") as fh:
+            fh.write(str(step))
+    return d
+
+
+def find_latest(root: str) -> int | None:
+    p = os.path.join(os.path.expanduser(root), LATEST)
+    if not os.path.exists(p):
+        return None
+    with open(p) as fh:
+        return int(fh.read().strip())
+
+
+def load_checkpoint(root: str, actor, data=None, critic=None, step: int | None = None, rank: int = 0,
+                    use_dcp: bool = False) -> int:
+    step = find_latest(root) if step is None else step
+    if step is None:
+        raise FileNotFoundError(f"no checkpoint under {root}")
+    d = step_dir(root, step)
+    load_worker(actor, os.path.join(d, "actor"), rank, use_dcp)
+    if critic is not None:
+        load_worker(critic, os.path.join(d, "critic"), rank, use_dcp)
+    meta = torch.load(os.path.join(d, "data.pt"), weights_only=False)
+    if data is not None and meta.get("data"):
+        data.load_state_dict(meta["data"])
+    return int(meta["global_step"])
