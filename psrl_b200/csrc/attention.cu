@@ -978,3 +978,88 @@ at::Tensor attn_decode(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at:
 }
 
 }  // namespace psrl
+
+// ------------------------------------------------------------------------------
+// Allocation-free variant of the paged decode entry point (declared in
+// noalloc.h, which documents the contract).  It has no counterpart in the
+// reference.  It reuses decode_kernel / decode_combine_kernel unchanged; only the
+// split scratch comes from the file-scope array below instead of a caller-
+// or torch-allocated buffer.
+#include <mutex>
+
+#include "noalloc.h"
+
+namespace psrl {
+namespace attn {
+
+constexpr long long NOALLOC_SCRATCH_FLOATS = PSRL_NOALLOC_SCRATCH_BYTES / 4;
+static __device__ __align__(256) float g_noalloc_scratch[NOALLOC_SCRATCH_FLOATS];
+
+constexpr int NOALLOC_MAX_DEVICES = 64;
+static float* g_noalloc_ptr[NOALLOC_MAX_DEVICES];  // device address of the scratch, per device
+static std::mutex g_noalloc_mu;
+
+// Once per device, with that device current: resolve the scratch array's device
+// address (in host code its name is only a host-side stand-in) and allow the
+// decode kernel its dynamic shared memory.
+static int noalloc_setup(int dev, float** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return PSRL_NOALLOC_ECUDA;
+    if (cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dec_smem()) !=
+        cudaSuccess)
+      return PSRL_NOALLOC_ECUDA;
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return PSRL_NOALLOC_OK;
+}
+
+}  // namespace attn
+}  // namespace psrl
+
+extern "C" __attribute__((visibility("default"))) int psrl_decode_attention_noalloc(
+    const void* q, const void* k_cache, const void* v_cache, const int* block_table, const int* kv_lens, void* out,
+    int batch, int num_heads, int num_kv_heads, int head_dim, int block_size, int max_blocks, int splits,
+    float scale, void* stream) {
+  using namespace psrl;
+  using namespace psrl::attn;
+  if (!q || !k_cache || !v_cache || !block_table || !kv_lens || !out) return PSRL_NOALLOC_EBADARG;
+  if (head_dim != D || batch < 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0 ||
+      num_heads / num_kv_heads > 16 || block_size <= 0 || max_blocks <= 0 || splits < 1 || splits > 32)
+    return PSRL_NOALLOC_EBADARG;
+  const long long need = splits > 1 ? (long long)batch * num_heads * splits * (D + 1) : 0;
+  if (need > NOALLOC_SCRATCH_FLOATS) return PSRL_NOALLOC_ETOOBIG;
+  if (batch == 0) return PSRL_NOALLOC_OK;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= NOALLOC_MAX_DEVICES) return PSRL_NOALLOC_ECUDA;
+  float* scratch = nullptr;
+  int rc = noalloc_setup(dev, &scratch);
+  if (rc != PSRL_NOALLOC_OK) return rc;
+  DecodeParams p{};
+  p.q = static_cast<const bf16*>(q);
+  p.kc = static_cast<const bf16*>(k_cache);
+  p.vc = static_cast<const bf16*>(v_cache);
+  p.block_table = block_table;
+  p.kv_lens = kv_lens;
+  p.max_blocks = max_blocks;
+  p.block_size = block_size;
+  p.nq = num_heads;
+  p.nkv = num_kv_heads;
+  p.splits = splits;
+  p.scale = scale;
+  p.o = static_cast<bf16*>(out);
+  if (splits > 1) {
+    p.part_o = scratch;
+    p.part_lse = scratch + (long long)batch * num_heads * splits * D;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  decode_kernel<<<dim3(batch, num_kv_heads, splits), NTHREADS, dec_smem(), st>>>(p);
+  if (cudaPeekAtLastError() != cudaSuccess) return PSRL_NOALLOC_ECUDA;
+  if (splits > 1) {
+    decode_combine_kernel<<<batch * num_heads, D, 0, st>>>(p.part_o, p.part_lse, p.o, splits);
+    if (cudaPeekAtLastError() != cudaSuccess) return PSRL_NOALLOC_ECUDA;
+  }
+  return PSRL_NOALLOC_OK;
+}
