@@ -77,6 +77,7 @@ def run_colocated(args) -> dict:
 
     cfg = build_cfg(args, 1)
     t = RLTrainer(cfg)
+    t.engine.capture_all()
     for _ in range(args.warmup):
         t.step()
     torch.cuda.synchronize()
@@ -96,6 +97,7 @@ def run_colocated(args) -> dict:
     wall = time.perf_counter() - w0
     clocks = sampler.stop()
     ms = start.elapsed_time(end)
+    t.stop_rollout()
     b1, o1 = transfer.snapshot()
     tokens = t.trained_tokens - tok0
     return {

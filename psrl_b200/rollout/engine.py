@@ -534,11 +534,29 @@ class RolloutEngine:
         if self._graph_pool is None:
             self._graph_pool = torch.cuda.graph_pool_handle()
         before = ops._ext.launches()
-        with torch.cuda.graph(g, pool=self._graph_pool):
+        # thread-local capture: a trainer thread may be launching work concurrently
+        with torch.cuda.graph(g, pool=self._graph_pool, capture_error_mode="thread_local"):
             self._decode_forward(nb)
         self._graph_launches[nb] = ops._ext.launches() - before
         self._graphs[nb] = g
         return g
+
+    def capture_all(self) -> None:
+        """Capture the decode graph of every batch bucket up front (before any
+        concurrent work starts on the device)."""
+        if not self.use_cuda_graph:
+            return
+        for b in (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256, 320, 384, 448, 512):
+            nb = min(b, self.max_num_seqs)
+            if nb not in self._graphs:
+                self.h_lens.numpy()[:nb] = 1
+                self.h_slots.numpy()[:nb] = -1
+                self.s_lens[:nb].copy_(self.h_lens[:nb])
+                self.s_slots[:nb].copy_(self.h_slots[:nb])
+                self.s_bt[:nb].zero_()
+                self._capture(nb)
+            if b >= self.max_num_seqs:
+                break
 
     # ------------------------------------------------------------- forward
     def _forward(self, ids, pos, slots, *, mode, cu_q=None, kv_lens=None, block_table=None, max_q=0, splits=1):

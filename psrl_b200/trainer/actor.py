@@ -88,7 +88,13 @@ class PolicyWorker:
         per = max(1, int(self.cfg.actor.ppo_mini_batch_size))
         return [[i for g in groups[s: s + per] for i in g] for s in range(0, len(groups), per)]
 
-    def update_policy(self, trajs: list[Trajectory], temperature: float = 1.0) -> dict:
+    def update_policy(self, trajs: list[Trajectory], temperature: float = 1.0, step_guard=None,
+                      sync_every_micro_batch: bool = False) -> dict:
+        """PPO-family update.  ``step_guard`` (a context manager) wraps each
+        optimizer step, i.e. the in-place parameter update (the PS exclusive-push
+        lock when a colocated rollout reads the parameters concurrently)."""
+        import contextlib
+        guard = step_guard if step_guard is not None else contextlib.nullcontext
         ac = self.cfg.actor
         self.model.train()
         stats: dict[str, list] = {}
@@ -124,7 +130,13 @@ class PolicyWorker:
                         m["entropy"] = (ent.detach() * mb.loss_mask).sum() / global_tokens
                     for k, v in m.items():
                         stats.setdefault(k, []).append(v)
-                st = self.dp.step()
+                    if sync_every_micro_batch and self.device.type == "cuda":
+                        # bounded launch queue: the host thread releases the GIL here
+                        torch.cuda.current_stream().synchronize()
+                with guard():
+                    st = self.dp.step()
+                    if self.device.type == "cuda":
+                        torch.cuda.current_stream().synchronize()
                 stats.setdefault("grad_norm", []).append(st["grad_norm"])
                 stats.setdefault("lr", []).append(torch.tensor(st["lr"]))
         out = {}

@@ -129,6 +129,13 @@ class RLTrainer:
                                         self.ps.get_ps_model_version, policy)
         self.global_step = 0
         self.trained_tokens = 0
+        # overlapped colocation: the engine runs in its own thread on a high-priority
+        # stream while the trainer trains (bounded by the staleness protocol)
+        self.overlap = bool(cfg.psrl.deployment.get("colocate_overlap", True)) and self.device.type == "cuda"
+        self._rollout_thread = None
+        self._rollout_stop = False
+        self._rollout_error: BaseException | None = None
+        self.rollout_stream = torch.cuda.Stream(device=self.device, priority=-1) if self.overlap else None
 
     # ----------------------------------------------------------- weights
     @torch.no_grad()
@@ -141,9 +148,48 @@ class RLTrainer:
             for k, t in self.engine_weights.tensors.items():
                 if k in src:
                     t.copy_(src[k].detach(), non_blocking=True)
+            if self.device.type == "cuda":
+                torch.cuda.current_stream().synchronize()
             self.engine.load_weights(None, v)
         finally:
             self.ps.release_shared_pull()
+
+    # ------------------------------------------------------- rollout thread
+    def _rollout_loop(self) -> None:
+        try:
+            with torch.cuda.stream(self.rollout_stream):
+                while not self._rollout_stop:
+                    self.instance.pump()
+                    if not self.engine.has_unfinished():
+                        time.sleep(0.0005)
+        except BaseException as exc:  # surfaced to the trainer thread
+            self._rollout_error = exc
+
+    def start_rollout(self) -> None:
+        if self.overlap and self._rollout_thread is None:
+            import threading
+            self._rollout_stop = False
+            self._rollout_thread = threading.Thread(target=self._rollout_loop, daemon=True, name="rollout")
+            self._rollout_thread.start()
+
+    def stop_rollout(self) -> None:
+        if self._rollout_thread is not None:
+            self._rollout_stop = True
+            self._rollout_thread.join()
+            self._rollout_thread = None
+
+    def _push_guard(self):
+        import contextlib
+
+        @contextlib.contextmanager
+        def guard():
+            if not self.ps.acquire_exclusive_push(timeout=600):
+                raise TimeoutError("could not take the exclusive push lock")
+            try:
+                yield
+            finally:
+                self.ps.release_exclusive_push()
+        return guard
 
     def _publish(self, version: int) -> None:
         if not self.ps.acquire_exclusive_push(timeout=600):
@@ -156,8 +202,15 @@ class RLTrainer:
     # -------------------------------------------------------------- step
     def wait_for_buffer(self, b: int, timeout_s: float = 3600.0) -> None:
         t0 = time.monotonic()
+        if self.overlap:
+            self.start_rollout()
         while not self.manager.buffer_ready(b):
-            self.instance.pump()
+            if self.overlap:
+                if self._rollout_error is not None:
+                    raise RuntimeError("rollout thread failed") from self._rollout_error
+                time.sleep(0.002)
+            else:
+                self.instance.pump()
             if time.monotonic() - t0 > timeout_s:
                 raise TimeoutError(f"buffer {b} not ready after {timeout_s}s: {self.manager.snapshot()}")
 
@@ -183,7 +236,9 @@ class RLTrainer:
         with self.log.span("TRAIN", step=b):
             if self.critic is not None:
                 metrics.update(self.critic.update_critic(trajs))
-            metrics.update(self.actor.update_policy(trajs, float(self.cfg.rollout.temperature)))
+            metrics.update(self.actor.update_policy(
+                trajs, float(self.cfg.rollout.temperature),
+                step_guard=self._push_guard() if self.overlap else None, sync_every_micro_batch=self.overlap))
         t2 = time.perf_counter()
         with self.log.span("PUSH", step=b):
             self._publish(b + 1)
