@@ -66,6 +66,7 @@ class AdditionSource:
     def __init__(self, tokenizer: CharTokenizer, seed: int):
         self.tok = tokenizer
         self.seed = seed
+        self.vocab = tokenizer.vocab_size
 
     def item(self, uid: int) -> PromptItem:
         rng = random.Random(self.seed * 1_000_003 + uid)

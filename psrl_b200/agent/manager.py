@@ -48,8 +48,12 @@ class _Group:
 
 
 class AgentLoopManager:
-    def __init__(self, cfg, ps: PSManager, data: DataProcessor, reward, initial_ps_version: int = 0):
+    def __init__(self, cfg, ps: PSManager, data: DataProcessor, reward, initial_ps_version: int = 0,
+                 agent_loop=None):
+        from .loops import build_agent_loop
         self.cfg = cfg
+        self.loop = agent_loop if agent_loop is not None else build_agent_loop(cfg, data.src.vocab
+                                                                               if hasattr(data.src, "vocab") else 1024)
         self.ps = ps
         self.data = data
         self.reward = reward
@@ -126,10 +130,13 @@ class AgentLoopManager:
                 self.ps.reserve_rollout_instance_requests(instance_id, rid, instance_version)
                 self.ps.update_request_status(rid, RequestStatus.ROLLOUT_RUNNING, model_version=instance_version,
                                               rollout_instance_id=instance_id)
-                # a request (re)starting on an instance takes that instance's version
-                req.version_tag = instance_version
-                if req.prev_output_ids:
-                    self.ps.update_request_version_tag(rid, instance_version)
+                # a fresh or partially generated request (re)starts at the instance's
+                # version (partial rollouts are promoted); a later turn of a
+                # multi-turn session keeps the version pinned at its first turn
+                if req.meta.get("turn", 0) == 0:
+                    req.version_tag = instance_version
+                    if req.prev_output_ids:
+                        self.ps.update_request_version_tag(rid, instance_version)
                 out.append(req)
             return out
 
@@ -137,9 +144,9 @@ class AgentLoopManager:
     def on_complete(self, outputs: list[RequestOutput], instance_id=None) -> None:
         with self.lock:
             for o in outputs:
-                self._complete_one(o)
+                self._complete_one(o, instance_id)
 
-    def _complete_one(self, o: RequestOutput) -> None:
+    def _complete_one(self, o: RequestOutput, instance_id=None) -> None:
         rid = o.request_id
         uid = rid // self.rollout_n
         g = self.groups.get(uid)
@@ -155,14 +162,20 @@ class AgentLoopManager:
         if st is None:
             self._member_dropped(rid)
             return
+        if self.loop.multi_turn:
+            nxt = self.loop.on_turn_complete(o, instance_id)
+            if nxt is not None:
+                self.queue.appendleft(nxt)       # next turn, sticky to this instance
+                return
+        sample = self.loop.finalize(o)
         # the engine promotes the tag when it re-prefills after a weight update
         self.ps.update_request_version_tag(rid, o.version_tag)
         if not self.ps.update_request_status(rid, RequestStatus.ROLLOUT_COMPLETED, model_version=o.version_tag):
             self._member_dropped(rid)
             return
-        traj = Trajectory(uid=uid, request_id=rid, prompt_ids=list(o.prompt_ids), response_ids=list(o.output_ids),
-                          rollout_logprobs=list(o.logprobs), versions=list(o.versions), version_tag=o.version_tag,
-                          meta=dict(o.meta))
+        traj = Trajectory(uid=uid, request_id=rid, prompt_ids=sample["prompt_ids"], response_ids=sample["response_ids"],
+                          rollout_logprobs=sample["logprobs"], versions=sample["versions"], version_tag=o.version_tag,
+                          response_mask=sample["response_mask"], meta={**o.meta, "turns": sample["turns"]})
         self.ps.update_request_status(rid, RequestStatus.REWARD_RUNNING)
         sc = self.reward.score(traj)
         traj.reward = float(sc["score"])
@@ -182,6 +195,8 @@ class AgentLoopManager:
                               ignore_eos=bool(rp.ignore_eos), seed=o.request_id * 7919 + 17)
 
     def _member_dropped(self, rid: int) -> None:
+        if getattr(self.loop, "multi_turn", False):
+            self.loop.drop(rid)
         uid = rid // self.rollout_n
         g = self.groups.get(uid)
         if g is None:

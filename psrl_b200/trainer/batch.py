@@ -34,6 +34,7 @@ class Trajectory:
     old_values: list | None = None
     ref_logprobs: list | None = None
     old_logprobs: list | None = None
+    response_mask: list | None = None   # multi-turn: 0 on environment tokens
     meta: dict = field(default_factory=dict)
 
     @property
@@ -108,7 +109,7 @@ def build_micro_batch(trajs: list[Trajectory], idx: list[int], device, field_old
         lab = np.asarray(toks[1:], dtype=np.int64)
         labels.append(lab)
         m = np.zeros(n, dtype=np.float32)
-        m[P - 1:] = 1.0
+        m[P - 1:] = 1.0 if t.response_mask is None else np.asarray(t.response_mask, dtype=np.float32)
         mask.append(m)
         o = np.zeros(n, dtype=np.float32)
         src = getattr(t, field_old) if getattr(t, field_old) is not None else t.rollout_logprobs
