@@ -266,6 +266,25 @@ class AgentLoopManager:
             st = self.ps.get_buffer_status(buffer_id)
             return st in (BufferStatus.READY, BufferStatus.READY_WITH_CAPACITY)
 
+    def occupied_prefix(self, buffer_id: int) -> int:
+        """Number of committed (OCCUPIED) entries at the head of a buffer's training region."""
+        with self.lock:
+            self.ps.ensure_train_buffer_exists(buffer_id)
+            buf = self.ps.staleness_inventory.buffers.get(buffer_id)
+            return 0 if buf is None else min(buf.get_first_non_occupied(), buf.ready_num_entries)
+
+    def peek(self, buffer_id: int, lo: int, hi: int) -> list[Trajectory]:
+        """Trajectories of entries [lo, hi) of a buffer without consuming them
+        (the objects are shared with what ``consume`` later returns)."""
+        with self.lock:
+            buf = self.ps.staleness_inventory.buffers[buffer_id]
+            out: list[Trajectory] = []
+            for e in buf.entries[lo:hi]:
+                info = e.entry_info
+                keep = set(info.get_all_request_ids(self.rollout_n))
+                out.extend(t for t in self.store.get(info.prompt_id, []) if t.request_id in keep)
+            return out
+
     def consume(self, buffer_id: int) -> list[Trajectory]:
         with self.lock:
             entries = self.ps.consume_buffer(buffer_id)

@@ -136,6 +136,8 @@ class RLTrainer:
         self._rollout_stop = False
         self._rollout_error: BaseException | None = None
         self.rollout_stream = torch.cuda.Stream(device=self.device, priority=-1) if self.overlap else None
+        from .strategies import build_step_strategy
+        self.strategy = build_step_strategy(self)
 
     # ----------------------------------------------------------- weights
     @torch.no_grad()
@@ -218,28 +220,7 @@ class RLTrainer:
         b = self.global_step
         metrics: dict = {}
         t0 = time.perf_counter()
-        with self.log.span("GEN", step=b):
-            self.wait_for_buffer(b)
-        t1 = time.perf_counter()
-        trajs = self.manager.consume(b)
-        idx = list(range(len(trajs)))
-        if self.critic is not None:
-            self.critic.compute_values(trajs, idx)
-        if self.ref is not None:
-            self.ref.compute_log_prob(trajs, idx, field="ref_logprobs")
-        if not self.cfg.psrl.log_prob.enable_rollout_engine_log_prob:
-            self.actor.compute_log_prob(trajs, idx, field="old_logprobs")
-        else:
-            for t in trajs:
-                t.old_logprobs = t.rollout_logprobs
-        metrics.update(compute_batch_advantages(self.cfg, trajs))
-        with self.log.span("TRAIN", step=b):
-            if self.critic is not None:
-                metrics.update(self.critic.update_critic(trajs))
-            metrics.update(self.actor.update_policy(
-                trajs, float(self.cfg.rollout.temperature),
-                step_guard=self._push_guard() if self.overlap else None, sync_every_micro_batch=self.overlap))
-        t2 = time.perf_counter()
+        trajs = self.strategy.run_step(b, metrics)
         with self.log.span("PUSH", step=b):
             self._publish(b + 1)
         self.global_step += 1
@@ -248,7 +229,7 @@ class RLTrainer:
         metrics.update({
             "step": b, "num_trajectories": len(trajs), "trained_tokens": ntok,
             "response_length/mean": sum(t.response_len for t in trajs) / max(1, len(trajs)),
-            "timing_s/gen_wait": t1 - t0, "timing_s/train": t2 - t1, "timing_s/step": time.perf_counter() - t0,
+            "timing_s/step": time.perf_counter() - t0,
             "ps_version": self.ps.get_ps_model_version(),
             "staleness/max": max((b - t.version_tag) for t in trajs) if trajs else 0,
         })

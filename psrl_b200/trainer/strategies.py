@@ -1,0 +1,140 @@
+"""Step strategies: how one training step pipelines its stages (C3).
+
+``STAGE_META`` tags each stage:
+
+* ``per_sample``     — may run on a chunk as soon as it arrives (old/ref
+  log-probs, values, reward);
+* ``batch_coupled``  — needs the whole (group-complete) batch (advantages);
+* ``optimizer_step`` — parameter updates.
+
+``FullBatchStepStrategy`` waits for the whole staleness buffer, then runs the
+stages in order.  ``FineGrainOverlapStrategy`` consumes the buffer in chunks
+while it fills: with ``overlap_scope=recompute`` the per-sample stages run on
+each arrived chunk (their cost hides under rollout time); with
+``overlap_scope=pre_step`` at ``mini_batch`` granularity each arrived
+mini-batch is also advantage-normalised and trained on immediately (its own
+optimizer step).  Reference: ``psrl/trainer/ppo/strategies/``.
+"""
+
+from __future__ import annotations
+
+import time
+
+STAGE_META: dict[str, str] = {
+    "old_log_prob": "per_sample",
+    "ref_log_prob": "per_sample",
+    "values": "per_sample",
+    "reward": "per_sample",
+    "advantage": "batch_coupled",
+    "update_actor": "optimizer_step",
+    "update_critic": "optimizer_step",
+}
+
+
+class StepStrategy:
+    def __init__(self, trainer):
+        self.t = trainer
+
+    # per-sample stages on a list of trajectories
+    def per_sample(self, trajs) -> None:
+        t = self.t
+        idx = list(range(len(trajs)))
+        if not trajs:
+            return
+        if t.critic is not None:
+            t.critic.compute_values(trajs, idx)
+        if t.ref is not None:
+            t.ref.compute_log_prob(trajs, idx, field="ref_logprobs")
+        if not t.cfg.psrl.log_prob.enable_rollout_engine_log_prob:
+            t.actor.compute_log_prob(trajs, idx, field="old_logprobs")
+        else:
+            for x in trajs:
+                x.old_logprobs = x.rollout_logprobs
+
+    def optimize(self, trajs, metrics: dict) -> None:
+        from .driver import compute_batch_advantages
+        t = self.t
+        metrics.update(compute_batch_advantages(t.cfg, trajs))
+        with t.log.span("TRAIN", step=t.global_step):
+            if t.critic is not None:
+                metrics.update(t.critic.update_critic(trajs))
+            metrics.update(t.actor.update_policy(
+                trajs, float(t.cfg.rollout.temperature),
+                step_guard=t._push_guard() if t.overlap else None, sync_every_micro_batch=t.overlap))
+
+    def run_step(self, buffer_id: int, metrics: dict):
+        raise NotImplementedError
+
+
+class FullBatchStepStrategy(StepStrategy):
+    def run_step(self, buffer_id, metrics):
+        t0 = time.perf_counter()
+        with self.t.log.span("GEN", step=buffer_id):
+            self.t.wait_for_buffer(buffer_id)
+        t1 = time.perf_counter()
+        trajs = self.t.manager.consume(buffer_id)
+        self.per_sample(trajs)
+        self.optimize(trajs, metrics)
+        metrics["timing_s/gen_wait"] = t1 - t0
+        metrics["timing_s/train"] = time.perf_counter() - t1
+        return trajs
+
+
+def resolve_fine_grain_chunk_size(cfg) -> tuple[str, int]:
+    fgo = cfg.psrl.fine_grain_overlap
+    mini = int(cfg.actor.ppo_mini_batch_size)
+    if fgo.granularity == "mini_batch":
+        return "mini_batch", max(1, mini)
+    mult = max(1, int(fgo.multiplier))
+    return "micro_batch", max(1, mini // mult)
+
+
+class FineGrainOverlapStrategy(StepStrategy):
+    def __init__(self, trainer):
+        super().__init__(trainer)
+        self.granularity, self.chunk_groups = resolve_fine_grain_chunk_size(trainer.cfg)
+        self.scope = trainer.cfg.psrl.fine_grain_overlap.overlap_scope
+        if self.scope == "pre_step" and self.granularity != "mini_batch":
+            raise ValueError("pre_step overlap needs mini_batch granularity")
+
+    def run_step(self, buffer_id, metrics):
+        t = self.t
+        t0 = time.perf_counter()
+        done_entries = 0
+        trained: list = []
+        nchunks = 0
+        ready_entries = t.manager.ready_entries
+        if t.overlap:
+            t.start_rollout()
+        while True:
+            ready = t.manager.buffer_ready(buffer_id)
+            avail = t.manager.occupied_prefix(buffer_id)
+            while avail - done_entries >= self.chunk_groups or (ready and avail > done_entries):
+                n = min(self.chunk_groups, avail - done_entries)
+                chunk = t.manager.peek(buffer_id, done_entries, done_entries + n)
+                self.per_sample(chunk)
+                if self.scope == "pre_step":
+                    self.optimize(chunk, metrics)
+                    trained.extend(chunk)
+                nchunks += 1
+                done_entries += n
+            if ready and done_entries >= ready_entries:
+                break
+            if not t.overlap:
+                t.instance.pump()
+            else:
+                time.sleep(0.002)
+        t1 = time.perf_counter()
+        trajs = t.manager.consume(buffer_id)
+        if self.scope != "pre_step":
+            self.optimize(trajs, metrics)
+        metrics["timing_s/gen_wait"] = t1 - t0
+        metrics["timing_s/train"] = time.perf_counter() - t1
+        metrics["fine_grain/chunks"] = nchunks
+        return trajs
+
+
+def build_step_strategy(trainer) -> StepStrategy:
+    if trainer.cfg.psrl.fine_grain_overlap.granularity == "none":
+        return FullBatchStepStrategy(trainer)
+    return FineGrainOverlapStrategy(trainer)

@@ -74,3 +74,17 @@ def test_multiturn_rl_cpu():
     assert t.engine.bm.hits > 0                      # later turns reuse the session prefix
     t2 = t.step()
     assert t2["num_trajectories"] == 16
+
+
+@pytest.mark.parametrize("scope", ["recompute", "pre_step"])
+def test_fine_grain_overlap_strategy_cpu(scope):
+    from psrl_b200.config import load_config
+    from psrl_b200.trainer import RLTrainer
+    cfg = load_config(preset="cpu_tiny_grpo", overrides=[
+        "psrl.fine_grain_overlap.granularity=mini_batch", f"psrl.fine_grain_overlap.overlap_scope={scope}",
+        "actor.ppo_mini_batch_size=4", "psrl.log_prob.enable_rollout_engine_log_prob=false",
+        "rollout.max_response_length=8"])
+    t = RLTrainer(cfg)
+    m = t.step()
+    assert m["num_trajectories"] == 32 and m["fine_grain/chunks"] == 2
+    assert all(tr is not None for tr in [m.get("actor/pg_loss")])

@@ -246,3 +246,28 @@ def test_engine_stats_recorder_and_zmq(tmp_path):
     assert got["instance_id"] == (2, 0)
     push.close()
     pull.close()
+
+
+def test_placement_roles():
+    from psrl_b200.config import load_config
+    from psrl_b200.parallel.placement import Role, plan_placement
+    cfg = load_config(preset="dapo_qwen2.5_3b")
+    p = plan_placement(8, cfg.psrl.deployment)
+    assert p.train_ranks == [0, 1, 2, 3] and len(p.instances) == 4 and p.role_of(5) is Role.Rollout
+    assert plan_placement(1, cfg.psrl.deployment).colocated
+    cfg7 = load_config(preset="ppo_qwen2.5_7b")
+    p = plan_placement(8, cfg7.psrl.deployment)
+    assert [i.ranks for i in p.instances] == [[4, 5], [6, 7]]
+    cfg7.psrl.deployment.heterogeneous_rollout.enable = True
+    cfg7.psrl.deployment.heterogeneous_rollout.tensor_model_parallel_size_per_instance = [1, 1, 2]
+    p = plan_placement(8, cfg7.psrl.deployment)
+    assert [i.tp for i in p.instances] == [1, 1, 2] and p.instance_of(7).instance_id == (2, 0)
+
+
+def test_cli_print_config_and_run(capsys):
+    from psrl_b200.trainer.main import main
+    assert main(["--preset", "cpu_tiny_grpo", "--print-config", "psrl.staleness=2"]) == 0
+    out = capsys.readouterr().out
+    assert "staleness: 2" in out
+    assert main(["--preset", "cpu_tiny_grpo", "--steps", "1", "rollout.max_response_length=8"]) == 0
+    assert '"step": 0' in capsys.readouterr().out
