@@ -35,6 +35,9 @@ at::Tensor ipc_open(pybind11::bytes handle, int64_t offset, int64_t numel, at::S
 void enable_peer_access(int64_t peer);
 void copy_segments(at::Tensor dst, std::vector<at::Tensor> srcs, std::vector<int64_t> dst_offsets_bytes,
                    std::vector<int64_t> src_offsets_bytes, std::vector<int64_t> lengths_bytes);
+at::Tensor tc_gemm(at::Tensor a, at::Tensor b, at::Tensor err);
+std::vector<at::Tensor> tc_linear_logprob(at::Tensor h, at::Tensor w, at::Tensor labels, double temperature,
+                                          at::Tensor err);
 }  // namespace psrl
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -60,4 +63,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_open", &psrl::ipc_open);
   m.def("enable_peer_access", &psrl::enable_peer_access);
   m.def("copy_segments", &psrl::copy_segments);
+  m.def("tc_gemm", &psrl::tc_gemm);
+  m.def("tc_linear_logprob", &psrl::tc_linear_logprob);
 }
