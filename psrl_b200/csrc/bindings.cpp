@@ -38,6 +38,9 @@ void copy_segments(at::Tensor dst, std::vector<at::Tensor> srcs, std::vector<int
 at::Tensor tc_gemm(at::Tensor a, at::Tensor b, at::Tensor err);
 std::vector<at::Tensor> tc_linear_logprob(at::Tensor h, at::Tensor w, at::Tensor labels, double temperature,
                                           at::Tensor err);
+void kv_copy_blocks(at::Tensor src_layers, at::Tensor dst_layers, at::Tensor src_blk, at::Tensor dst_blk,
+                    int64_t block_bytes);
+void register_vmm(pybind11::module& m);
 }  // namespace psrl
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -65,4 +68,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("copy_segments", &psrl::copy_segments);
   m.def("tc_gemm", &psrl::tc_gemm);
   m.def("tc_linear_logprob", &psrl::tc_linear_logprob);
+  m.def("kv_copy_blocks", &psrl::kv_copy_blocks);
+  psrl::register_vmm(m);
 }

@@ -33,3 +33,24 @@ def test_profiling_records(tmp_path):
     with m.around("x"):
         pass
     assert len(m.records) == 2
+
+
+def test_elastic_policy_up_down_and_cooldown():
+    from psrl_b200.utils.elastic import ElasticExecutor, InstanceSignal, ScalingPolicy, ThroughputFit
+    pol = ScalingPolicy(theta_low=0.2, theta_max=0.8, cooldown_ms=1000, fit=ThroughputFit(A=1000, B=0.1, k=1,
+                                                                                           tokens_per_request=100))
+    sig = [InstanceSignal((0, 0), True, num_running=8), InstanceSignal((1, 0), False)]
+    pol._lambda = 100.0                                   # far above one instance's service rate
+    d = pol.decide(sig, now_ms=0)
+    assert d.action == "up" and d.instance_id == (1, 0)
+    assert pol.decide(sig, now_ms=500).action == "none"   # cooldown
+    sig = [InstanceSignal((0, 0), True, num_running=1), InstanceSignal((1, 0), True, num_running=0)]
+    pol._lambda = 0.0
+    d = pol.decide(sig, now_ms=5000)
+    assert d.action == "down" and d.instance_id == (1, 0)
+    woke, slept = [], []
+    ex = ElasticExecutor(ScalingPolicy(cooldown_ms=0), lambda: [InstanceSignal((0, 0), True, kv_usage=0.99),
+                                                                 InstanceSignal((1, 0), False)],
+                         slept.append, woke.append)
+    ex.tick()
+    assert woke == [(1, 0)]
