@@ -126,6 +126,8 @@ def main():
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     world = int(os.environ.get("WORLD_SIZE", 1))
+    import faulthandler
+    faulthandler.dump_traceback_later(480, repeat=True)   # all-thread stacks if a run stalls
     if args.gpus > 1 or world > 1:
         from psrl_b200.trainer.distributed import run_disaggregated_bench
         res = run_disaggregated_bench(args)

@@ -53,9 +53,13 @@ at::Tensor ipc_open(py::bytes handle, int64_t offset, int64_t numel, at::ScalarT
       g_ipc_open[key] = base;
     }
   }
-  // The mapping lives until process exit; the tensor only views it.  The tensor
-  // is tagged with the exporting device (pointer attributes resolve there).
-  auto opts = at::TensorOptions().dtype(dtype).device(at::kCUDA, src_device);
+  // The mapping lives until process exit; the tensor only views it.  In the
+  // importing process the mapped pointer belongs to the current device (peer
+  // access makes the exporting GPU's memory addressable from here).
+  (void)src_device;
+  int cur = 0;
+  PSRL_CHECK_CUDA(cudaGetDevice(&cur));
+  auto opts = at::TensorOptions().dtype(dtype).device(at::kCUDA, cur);
   return at::from_blob(static_cast<char*>(base) + offset, {numel}, [](void*) {}, opts);
 }
 

@@ -19,6 +19,7 @@ world_size=2 plumbing configuration).
 from __future__ import annotations
 
 import os
+import sys
 import threading
 import time
 
@@ -54,6 +55,8 @@ class DispatcherService:
         self.phase = 0
         self._cv = threading.Condition()
         self.sync_stats = {"pulls": 0, "pull_s": 0.0}
+        self.last_seen: dict = {}
+        self.failed: dict = {}
 
     # setup
     def register_store(self, trainer_rank: int, desc: dict) -> None:
@@ -77,8 +80,12 @@ class DispatcherService:
         self.ps.register_rollout_instance(tuple(instance_id), version)
 
     # steady state
+    def report_failure(self, instance_id, message: str) -> None:
+        self.failed[tuple(instance_id)] = message
+
     def exchange(self, instance_id, version: int, free_slots: int, outputs: list):
         instance_id = tuple(instance_id)
+        self.last_seen[instance_id] = time.monotonic()
         if outputs:
             self.manager.on_complete(outputs, instance_id)
         reqs = self.manager.take_work(instance_id, version, free_slots) if free_slots > 0 else []
@@ -101,6 +108,11 @@ class DispatcherService:
 
     def set_phase(self, p: int) -> None:
         self.phase = p
+
+
+def log(msg: str) -> None:
+    r = os.environ.get("RANK", "0")
+    print(f"[rank {r} {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
 
 
 def _role_split(world: int, cfg) -> int:
@@ -134,6 +146,9 @@ class DisaggregatedRun:
         self.trained_tokens = 0
         self.global_step = 0
         self.server = None
+        self.liveness_s = float(cfg.trainer.get("liveness_timeout_s", 300))
+        self.buffer_timeout_s = float(cfg.trainer.get("buffer_timeout_s", 1800))
+        log(f"role split: {self.n_train} trainer rank(s), {self.world - self.n_train} rollout rank(s)")
         if self.rank == 0:
             rn, _, _, _ = redundant_settings(cfg)
             self.ps = PSManager.from_config(cfg)
@@ -143,6 +158,7 @@ class DisaggregatedRun:
             self.svc = DispatcherService(cfg, self.ps, self.manager, self.n_train)
             self.server = RPCServer({"svc": self.svc}, port=self.port)
         dist.barrier()
+        log("control plane up")
         self.client = None if self.rank == 0 else RPCClient(("127.0.0.1", self.port))
         self.svc_proxy = self.svc if self.rank == 0 else self.client.proxy("svc")
         if self.is_trainer:
@@ -164,13 +180,22 @@ class DisaggregatedRun:
         if self.rank == 0:
             self.svc.set_layout(self.layout)
         self.svc_proxy.register_store(self.rank, self.store.descriptor())
+        log(f"trainer ready: {self.layout.nbytes / 2**30:.2f} GiB published store ({mode})")
 
     def trainer_step(self) -> dict:
         b = self.global_step
         t0 = time.perf_counter()
         trajs = None
         if self.rank == 0:
+            t_wait = time.monotonic()
             while not self.manager.buffer_ready(b):
+                if self.svc.failed:
+                    raise RuntimeError(f"rollout instance failed: {self.svc.failed}")
+                now = time.monotonic()
+                stale = [i for i, t in self.svc.last_seen.items() if now - t > self.liveness_s]
+                if stale or now - t_wait > self.buffer_timeout_s:
+                    raise TimeoutError(f"buffer {b} not ready: silent instances {stale}, "
+                                       f"{self.manager.snapshot()}")
                 time.sleep(0.002)
             trajs = self.manager.consume(b)
             for t in trajs:
@@ -209,6 +234,7 @@ class DisaggregatedRun:
         cfg, a = self.cfg, self.args
         rc = cfg.rollout
         self.instance_id = (self.rank - self.n_train, 0)
+        log("rollout: waiting for trainer stores")
         layout, descs = self.svc_proxy.get_stores()
         self.layout = layout
         dtype = layout.dtype
@@ -235,6 +261,7 @@ class DisaggregatedRun:
                                  sm.sync.get("threshold"), sm.sync.get("indicator", "request_num"))
         self._pull()
         self.svc_proxy.register_instance(self.instance_id, self.engine.version)
+        log(f"rollout instance {self.instance_id} ready at version {self.engine.version}")
 
     def _pull(self) -> None:
         t0 = time.perf_counter()
@@ -308,18 +335,29 @@ def run_disaggregated(cfg, steps: int, warmup: int, info: pdist.DistInfo | None 
 
     metrics = []
     if run.is_trainer:
-        for _ in range(warmup):
-            run.trainer_step()
+        for i in range(warmup):
+            m = run.trainer_step()
+            if run.rank == 0:
+                log(f"warm-up step {i}: {m['timing_s/step']:.1f}s, {m['trained_tokens']} tokens")
         if run.rank == 0:
             run.svc.set_phase(1)
         mark(1)
-        for _ in range(steps):
+        for i in range(steps):
             metrics.append(run.trainer_step())
+            if run.rank == 0:
+                log(f"timed step {i}: {metrics[-1]['timing_s/step']:.1f}s")
         if run.rank == 0:
             run.svc.set_phase(2)
         mark(2)
     else:
-        run.rollout_loop(mark)
+        try:
+            run.rollout_loop(mark)
+        except BaseException as exc:
+            try:
+                run.svc_proxy.report_failure(run.instance_id, f"{type(exc).__name__}: {exc}")
+            except Exception:
+                pass
+            raise
     if is_cuda:
         torch.cuda.synchronize()
         ms = t_evt[1].elapsed_time(t_evt[2])

@@ -78,8 +78,9 @@ class RPCServer:
 
 
 class RPCClient:
-    def __init__(self, address, authkey: bytes = DEFAULT_AUTHKEY, retries: int = 600):
+    def __init__(self, address, authkey: bytes = DEFAULT_AUTHKEY, retries: int = 600, timeout: float = 900.0):
         import time
+        self.timeout = timeout
         last = None
         for _ in range(retries):
             try:
@@ -95,6 +96,8 @@ class RPCClient:
     def call(self, target: str, method: str, *args, **kwargs):
         with self._lock:
             self.conn.send((target, method, args, kwargs))
+            if not self.conn.poll(self.timeout):
+                raise RPCError(f"RPC {target}.{method} got no reply within {self.timeout}s")
             status, val = self.conn.recv()
         if status != "ok":
             raise RPCError(val)
