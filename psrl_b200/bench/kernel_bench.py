@@ -1,0 +1,167 @@
+"""Kernel micro-benchmarks with roofline fractions.
+
+Each case runs a kernel on inputs larger than L2 (or rotates buffers), times
+it with CUDA events after warm-up, and reports achieved bandwidth / FLOP rate
+as a fraction of the measured peaks (``MEASURED_PEAKS.json`` when present).
+
+    python -m psrl_b200.bench.kernel_bench [--only decode,gemm,...]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as fh:
+            d = json.load(fh)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+def timeit(fn, iters: int = 20, warmup: int = 5) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def bench_decode(pk):
+    from psrl_b200.ops import paged_decode_attention
+    from psrl_b200.ops.attention import decode_splits
+    out = []
+    for B, ctx, nq, nkv in ((256, 1024, 16, 2), (128, 4096, 16, 2), (64, 8192, 28, 4)):
+        bs, d = 64, 128
+        nblk = B * (ctx // bs)
+        kc = torch.randn(nblk, nkv, bs, d, device="cuda").bfloat16()
+        vc = torch.randn_like(kc)
+        bt = torch.arange(nblk, dtype=torch.int32, device="cuda").view(B, ctx // bs)
+        lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+        q = torch.randn(B, nq, d, device="cuda").bfloat16()
+        sp = decode_splits(B, nkv, ctx)
+        ms = timeit(lambda: paged_decode_attention(q, kc, vc, bt, lens, splits=sp))
+        nbytes = 2 * B * ctx * nkv * d * 2
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out.append({"case": f"decode B={B} ctx={ctx} {nq}/{nkv}", "ms": round(ms, 4), "GB/s": round(gbs, 1),
+                    "frac_hbm": round(gbs / pk["hbm_gbs"], 3), "splits": sp})
+        del kc, vc
+    return out
+
+
+def bench_gemm(pk):
+    from psrl_b200.ops.gemm import tc_linear
+    out = []
+    for M, N, K in ((10240, 2560, 2048), (10240, 22016, 2048), (10240, 2048, 11008), (8192, 151936, 2048)):
+        x = torch.randn(M, K, device="cuda").bfloat16()
+        w = torch.randn(N, K, device="cuda").bfloat16()
+        fl = 2.0 * M * N * K
+        ms_tc = timeit(lambda: tc_linear(x, w), iters=10)
+        ms_cb = timeit(lambda: x @ w.t(), iters=10)
+        out.append({"case": f"gemm {M}x{N}x{K}", "tcgen05_ms": round(ms_tc, 3), "cublas_ms": round(ms_cb, 3),
+                    "tcgen05_tflops": round(fl / ms_tc / 1e9, 1), "cublas_tflops": round(fl / ms_cb / 1e9, 1),
+                    "frac_peak_tcgen05": round(fl / ms_tc / 1e9 / pk["bf16_tflops"], 3)})
+    return out
+
+
+def bench_logprob(pk):
+    from psrl_b200.ops.gemm import tc_linear_logprob
+    from psrl_b200.ops.logprob import linear_logprob
+    out = []
+    T, H, V = 8192, 2048, 151936
+    h = (torch.randn(T, H, device="cuda") * 0.5).bfloat16()
+    w = (torch.randn(V, H, device="cuda") * 0.02).bfloat16()
+    lab = torch.randint(0, V, (T,), device="cuda")
+    fl = 2.0 * T * V * H
+    ms_f = timeit(lambda: tc_linear_logprob(h, w, lab), iters=10)
+    with torch.no_grad():
+        ms_c = timeit(lambda: linear_logprob(h, w, lab), iters=10)
+    out.append({"case": f"lm-head logprob T={T} V={V}", "fused_tcgen05_ms": round(ms_f, 3),
+                "cublas+lse_kernel_ms": round(ms_c, 3), "fused_tflops": round(fl / ms_f / 1e9, 1),
+                "frac_peak": round(fl / ms_f / 1e9 / pk["bf16_tflops"], 3)})
+    return out
+
+
+def bench_attn_train(pk):
+    from psrl_b200.ops import varlen_attention
+    out = []
+    for L, nseq in ((2048, 5), (8192, 1)):
+        nq, nkv, d = 16, 2, 128
+        T = L * nseq
+        qkv = torch.randn(T, (nq + 2 * nkv) * d, device="cuda").bfloat16().requires_grad_(True)
+        cu = torch.arange(0, T + 1, L, dtype=torch.int32, device="cuda")
+        fl = 4.0 * nseq * (L * L / 2) * d * nq
+        ms_f = timeit(lambda: varlen_attention(qkv, cu, L, nq, nkv, d), iters=10)
+        o = varlen_attention(qkv, cu, L, nq, nkv, d)
+        g = torch.randn_like(o)
+        ms_b = timeit(lambda: torch.autograd.grad(o, qkv, g, retain_graph=True), iters=10)
+        out.append({"case": f"varlen attn L={L}x{nseq} 16/2", "fwd_ms": round(ms_f, 3), "bwd_ms": round(ms_b, 3),
+                    "fwd_tflops": round(fl / ms_f / 1e9, 1), "bwd_tflops": round(2.5 * fl / ms_b / 1e9, 1)})
+    return out
+
+
+def bench_elementwise(pk):
+    from psrl_b200.ops import rms_norm, swiglu
+    out = []
+    T, h, I = 65536, 2048, 11008
+    x = torch.randn(T, h, device="cuda").bfloat16()
+    r = torch.randn_like(x)
+    w = torch.ones(h, device="cuda").bfloat16()
+    with torch.no_grad():
+        ms = timeit(lambda: rms_norm(x, w, 1e-6, r))
+    nb = 4 * T * h * 2
+    out.append({"case": f"rmsnorm+residual {T}x{h}", "ms": round(ms, 4), "GB/s": round(nb / ms / 1e6, 1),
+                "frac_hbm": round(nb / ms / 1e6 / pk["hbm_gbs"], 3)})
+    gu = torch.randn(16384, 2 * I, device="cuda").bfloat16()
+    with torch.no_grad():
+        ms = timeit(lambda: swiglu(gu))
+    nb = 16384 * 3 * I * 2
+    out.append({"case": f"swiglu 16384x{I}", "ms": round(ms, 4), "GB/s": round(nb / ms / 1e6, 1),
+                "frac_hbm": round(nb / ms / 1e6 / pk["hbm_gbs"], 3)})
+    return out
+
+
+def bench_sync(pk):
+    from psrl_b200.ops import ext
+    n = 3_300_000_000 // 2
+    src = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    dst = torch.empty_like(src)
+    nb = n * 2
+    ms = timeit(lambda: ext().copy_segments(dst, [src], [0], [0], [nb]), iters=10)
+    return [{"case": "weight store publish (local copy_segments, 3.3 GB)", "ms": round(ms, 3),
+             "GB/s (read+write)": round(2 * nb / ms / 1e6, 1), "frac_hbm": round(2 * nb / ms / 1e6 / pk["hbm_gbs"], 3)}]
+
+
+CASES = {"decode": bench_decode, "gemm": bench_gemm, "logprob": bench_logprob, "attn": bench_attn_train,
+         "elementwise": bench_elementwise, "sync": bench_sync}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default=",".join(CASES))
+    args = ap.parse_args(argv)
+    pk = peaks()
+    res = {"peaks": pk}
+    for name in args.only.split(","):
+        res[name] = CASES[name](pk)
+        print(json.dumps({name: res[name]}), flush=True)
+        torch.cuda.empty_cache()
+    return res
+
+
+if __name__ == "__main__":
+    main()

@@ -169,8 +169,13 @@ class RLTrainer:
 
     def start_rollout(self) -> None:
         if self.overlap and self._rollout_thread is None:
+            import atexit
             import threading
+            import weakref
             self._rollout_stop = False
+            ref = weakref.ref(self)
+            # never leave the engine thread running CUDA work into interpreter shutdown
+            atexit.register(lambda: ref() is not None and ref().stop_rollout())
             self._rollout_thread = threading.Thread(target=self._rollout_loop, daemon=True, name="rollout")
             self._rollout_thread.start()
 

@@ -313,5 +313,6 @@ def test_rl_step_gpu_tiny():
         m = t.step()
         assert m["num_trajectories"] == 32
         assert math.isfinite(m["actor/pg_loss"]) and math.isfinite(m["actor/grad_norm"])
+    t.stop_rollout()
     assert t.ps.get_ps_model_version() == 3
-    assert t.engine.version == 3 or t.engine.version == 2
+    assert t.engine.version in (2, 3)
