@@ -567,14 +567,36 @@ struct DecodeParams {
 
 // One CTA = (sequence, kv head, split). Warp w handles keys w*16..w*16+15 of each
 // 64-key tile with its own online softmax; warps are merged at the end.
-__global__ void __launch_bounds__(NTHREADS) decode_kernel(DecodeParams p) {
+// K/V tiles stream through a DEC_STAGES-deep cp.async ring; every thread
+// computes the paged address of the chunks it copies directly (no row table),
+// so a tile costs one barrier.  The warp-merge area aliases the ring.
+constexpr int DEC_STAGES = 2;   // x 3 resident CTAs per SM
+
+__device__ __forceinline__ void dec_load_tile(bf16* sm, const bf16* cache, const int* bt_row, int block_size,
+                                              int nkv, int kvh, int key0, int k_end) {
+  // BN rows x 16 chunks of 16 B; 128 threads -> 8 chunks each
+#pragma unroll
+  for (int i = 0; i < BN * 16 / NTHREADS; ++i) {
+    const int idx = threadIdx.x + i * NTHREADS;
+    const int r = idx >> 4, c = idx & 15;
+    const int key = key0 + r;
+    const bool ok = key < k_end;
+    const bf16* src = cache;
+    if (ok) {
+      const int blk = bt_row[key / block_size];
+      src = cache + (((int64_t)blk * nkv + kvh) * block_size + key % block_size) * D + c * 8;
+    }
+    cp_async16(sm + swz(r, c * 8), src, ok);
+  }
+}
+
+__global__ void __launch_bounds__(NTHREADS, 3) decode_kernel(DecodeParams p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   bf16* sQ = reinterpret_cast<bf16*>(smem_raw);  // [16][D]
-  bf16* sK = sQ + 16 * D;                         // [2][BN][D]
-  bf16* sV = sK + 2 * BN * D;
-  float* sO = reinterpret_cast<float*>(sV + 2 * BN * D);  // [NWARPS][16][D] merge area
+  bf16* sK = sQ + 16 * D;                         // [DEC_STAGES][BN][D]
+  bf16* sV = sK + DEC_STAGES * BN * D;            // [DEC_STAGES][BN][D]
+  float* sO = reinterpret_cast<float*>(sK);       // [NWARPS][16][D] merge area (after the loop)
   __shared__ float sM[NWARPS][16], sL[NWARPS][16];
-  __shared__ const bf16* rowp[BN];
 
   const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
   const int grp = p.nq / p.nkv;
@@ -583,37 +605,29 @@ __global__ void __launch_bounds__(NTHREADS) decode_kernel(DecodeParams p) {
   const int k_begin = split * per;
   const int k_end = min(kv_len, k_begin + per);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int* bt_row = p.block_table + (int64_t)b * p.max_blocks;
 
-  if (threadIdx.x < 16)
-    rowp[threadIdx.x] = threadIdx.x < grp ? p.q + ((int64_t)b * p.nq + kvh * grp + threadIdx.x) * D : nullptr;
-  __syncthreads();
-  load_tile<16>(sQ, rowp, p.q);
+  // Q rows (grp <= 16), zero padded
+#pragma unroll
+  for (int i = 0; i < 16 * 16 / NTHREADS; ++i) {
+    const int idx = threadIdx.x + i * NTHREADS;
+    const int r = idx >> 4, c = idx & 15;
+    const bool ok = r < grp;
+    const bf16* src = ok ? p.q + ((int64_t)b * p.nq + kvh * grp + r) * D + c * 8 : p.q;
+    cp_async16(sQ + swz(r, c * 8), src, ok);
+  }
   cp_async_commit();
 
   const int n_tiles = k_end > k_begin ? (k_end - k_begin + BN - 1) / BN : 0;
-  auto load_kv = [&](int t, int stage) {
-    __syncthreads();
-    if (threadIdx.x < BN) {
-      const int key = k_begin + t * BN + threadIdx.x;
-      const bool ok = key < k_end;
-      const int blk = ok ? p.block_table[(int64_t)b * p.max_blocks + key / p.block_size] : 0;
-      rowp[threadIdx.x] = ok ? p.kc + (((int64_t)blk * p.nkv + kvh) * p.block_size + key % p.block_size) * D : nullptr;
+#pragma unroll
+  for (int st = 0; st < DEC_STAGES - 1; ++st) {
+    if (st < n_tiles) {
+      dec_load_tile(sK + st * BN * D, p.kc, bt_row, p.block_size, p.nkv, kvh, k_begin + st * BN, k_end);
+      dec_load_tile(sV + st * BN * D, p.vc, bt_row, p.block_size, p.nkv, kvh, k_begin + st * BN, k_end);
     }
-    __syncthreads();
-    load_tile<BN>(sK + stage * BN * D, rowp, p.kc);
-    __syncthreads();
-    if (threadIdx.x < BN) {
-      const int key = k_begin + t * BN + threadIdx.x;
-      const bool ok = key < k_end;
-      const int blk = ok ? p.block_table[(int64_t)b * p.max_blocks + key / p.block_size] : 0;
-      rowp[threadIdx.x] = ok ? p.vc + (((int64_t)blk * p.nkv + kvh) * p.block_size + key % p.block_size) * D : nullptr;
-    }
-    __syncthreads();
-    load_tile<BN>(sV + stage * BN * D, rowp, p.vc);
-  };
-  if (n_tiles > 0) load_kv(0, 0);
-  cp_async_commit();
-  cp_async_wait<1>();
+    cp_async_commit();
+  }
+  cp_async_wait<DEC_STAGES - 1>();   // Q landed
   __syncthreads();
 
   uint32_t qf[8][4];
@@ -628,11 +642,19 @@ __global__ void __launch_bounds__(NTHREADS) decode_kernel(DecodeParams p) {
   const float sl2 = p.scale * LOG2E;
 
   for (int t = 0; t < n_tiles; ++t) {
-    const int stage = t & 1;
-    if (t + 1 < n_tiles) load_kv(t + 1, stage ^ 1);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
+    const int stage = t % DEC_STAGES;
+    cp_async_wait<DEC_STAGES - 2>();   // tile t landed (this thread's copies)
+    __syncthreads();                   // ... and everyone's; stage (t-1) is free to refill
+    {
+      const int tn = t + DEC_STAGES - 1;
+      if (tn < n_tiles) {
+        const int sn = tn % DEC_STAGES;
+        dec_load_tile(sK + sn * BN * D, p.kc, bt_row, p.block_size, p.nkv, kvh, k_begin + tn * BN, k_end);
+        dec_load_tile(sV + sn * BN * D, p.vc, bt_row, p.block_size, p.nkv, kvh, k_begin + tn * BN, k_end);
+      }
+      cp_async_commit();
+    }
+    const bf16* k_s = sK + stage * BN * D;
     const bf16* v_s = sV + stage * BN * D;
     float s[2][4];
     s[0][0] = s[0][1] = s[0][2] = s[0][3] = 0.f;
@@ -640,11 +662,9 @@ __global__ void __launch_bounds__(NTHREADS) decode_kernel(DecodeParams p) {
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
       uint32_t b0, b1, b2, b3;
-      const int r = (lane & 7) + ((lane >> 4) << 3);
+      const int ar = warp * 16 + (lane & 7) + ((lane >> 4) << 3);
       const int c = ks * 16 + ((lane >> 3) & 1) * 8;
-      // rows are relative to the warp's key slice; swizzle uses the absolute tile row
-      const int ar = warp * 16 + r;
-      ldsm_x4(b0, b1, b2, b3, sK + stage * BN * D + swz(ar, c));
+      ldsm_x4(b0, b1, b2, b3, k_s + swz(ar, c));
       mma16816(s[0], qf[ks], b0, b1);
       mma16816(s[1], qf[ks], b2, b3);
     }
@@ -699,15 +719,14 @@ __global__ void __launch_bounds__(NTHREADS) decode_kernel(DecodeParams p) {
       mma16816(o[2 * dp], pf, b0, b1);
       mma16816(o[2 * dp + 1], pf, b2, b3);
     }
-    __syncthreads();
   }
   cp_async_wait<0>();
+  __syncthreads();                     // ring no longer read: reuse it as the merge area
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     l_r[r] += __shfl_xor_sync(0xffffffffu, l_r[r], 1);
     l_r[r] += __shfl_xor_sync(0xffffffffu, l_r[r], 2);
   }
-  // merge warps through shared memory
   if ((lane & 3) == 0) {
     sM[warp][lane >> 2] = m_r[0];
     sM[warp][(lane >> 2) + 8] = m_r[1];
@@ -730,7 +749,6 @@ __global__ void __launch_bounds__(NTHREADS) decode_kernel(DecodeParams p) {
     }
   }
   __syncthreads();
-  // threads cooperatively reduce rows < grp
   for (int idx = threadIdx.x; idx < grp * D; idx += NTHREADS) {
     const int row = idx / D, col = idx % D;
     float mg = -INFINITY;
@@ -776,7 +794,12 @@ using namespace attn;
 
 static size_t fwd_smem() { return (size_t)(BM * D + 4 * BN * D) * sizeof(bf16); }
 static size_t bwd_smem() { return (size_t)(2 * BN * D + 2 * BM * D + BN * BM) * sizeof(bf16); }
-static size_t dec_smem() { return (size_t)(16 * D + 4 * BN * D) * sizeof(bf16) + NWARPS * 16 * D * sizeof(float); }
+static size_t dec_smem() {
+  // Q + K/V ring; the fp32 warp-merge area (NWARPS x 16 x D) aliases the ring
+  const size_t ring = (size_t)(16 * D + 2 * DEC_STAGES * BN * D) * sizeof(bf16);
+  const size_t merge = (size_t)16 * D * sizeof(bf16) + (size_t)NWARPS * 16 * D * sizeof(float);
+  return ring > merge ? ring : merge;
+}
 
 // Varlen causal attention forward over contiguous q/k/v views.
 // q: [T, nq, D] view, k/v: [T, nkv, D] views (token stride arbitrary, unit stride on D)
@@ -918,11 +941,24 @@ std::vector<at::Tensor> attn_varlen_bwd(at::Tensor dO, at::Tensor q, at::Tensor 
 }
 
 int64_t decode_num_splits(int64_t batch, int64_t nkv, int64_t max_ctx) {
-  const int64_t ctas = batch * nkv;
-  const int64_t target = 2 * num_sms();
-  int64_t s = (target + ctas - 1) / ctas;
-  s = std::min<int64_t>(s, std::max<int64_t>(1, (max_ctx + 255) / 256));
-  return std::max<int64_t>(1, std::min<int64_t>(s, 32));
+  // Pick the split count whose grid wastes the least of the last wave
+  // (3 resident CTAs per SM), keeping at least 4 key tiles per split.
+  const int64_t ctas = std::max<int64_t>(1, batch * nkv);
+  const int64_t cap = 3 * (int64_t)num_sms();
+  const int64_t max_s = std::max<int64_t>(1, std::min<int64_t>(32, (max_ctx + 4 * BN - 1) / (4 * BN)));
+  int64_t best = 1;
+  double best_eff = -1.0;
+  for (int64_t s = 1; s <= max_s; ++s) {
+    const int64_t n = ctas * s;
+    const int64_t waves = (n + cap - 1) / cap;
+    // efficiency of the waves, with a small penalty per extra split (combine cost)
+    const double eff = (double)n / (double)(waves * cap) - 0.01 * (double)(s - 1);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
 }
 
 // Paged decode. q: [B, nq, D] contiguous. `scratch` (optional) is a float buffer of

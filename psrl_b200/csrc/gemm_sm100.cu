@@ -278,7 +278,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 *reinterpret_cast<bf16x8*>(dst + j) = p;
               }
             } else {
-              for (int j = 0; j < 32 && cb + j < args.N; ++j) dst[j] = __float2bfloat16(v[j]);
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (cb + j < args.N) dst[j] = __float2bfloat16(v[j]);
             }
           }
         }

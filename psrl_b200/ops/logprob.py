@@ -14,6 +14,8 @@ import torch
 from ._ext import ext
 
 DEFAULT_CHUNK = 16384
+# forward through the fused tcgen05 kernel (csrc/gemm_sm100.cu) when shapes allow
+USE_TCGEN05 = True
 
 
 def linear_logprob_ref(h, W, labels, temperature: float = 1.0, want_entropy: bool = True):
@@ -29,6 +31,13 @@ class _LinearLogprobFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h, W, labels, temperature, chunk):
         T = h.shape[0]
+        from . import gemm as tc
+        if USE_TCGEN05 and tc.supported(h, W):
+            # fused tcgen05 GEMM + log-sum-exp epilogue: logits never leave TMEM
+            lp, ent, lse = tc.tc_linear_logprob(h, W, labels, temperature)
+            ctx.save_for_backward(h, W, labels, lse, ent)
+            ctx.cfg = (temperature, chunk)
+            return lp, ent
         lps, ents, lses = [], [], []
         for s in range(0, T, chunk):
             logits = h[s: s + chunk] @ W.t()
