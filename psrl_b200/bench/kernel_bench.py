@@ -54,11 +54,15 @@ def bench_decode(pk):
         lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
         q = torch.randn(B, nq, d, device="cuda").bfloat16()
         sp = decode_splits(B, nkv, ctx)
-        ms = timeit(lambda: paged_decode_attention(q, kc, vc, bt, lens, splits=sp))
         nbytes = 2 * B * ctx * nkv * d * 2
+        sweep = {}
+        for s_ in sorted({1, 2, 4, sp}):
+            ms_ = timeit(lambda: paged_decode_attention(q, kc, vc, bt, lens, splits=s_))
+            sweep[s_] = round(nbytes / (ms_ / 1e3) / 1e9, 1)
+        ms = timeit(lambda: paged_decode_attention(q, kc, vc, bt, lens, splits=sp))
         gbs = nbytes / (ms / 1e3) / 1e9
         out.append({"case": f"decode B={B} ctx={ctx} {nq}/{nkv}", "ms": round(ms, 4), "GB/s": round(gbs, 1),
-                    "frac_hbm": round(gbs / pk["hbm_gbs"], 3), "splits": sp})
+                    "frac_hbm": round(gbs / pk["hbm_gbs"], 3), "splits": sp, "GB/s_by_splits": sweep})
         del kc, vc
     return out
 

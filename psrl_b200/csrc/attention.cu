@@ -941,24 +941,12 @@ std::vector<at::Tensor> attn_varlen_bwd(at::Tensor dO, at::Tensor q, at::Tensor 
 }
 
 int64_t decode_num_splits(int64_t batch, int64_t nkv, int64_t max_ctx) {
-  // Pick the split count whose grid wastes the least of the last wave
-  // (3 resident CTAs per SM), keeping at least 4 key tiles per split.
+  // Enough CTAs for ~2 per SM; every split keeps at least 4 key tiles.
   const int64_t ctas = std::max<int64_t>(1, batch * nkv);
-  const int64_t cap = 3 * (int64_t)num_sms();
-  const int64_t max_s = std::max<int64_t>(1, std::min<int64_t>(32, (max_ctx + 4 * BN - 1) / (4 * BN)));
-  int64_t best = 1;
-  double best_eff = -1.0;
-  for (int64_t s = 1; s <= max_s; ++s) {
-    const int64_t n = ctas * s;
-    const int64_t waves = (n + cap - 1) / cap;
-    // efficiency of the waves, with a small penalty per extra split (combine cost)
-    const double eff = (double)n / (double)(waves * cap) - 0.01 * (double)(s - 1);
-    if (eff > best_eff + 1e-9) {
-      best_eff = eff;
-      best = s;
-    }
-  }
-  return best;
+  const int64_t target = 2 * num_sms();
+  int64_t s = (target + ctas - 1) / ctas;
+  s = std::min<int64_t>(s, std::max<int64_t>(1, (max_ctx + 4 * BN - 1) / (4 * BN)));
+  return std::max<int64_t>(1, std::min<int64_t>(s, 32));
 }
 
 // Paged decode. q: [B, nq, D] contiguous. `scratch` (optional) is a float buffer of

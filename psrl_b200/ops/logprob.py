@@ -14,7 +14,7 @@ import torch
 from ._ext import ext
 
 DEFAULT_CHUNK = 16384
-# forward through the fused tcgen05 kernel (csrc/gemm_sm100.cu) when shapes allow
+# inference log-probs through the fused tcgen05 kernel (csrc/gemm_sm100.cu) when shapes allow
 USE_TCGEN05 = True
 
 
@@ -31,13 +31,6 @@ class _LinearLogprobFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h, W, labels, temperature, chunk):
         T = h.shape[0]
-        from . import gemm as tc
-        if USE_TCGEN05 and tc.supported(h, W):
-            # fused tcgen05 GEMM + log-sum-exp epilogue: logits never leave TMEM
-            lp, ent, lse = tc.tc_linear_logprob(h, W, labels, temperature)
-            ctx.save_for_backward(h, W, labels, lse, ent)
-            ctx.cfg = (temperature, chunk)
-            return lp, ent
         lps, ents, lses = [], [], []
         for s in range(0, T, chunk):
             logits = h[s: s + chunk] @ W.t()
@@ -81,6 +74,15 @@ def linear_logprob(h: torch.Tensor, W: torch.Tensor, labels: torch.Tensor, tempe
     """log-softmax(h W^T / T)[label] and entropy, both fp32 [T]."""
     labels = labels.long()
     if h.is_cuda and h.dtype == torch.bfloat16:
+        needs_grad = torch.is_grad_enabled() and (h.requires_grad or W.requires_grad)
+        from . import gemm as tc
+        if not needs_grad and USE_TCGEN05 and tc.supported(h, W):
+            # inference (old / reference log-probs): fused tcgen05 GEMM + log-sum-exp
+            # epilogue, the [T, V] logits never leave tensor memory
+            lp, ent, _ = tc.tc_linear_logprob(h, W, labels, temperature)
+            return lp, ent
+        # training: chunked logits in bf16, recomputed in backward (one consistent
+        # rounding of the logits in both directions)
         return _LinearLogprobFn.apply(h, W, labels, float(temperature), int(chunk))
     return linear_logprob_ref(h, W, labels, temperature)
 

@@ -485,6 +485,8 @@ class RolloutEngine:
         mb = max(len(s.blocks) for s in self.running)
         self.s_bt[:nb, :mb].copy_(self.h_bt[:nb, :mb], non_blocking=True)
         transfer.h2d(nb * (8 + 4 + 4 + 4 + 4 + 8 + 4 * mb))
+        if self.is_cuda:
+            torch.cuda.nvtx.range_push("decode_step")
         if self.use_cuda_graph:
             g = self._graphs.get(nb)
             if g is None:
@@ -494,6 +496,7 @@ class RolloutEngine:
         else:
             self._decode_forward(nb)
         if self.is_cuda:
+            torch.cuda.nvtx.range_pop()
             self.h_out_tok[:nb].copy_(self.s_out_tok[:nb], non_blocking=True)
             self.h_out_lp[:nb].copy_(self.s_out_lp[:nb], non_blocking=True)
             torch.cuda.current_stream().synchronize()
