@@ -127,7 +127,7 @@ def main():
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     world = int(os.environ.get("WORLD_SIZE", 1))
     import faulthandler
-    faulthandler.dump_traceback_later(480, repeat=True)   # all-thread stacks if a run stalls
+    faulthandler.dump_traceback_later(240, repeat=True)   # all-thread stacks if a run stalls
     if args.gpus > 1 or world > 1:
         from psrl_b200.trainer.distributed import run_disaggregated_bench
         res = run_disaggregated_bench(args)

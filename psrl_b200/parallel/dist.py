@@ -44,24 +44,26 @@ def init_distributed(device: str = "auto", timeout_s: float = 600.0) -> DistInfo
     if world > 1 and not dist.is_initialized():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         os.environ.setdefault("MASTER_PORT", "29511")
-        kw = {}
-        if use_cuda:
-            kw["device_id"] = dev
+        # lazy NCCL communicator creation (no device_id binding): subgroups are then
+        # created only by their members, without a collective over the world
         dist.init_process_group(backend=backend, rank=rank, world_size=world,
-                                timeout=datetime.timedelta(seconds=timeout_s), **kw)
+                                timeout=datetime.timedelta(seconds=timeout_s))
     return DistInfo(rank, world, local, dev, backend)
 
 
 def new_subgroup(ranks: list[int], backend: str | None = None):
-    """Every rank must call this with the same list (collective)."""
+    """Create a subgroup; only member ranks call this (group-local synchronisation)."""
     if not dist.is_initialized():
         return None
-    return dist.new_group(ranks=ranks, backend=backend)
+    return dist.new_group(ranks=ranks, backend=backend, use_local_synchronization=True)
 
 
 def barrier(group=None):
     if dist.is_initialized():
-        dist.barrier(group=group)
+        if dist.get_backend(group) == "nccl" and torch.cuda.is_available():
+            dist.barrier(group=group, device_ids=[torch.cuda.current_device()])
+        else:
+            dist.barrier(group=group)
 
 
 def all_reduce_max(x: float, device, group=None) -> float:

@@ -70,8 +70,8 @@ class FlatShardedDP:
                  bucket_mode: str = "layer"):
         self.model = model
         self.group = group
-        self.world = dist.get_world_size(group) if (group is not None or dist.is_initialized()) and \
-            dist.is_initialized() else 1
+        # no group = this rank trains alone (even inside a larger job)
+        self.world = dist.get_world_size(group) if (group is not None and dist.is_initialized()) else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
         self.device = next(model.parameters()).device
         self.lr, self.betas, self.eps, self.wd = lr, tuple(betas), eps, weight_decay

@@ -139,8 +139,12 @@ class DisaggregatedRun:
         self.device = info.device
         trainer_ranks = list(range(self.n_train))
         backend = "nccl" if self.device.type == "cuda" else "gloo"
-        self.train_group = dist.new_group(trainer_ranks, backend=backend)
-        self.train_cpu_group = dist.new_group(trainer_ranks, backend="gloo")
+        self.train_group = None
+        self.train_cpu_group = None
+        if self.is_trainer and self.n_train > 1:
+            # created by the trainer ranks only (group-local synchronisation)
+            self.train_group = pdist.new_subgroup(trainer_ranks, backend=backend)
+            self.train_cpu_group = pdist.new_subgroup(trainer_ranks, backend="gloo")
         self.args = model_args_from_config(cfg.model)
         self.port = int(os.environ.get("MASTER_PORT", "29511")) + 17
         self.trained_tokens = 0
@@ -157,7 +161,7 @@ class DisaggregatedRun:
             self.manager = AgentLoopManager(cfg, self.ps, self.data, self.reward)
             self.svc = DispatcherService(cfg, self.ps, self.manager, self.n_train)
             self.server = RPCServer({"svc": self.svc}, port=self.port)
-        dist.barrier()
+        pdist.barrier()
         log("control plane up")
         self.client = None if self.rank == 0 else RPCClient(("127.0.0.1", self.port))
         self.svc_proxy = self.svc if self.rank == 0 else self.client.proxy("svc")
@@ -325,7 +329,7 @@ def run_disaggregated(cfg, steps: int, warmup: int, info: pdist.DistInfo | None 
     t_evt = {}
 
     def mark(p):
-        dist.barrier()
+        pdist.barrier()
         if is_cuda:
             torch.cuda.synchronize()
             ev = torch.cuda.Event(enable_timing=True)
@@ -372,7 +376,7 @@ def run_disaggregated(cfg, steps: int, warmup: int, info: pdist.DistInfo | None 
         out["tokens"] = sum(m["trained_tokens"] for m in metrics)
         out["sync"] = dict(run.svc.sync_stats)
         out["manager"] = run.manager.snapshot()
-    dist.barrier()
+    pdist.barrier()
     run.close()
     return out
 

@@ -31,7 +31,8 @@ class RPCError(RuntimeError):
 class RPCServer:
     def __init__(self, objects: dict, host: str = "127.0.0.1", port: int = 0, authkey: bytes = DEFAULT_AUTHKEY):
         self.objects = dict(objects)
-        self.listener = Listener((host, port), authkey=authkey)
+        # a deep accept backlog: many ranks connect at once at start-up
+        self.listener = Listener((host, port), backlog=128, authkey=authkey)
         self.address = self.listener.address
         self._stop = threading.Event()
         self._threads: list[threading.Thread] = []
@@ -42,11 +43,14 @@ class RPCServer:
         self.objects[name] = obj
 
     def _accept_loop(self):
+        import multiprocessing
         while not self._stop.is_set():
             try:
                 conn = self.listener.accept()
-            except (OSError, EOFError):
-                break
+            except (OSError, EOFError, multiprocessing.AuthenticationError):
+                if self._stop.is_set():
+                    break
+                continue          # a failed handshake must not stop the server
             t = threading.Thread(target=self._serve, args=(conn,), daemon=True, name="rpc-conn")
             t.start()
             self._threads.append(t)
@@ -77,6 +81,39 @@ class RPCServer:
             pass
 
 
+def _connect_with_timeout(address, authkey: bytes, timeout: float):
+    """``multiprocessing.connection.Client`` with a bounded connect + handshake.
+
+    The socket stays in blocking mode; kernel receive/send timeouts bound the
+    handshake and are cleared once it succeeded.
+    """
+    import socket
+    import struct
+    from multiprocessing.connection import Connection, answer_challenge, deliver_challenge
+
+    sock = socket.create_connection(address, timeout=timeout)
+    sock.settimeout(None)
+    tv = struct.pack("ll", int(timeout), 0)
+    sock.setsockopt(socket.SOL_SOCKET, socket.SO_RCVTIMEO, tv)
+    sock.setsockopt(socket.SOL_SOCKET, socket.SO_SNDTIMEO, tv)
+    conn = Connection(sock.detach())
+    try:
+        answer_challenge(conn, authkey)
+        deliver_challenge(conn, authkey)
+    except BlockingIOError as exc:
+        conn.close()
+        raise TimeoutError(f"RPC handshake with {address} timed out") from exc
+    except BaseException:
+        conn.close()
+        raise
+    s2 = socket.socket(fileno=conn.fileno())
+    zero = struct.pack("ll", 0, 0)
+    s2.setsockopt(socket.SOL_SOCKET, socket.SO_RCVTIMEO, zero)
+    s2.setsockopt(socket.SOL_SOCKET, socket.SO_SNDTIMEO, zero)
+    s2.detach()
+    return conn
+
+
 class RPCClient:
     def __init__(self, address, authkey: bytes = DEFAULT_AUTHKEY, retries: int = 600, timeout: float = 900.0):
         import time
@@ -84,9 +121,9 @@ class RPCClient:
         last = None
         for _ in range(retries):
             try:
-                self.conn = Client(address, authkey=authkey)
+                self.conn = _connect_with_timeout(address, authkey, 30.0)
                 break
-            except (ConnectionRefusedError, OSError) as exc:
+            except (ConnectionRefusedError, OSError, EOFError, TimeoutError) as exc:
                 last = exc
                 time.sleep(0.1)
         else:

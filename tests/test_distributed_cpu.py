@@ -53,3 +53,41 @@ def test_gloo_world2_plumbing():
     assert res["steps"] == [(0, 32), (1, 32), (2, 32), (3, 32)]
     assert res["tokens"] > 0
     assert res["sync"]["pulls"] >= 4      # initial pull + one per published version
+
+
+def _worker4(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch
+    torch.set_num_threads(1)
+    from psrl_b200.config import load_config
+    from psrl_b200.parallel.dist import init_distributed
+    from psrl_b200.trainer.distributed import run_disaggregated
+    cfg = load_config(preset="cpu_tiny_grpo", overrides=["rollout.max_response_length=12",
+                                                         "psrl.deployment.train_ngpus=2"])
+    info = init_distributed("cpu", timeout_s=120)
+    res = run_disaggregated(cfg, steps=2, warmup=1, info=info)
+    if rank == 0:
+        q.put({"n_train": res["n_train"], "steps": [m["num_trajectories"] for m in res["metrics"]],
+               "pulls": res["sync"]["pulls"]})
+    import torch.distributed as dist
+    dist.destroy_process_group()
+
+
+def test_gloo_world4_two_trainers_two_rollouts():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker4, args=(r, 4, port, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0, 0, 0], codes
+    res = q.get(timeout=5)
+    assert res["n_train"] == 2 and res["steps"] == [32, 32]
+    assert res["pulls"] >= 2 * 3
