@@ -118,6 +118,8 @@ def main():
     ap.add_argument("--max-num-seqs", type=int, default=512)
     ap.add_argument("--kv-cache-gb", type=float, default=60.0)
     ap.add_argument("--override", action="append", default=[])
+    ap.add_argument("--placement", default="auto", choices=["auto", "colocated", "hybrid", "disaggregated"],
+                    help="auto: colocated on one GPU, hybrid (every GPU trains and serves rollout) on several")
     ap.add_argument("--verbose", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -128,9 +130,12 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", 1))
     import faulthandler
     faulthandler.dump_traceback_later(240, repeat=True)   # all-thread stacks if a run stalls
-    if args.gpus > 1 or world > 1:
+    placement = args.placement
+    if placement == "auto":
+        placement = "hybrid" if (args.gpus > 1 or world > 1) else "colocated"
+    if placement != "colocated":
         from psrl_b200.trainer.distributed import run_disaggregated_bench
-        res = run_disaggregated_bench(args)
+        res = run_disaggregated_bench(args, placement)
         if res is None:
             return
     else:

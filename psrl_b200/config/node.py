@@ -70,6 +70,11 @@ class ConfigNode(dict):
     def __deepcopy__(self, memo):
         return ConfigNode(copy.deepcopy(self.to_dict(resolve=False), memo))
 
+    def __reduce__(self):
+        # a root pickles its raw tree (interpolations stay live); a sub-node
+        # pickles resolved values, since its root does not travel with it
+        return ConfigNode, (self.to_dict(resolve=self._root is not None),)
+
     # -- interpolation ---------------------------------------------------------
     def _resolve(self, value, _depth: int = 0):
         if not isinstance(value, str) or "${" not in value:

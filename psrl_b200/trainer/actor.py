@@ -29,6 +29,30 @@ def _dtype(name: str, device) -> torch.dtype:
     return {"bf16": torch.bfloat16, "fp32": torch.float32, "fp16": torch.float16}[name]
 
 
+def mini_batch_groups(trajs: list[Trajectory], mini_batch_size: int) -> list[list[int]]:
+    """Split by prompt group into ``mini_batch_size`` groups per mini-batch."""
+    by_uid: dict = {}
+    for i, t in enumerate(trajs):
+        by_uid.setdefault(t.uid, []).append(i)
+    groups = list(by_uid.values())
+    per = max(1, int(mini_batch_size))
+    return [[i for g in groups[s: s + per] for i in g] for s in range(0, len(groups), per)]
+
+
+def plan_update(trajs: list[Trajectory], mini_batch_size: int, dp_world: int) -> list[list[tuple]]:
+    """Per data-parallel rank, the list of ``(my_indices, global_tokens, num_seqs)``
+    of every PPO mini-batch (token-balanced split of each mini-batch).  Every
+    rank gets one entry per mini-batch, so all ranks take the same number of
+    optimizer steps (and collectives)."""
+    plans: list[list[tuple]] = [[] for _ in range(dp_world)]
+    for mini in mini_batch_groups(trajs, mini_batch_size):
+        gt = float(sum(trajs[i].response_len for i in mini))
+        parts = balance_across_ranks([trajs[i] for i in mini], dp_world)
+        for r in range(dp_world):
+            plans[r].append(([mini[j] for j in parts[r]], gt, len(mini)))
+    return plans
+
+
 class PolicyWorker:
     def __init__(self, cfg, args: ModelArgs, device, dp_group=None, seed: int = 0, trainable: bool = True,
                  dp_rank: int = 0, dp_world: int = 1):
@@ -80,30 +104,27 @@ class PolicyWorker:
 
     # -------------------------------------------------------------- update
     def _mini_batches(self, trajs: list[Trajectory]) -> list[list[int]]:
-        """Split by prompt group into ``ppo_mini_batch_size`` groups per mini-batch."""
-        by_uid: dict = {}
-        for i, t in enumerate(trajs):
-            by_uid.setdefault(t.uid, []).append(i)
-        groups = list(by_uid.values())
-        per = max(1, int(self.cfg.actor.ppo_mini_batch_size))
-        return [[i for g in groups[s: s + per] for i in g] for s in range(0, len(groups), per)]
+        return mini_batch_groups(trajs, int(self.cfg.actor.ppo_mini_batch_size))
 
     def update_policy(self, trajs: list[Trajectory], temperature: float = 1.0, step_guard=None,
-                      sync_every_micro_batch: bool = False) -> dict:
+                      sync_every_micro_batch: bool = False, plan: list[tuple] | None = None) -> dict:
         """PPO-family update.  ``step_guard`` (a context manager) wraps each
         optimizer step, i.e. the in-place parameter update (the PS exclusive-push
-        lock when a colocated rollout reads the parameters concurrently)."""
+        lock when a colocated rollout reads the parameters concurrently).
+        ``plan`` (from :func:`plan_update`) gives this rank's share of each
+        mini-batch when ``trajs`` holds only this rank's trajectories; without it
+        every rank sees the whole batch and takes its token-balanced share."""
         import contextlib
         guard = step_guard if step_guard is not None else contextlib.nullcontext
         ac = self.cfg.actor
         self.model.train()
         stats: dict[str, list] = {}
         use_tis = bool(self.cfg.algorithm.rollout_correction.tis)
+        if plan is None:
+            plan = [(self.my_share(trajs, mini), float(sum(trajs[i].response_len for i in mini)), len(mini))
+                    for mini in self._mini_batches(trajs)]
         for _epoch in range(int(ac.ppo_epochs)):
-            for mini in self._mini_batches(trajs):
-                global_tokens = float(sum(trajs[i].response_len for i in mini))
-                num_seqs = len(mini)
-                mine = self.my_share(trajs, mini)
+            for mine, global_tokens, num_seqs in plan:
                 for bin_ in pack_micro_batches(mine, trajs, self.max_tokens):
                     mb = build_micro_batch(trajs, bin_, self.device)
                     lp, ent = self.model.logprobs(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen,

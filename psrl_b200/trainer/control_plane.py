@@ -1,0 +1,302 @@
+"""The control plane as its own CPU process, and the GPU ranks' clients of it.
+
+:class:`ControlPlane` hosts the Parameter Server (C8: versions, staleness
+inventory, request tracker, push/pull lock), the agent-loop manager (C12:
+dispatch-ahead bound, admission = Reserve, reward, Occupy, staleness aborts)
+and a batch server.  It runs in one CPU-only process spawned by rank 0
+(:func:`spawn_control_plane`), so its Python work never competes for the GIL of
+a process that drives a GPU; every GPU rank reaches it over the RPC transport
+(:mod:`psrl_b200.utils.rpc`).  This takes the place of the reference's Ray
+actors for the PS and the agent-loop manager, of the router's admission calls
+and of the TransferQueue hop (``psrl/ps/ps_manager.py``,
+``psrl/workers/agent_loop/manager.py``, ``psrl/trainer/ppo/ray_trainer.py``).
+
+* Rollout instances call ``exchange`` (finished trajectories in; new requests,
+  aborts, the PS version and the run phase out) from an
+  :class:`ExchangeMailbox` thread, so an engine never waits on the control
+  plane between decode steps.
+* Trainer ranks call ``get_batch(b, rank)``: the first caller waits until
+  staleness buffer ``b`` is READY (failing fast when an instance reported an
+  error or went silent), consumes it, computes advantages and plans the PPO
+  mini-batches with a token-balanced split over the data-parallel ranks; each
+  rank receives only its own trajectories plus its plan, so no rank unpickles
+  the whole batch.
+* After every trainer rank finished its optimizer step, rank 0 calls
+  ``push_model(v)`` (PS version bump under the exclusive push lock).
+"""
+
+from __future__ import annotations
+
+import threading
+import time
+
+from ..utils.rpc import RPCClient, RPCServer
+
+
+class ControlPlane:
+    def __init__(self, cfg, vocab_size: int, n_train: int, liveness_s: float = 300.0):
+        from ..agent.data import DataProcessor
+        from ..agent.manager import AgentLoopManager
+        from ..config import redundant_settings
+        from ..ps import PSManager
+        from ..reward import RewardManager
+        self.cfg = cfg
+        rn, _, _, _ = redundant_settings(cfg)
+        self.ps = PSManager.from_config(cfg)
+        self.data = DataProcessor(cfg, vocab_size, rn)
+        self.reward = RewardManager(cfg, self.data.tokenizer)
+        self.manager = AgentLoopManager(cfg, self.ps, self.data, self.reward)
+        self.n_train = int(n_train)
+        self.liveness_s = float(liveness_s)
+        self.phase = 0
+        self.last_seen: dict = {}
+        self.failed: dict = {}
+        self.sync_stats = {"pulls": 0, "pull_s": 0.0}
+        self.exchange_stats = {"calls": 0, "outputs": 0, "requests": 0}
+        self.stores: dict[int, dict] = {}
+        self.layout = None
+        self._cv = threading.Condition()
+        self._batches: dict[int, dict] = {}
+        self._batch_locks: dict[int, threading.Lock] = {}
+        self._done = threading.Event()
+
+    # ----------------------------------------------------------------- setup
+    def ping(self) -> bool:
+        return True
+
+    def eos_id(self):
+        return self.data.tokenizer.eos_id
+
+    def register_store(self, trainer_rank: int, desc: dict) -> None:
+        with self._cv:
+            self.stores[int(trainer_rank)] = desc
+            self._cv.notify_all()
+
+    def set_layout(self, layout) -> None:
+        with self._cv:
+            self.layout = layout
+            self._cv.notify_all()
+
+    def get_stores(self, timeout: float = 600.0) -> tuple:
+        with self._cv:
+            ok = self._cv.wait_for(lambda: len(self.stores) == self.n_train and self.layout is not None, timeout)
+            if not ok:
+                raise TimeoutError("trainer stores were not registered in time")
+            return self.layout, [self.stores[r] for r in range(self.n_train)]
+
+    def register_instance(self, instance_id, version: int) -> None:
+        iid = tuple(instance_id)
+        self.ps.register_rollout_instance(iid, int(version))
+        self.last_seen[iid] = time.monotonic()
+
+    def report_failure(self, instance_id, message: str) -> None:
+        self.failed[tuple(instance_id)] = message
+
+    def set_phase(self, p: int) -> None:
+        self.phase = int(p)
+
+    def shutdown(self) -> None:
+        self._done.set()
+
+    # --------------------------------------------------------------- rollout
+    def exchange(self, instance_id, version: int, free_slots: int, outputs: list):
+        iid = tuple(instance_id)
+        self.last_seen[iid] = time.monotonic()
+        if outputs:
+            self.manager.on_complete(outputs, iid)
+        reqs = self.manager.take_work(iid, int(version), int(free_slots)) if free_slots > 0 else []
+        aborts = self.manager.take_aborts(iid)
+        st = self.exchange_stats
+        st["calls"] += 1
+        st["outputs"] += len(outputs)
+        st["requests"] += len(reqs)
+        return reqs, aborts, self.ps.get_ps_model_version(), self.phase
+
+    def acquire_pull(self, timeout: float = 600.0) -> bool:
+        return self.ps.acquire_shared_pull(timeout)
+
+    def release_pull(self) -> None:
+        self.ps.release_shared_pull()
+
+    def pull_model(self, instance_id, seconds: float | None = None) -> int:
+        v, _ = self.ps.pull_model(tuple(instance_id))
+        if seconds is not None:
+            self.report_pull(seconds)
+        return v
+
+    def report_pull(self, seconds: float) -> None:
+        self.sync_stats["pulls"] += 1
+        self.sync_stats["pull_s"] += float(seconds)
+
+    # --------------------------------------------------------------- trainer
+    def _wait_ready(self, b: int, timeout_s: float) -> None:
+        t0 = time.monotonic()
+        while not self.manager.buffer_ready(b):
+            if self.failed:
+                raise RuntimeError(f"rollout instance failed: {self.failed}")
+            now = time.monotonic()
+            silent = [i for i, t in self.last_seen.items() if now - t > self.liveness_s]
+            if silent or now - t0 > timeout_s:
+                raise TimeoutError(f"buffer {b} not ready: silent instances {silent}, {self.manager.snapshot()}")
+            time.sleep(0.002)
+
+    def _build(self, b: int, dp_world: int, timeout_s: float) -> dict:
+        from ..trainer.actor import plan_update
+        from ..trainer.driver import compute_batch_advantages
+        self._wait_ready(b, timeout_s)
+        trajs = self.manager.consume(b)
+        use_rollout_lp = bool(self.cfg.psrl.log_prob.enable_rollout_engine_log_prob)
+        for t in trajs:
+            t.old_logprobs = t.rollout_logprobs if use_rollout_lp else None
+        adv_metrics = compute_batch_advantages(self.cfg, trajs)
+        plans = plan_update(trajs, int(self.cfg.actor.ppo_mini_batch_size), dp_world)
+        per_rank = {}
+        for r in range(dp_world):
+            need = sorted({i for mine, _, _ in plans[r] for i in mine})
+            local = {g: j for j, g in enumerate(need)}
+            per_rank[r] = {"trajs": [trajs[i] for i in need],
+                           "plan": [([local[i] for i in mine], gt, ns) for mine, gt, ns in plans[r]]}
+        return {
+            "per_rank": per_rank, "left": set(range(dp_world)), "metrics": adv_metrics,
+            "num_trajectories": len(trajs), "trained_tokens": sum(len(t.prompt_ids) + t.response_len for t in trajs),
+            "response_length/mean": sum(t.response_len for t in trajs) / max(1, len(trajs)),
+            "staleness/max": max((b - t.version_tag) for t in trajs) if trajs else 0,
+        }
+
+    def get_batch(self, b: int, rank: int, dp_world: int, timeout_s: float = 1800.0) -> dict:
+        """Rank ``rank``'s share of staleness buffer ``b`` (blocks until READY)."""
+        b, rank = int(b), int(rank)
+        with self._cv:
+            lk = self._batch_locks.setdefault(b, threading.Lock())
+        with lk:
+            if b not in self._batches:
+                self._batches[b] = self._build(b, int(dp_world), timeout_s)
+            ent = self._batches[b]
+        mine = ent["per_rank"].pop(rank)
+        ent["left"].discard(rank)
+        if not ent["left"]:
+            with self._cv:
+                self._batches.pop(b, None)
+                self._batch_locks.pop(b, None)
+        out = {k: v for k, v in ent.items() if k not in ("per_rank", "left")}
+        out.update(mine)
+        return out
+
+    def push_model(self, version: int) -> None:
+        if not self.ps.acquire_exclusive_push(timeout=600):
+            raise TimeoutError("exclusive push lock")
+        try:
+            self.ps.push_model(int(version))
+        finally:
+            self.ps.release_exclusive_push()
+
+    def get_ps_version(self) -> int:
+        return self.ps.get_ps_model_version()
+
+    def stats(self) -> dict:
+        return {"sync": dict(self.sync_stats), "exchange": dict(self.exchange_stats),
+                "manager": self.manager.snapshot(), "ps_version": self.ps.get_ps_model_version()}
+
+
+def _control_plane_main(cfg, vocab_size: int, n_train: int, port: int, liveness_s: float) -> None:
+    import os
+    os.environ["CUDA_VISIBLE_DEVICES"] = ""        # this process never touches a GPU
+    import torch
+    torch.set_num_threads(1)
+    cp = ControlPlane(cfg, vocab_size, n_train, liveness_s)
+    server = RPCServer({"cp": cp}, port=port)
+    try:
+        cp._done.wait()
+    finally:
+        server.close()
+
+
+def spawn_control_plane(cfg, vocab_size: int, n_train: int, port: int, liveness_s: float = 300.0):
+    """Start the control-plane process (rank 0 calls this once); returns the process."""
+    import multiprocessing as mp
+    p = mp.get_context("spawn").Process(target=_control_plane_main, args=(cfg, vocab_size, n_train, port, liveness_s),
+                                        daemon=True, name="psrl-control-plane")
+    p.start()
+    return p
+
+
+def connect(port: int, timeout: float = 1800.0) -> RPCClient:
+    c = RPCClient(("127.0.0.1", int(port)), timeout=timeout)
+    return c
+
+
+class ExchangeMailbox:
+    """Runs a rollout instance's ``exchange`` RPCs on a background thread.
+
+    The engine loop ``post``s finished outputs and ``collect``s the requests and
+    aborts that came back; the thread batches outputs for at least
+    ``min_interval`` seconds, asks for as many requests as the engine has free
+    slots (minus those already received but not yet added), and keeps a
+    heartbeat every ``idle_interval`` seconds even when nothing happens.
+    """
+
+    def __init__(self, proxy, instance_id, engine, min_interval: float = 0.004, idle_interval: float = 0.02):
+        self.proxy = proxy
+        self.instance_id = tuple(instance_id)
+        self.engine = engine
+        self.min_interval = float(min_interval)
+        self.idle_interval = float(idle_interval)
+        self.ps_version = int(engine.version)
+        self.phase = 0
+        self.error: BaseException | None = None
+        self._lock = threading.Lock()
+        self._outputs: list = []
+        self._reqs: list = []
+        self._aborts: list = []
+        self._wake = threading.Event()
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._loop, daemon=True, name="exchange")
+        self._thread.start()
+
+    def post(self, outputs: list) -> None:
+        if outputs:
+            with self._lock:
+                self._outputs.extend(outputs)
+            self._wake.set()
+
+    def collect(self) -> tuple[list, list]:
+        with self._lock:
+            reqs, aborts = self._reqs, self._aborts
+            self._reqs, self._aborts = [], []
+        if self.error is not None:
+            raise RuntimeError("control-plane exchange failed") from self.error
+        return reqs, aborts
+
+    def kick(self) -> None:
+        self._wake.set()
+
+    def _loop(self) -> None:
+        last = 0.0
+        eng = self.engine
+        try:
+            while not self._stop.is_set():
+                self._wake.wait(self.idle_interval)
+                self._wake.clear()
+                if self._stop.is_set():
+                    break
+                dt = time.monotonic() - last
+                if dt < self.min_interval:
+                    time.sleep(self.min_interval - dt)
+                with self._lock:
+                    outs, self._outputs = self._outputs, []
+                    queued = len(self._reqs)
+                free = max(0, eng.max_num_seqs - eng.num_unfinished() - queued)
+                reqs, aborts, v, phase = self.proxy.exchange(self.instance_id, eng.version, free, outs)
+                last = time.monotonic()
+                with self._lock:
+                    self._reqs.extend(reqs)
+                    self._aborts.extend(aborts)
+                self.ps_version = int(v)
+                self.phase = int(phase)
+        except BaseException as exc:     # surfaced to the engine loop by collect()
+            self.error = exc
+
+    def close(self) -> None:
+        self._stop.set()
+        self._wake.set()
+        self._thread.join(timeout=30)

@@ -381,8 +381,10 @@ def run_disaggregated(cfg, steps: int, warmup: int, info: pdist.DistInfo | None 
     return out
 
 
-def run_disaggregated_bench(args):
-    """bench.py entry for N > 1 GPUs (launched by torch.distributed.run)."""
+def run_disaggregated_bench(args, placement: str = "disaggregated"):
+    """bench.py entry for torch.distributed.run launches (N >= 1 ranks):
+    ``placement`` is ``disaggregated`` (trainer ranks + rollout ranks) or
+    ``hybrid`` (every rank trains and serves rollout, :mod:`.hybrid`)."""
     from bench import build_cfg
     from ..ops import _ext
     from ..utils import transfer
@@ -393,7 +395,15 @@ def run_disaggregated_bench(args):
     sampler = ClockSampler(list(range(info.world_size))).start() if info.rank == 0 else None
     l0 = _ext.launches()
     b0, o0 = transfer.snapshot()
-    res = run_disaggregated(cfg, args.steps, args.warmup, info)
+    if placement == "hybrid":
+        from .hybrid import run_hybrid
+        res = run_hybrid(cfg, args.steps, args.warmup, info)
+        n_train = res["world"]
+        par = f"hybrid: train dp{n_train} + {n_train} overlapped rollout instances (tp1), local weight sync"
+    else:
+        res = run_disaggregated(cfg, args.steps, args.warmup, info)
+        n_train = res["n_train"]
+        par = f"train dp{n_train} + rollout dp{res['world'] - n_train} (tp1)"
     launches = pdist.all_reduce_sum(float(_ext.launches() - l0), info.device)
     b1, o1 = transfer.snapshot()
     h2d = pdist.all_reduce_sum(float(b1 - b0), info.device)
@@ -402,11 +412,10 @@ def run_disaggregated_bench(args):
     pdist.destroy()
     if info.rank != 0:
         return None
-    n_train = res["n_train"]
     res.update({
         "launches": launches, "clocks": clocks,
         "h2d": h2d / max(1, args.steps + args.warmup), "d2h": d2h / max(1, args.steps + args.warmup),
         "global_batch": cfg.psrl.staleness_buffer_entries * cfg.psrl.rollout_n,
-        "parallelism": f"train dp{n_train} + rollout dp{res['world'] - n_train} (tp1)",
+        "parallelism": par,
     })
     return res

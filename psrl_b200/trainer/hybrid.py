@@ -1,0 +1,281 @@
+"""Hybrid multi-GPU placement: every rank trains AND serves rollout.
+
+N processes, one per GPU (``torch.distributed.run``).  Each rank
+
+* trains: a full bf16 replica of the policy under
+  :class:`~psrl_b200.parallel.fsdp.FlatShardedDP` over all N ranks (fp32
+  gradients reduce-scattered, sharded AdamW, parameters all-gathered back —
+  NCCL over NVLink), on its token-balanced share of every staleness buffer;
+* serves rollout: one engine in its own thread on a high-priority stream,
+  overlapped with training exactly like the one-GPU colocation (the staleness
+  bound makes training on buffer ``b`` while generating later buffers legal);
+* syncs weights locally: after the optimizer step that produces version
+  ``v + 1`` every rank's parameters equal that version, so its engine pulls
+  with one in-HBM copy of the flat parameter buffer.  No weight byte crosses
+  NVLink; the only inter-GPU traffic is the gradient reduce-scatter and the
+  parameter all-gather of the optimizer step.
+
+The Parameter Server, the dispatcher and the batch planner run in a separate
+CPU process (:mod:`.control_plane`); rank 0 starts it.  The process-local
+reader-writer lock orders the in-place optimizer update (exclusive) against
+the engine's weight copy (shared); the global version is bumped by rank 0 only
+after every rank finished its optimizer step, so an engine's version label
+never exceeds the weights it holds.
+
+The reference runs trainers and rollout replicas as disjoint Ray resource
+pools (``psrl/trainer/main_ppo.py``, ``psrl/trainer/ppo/ray_trainer.py``);
+:mod:`.distributed` provides that disaggregated placement, this module the
+colocated one scaled out.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import os
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+from ..models import model_args_from_config
+from ..parallel import dist as pdist
+from ..parallel.weight_sync import WeightLayout
+from ..rollout.engine import EngineWeights, RolloutEngine
+from ..rollout.instance import SyncPolicy
+from ..utils.locks import RWLock
+from ..utils.rpc import RPCClient
+from .actor import PolicyWorker
+from .control_plane import ExchangeMailbox, spawn_control_plane
+
+
+def log(msg: str) -> None:
+    r = os.environ.get("RANK", "0")
+    print(f"[rank {r} {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
+class HybridRun:
+    def __init__(self, cfg, info: pdist.DistInfo):
+        self.cfg = cfg
+        self.info = info
+        self.rank, self.world = info.rank, info.world_size
+        self.device = info.device
+        self.is_cuda = self.device.type == "cuda"
+        self.args = model_args_from_config(cfg.model)
+        if cfg.critic.enable or cfg.algorithm.use_kl_in_reward:
+            raise NotImplementedError("hybrid placement trains critic-free estimators without in-reward KL; "
+                                      "use the one-GPU trainer or the disaggregated placement")
+        self.trained_tokens = 0
+        self.global_step = 0
+        self.liveness_s = float(cfg.trainer.get("liveness_timeout_s", 300))
+        self.buffer_timeout_s = float(cfg.trainer.get("buffer_timeout_s", 1800))
+        port = int(os.environ.get("MASTER_PORT", "29511")) + 23
+        self.cp_proc = None
+        if self.rank == 0:
+            self.cp_proc = spawn_control_plane(cfg, self.args.vocab_size, self.world, port, self.liveness_s)
+            self.cli_train = RPCClient(("127.0.0.1", port), retries=6000)
+            self.cli_train.call("cp", "ping")
+        pdist.barrier()
+        if self.rank != 0:
+            self.cli_train = RPCClient(("127.0.0.1", port), retries=6000)
+        self.cli_roll = RPCClient(("127.0.0.1", port), retries=6000)
+        self.cp = self.cli_train.proxy("cp")
+        self.cp_roll = self.cli_roll.proxy("cp")
+        self.cpu_group = pdist.new_subgroup(list(range(self.world)), backend="gloo") if self.world > 1 else None
+        dp_group = dist.group.WORLD if self.world > 1 else None
+        seed = int(cfg.trainer.seed)
+        self.actor = PolicyWorker(cfg, self.args, self.device, dp_group=dp_group, seed=seed,
+                                  dp_rank=self.rank, dp_world=self.world)
+        self.ref = None
+        if cfg.actor.use_kl_loss:
+            self.ref = PolicyWorker(cfg, self.args, self.device, seed=seed, trainable=False)
+        self.wlock = RWLock()
+        # engine weights: one flat copy in the trainer's flat layout (a pull is one copy)
+        layout = WeightLayout.from_dp(self.actor.dp)
+        self.eng_flat = self.actor.dp.flat.detach().clone()
+        w = EngineWeights(self.args, self.device, self.actor.dtype)
+        w.flat = self.eng_flat
+        w.tensors = layout.views(self.eng_flat)
+        for name, b in self.actor.model.named_buffers():
+            w.tensors[name] = b.to(self.device)
+        self.engine_weights = w
+        rc = cfg.rollout
+        max_len = int(rc.max_prompt_length) + int(rc.max_response_length) + 64
+        self.engine = RolloutEngine(
+            self.args, w, max_num_seqs=int(rc.max_num_seqs), max_model_len=max_len, block_size=int(rc.block_size),
+            max_num_batched_tokens=int(rc.max_num_batched_tokens), kv_cache_gb=float(rc.get("kv_cache_gb", 4.0)),
+            enable_prefix_caching=bool(rc.enable_prefix_caching), use_cuda_graph=bool(rc.cuda_graph),
+            keep_kv_on_update=bool(cfg.psrl.rollout_coordination.partial_rollout.get("keep_kv", False)),
+            eos_token_id=None if rc.ignore_eos else self.cp.eos_id())
+        sm = cfg.psrl.rollout_coordination.sync_and_mig_strategy
+        self.policy = SyncPolicy(sm.method, bool(cfg.psrl.rollout_coordination.partial_rollout.enable),
+                                 sm.sync.get("threshold"), sm.sync.get("indicator", "request_num"))
+        self.instance_id = (self.rank, 0)
+        self.cp.register_instance(self.instance_id, self.engine.version)
+        self.rollout_stream = torch.cuda.Stream(device=self.device, priority=-1) if self.is_cuda else None
+        self.mailbox: ExchangeMailbox | None = None
+        self._thread = None
+        self._stop = False
+        self._rollout_error: BaseException | None = None
+        self.pulls = 0
+        self.pull_s = 0.0
+        log(f"hybrid rank ready: trainer dp{self.world} + rollout instance {self.instance_id}")
+
+    # -------------------------------------------------------------- rollout
+    def _pull(self) -> None:
+        t0 = time.perf_counter()
+        with self.wlock.shared(600):
+            # the PS version is read first: the local parameters are at least that new
+            v = self.cp_roll.pull_model(self.instance_id)
+            self.eng_flat.copy_(self.actor.dp.flat, non_blocking=True)
+            if self.is_cuda:
+                torch.cuda.current_stream().synchronize()
+        self.engine.load_weights(None, v)
+        dt = time.perf_counter() - t0
+        self.pulls += 1
+        self.pull_s += dt
+        self.cp_roll.report_pull(dt)
+
+    def _rollout_loop(self) -> None:
+        eng = self.engine
+        mb = self.mailbox
+        try:
+            ctx = torch.cuda.stream(self.rollout_stream) if self.is_cuda else contextlib.nullcontext()
+            with ctx:
+                while not self._stop:
+                    reqs, aborts = mb.collect()
+                    for r in reqs:
+                        eng.add_request(r)
+                    for rid in aborts:
+                        eng.abort(rid)
+                    if self.policy.should_sync(eng, mb.ps_version):
+                        self._pull()
+                    if eng.has_unfinished():
+                        outs = eng.step()
+                        if outs:
+                            mb.post(outs)
+                    else:
+                        mb.kick()
+                        time.sleep(0.0005)
+        except BaseException as exc:    # surfaced to the trainer thread and the control plane
+            self._rollout_error = exc
+            with contextlib.suppress(Exception):
+                self.cp_roll.report_failure(self.instance_id, f"{type(exc).__name__}: {exc}")
+
+    def start_rollout(self) -> None:
+        if self._thread is None:
+            import threading
+            self._stop = False
+            self.mailbox = ExchangeMailbox(self.cp_roll, self.instance_id, self.engine)
+            self._thread = threading.Thread(target=self._rollout_loop, daemon=True, name="rollout")
+            self._thread.start()
+
+    def stop_rollout(self) -> None:
+        if self._thread is not None:
+            self._stop = True
+            self._thread.join()
+            self._thread = None
+        if self.mailbox is not None:
+            self.mailbox.close()
+            self.mailbox = None
+
+    # -------------------------------------------------------------- training
+    def step(self) -> dict:
+        b = self.global_step
+        if self._rollout_error is not None:
+            raise RuntimeError("rollout thread failed") from self._rollout_error
+        self.start_rollout()
+        t0 = time.perf_counter()
+        batch = self.cp.get_batch(b, self.rank, self.world, self.buffer_timeout_s)
+        trajs, plan = batch["trajs"], batch["plan"]
+        t1 = time.perf_counter()
+        idx = list(range(len(trajs)))
+        if self.ref is not None:
+            self.ref.compute_log_prob(trajs, idx, field="ref_logprobs")
+        if not bool(self.cfg.psrl.log_prob.enable_rollout_engine_log_prob):
+            self.actor.compute_log_prob(trajs, idx, field="old_logprobs")
+        metrics = self.actor.update_policy(trajs, float(self.cfg.rollout.temperature),
+                                           step_guard=lambda: self.wlock.exclusive(600),
+                                           sync_every_micro_batch=self.is_cuda, plan=plan)
+        t2 = time.perf_counter()
+        if self.cpu_group is not None:
+            dist.barrier(group=self.cpu_group)      # every replica holds version b + 1
+        if self.rank == 0:
+            self.cp.push_model(b + 1)
+        self.global_step += 1
+        self.trained_tokens += int(batch["trained_tokens"])
+        metrics.update(batch["metrics"])
+        metrics.update({
+            "step": b, "num_trajectories": batch["num_trajectories"], "trained_tokens": batch["trained_tokens"],
+            "response_length/mean": batch["response_length/mean"], "staleness/max": batch["staleness/max"],
+            "timing_s/gen_wait": t1 - t0, "timing_s/train": t2 - t1, "timing_s/step": time.perf_counter() - t0,
+            "rollout/pulls": self.pulls, "rollout/pull_s": self.pull_s,
+        })
+        metrics.update({f"rollout/{k}": v for k, v in self.engine.engine_stats().items() if isinstance(v, (int, float))})
+        return metrics
+
+    def close(self) -> None:
+        self.stop_rollout()
+        if self.rank == 0:
+            with contextlib.suppress(Exception):
+                self.cp.shutdown()
+        for c in (self.cli_roll, self.cli_train):
+            c.close()
+        if self.cp_proc is not None:
+            self.cp_proc.join(timeout=30)
+            if self.cp_proc.is_alive():
+                self.cp_proc.terminate()
+
+
+def run_hybrid(cfg, steps: int, warmup: int, info: pdist.DistInfo | None = None, capture: bool = True) -> dict:
+    """``warmup`` + ``steps`` training steps on every rank; returns the timing
+    (max over ranks) and, on rank 0, metrics, token counts and control-plane stats."""
+    info = info or pdist.init_distributed(cfg.trainer.get("device", "auto"))
+    run = HybridRun(cfg, info)
+    is_cuda = info.device.type == "cuda"
+    if capture and is_cuda and run.engine.use_cuda_graph:
+        run.engine.capture_all()
+    t_evt: dict = {}
+
+    def mark(p):
+        pdist.barrier()
+        if is_cuda:
+            torch.cuda.synchronize()
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            t_evt[p] = ev
+        t_evt[f"wall{p}"] = time.perf_counter()
+
+    metrics = []
+    try:
+        for i in range(warmup):
+            m = run.step()
+            if run.rank == 0:
+                log(f"warm-up step {i}: {m['timing_s/step']:.1f}s (wait {m['timing_s/gen_wait']:.1f}s), "
+                    f"{m['trained_tokens']} tokens")
+        mark(1)
+        for i in range(steps):
+            metrics.append(run.step())
+            if run.rank == 0:
+                m = metrics[-1]
+                log(f"timed step {i}: {m['timing_s/step']:.1f}s (wait {m['timing_s/gen_wait']:.1f}s), "
+                    f"{m['trained_tokens']} tokens")
+        mark(2)
+        if is_cuda:
+            torch.cuda.synchronize()
+            ms = t_evt[1].elapsed_time(t_evt[2])
+        else:
+            ms = (t_evt["wall2"] - t_evt["wall1"]) * 1000.0
+        wall = t_evt["wall2"] - t_evt["wall1"]
+        run.stop_rollout()
+        ms_max = pdist.all_reduce_max(ms, info.device)
+        wall_max = pdist.all_reduce_max(wall, info.device)
+        out = {"ms": ms_max, "wall_s": wall_max, "rank": run.rank, "metrics": metrics, "world": run.world,
+               "tokens": sum(int(m["trained_tokens"]) for m in metrics),
+               "param_checksum": float(run.actor.dp.flat.double().sum())}
+        if run.rank == 0:
+            out["cp"] = run.cp.stats()
+        pdist.barrier()
+    finally:
+        run.close()
+    return out

@@ -67,3 +67,60 @@ def wait_for_version(get_version, target: int, timeout: float = 600.0, poll_s: f
         if time.monotonic() - t0 > timeout:
             raise TimeoutError(f"version {target} not reached (at {v})")
         time.sleep(poll_s)
+
+
+class RWLock:
+    """Process-local reader-writer lock with bounded waits: the optimizer step of
+    a colocated trainer holds it exclusively (in-place parameter update) while
+    the rollout engine's weight pull holds it shared (reads the parameters)."""
+
+    def __init__(self):
+        self._cv = threading.Condition()
+        self._writer = False
+        self._readers = 0
+
+    def acquire_exclusive(self, timeout: float | None = None) -> bool:
+        with self._cv:
+            return self._cv.wait_for(lambda: not self._writer and self._readers == 0, timeout) and \
+                self._set_writer()
+
+    def _set_writer(self) -> bool:
+        self._writer = True
+        return True
+
+    def release_exclusive(self) -> None:
+        with self._cv:
+            self._writer = False
+            self._cv.notify_all()
+
+    def acquire_shared(self, timeout: float | None = None) -> bool:
+        with self._cv:
+            if not self._cv.wait_for(lambda: not self._writer, timeout):
+                return False
+            self._readers += 1
+            return True
+
+    def release_shared(self) -> None:
+        with self._cv:
+            if self._readers <= 0:
+                raise RuntimeError("shared lock released more often than acquired")
+            self._readers -= 1
+            self._cv.notify_all()
+
+    @contextlib.contextmanager
+    def exclusive(self, timeout: float | None = 600.0):
+        if not self.acquire_exclusive(timeout):
+            raise TimeoutError("exclusive lock not acquired")
+        try:
+            yield
+        finally:
+            self.release_exclusive()
+
+    @contextlib.contextmanager
+    def shared(self, timeout: float | None = 600.0):
+        if not self.acquire_shared(timeout):
+            raise TimeoutError("shared lock not acquired")
+        try:
+            yield
+        finally:
+            self.release_shared()

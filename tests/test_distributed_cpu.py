@@ -91,3 +91,47 @@ def test_gloo_world4_two_trainers_two_rollouts():
     res = q.get(timeout=5)
     assert res["n_train"] == 2 and res["steps"] == [32, 32]
     assert res["pulls"] >= 2 * 3
+
+
+def _worker_hybrid(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch
+    torch.set_num_threads(1)
+    from psrl_b200.config import load_config
+    from psrl_b200.parallel.dist import init_distributed
+    from psrl_b200.trainer.hybrid import run_hybrid
+    cfg = load_config(preset="cpu_tiny_grpo", overrides=["rollout.max_response_length=12"])
+    info = init_distributed("cpu", timeout_s=120)
+    res = run_hybrid(cfg, steps=2, warmup=1, info=info)
+    q.put({"rank": rank, "checksum": res["param_checksum"]})
+    if rank == 0:
+        q.put({"steps": [m["num_trajectories"] for m in res["metrics"]], "tokens": res["tokens"],
+               "pulls": res["cp"]["sync"]["pulls"], "ps_version": res["cp"]["ps_version"]})
+    import torch.distributed as dist
+    dist.destroy_process_group()
+
+
+def test_gloo_world2_hybrid_placement():
+    """Every rank trains (data parallel over gloo) and serves a rollout instance;
+    the control plane runs in its own process."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_hybrid, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0], codes
+    items = [q.get(timeout=5) for _ in range(3)]
+    sums = {d["rank"]: d["checksum"] for d in items if "checksum" in d}
+    res = next(d for d in items if "steps" in d)
+    assert sums[0] == sums[1]         # identical replicas after the data-parallel steps
+    assert res["steps"] == [32, 32] and res["tokens"] > 0
+    assert res["ps_version"] == 3
+    assert res["pulls"] >= 2          # both engines picked up at least one new version

@@ -125,4 +125,51 @@ def test_disaggregated_rl_two_gpus():
     assert codes == [0, 0], codes
     res = q.get(timeout=5)
     assert res["steps"] == [32, 32]
-    assert res["pulls"] >= 4 and res["ms"] > 0
+    assert res["pulls"] >= 3 and res["ms"] > 0     # initial pull + at least one per step
+
+
+def _hybrid_worker(rank, world, port, q):
+    import faulthandler
+    faulthandler.dump_traceback_later(90, repeat=True)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    from psrl_b200.config import load_config
+    from psrl_b200.parallel.dist import init_distributed
+    from psrl_b200.trainer.hybrid import run_hybrid
+    cfg = load_config(preset="cpu_tiny_grpo", overrides=[
+        "model.preset=tiny128", "model.dtype=bf16", "trainer.device=cuda",
+        "rollout.cuda_graph=true", "data.kind=synthetic_tokens", "data.prompt_len_min=16", "data.prompt_len_max=64",
+        "data.response_len_mu=3.0", "data.response_len_sigma=0.5", "data.response_len_cap=64",
+        "reward.kind=bernoulli_hash", "rollout.ignore_eos=true"])
+    info = init_distributed("cuda", timeout_s=60)
+    res = run_hybrid(cfg, steps=2, warmup=1, info=info)
+    q.put({"rank": rank, "checksum": res["param_checksum"]})
+    if rank == 0:
+        q.put({"steps": [m["num_trajectories"] for m in res["metrics"]], "ps_version": res["cp"]["ps_version"],
+               "ms": res["ms"]})
+    dist.destroy_process_group()
+
+
+def test_hybrid_rl_two_gpus():
+    """Both GPUs train (NCCL data parallel) and serve rollout; replicas stay identical."""
+    _need(2)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_hybrid_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(240)
+    codes = [p.exitcode for p in ps]
+    for p in ps:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0], codes
+    items = [q.get(timeout=5) for _ in range(3)]
+    sums = {d["rank"]: d["checksum"] for d in items if "checksum" in d}
+    res = next(d for d in items if "steps" in d)
+    assert sums[0] == sums[1]
+    assert res["steps"] == [32, 32] and res["ps_version"] == 3 and res["ms"] > 0
