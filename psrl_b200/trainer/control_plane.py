@@ -182,7 +182,18 @@ class ControlPlane:
         out.update(mine)
         return out
 
-    def push_model(self, version: int) -> None:
+    def acquire_push(self, timeout: float = 600.0) -> bool:
+        return self.ps.acquire_exclusive_push(timeout)
+
+    def release_push(self) -> None:
+        self.ps.release_exclusive_push()
+
+    def push_model(self, version: int, locked: bool = False) -> None:
+        """Publish ``version``; ``locked`` means the caller already holds the
+        exclusive push lock (it wrote weight stores that rollout ranks read)."""
+        if locked:
+            self.ps.push_model(int(version))
+            return
         if not self.ps.acquire_exclusive_push(timeout=600):
             raise TimeoutError("exclusive push lock")
         try:

@@ -1,11 +1,13 @@
 """Disaggregated asynchronous RL over N processes (one per device).
 
 Ranks ``[0, T)`` train (sharded data parallel over an NCCL group), ranks
-``[T, N)`` each run one rollout instance.  Rank 0 additionally hosts the
-Parameter Server, the dispatcher (agent-loop manager, reward) and an RPC
-service the rollout ranks talk to (this replaces the reference's Ray actors,
-the SMG router's gRPC admission calls and the TransferQueue hop: trajectories
-travel back in the same RPC that fetches new work).
+``[T, N)`` each run one rollout instance.  The Parameter Server, the
+dispatcher (agent-loop manager, reward) and the batch planner run in a CPU
+control-plane process started by rank 0 (:mod:`.control_plane`); rollout ranks
+talk to it through an asynchronous exchange mailbox (trajectories travel back
+in the same RPC that fetches new work, which replaces the reference's Ray
+actors, the SMG router's gRPC admission calls and the TransferQueue hop), and
+each trainer rank fetches only its own token-balanced share of a buffer.
 
 Weights: every trainer rank publishes its parameters into its
 :class:`~psrl_b200.parallel.weight_sync.WeightStore` (HBM) under the PS
@@ -18,96 +20,23 @@ world_size=2 plumbing configuration).
 
 from __future__ import annotations
 
+import contextlib
 import os
 import sys
-import threading
 import time
 
 import torch
 import torch.distributed as dist
 
-from ..agent.data import DataProcessor
-from ..agent.manager import AgentLoopManager
-from ..config import redundant_settings
-from ..models import build_model, model_args_from_config
+from ..models import model_args_from_config
 from ..models.qwen import zipf_prior
 from ..parallel import dist as pdist
 from ..parallel.weight_sync import WeightLayout, WeightPuller, WeightStore
-from ..ps import PSManager
-from ..reward import RewardManager
 from ..rollout.engine import EngineWeights, RolloutEngine
 from ..rollout.instance import SyncPolicy
-from ..utils.rpc import RPCClient, RPCServer
+from ..utils.rpc import RPCClient
 from .actor import PolicyWorker
-from .driver import compute_batch_advantages
-
-
-class DispatcherService:
-    """Rank-0 control plane exposed to rollout ranks."""
-
-    def __init__(self, cfg, ps: PSManager, manager: AgentLoopManager, n_train: int):
-        self.cfg = cfg
-        self.ps = ps
-        self.manager = manager
-        self.n_train = n_train
-        self.stores: dict[int, dict] = {}
-        self.layout = None
-        self.phase = 0
-        self._cv = threading.Condition()
-        self.sync_stats = {"pulls": 0, "pull_s": 0.0}
-        self.last_seen: dict = {}
-        self.failed: dict = {}
-
-    # setup
-    def register_store(self, trainer_rank: int, desc: dict) -> None:
-        with self._cv:
-            self.stores[trainer_rank] = desc
-            self._cv.notify_all()
-
-    def set_layout(self, layout) -> None:
-        with self._cv:
-            self.layout = layout
-            self._cv.notify_all()
-
-    def get_stores(self, timeout: float = 600.0) -> tuple:
-        with self._cv:
-            ok = self._cv.wait_for(lambda: len(self.stores) == self.n_train and self.layout is not None, timeout)
-            if not ok:
-                raise TimeoutError("trainer stores were not registered in time")
-            return self.layout, [self.stores[r] for r in range(self.n_train)]
-
-    def register_instance(self, instance_id, version: int) -> None:
-        self.ps.register_rollout_instance(tuple(instance_id), version)
-
-    # steady state
-    def report_failure(self, instance_id, message: str) -> None:
-        self.failed[tuple(instance_id)] = message
-
-    def exchange(self, instance_id, version: int, free_slots: int, outputs: list):
-        instance_id = tuple(instance_id)
-        self.last_seen[instance_id] = time.monotonic()
-        if outputs:
-            self.manager.on_complete(outputs, instance_id)
-        reqs = self.manager.take_work(instance_id, version, free_slots) if free_slots > 0 else []
-        aborts = self.manager.take_aborts(instance_id)
-        return reqs, aborts, self.ps.get_ps_model_version(), self.phase
-
-    def acquire_pull(self, timeout: float = 600.0) -> bool:
-        return self.ps.acquire_shared_pull(timeout)
-
-    def release_pull(self) -> None:
-        self.ps.release_shared_pull()
-
-    def pull_model(self, instance_id) -> int:
-        v, _ = self.ps.pull_model(tuple(instance_id))
-        return v
-
-    def report_pull(self, seconds: float) -> None:
-        self.sync_stats["pulls"] += 1
-        self.sync_stats["pull_s"] += seconds
-
-    def set_phase(self, p: int) -> None:
-        self.phase = p
+from .control_plane import ExchangeMailbox, spawn_control_plane
 
 
 def log(msg: str) -> None:
@@ -120,12 +49,6 @@ def _role_split(world: int, cfg) -> int:
     if t <= 0 or t >= world:
         t = max(1, world // 2)
     return t
-
-
-def _broadcast_objs(obj, src: int, group) -> object:
-    box = [obj]
-    dist.broadcast_object_list(box, src=src, group=group)
-    return box[0]
 
 
 class DisaggregatedRun:
@@ -146,25 +69,23 @@ class DisaggregatedRun:
             self.train_group = pdist.new_subgroup(trainer_ranks, backend=backend)
             self.train_cpu_group = pdist.new_subgroup(trainer_ranks, backend="gloo")
         self.args = model_args_from_config(cfg.model)
-        self.port = int(os.environ.get("MASTER_PORT", "29511")) + 17
         self.trained_tokens = 0
         self.global_step = 0
-        self.server = None
         self.liveness_s = float(cfg.trainer.get("liveness_timeout_s", 300))
         self.buffer_timeout_s = float(cfg.trainer.get("buffer_timeout_s", 1800))
         log(f"role split: {self.n_train} trainer rank(s), {self.world - self.n_train} rollout rank(s)")
+        port = int(os.environ.get("MASTER_PORT", "29511")) + 17
+        self.cp_proc = None
         if self.rank == 0:
-            rn, _, _, _ = redundant_settings(cfg)
-            self.ps = PSManager.from_config(cfg)
-            self.data = DataProcessor(cfg, self.args.vocab_size, rn)
-            self.reward = RewardManager(cfg, self.data.tokenizer)
-            self.manager = AgentLoopManager(cfg, self.ps, self.data, self.reward)
-            self.svc = DispatcherService(cfg, self.ps, self.manager, self.n_train)
-            self.server = RPCServer({"svc": self.svc}, port=self.port)
+            self.cp_proc = spawn_control_plane(cfg, self.args.vocab_size, self.n_train, port, self.liveness_s)
+            self.client = RPCClient(("127.0.0.1", port), retries=6000)
+            self.client.call("cp", "ping")
         pdist.barrier()
+        if self.rank != 0:
+            self.client = RPCClient(("127.0.0.1", port), retries=6000)
+        self.cp = self.client.proxy("cp")
         log("control plane up")
-        self.client = None if self.rank == 0 else RPCClient(("127.0.0.1", self.port))
-        self.svc_proxy = self.svc if self.rank == 0 else self.client.proxy("svc")
+        self.mailbox = None
         if self.is_trainer:
             self._init_trainer()
         else:
@@ -182,38 +103,23 @@ class DisaggregatedRun:
         if self.device.type == "cuda":
             torch.cuda.synchronize()
         if self.rank == 0:
-            self.svc.set_layout(self.layout)
-        self.svc_proxy.register_store(self.rank, self.store.descriptor())
+            self.cp.set_layout(self.layout)
+        self.cp.register_store(self.rank, self.store.descriptor())
         log(f"trainer ready: {self.layout.nbytes / 2**30:.2f} GiB published store ({mode})")
 
     def trainer_step(self) -> dict:
         b = self.global_step
         t0 = time.perf_counter()
-        trajs = None
-        if self.rank == 0:
-            t_wait = time.monotonic()
-            while not self.manager.buffer_ready(b):
-                if self.svc.failed:
-                    raise RuntimeError(f"rollout instance failed: {self.svc.failed}")
-                now = time.monotonic()
-                stale = [i for i, t in self.svc.last_seen.items() if now - t > self.liveness_s]
-                if stale or now - t_wait > self.buffer_timeout_s:
-                    raise TimeoutError(f"buffer {b} not ready: silent instances {stale}, "
-                                       f"{self.manager.snapshot()}")
-                time.sleep(0.002)
-            trajs = self.manager.consume(b)
-            for t in trajs:
-                t.old_logprobs = t.rollout_logprobs
-            adv_metrics = compute_batch_advantages(self.cfg, trajs)
+        batch = self.cp.get_batch(b, self.rank, self.n_train, self.buffer_timeout_s)
+        trajs, plan = batch["trajs"], batch["plan"]
         t1 = time.perf_counter()
-        if self.n_train > 1:
-            trajs = _broadcast_objs(trajs, 0, self.train_cpu_group)
-        metrics = self.actor.update_policy(trajs, float(self.cfg.rollout.temperature))
+        if not bool(self.cfg.psrl.log_prob.enable_rollout_engine_log_prob):
+            self.actor.compute_log_prob(trajs, list(range(len(trajs))), field="old_logprobs")
+        metrics = self.actor.update_policy(trajs, float(self.cfg.rollout.temperature), plan=plan)
         t2 = time.perf_counter()
-        # publish: PS exclusive lock (rank 0) -> every trainer writes its store -> version bump
-        if self.rank == 0:
-            if not self.ps.acquire_exclusive_push(timeout=600):
-                raise TimeoutError("exclusive push lock")
+        # publish: PS exclusive lock -> every trainer writes its store -> version bump
+        if self.rank == 0 and not self.cp.acquire_push(600):
+            raise TimeoutError("exclusive push lock")
         if self.n_train > 1:
             dist.barrier(group=self.train_cpu_group)
         self.store.publish(self.actor.dp.flat, b + 1)
@@ -222,13 +128,17 @@ class DisaggregatedRun:
         if self.n_train > 1:
             dist.barrier(group=self.train_cpu_group)
         if self.rank == 0:
-            self.ps.push_model(b + 1)
-            self.ps.release_exclusive_push()
-            metrics.update(adv_metrics)
+            try:
+                self.cp.push_model(b + 1, True)
+            finally:
+                self.cp.release_push()
         self.global_step += 1
-        ntok = sum(len(t.prompt_ids) + t.response_len for t in trajs)
-        self.trained_tokens += ntok
-        metrics.update({"step": b, "trained_tokens": ntok, "num_trajectories": len(trajs),
+        self.trained_tokens += int(batch["trained_tokens"])
+        metrics.update(batch["metrics"])
+        metrics.update({"step": b, "trained_tokens": batch["trained_tokens"],
+                        "num_trajectories": batch["num_trajectories"],
+                        "response_length/mean": batch["response_length/mean"],
+                        "staleness/max": batch["staleness/max"],
                         "timing_s/gen_wait": t1 - t0, "timing_s/train": t2 - t1,
                         "timing_s/step": time.perf_counter() - t0})
         return metrics
@@ -239,7 +149,7 @@ class DisaggregatedRun:
         rc = cfg.rollout
         self.instance_id = (self.rank - self.n_train, 0)
         log("rollout: waiting for trainer stores")
-        layout, descs = self.svc_proxy.get_stores()
+        layout, descs = self.cp.get_stores()
         self.layout = layout
         dtype = layout.dtype
         flat = torch.empty(layout.total, dtype=dtype, device=self.device)
@@ -254,75 +164,84 @@ class DisaggregatedRun:
         self.weights = w
         self.puller = WeightPuller(layout, descs, flat)
         max_len = int(rc.max_prompt_length) + int(rc.max_response_length) + 64
+        # a rollout-only GPU can give the KV cache and the batch more room
+        kv_gb = float(rc.get("kv_cache_gb_dedicated", 0) or rc.get("kv_cache_gb", 4.0))
+        max_seqs = int(rc.get("max_num_seqs_dedicated", 0) or rc.max_num_seqs)
         self.engine = RolloutEngine(
-            a, w, max_num_seqs=int(rc.max_num_seqs), max_model_len=max_len, block_size=int(rc.block_size),
-            max_num_batched_tokens=int(rc.max_num_batched_tokens), kv_cache_gb=float(rc.get("kv_cache_gb", 4.0)),
+            a, w, max_num_seqs=max_seqs, max_model_len=max_len, block_size=int(rc.block_size),
+            max_num_batched_tokens=int(rc.max_num_batched_tokens), kv_cache_gb=kv_gb,
             enable_prefix_caching=bool(rc.enable_prefix_caching), use_cuda_graph=bool(rc.cuda_graph),
             keep_kv_on_update=bool(cfg.psrl.rollout_coordination.partial_rollout.get("keep_kv", False)),
-            eos_token_id=None if rc.ignore_eos else 2)
+            eos_token_id=None if rc.ignore_eos else self.cp.eos_id())
         sm = cfg.psrl.rollout_coordination.sync_and_mig_strategy
         self.policy = SyncPolicy(sm.method, bool(cfg.psrl.rollout_coordination.partial_rollout.enable),
                                  sm.sync.get("threshold"), sm.sync.get("indicator", "request_num"))
         self._pull()
-        self.svc_proxy.register_instance(self.instance_id, self.engine.version)
-        log(f"rollout instance {self.instance_id} ready at version {self.engine.version}")
+        self.cp.register_instance(self.instance_id, self.engine.version)
+        log(f"rollout instance {self.instance_id} ready at version {self.engine.version} "
+            f"({max_seqs} seqs, {kv_gb:.0f} GB KV)")
 
     def _pull(self) -> None:
         t0 = time.perf_counter()
-        if not self.svc_proxy.acquire_pull():
+        if not self.cp.acquire_pull():
             raise TimeoutError("shared pull lock")
         try:
-            v = self.svc_proxy.pull_model(self.instance_id)
+            v = self.cp.pull_model(self.instance_id)
             self.puller.pull()
             if self.device.type == "cuda":
                 torch.cuda.current_stream().synchronize()
         finally:
-            self.svc_proxy.release_pull()
+            self.cp.release_pull()
         self.engine.load_weights(None, v)
-        self.svc_proxy.report_pull(time.perf_counter() - t0)
+        self.cp.report_pull(time.perf_counter() - t0)
 
     def rollout_loop(self, on_phase) -> None:
         """Serve until the driver reaches the final phase; ``on_phase(p)`` runs the
         collective steps tied to phase ``p`` (same order as on the trainers)."""
         eng = self.engine
+        if self.device.type == "cuda" and eng.use_cuda_graph:
+            eng.capture_all()
+        self.mailbox = mb = ExchangeMailbox(self.cp, self.instance_id, eng)
         seen = 0
-        last = 0.0
-        ps_v = eng.version
-        pending: list = []
-        while True:
-            if eng.has_unfinished():
-                pending.extend(eng.step())
-            free = eng.max_num_seqs - eng.num_unfinished()
-            now = time.monotonic()
-            if pending or (free >= 16 and now - last > 0.002) or now - last > 0.02:
-                reqs, aborts, ps_v, phase = self.svc_proxy.exchange(self.instance_id, eng.version, free, pending)
-                pending = []
-                last = now
-                for rid in aborts:
-                    o = eng.abort(rid)
-                    del o
+        try:
+            while True:
+                reqs, aborts = mb.collect()
                 for r in reqs:
                     eng.add_request(r)
-                while seen < phase:
+                for rid in aborts:
+                    eng.abort(rid)
+                while seen < mb.phase:
                     seen += 1
                     on_phase(seen)
                 if seen >= 2:
                     return
-            if self.policy.should_sync(eng, ps_v):
-                self._pull()
-            if not eng.has_unfinished():
-                time.sleep(0.001)
+                if self.policy.should_sync(eng, mb.ps_version):
+                    self._pull()
+                if eng.has_unfinished():
+                    outs = eng.step()
+                    if outs:
+                        mb.post(outs)
+                else:
+                    mb.kick()
+                    time.sleep(0.0005)
+        finally:
+            mb.close()
+            self.mailbox = None
 
     def close(self):
-        if self.client is not None:
-            self.client.close()
-        if self.server is not None:
-            self.server.close()
+        if self.rank == 0:
+            with contextlib.suppress(Exception):
+                self.cp.shutdown()
+        self.client.close()
+        if self.cp_proc is not None:
+            self.cp_proc.join(timeout=30)
+            if self.cp_proc.is_alive():
+                self.cp_proc.terminate()
 
 
 def run_disaggregated(cfg, steps: int, warmup: int, info: pdist.DistInfo | None = None):
     """Run ``warmup`` + ``steps`` training steps; returns per-rank timing dict
-    (rank 0 also gets metrics and token counts)."""
+    (rank 0 also gets metrics, token counts and control-plane stats)."""
     info = info or pdist.init_distributed(cfg.trainer.get("device", "auto"))
     run = DisaggregatedRun(cfg, info)
     is_cuda = info.device.type == "cuda"
@@ -338,46 +257,51 @@ def run_disaggregated(cfg, steps: int, warmup: int, info: pdist.DistInfo | None 
         t_evt[f"wall{p}"] = time.perf_counter()
 
     metrics = []
-    if run.is_trainer:
-        for i in range(warmup):
-            m = run.trainer_step()
+    try:
+        if run.is_trainer:
+            for i in range(warmup):
+                m = run.trainer_step()
+                if run.rank == 0:
+                    log(f"warm-up step {i}: {m['timing_s/step']:.1f}s (wait {m['timing_s/gen_wait']:.1f}s), "
+                        f"{m['trained_tokens']} tokens")
             if run.rank == 0:
-                log(f"warm-up step {i}: {m['timing_s/step']:.1f}s, {m['trained_tokens']} tokens")
-        if run.rank == 0:
-            run.svc.set_phase(1)
-        mark(1)
-        for i in range(steps):
-            metrics.append(run.trainer_step())
+                run.cp.set_phase(1)
+            mark(1)
+            for i in range(steps):
+                metrics.append(run.trainer_step())
+                if run.rank == 0:
+                    m = metrics[-1]
+                    log(f"timed step {i}: {m['timing_s/step']:.1f}s (wait {m['timing_s/gen_wait']:.1f}s), "
+                        f"{m['trained_tokens']} tokens")
             if run.rank == 0:
-                log(f"timed step {i}: {metrics[-1]['timing_s/step']:.1f}s")
-        if run.rank == 0:
-            run.svc.set_phase(2)
-        mark(2)
-    else:
-        try:
-            run.rollout_loop(mark)
-        except BaseException as exc:
+                run.cp.set_phase(2)
+            mark(2)
+        else:
             try:
-                run.svc_proxy.report_failure(run.instance_id, f"{type(exc).__name__}: {exc}")
-            except Exception:
-                pass
-            raise
-    if is_cuda:
-        torch.cuda.synchronize()
-        ms = t_evt[1].elapsed_time(t_evt[2])
-    else:
-        ms = (t_evt["wall2"] - t_evt["wall1"]) * 1000.0
-    wall = t_evt["wall2"] - t_evt["wall1"]
-    ms_max = pdist.all_reduce_max(ms, info.device)
-    wall_max = pdist.all_reduce_max(wall, info.device)
-    out = {"ms": ms_max, "wall_s": wall_max, "rank": run.rank, "metrics": metrics,
-           "n_train": run.n_train, "world": run.world}
-    if run.rank == 0:
-        out["tokens"] = sum(m["trained_tokens"] for m in metrics)
-        out["sync"] = dict(run.svc.sync_stats)
-        out["manager"] = run.manager.snapshot()
-    pdist.barrier()
-    run.close()
+                run.rollout_loop(mark)
+            except BaseException as exc:
+                with contextlib.suppress(Exception):
+                    run.cp.report_failure(run.instance_id, f"{type(exc).__name__}: {exc}")
+                raise
+        if is_cuda:
+            torch.cuda.synchronize()
+            ms = t_evt[1].elapsed_time(t_evt[2])
+        else:
+            ms = (t_evt["wall2"] - t_evt["wall1"]) * 1000.0
+        wall = t_evt["wall2"] - t_evt["wall1"]
+        ms_max = pdist.all_reduce_max(ms, info.device)
+        wall_max = pdist.all_reduce_max(wall, info.device)
+        out = {"ms": ms_max, "wall_s": wall_max, "rank": run.rank, "metrics": metrics,
+               "n_train": run.n_train, "world": run.world}
+        if run.rank == 0:
+            out["tokens"] = sum(int(m["trained_tokens"]) for m in metrics)
+            st = run.cp.stats()
+            out["sync"] = st["sync"]
+            out["manager"] = st["manager"]
+            out["cp"] = st
+        pdist.barrier()
+    finally:
+        run.close()
     return out
 
 
