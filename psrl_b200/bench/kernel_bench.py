@@ -42,27 +42,37 @@ def timeit(fn, iters: int = 20, warmup: int = 5) -> float:
 
 
 def bench_decode(pk):
+    """Paged decode attention; sweeps the split count and the K/V ring depth
+    (2 stages x 3 CTAs/SM vs 3 stages x 2 CTAs/SM).  Rollout-like cases first:
+    a short-context batch and a B=512 batch at the mean in-flight context of
+    lognormal(7.0, 0.8) responses."""
     from psrl_b200.ops import paged_decode_attention
     from psrl_b200.ops.attention import decode_splits
     out = []
-    for B, ctx, nq, nkv in ((256, 1024, 16, 2), (128, 4096, 16, 2), (64, 8192, 28, 4)):
+    for B, ctx, nq, nkv in ((256, 320, 16, 2), (512, 1728, 16, 2), (256, 1024, 16, 2), (128, 4096, 16, 2),
+                            (64, 8192, 28, 4)):
         bs, d = 64, 128
         nblk = B * (ctx // bs)
         kc = torch.randn(nblk, nkv, bs, d, device="cuda").bfloat16()
         vc = torch.randn_like(kc)
-        bt = torch.arange(nblk, dtype=torch.int32, device="cuda").view(B, ctx // bs)
+        # scattered pages, as the block manager hands them out
+        bt = torch.randperm(nblk, device="cuda").to(torch.int32).view(B, ctx // bs)
         lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
         q = torch.randn(B, nq, d, device="cuda").bfloat16()
         sp = decode_splits(B, nkv, ctx)
         nbytes = 2 * B * ctx * nkv * d * 2
         sweep = {}
-        for s_ in sorted({1, 2, 4, sp}):
-            ms_ = timeit(lambda: paged_decode_attention(q, kc, vc, bt, lens, splits=s_))
-            sweep[s_] = round(nbytes / (ms_ / 1e3) / 1e9, 1)
+        for st in (2, 3):
+            for s_ in sorted({1, 2, 4, sp}):
+                ms_ = timeit(lambda: paged_decode_attention(q, kc, vc, bt, lens, splits=s_, stages=st))
+                sweep[f"st{st}/sp{s_}"] = round(nbytes / (ms_ / 1e3) / 1e9, 1)
         ms = timeit(lambda: paged_decode_attention(q, kc, vc, bt, lens, splits=sp))
         gbs = nbytes / (ms / 1e3) / 1e9
+        bt_c = torch.arange(nblk, dtype=torch.int32, device="cuda").view(B, ctx // bs)
+        ms_c = timeit(lambda: paged_decode_attention(q, kc, vc, bt_c, lens, splits=sp))
         out.append({"case": f"decode B={B} ctx={ctx} {nq}/{nkv}", "ms": round(ms, 4), "GB/s": round(gbs, 1),
-                    "frac_hbm": round(gbs / pk["hbm_gbs"], 3), "splits": sp, "GB/s_by_splits": sweep})
+                    "frac_hbm": round(gbs / pk["hbm_gbs"], 3), "splits": sp, "GB/s_by_stages_splits": sweep,
+                    "GB/s_contiguous_pages": round(nbytes / (ms_c / 1e3) / 1e9, 1)})
         del kc, vc
     return out
 
@@ -150,7 +160,25 @@ def bench_sync(pk):
              "GB/s (read+write)": round(2 * nb / ms / 1e6, 1), "frac_hbm": round(2 * nb / ms / 1e6 / pk["hbm_gbs"], 3)}]
 
 
-CASES = {"decode": bench_decode, "gemm": bench_gemm, "logprob": bench_logprob, "attn": bench_attn_train,
+def bench_sample(pk):
+    """Fused Gumbel-max sampler over a [B, 151936] bf16 logits batch (one read
+    of the logits is the floor)."""
+    from psrl_b200.ops import sample
+    out = []
+    for B in (256, 512):
+        V = 151936
+        logits = torch.randn(B, V, device="cuda").bfloat16()
+        temps = torch.ones(B, device="cuda")
+        seeds = torch.arange(B, device="cuda")
+        streams = torch.zeros(B, device="cuda", dtype=torch.int32)
+        ms = timeit(lambda: sample(logits, temps, seeds, streams))
+        gbs = B * V * 2 / (ms / 1e3) / 1e9
+        out.append({"case": f"sample B={B} V={V}", "ms": round(ms, 4), "GB/s": round(gbs, 1),
+                    "frac_hbm": round(gbs / pk["hbm_gbs"], 3)})
+    return out
+
+
+CASES = {"sample": bench_sample, "decode": bench_decode, "gemm": bench_gemm, "logprob": bench_logprob, "attn": bench_attn_train,
          "elementwise": bench_elementwise, "sync": bench_sync}
 
 

@@ -553,7 +553,8 @@ __global__ void __launch_bounds__(NTHREADS) attn_bwd_kernel(BwdParams bp) {
 
 // ---------------------------------------------------------------- decode
 struct DecodeParams {
-  const bf16* q;      // [B, nq, D]
+  const bf16* q;      // [B, nq, D], rows q_row elements apart (heads contiguous)
+  int64_t q_row;
   const bf16* kc;     // [blocks, nkv, bs, D]
   const bf16* vc;
   const int* block_table;
@@ -570,11 +571,25 @@ struct DecodeParams {
 // K/V tiles stream through a DEC_STAGES-deep cp.async ring; every thread
 // computes the paged address of the chunks it copies directly (no row table),
 // so a tile costs one barrier.  The warp-merge area aliases the ring.
-constexpr int DEC_STAGES = 2;   // x 3 resident CTAs per SM
+constexpr int DEC_STAGES = 2;   // default ring depth (x 3 resident CTAs per SM)
 
 __device__ __forceinline__ void dec_load_tile(bf16* sm, const bf16* cache, const int* bt_row, int block_size,
                                               int nkv, int kvh, int key0, int k_end) {
   // BN rows x 16 chunks of 16 B; 128 threads -> 8 chunks each
+  if (block_size % BN == 0) {
+    // tiles start on multiples of BN, so the whole tile sits in one cache
+    // block: one block-table lookup and no per-chunk division
+    const int blk = bt_row[key0 / block_size];
+    const bf16* base = cache + (((int64_t)blk * nkv + kvh) * block_size + key0 % block_size) * D;
+#pragma unroll
+    for (int i = 0; i < BN * 16 / NTHREADS; ++i) {
+      const int idx = threadIdx.x + i * NTHREADS;
+      const int r = idx >> 4, c = idx & 15;
+      const bool ok = key0 + r < k_end;
+      cp_async16(sm + swz(r, c * 8), ok ? base + r * D + c * 8 : cache, ok);
+    }
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < BN * 16 / NTHREADS; ++i) {
     const int idx = threadIdx.x + i * NTHREADS;
@@ -590,11 +605,12 @@ __device__ __forceinline__ void dec_load_tile(bf16* sm, const bf16* cache, const
   }
 }
 
-__global__ void __launch_bounds__(NTHREADS, 3) decode_kernel(DecodeParams p) {
+template <int STAGES>
+__device__ __forceinline__ void decode_body(const DecodeParams& p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   bf16* sQ = reinterpret_cast<bf16*>(smem_raw);  // [16][D]
-  bf16* sK = sQ + 16 * D;                         // [DEC_STAGES][BN][D]
-  bf16* sV = sK + DEC_STAGES * BN * D;            // [DEC_STAGES][BN][D]
+  bf16* sK = sQ + 16 * D;                         // [STAGES][BN][D]
+  bf16* sV = sK + STAGES * BN * D;            // [STAGES][BN][D]
   float* sO = reinterpret_cast<float*>(sK);       // [NWARPS][16][D] merge area (after the loop)
   __shared__ float sM[NWARPS][16], sL[NWARPS][16];
 
@@ -613,21 +629,21 @@ __global__ void __launch_bounds__(NTHREADS, 3) decode_kernel(DecodeParams p) {
     const int idx = threadIdx.x + i * NTHREADS;
     const int r = idx >> 4, c = idx & 15;
     const bool ok = r < grp;
-    const bf16* src = ok ? p.q + ((int64_t)b * p.nq + kvh * grp + r) * D + c * 8 : p.q;
+    const bf16* src = ok ? p.q + (int64_t)b * p.q_row + (int64_t)(kvh * grp + r) * D + c * 8 : p.q;
     cp_async16(sQ + swz(r, c * 8), src, ok);
   }
   cp_async_commit();
 
   const int n_tiles = k_end > k_begin ? (k_end - k_begin + BN - 1) / BN : 0;
 #pragma unroll
-  for (int st = 0; st < DEC_STAGES - 1; ++st) {
+  for (int st = 0; st < STAGES - 1; ++st) {
     if (st < n_tiles) {
       dec_load_tile(sK + st * BN * D, p.kc, bt_row, p.block_size, p.nkv, kvh, k_begin + st * BN, k_end);
       dec_load_tile(sV + st * BN * D, p.vc, bt_row, p.block_size, p.nkv, kvh, k_begin + st * BN, k_end);
     }
     cp_async_commit();
   }
-  cp_async_wait<DEC_STAGES - 1>();   // Q landed
+  cp_async_wait<STAGES - 1>();   // Q landed
   __syncthreads();
 
   uint32_t qf[8][4];
@@ -642,13 +658,13 @@ __global__ void __launch_bounds__(NTHREADS, 3) decode_kernel(DecodeParams p) {
   const float sl2 = p.scale * LOG2E;
 
   for (int t = 0; t < n_tiles; ++t) {
-    const int stage = t % DEC_STAGES;
-    cp_async_wait<DEC_STAGES - 2>();   // tile t landed (this thread's copies)
+    const int stage = t % STAGES;
+    cp_async_wait<STAGES - 2>();   // tile t landed (this thread's copies)
     __syncthreads();                   // ... and everyone's; stage (t-1) is free to refill
     {
-      const int tn = t + DEC_STAGES - 1;
+      const int tn = t + STAGES - 1;
       if (tn < n_tiles) {
-        const int sn = tn % DEC_STAGES;
+        const int sn = tn % STAGES;
         dec_load_tile(sK + sn * BN * D, p.kc, bt_row, p.block_size, p.nkv, kvh, k_begin + tn * BN, k_end);
         dec_load_tile(sV + sn * BN * D, p.vc, bt_row, p.block_size, p.nkv, kvh, k_begin + tn * BN, k_end);
       }
@@ -772,6 +788,10 @@ __global__ void __launch_bounds__(NTHREADS, 3) decode_kernel(DecodeParams p) {
   }
 }
 
+__global__ void __launch_bounds__(NTHREADS, 3) decode_kernel(DecodeParams p) { decode_body<DEC_STAGES>(p); }
+// deeper ring (3 x 32 KB in flight per CTA) at 2 resident CTAs per SM
+__global__ void __launch_bounds__(NTHREADS, 2) decode_kernel_s3(DecodeParams p) { decode_body<3>(p); }
+
 __global__ void decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                                       bf16* __restrict__ o, int splits) {
   // one CTA (128 threads) per (b, head); lse in base 2
@@ -794,9 +814,9 @@ using namespace attn;
 
 static size_t fwd_smem() { return (size_t)(BM * D + 4 * BN * D) * sizeof(bf16); }
 static size_t bwd_smem() { return (size_t)(2 * BN * D + 2 * BM * D + BN * BM) * sizeof(bf16); }
-static size_t dec_smem() {
+static size_t dec_smem(int stages = DEC_STAGES) {
   // Q + K/V ring; the fp32 warp-merge area (NWARPS x 16 x D) aliases the ring
-  const size_t ring = (size_t)(16 * D + 2 * DEC_STAGES * BN * D) * sizeof(bf16);
+  const size_t ring = (size_t)(16 * D + 2 * stages * BN * D) * sizeof(bf16);
   const size_t merge = (size_t)16 * D * sizeof(bf16) + (size_t)NWARPS * 16 * D * sizeof(float);
   return ring > merge ? ring : merge;
 }
@@ -941,9 +961,12 @@ std::vector<at::Tensor> attn_varlen_bwd(at::Tensor dO, at::Tensor q, at::Tensor 
 }
 
 int64_t decode_num_splits(int64_t batch, int64_t nkv, int64_t max_ctx) {
-  // Enough CTAs for ~2 per SM; every split keeps at least 4 key tiles.
+  // Split a sequence's keys only while there is less than one CTA per SM (a
+  // split adds a combine pass and partial-result traffic; measured on B200 the
+  // unsplit 3-stage kernel wins from one CTA per SM on); every split keeps at
+  // least 4 key tiles.
   const int64_t ctas = std::max<int64_t>(1, batch * nkv);
-  const int64_t target = 2 * num_sms();
+  const int64_t target = num_sms();
   int64_t s = (target + ctas - 1) / ctas;
   s = std::min<int64_t>(s, std::max<int64_t>(1, (max_ctx + 4 * BN - 1) / (4 * BN)));
   return std::max<int64_t>(1, std::min<int64_t>(s, 32));
@@ -952,17 +975,23 @@ int64_t decode_num_splits(int64_t batch, int64_t nkv, int64_t max_ctx) {
 // Paged decode. q: [B, nq, D] contiguous. `scratch` (optional) is a float buffer of
 // at least B*nq*splits*(D+1) elements used when splits > 1.
 at::Tensor attn_decode(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor block_table,
-                       at::Tensor kv_lens, double scale, int64_t splits, c10::optional<at::Tensor> scratch) {
+                       at::Tensor kv_lens, double scale, int64_t splits, c10::optional<at::Tensor> scratch,
+                       int64_t stages) {
   CHECK_CUDA_TENSOR(q);
-  CHECK_CONTIG(q);
-  TORCH_CHECK(q.size(-1) == D, "head_dim must be 128");
+  TORCH_CHECK(q.dim() == 3 && q.size(-1) == D, "q must be [B, heads, 128]");
+  // rows may be strided (q viewed out of the fused qkv projection); heads and
+  // head dims must be contiguous and every row 16-byte aligned
+  TORCH_CHECK(q.stride(2) == 1 && q.stride(1) == D && q.stride(0) % 8 == 0 &&
+                  reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0,
+              "q rows must hold contiguous heads and start 16-byte aligned");
   const int B = q.size(0), nq = q.size(1), nkv = k_cache.size(1);
   TORCH_CHECK(nq % nkv == 0 && nq / nkv <= 16, "GQA group must be <= 16");
   at::cuda::CUDAGuard g(q.device());
-  auto o = at::empty_like(q);
+  auto o = at::empty({B, nq, D}, q.options());
   if (B == 0) return o;
   DecodeParams p{};
   p.q = reinterpret_cast<const bf16*>(q.data_ptr());
+  p.q_row = q.stride(0);
   p.kc = reinterpret_cast<const bf16*>(k_cache.data_ptr());
   p.vc = reinterpret_cast<const bf16*>(v_cache.data_ptr());
   p.block_table = block_table.data_ptr<int>();
@@ -985,14 +1014,21 @@ at::Tensor attn_decode(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at:
     p.part_o = buf.data_ptr<float>();
     p.part_lse = p.part_o + (int64_t)B * nq * splits * D;
   }
-  const size_t sm = dec_smem();
-  static bool attr = false;
-  if (!attr) {
-    PSRL_CHECK_CUDA(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
-    attr = true;
+  // ring depth: 3 stages x 2 CTAs/SM (default; 0.86-0.92 of copy bandwidth at
+  // rollout shapes) or 2 stages x 3 CTAs/SM (stages == 2)
+  const int st = stages == 2 ? 2 : 3;
+  const size_t sm = dec_smem(st);
+  static bool attr[2] = {false, false};
+  if (!attr[st == 3]) {
+    PSRL_CHECK_CUDA(cudaFuncSetAttribute(st == 3 ? decode_kernel_s3 : decode_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+    attr[st == 3] = true;
   }
   dim3 grid(B, nkv, splits);
-  decode_kernel<<<grid, NTHREADS, sm, stream()>>>(p);
+  if (st == 3)
+    decode_kernel_s3<<<grid, NTHREADS, sm, stream()>>>(p);
+  else
+    decode_kernel<<<grid, NTHREADS, sm, stream()>>>(p);
   PSRL_CHECK_LAUNCH();
   if (splits > 1) {
     decode_combine_kernel<<<B * nq, D, 0, stream()>>>(p.part_o, p.part_lse, p.o, (int)splits);
@@ -1063,6 +1099,7 @@ extern "C" __attribute__((visibility("default"))) int psrl_decode_attention_noal
   if (rc != PSRL_NOALLOC_OK) return rc;
   DecodeParams p{};
   p.q = static_cast<const bf16*>(q);
+  p.q_row = (int64_t)num_heads * D;
   p.kc = static_cast<const bf16*>(k_cache);
   p.vc = static_cast<const bf16*>(v_cache);
   p.block_table = block_table;

@@ -29,7 +29,8 @@ std::vector<at::Tensor> attn_varlen_bwd(at::Tensor dO, at::Tensor q, at::Tensor 
                                         at::Tensor lse, at::Tensor cu_seqlens, int64_t max_seqlen, double scale);
 int64_t decode_num_splits(int64_t batch, int64_t nkv, int64_t max_ctx);
 at::Tensor attn_decode(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor block_table,
-                       at::Tensor kv_lens, double scale, int64_t splits, c10::optional<at::Tensor> scratch);
+                       at::Tensor kv_lens, double scale, int64_t splits, c10::optional<at::Tensor> scratch,
+                       int64_t stages);
 std::tuple<pybind11::bytes, int64_t> ipc_handle(at::Tensor t);
 at::Tensor ipc_open(pybind11::bytes handle, int64_t offset, int64_t numel, at::ScalarType dtype, int64_t src_device);
 void enable_peer_access(int64_t peer);
@@ -41,6 +42,7 @@ std::vector<at::Tensor> tc_linear_logprob(at::Tensor h, at::Tensor w, at::Tensor
 void kv_copy_blocks(at::Tensor src_layers, at::Tensor dst_layers, at::Tensor src_blk, at::Tensor dst_blk,
                     int64_t block_bytes);
 void register_vmm(pybind11::module& m);
+pybind11::dict green_partition(int64_t device, int64_t reserve_sms, int64_t priority);
 }  // namespace psrl
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -61,7 +63,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_paged_prefill", &psrl::attn_paged_prefill);
   m.def("attn_varlen_bwd", &psrl::attn_varlen_bwd);
   m.def("decode_num_splits", &psrl::decode_num_splits);
-  m.def("attn_decode", &psrl::attn_decode);
+  m.def("attn_decode", &psrl::attn_decode, pybind11::arg("q"), pybind11::arg("k_cache"), pybind11::arg("v_cache"),
+        pybind11::arg("block_table"), pybind11::arg("kv_lens"), pybind11::arg("scale"), pybind11::arg("splits"), pybind11::arg("scratch"),
+        pybind11::arg("stages") = 0);
   m.def("ipc_handle", &psrl::ipc_handle);
   m.def("ipc_open", &psrl::ipc_open);
   m.def("enable_peer_access", &psrl::enable_peer_access);
@@ -70,4 +74,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_linear_logprob", &psrl::tc_linear_logprob);
   m.def("kv_copy_blocks", &psrl::kv_copy_blocks);
   psrl::register_vmm(m);
+  m.def("green_partition", &psrl::green_partition);
 }

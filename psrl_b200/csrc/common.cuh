@@ -133,4 +133,22 @@ __device__ __forceinline__ float uniform01(uint64_t seed, uint64_t stream, uint6
   return ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
 }
 
+// 32-bit integer hash "lowbias32" (C. Wellons, hash-prospector, public
+// domain): xorshift-multiply rounds with low avalanche bias.  Used for
+// per-element random bits once a 64-bit per-row key has been mixed.
+__device__ __forceinline__ uint32_t hash32(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return x;
+}
+
+// uniform (0, 1) from a per-row 64-bit key and a 32-bit element index
+__device__ __forceinline__ float uniform01_k(uint64_t key, uint32_t idx) {
+  const uint32_t h = hash32(hash32(idx ^ (uint32_t)key) + (uint32_t)(key >> 32));
+  return ((float)(h >> 8) + 0.5f) * (1.0f / 16777216.0f);
+}
+
 }  // namespace psrl

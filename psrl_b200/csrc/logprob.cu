@@ -177,6 +177,36 @@ __device__ __forceinline__ ArgMax amax(ArgMax a, ArgMax b) {
   return (b.key > a.key || (b.key == a.key && b.idx < a.idx)) ? b : a;
 }
 
+// Gumbel key of one element and its contribution to the running statistics.
+struct SampleAcc {
+  OnlineStat st;
+  ArgMax best;
+};
+
+// Add 8 scaled logits z[0..7] (indices i0..i0+7) to the accumulator: one
+// rescale of the running sum per group instead of one per element.
+__device__ __forceinline__ void sample_add8(SampleAcc& a, const float* z, int i0, bool greedy, uint64_t key) {
+  float m8 = z[0];
+#pragma unroll
+  for (int j = 1; j < 8; ++j) m8 = fmaxf(m8, z[j]);
+  if (m8 == -INFINITY) return;               // fully masked group: no mass, never sampled
+  if (m8 > a.st.m) {
+    const float c = (a.st.m == -INFINITY) ? 0.f : __expf(a.st.m - m8);
+    a.st.s *= c;
+    a.st.t *= c;
+    a.st.m = m8;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float e = __expf(z[j] - a.st.m);
+    a.st.s += e;
+    a.st.t += e * z[j];
+    float k = z[j];
+    if (!greedy) k = z[j] - __logf(-__logf(uniform01_k(key, (uint32_t)(i0 + j))));
+    if (k > a.best.key) a.best = ArgMax{k, i0 + j};   // ascending indices: first max wins
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(LP_THREADS)
     sample_kernel(const T* __restrict__ logits, int64_t ld, int V, const float* __restrict__ temps,
@@ -191,19 +221,37 @@ __global__ void __launch_bounds__(LP_THREADS)
   const float it = greedy ? 1.f : 1.f / tmp;
   const uint64_t seed = seeds ? (uint64_t)seeds[row] : 0ull;
   const uint64_t step = streams ? (uint64_t)streams[row] : 0ull;
-  OnlineStat st{-INFINITY, 0.f, 0.f};
-  ArgMax best{-INFINITY, 0x7fffffff};
-  for (int i = threadIdx.x; i < V; i += LP_THREADS) {
-    const float zi = to_f(z[i]) * it;
-    ostat_add(st, zi);
-    float key = zi;
-    if (!greedy) {
-      const float u = uniform01(seed, step, (uint64_t)i);
-      key = zi - __logf(-__logf(u));
+  // per-row key: the request's randomness depends only on (seed, position)
+  const uint64_t key = mix64(seed ^ mix64(step * 0x632be59bd9b4e019ull));
+  SampleAcc acc{{-INFINITY, 0.f, 0.f}, {-INFINITY, 0x7fffffff}};
+  constexpr int VEC = 16 / (int)sizeof(T);   // elements per 16-byte load
+  const bool vec_ok = (reinterpret_cast<uintptr_t>(z) % 16 == 0);
+  const int nvec = vec_ok ? V / 8 : 0;       // groups of 8 elements
+  for (int g = threadIdx.x; g < nvec; g += LP_THREADS) {
+    float v[8];
+    if constexpr (VEC == 8) {
+      const bf16x8 p = *reinterpret_cast<const bf16x8*>(z + (int64_t)g * 8);
+      unpack8(p, v);
+    } else {
+      const float4 p0 = *reinterpret_cast<const float4*>(z + (int64_t)g * 8);
+      const float4 p1 = *reinterpret_cast<const float4*>(z + (int64_t)g * 8 + 4);
+      v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
+      v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
     }
-    best = amax(best, ArgMax{key, i});
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] *= it;
+    sample_add8(acc, v, g * 8, greedy, key);
   }
-  st = ostat_block(st, sm);
+  // ragged tail (or the whole row when it is not 16-byte aligned)
+  for (int i = nvec * 8 + threadIdx.x; i < V; i += LP_THREADS) {
+    const float zi = to_f(z[i]) * it;
+    ostat_add(acc.st, zi);
+    float k = zi;
+    if (!greedy) k = zi - __logf(-__logf(uniform01_k(key, (uint32_t)i)));
+    acc.best = amax(acc.best, ArgMax{k, i});
+  }
+  OnlineStat st = ostat_block(acc.st, sm);
+  ArgMax best = acc.best;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {

@@ -150,14 +150,16 @@ def decode_splits(batch: int, nkv: int, max_ctx: int) -> int:
 
 
 def paged_decode_attention(q, k_cache, v_cache, block_table, kv_lens, scale=None, splits: int | None = None,
-                           scratch: torch.Tensor | None = None):
+                           scratch: torch.Tensor | None = None, stages: int = 0):
     """q [B, nq, d] -> [B, nq, d]; kv_lens include the current token."""
     d = q.shape[-1]
     scale = scale if scale is not None else 1.0 / math.sqrt(d)
     if q.is_cuda and d == 128:
         if splits is None:
             splits = decode_splits(q.shape[0], k_cache.shape[1], int(block_table.shape[1] * k_cache.shape[2]))
-        return ext().attn_decode(q.contiguous(), k_cache, v_cache, block_table, kv_lens, scale, int(splits), scratch)
+        if not (q.stride(2) == 1 and q.stride(1) == d and q.stride(0) % 8 == 0 and q.data_ptr() % 16 == 0):
+            q = q.contiguous()
+        return ext().attn_decode(q, k_cache, v_cache, block_table, kv_lens, scale, int(splits), scratch, int(stages))
     B = q.shape[0]
     cu = torch.arange(B + 1, dtype=torch.int32, device=q.device)
     return paged_attention_ref(q, k_cache, v_cache, cu, kv_lens, block_table, scale)

@@ -41,6 +41,33 @@ from . import algos
 from .actor import PolicyWorker
 
 
+
+def trainer_stream_for(cfg, device, active: bool):
+    """The stream the trainer launches on while a rollout engine runs beside
+    it: a green-context stream that leaves ``psrl.deployment.rollout_reserved_sms``
+    SMs to the engine, or None (the current stream)."""
+    k = int(cfg.psrl.deployment.get("rollout_reserved_sms", 0) or 0)
+    if not active or k <= 0 or torch.device(device).type != "cuda":
+        return None
+    from ..parallel.sm_partition import trainer_stream
+    s, _ = trainer_stream(torch.device(device), k)
+    return s
+
+
+def train_stream_ctx(stream):
+    import contextlib
+    return torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext()
+
+
+def _apply_switch_interval(cfg) -> None:
+    """A trainer thread that launches thousands of kernels per micro-batch holds
+    the GIL for long stretches; a short switch interval bounds how long the
+    rollout thread waits for it between decode steps."""
+    v = cfg.trainer.get("gil_switch_interval_s")
+    if v:
+        import sys
+        sys.setswitchinterval(float(v))
+
 def resolve_device(cfg) -> torch.device:
     d = cfg.trainer.get("device", "auto")
     if d == "auto":
@@ -136,6 +163,8 @@ class RLTrainer:
         self._rollout_stop = False
         self._rollout_error: BaseException | None = None
         self.rollout_stream = torch.cuda.Stream(device=self.device, priority=-1) if self.overlap else None
+        self.train_stream = trainer_stream_for(cfg, self.device, self.overlap)
+        _apply_switch_interval(cfg)
         from .strategies import build_step_strategy
         self.strategy = build_step_strategy(self)
 
@@ -225,7 +254,8 @@ class RLTrainer:
         b = self.global_step
         metrics: dict = {}
         t0 = time.perf_counter()
-        trajs = self.strategy.run_step(b, metrics)
+        with train_stream_ctx(self.train_stream):
+            trajs = self.strategy.run_step(b, metrics)
         with self.log.span("PUSH", step=b):
             self._publish(b + 1)
         self.global_step += 1

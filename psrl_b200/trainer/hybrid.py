@@ -47,6 +47,7 @@ from ..utils.locks import RWLock
 from ..utils.rpc import RPCClient
 from .actor import PolicyWorker
 from .control_plane import ExchangeMailbox, spawn_control_plane
+from .driver import _apply_switch_interval, train_stream_ctx, trainer_stream_for
 
 
 def log(msg: str) -> None:
@@ -113,6 +114,8 @@ class HybridRun:
         self.instance_id = (self.rank, 0)
         self.cp.register_instance(self.instance_id, self.engine.version)
         self.rollout_stream = torch.cuda.Stream(device=self.device, priority=-1) if self.is_cuda else None
+        self.train_stream = trainer_stream_for(cfg, self.device, self.is_cuda)
+        _apply_switch_interval(cfg)
         self.mailbox: ExchangeMailbox | None = None
         self._thread = None
         self._stop = False
@@ -190,13 +193,14 @@ class HybridRun:
         trajs, plan = batch["trajs"], batch["plan"]
         t1 = time.perf_counter()
         idx = list(range(len(trajs)))
-        if self.ref is not None:
-            self.ref.compute_log_prob(trajs, idx, field="ref_logprobs")
-        if not bool(self.cfg.psrl.log_prob.enable_rollout_engine_log_prob):
-            self.actor.compute_log_prob(trajs, idx, field="old_logprobs")
-        metrics = self.actor.update_policy(trajs, float(self.cfg.rollout.temperature),
-                                           step_guard=lambda: self.wlock.exclusive(600),
-                                           sync_every_micro_batch=self.is_cuda, plan=plan)
+        with train_stream_ctx(self.train_stream):
+            if self.ref is not None:
+                self.ref.compute_log_prob(trajs, idx, field="ref_logprobs")
+            if not bool(self.cfg.psrl.log_prob.enable_rollout_engine_log_prob):
+                self.actor.compute_log_prob(trajs, idx, field="old_logprobs")
+            metrics = self.actor.update_policy(trajs, float(self.cfg.rollout.temperature),
+                                               step_guard=lambda: self.wlock.exclusive(600),
+                                               sync_every_micro_batch=self.is_cuda, plan=plan)
         t2 = time.perf_counter()
         if self.cpu_group is not None:
             dist.barrier(group=self.cpu_group)      # every replica holds version b + 1

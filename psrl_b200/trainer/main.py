@@ -4,8 +4,10 @@
         psrl.staleness=3 ++trainer.total_training_steps=100
 
 One process runs colocated (trainer + rollout on one device).  Under
-``torch.distributed.run`` (one process per GPU, rendezvous on 127.0.0.1) the
-ranks split into trainer and rollout roles (:mod:`psrl_b200.parallel.placement`).
+``torch.distributed.run`` (one process per GPU, rendezvous on 127.0.0.1)
+``psrl.deployment.placement`` selects ``disaggregated`` (ranks split into
+trainer and rollout roles, :mod:`.distributed`) or ``hybrid`` (every rank
+trains and serves rollout, :mod:`.hybrid`).
 """
 
 from __future__ import annotations
@@ -33,9 +35,13 @@ def main(argv=None) -> int:
     world = int(os.environ.get("WORLD_SIZE", 1))
     if world > 1:
         from ..parallel.dist import destroy, init_distributed
-        from .distributed import run_disaggregated
         info = init_distributed(cfg.trainer.get("device", "auto"))
-        res = run_disaggregated(cfg, steps=steps, warmup=0, info=info)
+        if cfg.psrl.deployment.get("placement", "disaggregated") == "hybrid":
+            from .hybrid import run_hybrid
+            res = run_hybrid(cfg, steps=steps, warmup=0, info=info)
+        else:
+            from .distributed import run_disaggregated
+            res = run_disaggregated(cfg, steps=steps, warmup=0, info=info)
         if info.rank == 0:
             for m in res["metrics"]:
                 print(json.dumps(m, default=str), flush=True)

@@ -32,7 +32,8 @@ if os.environ.get("PSRL_PTXAS_VERBOSE"):
     NVCC_FLAGS.append("-Xptxas=-v")
 
 sources = sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + [os.path.join(CSRC, "bindings.cpp"),
-                                                          os.path.join(CSRC, "vmm.cpp")]
+                                                          os.path.join(CSRC, "vmm.cpp"),
+                                                          os.path.join(CSRC, "green.cpp")]
 
 setup(
     name="psrl_b200",
