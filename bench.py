@@ -63,6 +63,7 @@ def build_cfg(args, n_gpus: int):
         f"rollout.max_num_seqs={args.max_num_seqs}",
         f"++rollout.kv_cache_gb={args.kv_cache_gb}",
         "rollout.block_size=64",
+        f"model.enable_gradient_checkpointing={'true' if args.recompute else 'false'}",
     ] + list(args.override)
     return load_config(preset=args.preset, overrides=ov)
 
@@ -116,7 +117,10 @@ def main():
     ap.add_argument("--preset", default="dapo_qwen2.5_3b")
     ap.add_argument("--prompts-per-gpu", type=int, default=16)
     ap.add_argument("--max-num-seqs", type=int, default=512)
-    ap.add_argument("--kv-cache-gb", type=float, default=60.0)
+    ap.add_argument("--kv-cache-gb", type=float, default=32.0)
+    ap.add_argument("--recompute", action="store_true",
+                    help="activation recompute in the trainer (off by default: the 3B activations of a "
+                         "10k-token micro-batch fit in HBM next to the KV cache)")
     ap.add_argument("--override", action="append", default=[])
     ap.add_argument("--placement", default="auto", choices=["auto", "colocated", "hybrid", "disaggregated"],
                     help="auto: colocated on one GPU, hybrid (every GPU trains and serves rollout) on several")
@@ -166,6 +170,7 @@ def main():
             "seq_len": "prompt U[64,512] + response lognormal(7.0,0.8) cap 8192",
             "parallelism": res["parallelism"],
             "l2": "inputs larger than L2 (weights 6.2 GB, KV cache tens of GB)",
+            "activation_recompute": bool(args.recompute),
         },
         "clocks": res["clocks"],
         "e2e": {"value": round(e2e, 1), "unit": "trained tokens/s (wall clock, public API RLTrainer.step)",
