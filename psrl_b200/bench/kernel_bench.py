@@ -113,11 +113,11 @@ def bench_logprob(pk):
 def bench_attn_train(pk):
     from psrl_b200.ops import varlen_attention
     out = []
-    for L, nseq in ((2048, 5), (8192, 1)):
+    for L, nseq in ((1700, 6), (2048, 5), (8192, 1)):
         nq, nkv, d = 16, 2, 128
         T = L * nseq
         qkv = torch.randn(T, (nq + 2 * nkv) * d, device="cuda").bfloat16().requires_grad_(True)
-        cu = torch.arange(0, T + 1, L, dtype=torch.int32, device="cuda")
+        cu = torch.arange(0, T + 1, L, dtype=torch.int32, device="cuda")   # nseq sequences of L tokens
         fl = 4.0 * nseq * (L * L / 2) * d * nq
         ms_f = timeit(lambda: varlen_attention(qkv, cu, L, nq, nkv, d), iters=10)
         o = varlen_attention(qkv, cu, L, nq, nkv, d)

@@ -90,6 +90,19 @@ __device__ __forceinline__ void load_tile(bf16* sm, const bf16* const* rowptr, c
   }
 }
 
+// Load rows [0, ROWS) of a row-strided matrix starting at `base` (rows past
+// `n_valid` are zero-filled); each thread computes its chunk addresses directly.
+template <int ROWS>
+__device__ __forceinline__ void load_rows(bf16* sm, const bf16* base, int64_t stride, int n_valid) {
+#pragma unroll
+  for (int i = 0; i < ROWS * 16 / NTHREADS; ++i) {
+    const int idx = threadIdx.x + i * NTHREADS;
+    const int r = idx >> 4, c = idx & 15;
+    const bool ok = r < n_valid;
+    cp_async16(sm + swz(r, c * 8), ok ? base + (int64_t)r * stride + c * 8 : base, ok);
+  }
+}
+
 struct Params {
   const bf16* q;
   int64_t q_row;      // element stride between tokens
@@ -143,12 +156,8 @@ __global__ void __launch_bounds__(NTHREADS) attn_fwd_kernel(Params p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   // Q tile
-  if (threadIdx.x < BM) {
-    const int r = mb * BM + threadIdx.x;
-    rowp[threadIdx.x] = r < q_len ? p.q + (int64_t)(q0 + r) * p.q_row + (int64_t)h * p.q_head : nullptr;
-  }
-  __syncthreads();
-  load_tile<BM>(sQ, rowp, p.q);
+  load_rows<BM>(sQ, p.q + (int64_t)(q0 + mb * BM) * p.q_row + (int64_t)h * p.q_head, p.q_row,
+                min(BM, q_len - mb * BM));
   cp_async_commit();
 
   const int q_hi = min(q_len, (mb + 1) * BM);           // exclusive
@@ -156,6 +165,26 @@ __global__ void __launch_bounds__(NTHREADS) attn_fwd_kernel(Params p) {
   const int n_tiles = (k_end + BN - 1) / BN;
 
   auto load_kv = [&](int t, int stage) {
+    // the stage being refilled was last read before the previous iteration's
+    // closing barrier
+    if constexpr (!PAGED) {
+      const int nk = min(BN, k_end - t * BN);
+      const int64_t r0 = (int64_t)p.cu_k[b] + t * BN;
+      load_rows<BN>(sK + stage * BN * D, p.k + r0 * p.k_row + (int64_t)kvh * p.kv_head, p.k_row, nk);
+      load_rows<BN>(sV + stage * BN * D, p.v + r0 * p.v_row + (int64_t)kvh * p.kv_head, p.v_row, nk);
+      return;
+    } else {
+      if (p.block_size % BN == 0) {
+        // the tile sits in one cache block: one block-table lookup
+        const int key0 = t * BN;
+        const int blk = p.block_table[(int64_t)b * p.max_blocks + key0 / p.block_size];
+        const int64_t off = (((int64_t)blk * p.nkv + kvh) * p.block_size + key0 % p.block_size) * D;
+        const int nk = min(BN, k_end - key0);
+        load_rows<BN>(sK + stage * BN * D, p.k + off, D, nk);
+        load_rows<BN>(sV + stage * BN * D, p.v + off, D, nk);
+        return;
+      }
+    }
     __syncthreads();
     if (threadIdx.x < BN) {
       const int key = t * BN + threadIdx.x;
@@ -337,6 +366,10 @@ struct BwdParams {
   int T;
 };
 
+// One CTA = (key tile, kv head, sequence).  It loops over the GQA group's query
+// heads and the causal query tiles; the next query tile's Q / dO / lse / D
+// loads are issued as soon as the current tile's last reader of them is done
+// (before the dQ product and its atomics), so the copy overlaps that work.
 __global__ void __launch_bounds__(NTHREADS) attn_bwd_kernel(BwdParams bp) {
   const Params& p = bp.f;
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -346,7 +379,6 @@ __global__ void __launch_bounds__(NTHREADS) attn_bwd_kernel(BwdParams bp) {
   bf16* sdO = sQ + BM * D;                        // [BM][D]
   bf16* sdS = sdO + BM * D;                       // [BN][BM] (keys x queries), swizzled as 64-wide rows
   __shared__ float sLse[BM], sDd[BM];
-  __shared__ const bf16* rowp[BM];
 
   const int nb = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int s0 = p.cu_q[b];
@@ -357,19 +389,9 @@ __global__ void __launch_bounds__(NTHREADS) attn_bwd_kernel(BwdParams bp) {
   const float sl2 = p.scale * LOG2E;
 
   // K, V tiles of this CTA
-  if (threadIdx.x < BN) {
-    const int key = nb * BN + threadIdx.x;
-    rowp[threadIdx.x] = key < len ? p.k + (int64_t)(s0 + key) * p.k_row + (int64_t)kvh * p.kv_head : nullptr;
-  }
-  __syncthreads();
-  load_tile<BN>(sK, rowp, p.k);
-  __syncthreads();
-  if (threadIdx.x < BN) {
-    const int key = nb * BN + threadIdx.x;
-    rowp[threadIdx.x] = key < len ? p.v + (int64_t)(s0 + key) * p.v_row + (int64_t)kvh * p.kv_head : nullptr;
-  }
-  __syncthreads();
-  load_tile<BN>(sV, rowp, p.v);
+  const int nk = min(BN, len - nb * BN);
+  load_rows<BN>(sK, p.k + (int64_t)(s0 + nb * BN) * p.k_row + (int64_t)kvh * p.kv_head, p.k_row, nk);
+  load_rows<BN>(sV, p.v + (int64_t)(s0 + nb * BN) * p.v_row + (int64_t)kvh * p.kv_head, p.v_row, nk);
   cp_async_commit();
 
   float dk[16][4], dv[16][4];
@@ -381,156 +403,160 @@ __global__ void __launch_bounds__(NTHREADS) attn_bwd_kernel(BwdParams bp) {
   const int key_row0 = nb * BN + warp * 16 + (lane >> 2);  // this thread's keys: key_row0, +8
   const int m_start = (nb * BN) / BM;                       // causal: first query tile touching this key tile
   const int m_tiles = (len + BM - 1) / BM;
+  const int per_head = m_tiles - m_start;
+  const int n_iter = grp * per_head;
 
-  for (int hg = 0; hg < grp; ++hg) {
-    const int h = kvh * grp + hg;
-    for (int mt = m_start; mt < m_tiles; ++mt) {
-      __syncthreads();
-      if (threadIdx.x < BM) {
-        const int q = mt * BM + threadIdx.x;
-        rowp[threadIdx.x] = q < len ? p.q + (int64_t)(s0 + q) * p.q_row + (int64_t)h * p.q_head : nullptr;
-        sLse[threadIdx.x] = q < len ? bp.lse[(int64_t)h * bp.T + s0 + q] * LOG2E : INFINITY;
-        sDd[threadIdx.x] = q < len ? bp.Dd[(int64_t)h * bp.T + s0 + q] : 0.f;
-      }
-      __syncthreads();
-      load_tile<BM>(sQ, rowp, p.q);
-      __syncthreads();
-      if (threadIdx.x < BM) {
-        const int q = mt * BM + threadIdx.x;
-        rowp[threadIdx.x] = q < len ? bp.dO + (int64_t)(s0 + q) * bp.do_row + (int64_t)h * bp.do_head : nullptr;
-      }
-      __syncthreads();
-      load_tile<BM>(sdO, rowp, bp.dO);
-      cp_async_commit();
-      cp_async_wait<0>();
-      __syncthreads();
+  // issue the loads of iteration `it` (query head, query tile) into the single buffer
+  auto issue = [&](int it) {
+    const int h = kvh * grp + it / per_head;
+    const int mt = m_start + it % per_head;
+    const int nq_valid = min(BM, len - mt * BM);
+    load_rows<BM>(sQ, p.q + (int64_t)(s0 + mt * BM) * p.q_row + (int64_t)h * p.q_head, p.q_row, nq_valid);
+    load_rows<BM>(sdO, bp.dO + (int64_t)(s0 + mt * BM) * bp.do_row + (int64_t)h * bp.do_head, bp.do_row,
+                  nq_valid);
+    cp_async_commit();
+    if (threadIdx.x < BM) {
+      const int q = mt * BM + threadIdx.x;
+      sLse[threadIdx.x] = q < len ? bp.lse[(int64_t)h * bp.T + s0 + q] * LOG2E : INFINITY;
+      sDd[threadIdx.x] = q < len ? bp.Dd[(int64_t)h * bp.T + s0 + q] : 0.f;
+    }
+  };
+  if (n_iter > 0) issue(0);
 
-      // S^T (16 keys x 64 queries per warp) = K Q^T
-      float s[8][4];
+  for (int it = 0; it < n_iter; ++it) {
+    const int h = kvh * grp + it / per_head;
+    const int mt = m_start + it % per_head;
+    cp_async_wait<0>();
+    __syncthreads();   // Q / dO / lse / D of this iteration visible; sdS of the previous one consumed
+
+    // S^T (16 keys x 64 queries per warp) = K Q^T
+    float s[8][4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+    for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t a[4];
+      ldsm_x4(a[0], a[1], a[2], a[3], sK + swz(warp * 16 + (lane & 15), ks * 16 + (lane >> 4) * 8));
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(b0, b1, b2, b3, sQ + swz(np * 16 + (lane & 7) + ((lane >> 4) << 3), ks * 16 + ((lane >> 3) & 1) * 8));
+        mma16816(s[2 * np], a, b0, b1);
+        mma16816(s[2 * np + 1], a, b2, b3);
+      }
+    }
+    // P^T = exp2(S*scale*log2e - lse*log2e), causal mask (query >= key)
+    uint32_t pf[4][4];
+    float (&pval)[8][4] = s;  // P^T overwrites S^T
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int qi = nt * 8 + (lane & 3) * 2 + (e & 1);
+        const int q = mt * BM + qi;
+        const int key = key_row0 + (e >> 1) * 8;
+        float pv = ex2(s[nt][e] * sl2 - sLse[qi]);
+        if (q < key || q >= len || key >= len) pv = 0.f;
+        pval[nt][e] = pv;
+      }
+      pf[nt >> 1][(nt & 1) * 2 + 0] = pack_bf16(pval[nt][0], pval[nt][1]);
+      pf[nt >> 1][(nt & 1) * 2 + 1] = pack_bf16(pval[nt][2], pval[nt][3]);
+    }
+    // dV += P^T dO  (k = queries, n = d)
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+      for (int dp = 0; dp < 8; ++dp) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(b0, b1, b2, b3, sdO + swz(ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, dp * 16 + (lane >> 4) * 8));
+        mma16816(dv[2 * dp], pf[ks], b0, b1);
+        mma16816(dv[2 * dp + 1], pf[ks], b2, b3);
+      }
+    }
+    // dP^T = V dO^T
+    float dp_[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dp_[i][0] = dp_[i][1] = dp_[i][2] = dp_[i][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t a[4];
+      ldsm_x4(a[0], a[1], a[2], a[3], sV + swz(warp * 16 + (lane & 15), ks * 16 + (lane >> 4) * 8));
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(b0, b1, b2, b3, sdO + swz(np * 16 + (lane & 7) + ((lane >> 4) << 3), ks * 16 + ((lane >> 3) & 1) * 8));
+        mma16816(dp_[2 * np], a, b0, b1);
+        mma16816(dp_[2 * np + 1], a, b2, b3);
+      }
+    }
+    // dS^T = P^T * (dP^T - D) * scale ; stage to smem as [keys][queries]
+    uint32_t dsf[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      float ds[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int qi = nt * 8 + (lane & 3) * 2 + (e & 1);
+        ds[e] = pval[nt][e] * (dp_[nt][e] - sDd[qi]) * p.scale;
+      }
+      dsf[nt >> 1][(nt & 1) * 2 + 0] = pack_bf16(ds[0], ds[1]);
+      dsf[nt >> 1][(nt & 1) * 2 + 1] = pack_bf16(ds[2], ds[3]);
+      const int kr = warp * 16 + (lane >> 2);
+      const int qc = nt * 8 + (lane & 3) * 2;
+      // sdS rows are 64 wide (128 B): swizzle with 8 chunks
+      const int o0 = kr * BM + ((((qc >> 3) ^ (kr & 7))) << 3) + (qc & 7);
+      const int o1 = (kr + 8) * BM + ((((qc >> 3) ^ ((kr + 8) & 7))) << 3) + (qc & 7);
+      *reinterpret_cast<uint32_t*>(sdS + o0) = dsf[nt >> 1][(nt & 1) * 2 + 0];
+      *reinterpret_cast<uint32_t*>(sdS + o1) = dsf[nt >> 1][(nt & 1) * 2 + 1];
+    }
+    // dK += dS^T Q  (k = queries, n = d)
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+      for (int dp = 0; dp < 8; ++dp) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(b0, b1, b2, b3, sQ + swz(ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, dp * 16 + (lane >> 4) * 8));
+        mma16816(dk[2 * dp], dsf[ks], b0, b1);
+        mma16816(dk[2 * dp + 1], dsf[ks], b2, b3);
+      }
+    }
+    __syncthreads();   // sQ / sdO / lse / D no longer read; sdS complete
+    if (it + 1 < n_iter) issue(it + 1);
+    // dQ (warp: 16 queries x 128 d) += dS K, with dS = (dS^T)^T read transposed from smem
+    // two halves of the head dimension keep the dQ accumulator at 32 registers
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float dq[8][4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {  // keys in steps of 16
         uint32_t a[4];
-        ldsm_x4(a[0], a[1], a[2], a[3], sK + swz(warp * 16 + (lane & 15), ks * 16 + (lane >> 4) * 8));
+        // A = dS[q][key] (16 q x 16 keys) = transpose of sdS[key][q]
+        {
+          const int kr = ks * 16 + (lane & 7) + ((lane >> 4) << 3);
+          const int qc = warp * 16 + ((lane >> 3) & 1) * 8;
+          const int off = kr * BM + ((((qc >> 3) ^ (kr & 7))) << 3);
+          ldsm_x4_t(a[0], a[1], a[2], a[3], sdS + off);
+        }
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
+        for (int j = 0; j < 4; ++j) {
+          const int dp = half * 4 + j;
           uint32_t b0, b1, b2, b3;
-          ldsm_x4(b0, b1, b2, b3, sQ + swz(np * 16 + (lane & 7) + ((lane >> 4) << 3), ks * 16 + ((lane >> 3) & 1) * 8));
-          mma16816(s[2 * np], a, b0, b1);
-          mma16816(s[2 * np + 1], a, b2, b3);
+          ldsm_x4_t(b0, b1, b2, b3, sK + swz(ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, dp * 16 + (lane >> 4) * 8));
+          mma16816(dq[2 * j], a, b0, b1);
+          mma16816(dq[2 * j + 1], a, b2, b3);
         }
       }
-      // P^T = exp2(S*scale*log2e - lse*log2e), causal mask (query >= key)
-      uint32_t pf[4][4];
-      float (&pval)[8][4] = s;  // P^T overwrites S^T
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+      for (int r = 0; r < 2; ++r) {
+        const int q = mt * BM + warp * 16 + (lane >> 2) + r * 8;
+        if (q >= len) continue;
+        float* dst = bp.dq + ((int64_t)(s0 + q) * p.nq + h) * D + half * 64;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int qi = nt * 8 + (lane & 3) * 2 + (e & 1);
-          const int q = mt * BM + qi;
-          const int key = key_row0 + (e >> 1) * 8;
-          float pv = ex2(s[nt][e] * sl2 - sLse[qi]);
-          if (q < key || q >= len || key >= len) pv = 0.f;
-          pval[nt][e] = pv;
-        }
-        pf[nt >> 1][(nt & 1) * 2 + 0] = pack_bf16(pval[nt][0], pval[nt][1]);
-        pf[nt >> 1][(nt & 1) * 2 + 1] = pack_bf16(pval[nt][2], pval[nt][3]);
-      }
-      // dV += P^T dO  (k = queries, n = d)
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-#pragma unroll
-        for (int dp = 0; dp < 8; ++dp) {
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(b0, b1, b2, b3, sdO + swz(ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, dp * 16 + (lane >> 4) * 8));
-          mma16816(dv[2 * dp], pf[ks], b0, b1);
-          mma16816(dv[2 * dp + 1], pf[ks], b2, b3);
-        }
-      }
-      // dP^T = V dO^T
-      float dp_[8][4];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) dp_[i][0] = dp_[i][1] = dp_[i][2] = dp_[i][3] = 0.f;
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        uint32_t a[4];
-        ldsm_x4(a[0], a[1], a[2], a[3], sV + swz(warp * 16 + (lane & 15), ks * 16 + (lane >> 4) * 8));
-#pragma unroll
-        for (int np = 0; np < 4; ++np) {
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4(b0, b1, b2, b3, sdO + swz(np * 16 + (lane & 7) + ((lane >> 4) << 3), ks * 16 + ((lane >> 3) & 1) * 8));
-          mma16816(dp_[2 * np], a, b0, b1);
-          mma16816(dp_[2 * np + 1], a, b2, b3);
-        }
-      }
-      // dS^T = P^T * (dP^T - D) * scale ; stage to smem as [keys][queries]
-      uint32_t dsf[4][4];
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        float ds[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int qi = nt * 8 + (lane & 3) * 2 + (e & 1);
-          ds[e] = pval[nt][e] * (dp_[nt][e] - sDd[qi]) * p.scale;
-        }
-        dsf[nt >> 1][(nt & 1) * 2 + 0] = pack_bf16(ds[0], ds[1]);
-        dsf[nt >> 1][(nt & 1) * 2 + 1] = pack_bf16(ds[2], ds[3]);
-        const int kr = warp * 16 + (lane >> 2);
-        const int qc = nt * 8 + (lane & 3) * 2;
-        // sdS rows are 64 wide (128 B): swizzle with 8 chunks
-        const int o0 = kr * BM + ((((qc >> 3) ^ (kr & 7))) << 3) + (qc & 7);
-        const int o1 = (kr + 8) * BM + ((((qc >> 3) ^ ((kr + 8) & 7))) << 3) + (qc & 7);
-        *reinterpret_cast<uint32_t*>(sdS + o0) = dsf[nt >> 1][(nt & 1) * 2 + 0];
-        *reinterpret_cast<uint32_t*>(sdS + o1) = dsf[nt >> 1][(nt & 1) * 2 + 1];
-      }
-      // dK += dS^T Q  (k = queries, n = d)
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-#pragma unroll
-        for (int dp = 0; dp < 8; ++dp) {
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(b0, b1, b2, b3, sQ + swz(ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, dp * 16 + (lane >> 4) * 8));
-          mma16816(dk[2 * dp], dsf[ks], b0, b1);
-          mma16816(dk[2 * dp + 1], dsf[ks], b2, b3);
-        }
-      }
-      __syncthreads();
-      // dQ (warp: 16 queries x 128 d) += dS K, with dS = (dS^T)^T read transposed from smem
-      {
-        float dq[16][4];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {  // keys in steps of 16
-          uint32_t a[4];
-          // A = dS[q][key] (16 q x 16 keys) = transpose of sdS[key][q]
-          {
-            const int kr = ks * 16 + (lane & 7) + ((lane >> 4) << 3);
-            const int qc = warp * 16 + ((lane >> 3) & 1) * 8;
-            const int off = kr * BM + ((((qc >> 3) ^ (kr & 7))) << 3);
-            ldsm_x4_t(a[0], a[1], a[2], a[3], sdS + off);
-          }
-#pragma unroll
-          for (int dp = 0; dp < 8; ++dp) {
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4_t(b0, b1, b2, b3, sK + swz(ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, dp * 16 + (lane >> 4) * 8));
-            mma16816(dq[2 * dp], a, b0, b1);
-            mma16816(dq[2 * dp + 1], a, b2, b3);
-          }
-        }
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          const int q = mt * BM + warp * 16 + (lane >> 2) + r * 8;
-          if (q >= len) continue;
-          float* dst = bp.dq + ((int64_t)(s0 + q) * p.nq + h) * D;
-#pragma unroll
-          for (int dt = 0; dt < 16; ++dt) {
-            const int c = dt * 8 + (lane & 3) * 2;
-            atomicAdd(dst + c, dq[dt][r * 2]);
-            atomicAdd(dst + c + 1, dq[dt][r * 2 + 1]);
-          }
+        for (int dt = 0; dt < 8; ++dt) {
+          const int c = dt * 8 + (lane & 3) * 2;
+          atomicAdd(reinterpret_cast<float2*>(dst + c), make_float2(dq[dt][r * 2], dq[dt][r * 2 + 1]));
         }
       }
     }
@@ -833,6 +859,9 @@ std::vector<at::Tensor> attn_varlen_fwd(at::Tensor q, at::Tensor k, at::Tensor v
   auto o = at::empty({T, nq, D}, q.options());
   auto lse = want_lse ? at::empty({nq, T}, q.options().dtype(at::kFloat)) : at::Tensor();
   if (T == 0 || B == 0) return {o, lse};
+  for (const at::Tensor* t : {&q, &k, &v})
+    TORCH_CHECK(t->stride(0) % 8 == 0 && t->stride(1) % 8 == 0 && reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
+                "q/k/v rows and heads must start on 16-byte boundaries");
   Params p{};
   p.q = reinterpret_cast<const bf16*>(q.data_ptr());
   p.q_row = q.stride(0);
@@ -875,6 +904,8 @@ at::Tensor attn_paged_prefill(at::Tensor q, at::Tensor k_cache, at::Tensor v_cac
   at::cuda::CUDAGuard g(q.device());
   auto o = at::empty({T, nq, D}, q.options());
   if (T == 0 || B == 0) return o;
+  TORCH_CHECK(q.stride(0) % 8 == 0 && q.stride(1) % 8 == 0 && reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0,
+              "q rows and heads must start on 16-byte boundaries");
   Params p{};
   p.q = reinterpret_cast<const bf16*>(q.data_ptr());
   p.q_row = q.stride(0);
@@ -916,6 +947,10 @@ std::vector<at::Tensor> attn_varlen_bwd(at::Tensor dO, at::Tensor q, at::Tensor 
   auto Dd = at::empty({nq, T}, q.options().dtype(at::kFloat));
   if (T == 0 || B == 0) return {dq.to(at::kBFloat16), dk, dv};
   TORCH_CHECK(dO.stride(-1) == 1 && o.stride(-1) == 1, "dO/O need unit stride on D");
+  // rows are copied in 16-byte chunks
+  for (const at::Tensor* t : {&q, &k, &v, &dO})
+    TORCH_CHECK(t->stride(0) % 8 == 0 && t->stride(1) % 8 == 0 && reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
+                "q/k/v/dO rows and heads must start on 16-byte boundaries");
   {
     const int64_t warps = (int64_t)T * nq;
     bwd_dot_kernel<<<(warps * 32 + 255) / 256, 256, 0, stream()>>>(

@@ -37,6 +37,11 @@ void enable_peer_access(int64_t peer);
 void copy_segments(at::Tensor dst, std::vector<at::Tensor> srcs, std::vector<int64_t> dst_offsets_bytes,
                    std::vector<int64_t> src_offsets_bytes, std::vector<int64_t> lengths_bytes);
 at::Tensor tc_gemm(at::Tensor a, at::Tensor b, at::Tensor err);
+at::Tensor tc_grouped_gemm(at::Tensor a, at::Tensor w, at::Tensor seg, at::Tensor err);
+std::vector<at::Tensor> moe_route(at::Tensor logits, c10::optional<at::Tensor> prior, int64_t k, bool renorm);
+std::vector<at::Tensor> moe_permute(at::Tensor ids, at::Tensor counts, int64_t bm, int64_t tiles_n);
+at::Tensor moe_gather(at::Tensor x, at::Tensor token_of_row);
+at::Tensor moe_combine(at::Tensor ys, at::Tensor pos, at::Tensor w);
 std::vector<at::Tensor> tc_linear_logprob(at::Tensor h, at::Tensor w, at::Tensor labels, double temperature,
                                           at::Tensor err);
 void kv_copy_blocks(at::Tensor src_layers, at::Tensor dst_layers, at::Tensor src_blk, at::Tensor dst_blk,
@@ -71,6 +76,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("enable_peer_access", &psrl::enable_peer_access);
   m.def("copy_segments", &psrl::copy_segments);
   m.def("tc_gemm", &psrl::tc_gemm);
+  m.def("tc_grouped_gemm", &psrl::tc_grouped_gemm);
+  m.def("moe_route", &psrl::moe_route);
+  m.def("moe_permute", &psrl::moe_permute);
+  m.def("moe_gather", &psrl::moe_gather);
+  m.def("moe_combine", &psrl::moe_combine);
   m.def("tc_linear_logprob", &psrl::tc_linear_logprob);
   m.def("kv_copy_blocks", &psrl::kv_copy_blocks);
   psrl::register_vmm(m);

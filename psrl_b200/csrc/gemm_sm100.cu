@@ -52,7 +52,51 @@ struct Args {
   float* part;        // [M, tiles_n, 3]
   float* label_logit; // [M]
   int* err;           // error flag (0 = ok)
+  // grouped mode (MoE experts): A rows are expert-sorted segments seg[e]..seg[e+1],
+  // B is [E * N, K] (expert e's weight rows e*N..e*N+N-1), tiles are numbered
+  // expert-major from tile_off (device arrays, so the launch needs no host sync)
+  int grouped;
+  int E;
+  const int* seg;      // [E + 1]
+  const int* tile_off; // [E + 1]
 };
+
+struct TileCoord {
+  int a_row, b_row, col0, row_lo, row_hi;
+};
+
+__device__ __forceinline__ int total_tiles(const Args& a) { return a.grouped ? a.tile_off[a.E] : a.num_tiles; }
+
+__device__ __forceinline__ TileCoord tile_coord(const Args& a, int tile) {
+  TileCoord c;
+  if (!a.grouped) {
+    const int tm = tile % a.tiles_m, tn = tile / a.tiles_m;
+    c.a_row = tm * BM;
+    c.b_row = tn * BN;
+    c.col0 = tn * BN;
+    c.row_lo = tm * BM;
+    c.row_hi = a.M;
+    return c;
+  }
+  // expert e with tile_off[e] <= tile < tile_off[e + 1] (empty experts have no tiles)
+  int lo = 0, hi = a.E;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (a.tile_off[mid] <= tile) lo = mid;
+    else hi = mid;
+  }
+  const int e = lo;
+  const int s0 = a.seg[e], s1 = a.seg[e + 1];
+  const int tms = (s1 - s0 + BM - 1) / BM;
+  const int local = tile - a.tile_off[e];
+  const int tm = local % tms, tn = local / tms;
+  c.a_row = s0 + tm * BM;
+  c.b_row = e * a.N + tn * BN;
+  c.col0 = tn * BN;
+  c.row_lo = s0 + tm * BM;
+  c.row_hi = s1;
+  return c;
+}
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -182,8 +226,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < args.num_tiles && !s_abort; tile += gridDim.x) {
-        const int tm = tile % args.tiles_m, tn = tile / args.tiles_m;
+      const int ntiles = total_tiles(args);
+      for (int tile = blockIdx.x; tile < ntiles && !s_abort; tile += gridDim.x) {
+        const TileCoord tc = tile_coord(args, tile);
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(empty0 + 8 * stage, phase ^ 1)) {
             set_err(args.err, 1);
@@ -193,8 +238,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const uint32_t fb = full0 + 8 * stage;
           mbar_expect_tx(fb, STAGE_BYTES);
           const uint32_t sa = smem_addr(smem + stage * STAGE_BYTES);
-          tma_load_2d(sa, &tmA, kb * BK, tm * BM, fb);
-          tma_load_2d(sa + A_BYTES, &tmB, kb * BK, tn * BN, fb);
+          tma_load_2d(sa, &tmA, kb * BK, tc.a_row, fb);
+          tma_load_2d(sa + A_BYTES, &tmB, kb * BK, tc.b_row, fb);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -210,7 +255,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       const uint32_t idesc = idesc_bf16(BM, BN);
-      for (int tile = blockIdx.x; tile < args.num_tiles && !s_abort; tile += gridDim.x) {
+      const int ntiles = total_tiles(args);
+      for (int tile = blockIdx.x; tile < ntiles && !s_abort; tile += gridDim.x) {
         if (!mbar_wait(acce0 + 8 * acc, acc_phase ^ 1)) {
           set_err(args.err, 2);
           s_abort = 1;
@@ -251,7 +297,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int row_in_tile = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x) {
+    const int ntiles = total_tiles(args);
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
       if (!mbar_wait(accf0 + 8 * acc, acc_phase)) {
         set_err(args.err, 4);
         s_abort = 1;
@@ -259,9 +306,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       if (s_abort) break;
       tc_fence_after();
-      const int tm = tile % args.tiles_m, tn = tile / args.tiles_m;
-      const int row = tm * BM + row_in_tile;
-      const int col0 = tn * BN;
+      const TileCoord tc = tile_coord(args, tile);
+      const int tn = tc.col0 / BN;
+      const int row = tc.row_lo + row_in_tile;
+      const int row_end = tc.row_hi;
+      const int col0 = tc.col0;
       const uint32_t taddr = tmem_base + acc * BN + ((uint32_t)(quad * 32) << 16);
       if constexpr (EPI == EPI_STORE) {
 #pragma unroll 1
@@ -269,7 +318,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           float v[32];
           tmem_ld32(taddr + c * 32, v);
           const int cb = col0 + c * 32;
-          if (row < args.M) {
+          if (row < row_end) {
             bf16* dst = args.C + (int64_t)row * args.ldc + cb;
             if (cb + 32 <= args.N) {
 #pragma unroll
@@ -287,7 +336,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       } else {
         // online (max, sum exp, sum exp*z) over this tile's columns of the row
         float m = -INFINITY, s = 0.f, t = 0.f;
-        const int64_t lab = row < args.M ? args.labels[row] : -1;
+        const int64_t lab = row < row_end ? args.labels[row] : -1;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           float v[32];
@@ -299,7 +348,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             v[j] = (cb + j < args.N) ? v[j] * args.inv_temp : -INFINITY;
             cm = fmaxf(cm, v[j]);
           }
-          if (lab >= cb && lab < cb + 32 && row < args.M) {
+          if (lab >= cb && lab < cb + 32 && row < row_end) {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
               if (cb + j == lab) args.label_logit[row] = v[j];
@@ -319,7 +368,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
           m = nm;
         }
-        if (row < args.M) {
+        if (row < row_end) {
           float* p = args.part + ((int64_t)row * args.tiles_n + tn) * 3;
           p[0] = m;
           p[1] = s;
@@ -405,7 +454,8 @@ static void launch(const at::Tensor& a, const at::Tensor& b, Args& args) {
     attr = true;
   }
   CUtensorMap ta = make_tmap(a, BM), tb = make_tmap(b, BN);
-  const int grid = std::min(args.num_tiles, num_sms());
+  // grouped: the tile count lives on the device; one persistent CTA per SM
+  const int grid = args.grouped ? num_sms() : std::min(args.num_tiles, num_sms());
   tc_gemm_kernel<EPI><<<grid, NTHREADS, SMEM_BYTES, stream()>>>(ta, tb, args);
   PSRL_CHECK_LAUNCH();
 }
@@ -437,6 +487,57 @@ at::Tensor tc_gemm(at::Tensor a, at::Tensor b, at::Tensor err) {
   args.ldc = args.N;
   args.err = err.data_ptr<int>();
   launch<EPI_STORE>(a, b, args);
+  return c;
+}
+
+// tile_off[e + 1] = sum over experts <= e of ceil(rows_e / BM) * tiles_n (one CTA, E <= 1024)
+__global__ void grouped_tile_offsets_kernel(const int* __restrict__ seg, int E, int tiles_n, int* __restrict__ tile_off) {
+  __shared__ int st[1024];
+  const int e = threadIdx.x;
+  st[e] = e < E ? (seg[e + 1] - seg[e] + BM - 1) / BM * tiles_n : 0;
+  __syncthreads();
+  for (int o = 1; o < 1024; o <<= 1) {
+    const int v = e >= o ? st[e - o] : 0;
+    __syncthreads();
+    st[e] += v;
+    __syncthreads();
+  }
+  if (e < E) tile_off[e + 1] = st[e];
+  if (e == 0) tile_off[0] = 0;
+}
+
+// Grouped GEMM for expert MLPs: C[r, :] = A[r, :] @ W[e]^T for the rows r of
+// expert e's segment seg[e]..seg[e+1] (A rows sorted by expert).  A: bf16
+// [R, K]; W: bf16 [E, N, K]; seg: int32 [E + 1] on the device.  No host sync:
+// the tile schedule is derived on the device from seg.
+at::Tensor tc_grouped_gemm(at::Tensor a, at::Tensor w, at::Tensor seg, at::Tensor err) {
+  CHECK_CUDA_TENSOR(a);
+  CHECK_DTYPE(a, at::kBFloat16);
+  CHECK_DTYPE(w, at::kBFloat16);
+  TORCH_CHECK(w.dim() == 3 && w.is_contiguous(), "w must be contiguous [E, N, K]");
+  TORCH_CHECK(seg.scalar_type() == at::kInt && seg.numel() == w.size(0) + 1, "seg must be int32 [E + 1]");
+  const int E = w.size(0), N = w.size(1), K = w.size(2);
+  TORCH_CHECK(a.size(1) == K && K % BK == 0, "K must match and be a multiple of 64");
+  TORCH_CHECK(N % 8 == 0 && E <= 1024, "N % 8 == 0 and E <= 1024");
+  at::cuda::CUDAGuard g(a.device());
+  auto c = at::empty({a.size(0), N}, a.options());
+  if (a.size(0) == 0) return c;
+  Args args{};
+  args.M = a.size(0);
+  args.N = N;
+  args.K = K;
+  args.tiles_n = (N + BN - 1) / BN;
+  args.grouped = 1;
+  args.E = E;
+  auto tile_off = at::empty({E + 1}, seg.options());
+  grouped_tile_offsets_kernel<<<1, 1024, 0, stream()>>>(seg.data_ptr<int>(), E, args.tiles_n, tile_off.data_ptr<int>());
+  PSRL_CHECK_LAUNCH();
+  args.seg = seg.data_ptr<int>();
+  args.tile_off = tile_off.data_ptr<int>();
+  args.C = reinterpret_cast<bf16*>(c.data_ptr());
+  args.ldc = N;
+  args.err = err.data_ptr<int>();
+  launch<EPI_STORE>(a, w.view({(int64_t)E * N, K}), args);
   return c;
 }
 

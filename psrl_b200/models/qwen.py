@@ -96,6 +96,10 @@ class MoE(nn.Module):
         return w, idx
 
     def forward(self, x):
+        from ..ops import moe as moe_ops
+        if moe_ops.supported(x, self.experts_w13, self.experts_w2):
+            return moe_ops.moe_mlp(x, self.router(x).float(), self.router_prior, self.experts_w13, self.experts_w2,
+                                   self.a.num_experts_per_tok, bool(self.a.norm_topk_prob))
         from ..parallel.moe import moe_forward_local
         w, idx = self.route(x)
         return moe_forward_local(x, w.to(x.dtype), idx, self.experts_w13, self.experts_w2)

@@ -3,8 +3,8 @@
 ``moe_forward_local`` runs all experts on this rank: tokens are permuted into
 expert-contiguous order (stable sort of the flattened top-k assignment), each
 expert applies SwiGLU(x W13^T) W2^T to its segment, and results are combined
-with the routing weights by an index-add.  The expert-parallel variant
-(dispatch/combine across ranks) lives in :mod:`psrl_b200.parallel.ep`.
+with the routing weights by an index-add.  This is the portable (CPU) path
+and the numerics oracle of the fused CUDA path in :mod:`psrl_b200.ops.moe`.
 """
 
 from __future__ import annotations

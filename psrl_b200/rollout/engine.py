@@ -600,8 +600,13 @@ class RolloutEngine:
         return hN
 
     def _moe(self, h, pre):
+        from ..ops import moe as moe_ops
         from ..parallel.moe import moe_forward_local
         a, W = self.args, self.w
+        if moe_ops.supported(h, W[pre + "mlp.experts_w13"], W[pre + "mlp.experts_w2"]):
+            return moe_ops.moe_mlp(h, F.linear(h, W[pre + "mlp.router.weight"]).float(), W[pre + "mlp.router_prior"],
+                                   W[pre + "mlp.experts_w13"], W[pre + "mlp.experts_w2"], a.num_experts_per_tok,
+                                   bool(a.norm_topk_prob))
         logits = F.linear(h, W[pre + "mlp.router.weight"]).float() + W[pre + "mlp.router_prior"]
         probs = logits.softmax(-1)
         wt, idx = probs.topk(a.num_experts_per_tok, dim=-1)
