@@ -52,7 +52,7 @@ def test_gloo_world2_plumbing():
     assert res["n_train"] == 1 and res["world"] == 2
     assert res["steps"] == [(0, 32), (1, 32), (2, 32), (3, 32)]
     assert res["tokens"] > 0
-    assert res["sync"]["pulls"] >= 4      # initial pull + one per published version
+    assert res["sync"]["pulls"] >= 2      # initial pull + at least one newer version
 
 
 def _worker4(rank, world, port, q):
@@ -90,7 +90,9 @@ def test_gloo_world4_two_trainers_two_rollouts():
     assert codes == [0, 0, 0, 0], codes
     res = q.get(timeout=5)
     assert res["n_train"] == 2 and res["steps"] == [32, 32]
-    assert res["pulls"] >= 2 * 3
+    # each rollout instance: the initial pull plus at least one newer version
+    # (an instance that sees two new versions at once pulls only the latest)
+    assert res["pulls"] >= 2 * 2
 
 
 def _worker_hybrid(rank, world, port, q):
