@@ -178,7 +178,41 @@ def bench_sample(pk):
     return out
 
 
-CASES = {"sample": bench_sample, "decode": bench_decode, "gemm": bench_gemm, "logprob": bench_logprob, "attn": bench_attn_train,
+def bench_train_mb(pk):
+    """One trainer micro-batch of the DAPO 3B workload: 6 sequences x 1700
+    tokens (10.2k tokens) through the Qwen2.5-3B decoder, forward + backward
+    of the fused LM-head log-prob, no activation recompute.  2 warm-up + 3
+    timed iterations (5 in total, so a launch-list capture of the whole run
+    shows each kernel 5 times)."""
+    from psrl_b200.models import PRESETS, build_model
+    from psrl_b200.trainer.batch import Trajectory, build_micro_batch
+    a = PRESETS["qwen2.5-3b"]
+    model = build_model(a, torch.device("cuda"), torch.bfloat16, seed=0)
+    g = torch.Generator().manual_seed(0)
+    trajs = []
+    for i in range(6):
+        toks = torch.randint(3, a.vocab_size, (1700,), generator=g).tolist()
+        trajs.append(Trajectory(uid=i, request_id=i, prompt_ids=toks[:200], response_ids=toks[200:],
+                                rollout_logprobs=[0.0] * 1500, old_logprobs=[0.0] * 1500, advantage=1.0))
+    mb = build_micro_batch(trajs, list(range(6)), torch.device("cuda"))
+
+    def run():
+        lp, ent = model.logprobs(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen, mb.labels)
+        (lp.sum() * 1e-6 + ent.sum() * 1e-9).backward()
+
+    ms = timeit(run, iters=3, warmup=2)
+    T = mb.input_ids.numel()
+    # matmul FLOPs (6 x params x tokens, LM head included) + causal attention (fwd 1x, bwd 2.5x)
+    n_params = sum(p.numel() for p in model.parameters())
+    fl = 6.0 * n_params * T + 3.5 * 4.0 * a.num_layers * a.num_heads * a.head_dim * sum(
+        (1700 * 1700) / 2 for _ in range(6))
+    del model
+    return [{"case": f"train micro-batch qwen2.5-3b 6x1700 tokens fwd+bwd", "ms": round(ms, 2),
+             "tok_per_s": round(T / ms * 1e3, 0), "tflops": round(fl / ms / 1e9, 1),
+             "frac_bf16": round(fl / ms / 1e9 / pk["bf16_tflops"], 3)}]
+
+
+CASES = {"train_mb": bench_train_mb, "sample": bench_sample, "decode": bench_decode, "gemm": bench_gemm, "logprob": bench_logprob, "attn": bench_attn_train,
          "elementwise": bench_elementwise, "sync": bench_sync}
 
 

@@ -42,6 +42,11 @@ std::vector<at::Tensor> moe_route(at::Tensor logits, c10::optional<at::Tensor> p
 std::vector<at::Tensor> moe_permute(at::Tensor ids, at::Tensor counts, int64_t bm, int64_t tiles_n);
 at::Tensor moe_gather(at::Tensor x, at::Tensor token_of_row);
 at::Tensor moe_combine(at::Tensor ys, at::Tensor pos, at::Tensor w);
+void peer_reduce(std::vector<at::Tensor> grads, std::vector<at::Tensor> flats, at::Tensor start, at::Tensor src_off,
+                 at::Tensor red, at::Tensor sq, at::Tensor partial);
+void peer_adamw(std::vector<at::Tensor> grads, std::vector<at::Tensor> flats, at::Tensor start, at::Tensor src_off,
+                at::Tensor master, at::Tensor red, at::Tensor m, at::Tensor v, double lr, double b1, double b2,
+                double eps, double wd, int64_t step, at::Tensor coef, double gscale);
 std::vector<at::Tensor> tc_linear_logprob(at::Tensor h, at::Tensor w, at::Tensor labels, double temperature,
                                           at::Tensor err);
 void kv_copy_blocks(at::Tensor src_layers, at::Tensor dst_layers, at::Tensor src_blk, at::Tensor dst_blk,
@@ -81,6 +86,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_permute", &psrl::moe_permute);
   m.def("moe_gather", &psrl::moe_gather);
   m.def("moe_combine", &psrl::moe_combine);
+  m.def("peer_reduce", &psrl::peer_reduce);
+  m.def("peer_adamw", &psrl::peer_adamw);
   m.def("tc_linear_logprob", &psrl::tc_linear_logprob);
   m.def("kv_copy_blocks", &psrl::kv_copy_blocks);
   psrl::register_vmm(m);

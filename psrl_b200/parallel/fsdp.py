@@ -17,8 +17,10 @@ The reference trains with FSDP2 full-shard (parameters re-gathered per layer
 in every forward and backward, ``engine_train_worker.py:80-85``); keeping
 parameters resident trades 2 bytes/param of HBM for one all-gather per
 optimizer step instead of two per micro-batch.  Collectives here are NCCL
-(the baseline path); :mod:`psrl_b200.parallel.peer` provides the peer-memory
-reduce-scatter + AdamW kernel path.
+(the baseline path); :mod:`psrl_b200.parallel.peer` provides the fused
+peer-memory path (one kernel reduces this rank's shard from every peer's
+gradient buffer over NVLink, one kernel runs AdamW on it and stores the bf16
+shard into every peer's parameter buffer).
 """
 
 from __future__ import annotations
@@ -33,7 +35,7 @@ from .. import ops
 
 class _Bucket:
     def __init__(self, names, params, world: int, rank: int, device, pad_to: int, flat: torch.Tensor,
-                 grad: torch.Tensor, base: int):
+                 grad: torch.Tensor, base: int, shard_bufs: tuple, shard_start: int):
         self.names = names
         self.params = params
         n = sum(p.numel() for p in params)
@@ -55,10 +57,16 @@ class _Bucket:
             off += k
         lo = rank * self.shard
         self.lo, self.hi = lo, lo + self.shard
-        self.master = self.flat[lo: self.hi].float().clone()
-        self.m = torch.zeros_like(self.master)
-        self.v = torch.zeros_like(self.master)
-        self.grad_shard = self.grad[lo: self.hi] if world == 1 else torch.zeros_like(self.master)
+        # this rank's shard of the bucket: views into model-wide contiguous shard
+        # buffers (master, m, v, reduced grad), so one kernel can sweep them all
+        master_all, m_all, v_all, gs_all = shard_bufs
+        self.shard_start = shard_start
+        sl = slice(shard_start, shard_start + self.shard)
+        self.master = master_all[sl]
+        self.master.copy_(self.flat[lo: self.hi].float())
+        self.m = m_all[sl]
+        self.v = v_all[sl]
+        self.grad_shard = self.grad[lo: self.hi] if world == 1 else gs_all[sl]
 
     def param_shard(self) -> torch.Tensor:
         return self.flat[self.lo: self.hi]
@@ -98,20 +106,40 @@ class FlatShardedDP:
         dtype = next(model.parameters()).dtype
         self.flat = torch.zeros(self.total, dtype=dtype, device=self.device)
         self.flat_grad = torch.zeros(self.total, dtype=torch.float32, device=self.device)
+        self.shard_total = self.total // self.world
+        f32 = dict(dtype=torch.float32, device=self.device)
+        self.master_all = torch.zeros(self.shard_total, **f32)
+        self.m_all = torch.zeros(self.shard_total, **f32)
+        self.v_all = torch.zeros(self.shard_total, **f32)
+        self.grad_shard_all = torch.zeros(self.shard_total if self.world > 1 else 0, **f32)
+        bufs = (self.master_all, self.m_all, self.v_all, self.grad_shard_all)
         base = 0
+        shard_start = 0
         self.layout: list[tuple[str, tuple, int]] = []   # (name, shape, offset) in the flat buffer
         for key, sz in zip(order, sizes):
             names = [n for n, _ in groups[key]]
             params = [p for _, p in groups[key]]
-            b = _Bucket(names, params, self.world, self.rank, self.device, pad_to, self.flat, self.flat_grad, base)
+            b = _Bucket(names, params, self.world, self.rank, self.device, pad_to, self.flat, self.flat_grad, base,
+                        bufs, shard_start)
             for nm, p, off in zip(names, params, b.offsets):
                 self.layout.append((nm, tuple(p.shape), base + off))
             base += sz
+            shard_start += b.shard
             for i, p in enumerate(params):
                 self.param_to_bucket[p] = (b, b.offsets[i])
             self.buckets.append(b)
         self._hooks = [p.register_post_accumulate_grad_hook(self._accumulate) for p in self.param_to_bucket]
         self.norm = ops.NormAccumulator(self.device)
+        self.peer = None            # peer-memory step (parallel.peer.PeerShardedStep), set by enable_peer_step
+
+    def enable_peer_step(self) -> bool:
+        """Use the fused peer-memory reduce-scatter + AdamW + all-gather kernels
+        for the optimizer step (CUDA, world > 1).  Returns whether it is on."""
+        if self.world <= 1 or self.device.type != "cuda":
+            return False
+        from .peer import PeerShardedStep
+        self.peer = PeerShardedStep(self)
+        return True
 
     # --------------------------------------------------------------- grads
     def _accumulate(self, p: torch.Tensor) -> None:
@@ -133,6 +161,9 @@ class FlatShardedDP:
         """Reduce, clip, update, re-gather.  Gradients are *summed* across ranks
         (callers normalise the loss by the global token/sequence count)."""
         self.step_count += 1
+        if self.peer is not None:
+            out = self.peer.step(grad_scale)
+            return out
         self.norm.reset()
         for b in self.buckets:
             if self.world > 1:

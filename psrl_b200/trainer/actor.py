@@ -70,6 +70,9 @@ class PolicyWorker:
                                     eps=float(oc.get("eps", 1e-8)), weight_decay=float(oc.weight_decay),
                                     max_grad_norm=float(cfg.actor.grad_clip),
                                     warmup_steps=int(oc.get("lr_warmup_steps", 0)))
+            if bool(cfg.actor.get("fsdp_peer_step", True)):
+                # fused peer-memory reduce-scatter + AdamW + all-gather (CUDA, world > 1)
+                self.dp.enable_peer_step()
         else:
             for p in self.model.parameters():
                 p.requires_grad_(False)

@@ -173,3 +173,69 @@ def test_hybrid_rl_two_gpus():
     res = next(d for d in items if "steps" in d)
     assert sums[0] == sums[1]
     assert res["steps"] == [32, 32] and res["ps_version"] == 3 and res["ms"] > 0
+
+
+def _peer_step_worker(rank, world, port, q):
+    import faulthandler
+    faulthandler.dump_traceback_later(90, repeat=True)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    from psrl_b200.models import PRESETS, build_model
+    from psrl_b200.parallel.dist import init_distributed
+    from psrl_b200.parallel.fsdp import FlatShardedDP
+    info = init_distributed("cuda", timeout_s=60)
+    a = PRESETS["tiny128"]
+    dps = []
+    for peer in (False, True):
+        m = build_model(a, info.device, torch.bfloat16, seed=11)
+        dp = FlatShardedDP(m, dist.group.WORLD, lr=1e-3, weight_decay=0.1, max_grad_norm=1.0)
+        if peer:
+            assert dp.enable_peer_step()
+        dps.append(dp)
+    g = torch.Generator(device="cuda").manual_seed(100 + rank)
+    norms = []
+    for _ in range(3):
+        grad = torch.randn(dps[0].total, device="cuda", generator=g) * 0.01
+        for dp in dps:
+            dp.flat_grad.copy_(grad)
+        norms.append([float(dp.step()["grad_norm"]) for dp in dps])
+    torch.cuda.synchronize()
+    base, peer = dps
+    diff_master = float((base.master_all - peer.master_all).abs().max())
+    diff_flat = float((base.flat.float() - peer.flat.float()).abs().max())
+    # every rank must hold the same full parameters after the fused all-gather
+    fl = peer.flat.float().clone()
+    dist.all_reduce(fl, op=dist.ReduceOp.MAX)
+    same = bool(torch.equal(fl, peer.flat.float()))
+    q.put({"rank": rank, "diff_master": diff_master, "diff_flat": diff_flat, "same": same, "norms": norms,
+           "zeroed": float(peer.flat_grad.abs().max())})
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_peer_optimizer_step_matches_nccl_two_gpus():
+    """Fused peer-memory reduce-scatter + AdamW + all-gather == NCCL path."""
+    _need(2)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_peer_step_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(180)
+    codes = [p.exitcode for p in ps]
+    for p in ps:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0], codes
+    for _ in range(2):
+        r = q.get(timeout=5)
+        assert r["same"], r
+        assert r["zeroed"] == 0.0, r
+        assert r["diff_master"] < 1e-6, r
+        assert r["diff_flat"] <= 2 ** -7, r
+        for nb, npeer in r["norms"]:
+            assert abs(nb - npeer) <= 1e-4 * max(1.0, nb), r
