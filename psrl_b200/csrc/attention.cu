@@ -360,16 +360,21 @@ struct BwdParams {
   const float* lse;    // [nq, T]
   const float* Dd;     // [nq, T]
   float* dq;           // [T, nq, D] fp32 accumulators
-  bf16* dk;            // [T, nkv, D]
-  bf16* dv;
+  float* dk;           // [T, nkv, D] fp32 accumulators (the GQA group is split over CTAs)
+  float* dv;
+  int B;               // sequences
   int64_t dkv_row;     // = nkv * D
   int T;
 };
 
-// One CTA = (key tile, kv head, sequence).  It loops over the GQA group's query
-// heads and the causal query tiles; the next query tile's Q / dO / lse / D
-// loads are issued as soon as the current tile's last reader of them is done
-// (before the dQ product and its atomics), so the copy overlaps that work.
+// One CTA = (key tile, half of the GQA group, kv head, sequence), numbered so
+// that the longest CTAs (first key tiles: most causal query tiles) start first.
+// It loops over its query heads and the causal query tiles; the next query
+// tile's Q / dO / lse / D loads are issued as soon as the current tile's last
+// reader of them is done (before the dQ product and its atomics), so the copy
+// overlaps that work.  dK / dV of the two group halves meet in fp32 atomics.
+constexpr int BWD_HSPLIT = 2;
+
 __global__ void __launch_bounds__(NTHREADS) attn_bwd_kernel(BwdParams bp) {
   const Params& p = bp.f;
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -380,11 +385,21 @@ __global__ void __launch_bounds__(NTHREADS) attn_bwd_kernel(BwdParams bp) {
   bf16* sdS = sdO + BM * D;                       // [BN][BM] (keys x queries), swizzled as 64-wide rows
   __shared__ float sLse[BM], sDd[BM];
 
-  const int nb = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  int idx = blockIdx.x;
+  const int b = idx % bp.B;
+  idx /= bp.B;
+  const int kvh = idx % p.nkv;
+  idx /= p.nkv;
+  const int hs = idx % BWD_HSPLIT;
+  const int nb = idx / BWD_HSPLIT;
   const int s0 = p.cu_q[b];
   const int len = p.cu_q[b + 1] - s0;
   if (nb * BN >= len) return;
-  const int grp = p.nq / p.nkv;
+  const int grp_all = p.nq / p.nkv;
+  const int per_split = (grp_all + BWD_HSPLIT - 1) / BWD_HSPLIT;
+  const int h_first = kvh * grp_all + hs * per_split;
+  const int grp = max(0, min(per_split, grp_all - hs * per_split));   // query heads of this CTA
+  if (grp == 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float sl2 = p.scale * LOG2E;
 
@@ -408,7 +423,7 @@ __global__ void __launch_bounds__(NTHREADS) attn_bwd_kernel(BwdParams bp) {
 
   // issue the loads of iteration `it` (query head, query tile) into the single buffer
   auto issue = [&](int it) {
-    const int h = kvh * grp + it / per_head;
+    const int h = h_first + it / per_head;
     const int mt = m_start + it % per_head;
     const int nq_valid = min(BM, len - mt * BM);
     load_rows<BM>(sQ, p.q + (int64_t)(s0 + mt * BM) * p.q_row + (int64_t)h * p.q_head, p.q_row, nq_valid);
@@ -424,7 +439,7 @@ __global__ void __launch_bounds__(NTHREADS) attn_bwd_kernel(BwdParams bp) {
   if (n_iter > 0) issue(0);
 
   for (int it = 0; it < n_iter; ++it) {
-    const int h = kvh * grp + it / per_head;
+    const int h = h_first + it / per_head;
     const int mt = m_start + it % per_head;
     cp_async_wait<0>();
     __syncthreads();   // Q / dO / lse / D of this iteration visible; sdS of the previous one consumed
@@ -561,18 +576,18 @@ __global__ void __launch_bounds__(NTHREADS) attn_bwd_kernel(BwdParams bp) {
       }
     }
   }
-  // write dK, dV
+  // add this CTA's share of dK, dV
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const int key = key_row0 + r * 8;
     if (key >= len) continue;
-    bf16* dkr = bp.dk + (int64_t)(s0 + key) * bp.dkv_row + (int64_t)kvh * D;
-    bf16* dvr = bp.dv + (int64_t)(s0 + key) * bp.dkv_row + (int64_t)kvh * D;
+    float* dkr = bp.dk + (int64_t)(s0 + key) * bp.dkv_row + (int64_t)kvh * D;
+    float* dvr = bp.dv + (int64_t)(s0 + key) * bp.dkv_row + (int64_t)kvh * D;
 #pragma unroll
     for (int dt = 0; dt < 16; ++dt) {
       const int c = dt * 8 + (lane & 3) * 2;
-      *reinterpret_cast<bf162*>(dkr + c) = __floats2bfloat162_rn(dk[dt][r * 2], dk[dt][r * 2 + 1]);
-      *reinterpret_cast<bf162*>(dvr + c) = __floats2bfloat162_rn(dv[dt][r * 2], dv[dt][r * 2 + 1]);
+      atomicAdd(reinterpret_cast<float2*>(dkr + c), make_float2(dk[dt][r * 2], dk[dt][r * 2 + 1]));
+      atomicAdd(reinterpret_cast<float2*>(dvr + c), make_float2(dv[dt][r * 2], dv[dt][r * 2 + 1]));
     }
   }
 }
@@ -942,10 +957,10 @@ std::vector<at::Tensor> attn_varlen_bwd(at::Tensor dO, at::Tensor q, at::Tensor 
   const int B = cu_seqlens.numel() - 1;
   at::cuda::CUDAGuard g(q.device());
   auto dq = at::zeros({T, nq, D}, q.options().dtype(at::kFloat));
-  auto dk = at::empty({T, nkv, D}, q.options());
-  auto dv = at::empty({T, nkv, D}, q.options());
+  auto dk = at::zeros({T, nkv, D}, q.options().dtype(at::kFloat));
+  auto dv = at::zeros({T, nkv, D}, q.options().dtype(at::kFloat));
   auto Dd = at::empty({nq, T}, q.options().dtype(at::kFloat));
-  if (T == 0 || B == 0) return {dq.to(at::kBFloat16), dk, dv};
+  if (T == 0 || B == 0) return {dq.to(at::kBFloat16), dk.to(at::kBFloat16), dv.to(at::kBFloat16)};
   TORCH_CHECK(dO.stride(-1) == 1 && o.stride(-1) == 1, "dO/O need unit stride on D");
   // rows are copied in 16-byte chunks
   for (const at::Tensor* t : {&q, &k, &v, &dO})
@@ -979,20 +994,21 @@ std::vector<at::Tensor> attn_varlen_bwd(at::Tensor dO, at::Tensor q, at::Tensor 
   bp.lse = lse.data_ptr<float>();
   bp.Dd = Dd.data_ptr<float>();
   bp.dq = dq.data_ptr<float>();
-  bp.dk = reinterpret_cast<bf16*>(dk.data_ptr());
-  bp.dv = reinterpret_cast<bf16*>(dv.data_ptr());
+  bp.dk = dk.data_ptr<float>();
+  bp.dv = dv.data_ptr<float>();
   bp.dkv_row = (int64_t)nkv * D;
   bp.T = T;
+  bp.B = B;
   const size_t sm = bwd_smem();
   static bool attr = false;
   if (!attr) {
     PSRL_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
     attr = true;
   }
-  dim3 grid((max_seqlen + BN - 1) / BN, nkv, B);
-  attn_bwd_kernel<<<grid, NTHREADS, sm, stream()>>>(bp);
+  const int64_t nblk = (int64_t)((max_seqlen + BN - 1) / BN) * BWD_HSPLIT * nkv * B;
+  attn_bwd_kernel<<<(unsigned)nblk, NTHREADS, sm, stream()>>>(bp);
   PSRL_CHECK_LAUNCH();
-  return {dq.to(at::kBFloat16), dk, dv};
+  return {dq.to(at::kBFloat16), dk.to(at::kBFloat16), dv.to(at::kBFloat16)};
 }
 
 int64_t decode_num_splits(int64_t batch, int64_t nkv, int64_t max_ctx) {
