@@ -137,3 +137,25 @@ def test_gloo_world2_hybrid_placement():
     assert res["steps"] == [32, 32] and res["tokens"] > 0
     assert res["ps_version"] == 3
     assert res["pulls"] >= 2          # both engines picked up at least one new version
+
+
+def test_gloo_world4_hybrid_placement():
+    """Four ranks, each a trainer replica and a rollout instance."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_hybrid, args=(r, 4, port, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0, 0, 0], codes
+    items = [q.get(timeout=5) for _ in range(5)]
+    sums = {d["rank"]: d["checksum"] for d in items if "checksum" in d}
+    res = next(d for d in items if "steps" in d)
+    assert len(set(sums.values())) == 1, sums
+    assert res["steps"] == [32, 32] and res["ps_version"] == 3
