@@ -116,6 +116,8 @@ def save_hf(model, path: str, max_shard_bytes: int = 5 << 30) -> list[str]:
     """Write ``config.json`` + safetensors shards (+ index) in HF format."""
     from safetensors.torch import save_file
 
+    if any(getattr(getattr(layer, "mlp", None), "ep", None) is not None for layer in model.layers):
+        raise NotImplementedError("HF export of an expert-parallel model needs its experts gathered first")
     os.makedirs(path, exist_ok=True)
     a: ModelArgs = model.args
     state = {k: v.detach().to("cpu").contiguous() for k, v in model.state_dict().items()}

@@ -97,6 +97,12 @@ class MoE(nn.Module):
 
     def forward(self, x):
         from ..ops import moe as moe_ops
+        ep = getattr(self, "ep", None)
+        if ep is not None:
+            # expert parallel: this rank holds experts [ep.first, ep.first + ep.local)
+            from ..parallel.ep import moe_forward_ep
+            w, idx = self.route(x)
+            return moe_forward_ep(x, w, idx, self.experts_w13, self.experts_w2, ep)
         if moe_ops.supported(x, self.experts_w13, self.experts_w2):
             return moe_ops.moe_mlp(x, self.router(x).float(), self.router_prior, self.experts_w13, self.experts_w2,
                                    self.a.num_experts_per_tok, bool(self.a.norm_topk_prob))

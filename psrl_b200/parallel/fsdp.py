@@ -75,9 +75,14 @@ class _Bucket:
 class FlatShardedDP:
     def __init__(self, model: torch.nn.Module, group=None, *, lr: float = 1e-6, betas=(0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 0.0, max_grad_norm: float = 1.0, warmup_steps: int = 0,
-                 bucket_mode: str = "layer"):
+                 bucket_mode: str = "layer", param_filter=None, norm_group=None):
+        """``param_filter(name) -> bool`` selects the parameters this instance
+        owns (default: all trainable ones).  ``norm_group``: ranks whose
+        parameters are disjoint from this rank's (expert parallelism), summed
+        into the squared gradient norm in addition to ``group``'s shards."""
         self.model = model
         self.group = group
+        self.norm_group = norm_group
         # no group = this rank trains alone (even inside a larger job)
         self.world = dist.get_world_size(group) if (group is not None and dist.is_initialized()) else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
@@ -90,7 +95,7 @@ class FlatShardedDP:
         groups: dict[str, list] = {}
         order: list[str] = []
         for name, p in model.named_parameters():
-            if not p.requires_grad:
+            if not p.requires_grad or (param_filter is not None and not param_filter(name)):
                 continue
             key = ".".join(name.split(".")[:2]) if (bucket_mode == "layer" and name.startswith("layers.")) else "misc"
             if key not in groups:
@@ -104,6 +109,7 @@ class FlatShardedDP:
         sizes = [math.ceil(sum(p.numel() for _, p in groups[k]) / pad_to) * pad_to for k in order]
         self.total = sum(sizes)
         dtype = next(model.parameters()).dtype
+        self.num_params = sum(p.numel() for k in order for _, p in groups[k])
         self.flat = torch.zeros(self.total, dtype=dtype, device=self.device)
         self.flat_grad = torch.zeros(self.total, dtype=torch.float32, device=self.device)
         self.shard_total = self.total // self.world
@@ -157,13 +163,32 @@ class FlatShardedDP:
         return self.lr
 
     @torch.no_grad()
-    def step(self, grad_scale: float = 1.0) -> dict:
+    def step(self, grad_scale: float = 1.0, partners: list | None = None) -> dict:
         """Reduce, clip, update, re-gather.  Gradients are *summed* across ranks
-        (callers normalise the loss by the global token/sequence count)."""
-        self.step_count += 1
-        if self.peer is not None:
-            out = self.peer.step(grad_scale)
-            return out
+        (callers normalise the loss by the global token/sequence count).
+        ``partners``: other FlatShardedDP instances of the same model (e.g. the
+        expert-parallel parameters) stepped with one shared clip coefficient."""
+        group_all = [self] + list(partners or [])
+        for d in group_all:
+            d.step_count += 1
+        if self.peer is not None and not partners:
+            return self.peer.step(grad_scale)
+        sq = torch.zeros(1, dtype=torch.float32, device=self.device)
+        for d in group_all:
+            sq += d.reduce_grads()
+        if grad_scale != 1.0:
+            sq.mul_(grad_scale * grad_scale)
+        self.norm.sq.copy_(sq)
+        coef, gnorm = self.norm.clip_coef(self.max_grad_norm)
+        lr = self.current_lr()
+        for d in group_all:
+            d.apply_update(coef, lr, grad_scale)
+        return {"grad_norm": gnorm, "lr": lr}
+
+    @torch.no_grad()
+    def reduce_grads(self) -> torch.Tensor:
+        """Reduce-scatter the main grads into this rank's shards; returns the
+        global squared norm of this instance's gradients (device scalar)."""
         self.norm.reset()
         for b in self.buckets:
             if self.world > 1:
@@ -171,10 +196,12 @@ class FlatShardedDP:
             self.norm.add(b.grad_shard)
         if self.world > 1:
             dist.all_reduce(self.norm.sq, group=self.group)
-        if grad_scale != 1.0:
-            self.norm.sq.mul_(grad_scale * grad_scale)
-        coef, gnorm = self.norm.clip_coef(self.max_grad_norm)
-        lr = self.current_lr()
+        if self.norm_group is not None:
+            dist.all_reduce(self.norm.sq, group=self.norm_group)
+        return self.norm.sq.clone()
+
+    @torch.no_grad()
+    def apply_update(self, coef: torch.Tensor, lr: float, grad_scale: float = 1.0) -> None:
         b1, b2 = self.betas
         for b in self.buckets:
             ops.adamw_(b.master, b.grad_shard, b.m, b.v, b.param_shard(), lr, b1, b2, self.eps, self.wd,
@@ -182,7 +209,6 @@ class FlatShardedDP:
             if self.world > 1:
                 dist.all_gather_into_tensor(b.flat, b.param_shard(), group=self.group)
         self.zero_grad()
-        return {"grad_norm": gnorm, "lr": lr}
 
     # -------------------------------------------------------------- state
     def full_params(self) -> dict[str, torch.Tensor]:

@@ -64,13 +64,29 @@ class PolicyWorker:
         self.model.gradient_checkpointing = bool(cfg.model.enable_gradient_checkpointing)
         self.dp_rank, self.dp_world = dp_rank, dp_world
         self.dp = None
+        self.dp_experts = None
+        self.ep = None
+        expert_names: set = set()
+        ep_size = int(cfg.actor.get("expert_parallel_size", 1) or 1)
+        if args.is_moe and ep_size > 1:
+            # expert parallelism over the data-parallel group: rank r keeps
+            # experts [r E/P, (r+1) E/P) of every layer (K12)
+            from ..parallel.ep import make_ep_group, shard_experts
+            if dp_group is None or dp_world != ep_size:
+                raise ValueError("expert_parallel_size must equal the data-parallel world size")
+            self.ep = make_ep_group(dp_group, args.num_experts)
+            expert_names = set(shard_experts(self.model, self.ep))
         if trainable:
             oc = cfg.actor.optim if not args.value_head else cfg.critic.optim
-            self.dp = FlatShardedDP(self.model, dp_group, lr=float(oc.lr), betas=tuple(oc.get("betas", (0.9, 0.999))),
-                                    eps=float(oc.get("eps", 1e-8)), weight_decay=float(oc.weight_decay),
-                                    max_grad_norm=float(cfg.actor.grad_clip),
-                                    warmup_steps=int(oc.get("lr_warmup_steps", 0)))
-            if bool(cfg.actor.get("fsdp_peer_step", True)):
+            kw = dict(lr=float(oc.lr), betas=tuple(oc.get("betas", (0.9, 0.999))), eps=float(oc.get("eps", 1e-8)),
+                      weight_decay=float(oc.weight_decay), max_grad_norm=float(cfg.actor.grad_clip),
+                      warmup_steps=int(oc.get("lr_warmup_steps", 0)))
+            self.dp = FlatShardedDP(self.model, dp_group, param_filter=lambda n: n not in expert_names, **kw)
+            if expert_names:
+                # each rank's experts are its own: no reduction, but the clip norm spans all ranks
+                self.dp_experts = FlatShardedDP(self.model, None, param_filter=lambda n: n in expert_names,
+                                                norm_group=dp_group, **kw)
+            elif bool(cfg.actor.get("fsdp_peer_step", True)):
                 # fused peer-memory reduce-scatter + AdamW + all-gather (CUDA, world > 1)
                 self.dp.enable_peer_step()
         else:
@@ -158,7 +174,7 @@ class PolicyWorker:
                         # bounded launch queue: the host thread releases the GIL here
                         torch.cuda.current_stream().synchronize()
                 with guard():
-                    st = self.dp.step()
+                    st = self.dp.step(partners=[self.dp_experts] if self.dp_experts else None)
                     if self.device.type == "cuda":
                         torch.cuda.current_stream().synchronize()
                 stats.setdefault("grad_norm", []).append(st["grad_norm"])
@@ -189,7 +205,7 @@ class PolicyWorker:
                 m["vf_loss"] = loss.detach()
                 for k, val in m.items():
                     stats.setdefault(k, []).append(val)
-            st = self.dp.step()
+            st = self.dp.step(partners=[self.dp_experts] if self.dp_experts else None)
             stats.setdefault("grad_norm", []).append(st["grad_norm"])
         return {f"critic/{k}": float(torch.stack([x.reshape(()).float() for x in vs]).mean()) for k, vs in stats.items()}
 

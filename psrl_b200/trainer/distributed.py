@@ -96,6 +96,9 @@ class DisaggregatedRun:
         cfg = self.cfg
         self.actor = PolicyWorker(cfg, self.args, self.device, dp_group=self.train_group,
                                   seed=int(cfg.trainer.seed), dp_rank=self.rank, dp_world=self.n_train)
+        if self.actor.ep is not None:
+            raise NotImplementedError("rollout weight sync from an expert-parallel trainer (experts are sharded "
+                                      "over the trainer ranks) is not wired yet")
         self.layout = WeightLayout.from_dp(self.actor.dp)
         mode = "hbm" if (cfg.psrl.ps_mode == "hbm" and self.device.type == "cuda") else "cpu"
         self.store = WeightStore(self.layout, self.device, mode)

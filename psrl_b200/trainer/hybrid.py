@@ -87,6 +87,9 @@ class HybridRun:
         seed = int(cfg.trainer.seed)
         self.actor = PolicyWorker(cfg, self.args, self.device, dp_group=dp_group, seed=seed,
                                   dp_rank=self.rank, dp_world=self.world)
+        if self.actor.ep is not None:
+            raise NotImplementedError("rollout weight sync from an expert-parallel trainer (experts are sharded "
+                                      "over the trainer ranks) is not wired yet")
         self.ref = None
         if cfg.actor.use_kl_loss:
             self.ref = PolicyWorker(cfg, self.args, self.device, seed=seed, trainable=False)

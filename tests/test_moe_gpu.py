@@ -87,3 +87,37 @@ def test_moe_mlp_gradients():
     for gf, gr in zip(*outs):
         rel = (gf - gr).norm() / gr.norm().clamp_min(1e-12)
         assert rel < 5e-2, float(rel)
+
+
+def test_moe_model_fused_path_matches_local_path(monkeypatch):
+    from psrl_b200.models import PRESETS, build_model, packed_positions
+    from psrl_b200.ops import moe
+    a = PRESETS["tiny-moe"]
+    m = build_model(a, "cuda", torch.bfloat16, seed=2)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    lens = [37, 64, 5]
+    ids = torch.randint(0, a.vocab_size, (sum(lens),), device="cuda", generator=g)
+    pos, cu, mx = packed_positions(lens, "cuda")
+    with torch.no_grad():
+        h_fused = m.hidden_states(ids, pos, cu, mx).float()
+        monkeypatch.setattr(moe, "supported", lambda *args: False)
+        h_local = m.hidden_states(ids, pos, cu, mx).float()
+    rel = (h_fused - h_local).norm() / h_local.norm()
+    assert rel < 3e-2, float(rel)
+
+
+def test_moe_rollout_engine_decodes_with_graphs():
+    from psrl_b200.models import PRESETS, build_model
+    from psrl_b200.rollout import EngineWeights, GenRequest, RolloutEngine, SamplingParams
+    a = PRESETS["tiny-moe"]
+    m = build_model(a, "cuda", torch.bfloat16, seed=2)
+    eng = RolloutEngine(a, EngineWeights.from_model(m), max_num_seqs=8, max_model_len=256, block_size=64,
+                        kv_cache_gb=0.5, use_cuda_graph=True)
+    for i in range(5):
+        eng.add_request(GenRequest(i, list(range(3, 3 + 10 + i)), SamplingParams(max_tokens=12, ignore_eos=True,
+                                                                                seed=i)))
+    outs = []
+    while eng.has_unfinished():
+        outs += eng.step()
+    assert len(outs) == 5 and all(len(o.output_ids) == 12 for o in outs)
+    assert all(0 <= t < a.vocab_size for o in outs for t in o.output_ids)
