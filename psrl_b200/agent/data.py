@@ -101,6 +101,13 @@ class DataProcessor:
         self.cursor += 1
         return it
 
+    # validation prompts come from their own uid range, disjoint from training
+    VAL_UID_BASE = 1 << 40
+
+    def validation_items(self, n: int) -> list[PromptItem]:
+        """The first ``n`` validation prompts (deterministic, never trained on)."""
+        return [self.src.item(self.VAL_UID_BASE + i) for i in range(int(n))]
+
     def state_dict(self) -> dict:
         return {"cursor": self.cursor}
 

@@ -281,7 +281,72 @@ class RLTrainer:
             freq = int(self.cfg.trainer.save_freq)
             if freq > 0 and self.global_step % freq == 0:
                 self.save_checkpoint()
+            tf = int(self.cfg.trainer.get("test_freq", -1))
+            if tf > 0 and self.global_step % tf == 0:
+                out[-1].update(self.validate())
         return out
+
+    # --------------------------------------------------------- validation
+    VAL_RID_BASE = 1 << 50
+
+    def validate(self, num_prompts: int | None = None) -> dict:
+        """Generate on the validation prompts with the current weights and
+        score them (``val/score_mean``, ``val/response_length/mean``).
+
+        The rollout engine is shared with training: the overlapped rollout
+        thread is paused, validation requests join the in-flight training
+        requests (whose completions still go to the agent-loop manager), and
+        generation continues until every validation request finished.  The
+        engine first pulls the latest published weights.  Validation samples
+        use ``trainer.val_temperature`` (0 = greedy) and ``psrl.val_rollout_n``
+        samples per prompt.  Reference: the trainer's validate step
+        (``psrl/trainer/ppo/ray_trainer.py``, ``test_freq``)."""
+        from ..rollout.engine import GenRequest, SamplingParams
+        from .batch import Trajectory
+        self.stop_rollout()
+        cfg = self.cfg
+        n = int(num_prompts if num_prompts is not None else cfg.data.get("val_size", 32))
+        per = max(1, int(cfg.psrl.get("val_rollout_n", 1)))
+        temp = float(cfg.trainer.get("val_temperature", 0.0))
+        rc = cfg.rollout
+        ps_v = self.ps.get_ps_model_version()
+        if ps_v > self.engine.version:
+            self._pull_weights(ps_v)
+        items = self.data.validation_items(n)
+        pending: dict[int, tuple] = {}
+        for i, it in enumerate(items):
+            for j in range(per):
+                rid = self.VAL_RID_BASE + i * per + j
+                mt = int(it.response_lens[j % len(it.response_lens)]) if it.response_lens else int(rc.max_response_length)
+                params = SamplingParams(temperature=temp, top_p=1.0, top_k=-1, max_tokens=mt,
+                                        ignore_eos=bool(rc.ignore_eos), seed=rid)
+                meta = dict(it.meta)
+                if it.answer is not None:
+                    meta["answer"] = it.answer
+                self.engine.add_request(GenRequest(rid, list(it.prompt_ids), params, self.engine.version, meta))
+                pending[rid] = (it, meta)
+        scores, lens = [], []
+        ctx = torch.cuda.stream(self.rollout_stream) if self.rollout_stream is not None else None
+        import contextlib
+        with ctx or contextlib.nullcontext():
+            while pending:
+                outs = self.engine.step()
+                train_outs = []
+                for o in outs:
+                    if o.request_id in pending:
+                        it, meta = pending.pop(o.request_id)
+                        tr = Trajectory(uid=it.uid, request_id=o.request_id, prompt_ids=list(o.prompt_ids),
+                                        response_ids=list(o.output_ids), rollout_logprobs=list(o.logprobs),
+                                        meta=meta)
+                        scores.append(float(self.reward.score(tr)["score"]))
+                        lens.append(len(o.output_ids))
+                    else:
+                        train_outs.append(o)
+                if train_outs:
+                    self.manager.on_complete(train_outs, self.instance_id)
+        m = len(scores)
+        return {"val/score_mean": sum(scores) / max(1, m), "val/response_length/mean": sum(lens) / max(1, m),
+                "val/num_samples": m}
 
     # -------------------------------------------------------- checkpoints
     def save_checkpoint(self) -> str:
