@@ -15,6 +15,10 @@ Selection pipeline for one request over the live instances:
    or ``cache_aware`` (longest prefix match in the instance's recent-prefix
    index, unless the load imbalance exceeds the balance thresholds).
 
+The prefix index and the policy arithmetic run in the native router core
+(``csrc_host/router_core.cpp``, module ``psrl_b200._router``); the stages that
+consult Python objects (eligibility, PS admission, stickiness) stay here.
+
 Reference: ``psrl/workers/gen/smg_adapter.py:47-153`` (router arguments) and
 ``docs/design/router_tito.md``.
 """
@@ -22,8 +26,9 @@ Reference: ``psrl/workers/gen/smg_adapter.py:47-153`` (router arguments) and
 from __future__ import annotations
 
 import random
-from collections import OrderedDict
 from dataclasses import dataclass, field
+
+import numpy as np
 
 
 @dataclass
@@ -45,35 +50,22 @@ class InstanceState:
 
 
 class PrefixIndex:
-    """Per-instance LRU set of block-hash chains of recently routed prompts."""
+    """Per-instance LRU set of block-hash chains of recently routed prompts
+    (native: ``csrc_host/router_core.cpp``)."""
 
     def __init__(self, block_size: int = 16, max_entries: int = 1 << 16):
+        from .. import _router
         self.bs = block_size
-        self.max = max_entries
-        self.entries: OrderedDict[int, None] = OrderedDict()
-
-    def _chain(self, tokens) -> list[int]:
-        hs, h = [], 0
-        for i in range(len(tokens) // self.bs):
-            h = hash((h, tuple(tokens[i * self.bs:(i + 1) * self.bs])))
-            hs.append(h)
-        return hs
+        self._ix = _router.PrefixIndex(block_size, max_entries)
 
     def match(self, tokens) -> int:
-        n = 0
-        for h in self._chain(tokens):
-            if h not in self.entries:
-                break
-            self.entries.move_to_end(h)
-            n += 1
-        return n * self.bs
+        return int(self._ix.match(np.asarray(tokens, dtype=np.int64)))
 
     def insert(self, tokens) -> None:
-        for h in self._chain(tokens):
-            self.entries[h] = None
-            self.entries.move_to_end(h)
-        while len(self.entries) > self.max:
-            self.entries.popitem(last=False)
+        self._ix.insert(np.asarray(tokens, dtype=np.int64))
+
+    def __len__(self) -> int:
+        return len(self._ix)
 
 
 class ThroughputModel:
@@ -144,29 +136,22 @@ class Router:
 
     # -------------------------------------------------------------- policy
     def pick(self, req, cands: list[InstanceState]) -> InstanceState:
+        """Policy choice among admitted candidates (native core except ``random``)."""
+        from .. import _router
         m = self.method
         if m == "random":
             return self.rng.choice(cands)
-        if m == "round_robin":
-            s = cands[self.rr % len(cands)]
-            self.rr += 1
-            return s
-        if m == "request_num_balance":
-            return min(cands, key=lambda s: (s.load, s.kv_usage))
-        if m in ("throughput_optimal", "throughput_optimal_with_budget"):
-            pool = cands
-            if m.endswith("budget"):
-                pool = [s for s in cands if s.load < self.request_budget] or cands
-            return max(pool, key=lambda s: self.tput.marginal(s.load))
-        # cache aware
         loads = [s.load for s in cands]
-        lo, hi = min(loads), max(loads)
-        if hi - lo > self.balance_abs and hi > self.balance_rel * max(lo, 1):
-            return min(cands, key=lambda s: s.load)
-        toks = list(req.prompt_ids) + list(getattr(req, "prev_output_ids", []))
-        best = max(cands, key=lambda s: (self.prefix.setdefault(s.instance_id, PrefixIndex(self.block_size)).match(toks),
-                                         -s.load))
-        return best
+        kv = [float(s.kv_usage) for s in cands]
+        match = [0] * len(cands)
+        if m.startswith("cache_aware"):
+            toks = list(req.prompt_ids) + list(getattr(req, "prev_output_ids", []))
+            match = [self.prefix.setdefault(s.instance_id, PrefixIndex(self.block_size)).match(toks) for s in cands]
+        i = _router.pick(m, loads, kv, match, self.rr, self.request_budget, self.balance_abs, float(self.balance_rel),
+                         float(self.tput.A), float(self.tput.B), float(self.tput.k))
+        if m == "round_robin":
+            self.rr += 1
+        return cands[i]
 
     def route(self, req, instances: list[InstanceState]) -> InstanceState | None:
         cands = self.eligible(req, instances)

@@ -10,6 +10,7 @@ import glob
 import os
 
 from setuptools import find_packages, setup
+from pybind11.setup_helpers import Pybind11Extension
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -46,7 +47,15 @@ setup(
             sources=[os.path.relpath(s, ROOT) for s in sources],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
             libraries=["cuda"],
-        )
+        ),
+        # host-only runtime pieces (plain pybind11, no CUDA or torch linkage):
+        # they load on CPU-only machines too
+        Pybind11Extension(
+            "psrl_b200._router",
+            [os.path.relpath(os.path.join(ROOT, "psrl_b200", "csrc_host", "router_core.cpp"), ROOT)],
+            cxx_std=17,
+            extra_compile_args=["-O3"],
+        ),
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )

@@ -271,3 +271,31 @@ def test_cli_print_config_and_run(capsys):
     assert "staleness: 2" in out
     assert main(["--preset", "cpu_tiny_grpo", "--steps", "1", "rollout.max_response_length=8"]) == 0
     assert '"step": 0' in capsys.readouterr().out
+
+
+def test_native_router_core_prefix_and_policies():
+    import random
+
+    import numpy as np
+
+    from psrl_b200 import _router
+    ix = _router.PrefixIndex(4, 3)
+    ix.insert(np.arange(8))                    # 2 blocks
+    assert ix.match(np.arange(12)) == 8 and ix.match(np.array([9, 9, 9, 9])) == 0
+    ix.insert(np.arange(100, 108))             # 2 more blocks: capacity 3 evicts the oldest
+    assert len(ix) == 3 and ix.match(np.arange(8)) == 0
+    rng = random.Random(0)
+    for _ in range(200):
+        n = rng.randint(1, 6)
+        load = [rng.randint(0, 40) for _ in range(n)]
+        kv = [rng.random() for _ in range(n)]
+        match = [rng.choice([0, 16, 32]) for _ in range(n)]
+        # request_num_balance: first minimal (load, kv)
+        assert _router.pick("request_num_balance", load, kv, match, 0, 1024, 16, 1.5, 7271.5, 0.05, 1.0) == \
+            min(range(n), key=lambda i: (load[i], kv[i]))
+        # cache_aware without imbalance: longest match, then least loaded
+        i = _router.pick("cache_aware", load, kv, match, 0, 1024, 10 ** 6, 1.5, 7271.5, 0.05, 1.0)
+        assert i == max(range(n), key=lambda j: (match[j], -load[j], -j))
+        # throughput_optimal: the concave curve's marginal gain is largest at the lowest load
+        t = _router.pick("throughput_optimal", load, kv, match, 0, 1024, 16, 1.5, 7271.5, 0.05, 1.0)
+        assert load[t] == min(load)
