@@ -1,0 +1,155 @@
+"""Megatron-style tensor parallelism for the trainer's dense decoder (K15,
+baseline collectives).
+
+With a tensor-parallel group of size P, rank r keeps
+
+* attention: query heads [r nq/P, (r+1) nq/P) and KV heads [r nkv/P, ...) of
+  the fused QKV projection (column parallel, bias sliced alike) and the
+  matching input columns of the output projection (row parallel);
+* MLP: intermediate columns [r I/P, (r+1) I/P) of both the gate and the up
+  halves of ``gate_up`` (column parallel, still [gate | up] per rank) and the
+  matching input columns of ``down`` (row parallel);
+* everything else (embedding, norms, q/k head norms, LM head) replicated.
+
+A layer's input enters the column-parallel projections through
+``copy_to_tp`` (identity forward, all-reduce of the gradient backward) and the
+row-parallel outputs leave through ``reduce_from_tp`` (all-reduce forward,
+identity backward), so replicated parameters see identical activations and
+gradients on every rank.  The collectives are NCCL on GPU (the baseline path;
+the GEMM-fused reduce-scatter / all-gather kernels are not built) and gloo on
+CPU.  Shards are sliced from the full deterministically initialised model, so
+TP and single-rank runs start from the same weights.
+
+Reference: the Megatron TP layouts the reference converts
+(``psrl/utils/megatron_converter.py``) and the 7B PPO recipe at TP=2.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, replace
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .. import ops
+
+
+@dataclass
+class TPGroup:
+    group: object
+    world: int
+    rank: int
+
+
+def make_tp_group(group) -> TPGroup:
+    return TPGroup(group, dist.get_world_size(group), dist.get_rank(group))
+
+
+class _CopyToTP(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        g = g.contiguous().clone()
+        dist.all_reduce(g, group=ctx.group)
+        return g, None
+
+
+class _ReduceFromTP(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, group):
+        y = x.contiguous().clone()
+        dist.all_reduce(y, group=group)
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        return g, None
+
+
+def copy_to_tp(x, tp: TPGroup):
+    return _CopyToTP.apply(x, tp.group)
+
+
+def reduce_from_tp(x, tp: TPGroup):
+    return _ReduceFromTP.apply(x, tp.group)
+
+
+class TPAttention(nn.Module):
+    def __init__(self, full, tp: TPGroup):
+        super().__init__()
+        a = full.a
+        if a.num_heads % tp.world or a.num_kv_heads % tp.world:
+            raise ValueError(f"{a.num_heads} query / {a.num_kv_heads} KV heads do not split over TP={tp.world}")
+        self.tp = tp
+        self.a = a
+        self.la = replace(a, num_heads=a.num_heads // tp.world, num_kv_heads=a.num_kv_heads // tp.world)
+        d, r = a.head_dim, tp.rank
+        qn, kn = self.la.num_heads * d, self.la.num_kv_heads * d
+        rows = torch.cat([torch.arange(r * qn, (r + 1) * qn),
+                          a.q_size + torch.arange(r * kn, (r + 1) * kn),
+                          a.q_size + a.kv_size + torch.arange(r * kn, (r + 1) * kn)])
+        w = full.qkv.weight.data
+        self.qkv_weight = nn.Parameter(w.index_select(0, rows.to(w.device)).clone())
+        self.qkv_bias = None
+        if full.qkv.bias is not None:
+            self.qkv_bias = nn.Parameter(full.qkv.bias.data.index_select(0, rows.to(w.device)).clone())
+        self.o_weight = nn.Parameter(full.o.weight.data[:, r * qn:(r + 1) * qn].clone())
+        if a.qk_norm:
+            self.q_norm = nn.Parameter(full.q_norm.data.clone())
+            self.k_norm = nn.Parameter(full.k_norm.data.clone())
+
+    def forward(self, x, positions, cu_seqlens, max_seqlen):
+        la = self.la
+        x = copy_to_tp(x, self.tp)
+        qkv = F.linear(x, self.qkv_weight, self.qkv_bias)
+        if la.qk_norm:
+            T = qkv.shape[0]
+            q, k, v = qkv.split([la.q_size, la.kv_size, la.kv_size], dim=-1)
+            q = ops.head_rms_norm(q.reshape(T, la.num_heads, la.head_dim), self.q_norm, la.rms_eps).reshape(T, -1)
+            k = ops.head_rms_norm(k.reshape(T, la.num_kv_heads, la.head_dim), self.k_norm, la.rms_eps).reshape(T, -1)
+            qkv = torch.cat([q, k, v], dim=-1)
+        qkv = ops.rope_qkv(qkv.contiguous(), positions, la.num_heads, la.num_kv_heads, la.head_dim, la.rope_theta)
+        o = ops.varlen_attention(qkv, cu_seqlens, max_seqlen, la.num_heads, la.num_kv_heads, la.head_dim)
+        return reduce_from_tp(F.linear(o, self.o_weight), self.tp)
+
+
+class TPMLP(nn.Module):
+    def __init__(self, full, tp: TPGroup, intermediate: int):
+        super().__init__()
+        if intermediate % tp.world:
+            raise ValueError(f"intermediate size {intermediate} does not split over TP={tp.world}")
+        self.tp = tp
+        il, r = intermediate // tp.world, tp.rank
+        w = full.gate_up.weight.data
+        self.gate_up_weight = nn.Parameter(torch.cat([w[r * il:(r + 1) * il], w[intermediate + r * il:
+                                                                                   intermediate + (r + 1) * il]]).clone())
+        self.down_weight = nn.Parameter(full.down.weight.data[:, r * il:(r + 1) * il].clone())
+
+    def forward(self, x):
+        x = copy_to_tp(x, self.tp)
+        return reduce_from_tp(F.linear(ops.swiglu(F.linear(x, self.gate_up_weight)), self.down_weight), self.tp)
+
+
+@torch.no_grad()
+def apply_tensor_parallel(model, tp: TPGroup) -> list[str]:
+    """Shard every dense decoder layer of ``model`` in place; returns the names
+    of the sharded parameters (the rest are replicated)."""
+    a = model.args
+    if a.is_moe:
+        raise ValueError("tensor parallelism here covers dense decoders; MoE layers use expert parallelism")
+    names = []
+    for i, layer in enumerate(model.layers):
+        layer.attn = TPAttention(layer.attn, tp)
+        layer.mlp = TPMLP(layer.mlp, tp, a.intermediate_size)
+        names += [f"layers.{i}.attn.qkv_weight", f"layers.{i}.attn.o_weight", f"layers.{i}.mlp.gate_up_weight",
+                  f"layers.{i}.mlp.down_weight"]
+        if layer.attn.qkv_bias is not None:
+            names.append(f"layers.{i}.attn.qkv_bias")
+    model.tp = tp
+    return names

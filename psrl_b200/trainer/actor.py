@@ -29,6 +29,11 @@ def _dtype(name: str, device) -> torch.dtype:
     return {"bf16": torch.bfloat16, "fp32": torch.float32, "fp16": torch.float16}[name]
 
 
+def dist_world(group) -> int:
+    import torch.distributed as dist
+    return dist.get_world_size(group) if dist.is_initialized() else 1
+
+
 def mini_batch_groups(trajs: list[Trajectory], mini_batch_size: int) -> list[list[int]]:
     """Split by prompt group into ``mini_batch_size`` groups per mini-batch."""
     by_uid: dict = {}
@@ -55,7 +60,7 @@ def plan_update(trajs: list[Trajectory], mini_batch_size: int, dp_world: int) ->
 
 class PolicyWorker:
     def __init__(self, cfg, args: ModelArgs, device, dp_group=None, seed: int = 0, trainable: bool = True,
-                 dp_rank: int = 0, dp_world: int = 1):
+                 dp_rank: int = 0, dp_world: int = 1, tp_group=None):
         self.cfg = cfg
         self.args = args
         self.device = torch.device(device)
@@ -64,9 +69,15 @@ class PolicyWorker:
         self.model.gradient_checkpointing = bool(cfg.model.enable_gradient_checkpointing)
         self.dp_rank, self.dp_world = dp_rank, dp_world
         self.dp = None
-        self.dp_experts = None
+        self.dp_partner = None
         self.ep = None
         expert_names: set = set()
+        self.tp = None
+        if tp_group is not None and dist_world(tp_group) > 1:
+            # tensor parallelism inside tp_group (data parallelism across dp_group)
+            from ..parallel.tp import apply_tensor_parallel, make_tp_group
+            self.tp = make_tp_group(tp_group)
+            self.tp_sharded = set(apply_tensor_parallel(self.model, self.tp))
         ep_size = int(cfg.actor.get("expert_parallel_size", 1) or 1)
         if args.is_moe and ep_size > 1:
             # expert parallelism over the data-parallel group: rank r keeps
@@ -81,12 +92,20 @@ class PolicyWorker:
             kw = dict(lr=float(oc.lr), betas=tuple(oc.get("betas", (0.9, 0.999))), eps=float(oc.get("eps", 1e-8)),
                       weight_decay=float(oc.weight_decay), max_grad_norm=float(cfg.actor.grad_clip),
                       warmup_steps=int(oc.get("lr_warmup_steps", 0)))
-            self.dp = FlatShardedDP(self.model, dp_group, param_filter=lambda n: n not in expert_names, **kw)
-            if expert_names:
+            if self.tp is not None:
+                # TP-sharded parameters: disjoint across the TP group (norm summed over it);
+                # replicated parameters: identical across it (counted once)
+                sh = self.tp_sharded
+                self.dp = FlatShardedDP(self.model, dp_group, param_filter=lambda n: n not in sh, **kw)
+                self.dp_partner = FlatShardedDP(self.model, dp_group, param_filter=lambda n: n in sh,
+                                                norm_group=tp_group, **kw)
+            else:
+                self.dp = FlatShardedDP(self.model, dp_group, param_filter=lambda n: n not in expert_names, **kw)
+            if self.tp is None and expert_names:
                 # each rank's experts are its own: no reduction, but the clip norm spans all ranks
-                self.dp_experts = FlatShardedDP(self.model, None, param_filter=lambda n: n in expert_names,
+                self.dp_partner = FlatShardedDP(self.model, None, param_filter=lambda n: n in expert_names,
                                                 norm_group=dp_group, **kw)
-            elif bool(cfg.actor.get("fsdp_peer_step", True)):
+            elif self.tp is None and bool(cfg.actor.get("fsdp_peer_step", True)):
                 # fused peer-memory reduce-scatter + AdamW + all-gather (CUDA, world > 1)
                 self.dp.enable_peer_step()
         else:
@@ -174,7 +193,7 @@ class PolicyWorker:
                         # bounded launch queue: the host thread releases the GIL here
                         torch.cuda.current_stream().synchronize()
                 with guard():
-                    st = self.dp.step(partners=[self.dp_experts] if self.dp_experts else None)
+                    st = self.dp.step(partners=[self.dp_partner] if self.dp_partner else None)
                     if self.device.type == "cuda":
                         torch.cuda.current_stream().synchronize()
                 stats.setdefault("grad_norm", []).append(st["grad_norm"])
@@ -205,7 +224,7 @@ class PolicyWorker:
                 m["vf_loss"] = loss.detach()
                 for k, val in m.items():
                     stats.setdefault(k, []).append(val)
-            st = self.dp.step(partners=[self.dp_experts] if self.dp_experts else None)
+            st = self.dp.step(partners=[self.dp_partner] if self.dp_partner else None)
             stats.setdefault("grad_norm", []).append(st["grad_norm"])
         return {f"critic/{k}": float(torch.stack([x.reshape(()).float() for x in vs]).mean()) for k, vs in stats.items()}
 

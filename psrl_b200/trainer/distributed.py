@@ -69,6 +69,8 @@ class DisaggregatedRun:
             self.train_group = pdist.new_subgroup(trainer_ranks, backend=backend)
             self.train_cpu_group = pdist.new_subgroup(trainer_ranks, backend="gloo")
         self.args = model_args_from_config(cfg.model)
+        if int(cfg.actor.get("tensor_parallel_size", 1) or 1) > 1:
+            raise NotImplementedError("tensor-parallel trainers are not wired into the multi-GPU placements yet")
         self.trained_tokens = 0
         self.global_step = 0
         self.liveness_s = float(cfg.trainer.get("liveness_timeout_s", 300))

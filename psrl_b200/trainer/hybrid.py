@@ -63,6 +63,8 @@ class HybridRun:
         self.device = info.device
         self.is_cuda = self.device.type == "cuda"
         self.args = model_args_from_config(cfg.model)
+        if int(cfg.actor.get("tensor_parallel_size", 1) or 1) > 1:
+            raise NotImplementedError("tensor-parallel trainers are not wired into the multi-GPU placements yet")
         if cfg.critic.enable or cfg.algorithm.use_kl_in_reward:
             raise NotImplementedError("hybrid placement trains critic-free estimators without in-reward KL; "
                                       "use the one-GPU trainer or the disaggregated placement")

@@ -61,7 +61,7 @@ def _worker(rank, world, port, q):
     h = w.model.hidden_states(ids, pos, cu, mx)
     (h * coef).sum().backward()
     before = w.model.layers[0].mlp.experts_w13.detach().clone()
-    st = w.dp.step(partners=[w.dp_experts])
+    st = w.dp.step(partners=[w.dp_partner])
     out["moved"] = float((w.model.layers[0].mlp.experts_w13.detach() - before).abs().max())
     out["grad_norm"] = float(st["grad_norm"])
     q.put(out)
