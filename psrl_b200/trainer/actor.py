@@ -204,13 +204,16 @@ class PolicyWorker:
             out[f"actor/{k}"] = float(t.sum()) if k in ("pg_loss", "entropy") else float(t.mean())
         return out
 
-    def update_critic(self, trajs: list[Trajectory]) -> dict:
+    def update_critic(self, trajs: list[Trajectory], plan: list[tuple] | None = None) -> dict:
+        """Value-loss update; ``plan`` as in :meth:`update_policy`."""
         cc = self.cfg.critic
         self.model.train()
         stats: dict[str, list] = {}
-        for mini in self._mini_batches(trajs):
-            global_tokens = float(sum(trajs[i].response_len for i in mini))
-            for bin_ in pack_micro_batches(self.my_share(trajs, mini), trajs, self.max_tokens):
+        if plan is None:
+            plan = [(self.my_share(trajs, mini), float(sum(trajs[i].response_len for i in mini)), len(mini))
+                    for mini in self._mini_batches(trajs)]
+        for mine, global_tokens, _ in plan:
+            for bin_ in pack_micro_batches(mine, trajs, self.max_tokens):
                 mb = build_micro_batch(trajs, bin_, self.device)
                 v = self.model.values(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen)
                 old_v = torch.zeros_like(v)

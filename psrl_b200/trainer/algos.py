@@ -100,8 +100,10 @@ def reinforce_pp_returns(token_rewards: torch.Tensor, mask: torch.Tensor, gamma:
     return masked_whiten(ret, mask)
 
 
-def gae_advantage(token_rewards: torch.Tensor, values: torch.Tensor, mask: torch.Tensor, gamma: float, lam: float):
-    """[N, L] tensors -> (advantages whitened [N, L], returns [N, L])."""
+def gae_advantage(token_rewards: torch.Tensor, values: torch.Tensor, mask: torch.Tensor, gamma: float, lam: float,
+                  whiten: bool = True):
+    """[N, L] tensors -> (advantages [N, L] (whitened over the batch unless
+    ``whiten`` is False), returns [N, L])."""
     N, L = token_rewards.shape
     adv = torch.zeros(N, L, dtype=torch.float32)
     last = torch.zeros(N, dtype=torch.float32)
@@ -114,7 +116,7 @@ def gae_advantage(token_rewards: torch.Tensor, values: torch.Tensor, mask: torch
         adv[:, t] = last
         nextv = torch.where(m > 0, values[:, t].float(), nextv)
     returns = adv + values.float()
-    return masked_whiten(adv, mask), returns * mask
+    return (masked_whiten(adv, mask) if whiten else adv * mask), returns * mask
 
 
 def optimal_token_baseline_advantage(scores: torch.Tensor, uids, lengths: torch.Tensor, eps: float = 1e-6):

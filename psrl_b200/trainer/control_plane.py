@@ -148,7 +148,14 @@ class ControlPlane:
         use_rollout_lp = bool(self.cfg.psrl.log_prob.enable_rollout_engine_log_prob)
         for t in trajs:
             t.old_logprobs = t.rollout_logprobs if use_rollout_lp else None
-        adv_metrics = compute_batch_advantages(self.cfg, trajs)
+        if self.cfg.critic.enable:
+            # GAE needs the critic's values: the trainer ranks compute advantages on
+            # their own shares (whitened with global statistics)
+            sc = [t.reward for t in trajs]
+            adv_metrics = {"critic/score_mean": sum(sc) / max(1, len(sc)), "critic/score_max": max(sc, default=0.0),
+                           "critic/score_min": min(sc, default=0.0)}
+        else:
+            adv_metrics = compute_batch_advantages(self.cfg, trajs)
         plans = plan_update(trajs, int(self.cfg.actor.ppo_mini_batch_size), dp_world)
         per_rank = {}
         for r in range(dp_world):

@@ -65,9 +65,8 @@ class HybridRun:
         self.args = model_args_from_config(cfg.model)
         if int(cfg.actor.get("tensor_parallel_size", 1) or 1) > 1:
             raise NotImplementedError("tensor-parallel trainers are not wired into the multi-GPU placements yet")
-        if cfg.critic.enable or cfg.algorithm.use_kl_in_reward:
-            raise NotImplementedError("hybrid placement trains critic-free estimators without in-reward KL; "
-                                      "use the one-GPU trainer or the disaggregated placement")
+        if cfg.algorithm.use_kl_in_reward:
+            raise NotImplementedError("hybrid placement: in-reward KL is not wired (use_kl_loss is)")
         self.trained_tokens = 0
         self.global_step = 0
         self.liveness_s = float(cfg.trainer.get("liveness_timeout_s", 300))
@@ -92,6 +91,12 @@ class HybridRun:
         if self.actor.ep is not None:
             raise NotImplementedError("rollout weight sync from an expert-parallel trainer (experts are sharded "
                                       "over the trainer ranks) is not wired yet")
+        self.critic = None
+        if cfg.critic.enable:
+            from dataclasses import replace as _replace
+            cargs = _replace(self.args, value_head=True, tie_word_embeddings=False)
+            self.critic = PolicyWorker(cfg, cargs, self.device, dp_group=dp_group, seed=seed + 1,
+                                       dp_rank=self.rank, dp_world=self.world)
         self.ref = None
         if cfg.actor.use_kl_loss:
             self.ref = PolicyWorker(cfg, self.args, self.device, seed=seed, trainable=False)
@@ -203,6 +208,11 @@ class HybridRun:
                 self.ref.compute_log_prob(trajs, idx, field="ref_logprobs")
             if not bool(self.cfg.psrl.log_prob.enable_rollout_engine_log_prob):
                 self.actor.compute_log_prob(trajs, idx, field="old_logprobs")
+            critic_metrics = {}
+            if self.critic is not None:
+                self.critic.compute_values(trajs, idx)
+                self._gae(trajs)
+                critic_metrics = self.critic.update_critic(trajs, plan=plan)
             metrics = self.actor.update_policy(trajs, float(self.cfg.rollout.temperature),
                                                step_guard=lambda: self.wlock.exclusive(600),
                                                sync_every_micro_batch=self.is_cuda, plan=plan)
@@ -214,6 +224,7 @@ class HybridRun:
         self.global_step += 1
         self.trained_tokens += int(batch["trained_tokens"])
         metrics.update(batch["metrics"])
+        metrics.update(critic_metrics)
         metrics.update({
             "step": b, "num_trajectories": batch["num_trajectories"], "trained_tokens": batch["trained_tokens"],
             "response_length/mean": batch["response_length/mean"], "staleness/max": batch["staleness/max"],
@@ -222,6 +233,33 @@ class HybridRun:
         })
         metrics.update({f"rollout/{k}": v for k, v in self.engine.engine_stats().items() if isinstance(v, (int, float))})
         return metrics
+
+    def _gae(self, trajs) -> None:
+        """GAE on this rank's trajectories, whitened with the mean and variance
+        of all ranks' response tokens (one all-reduce of three numbers)."""
+        from . import algos
+        cfg = self.cfg
+        L = max((t.response_len for t in trajs), default=1)
+        N = len(trajs)
+        rew, vals, mask = torch.zeros(N, L), torch.zeros(N, L), torch.zeros(N, L)
+        for i, t in enumerate(trajs):
+            n = t.response_len
+            mask[i, :n] = 1
+            rew[i, n - 1] = t.reward
+            vals[i, :n] = torch.tensor(t.old_values[:n])
+        adv, ret = algos.gae_advantage(rew, vals, mask, float(cfg.algorithm.gamma), float(cfg.algorithm.lam),
+                                       whiten=False)
+        st = torch.tensor([float((adv * mask).sum()), float((adv * adv * mask).sum()), float(mask.sum())],
+                          dtype=torch.float64)
+        if self.cpu_group is not None:
+            dist.all_reduce(st, group=self.cpu_group)
+        mean = st[0] / st[2].clamp_min(1)
+        var = st[1] / st[2].clamp_min(1) - mean * mean
+        adv = ((adv - float(mean)) * float(torch.rsqrt(var.clamp_min(0) + 1e-8))) * mask
+        for i, t in enumerate(trajs):
+            n = t.response_len
+            t.token_advantages = adv[i, :n].tolist()
+            t.returns = ret[i, :n].tolist()
 
     def close(self) -> None:
         self.stop_rollout()

@@ -159,3 +159,43 @@ def test_gloo_world4_hybrid_placement():
     res = next(d for d in items if "steps" in d)
     assert len(set(sums.values())) == 1, sums
     assert res["steps"] == [32, 32] and res["ps_version"] == 3
+
+
+def _worker_hybrid_ppo(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch
+    torch.set_num_threads(1)
+    from psrl_b200.config import load_config
+    from psrl_b200.parallel.dist import init_distributed
+    from psrl_b200.trainer.hybrid import run_hybrid
+    cfg = load_config(preset="cpu_tiny_grpo", overrides=["rollout.max_response_length=12", "critic.enable=true",
+                                                         "algorithm.adv_estimator=gae"])
+    info = init_distributed("cpu", timeout_s=120)
+    res = run_hybrid(cfg, steps=2, warmup=0, info=info)
+    if rank == 0:
+        q.put({"steps": [m["num_trajectories"] for m in res["metrics"]],
+               "vf": [m.get("critic/vf_loss") for m in res["metrics"]]})
+    import torch.distributed as dist
+    dist.destroy_process_group()
+
+
+def test_gloo_world2_hybrid_ppo_with_critic():
+    """PPO with a critic in the hybrid placement: values on each rank's share,
+    GAE whitened with all ranks' statistics, critic and actor updates."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_hybrid_ppo, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0], codes
+    res = q.get(timeout=5)
+    assert res["steps"] == [32, 32]
+    assert all(v is not None and v >= 0 for v in res["vf"]), res
