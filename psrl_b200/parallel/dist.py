@@ -58,6 +58,15 @@ def new_subgroup(ranks: list[int], backend: str | None = None):
     return dist.new_group(ranks=ranks, backend=backend, use_local_synchronization=True)
 
 
+def broadcast_value(v, src: int = 0, group=None):
+    """Broadcast a picklable value from ``src`` (identity without a process group)."""
+    if not dist.is_initialized():
+        return v
+    box = [v]
+    dist.broadcast_object_list(box, src=src, group=group)
+    return box[0]
+
+
 def barrier(group=None):
     if dist.is_initialized():
         if dist.get_backend(group) == "nccl" and torch.cuda.is_available():

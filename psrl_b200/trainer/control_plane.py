@@ -216,26 +216,44 @@ class ControlPlane:
                 "manager": self.manager.snapshot(), "ps_version": self.ps.get_ps_model_version()}
 
 
-def _control_plane_main(cfg, vocab_size: int, n_train: int, port: int, liveness_s: float) -> None:
+def _control_plane_main(cfg, vocab_size: int, n_train: int, port: int, liveness_s: float, ready=None) -> None:
     import os
     os.environ["CUDA_VISIBLE_DEVICES"] = ""        # this process never touches a GPU
     import torch
     torch.set_num_threads(1)
     cp = ControlPlane(cfg, vocab_size, n_train, liveness_s)
     server = RPCServer({"cp": cp}, port=port)
+    if ready is not None:
+        ready.put(int(server.address[1]))           # the port actually bound (port=0: any free one)
     try:
         cp._done.wait()
     finally:
         server.close()
 
 
-def spawn_control_plane(cfg, vocab_size: int, n_train: int, port: int, liveness_s: float = 300.0):
-    """Start the control-plane process (rank 0 calls this once); returns the process."""
+def spawn_control_plane(cfg, vocab_size: int, n_train: int, port: int = 0, liveness_s: float = 300.0,
+                        timeout_s: float = 600.0):
+    """Start the control-plane process (rank 0 calls this once); returns
+    ``(process, port)``.  With ``port=0`` the process binds a free port and
+    reports it, so concurrent jobs on one machine never collide."""
     import multiprocessing as mp
-    p = mp.get_context("spawn").Process(target=_control_plane_main, args=(cfg, vocab_size, n_train, port, liveness_s),
-                                        daemon=True, name="psrl-control-plane")
+    import queue
+    ctx = mp.get_context("spawn")
+    ready = ctx.Queue()
+    p = ctx.Process(target=_control_plane_main, args=(cfg, vocab_size, n_train, port, liveness_s, ready),
+                    daemon=True, name="psrl-control-plane")
     p.start()
-    return p
+    t0 = time.monotonic()
+    while True:
+        try:
+            bound = ready.get(timeout=1.0)
+            return p, int(bound)
+        except queue.Empty:
+            if not p.is_alive():
+                raise RuntimeError(f"control-plane process exited with code {p.exitcode} before serving")
+            if time.monotonic() - t0 > timeout_s:
+                p.terminate()
+                raise TimeoutError("control-plane process did not start in time")
 
 
 def connect(port: int, timeout: float = 1800.0) -> RPCClient:

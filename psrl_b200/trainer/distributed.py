@@ -76,13 +76,13 @@ class DisaggregatedRun:
         self.liveness_s = float(cfg.trainer.get("liveness_timeout_s", 300))
         self.buffer_timeout_s = float(cfg.trainer.get("buffer_timeout_s", 1800))
         log(f"role split: {self.n_train} trainer rank(s), {self.world - self.n_train} rollout rank(s)")
-        port = int(os.environ.get("MASTER_PORT", "29511")) + 17
         self.cp_proc = None
+        port = 0
         if self.rank == 0:
-            self.cp_proc = spawn_control_plane(cfg, self.args.vocab_size, self.n_train, port, self.liveness_s)
+            self.cp_proc, port = spawn_control_plane(cfg, self.args.vocab_size, self.n_train, 0, self.liveness_s)
             self.client = RPCClient(("127.0.0.1", port), retries=6000)
             self.client.call("cp", "ping")
-        pdist.barrier()
+        port = pdist.broadcast_value(port)
         if self.rank != 0:
             self.client = RPCClient(("127.0.0.1", port), retries=6000)
         self.cp = self.client.proxy("cp")

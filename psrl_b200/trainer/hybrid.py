@@ -71,13 +71,13 @@ class HybridRun:
         self.global_step = 0
         self.liveness_s = float(cfg.trainer.get("liveness_timeout_s", 300))
         self.buffer_timeout_s = float(cfg.trainer.get("buffer_timeout_s", 1800))
-        port = int(os.environ.get("MASTER_PORT", "29511")) + 23
         self.cp_proc = None
+        port = 0
         if self.rank == 0:
-            self.cp_proc = spawn_control_plane(cfg, self.args.vocab_size, self.world, port, self.liveness_s)
+            self.cp_proc, port = spawn_control_plane(cfg, self.args.vocab_size, self.world, 0, self.liveness_s)
             self.cli_train = RPCClient(("127.0.0.1", port), retries=6000)
             self.cli_train.call("cp", "ping")
-        pdist.barrier()
+        port = pdist.broadcast_value(port)
         if self.rank != 0:
             self.cli_train = RPCClient(("127.0.0.1", port), retries=6000)
         self.cli_roll = RPCClient(("127.0.0.1", port), retries=6000)
