@@ -90,11 +90,18 @@ class RewardManager:
             "max_response_length": int(cfg.rollout.max_response_length),
             "task": r.get("task", "bernoulli_hash" if r.kind in ("naive", "dapo") else r.kind),
         }
-        if self.kind not in REWARD_LOOPS:
+        if ":" in self.kind:
+            # user code named in the config: "package.module:fn" or "path/file.py:fn",
+            # called as fn(ctx, traj) -> {"score": float, ...}
+            from ..utils.common import load_object
+            self._fn = load_object(self.kind)
+        elif self.kind not in REWARD_LOOPS:
             raise KeyError(f"unknown reward loop {self.kind!r}; registered: {sorted(REWARD_LOOPS)}")
+        else:
+            self._fn = REWARD_LOOPS[self.kind]
 
     def score(self, traj) -> dict:
-        return REWARD_LOOPS[self.kind](self.ctx, traj)
+        return self._fn(self.ctx, traj)
 
     @staticmethod
     def normalize_reward(scores: list[float]) -> list[float]:

@@ -54,3 +54,43 @@ def test_elastic_policy_up_down_and_cooldown():
                          slept.append, woke.append)
     ex.tick()
     assert woke == [(1, 0)]
+
+
+def test_common_helpers(tmp_path):
+    from psrl_b200.utils.common import (HttpPostPool, chatml, load_object, pack_sample, parse_worker_name,
+                                        unpack_sample, worker_name)
+    f = tmp_path / "myreward.py"
+    f.write_text("def score(ctx, traj):\n    return {'score': float(len(traj.response_ids))}\n")
+    fn = load_object(f"{f}:score")
+    assert load_object("os.path:join") is __import__("os").path.join
+    from psrl_b200.trainer.batch import Trajectory
+    t = Trajectory(uid=0, request_id=1, prompt_ids=[1], response_ids=[2, 3, 4], rollout_logprobs=[0.0] * 3)
+    assert fn({}, t)["score"] == 3.0
+    n = worker_name("rollout", 5, (2, 0))
+    assert n == "rollout-i2.0-r5" and parse_worker_name(n) == {"role": "rollout", "instance": (2, 0), "rank": 5}
+    s = {"ids": [1, 2, 3], "lp": [-0.5, -1.25], "meta": {"turns": 2}}
+    assert unpack_sample(pack_sample(s)) == s
+    assert chatml([{"role": "user", "content": "hi"}]) == "<|im_start|>user\nhi<|im_end|>\n<|im_start|>assistant\n"
+    calls = {"n": 0}
+
+    def flaky(url, payload, timeout):
+        calls["n"] += 1
+        if calls["n"] == 1:
+            raise ConnectionError("first try fails")
+        return {"echo": payload["x"]}
+    pool = HttpPostPool(max_inflight=2, retries=2, backoff_s=0.0, post=flaky)
+    assert pool.submit("http://unused", {"x": 7}).result(timeout=5) == {"echo": 7}
+    assert pool.stats["retried"] == 1 and pool.stats["ok"] == 1
+    pool.close()
+
+
+def test_reward_from_user_module(tmp_path):
+    f = tmp_path / "rw.py"
+    f.write_text("def fn(ctx, traj):\n    return {'score': 0.25}\n")
+    from psrl_b200.config import load_config
+    from psrl_b200.reward import RewardManager
+    from psrl_b200.trainer.batch import Trajectory
+    cfg = load_config(preset="cpu_tiny_grpo", overrides=[f"reward.kind={f}:fn"])
+    rm = RewardManager(cfg)
+    t = Trajectory(uid=0, request_id=1, prompt_ids=[1], response_ids=[2], rollout_logprobs=[0.0])
+    assert rm.score(t)["score"] == 0.25
