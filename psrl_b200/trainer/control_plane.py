@@ -170,17 +170,22 @@ class ControlPlane:
             "staleness/max": max((b - t.version_tag) for t in trajs) if trajs else 0,
         }
 
-    def get_batch(self, b: int, rank: int, dp_world: int, timeout_s: float = 1800.0) -> dict:
-        """Rank ``rank``'s share of staleness buffer ``b`` (blocks until READY)."""
+    def get_batch(self, b: int, rank: int, dp_world: int, timeout_s: float = 1800.0, tp_index: int = 0,
+                  tp_size: int = 1) -> dict:
+        """Data-parallel rank ``rank``'s share of staleness buffer ``b`` (blocks
+        until READY).  The ``tp_size`` tensor-parallel ranks of one
+        data-parallel rank all receive the same share."""
         b, rank = int(b), int(rank)
         with self._cv:
             lk = self._batch_locks.setdefault(b, threading.Lock())
         with lk:
             if b not in self._batches:
-                self._batches[b] = self._build(b, int(dp_world), timeout_s)
+                ent = self._build(b, int(dp_world), timeout_s)
+                ent["left"] = {(r, t) for r in range(int(dp_world)) for t in range(int(tp_size))}
+                self._batches[b] = ent
             ent = self._batches[b]
-        mine = ent["per_rank"].pop(rank)
-        ent["left"].discard(rank)
+            mine = ent["per_rank"][rank]
+            ent["left"].discard((rank, int(tp_index)))
         if not ent["left"]:
             with self._cv:
                 self._batches.pop(b, None)

@@ -63,8 +63,6 @@ class HybridRun:
         self.device = info.device
         self.is_cuda = self.device.type == "cuda"
         self.args = model_args_from_config(cfg.model)
-        if int(cfg.actor.get("tensor_parallel_size", 1) or 1) > 1:
-            raise NotImplementedError("tensor-parallel trainers are not wired into the multi-GPU placements yet")
         if cfg.algorithm.use_kl_in_reward:
             raise NotImplementedError("hybrid placement: in-reward KL is not wired (use_kl_loss is)")
         self.trained_tokens = 0
@@ -84,31 +82,69 @@ class HybridRun:
         self.cp = self.cli_train.proxy("cp")
         self.cp_roll = self.cli_roll.proxy("cp")
         self.cpu_group = pdist.new_subgroup(list(range(self.world)), backend="gloo") if self.world > 1 else None
-        dp_group = dist.group.WORLD if self.world > 1 else None
+        # trainer layout: tensor-parallel groups of `tp` consecutive ranks, data
+        # parallelism across them (expert parallelism spans the data-parallel group)
+        tp = int(cfg.actor.get("tensor_parallel_size", 1) or 1)
+        if self.world % tp:
+            raise ValueError(f"world size {self.world} is not a multiple of tensor_parallel_size={tp}")
+        self.tp_size = tp
+        self.dp_rank, self.dp_world = self.rank // tp, self.world // tp
+        dp_group = tp_group = None
+        if self.world > 1:
+            if tp == 1:
+                dp_group = dist.group.WORLD
+            else:
+                for k in range(self.dp_world):        # every rank creates every group (same order)
+                    g = dist.new_group(list(range(k * tp, (k + 1) * tp)))
+                    if k == self.dp_rank:
+                        tp_group = g
+                for j in range(tp):
+                    g = dist.new_group(list(range(j, self.world, tp)))
+                    if j == self.rank % tp:
+                        dp_group = g
+                if self.dp_world == 1:
+                    dp_group = None
         seed = int(cfg.trainer.seed)
         self.actor = PolicyWorker(cfg, self.args, self.device, dp_group=dp_group, seed=seed,
-                                  dp_rank=self.rank, dp_world=self.world)
-        if self.actor.ep is not None:
-            raise NotImplementedError("rollout weight sync from an expert-parallel trainer (experts are sharded "
-                                      "over the trainer ranks) is not wired yet")
+                                  dp_rank=self.dp_rank, dp_world=self.dp_world, tp_group=tp_group)
+        self.assembler = None
+        if self.actor.ep is not None or self.actor.tp is not None:
+            # the engine holds the full model; sharded weights are all-gathered after each step
+            from ..parallel.assemble import FullWeightAssembler
+            self.assembler = FullWeightAssembler(
+                self.actor.model, ep=self.actor.ep, tp=self.actor.tp,
+                ep_names=[n for n in dict(self.actor.model.named_parameters()) if "experts_w" in n]
+                if self.actor.ep is not None else (),
+                tp_names=sorted(self.actor.tp_sharded) if self.actor.tp is not None else ())
         self.critic = None
         if cfg.critic.enable:
             from dataclasses import replace as _replace
             cargs = _replace(self.args, value_head=True, tie_word_embeddings=False)
             self.critic = PolicyWorker(cfg, cargs, self.device, dp_group=dp_group, seed=seed + 1,
-                                       dp_rank=self.rank, dp_world=self.world)
+                                       dp_rank=self.dp_rank, dp_world=self.dp_world, tp_group=tp_group)
         self.ref = None
         if cfg.actor.use_kl_loss:
             self.ref = PolicyWorker(cfg, self.args, self.device, seed=seed, trainable=False)
         self.wlock = RWLock()
-        # engine weights: one flat copy in the trainer's flat layout (a pull is one copy)
-        layout = WeightLayout.from_dp(self.actor.dp)
-        self.eng_flat = self.actor.dp.flat.detach().clone()
-        w = EngineWeights(self.args, self.device, self.actor.dtype)
-        w.flat = self.eng_flat
-        w.tensors = layout.views(self.eng_flat)
-        for name, b in self.actor.model.named_buffers():
-            w.tensors[name] = b.to(self.device)
+        if self.assembler is None:
+            # engine weights: one flat copy in the trainer's flat layout (a pull is one copy)
+            layout = WeightLayout.from_dp(self.actor.dp)
+            self.eng_flat = self.actor.dp.flat.detach().clone()
+            w = EngineWeights(self.args, self.device, self.actor.dtype)
+            w.flat = self.eng_flat
+            w.tensors = layout.views(self.eng_flat)
+            for name, b in self.actor.model.named_buffers():
+                w.tensors[name] = b.to(self.device)
+        else:
+            # engine weights: the full (unsharded) model, filled by the assembler
+            from ..models import build_model
+            full = build_model(self.args, self.device, self.actor.dtype, seed=seed)
+            w = EngineWeights.from_model(full, self.device, dtype=self.actor.dtype)
+            del full
+            self.eng_flat = None
+            with self.wlock.exclusive(600):
+                self.assembler.gather()
+                self.assembler.assemble_into(w.tensors)
         self.engine_weights = w
         rc = cfg.rollout
         max_len = int(rc.max_prompt_length) + int(rc.max_response_length) + 64
@@ -140,7 +176,10 @@ class HybridRun:
         with self.wlock.shared(600):
             # the PS version is read first: the local parameters are at least that new
             v = self.cp_roll.pull_model(self.instance_id)
-            self.eng_flat.copy_(self.actor.dp.flat, non_blocking=True)
+            if self.assembler is None:
+                self.eng_flat.copy_(self.actor.dp.flat, non_blocking=True)
+            else:
+                self.assembler.assemble_into(self.engine_weights.tensors)
             if self.is_cuda:
                 torch.cuda.current_stream().synchronize()
         self.engine.load_weights(None, v)
@@ -199,7 +238,8 @@ class HybridRun:
             raise RuntimeError("rollout thread failed") from self._rollout_error
         self.start_rollout()
         t0 = time.perf_counter()
-        batch = self.cp.get_batch(b, self.rank, self.world, self.buffer_timeout_s)
+        batch = self.cp.get_batch(b, self.dp_rank, self.dp_world, self.buffer_timeout_s, self.rank % self.tp_size,
+                                  self.tp_size)
         trajs, plan = batch["trajs"], batch["plan"]
         t1 = time.perf_counter()
         idx = list(range(len(trajs)))
@@ -216,6 +256,12 @@ class HybridRun:
             metrics = self.actor.update_policy(trajs, float(self.cfg.rollout.temperature),
                                                step_guard=lambda: self.wlock.exclusive(600),
                                                sync_every_micro_batch=self.is_cuda, plan=plan)
+            if self.assembler is not None:
+                # all ranks: gather the sharded weights for the full-model engines
+                with self.wlock.exclusive(600):
+                    self.assembler.gather()
+                    if self.is_cuda:
+                        torch.cuda.current_stream().synchronize()
         t2 = time.perf_counter()
         if self.cpu_group is not None:
             dist.barrier(group=self.cpu_group)      # every replica holds version b + 1
@@ -319,7 +365,9 @@ def run_hybrid(cfg, steps: int, warmup: int, info: pdist.DistInfo | None = None,
         wall_max = pdist.all_reduce_max(wall, info.device)
         out = {"ms": ms_max, "wall_s": wall_max, "rank": run.rank, "metrics": metrics, "world": run.world,
                "tokens": sum(int(m["trained_tokens"]) for m in metrics),
-               "param_checksum": float(run.actor.dp.flat.double().sum())}
+               "param_checksum": float(run.actor.dp.flat.double().sum()),
+               "engine_checksum": float(sum(t.double().sum() for k, t in run.engine_weights.tensors.items()
+                                            if "prior" not in k))}
         if run.rank == 0:
             out["cp"] = run.cp.stats()
         pdist.barrier()

@@ -199,3 +199,53 @@ def test_gloo_world2_hybrid_ppo_with_critic():
     res = q.get(timeout=5)
     assert res["steps"] == [32, 32]
     assert all(v is not None and v >= 0 for v in res["vf"]), res
+
+
+def _worker_hybrid_sharded(rank, world, port, q, overrides):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch
+    torch.set_num_threads(1)
+    from psrl_b200.config import load_config
+    from psrl_b200.parallel.dist import init_distributed
+    from psrl_b200.trainer.hybrid import run_hybrid
+    cfg = load_config(preset="cpu_tiny_grpo", overrides=["rollout.max_response_length=12"] + list(overrides))
+    info = init_distributed("cpu", timeout_s=120)
+    res = run_hybrid(cfg, steps=2, warmup=0, info=info)
+    q.put({"rank": rank, "engine": res["engine_checksum"], "tokens": res["tokens"],
+           "steps": [m["num_trajectories"] for m in res["metrics"]] if rank == 0 else None})
+    import torch.distributed as dist
+    dist.destroy_process_group()
+
+
+def _run_sharded(overrides):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_hybrid_sharded, args=(r, 2, port, q, overrides)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0], codes
+    return sorted([q.get(timeout=5) for _ in range(2)], key=lambda d: d["rank"])
+
+
+def test_gloo_world2_hybrid_expert_parallel_moe():
+    """MoE trainer with experts sharded over two ranks; both full-model
+    engines receive identical assembled weights."""
+    res = _run_sharded(["model.preset=tiny-moe", "++actor.expert_parallel_size=2"])
+    assert res[0]["steps"] == [32, 32]
+    assert abs(res[0]["engine"] - res[1]["engine"]) < 1e-6 * max(1.0, abs(res[0]["engine"]))
+
+
+def test_gloo_world2_hybrid_tensor_parallel():
+    """Dense trainer at TP=2 (one data-parallel rank); both engines hold the
+    assembled full weights."""
+    res = _run_sharded(["++actor.tensor_parallel_size=2"])
+    assert res[0]["steps"] == [32, 32]
+    assert abs(res[0]["engine"] - res[1]["engine"]) < 1e-6 * max(1.0, abs(res[0]["engine"]))

@@ -102,3 +102,53 @@ def test_tensor_parallel_matches_unsharded_decoder():
         # Adam's first step is sign-like (lr = 1e-2 per element): near-zero gradients
         # that differ in the last bits may move differently, never by a whole step
         assert r["param_diff"] < 1e-3, r
+
+
+def _assemble_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch
+    import torch.distributed as dist
+    torch.set_num_threads(1)
+    from psrl_b200.config import load_config
+    from psrl_b200.models import PRESETS, build_model
+    from psrl_b200.parallel.assemble import FullWeightAssembler
+    from psrl_b200.parallel.dist import init_distributed
+    from psrl_b200.rollout.engine import EngineWeights
+    from psrl_b200.trainer.actor import PolicyWorker
+    init_distributed("cpu", timeout_s=120)
+    worst = {}
+    for preset, kw in (("tiny", {"tp_group": dist.group.WORLD}),
+                       ("tiny-moe", {"dp_group": dist.group.WORLD, "dp_rank": rank, "dp_world": world})):
+        a = PRESETS[preset]
+        cfg = load_config(preset="cpu_tiny_grpo", overrides=[f"model.preset={preset}",
+                                                             "++actor.expert_parallel_size=2"])
+        w = PolicyWorker(cfg, a, "cpu", seed=9, **kw)
+        asm = FullWeightAssembler(w.model, ep=w.ep, tp=w.tp,
+                                  ep_names=[n for n, _ in w.model.named_parameters() if "experts_w" in n]
+                                  if w.ep is not None else (),
+                                  tp_names=sorted(w.tp_sharded) if w.tp is not None else ())
+        eng = EngineWeights.from_model(build_model(a, "cpu", torch.float32, seed=123), "cpu", torch.float32)
+        asm.gather()
+        asm.assemble_into(eng.tensors)
+        ref = dict(build_model(a, "cpu", torch.float32, seed=9).named_parameters())
+        worst[preset] = max(float((eng.tensors[n] - p.detach()).abs().max()) for n, p in ref.items())
+    q.put(worst)
+    dist.destroy_process_group()
+
+
+def test_full_weight_assembly_from_tp_and_ep_shards():
+    """The rollout engine's full weights assembled from TP / EP shards equal
+    the unsharded model's weights exactly."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_assemble_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(240)
+    assert [p.exitcode for p in procs] == [0, 0]
+    for _ in range(2):
+        w = q.get(timeout=5)
+        assert w["tiny"] == 0.0 and w["tiny-moe"] == 0.0, w
