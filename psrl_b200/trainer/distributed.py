@@ -64,13 +64,29 @@ class DisaggregatedRun:
         backend = "nccl" if self.device.type == "cuda" else "gloo"
         self.train_group = None
         self.train_cpu_group = None
+        # trainer layout: tensor-parallel groups of `tp` consecutive trainer ranks,
+        # data parallelism across them
+        tp = int(cfg.actor.get("tensor_parallel_size", 1) or 1)
+        if self.n_train % tp:
+            raise ValueError(f"{self.n_train} trainer ranks are not a multiple of tensor_parallel_size={tp}")
+        self.tp_size = tp
+        self.dp_rank, self.dp_world = self.rank // tp, self.n_train // tp
+        self.tp_group = None
         if self.is_trainer and self.n_train > 1:
             # created by the trainer ranks only (group-local synchronisation)
-            self.train_group = pdist.new_subgroup(trainer_ranks, backend=backend)
             self.train_cpu_group = pdist.new_subgroup(trainer_ranks, backend="gloo")
+            if tp == 1:
+                self.train_group = pdist.new_subgroup(trainer_ranks, backend=backend)
+            else:
+                for k in range(self.dp_world):
+                    g = pdist.new_subgroup(list(range(k * tp, (k + 1) * tp)), backend=backend) \
+                        if k == self.dp_rank else None
+                    if g is not None:
+                        self.tp_group = g
+                j = self.rank % tp
+                if self.dp_world > 1:
+                    self.train_group = pdist.new_subgroup(list(range(j, self.n_train, tp)), backend=backend)
         self.args = model_args_from_config(cfg.model)
-        if int(cfg.actor.get("tensor_parallel_size", 1) or 1) > 1:
-            raise NotImplementedError("tensor-parallel trainers are not wired into the multi-GPU placements yet")
         self.trained_tokens = 0
         self.global_step = 0
         self.liveness_s = float(cfg.trainer.get("liveness_timeout_s", 300))
@@ -97,14 +113,39 @@ class DisaggregatedRun:
     def _init_trainer(self):
         cfg = self.cfg
         self.actor = PolicyWorker(cfg, self.args, self.device, dp_group=self.train_group,
-                                  seed=int(cfg.trainer.seed), dp_rank=self.rank, dp_world=self.n_train)
-        if self.actor.ep is not None:
-            raise NotImplementedError("rollout weight sync from an expert-parallel trainer (experts are sharded "
-                                      "over the trainer ranks) is not wired yet")
-        self.layout = WeightLayout.from_dp(self.actor.dp)
+                                  seed=int(cfg.trainer.seed), dp_rank=self.dp_rank, dp_world=self.dp_world,
+                                  tp_group=self.tp_group)
+        self.assembler = None
+        if self.actor.ep is not None or self.actor.tp is not None:
+            # sharded trainer: every trainer rank publishes the full model, assembled
+            # from the shards after each optimizer step (rollout ranks pull as usual)
+            from ..models.qwen import QwenModel
+            from ..parallel.assemble import FullWeightAssembler
+            m = self.actor.model
+            self.assembler = FullWeightAssembler(
+                m, ep=self.actor.ep, tp=self.actor.tp,
+                ep_names=[n for n, _ in m.named_parameters() if "experts_w" in n] if self.actor.ep is not None else (),
+                tp_names=sorted(self.actor.tp_sharded) if self.actor.tp is not None else ())
+            with torch.device("meta"):        # parameter names and shapes of the unsharded model
+                shapes = [(n, tuple(p.shape)) for n, p in QwenModel(self.args).named_parameters()]
+            entries, off = [], 0
+            for n, shp in shapes:
+                entries.append((n, shp, off))
+                k = 1
+                for d in shp:
+                    k *= d
+                off += (k + 63) // 64 * 64          # 16-byte aligned segments
+            self.layout = WeightLayout(entries, off, self.actor.dtype)
+            self.pub_flat = torch.zeros(off, dtype=self.actor.dtype, device=self.device)
+            self.pub_views = self.layout.views(self.pub_flat)
+            self.assembler.gather()
+            self.assembler.assemble_into(self.pub_views)
+        else:
+            self.layout = WeightLayout.from_dp(self.actor.dp)
+            self.pub_flat = self.actor.dp.flat
         mode = "hbm" if (cfg.psrl.ps_mode == "hbm" and self.device.type == "cuda") else "cpu"
         self.store = WeightStore(self.layout, self.device, mode)
-        self.store.publish(self.actor.dp.flat, 0)
+        self.store.publish(self.pub_flat, 0)
         if self.device.type == "cuda":
             torch.cuda.synchronize()
         if self.rank == 0:
@@ -115,19 +156,23 @@ class DisaggregatedRun:
     def trainer_step(self) -> dict:
         b = self.global_step
         t0 = time.perf_counter()
-        batch = self.cp.get_batch(b, self.rank, self.n_train, self.buffer_timeout_s)
+        batch = self.cp.get_batch(b, self.dp_rank, self.dp_world, self.buffer_timeout_s, self.rank % self.tp_size,
+                                  self.tp_size)
         trajs, plan = batch["trajs"], batch["plan"]
         t1 = time.perf_counter()
         if not bool(self.cfg.psrl.log_prob.enable_rollout_engine_log_prob):
             self.actor.compute_log_prob(trajs, list(range(len(trajs))), field="old_logprobs")
         metrics = self.actor.update_policy(trajs, float(self.cfg.rollout.temperature), plan=plan)
+        if self.assembler is not None:
+            self.assembler.gather()                  # collective over the trainer shards
+            self.assembler.assemble_into(self.pub_views)
         t2 = time.perf_counter()
         # publish: PS exclusive lock -> every trainer writes its store -> version bump
         if self.rank == 0 and not self.cp.acquire_push(600):
             raise TimeoutError("exclusive push lock")
         if self.n_train > 1:
             dist.barrier(group=self.train_cpu_group)
-        self.store.publish(self.actor.dp.flat, b + 1)
+        self.store.publish(self.pub_flat, b + 1)
         if self.device.type == "cuda":
             torch.cuda.current_stream().synchronize()
         if self.n_train > 1:

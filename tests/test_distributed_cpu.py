@@ -249,3 +249,41 @@ def test_gloo_world2_hybrid_tensor_parallel():
     res = _run_sharded(["++actor.tensor_parallel_size=2"])
     assert res[0]["steps"] == [32, 32]
     assert abs(res[0]["engine"] - res[1]["engine"]) < 1e-6 * max(1.0, abs(res[0]["engine"]))
+
+
+def _worker_disagg_sharded(rank, world, port, q, overrides):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch
+    torch.set_num_threads(1)
+    from psrl_b200.config import load_config
+    from psrl_b200.parallel.dist import init_distributed
+    from psrl_b200.trainer.distributed import run_disaggregated
+    cfg = load_config(preset="cpu_tiny_grpo", overrides=["rollout.max_response_length=12",
+                                                         "psrl.deployment.train_ngpus=2"] + list(overrides))
+    info = init_distributed("cpu", timeout_s=120)
+    res = run_disaggregated(cfg, steps=2, warmup=0, info=info)
+    if rank == 0:
+        q.put({"steps": [m["num_trajectories"] for m in res["metrics"]], "pulls": res["sync"]["pulls"]})
+    import torch.distributed as dist
+    dist.destroy_process_group()
+
+
+def test_gloo_world3_disaggregated_tensor_parallel_trainer():
+    """Two trainer ranks at TP=2 publish the assembled full model; one rollout rank pulls it."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_disagg_sharded, args=(r, 3, port, q, ["++actor.tensor_parallel_size=2"]))
+             for r in range(3)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0, 0], codes
+    res = q.get(timeout=5)
+    assert res["steps"] == [32, 32] and res["pulls"] >= 2
