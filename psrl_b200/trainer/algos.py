@@ -257,3 +257,30 @@ def compute_advantages(estimator: str, *, scores: torch.Tensor, uids, gamma: flo
     if estimator == "gae":
         return gae_advantage(token_rewards, values, mask, gamma, lam)
     raise ValueError(f"unknown adv_estimator {estimator!r}")
+
+
+def gae_with_global_whitening(cfg, trajs, group=None) -> None:
+    """GAE on this rank's trajectories (``old_values`` set), whitened with the
+    mean and variance of all ranks' response tokens in ``group`` (one
+    all-reduce of three numbers); fills ``token_advantages`` and ``returns``."""
+    import torch.distributed as dist
+    L = max((t.response_len for t in trajs), default=1)
+    N = len(trajs)
+    rew, vals, mask = torch.zeros(N, L), torch.zeros(N, L), torch.zeros(N, L)
+    for i, t in enumerate(trajs):
+        n = t.response_len
+        mask[i, :n] = 1
+        rew[i, n - 1] = t.reward
+        vals[i, :n] = torch.tensor(t.old_values[:n])
+    adv, ret = gae_advantage(rew, vals, mask, float(cfg.algorithm.gamma), float(cfg.algorithm.lam), whiten=False)
+    st = torch.tensor([float((adv * mask).sum()), float((adv * adv * mask).sum()), float(mask.sum())],
+                      dtype=torch.float64)
+    if group is not None and dist.is_initialized():
+        dist.all_reduce(st, group=group)
+    mean = st[0] / st[2].clamp_min(1)
+    var = st[1] / st[2].clamp_min(1) - mean * mean
+    adv = ((adv - float(mean)) * float(torch.rsqrt(var.clamp_min(0) + 1e-8))) * mask
+    for i, t in enumerate(trajs):
+        n = t.response_len
+        t.token_advantages = adv[i, :n].tolist()
+        t.returns = ret[i, :n].tolist()

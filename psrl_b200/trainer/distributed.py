@@ -143,6 +143,13 @@ class DisaggregatedRun:
         else:
             self.layout = WeightLayout.from_dp(self.actor.dp)
             self.pub_flat = self.actor.dp.flat
+        self.critic = None
+        if cfg.critic.enable:
+            from dataclasses import replace as _replace
+            cargs = _replace(self.args, value_head=True, tie_word_embeddings=False)
+            self.critic = PolicyWorker(cfg, cargs, self.device, dp_group=self.train_group,
+                                       seed=int(cfg.trainer.seed) + 1, dp_rank=self.dp_rank, dp_world=self.dp_world,
+                                       tp_group=self.tp_group)
         mode = "hbm" if (cfg.psrl.ps_mode == "hbm" and self.device.type == "cuda") else "cpu"
         self.store = WeightStore(self.layout, self.device, mode)
         self.store.publish(self.pub_flat, 0)
@@ -162,7 +169,14 @@ class DisaggregatedRun:
         t1 = time.perf_counter()
         if not bool(self.cfg.psrl.log_prob.enable_rollout_engine_log_prob):
             self.actor.compute_log_prob(trajs, list(range(len(trajs))), field="old_logprobs")
+        critic_metrics = {}
+        if self.critic is not None:
+            from .algos import gae_with_global_whitening
+            self.critic.compute_values(trajs, list(range(len(trajs))))
+            gae_with_global_whitening(self.cfg, trajs, self.train_cpu_group)
+            critic_metrics = self.critic.update_critic(trajs, plan=plan)
         metrics = self.actor.update_policy(trajs, float(self.cfg.rollout.temperature), plan=plan)
+        metrics.update(critic_metrics)
         if self.assembler is not None:
             self.assembler.gather()                  # collective over the trainer shards
             self.assembler.assemble_into(self.pub_views)

@@ -281,31 +281,8 @@ class HybridRun:
         return metrics
 
     def _gae(self, trajs) -> None:
-        """GAE on this rank's trajectories, whitened with the mean and variance
-        of all ranks' response tokens (one all-reduce of three numbers)."""
-        from . import algos
-        cfg = self.cfg
-        L = max((t.response_len for t in trajs), default=1)
-        N = len(trajs)
-        rew, vals, mask = torch.zeros(N, L), torch.zeros(N, L), torch.zeros(N, L)
-        for i, t in enumerate(trajs):
-            n = t.response_len
-            mask[i, :n] = 1
-            rew[i, n - 1] = t.reward
-            vals[i, :n] = torch.tensor(t.old_values[:n])
-        adv, ret = algos.gae_advantage(rew, vals, mask, float(cfg.algorithm.gamma), float(cfg.algorithm.lam),
-                                       whiten=False)
-        st = torch.tensor([float((adv * mask).sum()), float((adv * adv * mask).sum()), float(mask.sum())],
-                          dtype=torch.float64)
-        if self.cpu_group is not None:
-            dist.all_reduce(st, group=self.cpu_group)
-        mean = st[0] / st[2].clamp_min(1)
-        var = st[1] / st[2].clamp_min(1) - mean * mean
-        adv = ((adv - float(mean)) * float(torch.rsqrt(var.clamp_min(0) + 1e-8))) * mask
-        for i, t in enumerate(trajs):
-            n = t.response_len
-            t.token_advantages = adv[i, :n].tolist()
-            t.returns = ret[i, :n].tolist()
+        from .algos import gae_with_global_whitening
+        gae_with_global_whitening(self.cfg, trajs, self.cpu_group)
 
     def close(self) -> None:
         self.stop_rollout()

@@ -287,3 +287,22 @@ def test_gloo_world3_disaggregated_tensor_parallel_trainer():
     assert codes == [0, 0, 0], codes
     res = q.get(timeout=5)
     assert res["steps"] == [32, 32] and res["pulls"] >= 2
+
+
+def test_gloo_world3_disaggregated_ppo_with_critic():
+    """PPO with a critic in the disaggregated placement (two trainer ranks, one rollout rank)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ov = ["critic.enable=true", "algorithm.adv_estimator=gae"]
+    procs = [ctx.Process(target=_worker_disagg_sharded, args=(r, 3, port, q, ov)) for r in range(3)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0, 0], codes
+    assert q.get(timeout=5)["steps"] == [32, 32]
