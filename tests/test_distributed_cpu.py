@@ -306,3 +306,16 @@ def test_gloo_world3_disaggregated_ppo_with_critic():
             p.kill()
     assert codes == [0, 0, 0], codes
     assert q.get(timeout=5)["steps"] == [32, 32]
+
+
+def test_gloo_world2_hybrid_multiturn_agentic():
+    """Multi-turn sessions (environment observations between turns, version
+    pinned at the first turn) through the control-plane process and two
+    hybrid ranks."""
+    ov = ["psrl.agentic_rl.max_turns=3", "++psrl.agentic_rl.obs_len_min=4", "++psrl.agentic_rl.obs_len_max=8",
+          "data.kind=synthetic_tokens", "data.prompt_len_min=8", "data.prompt_len_max=16",
+          "data.response_len_mu=1.5", "data.response_len_sigma=0.3", "data.response_len_cap=8",
+          "reward.kind=bernoulli_hash", "rollout.ignore_eos=true", "rollout.block_size=4",
+          "psrl.staleness_buffer_entries=4", "actor.ppo_mini_batch_size=4"]
+    res = _run_sharded(ov)
+    assert res[0]["steps"] == [16, 16]
