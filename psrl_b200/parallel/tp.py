@@ -153,3 +153,29 @@ def apply_tensor_parallel(model, tp: TPGroup) -> list[str]:
             names.append(f"layers.{i}.attn.qkv_bias")
     model.tp = tp
     return names
+
+
+@torch.no_grad()
+def shard_engine_tensors(args, tensors: dict, tp: TPGroup) -> dict:
+    """This TP rank's shard of full engine tensors (``layers.{i}.attn.qkv.weight``
+    and so on), in the layout the TP trainer's shards and a TP rollout engine
+    use; replicated tensors are shared, not copied."""
+    d, r, P = args.head_dim, tp.rank, tp.world
+    qn, kn = args.num_heads // P * d, args.num_kv_heads // P * d
+    il = args.intermediate_size // P
+    rows = torch.cat([torch.arange(r * qn, (r + 1) * qn), args.q_size + torch.arange(r * kn, (r + 1) * kn),
+                      args.q_size + args.kv_size + torch.arange(r * kn, (r + 1) * kn)])
+    out = {}
+    for n, t in tensors.items():
+        if n.endswith("attn.qkv.weight") or n.endswith("attn.qkv.bias"):
+            out[n] = t.index_select(0, rows.to(t.device)).contiguous()
+        elif n.endswith("attn.o.weight"):
+            out[n] = t[:, r * qn:(r + 1) * qn].contiguous()
+        elif n.endswith("mlp.gate_up.weight"):
+            I = args.intermediate_size
+            out[n] = torch.cat([t[r * il:(r + 1) * il], t[I + r * il:I + (r + 1) * il]]).contiguous()
+        elif n.endswith("mlp.down.weight"):
+            out[n] = t[:, r * il:(r + 1) * il].contiguous()
+        else:
+            out[n] = t
+    return out

@@ -29,6 +29,7 @@ from dataclasses import dataclass, field
 
 import numpy as np
 import torch
+import torch.distributed as dist
 import torch.nn.functional as F
 
 from .. import ops
@@ -141,7 +142,23 @@ class RolloutEngine:
                  max_model_len: int = 8192 + 1024, block_size: int = 64, max_num_batched_tokens: int = 10240,
                  kv_cache_gb: float | None = None, num_blocks: int | None = None, enable_prefix_caching: bool = True,
                  use_cuda_graph: bool = True, keep_kv_on_update: bool = False, version: int = 0,
-                 eos_token_id: int | None = None):
+                 eos_token_id: int | None = None, tp=None):
+        # tensor parallelism (``tp``: parallel.tp.TPGroup): this engine holds query heads,
+        # KV heads and MLP columns [r/P, (r+1)/P) of every layer (weights in the same
+        # layout as the TP trainer's shards) and its KV cache for its own KV heads; the
+        # O and down projections end in an all-reduce over the TP group.  Every TP rank
+        # runs the same schedule (the caller feeds them identical requests), so the
+        # replicated LM head gives identical logits and identical sampled tokens.
+        self.tp = tp
+        self.full_args = args
+        if tp is not None and tp.world > 1:
+            if args.is_moe:
+                raise ValueError("tensor-parallel rollout covers dense decoders")
+            from dataclasses import replace
+            args = replace(args, num_heads=args.num_heads // tp.world, num_kv_heads=args.num_kv_heads // tp.world,
+                           intermediate_size=args.intermediate_size // tp.world)
+        else:
+            self.tp = None
         self.args = args
         self.w = weights
         self.device = weights.device
@@ -591,11 +608,15 @@ class RolloutEngine:
                                                splits=splits if self.is_cuda else None,
                                                scratch=self.decode_scratch if self.is_cuda else None)
             attn = F.linear(o.reshape(T, a.q_size), W[pre + "attn.o.weight"])
+            if self.tp is not None:
+                dist.all_reduce(attn, group=self.tp.group)
             h2, resid = ops.rms_norm(attn, W[pre + "ln2"], a.rms_eps, residual=resid)
             if a.is_moe:
                 x = self._moe(h2, pre)
             else:
                 x = F.linear(ops.swiglu(F.linear(h2, W[pre + "mlp.gate_up.weight"])), W[pre + "mlp.down.weight"])
+                if self.tp is not None:
+                    dist.all_reduce(x, group=self.tp.group)
         hN, _ = ops.rms_norm(x, W["norm"], a.rms_eps, residual=resid)
         return hN
 

@@ -108,7 +108,23 @@ class HybridRun:
         self.actor = PolicyWorker(cfg, self.args, self.device, dp_group=dp_group, seed=seed,
                                   dp_rank=self.dp_rank, dp_world=self.dp_world, tp_group=tp_group)
         self.assembler = None
-        if self.actor.ep is not None or self.actor.tp is not None:
+        # rollout TP equal to the trainer's: each engine holds the same shards as its trainer
+        rtp = int(cfg.rollout.get("tensor_parallel_size", 1) or 1)
+        self.eng_tp = None
+        if rtp > 1:
+            if self.actor.tp is None or rtp != tp or self.actor.ep is not None:
+                raise ValueError("rollout.tensor_parallel_size > 1 needs the same actor.tensor_parallel_size")
+            from ..parallel.tp import make_tp_group
+            k = self.dp_rank
+            ranks = list(range(k * tp, (k + 1) * tp))
+            # separate communicators: the engine's all-reduces run on the rollout thread
+            eng_groups = [dist.new_group(list(range(j * tp, (j + 1) * tp))) for j in range(self.dp_world)]
+            cpu_groups = [dist.new_group(list(range(j * tp, (j + 1) * tp)), backend="gloo")
+                          for j in range(self.dp_world)]
+            self.eng_tp = make_tp_group(eng_groups[k])
+            self.eng_tp_cpu = cpu_groups[k]
+            self.eng_leader = ranks[0]
+        elif self.actor.ep is not None or self.actor.tp is not None:
             # the engine holds the full model; sharded weights are all-gathered after each step
             from ..parallel.assemble import FullWeightAssembler
             self.assembler = FullWeightAssembler(
@@ -126,7 +142,20 @@ class HybridRun:
         if cfg.actor.use_kl_loss:
             self.ref = PolicyWorker(cfg, self.args, self.device, seed=seed, trainable=False)
         self.wlock = RWLock()
-        if self.assembler is None:
+        self.eng_sources = None
+        if self.eng_tp is not None:
+            # engine weights: copies of this rank's trainer shards (engine names)
+            from ..parallel.assemble import engine_name
+            w = EngineWeights(self.args, self.device, self.actor.dtype)
+            self.eng_sources = []
+            for n, p in self.actor.model.named_parameters():
+                t = p.detach().clone()
+                w.tensors[engine_name(n)] = t
+                self.eng_sources.append((t, p))
+            for name, b in self.actor.model.named_buffers():
+                w.tensors[name] = b.to(self.device)
+            self.eng_flat = None
+        elif self.assembler is None:
             # engine weights: one flat copy in the trainer's flat layout (a pull is one copy)
             layout = WeightLayout.from_dp(self.actor.dp)
             self.eng_flat = self.actor.dp.flat.detach().clone()
@@ -153,12 +182,15 @@ class HybridRun:
             max_num_batched_tokens=int(rc.max_num_batched_tokens), kv_cache_gb=float(rc.get("kv_cache_gb", 4.0)),
             enable_prefix_caching=bool(rc.enable_prefix_caching), use_cuda_graph=bool(rc.cuda_graph),
             keep_kv_on_update=bool(cfg.psrl.rollout_coordination.partial_rollout.get("keep_kv", False)),
-            eos_token_id=None if rc.ignore_eos else self.cp.eos_id())
+            eos_token_id=None if rc.ignore_eos else self.cp.eos_id(), tp=self.eng_tp)
         sm = cfg.psrl.rollout_coordination.sync_and_mig_strategy
         self.policy = SyncPolicy(sm.method, bool(cfg.psrl.rollout_coordination.partial_rollout.enable),
                                  sm.sync.get("threshold"), sm.sync.get("indicator", "request_num"))
-        self.instance_id = (self.rank, 0)
-        self.cp.register_instance(self.instance_id, self.engine.version)
+        # one rollout instance per engine; a TP engine's instance is its leader's
+        self.is_leader = self.eng_tp is None or self.rank == self.eng_leader
+        self.instance_id = (self.rank if self.eng_tp is None else self.eng_leader, 0)
+        if self.is_leader:
+            self.cp.register_instance(self.instance_id, self.engine.version)
         self.rollout_stream = torch.cuda.Stream(device=self.device, priority=-1) if self.is_cuda else None
         self.train_stream = trainer_stream_for(cfg, self.device, self.is_cuda)
         _apply_switch_interval(cfg)
@@ -171,12 +203,18 @@ class HybridRun:
         log(f"hybrid rank ready: trainer dp{self.world} + rollout instance {self.instance_id}")
 
     # -------------------------------------------------------------- rollout
-    def _pull(self) -> None:
+    def _pull(self, v: int | None = None) -> None:
+        """Refresh the engine from the local trainer.  ``v``: the version a TP
+        leader already read (followers take it from the leader's broadcast)."""
         t0 = time.perf_counter()
         with self.wlock.shared(600):
             # the PS version is read first: the local parameters are at least that new
-            v = self.cp_roll.pull_model(self.instance_id)
-            if self.assembler is None:
+            if v is None:
+                v = self.cp_roll.pull_model(self.instance_id)
+            if self.eng_sources is not None:
+                for t, p in self.eng_sources:
+                    t.copy_(p.detach(), non_blocking=True)
+            elif self.assembler is None:
                 self.eng_flat.copy_(self.actor.dp.flat, non_blocking=True)
             else:
                 self.assembler.assemble_into(self.engine_weights.tensors)
@@ -186,9 +224,55 @@ class HybridRun:
         dt = time.perf_counter() - t0
         self.pulls += 1
         self.pull_s += dt
-        self.cp_roll.report_pull(dt)
+        if self.is_leader:
+            self.cp_roll.report_pull(dt)
+
+    def _tp_rollout_loop(self) -> None:
+        """TP engine: the leader talks to the control plane and broadcasts each
+        round's requests, aborts, weight version and stop flag to its followers,
+        so every TP rank applies identical operations and steps in lockstep."""
+        eng = self.engine
+        mb = self.mailbox
+        leader = self.is_leader
+        try:
+            ctx = torch.cuda.stream(self.rollout_stream) if self.is_cuda else contextlib.nullcontext()
+            with ctx:
+                while True:
+                    msg = None
+                    if leader:
+                        reqs, aborts = mb.collect()
+                        v = None
+                        if self.policy.should_sync(eng, mb.ps_version):
+                            v = self.cp_roll.pull_model(self.instance_id)
+                        msg = (reqs, aborts, v, bool(self._stop))
+                    box = [msg]
+                    dist.broadcast_object_list(box, src=self.eng_leader, group=self.eng_tp_cpu)
+                    reqs, aborts, v, stop = box[0]
+                    if stop:
+                        break
+                    for r in reqs:
+                        eng.add_request(r)
+                    for rid in aborts:
+                        eng.abort(rid)
+                    if v is not None:
+                        self._pull(v)
+                    if eng.has_unfinished():
+                        outs = eng.step()
+                        if outs and leader:
+                            mb.post(outs)
+                    else:
+                        if leader:
+                            mb.kick()
+                        time.sleep(0.0005)
+        except BaseException as exc:
+            self._rollout_error = exc
+            if leader:
+                with contextlib.suppress(Exception):
+                    self.cp_roll.report_failure(self.instance_id, f"{type(exc).__name__}: {exc}")
 
     def _rollout_loop(self) -> None:
+        if self.eng_tp is not None:
+            return self._tp_rollout_loop()
         eng = self.engine
         mb = self.mailbox
         try:
@@ -218,7 +302,8 @@ class HybridRun:
         if self._thread is None:
             import threading
             self._stop = False
-            self.mailbox = ExchangeMailbox(self.cp_roll, self.instance_id, self.engine)
+            if self.is_leader:
+                self.mailbox = ExchangeMailbox(self.cp_roll, self.instance_id, self.engine)
             self._thread = threading.Thread(target=self._rollout_loop, daemon=True, name="rollout")
             self._thread.start()
 

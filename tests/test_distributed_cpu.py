@@ -319,3 +319,11 @@ def test_gloo_world2_hybrid_multiturn_agentic():
           "psrl.staleness_buffer_entries=4", "actor.ppo_mini_batch_size=4"]
     res = _run_sharded(ov)
     assert res[0]["steps"] == [16, 16]
+
+
+def test_gloo_world2_hybrid_tensor_parallel_rollout():
+    """Trainer and rollout engine both at TP=2 over the same two ranks: the
+    engine keeps the trainer's shards, the leader feeds both ranks the same
+    schedule."""
+    res = _run_sharded(["++actor.tensor_parallel_size=2", "++rollout.tensor_parallel_size=2"])
+    assert res[0]["steps"] == [32, 32]

@@ -152,3 +152,58 @@ def test_full_weight_assembly_from_tp_and_ep_shards():
     for _ in range(2):
         w = q.get(timeout=5)
         assert w["tiny"] == 0.0 and w["tiny-moe"] == 0.0, w
+
+
+def _engine_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch
+    import torch.distributed as dist
+    torch.set_num_threads(1)
+    from psrl_b200.models import PRESETS, build_model
+    from psrl_b200.parallel.dist import init_distributed
+    from psrl_b200.parallel.tp import make_tp_group, shard_engine_tensors
+    from psrl_b200.rollout.engine import EngineWeights, GenRequest, RolloutEngine, SamplingParams
+    init_distributed("cpu", timeout_s=120)
+    a = PRESETS["tiny"]
+    full = EngineWeights.from_model(build_model(a, "cpu", torch.float32, seed=4), "cpu", torch.float32)
+    tp = make_tp_group(dist.group.WORLD)
+    shard = EngineWeights(a, "cpu", torch.float32)
+    shard.tensors = shard_engine_tensors(a, full.tensors, tp)
+
+    def run(w, tpg):
+        eng = RolloutEngine(a, w, max_num_seqs=4, max_model_len=128, block_size=16, kv_cache_gb=0.05,
+                            use_cuda_graph=False, enable_prefix_caching=False, tp=tpg)
+        for i in range(3):
+            eng.add_request(GenRequest(i, list(range(5, 20 + 3 * i)), SamplingParams(temperature=0.0, max_tokens=10,
+                                                                                     ignore_eos=True, seed=i)))
+        outs = {}
+        while eng.has_unfinished():
+            for o in eng.step():
+                outs[o.request_id] = (list(o.output_ids), list(o.logprobs))
+        return outs
+
+    ref = run(full, None)
+    got = run(shard, tp)
+    same = all(ref[i][0] == got[i][0] for i in ref)
+    lp = max(abs(x - y) for i in ref for x, y in zip(ref[i][1], got[i][1]))
+    q.put({"rank": rank, "same_tokens": same, "lp_diff": lp})
+    dist.destroy_process_group()
+
+
+def test_tensor_parallel_rollout_engine_matches_single_rank():
+    """A TP=2 rollout engine (two gloo ranks, identical request streams) decodes
+    the same greedy tokens and log-probs as the unsharded engine."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_engine_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(240)
+    assert [p.exitcode for p in procs] == [0, 0]
+    for _ in range(2):
+        r = q.get(timeout=5)
+        assert r["same_tokens"], r
+        assert r["lp_diff"] < 1e-4, r
