@@ -105,7 +105,21 @@ def run_colocated(args) -> dict:
         "ms": ms, "wall_s": wall, "tokens": tokens, "launches": _ext.launches() - l0, "clocks": clocks,
         "h2d": (b1 - b0) / args.steps, "d2h": (o1 - o0) / args.steps, "metrics": metrics,
         "global_batch": cfg.psrl.staleness_buffer_entries * cfg.psrl.rollout_n, "parallelism": "colocated-1gpu",
+        "sync": {"pulls": int(t.instance.sync_count), "pull_s": float(t.instance.sync_time),
+                 "path": "in-HBM copy trainer -> engine weights (same GPU)"},
     }
+
+
+def _sync_summary(res: dict) -> dict | None:
+    """Weight-sync latency over the whole run (warm-up included): the rollout
+    side's wall time per pull of a new version."""
+    sync = res.get("sync") or (res.get("cp") or {}).get("sync")
+    if not sync or not sync.get("pulls"):
+        return None
+    out = {"pulls": int(sync["pulls"]), "mean_ms": round(1000.0 * float(sync["pull_s"]) / int(sync["pulls"]), 2)}
+    out["path"] = sync.get("path", "NVLink peer loads from the trainers' HBM stores" if "n_train" in res
+                           else "in-HBM copy from the local trainer replica")
+    return out
 
 
 def main():
@@ -176,6 +190,7 @@ def main():
         "e2e": {"value": round(e2e, 1), "unit": "trained tokens/s (wall clock, public API RLTrainer.step)",
                 "h2d_bytes_per_step": int(res["h2d"]), "d2h_bytes_per_step": int(res["d2h"])},
         "gpu_launches": int(res["launches"]),
+        "weight_sync": _sync_summary(res),
     }
     print(json.dumps(line), flush=True)
 
