@@ -116,8 +116,10 @@ def save_hf(model, path: str, max_shard_bytes: int = 5 << 30) -> list[str]:
     """Write ``config.json`` + safetensors shards (+ index) in HF format."""
     from safetensors.torch import save_file
 
-    if any(getattr(getattr(layer, "mlp", None), "ep", None) is not None for layer in model.layers):
-        raise NotImplementedError("HF export of an expert-parallel model needs its experts gathered first")
+    if getattr(model, "tp", None) is not None or \
+            any(getattr(getattr(layer, "mlp", None), "ep", None) is not None for layer in model.layers):
+        raise ValueError("save_hf needs the unsharded model: save a TP / EP worker through "
+                         "utils.checkpoint.save_worker, which assembles the shards")
     os.makedirs(path, exist_ok=True)
     a: ModelArgs = model.args
     state = {k: v.detach().to("cpu").contiguous() for k, v in model.state_dict().items()}

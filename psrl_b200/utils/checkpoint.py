@@ -30,9 +30,53 @@ def step_dir(root: str, step: int) -> str:
     return os.path.join(os.path.expanduser(root), f"global_step_{step}")
 
 
+def _is_sharded(worker) -> bool:
+    return getattr(worker, "tp", None) is not None or getattr(worker, "ep", None) is not None
+
+
+def _full_model_from_shards(worker):
+    """The unsharded model (CPU, fp32) assembled from a TP / EP worker's shards;
+    a collective over the worker's TP / EP groups (every rank calls it)."""
+    from ..models.qwen import QwenModel
+    from ..parallel.assemble import FullWeightAssembler
+    m = worker.model
+    asm = FullWeightAssembler(
+        m, ep=worker.ep, tp=worker.tp,
+        ep_names=[n for n, _ in m.named_parameters() if "experts_w" in n] if worker.ep is not None else (),
+        tp_names=sorted(worker.tp_sharded) if worker.tp is not None else ())
+    full = QwenModel(worker.args)
+    asm.gather()
+    tensors = {n: p.data for n, p in full.named_parameters()}
+    asm.assemble_into(tensors)
+    return full
+
+
+def _shard_into(worker, full) -> None:
+    """Copy this rank's shards of an unsharded model into a TP / EP worker."""
+    fp = {n: p.detach() for n, p in full.named_parameters()}
+    if worker.tp is not None:
+        from ..parallel.assemble import engine_name
+        from ..parallel.tp import shard_engine_tensors
+        fp = shard_engine_tensors(worker.args, fp, worker.tp)
+    with torch.no_grad():
+        for n, p in worker.model.named_parameters():
+            src = fp[engine_name(n)] if worker.tp is not None else fp[n]
+            if worker.ep is not None and "experts_w" in n:
+                src = src[worker.ep.first: worker.ep.first + worker.ep.local]
+            p.copy_(src.to(p.dtype))
+
+
 def save_worker(worker, path: str, rank: int = 0, use_dcp: bool = False) -> None:
     os.makedirs(path, exist_ok=True)
-    if rank == 0:
+    if _is_sharded(worker):
+        # HF export of the whole model, assembled from the TP / EP shards (collective)
+        full = _full_model_from_shards(worker)
+        if rank == 0:
+            save_hf(full, path)
+        partner = getattr(worker, "dp_partner", None)
+        if partner is not None:
+            torch.save(partner.optimizer_state(), os.path.join(path, f"optim_partner_rank{rank}.pt"))
+    elif rank == 0:
         save_hf(worker.model, path)
     if use_dcp:
         import torch.distributed.checkpoint as dcp
@@ -47,6 +91,11 @@ def load_worker(worker, path: str, rank: int = 0, use_dcp: bool = False) -> None
         import torch.distributed.checkpoint as dcp
         sd = {k: v.detach() for k, v in worker.model.state_dict().items()}
         dcp.load(sd, checkpoint_id=os.path.join(path, "dcp"))
+    elif _is_sharded(worker):
+        from ..models.qwen import QwenModel
+        full = QwenModel(worker.args)
+        load_hf_into(full, path)
+        _shard_into(worker, full)
     else:
         load_hf_into(worker.model, path)
     opt = os.path.join(path, f"optim_rank{rank}.pt")
@@ -55,6 +104,13 @@ def load_worker(worker, path: str, rank: int = 0, use_dcp: bool = False) -> None
             worker.dp.load_optimizer_state(torch.load(opt, map_location="cpu", weights_only=False))
         else:
             worker.dp.sync_master_from_params()
+    partner = getattr(worker, "dp_partner", None)
+    if partner is not None:
+        popt = os.path.join(path, f"optim_partner_rank{rank}.pt")
+        if os.path.exists(popt):
+            partner.load_optimizer_state(torch.load(popt, map_location="cpu", weights_only=False))
+        else:
+            partner.sync_master_from_params()
 
 
 def save_checkpoint(root: str, step: int, actor, data=None, critic=None, ps_version: int | None = None,

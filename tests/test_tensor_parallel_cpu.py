@@ -207,3 +207,59 @@ def test_tensor_parallel_rollout_engine_matches_single_rank():
         r = q.get(timeout=5)
         assert r["same_tokens"], r
         assert r["lp_diff"] < 1e-4, r
+
+
+def _ckpt_worker(rank, world, port, q, path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch
+    import torch.distributed as dist
+    torch.set_num_threads(1)
+    from psrl_b200.config import load_config
+    from psrl_b200.models import PRESETS, build_model
+    from psrl_b200.models.hf_io import load_hf_into
+    from psrl_b200.parallel.dist import init_distributed
+    from psrl_b200.trainer.actor import PolicyWorker
+    from psrl_b200.utils.checkpoint import load_worker, save_worker
+    init_distributed("cpu", timeout_s=120)
+    out = {"rank": rank}
+    for preset, kw in (("tiny", {"tp_group": dist.group.WORLD}),
+                       ("tiny-moe", {"dp_group": dist.group.WORLD, "dp_rank": rank, "dp_world": world})):
+        a = PRESETS[preset]
+        cfg = load_config(preset="cpu_tiny_grpo", overrides=[f"model.preset={preset}",
+                                                             "++actor.expert_parallel_size=2"])
+        d = os.path.join(path, preset)
+        w = PolicyWorker(cfg, a, "cpu", seed=21, **kw)
+        save_worker(w, d, rank)
+        dist.barrier()
+        # the HF export is the unsharded model
+        full = build_model(a, "cpu", torch.float32, seed=0)
+        load_hf_into(full, d)
+        ref = build_model(a, "cpu", torch.float32, seed=21)
+        rp = dict(ref.named_parameters())
+        out[preset + "_hf"] = max(float((p.detach() - rp[n].detach()).abs().max()) for n, p in full.named_parameters())
+        # a differently initialised sharded worker reloads the same shards
+        w2 = PolicyWorker(cfg, a, "cpu", seed=99, **kw)
+        load_worker(w2, d, rank)
+        p1 = dict(w.model.named_parameters())
+        out[preset + "_reload"] = max(float((p.detach() - p1[n].detach()).abs().max())
+                                      for n, p in w2.model.named_parameters())
+    q.put(out)
+    dist.destroy_process_group()
+
+
+def test_sharded_worker_checkpoint_roundtrip(tmp_path):
+    """TP and EP workers export the full model in HF format and reload their shards."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ckpt_worker, args=(r, 2, port, q, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(240)
+    assert [p.exitcode for p in procs] == [0, 0]
+    for _ in range(2):
+        r = q.get(timeout=5)
+        for k in ("tiny_hf", "tiny_reload", "tiny-moe_hf", "tiny-moe_reload"):
+            assert r[k] == 0.0, r
