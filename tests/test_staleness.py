@@ -208,3 +208,10 @@ def test_protocol_simulation_progresses(staleness):
        extra=st.integers(0, 2))
 def test_protocol_simulation_property(seed, staleness, ready, extra):
     _simulate(seed, staleness, ready + extra, ready, steps=250)
+
+
+def test_reservation_exchange_with_parked_spare_entry():
+    """Regression: a wasted redundant rollout parked in a spare slot sits behind
+    the EMPTY slots; reservations and reservation exchanges must take the last
+    EMPTY slot, not the parked entry."""
+    assert _simulate(477, 3, 3, 1, steps=250) > 0
