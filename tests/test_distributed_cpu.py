@@ -25,7 +25,7 @@ def _worker(rank, world, port, q):
     from psrl_b200.parallel.dist import init_distributed
     from psrl_b200.trainer.distributed import run_disaggregated
     cfg = load_config(preset="cpu_tiny_grpo")
-    info = init_distributed("cpu", timeout_s=120)
+    info = init_distributed("cpu", timeout_s=300)
     res = run_disaggregated(cfg, steps=4, warmup=0, info=info)
     if rank == 0:
         q.put({k: res[k] for k in ("tokens", "sync", "manager", "n_train", "world")} |
@@ -42,7 +42,7 @@ def test_gloo_world2_plumbing():
     for p in procs:
         p.start()
     for p in procs:
-        p.join(300)
+        p.join(900)
     codes = [p.exitcode for p in procs]
     for p in procs:
         if p.is_alive():
@@ -65,7 +65,7 @@ def _worker4(rank, world, port, q):
     from psrl_b200.trainer.distributed import run_disaggregated
     cfg = load_config(preset="cpu_tiny_grpo", overrides=["rollout.max_response_length=12",
                                                          "psrl.deployment.train_ngpus=2"])
-    info = init_distributed("cpu", timeout_s=120)
+    info = init_distributed("cpu", timeout_s=300)
     res = run_disaggregated(cfg, steps=2, warmup=1, info=info)
     if rank == 0:
         q.put({"n_train": res["n_train"], "steps": [m["num_trajectories"] for m in res["metrics"]],
@@ -82,7 +82,7 @@ def test_gloo_world4_two_trainers_two_rollouts():
     for p in procs:
         p.start()
     for p in procs:
-        p.join(300)
+        p.join(900)
     codes = [p.exitcode for p in procs]
     for p in procs:
         if p.is_alive():
@@ -104,7 +104,7 @@ def _worker_hybrid(rank, world, port, q):
     from psrl_b200.parallel.dist import init_distributed
     from psrl_b200.trainer.hybrid import run_hybrid
     cfg = load_config(preset="cpu_tiny_grpo", overrides=["rollout.max_response_length=12"])
-    info = init_distributed("cpu", timeout_s=120)
+    info = init_distributed("cpu", timeout_s=300)
     res = run_hybrid(cfg, steps=2, warmup=1, info=info)
     q.put({"rank": rank, "checksum": res["param_checksum"]})
     if rank == 0:
@@ -124,7 +124,7 @@ def test_gloo_world2_hybrid_placement():
     for p in procs:
         p.start()
     for p in procs:
-        p.join(300)
+        p.join(900)
     codes = [p.exitcode for p in procs]
     for p in procs:
         if p.is_alive():
@@ -148,7 +148,7 @@ def test_gloo_world4_hybrid_placement():
     for p in procs:
         p.start()
     for p in procs:
-        p.join(300)
+        p.join(900)
     codes = [p.exitcode for p in procs]
     for p in procs:
         if p.is_alive():
@@ -171,7 +171,7 @@ def _worker_hybrid_ppo(rank, world, port, q):
     from psrl_b200.trainer.hybrid import run_hybrid
     cfg = load_config(preset="cpu_tiny_grpo", overrides=["rollout.max_response_length=12", "critic.enable=true",
                                                          "algorithm.adv_estimator=gae"])
-    info = init_distributed("cpu", timeout_s=120)
+    info = init_distributed("cpu", timeout_s=300)
     res = run_hybrid(cfg, steps=2, warmup=0, info=info)
     if rank == 0:
         q.put({"steps": [m["num_trajectories"] for m in res["metrics"]],
@@ -190,7 +190,7 @@ def test_gloo_world2_hybrid_ppo_with_critic():
     for p in procs:
         p.start()
     for p in procs:
-        p.join(300)
+        p.join(900)
     codes = [p.exitcode for p in procs]
     for p in procs:
         if p.is_alive():
@@ -210,7 +210,7 @@ def _worker_hybrid_sharded(rank, world, port, q, overrides):
     from psrl_b200.parallel.dist import init_distributed
     from psrl_b200.trainer.hybrid import run_hybrid
     cfg = load_config(preset="cpu_tiny_grpo", overrides=["rollout.max_response_length=12"] + list(overrides))
-    info = init_distributed("cpu", timeout_s=120)
+    info = init_distributed("cpu", timeout_s=300)
     res = run_hybrid(cfg, steps=2, warmup=0, info=info)
     q.put({"rank": rank, "engine": res["engine_checksum"], "tokens": res["tokens"],
            "steps": [m["num_trajectories"] for m in res["metrics"]] if rank == 0 else None})
@@ -226,7 +226,7 @@ def _run_sharded(overrides):
     for p in procs:
         p.start()
     for p in procs:
-        p.join(300)
+        p.join(900)
     codes = [p.exitcode for p in procs]
     for p in procs:
         if p.is_alive():
@@ -261,7 +261,7 @@ def _worker_disagg_sharded(rank, world, port, q, overrides):
     from psrl_b200.trainer.distributed import run_disaggregated
     cfg = load_config(preset="cpu_tiny_grpo", overrides=["rollout.max_response_length=12",
                                                          "psrl.deployment.train_ngpus=2"] + list(overrides))
-    info = init_distributed("cpu", timeout_s=120)
+    info = init_distributed("cpu", timeout_s=300)
     res = run_disaggregated(cfg, steps=2, warmup=0, info=info)
     if rank == 0:
         q.put({"steps": [m["num_trajectories"] for m in res["metrics"]], "pulls": res["sync"]["pulls"]})
@@ -279,7 +279,7 @@ def test_gloo_world3_disaggregated_tensor_parallel_trainer():
     for p in procs:
         p.start()
     for p in procs:
-        p.join(300)
+        p.join(900)
     codes = [p.exitcode for p in procs]
     for p in procs:
         if p.is_alive():
@@ -299,7 +299,7 @@ def test_gloo_world3_disaggregated_ppo_with_critic():
     for p in procs:
         p.start()
     for p in procs:
-        p.join(300)
+        p.join(900)
     codes = [p.exitcode for p in procs]
     for p in procs:
         if p.is_alive():

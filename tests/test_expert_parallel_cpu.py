@@ -23,7 +23,7 @@ def _worker(rank, world, port, q):
     from psrl_b200.models import PRESETS, build_model, packed_positions
     from psrl_b200.parallel.dist import init_distributed
     from psrl_b200.parallel.ep import make_ep_group, shard_experts
-    init_distributed("cpu", timeout_s=120)
+    init_distributed("cpu", timeout_s=300)
     a = PRESETS["tiny-moe"]
     ref = build_model(a, "cpu", torch.float32, seed=5)
     epm = build_model(a, "cpu", torch.float32, seed=5)
@@ -76,7 +76,7 @@ def test_expert_parallel_matches_unsharded_moe():
     for p in procs:
         p.start()
     for p in procs:
-        p.join(240)
+        p.join(900)
     codes = [p.exitcode for p in procs]
     for p in procs:
         if p.is_alive():

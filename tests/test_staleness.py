@@ -203,7 +203,7 @@ def test_protocol_simulation_progresses(staleness):
     assert consumed > 10
 
 
-@settings(max_examples=60, deadline=None)
+@settings(max_examples=60, deadline=None, derandomize=True)
 @given(seed=st.integers(0, 10_000), staleness=st.integers(0, 4), ready=st.integers(1, 6),
        extra=st.integers(0, 2))
 def test_protocol_simulation_property(seed, staleness, ready, extra):

@@ -24,7 +24,7 @@ def _worker(rank, world, port, q):
     from psrl_b200.models import PRESETS, packed_positions
     from psrl_b200.parallel.dist import init_distributed
     from psrl_b200.trainer.actor import PolicyWorker
-    init_distributed("cpu", timeout_s=120)
+    init_distributed("cpu", timeout_s=300)
     a = PRESETS["tiny"]
     cfg = load_config(preset="cpu_tiny_grpo", overrides=["actor.optim.lr=1e-2"])
     ref = PolicyWorker(cfg, a, "cpu", seed=3)                                     # unsharded, single rank
@@ -88,7 +88,7 @@ def test_tensor_parallel_matches_unsharded_decoder():
     for p in procs:
         p.start()
     for p in procs:
-        p.join(240)
+        p.join(900)
     codes = [p.exitcode for p in procs]
     for p in procs:
         if p.is_alive():
@@ -116,7 +116,7 @@ def _assemble_worker(rank, world, port, q):
     from psrl_b200.parallel.dist import init_distributed
     from psrl_b200.rollout.engine import EngineWeights
     from psrl_b200.trainer.actor import PolicyWorker
-    init_distributed("cpu", timeout_s=120)
+    init_distributed("cpu", timeout_s=300)
     worst = {}
     for preset, kw in (("tiny", {"tp_group": dist.group.WORLD}),
                        ("tiny-moe", {"dp_group": dist.group.WORLD, "dp_rank": rank, "dp_world": world})):
@@ -147,7 +147,7 @@ def test_full_weight_assembly_from_tp_and_ep_shards():
     for p in procs:
         p.start()
     for p in procs:
-        p.join(240)
+        p.join(900)
     assert [p.exitcode for p in procs] == [0, 0]
     for _ in range(2):
         w = q.get(timeout=5)
@@ -164,7 +164,7 @@ def _engine_worker(rank, world, port, q):
     from psrl_b200.parallel.dist import init_distributed
     from psrl_b200.parallel.tp import make_tp_group, shard_engine_tensors
     from psrl_b200.rollout.engine import EngineWeights, GenRequest, RolloutEngine, SamplingParams
-    init_distributed("cpu", timeout_s=120)
+    init_distributed("cpu", timeout_s=300)
     a = PRESETS["tiny"]
     full = EngineWeights.from_model(build_model(a, "cpu", torch.float32, seed=4), "cpu", torch.float32)
     tp = make_tp_group(dist.group.WORLD)
@@ -201,7 +201,7 @@ def test_tensor_parallel_rollout_engine_matches_single_rank():
     for p in procs:
         p.start()
     for p in procs:
-        p.join(240)
+        p.join(900)
     assert [p.exitcode for p in procs] == [0, 0]
     for _ in range(2):
         r = q.get(timeout=5)
@@ -221,7 +221,7 @@ def _ckpt_worker(rank, world, port, q, path):
     from psrl_b200.parallel.dist import init_distributed
     from psrl_b200.trainer.actor import PolicyWorker
     from psrl_b200.utils.checkpoint import load_worker, save_worker
-    init_distributed("cpu", timeout_s=120)
+    init_distributed("cpu", timeout_s=300)
     out = {"rank": rank}
     for preset, kw in (("tiny", {"tp_group": dist.group.WORLD}),
                        ("tiny-moe", {"dp_group": dist.group.WORLD, "dp_rank": rank, "dp_world": world})):
@@ -257,7 +257,7 @@ def test_sharded_worker_checkpoint_roundtrip(tmp_path):
     for p in procs:
         p.start()
     for p in procs:
-        p.join(240)
+        p.join(900)
     assert [p.exitcode for p in procs] == [0, 0]
     for _ in range(2):
         r = q.get(timeout=5)
