@@ -54,7 +54,8 @@ class PrefixIndex:
     (native: ``csrc_host/router_core.cpp``)."""
 
     def __init__(self, block_size: int = 16, max_entries: int = 1 << 16):
-        from .. import _router
+        from ..native import router as _native_router
+        _router = _native_router()
         self.bs = block_size
         self._ix = _router.PrefixIndex(block_size, max_entries)
 
@@ -137,7 +138,8 @@ class Router:
     # -------------------------------------------------------------- policy
     def pick(self, req, cands: list[InstanceState]) -> InstanceState:
         """Policy choice among admitted candidates (native core except ``random``)."""
-        from .. import _router
+        from ..native import router as _native_router
+        _router = _native_router()
         m = self.method
         if m == "random":
             return self.rng.choice(cands)

@@ -278,7 +278,8 @@ def test_native_router_core_prefix_and_policies():
 
     import numpy as np
 
-    from psrl_b200 import _router
+    from psrl_b200.native import router
+    _router = router()
     ix = _router.PrefixIndex(4, 3)
     ix.insert(np.arange(8))                    # 2 blocks
     assert ix.match(np.arange(12)) == 8 and ix.match(np.array([9, 9, 9, 9])) == 0
