@@ -24,6 +24,8 @@
 // TMA loads here are plain (no cluster multicast): A/B are local tensors.
 #include <cuda.h>
 
+#include "driver_api.h"
+
 #include "common.cuh"
 
 namespace psrl {
@@ -439,7 +441,7 @@ static CUtensorMap make_tmap(const at::Tensor& t, uint32_t box_rows) {
   cuuint64_t strides[1] = {(cuuint64_t)t.stride(0) * 2};
   cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = cuTensorMapEncodeTiled(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, t.data_ptr(), dims, strides, box, estr,
+  CUresult r = PSRL_DRV(cuTensorMapEncodeTiled)(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, t.data_ptr(), dims, strides, box, estr,
                                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (", (int)r, ")");

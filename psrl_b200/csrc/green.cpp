@@ -14,6 +14,8 @@
 // groups plus the split's remainder, and returns a stream of that context.
 // Contexts and streams live until process exit.
 #include <cuda.h>
+
+#include "driver_api.h"
 #include <pybind11/pybind11.h>
 #include <torch/extension.h>
 
@@ -36,7 +38,7 @@ std::vector<Partition> g_parts;   // kept alive until exit
 void check(CUresult r, const char* what) {
   if (r != CUDA_SUCCESS) {
     const char* msg = nullptr;
-    cuGetErrorString(r, &msg);
+    PSRL_DRV(cuGetErrorString)(r, &msg);
     TORCH_CHECK(false, what, " failed: ", msg ? msg : "unknown", " (", (int)r, ")");
   }
 }
@@ -45,18 +47,18 @@ void check(CUresult r, const char* what) {
 py::dict green_partition(int64_t device, int64_t reserve_sms, int64_t priority) {
   std::lock_guard<std::mutex> lk(g_mu);
   CUdevice dev;
-  check(cuDeviceGet(&dev, (int)device), "cuDeviceGet");
+  check(PSRL_DRV(cuDeviceGet)(&dev, (int)device), "cuDeviceGet");
   CUdevResource all;
-  check(cuDeviceGetDevResource(dev, &all, CU_DEV_RESOURCE_TYPE_SM), "cuDeviceGetDevResource");
+  check(PSRL_DRV(cuDeviceGetDevResource)(dev, &all, CU_DEV_RESOURCE_TYPE_SM), "cuDeviceGetDevResource");
   const unsigned total = all.sm.smCount;
   TORCH_CHECK(reserve_sms > 0 && (unsigned)reserve_sms < total, "reserve_sms must be in (0, ", total, ")");
   // groups of 8 SMs (the split's alignment on this architecture)
   unsigned n = 0;
-  check(cuDevSmResourceSplitByCount(nullptr, &n, &all, nullptr, 0, 8), "cuDevSmResourceSplitByCount(query)");
+  check(PSRL_DRV(cuDevSmResourceSplitByCount)(nullptr, &n, &all, nullptr, 0, 8), "cuDevSmResourceSplitByCount(query)");
   TORCH_CHECK(n >= 2, "cannot split the SMs into groups");
   std::vector<CUdevResource> groups(n);
   CUdevResource rest{};
-  check(cuDevSmResourceSplitByCount(groups.data(), &n, &all, &rest, 0, 8), "cuDevSmResourceSplitByCount");
+  check(PSRL_DRV(cuDevSmResourceSplitByCount)(groups.data(), &n, &all, &rest, 0, 8), "cuDevSmResourceSplitByCount");
   unsigned reserved = 0, k = 0;
   while (k < n && reserved < (unsigned)reserve_sms) reserved += groups[k++].sm.smCount;
   TORCH_CHECK(k < n, "reserve_sms leaves no SM group for the trainer");
@@ -65,10 +67,10 @@ py::dict green_partition(int64_t device, int64_t reserve_sms, int64_t priority) 
   unsigned sms = 0;
   for (auto& g : mine) sms += g.sm.smCount;
   CUdevResourceDesc desc;
-  check(cuDevResourceGenerateDesc(&desc, mine.data(), (unsigned)mine.size()), "cuDevResourceGenerateDesc");
+  check(PSRL_DRV(cuDevResourceGenerateDesc)(&desc, mine.data(), (unsigned)mine.size()), "cuDevResourceGenerateDesc");
   Partition p;
-  check(cuGreenCtxCreate(&p.gctx, desc, dev, CU_GREEN_CTX_DEFAULT_STREAM), "cuGreenCtxCreate");
-  check(cuGreenCtxStreamCreate(&p.stream, p.gctx, CU_STREAM_NON_BLOCKING, (int)priority), "cuGreenCtxStreamCreate");
+  check(PSRL_DRV(cuGreenCtxCreate)(&p.gctx, desc, dev, CU_GREEN_CTX_DEFAULT_STREAM), "cuGreenCtxCreate");
+  check(PSRL_DRV(cuGreenCtxStreamCreate)(&p.stream, p.gctx, CU_STREAM_NON_BLOCKING, (int)priority), "cuGreenCtxStreamCreate");
   p.sms = sms;
   p.reserved = reserved;
   p.total = total;

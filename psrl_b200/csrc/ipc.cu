@@ -9,6 +9,8 @@
 //    loads/stores; when a source is another GPU's memory the loads travel over
 //    NVLink (no copy engine, no staging, no TMA multicast).
 #include <cuda.h>
+
+#include "driver_api.h"
 #include <pybind11/pybind11.h>
 
 #include <map>
@@ -26,7 +28,7 @@ std::tuple<py::bytes, int64_t> ipc_handle(at::Tensor t) {
   at::cuda::CUDAGuard g(t.device());
   CUdeviceptr base = 0;
   size_t size = 0;
-  CUresult r = cuMemGetAddressRange(&base, &size, (CUdeviceptr)t.data_ptr());
+  CUresult r = PSRL_DRV(cuMemGetAddressRange)(&base, &size, (CUdeviceptr)t.data_ptr());
   TORCH_CHECK(r == CUDA_SUCCESS, "cuMemGetAddressRange failed (", (int)r, ")");
   cudaIpcMemHandle_t h;
   PSRL_CHECK_CUDA(cudaIpcGetMemHandle(&h, (void*)base));

@@ -9,6 +9,8 @@
 // training state are paused to share a GPU between roles.  Physical handles
 // are created as POSIX-fd exportable so peers can map them.
 #include <cuda.h>
+
+#include "driver_api.h"
 #include <cuda_runtime.h>
 #include <torch/extension.h>
 
@@ -21,7 +23,7 @@ namespace psrl {
     CUresult _r = (x);                                                               \
     if (_r != CUDA_SUCCESS) {                                                        \
       const char* msg = nullptr;                                                     \
-      cuGetErrorString(_r, &msg);                                                    \
+      PSRL_DRV(cuGetErrorString)(_r, &msg);                                                    \
       TORCH_CHECK(false, "CUDA driver error ", (int)_r, " (", msg ? msg : "?", ") at ", #x); \
     }                                                                                \
   } while (0)
@@ -35,18 +37,18 @@ class VmmRegion {
     prop.location.id = device_;
     prop.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
     size_t gran = 0;
-    CU_CHECK(cuMemGetAllocationGranularity(&gran, &prop, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED));
+    CU_CHECK(PSRL_DRV(cuMemGetAllocationGranularity)(&gran, &prop, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED));
     size_ = ((size_t)bytes + gran - 1) / gran * gran;
     prop_ = prop;
-    CU_CHECK(cuMemAddressReserve(&va_, size_, gran, 0, 0));
+    CU_CHECK(PSRL_DRV(cuMemAddressReserve)(&va_, size_, gran, 0, 0));
     map_();
   }
   ~VmmRegion() {
     if (mapped_) {
-      cuMemUnmap(va_, size_);
-      cuMemRelease(handle_);
+      PSRL_DRV(cuMemUnmap)(va_, size_);
+      PSRL_DRV(cuMemRelease)(handle_);
     }
-    if (va_) cuMemAddressFree(va_, size_);
+    if (va_) PSRL_DRV(cuMemAddressFree)(va_, size_);
     if (host_) cudaFreeHost(host_);
   }
   int64_t ptr() const { return (int64_t)va_; }
@@ -63,8 +65,8 @@ class VmmRegion {
     } else {
       has_backup_ = false;
     }
-    CU_CHECK(cuMemUnmap(va_, size_));
-    CU_CHECK(cuMemRelease(handle_));
+    CU_CHECK(PSRL_DRV(cuMemUnmap)(va_, size_));
+    CU_CHECK(PSRL_DRV(cuMemRelease)(handle_));
     mapped_ = false;
   }
 
@@ -81,13 +83,13 @@ class VmmRegion {
 
  private:
   void map_() {
-    CU_CHECK(cuMemCreate(&handle_, size_, &prop_, 0));
-    CU_CHECK(cuMemMap(va_, size_, 0, handle_, 0));
+    CU_CHECK(PSRL_DRV(cuMemCreate)(&handle_, size_, &prop_, 0));
+    CU_CHECK(PSRL_DRV(cuMemMap)(va_, size_, 0, handle_, 0));
     CUmemAccessDesc acc{};
     acc.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
     acc.location.id = device_;
     acc.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
-    CU_CHECK(cuMemSetAccess(va_, size_, &acc, 1));
+    CU_CHECK(PSRL_DRV(cuMemSetAccess)(va_, size_, &acc, 1));
     mapped_ = true;
   }
   int device_;

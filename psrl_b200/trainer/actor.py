@@ -119,12 +119,36 @@ class PolicyWorker:
         parts = balance_across_ranks([trajs[i] for i in idx], self.dp_world)
         return [idx[j] for j in parts[self.dp_rank]]
 
+    def _lockstep(self, bins: list) -> list:
+        """Expert-parallel forwards are collectives over the expert group
+        (token dispatch and combine, and their transposes in backward), so
+        every rank runs the same number of micro-batches: this rank's list is
+        padded with ``None`` up to the group maximum (one all-reduce of an
+        int).  A ``None`` entry runs a one-token placeholder whose result is
+        discarded (its loss is multiplied by zero)."""
+        if self.ep is None:
+            return list(bins)
+        import torch.distributed as dist
+        dev = self.device if self.device.type == "cuda" else torch.device("cpu")
+        n = torch.tensor([len(bins)], dtype=torch.int64, device=dev)
+        dist.all_reduce(n, op=dist.ReduceOp.MAX, group=self.ep.group)
+        return list(bins) + [None] * (int(n.item()) - len(bins))
+
+    def _placeholder(self):
+        t = Trajectory(uid=-1, request_id=-1, prompt_ids=[0], response_ids=[0], rollout_logprobs=[0.0],
+                       response_mask=[0])
+        return build_micro_batch([t], [0], self.device)
+
     # ------------------------------------------------------------- logprob
     @torch.no_grad()
     def compute_log_prob(self, trajs: list[Trajectory], idx: list[int], field: str = "old_logprobs",
                          temperature: float = 1.0) -> None:
         self.model.eval()
-        for bin_ in pack_micro_batches(idx, trajs, self.max_tokens):
+        for bin_ in self._lockstep(pack_micro_batches(idx, trajs, self.max_tokens)):
+            if bin_ is None:
+                mb = self._placeholder()
+                self.model.logprobs(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen, mb.labels, temperature)
+                continue
             mb = build_micro_batch(trajs, bin_, self.device)
             lp, _ = self.model.logprobs(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen, mb.labels,
                                         temperature)
@@ -134,7 +158,11 @@ class PolicyWorker:
 
     @torch.no_grad()
     def compute_values(self, trajs: list[Trajectory], idx: list[int]) -> None:
-        for bin_ in pack_micro_batches(idx, trajs, self.max_tokens):
+        for bin_ in self._lockstep(pack_micro_batches(idx, trajs, self.max_tokens)):
+            if bin_ is None:
+                mb = self._placeholder()
+                self.model.values(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen)
+                continue
             mb = build_micro_batch(trajs, bin_, self.device)
             v = self.model.values(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen).float().cpu()
             for i, sl in response_slices(mb, trajs):
@@ -163,7 +191,13 @@ class PolicyWorker:
                     for mini in self._mini_batches(trajs)]
         for _epoch in range(int(ac.ppo_epochs)):
             for mine, global_tokens, num_seqs in plan:
-                for bin_ in pack_micro_batches(mine, trajs, self.max_tokens):
+                for bin_ in self._lockstep(pack_micro_batches(mine, trajs, self.max_tokens)):
+                    if bin_ is None:
+                        mb = self._placeholder()
+                        lp, ent = self.model.logprobs(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen,
+                                                      mb.labels, temperature)
+                        ((lp * 0).sum() + (ent * 0).sum()).backward()
+                        continue
                     mb = build_micro_batch(trajs, bin_, self.device)
                     lp, ent = self.model.logprobs(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen,
                                                   mb.labels, temperature)
@@ -213,7 +247,11 @@ class PolicyWorker:
             plan = [(self.my_share(trajs, mini), float(sum(trajs[i].response_len for i in mini)), len(mini))
                     for mini in self._mini_batches(trajs)]
         for mine, global_tokens, _ in plan:
-            for bin_ in pack_micro_batches(mine, trajs, self.max_tokens):
+            for bin_ in self._lockstep(pack_micro_batches(mine, trajs, self.max_tokens)):
+                if bin_ is None:
+                    mb = self._placeholder()
+                    (self.model.values(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen) * 0).sum().backward()
+                    continue
                 mb = build_micro_batch(trajs, bin_, self.device)
                 v = self.model.values(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen)
                 old_v = torch.zeros_like(v)

@@ -259,20 +259,183 @@ def compute_advantages(estimator: str, *, scores: torch.Tensor, uids, gamma: flo
     raise ValueError(f"unknown adv_estimator {estimator!r}")
 
 
+# --------------------------------------------------------- in-reward KL
+
+
+class FixedKLController:
+    """Constant in-reward KL coefficient (``algorithm.kl_ctrl.type=fixed``)."""
+
+    def __init__(self, kl_coef: float):
+        self.value = float(kl_coef)
+
+    def update(self, current_kl: float, n_steps: int) -> None:
+        pass
+
+
+class AdaptiveKLController:
+    """Proportional controller of Ziegler et al. 2019 ("Fine-Tuning Language
+    Models from Human Preferences", section 2.2): the coefficient moves toward
+    the value that keeps the measured KL at ``target_kl``, by at most 20 %
+    of ``n_steps / horizon`` per update."""
+
+    def __init__(self, init_kl_coef: float, target_kl: float, horizon: int):
+        self.value = float(init_kl_coef)
+        self.target = float(target_kl)
+        self.horizon = int(horizon)
+
+    def update(self, current_kl: float, n_steps: int) -> None:
+        err = min(max(float(current_kl) / self.target - 1.0, -0.2), 0.2)
+        self.value *= 1.0 + err * float(n_steps) / self.horizon
+
+
+def kl_controller(alg_cfg):
+    """The in-reward KL controller ``algorithm.kl_ctrl`` names (reference
+    config ``psrl/trainer/config/ppo_trainer.yaml`` ``algorithm.kl_ctrl``)."""
+    kc = alg_cfg.get("kl_ctrl", None) or {}
+    kind = str(kc.get("type", "fixed"))
+    coef = float(kc.get("kl_coef", alg_cfg.get("kl_coef", 0.001)))
+    if kind == "fixed":
+        return FixedKLController(coef)
+    if kind == "adaptive":
+        return AdaptiveKLController(coef, float(kc.get("target_kl", 0.1)), int(kc.get("horizon", 10000)))
+    raise ValueError(f"unknown kl_ctrl.type {kind!r}")
+
+
+def token_reward_row(t) -> list:
+    """Per-response-token rewards of one trajectory: the in-reward KL rewards
+    when they were applied, else the outcome reward on the last token."""
+    if getattr(t, "token_rewards", None) is not None:
+        return list(t.token_rewards)
+    row = [0.0] * t.response_len
+    if row:
+        row[-1] = float(t.reward)
+    return row
+
+
+def trajectory_score(t) -> float:
+    """Sequence score an outcome estimator normalises: the sum of the
+    per-token rewards (the outcome reward when no KL term was applied)."""
+    if getattr(t, "token_rewards", None) is not None:
+        return float(sum(t.token_rewards))
+    return float(t.reward)
+
+
+def apply_kl_in_reward(trajs, ctrl, kind: str = "kl", group=None, replicas: int = 1) -> dict:
+    """Per-token rewards ``score·[last] - beta·KL(old || ref)`` on every
+    trajectory (``token_rewards``), then one controller update with the batch
+    KL (each trajectory's masked token mean, averaged over trajectories).
+
+    With ``group`` the KL statistic is summed over its ranks (one all-reduce
+    of two numbers), so every rank applies the same coefficient update.
+    When each trajectory sits on ``replicas`` ranks of the group (tensor-
+    parallel replicas of one data-parallel share), both sums scale alike and
+    the mean is unchanged; ``n_steps`` divides the count by ``replicas``.
+
+    Reference: ``psrl/trainer/ppo/ray_trainer.py:2834-2842`` (veRL's
+    ``apply_kl_penalty`` with ``kl_ctrl_in_reward``).
+    """
+    import torch.distributed as dist
+    beta = float(ctrl.value)
+    kl_sum, n = 0.0, 0
+    for t in trajs:
+        ln = t.response_len
+        if ln == 0:
+            t.token_rewards = []
+            continue
+        old = t.old_logprobs if t.old_logprobs is not None else t.rollout_logprobs
+        lp = torch.tensor(old[:ln], dtype=torch.float32)
+        ref = torch.tensor(t.ref_logprobs[:ln], dtype=torch.float32)
+        m = torch.tensor(t.response_mask[:ln], dtype=torch.float32) if t.response_mask is not None else torch.ones(ln)
+        kld = kl_penalty(lp, ref, kind) * m
+        row = (-beta * kld)
+        row[ln - 1] += float(t.reward)
+        t.token_rewards = row.tolist()
+        kl_sum += float(kld.sum() / m.sum().clamp_min(1.0))
+        n += 1
+    st = torch.tensor([kl_sum, float(n)], dtype=torch.float64)
+    if group is not None and dist.is_initialized():
+        dist.all_reduce(st, group=group)
+    current = float(st[0] / st[1].clamp_min(1.0))
+    ctrl.update(current, n_steps=int(round(float(st[1]) / max(1, int(replicas)))))
+    return {"actor/reward_kl_penalty": current, "actor/reward_kl_penalty_coeff": beta}
+
+
+def outcome_advantages_global(cfg, trajs, group=None) -> None:
+    """Outcome estimator over the trajectories of every rank in ``group``:
+    each rank contributes ``(request_id, uid, score, length)`` of its own
+    trajectories (one all-gather of small records), duplicates (replicas that
+    hold the same share) are dropped by ``request_id``, the estimator runs on
+    the whole set, and each rank keeps its own trajectories' advantages."""
+    import torch.distributed as dist
+    mine = [(int(t.request_id), t.uid, trajectory_score(t), t.response_len) for t in trajs]
+    recs = [mine]
+    if group is not None and dist.is_initialized():
+        recs = [None] * dist.get_world_size(group)
+        dist.all_gather_object(recs, mine, group=group)
+    seen: dict = {}
+    for part in recs:
+        for r in part:
+            seen.setdefault(r[0], r)
+    allr = [seen[k] for k in sorted(seen)]
+    if not allr:
+        return
+    adv = compute_advantages(cfg.algorithm.adv_estimator, scores=torch.tensor([r[2] for r in allr]),
+                             uids=[r[1] for r in allr], norm_by_std=bool(cfg.algorithm.norm_adv_by_std_in_grpo),
+                             lengths=torch.tensor([r[3] for r in allr]))
+    pos = {r[0]: i for i, r in enumerate(allr)}
+    for t in trajs:
+        t.advantage = float(adv[pos[int(t.request_id)]])
+        t.token_advantages = None
+
+
+def shard_advantages(cfg, trajs, group=None, kl_ctrl=None, replicas: int = 1, critic: bool = False) -> dict:
+    """Advantages on one rank's share of a batch that is spread over
+    ``group`` (the multi-GPU placements, where the control plane already
+    filled the outcome advantages from the trajectory rewards).
+
+    In-reward KL (``kl_ctrl``) changes every trajectory's reward, so outcome
+    estimators are recomputed over the whole batch and token-level ones
+    (REINFORCE++) are recomputed with global whitening; with a critic GAE
+    always runs here on the rank's values."""
+    out: dict = {}
+    if kl_ctrl is not None:
+        out.update(apply_kl_in_reward(trajs, kl_ctrl, str(cfg.algorithm.get("kl_penalty", "kl")), group, replicas))
+    token_level = cfg.algorithm.adv_estimator in ("gae", "reinforce_plus_plus")
+    if critic or (kl_ctrl is not None and token_level):
+        gae_with_global_whitening(cfg, trajs, group)
+    elif kl_ctrl is not None:
+        outcome_advantages_global(cfg, trajs, group)
+    return out
+
+
 def gae_with_global_whitening(cfg, trajs, group=None) -> None:
-    """GAE on this rank's trajectories (``old_values`` set), whitened with the
-    mean and variance of all ranks' response tokens in ``group`` (one
-    all-reduce of three numbers); fills ``token_advantages`` and ``returns``."""
+    """GAE (``old_values`` set) or, with no critic, REINFORCE++ returns on
+    this rank's trajectories, whitened with the mean and variance of all
+    ranks' response tokens in ``group`` (one all-reduce of three numbers);
+    fills ``token_advantages`` and ``returns``.  Per-token rewards come from
+    ``token_reward_row`` (in-reward KL when applied)."""
     import torch.distributed as dist
     L = max((t.response_len for t in trajs), default=1)
     N = len(trajs)
     rew, vals, mask = torch.zeros(N, L), torch.zeros(N, L), torch.zeros(N, L)
+    use_values = all(t.old_values is not None for t in trajs)
     for i, t in enumerate(trajs):
         n = t.response_len
         mask[i, :n] = 1
-        rew[i, n - 1] = t.reward
-        vals[i, :n] = torch.tensor(t.old_values[:n])
-    adv, ret = gae_advantage(rew, vals, mask, float(cfg.algorithm.gamma), float(cfg.algorithm.lam), whiten=False)
+        rew[i, :n] = torch.tensor(token_reward_row(t), dtype=torch.float32)
+        if use_values:
+            vals[i, :n] = torch.tensor(t.old_values[:n])
+    if use_values:
+        adv, ret = gae_advantage(rew, vals, mask, float(cfg.algorithm.gamma), float(cfg.algorithm.lam),
+                                 whiten=False)
+    else:
+        g = float(cfg.algorithm.gamma)
+        ret = torch.zeros(N, L)
+        run = torch.zeros(N)
+        for j in reversed(range(L)):
+            run = rew[:, j] + g * run * mask[:, j]
+            ret[:, j] = run
+        adv = ret * mask
     st = torch.tensor([float((adv * mask).sum()), float((adv * adv * mask).sum()), float(mask.sum())],
                       dtype=torch.float64)
     if group is not None and dist.is_initialized():
@@ -280,6 +443,8 @@ def gae_with_global_whitening(cfg, trajs, group=None) -> None:
     mean = st[0] / st[2].clamp_min(1)
     var = st[1] / st[2].clamp_min(1) - mean * mean
     adv = ((adv - float(mean)) * float(torch.rsqrt(var.clamp_min(0) + 1e-8))) * mask
+    if not use_values:
+        ret = adv
     for i, t in enumerate(trajs):
         n = t.response_len
         t.token_advantages = adv[i, :n].tolist()

@@ -35,6 +35,7 @@ class Trajectory:
     ref_logprobs: list | None = None
     old_logprobs: list | None = None
     response_mask: list | None = None   # multi-turn: 0 on environment tokens
+    token_rewards: list | None = None   # per-token rewards when the in-reward KL term is applied
     meta: dict = field(default_factory=dict)
 
     @property

@@ -35,6 +35,7 @@ from ..parallel.weight_sync import WeightLayout, WeightPuller, WeightStore
 from ..rollout.engine import EngineWeights, RolloutEngine
 from ..rollout.instance import SyncPolicy
 from ..utils.rpc import RPCClient
+from . import algos
 from .actor import PolicyWorker
 from .control_plane import ExchangeMailbox, spawn_control_plane
 
@@ -150,6 +151,13 @@ class DisaggregatedRun:
             self.critic = PolicyWorker(cfg, cargs, self.device, dp_group=self.train_group,
                                        seed=int(cfg.trainer.seed) + 1, dp_rank=self.dp_rank, dp_world=self.dp_world,
                                        tp_group=self.tp_group)
+        self.ref = None
+        if cfg.actor.use_kl_loss or cfg.algorithm.use_kl_in_reward:
+            # sharded like the actor (expert / tensor parallel forwards are collectives)
+            self.ref = PolicyWorker(cfg, self.args, self.device, dp_group=self.train_group,
+                                    seed=int(cfg.trainer.seed), trainable=False, dp_rank=self.dp_rank,
+                                    dp_world=self.dp_world, tp_group=self.tp_group)
+        self.kl_ctrl = algos.kl_controller(cfg.algorithm) if cfg.algorithm.use_kl_in_reward else None
         mode = "hbm" if (cfg.psrl.ps_mode == "hbm" and self.device.type == "cuda") else "cpu"
         self.store = WeightStore(self.layout, self.device, mode)
         self.store.publish(self.pub_flat, 0)
@@ -169,12 +177,15 @@ class DisaggregatedRun:
         t1 = time.perf_counter()
         if not bool(self.cfg.psrl.log_prob.enable_rollout_engine_log_prob):
             self.actor.compute_log_prob(trajs, list(range(len(trajs))), field="old_logprobs")
-        critic_metrics = {}
+        idx = list(range(len(trajs)))
+        if self.ref is not None:
+            self.ref.compute_log_prob(trajs, idx, field="ref_logprobs")
         if self.critic is not None:
-            from .algos import gae_with_global_whitening
-            self.critic.compute_values(trajs, list(range(len(trajs))))
-            gae_with_global_whitening(self.cfg, trajs, self.train_cpu_group)
-            critic_metrics = self.critic.update_critic(trajs, plan=plan)
+            self.critic.compute_values(trajs, idx)
+        critic_metrics = algos.shard_advantages(self.cfg, trajs, self.train_cpu_group, self.kl_ctrl, self.tp_size,
+                                                critic=self.critic is not None)
+        if self.critic is not None:
+            critic_metrics.update(self.critic.update_critic(trajs, plan=plan))
         metrics = self.actor.update_policy(trajs, float(self.cfg.rollout.temperature), plan=plan)
         metrics.update(critic_metrics)
         if self.assembler is not None:

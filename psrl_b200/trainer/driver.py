@@ -75,12 +75,19 @@ def resolve_device(cfg) -> torch.device:
     return torch.device(d)
 
 
-def compute_batch_advantages(cfg, trajs) -> dict:
-    """Fill ``advantage`` / ``token_advantages`` / ``returns`` on the trajectories."""
+def compute_batch_advantages(cfg, trajs, kl_ctrl=None) -> dict:
+    """Fill ``advantage`` / ``token_advantages`` / ``returns`` on the
+    trajectories.  With ``kl_ctrl`` (``algorithm.use_kl_in_reward``) the
+    per-token rewards first get the KL penalty against the reference policy
+    (``ref_logprobs`` must be set)."""
     est = cfg.algorithm.adv_estimator
     if not trajs:
         return {}
-    scores = torch.tensor([t.reward for t in trajs], dtype=torch.float32)
+    out = {}
+    if kl_ctrl is not None:
+        out.update(algos.apply_kl_in_reward(trajs, kl_ctrl, str(cfg.algorithm.get("kl_penalty", "kl"))))
+    raw = torch.tensor([t.reward for t in trajs], dtype=torch.float32)
+    scores = torch.tensor([algos.trajectory_score(t) for t in trajs], dtype=torch.float32)
     uids = [t.uid for t in trajs]
     if est in ("grpo", "rloo", "gdpo", "optimal_token_baseline"):
         lengths = torch.tensor([t.response_len for t in trajs])
@@ -98,7 +105,7 @@ def compute_batch_advantages(cfg, trajs) -> dict:
         for i, t in enumerate(trajs):
             n = t.response_len
             mask[i, :n] = 1
-            rew[i, n - 1] = t.reward
+            rew[i, :n] = torch.tensor(algos.token_reward_row(t), dtype=torch.float32)
             if t.old_values is not None:
                 vals[i, :n] = torch.tensor(t.old_values[:n])
         if est == "gae":
@@ -111,8 +118,11 @@ def compute_batch_advantages(cfg, trajs) -> dict:
             n = t.response_len
             t.token_advantages = adv[i, :n].tolist()
             t.returns = ret[i, :n].tolist()
-    return {"critic/score_mean": float(scores.mean()), "critic/score_max": float(scores.max()),
-            "critic/score_min": float(scores.min())}
+    out.update({"critic/score_mean": float(raw.mean()), "critic/score_max": float(raw.max()),
+                "critic/score_min": float(raw.min())})
+    if kl_ctrl is not None:
+        out["critic/rewards_mean"] = float(scores.mean())
+    return out
 
 
 class RLTrainer:
@@ -138,6 +148,7 @@ class RLTrainer:
         self.ref = None
         if cfg.actor.use_kl_loss or cfg.algorithm.use_kl_in_reward:
             self.ref = PolicyWorker(cfg, self.args, self.device, seed=self.seed, trainable=False)
+        self.kl_ctrl = algos.kl_controller(cfg.algorithm) if cfg.algorithm.use_kl_in_reward else None
         rc = cfg.rollout
         self.engine_weights = EngineWeights.from_model(self.actor.model, self.device, dtype=self.actor.dtype)
         max_len = int(rc.max_prompt_length) + int(rc.max_response_length) + 64
@@ -351,9 +362,10 @@ class RLTrainer:
     # -------------------------------------------------------- checkpoints
     def save_checkpoint(self) -> str:
         from ..utils.checkpoint import save_checkpoint
+        extra = {"kl_coef": self.kl_ctrl.value} if self.kl_ctrl is not None else {}
         return save_checkpoint(self.cfg.trainer.default_local_dir, self.global_step, self.actor, self.data,
                                self.critic, self.ps.get_ps_model_version(),
-                               use_dcp=bool(self.cfg.psrl.checkpoint.use_dcp_save))
+                               use_dcp=bool(self.cfg.psrl.checkpoint.use_dcp_save), extra=extra)
 
     def resume(self, step: int | None = None) -> int:
         """Load weights/optimizer/data cursor and re-seat the PS at that version."""
@@ -361,8 +373,11 @@ class RLTrainer:
         root = self.cfg.trainer.get("resume_from_path") or self.cfg.trainer.default_local_dir
         if step is None and find_latest(root) is None:
             return 0
+        extra: dict = {}
         step = load_checkpoint(root, self.actor, self.data, self.critic, step,
-                               use_dcp=bool(self.cfg.psrl.checkpoint.use_dcp_save))
+                               use_dcp=bool(self.cfg.psrl.checkpoint.use_dcp_save), extra_out=extra)
+        if self.kl_ctrl is not None and "kl_coef" in extra:
+            self.kl_ctrl.value = float(extra["kl_coef"])
         self.global_step = step
         self.ps.init_model_version_for_resume(step + 1)
         self.manager.initial_ps_version = step

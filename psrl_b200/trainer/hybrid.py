@@ -45,6 +45,7 @@ from ..rollout.engine import EngineWeights, RolloutEngine
 from ..rollout.instance import SyncPolicy
 from ..utils.locks import RWLock
 from ..utils.rpc import RPCClient
+from . import algos
 from .actor import PolicyWorker
 from .control_plane import ExchangeMailbox, spawn_control_plane
 from .driver import _apply_switch_interval, train_stream_ctx, trainer_stream_for
@@ -63,8 +64,6 @@ class HybridRun:
         self.device = info.device
         self.is_cuda = self.device.type == "cuda"
         self.args = model_args_from_config(cfg.model)
-        if cfg.algorithm.use_kl_in_reward:
-            raise NotImplementedError("hybrid placement: in-reward KL is not wired (use_kl_loss is)")
         self.trained_tokens = 0
         self.global_step = 0
         self.liveness_s = float(cfg.trainer.get("liveness_timeout_s", 300))
@@ -139,8 +138,11 @@ class HybridRun:
             self.critic = PolicyWorker(cfg, cargs, self.device, dp_group=dp_group, seed=seed + 1,
                                        dp_rank=self.dp_rank, dp_world=self.dp_world, tp_group=tp_group)
         self.ref = None
-        if cfg.actor.use_kl_loss:
-            self.ref = PolicyWorker(cfg, self.args, self.device, seed=seed, trainable=False)
+        if cfg.actor.use_kl_loss or cfg.algorithm.use_kl_in_reward:
+            # sharded like the actor (expert / tensor parallel forwards are collectives)
+            self.ref = PolicyWorker(cfg, self.args, self.device, dp_group=dp_group, seed=seed, trainable=False,
+                                    dp_rank=self.dp_rank, dp_world=self.dp_world, tp_group=tp_group)
+        self.kl_ctrl = algos.kl_controller(cfg.algorithm) if cfg.algorithm.use_kl_in_reward else None
         self.wlock = RWLock()
         self.eng_sources = None
         if self.eng_tp is not None:
@@ -333,11 +335,12 @@ class HybridRun:
                 self.ref.compute_log_prob(trajs, idx, field="ref_logprobs")
             if not bool(self.cfg.psrl.log_prob.enable_rollout_engine_log_prob):
                 self.actor.compute_log_prob(trajs, idx, field="old_logprobs")
-            critic_metrics = {}
             if self.critic is not None:
                 self.critic.compute_values(trajs, idx)
-                self._gae(trajs)
-                critic_metrics = self.critic.update_critic(trajs, plan=plan)
+            critic_metrics = algos.shard_advantages(self.cfg, trajs, self.cpu_group, self.kl_ctrl, self.tp_size,
+                                                    critic=self.critic is not None)
+            if self.critic is not None:
+                critic_metrics.update(self.critic.update_critic(trajs, plan=plan))
             metrics = self.actor.update_policy(trajs, float(self.cfg.rollout.temperature),
                                                step_guard=lambda: self.wlock.exclusive(600),
                                                sync_every_micro_batch=self.is_cuda, plan=plan)
@@ -364,10 +367,6 @@ class HybridRun:
         })
         metrics.update({f"rollout/{k}": v for k, v in self.engine.engine_stats().items() if isinstance(v, (int, float))})
         return metrics
-
-    def _gae(self, trajs) -> None:
-        from .algos import gae_with_global_whitening
-        gae_with_global_whitening(self.cfg, trajs, self.cpu_group)
 
     def close(self) -> None:
         self.stop_rollout()

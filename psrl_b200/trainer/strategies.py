@@ -54,7 +54,7 @@ class StepStrategy:
     def optimize(self, trajs, metrics: dict) -> None:
         from .driver import compute_batch_advantages
         t = self.t
-        metrics.update(compute_batch_advantages(t.cfg, trajs))
+        metrics.update(compute_batch_advantages(t.cfg, trajs, getattr(t, "kl_ctrl", None)))
         with t.log.span("TRAIN", step=t.global_step):
             if t.critic is not None:
                 metrics.update(t.critic.update_critic(trajs))

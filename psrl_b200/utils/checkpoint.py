@@ -114,14 +114,17 @@ def load_worker(worker, path: str, rank: int = 0, use_dcp: bool = False) -> None
 
 
 def save_checkpoint(root: str, step: int, actor, data=None, critic=None, ps_version: int | None = None,
-                    rank: int = 0, use_dcp: bool = False) -> str:
+                    rank: int = 0, use_dcp: bool = False, extra: dict | None = None) -> str:
+    """``extra``: small trainer state kept beside the data cursor (e.g. the
+    adaptive in-reward KL coefficient); :func:`load_checkpoint` returns it
+    through ``extra_out``."""
     d = step_dir(root, step)
     save_worker(actor, os.path.join(d, "actor"), rank, use_dcp)
     if critic is not None:
         save_worker(critic, os.path.join(d, "critic"), rank, use_dcp)
     if rank == 0:
         torch.save({"data": data.state_dict() if data is not None else None, "ps_version": ps_version,
-                    "global_step": step}, os.path.join(d, "data.pt"))
+                    "global_step": step, "extra": dict(extra or {})}, os.path.join(d, "data.pt"))
         with open(os.path.join(os.path.expanduser(root), LATEST), "w") as fh:
             fh.write(str(step))
     return d
@@ -136,7 +139,7 @@ def find_latest(root: str) -> int | None:
 
 
 def load_checkpoint(root: str, actor, data=None, critic=None, step: int | None = None, rank: int = 0,
-                    use_dcp: bool = False) -> int:
+                    use_dcp: bool = False, extra_out: dict | None = None) -> int:
     step = find_latest(root) if step is None else step
     if step is None:
         raise FileNotFoundError(f"no checkpoint under {root}")
@@ -147,4 +150,6 @@ def load_checkpoint(root: str, actor, data=None, critic=None, step: int | None =
     meta = torch.load(os.path.join(d, "data.pt"), weights_only=False)
     if data is not None and meta.get("data"):
         data.load_state_dict(meta["data"])
+    if extra_out is not None:
+        extra_out.update(meta.get("extra") or {})
     return int(meta["global_step"])

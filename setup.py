@@ -46,7 +46,8 @@ setup(
             name="psrl_b200._C",
             sources=[os.path.relpath(s, ROOT) for s in sources],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
-            libraries=["cuda"],
+            # no libcuda link: driver-API calls are resolved at run time
+            # (csrc/driver_api.h), so the module imports on driver-less hosts
         ),
         # host-only runtime pieces (plain pybind11, no CUDA or torch linkage):
         # they load on CPU-only machines too

@@ -50,3 +50,19 @@ def test_trainer_checkpoint_resume(tmp_path):
     assert t2.actor.dp.step_count == t.actor.dp.step_count
     m = t2.step()                  # continues from buffer 2
     assert m["step"] == 2
+
+
+def test_adaptive_kl_coefficient_survives_resume(tmp_path):
+    from psrl_b200.trainer import RLTrainer
+    root = str(tmp_path / "ckpt")
+    ov = [f"trainer.default_local_dir={root}", "psrl.checkpoint.use_dcp_save=false",
+          "algorithm.use_kl_in_reward=true", "algorithm.kl_ctrl.type=adaptive", "rollout.max_response_length=12"]
+    t = RLTrainer(load_config(preset="cpu_tiny_grpo", overrides=ov))
+    t.step()
+    t.save_checkpoint()
+    t.stop_rollout()
+    coef = t.kl_ctrl.value
+    assert coef != 0.001
+    t2 = RLTrainer(load_config(preset="cpu_tiny_grpo", overrides=ov + ["trainer.resume_mode=auto"]), seed=7)
+    assert t2.resume() == 1
+    assert t2.kl_ctrl.value == coef

@@ -213,7 +213,9 @@ def _worker_hybrid_sharded(rank, world, port, q, overrides):
     info = init_distributed("cpu", timeout_s=300)
     res = run_hybrid(cfg, steps=2, warmup=0, info=info)
     q.put({"rank": rank, "engine": res["engine_checksum"], "tokens": res["tokens"],
-           "steps": [m["num_trajectories"] for m in res["metrics"]] if rank == 0 else None})
+           "steps": [m["num_trajectories"] for m in res["metrics"]] if rank == 0 else None,
+           "kl": [m.get("actor/reward_kl_penalty") for m in res["metrics"]] if rank == 0 else None,
+           "kl_coef": [m.get("actor/reward_kl_penalty_coeff") for m in res["metrics"]] if rank == 0 else None})
     import torch.distributed as dist
     dist.destroy_process_group()
 
@@ -240,6 +242,23 @@ def test_gloo_world2_hybrid_expert_parallel_moe():
     engines receive identical assembled weights."""
     res = _run_sharded(["model.preset=tiny-moe", "++actor.expert_parallel_size=2"])
     assert res[0]["steps"] == [32, 32]
+    assert abs(res[0]["engine"] - res[1]["engine"]) < 1e-6 * max(1.0, abs(res[0]["engine"]))
+
+
+def test_gloo_world2_hybrid_expert_parallel_in_reward_kl():
+    """MoE at EP=2 with in-reward KL (adaptive coefficient), the KL loss and
+    trainer-side old log-probs, with a token budget small enough that the two
+    ranks pack different numbers of micro-batches (expert-parallel forwards
+    stay in lockstep)."""
+    res = _run_sharded(["model.preset=tiny-moe", "++actor.expert_parallel_size=2",
+                        "algorithm.use_kl_in_reward=true", "algorithm.kl_ctrl.type=adaptive",
+                        "actor.use_kl_loss=true", "psrl.log_prob.enable_rollout_engine_log_prob=false",
+                        "actor.ppo_max_token_len_per_gpu=160"])
+    assert res[0]["steps"] == [32, 32]
+    kl, coef = res[0]["kl"], res[0]["kl_coef"]
+    assert kl[0] is not None and abs(kl[0]) < 1e-6, kl       # step 0: actor == reference
+    assert kl[1] is not None and kl[1] == kl[1], kl
+    assert coef[0] == 0.001 and coef[1] < coef[0], coef      # adaptive: KL below target lowers beta
     assert abs(res[0]["engine"] - res[1]["engine"]) < 1e-6 * max(1.0, abs(res[0]["engine"]))
 
 
