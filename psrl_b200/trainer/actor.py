@@ -201,10 +201,11 @@ class PolicyWorker:
                     mb = build_micro_batch(trajs, bin_, self.device)
                     lp, ent = self.model.logprobs(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen,
                                                   mb.labels, temperature)
-                    tis = None
+                    tis = mb.extra.get("is_weights")
                     if use_tis:
                         rl = build_micro_batch(trajs, bin_, self.device, field_old="rollout_logprobs").old_logprobs
-                        tis = algos.truncated_is_weight(mb.old_logprobs, rl, float(self.cfg.algorithm.rollout_correction.tis_cap))
+                        w = algos.truncated_is_weight(mb.old_logprobs, rl, float(self.cfg.algorithm.rollout_correction.tis_cap))
+                        tis = w if tis is None else tis * w
                     agg = dict(seq_ids=mb.seq_ids, num_seqs=num_seqs, global_tokens=global_tokens)
                     loss, m = algos.ppo_policy_loss(lp, mb.old_logprobs, mb.advantages, mb.loss_mask,
                                                     float(ac.clip_ratio_low), float(ac.clip_ratio_high),

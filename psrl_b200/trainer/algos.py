@@ -259,6 +259,80 @@ def compute_advantages(estimator: str, *, scores: torch.Tensor, uids, gamma: flo
     raise ValueError(f"unknown adv_estimator {estimator!r}")
 
 
+# ------------------------------------------------------- rollout correction
+
+
+def apply_rollout_correction(rc, trajs) -> dict:
+    """Off-policy correction between the rollout engine's log-probs and the
+    trainer's old-policy log-probs, per trajectory (after ``old_logprobs``
+    are known; a no-op when both are the same numbers).
+
+    ``rc.rollout_is`` (``token`` | ``sequence``): importance weights
+    ``pi_old / pi_rollout`` (per token, or the product over the sequence),
+    truncated at ``rollout_is_threshold``; stored as ``is_weights`` and
+    multiplied into the policy loss.  ``rc.rollout_rs`` (``token`` |
+    ``sequence`` | ``geometric``): rejection sampling, which zeroes
+    ``response_mask`` on tokens (or whole sequences) whose ratio (token,
+    sequence product, or per-token geometric mean) leaves
+    ``[rollout_rs_threshold_lower, rollout_rs_threshold]`` (lower bound
+    defaults to the reciprocal of the upper).
+
+    Reference: ``psrl/trainer/ppo/ray_trainer.py:2843-2856`` (veRL's
+    ``compute_rollout_correction_and_add_to_batch``).
+    """
+    level = rc.get("rollout_is", None)
+    rs = rc.get("rollout_rs", None)
+    if not level and not rs:
+        return {}
+    thr = float(rc.get("rollout_is_threshold", 2.0))
+    hi = float(rc.get("rollout_rs_threshold", 2.0))
+    lo = rc.get("rollout_rs_threshold_lower", None)
+    lo = 1.0 / hi if lo is None else float(lo)
+    kept = total = 0.0
+    kl_sum = w_sum = 0.0
+    n_seq = 0
+    for t in trajs:
+        ln = t.response_len
+        if ln == 0 or t.old_logprobs is None:
+            continue
+        old = torch.tensor(t.old_logprobs[:ln], dtype=torch.float64)
+        roll = torch.tensor(t.rollout_logprobs[:ln], dtype=torch.float64)
+        m = (torch.tensor(t.response_mask[:ln], dtype=torch.float64) if t.response_mask is not None
+             else torch.ones(ln, dtype=torch.float64))
+        lr = (old - roll).clamp(-20.0, 20.0) * m
+        cnt = float(m.sum())
+        total += cnt
+        kl_sum += float((-lr).sum() / max(cnt, 1.0))
+        n_seq += 1
+        if rs:
+            if rs == "token":
+                r = torch.exp(lr)
+                keep = ((r >= lo) & (r <= hi)).double()
+            else:
+                agg = lr.sum() if rs == "sequence" else lr.sum() / max(cnt, 1.0)
+                r = float(torch.exp(agg.clamp(-20.0, 20.0)))
+                keep = torch.full((ln,), 1.0 if lo <= r <= hi else 0.0, dtype=torch.float64)
+            m = m * keep
+            t.response_mask = [int(x) for x in m.tolist()]
+        kept += float(m.sum())
+        if level:
+            if level == "token":
+                w = torch.exp(lr).clamp(max=thr)
+            elif level == "sequence":
+                w = torch.full((ln,), float(torch.exp(lr.sum().clamp(-20.0, 20.0)).clamp(max=thr)),
+                               dtype=torch.float64)
+            else:
+                raise ValueError(f"unknown rollout_is level {level!r}")
+            t.is_weights = (w * m).tolist()
+            w_sum += float((w * m).sum() / max(float(m.sum()), 1.0))
+    out = {"rollout_corr/kl": kl_sum / max(n_seq, 1)}
+    if rs:
+        out["rollout_corr/rs_masked_fraction"] = 1.0 - kept / max(total, 1.0)
+    if level:
+        out["rollout_corr/is_weight_mean"] = w_sum / max(n_seq, 1)
+    return out
+
+
 # --------------------------------------------------------- in-reward KL
 
 

@@ -36,6 +36,7 @@ class Trajectory:
     old_logprobs: list | None = None
     response_mask: list | None = None   # multi-turn: 0 on environment tokens
     token_rewards: list | None = None   # per-token rewards when the in-reward KL term is applied
+    is_weights: list | None = None      # rollout-correction importance weights per response token
     meta: dict = field(default_factory=dict)
 
     @property
@@ -98,8 +99,9 @@ def pack_micro_batches(idx: list[int], trajs: list[Trajectory], max_tokens: int)
 
 
 def build_micro_batch(trajs: list[Trajectory], idx: list[int], device, field_old: str = "old_logprobs") -> MicroBatch:
-    ids, pos, labels, mask, old, adv, seq = [], [], [], [], [], [], []
+    ids, pos, labels, mask, old, adv, seq, isw = [], [], [], [], [], [], [], []
     cu = [0]
+    any_isw = any(trajs[i].is_weights is not None for i in idx)
     for j, i in enumerate(idx):
         t = trajs[i]
         toks = list(t.prompt_ids) + list(t.response_ids)
@@ -122,6 +124,11 @@ def build_micro_batch(trajs: list[Trajectory], idx: list[int], device, field_old
         else:
             a[P - 1:] = t.advantage
         adv.append(a)
+        if any_isw:
+            w = np.ones(n, dtype=np.float32)
+            if t.is_weights is not None:
+                w[P - 1:] = np.asarray(t.is_weights, dtype=np.float32)
+            isw.append(w)
         seq.append(np.full(n, j, dtype=np.int64))
         cu.append(cu[-1] + n)
 
@@ -139,7 +146,8 @@ def build_micro_batch(trajs: list[Trajectory], idx: list[int], device, field_old
         input_ids=cat(ids, torch.long), positions=cat(pos, torch.int32),
         cu_seqlens=torch.tensor(cu, dtype=torch.int32).to(device), max_seqlen=max(lens) if lens else 0,
         labels=cat(labels, torch.long), loss_mask=cat(mask, torch.float32), old_logprobs=cat(old, torch.float32),
-        advantages=cat(adv, torch.float32), seq_ids=cat(seq, torch.long), traj_index=list(idx))
+        advantages=cat(adv, torch.float32), seq_ids=cat(seq, torch.long), traj_index=list(idx),
+        extra={"is_weights": cat(isw, torch.float32)} if any_isw else {})
 
 
 def response_slices(mb: MicroBatch, trajs: list[Trajectory]):

@@ -184,6 +184,7 @@ class DisaggregatedRun:
             self.critic.compute_values(trajs, idx)
         critic_metrics = algos.shard_advantages(self.cfg, trajs, self.train_cpu_group, self.kl_ctrl, self.tp_size,
                                                 critic=self.critic is not None)
+        critic_metrics.update(algos.apply_rollout_correction(self.cfg.algorithm.rollout_correction, trajs))
         if self.critic is not None:
             critic_metrics.update(self.critic.update_critic(trajs, plan=plan))
         metrics = self.actor.update_policy(trajs, float(self.cfg.rollout.temperature), plan=plan)

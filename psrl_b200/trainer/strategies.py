@@ -20,6 +20,8 @@ from __future__ import annotations
 
 import time
 
+from . import algos
+
 STAGE_META: dict[str, str] = {
     "old_log_prob": "per_sample",
     "ref_log_prob": "per_sample",
@@ -55,6 +57,7 @@ class StepStrategy:
         from .driver import compute_batch_advantages
         t = self.t
         metrics.update(compute_batch_advantages(t.cfg, trajs, getattr(t, "kl_ctrl", None)))
+        metrics.update(algos.apply_rollout_correction(t.cfg.algorithm.rollout_correction, trajs))
         with t.log.span("TRAIN", step=t.global_step):
             if t.critic is not None:
                 metrics.update(t.critic.update_critic(trajs))
