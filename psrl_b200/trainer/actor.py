@@ -44,6 +44,12 @@ def mini_batch_groups(trajs: list[Trajectory], mini_batch_size: int) -> list[lis
     return [[i for g in groups[s: s + per] for i in g] for s in range(0, len(groups), per)]
 
 
+def loss_tokens(t: Trajectory) -> int:
+    """Response tokens that enter the policy loss (environment tokens of a
+    multi-turn response and rejected tokens are masked out)."""
+    return int(sum(t.response_mask)) if t.response_mask is not None else t.response_len
+
+
 def plan_update(trajs: list[Trajectory], mini_batch_size: int, dp_world: int) -> list[list[tuple]]:
     """Per data-parallel rank, the list of ``(my_indices, global_tokens, num_seqs)``
     of every PPO mini-batch (token-balanced split of each mini-batch).  Every
@@ -51,7 +57,7 @@ def plan_update(trajs: list[Trajectory], mini_batch_size: int, dp_world: int) ->
     optimizer steps (and collectives)."""
     plans: list[list[tuple]] = [[] for _ in range(dp_world)]
     for mini in mini_batch_groups(trajs, mini_batch_size):
-        gt = float(sum(trajs[i].response_len for i in mini))
+        gt = float(sum(loss_tokens(trajs[i]) for i in mini))
         parts = balance_across_ranks([trajs[i] for i in mini], dp_world)
         for r in range(dp_world):
             plans[r].append(([mini[j] for j in parts[r]], gt, len(mini)))
@@ -134,6 +140,21 @@ class PolicyWorker:
         dist.all_reduce(n, op=dist.ReduceOp.MAX, group=self.ep.group)
         return list(bins) + [None] * (int(n.item()) - len(bins))
 
+    def _recount_plan(self, trajs: list[Trajectory], plan: list[tuple]) -> list[tuple]:
+        """A plan made before rejection sampling counted tokens that are now
+        masked: recount each mini-batch's loss tokens over the data-parallel
+        group (one all-reduce of one number per mini-batch)."""
+        import torch.distributed as dist
+        local = torch.tensor([float(sum(loss_tokens(trajs[i]) for i in mine)) for mine, _, _ in plan],
+                             dtype=torch.float64)
+        grp = self.dp.group if self.dp is not None else None
+        if grp is not None and dist.is_initialized() and dist_world(grp) > 1:
+            dev = self.device if self.device.type == "cuda" else torch.device("cpu")
+            local = local.to(dev)
+            dist.all_reduce(local, group=grp)
+            local = local.cpu()
+        return [(mine, max(1.0, float(n)), ns) for (mine, _, ns), n in zip(plan, local.tolist())]
+
     def _placeholder(self):
         t = Trajectory(uid=-1, request_id=-1, prompt_ids=[0], response_ids=[0], rollout_logprobs=[0.0],
                        response_mask=[0])
@@ -187,8 +208,10 @@ class PolicyWorker:
         stats: dict[str, list] = {}
         use_tis = bool(self.cfg.algorithm.rollout_correction.tis)
         if plan is None:
-            plan = [(self.my_share(trajs, mini), float(sum(trajs[i].response_len for i in mini)), len(mini))
+            plan = [(self.my_share(trajs, mini), float(sum(loss_tokens(trajs[i]) for i in mini)), len(mini))
                     for mini in self._mini_batches(trajs)]
+        elif self.cfg.algorithm.rollout_correction.get("rollout_rs", None):
+            plan = self._recount_plan(trajs, plan)
         for _epoch in range(int(ac.ppo_epochs)):
             for mine, global_tokens, num_seqs in plan:
                 for bin_ in self._lockstep(pack_micro_batches(mine, trajs, self.max_tokens)):
@@ -245,7 +268,7 @@ class PolicyWorker:
         self.model.train()
         stats: dict[str, list] = {}
         if plan is None:
-            plan = [(self.my_share(trajs, mini), float(sum(trajs[i].response_len for i in mini)), len(mini))
+            plan = [(self.my_share(trajs, mini), float(sum(loss_tokens(trajs[i]) for i in mini)), len(mini))
                     for mini in self._mini_batches(trajs)]
         for mine, global_tokens, _ in plan:
             for bin_ in self._lockstep(pack_micro_batches(mine, trajs, self.max_tokens)):

@@ -262,6 +262,16 @@ def test_gloo_world2_hybrid_expert_parallel_in_reward_kl():
     assert abs(res[0]["engine"] - res[1]["engine"]) < 1e-6 * max(1.0, abs(res[0]["engine"]))
 
 
+def test_gloo_world2_hybrid_rollout_correction():
+    """Trainer-side old log-probs with sequence IS weights and token
+    rejection sampling; the loss normaliser is recounted over both ranks."""
+    res = _run_sharded(["psrl.log_prob.enable_rollout_engine_log_prob=false",
+                        "algorithm.rollout_correction.rollout_is=sequence",
+                        "algorithm.rollout_correction.rollout_rs=token"])
+    assert res[0]["steps"] == [32, 32]
+    assert abs(res[0]["engine"] - res[1]["engine"]) < 1e-6 * max(1.0, abs(res[0]["engine"]))
+
+
 def test_gloo_world2_hybrid_tensor_parallel():
     """Dense trainer at TP=2 (one data-parallel rank); both engines hold the
     assembled full weights."""

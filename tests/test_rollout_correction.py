@@ -94,3 +94,12 @@ def test_colocated_training_with_correction():
         assert 0.0 <= m["rollout_corr/rs_masked_fraction"] <= 1.0
         assert m["rollout_corr/is_weight_mean"] > 0.0
         assert math.isfinite(m["actor/pg_loss"])
+
+
+def test_plan_counts_only_loss_tokens():
+    from psrl_b200.trainer.actor import loss_tokens, plan_update
+    a = _traj([-1.0] * 4, [-1.0] * 4, rid=0, mask=[1, 0, 0, 1])
+    b = _traj([-1.0] * 3, [-1.0] * 3, rid=1)
+    assert loss_tokens(a) == 2 and loss_tokens(b) == 3
+    plans = plan_update([a, b], 2, 1)
+    assert plans[0][0][1] == 5.0
