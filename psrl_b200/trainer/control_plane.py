@@ -58,6 +58,7 @@ class ControlPlane:
         self._cv = threading.Condition()
         self._batches: dict[int, dict] = {}
         self._batch_locks: dict[int, threading.Lock] = {}
+        self._pre: dict[int, dict] = {}     # buffer -> request id -> per-sample fields computed early
         self._done = threading.Event()
 
     # ----------------------------------------------------------------- setup
@@ -140,14 +141,37 @@ class ControlPlane:
                 raise TimeoutError(f"buffer {b} not ready: silent instances {silent}, {self.manager.snapshot()}")
             time.sleep(0.002)
 
+    # ------------------------------------------- fine-grain overlap (recompute)
+    def progress(self, b: int) -> tuple:
+        """(committed entries at the head of buffer ``b``, buffer READY,
+        entries that make it READY)."""
+        b = int(b)
+        return self.manager.occupied_prefix(b), self.manager.buffer_ready(b), int(self.manager.ready_entries)
+
+    def peek_chunk(self, b: int, lo: int, hi: int) -> list:
+        """Trajectories of entries [lo, hi) of buffer ``b`` (not consumed), for
+        per-sample stages that run while the buffer fills."""
+        return self.manager.peek(int(b), int(lo), int(hi))
+
+    def post_per_sample(self, b: int, fields: dict) -> None:
+        """Per-sample results (``{request_id: {field: list}}``: old / ref
+        log-probs, values) computed on trainer ranks before the buffer was
+        consumed; :meth:`_build` attaches them to the trajectories."""
+        with self._cv:
+            self._pre.setdefault(int(b), {}).update(fields)
+
     def _build(self, b: int, dp_world: int, timeout_s: float) -> dict:
         from ..trainer.actor import plan_update
         from ..trainer.driver import compute_batch_advantages
         self._wait_ready(b, timeout_s)
         trajs = self.manager.consume(b)
         use_rollout_lp = bool(self.cfg.psrl.log_prob.enable_rollout_engine_log_prob)
+        with self._cv:
+            pre = self._pre.pop(int(b), {})
         for t in trajs:
             t.old_logprobs = t.rollout_logprobs if use_rollout_lp else None
+            for k, v in pre.get(t.request_id, {}).items():
+                setattr(t, k, v)
         if self.cfg.critic.enable:
             # GAE needs the critic's values: the trainer ranks compute advantages on
             # their own shares (whitened with global statistics)

@@ -38,6 +38,7 @@ from ..utils.rpc import RPCClient
 from . import algos
 from .actor import PolicyWorker
 from .control_plane import ExchangeMailbox, spawn_control_plane
+from .strategies import overlap_per_sample, per_sample_missing, sharded_overlap_enabled
 
 
 def log(msg: str) -> None:
@@ -158,6 +159,7 @@ class DisaggregatedRun:
                                     seed=int(cfg.trainer.seed), trainable=False, dp_rank=self.dp_rank,
                                     dp_world=self.dp_world, tp_group=self.tp_group)
         self.kl_ctrl = algos.kl_controller(cfg.algorithm) if cfg.algorithm.use_kl_in_reward else None
+        self.sharded_overlap = sharded_overlap_enabled(cfg)
         mode = "hbm" if (cfg.psrl.ps_mode == "hbm" and self.device.type == "cuda") else "cpu"
         self.store = WeightStore(self.layout, self.device, mode)
         self.store.publish(self.pub_flat, 0)
@@ -171,17 +173,19 @@ class DisaggregatedRun:
     def trainer_step(self) -> dict:
         b = self.global_step
         t0 = time.perf_counter()
+        chunks = 0
+        if self.sharded_overlap:
+            chunks = overlap_per_sample(
+                self.cfg, self.cp, b, lambda ts: per_sample_missing(self.cfg, ts, self.actor, self.ref, self.critic),
+                group=self.train_cpu_group, src=0, dp_rank=self.dp_rank, dp_world=self.dp_world,
+                post=self.rank % self.tp_size == 0, timeout_s=self.buffer_timeout_s)
         batch = self.cp.get_batch(b, self.dp_rank, self.dp_world, self.buffer_timeout_s, self.rank % self.tp_size,
                                   self.tp_size)
         trajs, plan = batch["trajs"], batch["plan"]
         t1 = time.perf_counter()
-        if not bool(self.cfg.psrl.log_prob.enable_rollout_engine_log_prob):
-            self.actor.compute_log_prob(trajs, list(range(len(trajs))), field="old_logprobs")
-        idx = list(range(len(trajs)))
-        if self.ref is not None:
-            self.ref.compute_log_prob(trajs, idx, field="ref_logprobs")
-        if self.critic is not None:
-            self.critic.compute_values(trajs, idx)
+        pre = sum(1 for t in trajs if t.ref_logprobs is not None or t.old_values is not None
+                  or (t.old_logprobs is not None and t.old_logprobs is not t.rollout_logprobs))
+        per_sample_missing(self.cfg, trajs, self.actor, self.ref, self.critic)
         critic_metrics = algos.shard_advantages(self.cfg, trajs, self.train_cpu_group, self.kl_ctrl, self.tp_size,
                                                 critic=self.critic is not None)
         critic_metrics.update(algos.apply_rollout_correction(self.cfg.algorithm.rollout_correction, trajs))
@@ -211,7 +215,8 @@ class DisaggregatedRun:
         self.global_step += 1
         self.trained_tokens += int(batch["trained_tokens"])
         metrics.update(batch["metrics"])
-        metrics.update({"step": b, "trained_tokens": batch["trained_tokens"],
+        metrics.update({"step": b, "trained_tokens": batch["trained_tokens"], "fine_grain/chunks": chunks,
+                        "fine_grain/precomputed": pre,
                         "num_trajectories": batch["num_trajectories"],
                         "response_length/mean": batch["response_length/mean"],
                         "staleness/max": batch["staleness/max"],

@@ -49,6 +49,7 @@ from . import algos
 from .actor import PolicyWorker
 from .control_plane import ExchangeMailbox, spawn_control_plane
 from .driver import _apply_switch_interval, train_stream_ctx, trainer_stream_for
+from .strategies import overlap_per_sample, per_sample_missing, sharded_overlap_enabled
 
 
 def log(msg: str) -> None:
@@ -143,6 +144,7 @@ class HybridRun:
             self.ref = PolicyWorker(cfg, self.args, self.device, dp_group=dp_group, seed=seed, trainable=False,
                                     dp_rank=self.dp_rank, dp_world=self.dp_world, tp_group=tp_group)
         self.kl_ctrl = algos.kl_controller(cfg.algorithm) if cfg.algorithm.use_kl_in_reward else None
+        self.sharded_overlap = sharded_overlap_enabled(cfg)
         self.wlock = RWLock()
         self.eng_sources = None
         if self.eng_tp is not None:
@@ -325,18 +327,21 @@ class HybridRun:
             raise RuntimeError("rollout thread failed") from self._rollout_error
         self.start_rollout()
         t0 = time.perf_counter()
+        chunks = 0
+        if self.sharded_overlap:
+            with train_stream_ctx(self.train_stream):
+                chunks = overlap_per_sample(
+                    self.cfg, self.cp, b, lambda ts: per_sample_missing(self.cfg, ts, self.actor, self.ref, self.critic),
+                    group=self.cpu_group, src=0, dp_rank=self.dp_rank, dp_world=self.dp_world,
+                    post=self.rank % self.tp_size == 0, timeout_s=self.buffer_timeout_s)
         batch = self.cp.get_batch(b, self.dp_rank, self.dp_world, self.buffer_timeout_s, self.rank % self.tp_size,
                                   self.tp_size)
         trajs, plan = batch["trajs"], batch["plan"]
         t1 = time.perf_counter()
-        idx = list(range(len(trajs)))
+        pre = sum(1 for t in trajs if t.ref_logprobs is not None or t.old_values is not None
+                  or (t.old_logprobs is not None and t.old_logprobs is not t.rollout_logprobs))
         with train_stream_ctx(self.train_stream):
-            if self.ref is not None:
-                self.ref.compute_log_prob(trajs, idx, field="ref_logprobs")
-            if not bool(self.cfg.psrl.log_prob.enable_rollout_engine_log_prob):
-                self.actor.compute_log_prob(trajs, idx, field="old_logprobs")
-            if self.critic is not None:
-                self.critic.compute_values(trajs, idx)
+            per_sample_missing(self.cfg, trajs, self.actor, self.ref, self.critic)
             critic_metrics = algos.shard_advantages(self.cfg, trajs, self.cpu_group, self.kl_ctrl, self.tp_size,
                                                     critic=self.critic is not None)
             critic_metrics.update(algos.apply_rollout_correction(self.cfg.algorithm.rollout_correction, trajs))
@@ -364,7 +369,8 @@ class HybridRun:
             "step": b, "num_trajectories": batch["num_trajectories"], "trained_tokens": batch["trained_tokens"],
             "response_length/mean": batch["response_length/mean"], "staleness/max": batch["staleness/max"],
             "timing_s/gen_wait": t1 - t0, "timing_s/train": t2 - t1, "timing_s/step": time.perf_counter() - t0,
-            "rollout/pulls": self.pulls, "rollout/pull_s": self.pull_s,
+            "rollout/pulls": self.pulls, "rollout/pull_s": self.pull_s, "fine_grain/chunks": chunks,
+            "fine_grain/precomputed": pre,
         })
         metrics.update({f"rollout/{k}": v for k, v in self.engine.engine_stats().items() if isinstance(v, (int, float))})
         return metrics

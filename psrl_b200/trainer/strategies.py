@@ -141,3 +141,79 @@ def build_step_strategy(trainer) -> StepStrategy:
     if trainer.cfg.psrl.fine_grain_overlap.granularity == "none":
         return FullBatchStepStrategy(trainer)
     return FineGrainOverlapStrategy(trainer)
+
+
+# --------------------------------------------- multi-GPU placements (sharded)
+
+
+def per_sample_missing(cfg, trajs, actor, ref=None, critic=None) -> None:
+    """Per-sample stages on trajectories that do not carry their result yet
+    (reference log-probs, old log-probs unless the rollout engine's are used,
+    critic values).  Every worker call runs even with nothing to do, so
+    expert- and tensor-parallel forwards stay matched across ranks."""
+    if ref is not None:
+        ref.compute_log_prob(trajs, [i for i, t in enumerate(trajs) if t.ref_logprobs is None], field="ref_logprobs")
+    if not bool(cfg.psrl.log_prob.enable_rollout_engine_log_prob):
+        actor.compute_log_prob(trajs, [i for i, t in enumerate(trajs) if t.old_logprobs is None],
+                               field="old_logprobs")
+    if critic is not None:
+        critic.compute_values(trajs, [i for i, t in enumerate(trajs) if t.old_values is None])
+
+
+def sharded_overlap_enabled(cfg) -> bool:
+    fgo = cfg.psrl.fine_grain_overlap
+    if fgo.granularity == "none":
+        return False
+    if fgo.overlap_scope != "recompute":
+        raise ValueError("the multi-GPU placements overlap the per-sample stages only "
+                         "(psrl.fine_grain_overlap.overlap_scope=recompute); pre_step runs colocated")
+    return True
+
+
+def overlap_per_sample(cfg, cp, b: int, compute, *, group=None, src: int = 0, dp_rank: int = 0, dp_world: int = 1,
+                       post: bool = True, poll_s: float = 0.01, timeout_s: float = 1800.0) -> int:
+    """Fine-grain overlap (``overlap_scope=recompute``) in the multi-GPU
+    placements: while staleness buffer ``b`` fills, the trainer ranks run the
+    per-sample stages on each committed chunk of entries and post the results
+    to the control plane, which attaches them when it builds the batch; the
+    step then computes only what is still missing.
+
+    Rank ``src`` polls the buffer's progress and broadcasts it over ``group``
+    (trainer ranks, gloo), so every rank takes the same chunks.  Each data-
+    parallel rank takes every ``dp_world``-th trajectory of a chunk (the
+    tensor-parallel ranks of one data-parallel rank compute it together;
+    ``post`` is set on one of them).  Returns the number of chunks.
+    Reference: ``psrl/trainer/ppo/strategies/`` (fine-grain overlap)."""
+    import torch.distributed as dist
+    _, chunk = resolve_fine_grain_chunk_size(cfg)
+    t0 = time.monotonic()
+    done = chunks = 0
+    while True:
+        lead = group is None or dist.get_rank() == src
+        msg = [cp.progress(b) if lead else None]
+        if group is not None:
+            dist.broadcast_object_list(msg, src=src, group=group)
+        avail, ready, _need = msg[0]
+        if avail - done >= chunk or (ready and avail > done):
+            hi = min(int(avail), done + chunk)
+            trajs = cp.peek_chunk(b, done, hi)
+            mine = [t for i, t in enumerate(trajs) if i % dp_world == dp_rank]
+            compute(mine)
+            if post:
+                fields = {}
+                for t in mine:
+                    f = {k: getattr(t, k) for k in ("old_logprobs", "ref_logprobs", "old_values")
+                         if getattr(t, k) is not None}
+                    if f:
+                        fields[t.request_id] = f
+                if fields:
+                    cp.post_per_sample(b, fields)
+            done = hi
+            chunks += 1
+            t0 = time.monotonic()
+        elif ready:
+            return chunks
+        else:
+            if time.monotonic() - t0 > timeout_s:
+                raise TimeoutError(f"buffer {b}: no progress for the per-sample overlap")
+            time.sleep(poll_s)

@@ -215,7 +215,9 @@ def _worker_hybrid_sharded(rank, world, port, q, overrides):
     q.put({"rank": rank, "engine": res["engine_checksum"], "tokens": res["tokens"],
            "steps": [m["num_trajectories"] for m in res["metrics"]] if rank == 0 else None,
            "kl": [m.get("actor/reward_kl_penalty") for m in res["metrics"]] if rank == 0 else None,
-           "kl_coef": [m.get("actor/reward_kl_penalty_coeff") for m in res["metrics"]] if rank == 0 else None})
+           "kl_coef": [m.get("actor/reward_kl_penalty_coeff") for m in res["metrics"]] if rank == 0 else None,
+           "chunks": [m.get("fine_grain/chunks") for m in res["metrics"]] if rank == 0 else None,
+           "pre": [m.get("fine_grain/precomputed") for m in res["metrics"]] if rank == 0 else None})
     import torch.distributed as dist
     dist.destroy_process_group()
 
@@ -272,6 +274,17 @@ def test_gloo_world2_hybrid_rollout_correction():
     assert abs(res[0]["engine"] - res[1]["engine"]) < 1e-6 * max(1.0, abs(res[0]["engine"]))
 
 
+def test_gloo_world2_hybrid_fine_grain_per_sample_overlap():
+    """Old and reference log-probs computed chunk by chunk while the buffer
+    fills (posted to the control plane), with the KL loss on."""
+    res = _run_sharded(["psrl.log_prob.enable_rollout_engine_log_prob=false", "actor.use_kl_loss=true",
+                        "psrl.fine_grain_overlap.granularity=micro_batch", "psrl.fine_grain_overlap.multiplier=2"])
+    assert res[0]["steps"] == [32, 32]
+    assert all(c is not None and c >= 1 for c in res[0]["chunks"]), res[0]["chunks"]
+    assert all(p is not None and p > 0 for p in res[0]["pre"]), res[0]["pre"]
+    assert abs(res[0]["engine"] - res[1]["engine"]) < 1e-6 * max(1.0, abs(res[0]["engine"]))
+
+
 def test_gloo_world2_hybrid_tensor_parallel():
     """Dense trainer at TP=2 (one data-parallel rank); both engines hold the
     assembled full weights."""
@@ -293,7 +306,9 @@ def _worker_disagg_sharded(rank, world, port, q, overrides):
     info = init_distributed("cpu", timeout_s=300)
     res = run_disaggregated(cfg, steps=2, warmup=0, info=info)
     if rank == 0:
-        q.put({"steps": [m["num_trajectories"] for m in res["metrics"]], "pulls": res["sync"]["pulls"]})
+        q.put({"steps": [m["num_trajectories"] for m in res["metrics"]], "pulls": res["sync"]["pulls"],
+               "pre": [m.get("fine_grain/precomputed") for m in res["metrics"]],
+               "kl": [m.get("actor/reward_kl_penalty") for m in res["metrics"]]})
     import torch.distributed as dist
     dist.destroy_process_group()
 
@@ -335,6 +350,31 @@ def test_gloo_world3_disaggregated_ppo_with_critic():
             p.kill()
     assert codes == [0, 0, 0], codes
     assert q.get(timeout=5)["steps"] == [32, 32]
+
+
+def test_gloo_world3_disaggregated_critic_kl_in_reward_fine_grain():
+    """Disaggregated PPO with a critic, in-reward KL against a reference model
+    and per-sample stages (old / reference log-probs, values) overlapped with
+    the buffer filling."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ov = ["critic.enable=true", "algorithm.adv_estimator=gae", "algorithm.use_kl_in_reward=true",
+          "psrl.log_prob.enable_rollout_engine_log_prob=false", "psrl.fine_grain_overlap.granularity=mini_batch"]
+    procs = [ctx.Process(target=_worker_disagg_sharded, args=(r, 3, port, q, ov)) for r in range(3)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(900)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0, 0], codes
+    res = q.get(timeout=5)
+    assert res["steps"] == [32, 32]
+    assert all(p is not None and p > 0 for p in res["pre"]), res
+    assert all(k is not None for k in res["kl"]), res
 
 
 def test_gloo_world2_hybrid_multiturn_agentic():
