@@ -7,7 +7,9 @@ Registered loops (reference ``psrl/workers/reward/reward_loop/registry.py:22``):
   ``-min(1, (len - (max_len - buffer)) / buffer) * factor`` beyond the soft limit;
 * ``bernoulli_hash`` — Bernoulli(p) decided by a seeded hash of the trajectory id
   (synthetic benchmark reward);
-* ``addition`` — 1.0 if the integer after the ``####`` marker equals the sum.
+* ``addition`` — 1.0 if the integer after the ``####`` marker equals the sum;
+* ``prime``, ``gdpo``, ``gen`` — process-pool scoring with timeouts,
+  multi-component rewards and the generative reward model (``loops.py``).
 
 ``RewardManager.score`` is called per finished trajectory on the driver;
 ``normalize_reward`` mirrors the reference's batch normalisation hook.
@@ -18,6 +20,8 @@ from __future__ import annotations
 import hashlib
 import re
 from typing import Callable
+
+from . import loops as _loops
 
 REWARD_LOOPS: dict[str, Callable] = {}
 
@@ -78,8 +82,17 @@ def _dapo(ctx, traj) -> dict:
     return {"score": base["score"] + pen, "acc": base["score"], "overlong_penalty": pen}
 
 
+register_reward_loop("prime")(_loops.prime_loop)
+register_reward_loop("gdpo")(_loops.gdpo_loop)
+register_reward_loop("gen")(_loops.gen_loop)
+
+
 class RewardManager:
-    def __init__(self, cfg, tokenizer=None):
+    """``reward_model``: the service the ``gen`` loop sends judge prompts to
+    (anything with ``generate(prompt_ids) -> str``); built from
+    ``reward.gen_rm`` when it names the ``http`` backend."""
+
+    def __init__(self, cfg, tokenizer=None, reward_model=None):
         r = cfg.reward
         self.kind = r.kind
         self.ctx = {
@@ -89,7 +102,22 @@ class RewardManager:
             "overlong_buffer": r.get("overlong_buffer"),
             "max_response_length": int(cfg.rollout.max_response_length),
             "task": r.get("task", "bernoulli_hash" if r.kind in ("naive", "dapo") else r.kind),
+            "num_processes": int(r.get("num_processes", 8)),
+            "timeout_s": float(r.get("timeout_s", 300.0)),
+            "gdpo_components": list(r.get("gdpo_components") or []),
         }
+        cs = r.get("compute_score")
+        if cs:
+            from ..utils.common import load_object
+            self.ctx["compute_score"] = load_object(cs)
+        else:
+            self.ctx["compute_score"] = _loops.default_compute_score
+        g = r.get("gen_rm") or {}
+        self.ctx["gen_rm_function"] = g.get("function", "default")
+        if reward_model is None and g.get("backend") == "http" and g.get("url"):
+            reward_model = _loops.HttpRewardModel(g["url"], tokenizer, int(g.get("max_tokens", 512)),
+                                                  float(g.get("temperature", 0.0)), model=g.get("model"))
+        self.ctx["reward_model"] = reward_model
         if ":" in self.kind:
             # user code named in the config: "package.module:fn" or "path/file.py:fn",
             # called as fn(ctx, traj) -> {"score": float, ...}
@@ -102,6 +130,11 @@ class RewardManager:
 
     def score(self, traj) -> dict:
         return self._fn(self.ctx, traj)
+
+    def close(self) -> None:
+        scorer = self.ctx.pop("_prime", None)
+        if scorer is not None:
+            scorer.close()
 
     @staticmethod
     def normalize_reward(scores: list[float]) -> list[float]:

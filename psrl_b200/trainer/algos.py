@@ -434,6 +434,16 @@ def apply_kl_in_reward(trajs, ctrl, kind: str = "kl", group=None, replicas: int 
     return {"actor/reward_kl_penalty": current, "actor/reward_kl_penalty_coeff": beta}
 
 
+def score_components(trajs):
+    """[N, K] reward components from the ``gdpo`` reward loop (stored in
+    ``meta["reward_extra"]["components"]``), or None when any trajectory
+    lacks them or their counts differ."""
+    rows = [((t.meta or {}).get("reward_extra") or {}).get("components") for t in trajs]
+    if not rows or any(r is None for r in rows) or len({len(r) for r in rows}) != 1:
+        return None
+    return torch.tensor(rows, dtype=torch.float32)
+
+
 def outcome_advantages_global(cfg, trajs, group=None) -> None:
     """Outcome estimator over the trajectories of every rank in ``group``:
     each rank contributes ``(request_id, uid, score, length)`` of its own
@@ -441,7 +451,9 @@ def outcome_advantages_global(cfg, trajs, group=None) -> None:
     hold the same share) are dropped by ``request_id``, the estimator runs on
     the whole set, and each rank keeps its own trajectories' advantages."""
     import torch.distributed as dist
-    mine = [(int(t.request_id), t.uid, trajectory_score(t), t.response_len) for t in trajs]
+    comps = score_components(trajs)
+    mine = [(int(t.request_id), t.uid, trajectory_score(t), t.response_len,
+             comps[i].tolist() if comps is not None else None) for i, t in enumerate(trajs)]
     recs = [mine]
     if group is not None and dist.is_initialized():
         recs = [None] * dist.get_world_size(group)
@@ -453,9 +465,12 @@ def outcome_advantages_global(cfg, trajs, group=None) -> None:
     allr = [seen[k] for k in sorted(seen)]
     if not allr:
         return
+    comp_rows = [r[4] for r in allr]
+    comps = (torch.tensor(comp_rows, dtype=torch.float32)
+             if all(c is not None for c in comp_rows) and len({len(c) for c in comp_rows}) == 1 else None)
     adv = compute_advantages(cfg.algorithm.adv_estimator, scores=torch.tensor([r[2] for r in allr]),
                              uids=[r[1] for r in allr], norm_by_std=bool(cfg.algorithm.norm_adv_by_std_in_grpo),
-                             lengths=torch.tensor([r[3] for r in allr]))
+                             lengths=torch.tensor([r[3] for r in allr]), score_components=comps)
     pos = {r[0]: i for i, r in enumerate(allr)}
     for t in trajs:
         t.advantage = float(adv[pos[int(t.request_id)]])

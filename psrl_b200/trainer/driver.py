@@ -92,7 +92,7 @@ def compute_batch_advantages(cfg, trajs, kl_ctrl=None) -> dict:
     if est in ("grpo", "rloo", "gdpo", "optimal_token_baseline"):
         lengths = torch.tensor([t.response_len for t in trajs])
         adv = algos.compute_advantages(est, scores=scores, uids=uids, norm_by_std=bool(cfg.algorithm.norm_adv_by_std_in_grpo),
-                                       lengths=lengths)
+                                       lengths=lengths, score_components=algos.score_components(trajs))
         for t, a in zip(trajs, adv.tolist()):
             t.advantage = a
             t.token_advantages = None
