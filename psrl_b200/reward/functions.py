@@ -87,6 +87,11 @@ register_reward_loop("gdpo")(_loops.gdpo_loop)
 register_reward_loop("gen")(_loops.gen_loop)
 
 
+def _cuda_available() -> bool:
+    import torch
+    return torch.cuda.is_available()
+
+
 class RewardManager:
     """``reward_model``: the service the ``gen`` loop sends judge prompts to
     (anything with ``generate(prompt_ids) -> str``); built from
@@ -114,9 +119,13 @@ class RewardManager:
             self.ctx["compute_score"] = _loops.default_compute_score
         g = r.get("gen_rm") or {}
         self.ctx["gen_rm_function"] = g.get("function", "default")
-        if reward_model is None and g.get("backend") == "http" and g.get("url"):
-            reward_model = _loops.HttpRewardModel(g["url"], tokenizer, int(g.get("max_tokens", 512)),
-                                                  float(g.get("temperature", 0.0)), model=g.get("model"))
+        if reward_model is None and self.kind == "gen":
+            if g.get("backend") == "http" and g.get("url"):
+                reward_model = _loops.HttpRewardModel(g["url"], tokenizer, int(g.get("max_tokens", 512)),
+                                                      float(g.get("temperature", 0.0)), model=g.get("model"))
+            elif g.get("backend", "engine") == "engine" and (g.get("preset") or g.get("path")):
+                dev = "cuda" if cfg.trainer.get("device", "auto") != "cpu" and _cuda_available() else "cpu"
+                reward_model = _loops.build_engine_reward_model(g, tokenizer, dev)
         self.ctx["reward_model"] = reward_model
         if ":" in self.kind:
             # user code named in the config: "package.module:fn" or "path/file.py:fn",

@@ -234,6 +234,32 @@ class EngineRewardModel:
                     raise RuntimeError("reward-model engine dropped the request")
 
 
+def build_engine_reward_model(gcfg, tokenizer, device: str = "cpu") -> EngineRewardModel:
+    """Reward-model replicas from ``reward.gen_rm``: the model named by
+    ``preset`` or ``path`` (an HF directory; weights loaded when present),
+    ``replicas`` engines on ``device``, each with ``kv_cache_gb`` of KV."""
+    import torch
+
+    from ..models import build_model, model_args_from_config
+    from ..models.hf_io import load_hf_into
+    from ..rollout.engine import EngineWeights, RolloutEngine
+    args = model_args_from_config({"preset": gcfg.get("preset"), "path": gcfg.get("path")})
+    dev = torch.device(gcfg.get("device") or device)
+    dtype = torch.bfloat16 if dev.type == "cuda" else torch.float32
+    engines = []
+    for _ in range(max(1, int(gcfg.get("replicas", 1)))):
+        m = build_model(args, dev, dtype, seed=int(gcfg.get("seed", 0)))
+        if gcfg.get("path"):
+            load_hf_into(m, gcfg["path"])
+        engines.append(RolloutEngine(args, EngineWeights.from_model(m, dev, dtype),
+                                     max_num_seqs=int(gcfg.get("max_num_seqs", 16)),
+                                     max_model_len=int(gcfg.get("max_model_len", 4096)), block_size=16,
+                                     kv_cache_gb=float(gcfg.get("kv_cache_gb", 1.0)),
+                                     use_cuda_graph=dev.type == "cuda"))
+        del m
+    return EngineRewardModel(engines, tokenizer, int(gcfg.get("max_tokens", 512)), float(gcfg.get("temperature", 0.0)))
+
+
 class HttpRewardModel:
     """An OpenAI-style completions endpoint (``POST {url}/v1/completions``,
     answer in ``choices[0].text``) through the bounded POST pool."""

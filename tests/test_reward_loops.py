@@ -125,3 +125,11 @@ def test_gen_reward_model_on_engine_replicas():
     for i in range(3):
         assert m.score(_traj("#### 42", 42, rid=i))["score"] in (0.0, 1.0)
     assert all(not e.has_unfinished() for e in engines)
+
+
+def test_gen_reward_model_built_from_config():
+    m = _mgr("gen", "reward.gen_rm.preset=tiny", "reward.gen_rm.replicas=2", "reward.gen_rm.max_tokens=4",
+             "reward.gen_rm.kv_cache_gb=0.05", "++reward.gen_rm.max_model_len=1024", "trainer.device=cpu")
+    rm = m.ctx["reward_model"]
+    assert isinstance(rm, EngineRewardModel) and len(rm.engines) == 2
+    assert m.score(_traj("#### 42", 42))["score"] in (0.0, 1.0)
