@@ -48,8 +48,9 @@ class GenerateAgentLoop:
 class MultiTurnAgentLoop:
     multi_turn = True
 
-    def __init__(self, env_factory, turn_len_fn, max_turns: int = 8):
+    def __init__(self, env_factory, turn_len_fn, max_turns: int = 8, ignore_eos: bool = True):
         self.env_factory = env_factory
+        self.ignore_eos = bool(ignore_eos)
         self.turn_len = turn_len_fn
         self.max_turns = max_turns
         self.sessions: dict[int, dict] = {}
@@ -59,8 +60,8 @@ class MultiTurnAgentLoop:
         s = self.sessions.get(o.request_id)
         if s is None:
             env: Environment = self.env_factory()
-            env.reset({"uid": o.meta.get("uid", 0), "request_id": o.request_id})
-            s = {"env": env, "turns": [], "tag": o.version_tag}
+            env.reset({**o.meta, "uid": o.meta.get("uid", 0), "request_id": o.request_id})
+            s = {"env": env, "turns": [], "tag": o.version_tag, "info": {}}
             self.sessions[o.request_id] = s
         return s
 
@@ -70,7 +71,8 @@ class MultiTurnAgentLoop:
             s = self._session(o)
             s["turns"].append(TurnRecord(list(o.prompt_ids), list(o.output_ids), list(o.logprobs), list(o.versions)))
             turn = len(s["turns"]) - 1
-            obs, done, _ = s["env"].step(turn, list(o.output_ids))
+            obs, done, info = s["env"].step(turn, list(o.output_ids))
+            s["info"] = dict(info or {})
             if done or turn + 1 >= self.max_turns:
                 return None
             ctx = list(o.prompt_ids) + list(o.output_ids) + list(obs)
@@ -80,27 +82,49 @@ class MultiTurnAgentLoop:
                 meta["sticky_instance"] = tuple(instance_id)
             mt = int(self.turn_len(o.request_id, turn + 1))
             meta["max_tokens"] = mt
-            params = SamplingParams(max_tokens=mt, ignore_eos=True, seed=o.request_id * 7919 + 17 + turn + 1)
+            params = SamplingParams(max_tokens=mt, ignore_eos=self.ignore_eos, seed=o.request_id * 7919 + 17 + turn + 1)
             return GenRequest(o.request_id, ctx, params, s["tag"], meta)
 
     def finalize(self, o: RequestOutput) -> dict:
         with self.lock:
             s = self.sessions.pop(o.request_id, None)
+        if s:
+            s["env"].close()
         turns = s["turns"] if s else [TurnRecord(list(o.prompt_ids), list(o.output_ids), list(o.logprobs),
                                                  list(o.versions))]
         smp = build_training_data(turns)
         return {"prompt_ids": smp.prompt_ids, "response_ids": smp.response_ids, "logprobs": smp.rollout_logprobs,
-                "versions": smp.versions, "response_mask": smp.response_mask, "turns": smp.turn_count}
+                "versions": smp.versions, "response_mask": smp.response_mask, "turns": smp.turn_count,
+                "env_info": s["info"] if s else {}}
 
     def drop(self, request_id: int) -> None:
         with self.lock:
-            self.sessions.pop(request_id, None)
+            s = self.sessions.pop(request_id, None)
+        if s:
+            s["env"].close()
 
 
-def build_agent_loop(cfg, vocab_size: int):
+def build_agent_loop(cfg, vocab_size: int, tokenizer=None):
+    """``psrl.agentic_rl.env`` picks the environment of multi-turn episodes:
+    ``synthetic_tokens`` (the benchmark workload), ``shell_env`` or
+    ``tool_env`` (decoded turns; ``rollout.max_response_length`` tokens per
+    turn, stopping at EOS)."""
     turns = int(cfg.psrl.agentic_rl.get("max_turns", 1))
     if turns <= 1:
         return GenerateAgentLoop()
+    ar = cfg.psrl.agentic_rl
+    env_name = str(ar.get("env", "synthetic_tokens"))
+    if env_name != "synthetic_tokens":
+        from .envs import make_environment
+        kw = {"tokenizer": tokenizer, "max_turns": turns}
+        if env_name == "shell_env":
+            kw.update(timeout_s=float(ar.get("command_timeout_s", 30.0)), docker_image=ar.get("docker_image"))
+        elif env_name == "tool_env":
+            from .tools import ToolRegistry
+            kw.update(tools=ToolRegistry(), parser=str(ar.get("tool_parser", "hermes")))
+        per_turn = int(cfg.rollout.max_response_length)
+        return MultiTurnAgentLoop(lambda: make_environment(env_name, **kw), lambda rid, turn: per_turn, turns,
+                                  ignore_eos=False)
     d = cfg.data
     mu, sigma, cap = float(d.response_len_mu), float(d.response_len_sigma), int(d.response_len_cap)
     ar = cfg.psrl.agentic_rl

@@ -52,8 +52,9 @@ class AgentLoopManager:
                  agent_loop=None):
         from .loops import build_agent_loop
         self.cfg = cfg
-        self.loop = agent_loop if agent_loop is not None else build_agent_loop(cfg, data.src.vocab
-                                                                               if hasattr(data.src, "vocab") else 1024)
+        vocab = data.src.vocab if hasattr(data.src, "vocab") else 1024
+        self.loop = agent_loop if agent_loop is not None else build_agent_loop(cfg, vocab,
+                                                                               getattr(data, "tokenizer", None))
         self.ps = ps
         self.data = data
         self.reward = reward
@@ -175,7 +176,8 @@ class AgentLoopManager:
             return
         traj = Trajectory(uid=uid, request_id=rid, prompt_ids=sample["prompt_ids"], response_ids=sample["response_ids"],
                           rollout_logprobs=sample["logprobs"], versions=sample["versions"], version_tag=o.version_tag,
-                          response_mask=sample["response_mask"], meta={**o.meta, "turns": sample["turns"]})
+                          response_mask=sample["response_mask"], meta={**o.meta, "turns": sample["turns"],
+                                                                      "env_info": sample.get("env_info") or {}})
         self.ps.update_request_status(rid, RequestStatus.REWARD_RUNNING)
         sc = self.reward.score(traj)
         traj.reward = float(sc["score"])

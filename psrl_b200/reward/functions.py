@@ -82,6 +82,14 @@ def _dapo(ctx, traj) -> dict:
     return {"score": base["score"] + pen, "acc": base["score"], "overlong_penalty": pen}
 
 
+@register_reward_loop("env")
+def _env(ctx, traj) -> dict:
+    """The reward the episode's environment reported (e.g. the shell task's tests)."""
+    info = (traj.meta or {}).get("env_info") or {}
+    return {"score": float(info.get("reward", 0.0)), **{k: float(v) for k, v in info.items()
+                                                        if isinstance(v, (int, float)) and k != "reward"}}
+
+
 register_reward_loop("prime")(_loops.prime_loop)
 register_reward_loop("gdpo")(_loops.gdpo_loop)
 register_reward_loop("gen")(_loops.gen_loop)
