@@ -1,7 +1,7 @@
 """Common helpers (C39): dynamic import of user code named in a config, worker
-naming, compact serialisation of samples, a ChatML chat template, and a
-bounded HTTP POST pool for external services (reward models, sandboxes,
-environments).
+naming, compact serialisation of samples, a ChatML chat template, a bounded
+HTTP POST pool for external services (reward models, sandboxes,
+environments), and a safety-net cleanup of labelled Docker containers.
 
 Reference: ``psrl/utils/common/*.py`` (``worker_naming.py``, ``http_utils.py``,
 dynamic import and serialisation helpers, chat templates).
@@ -161,3 +161,23 @@ class HttpPostPool:
 
     def close(self) -> None:
         self._ex.shutdown(wait=True)
+
+
+# ------------------------------------------------------------------ docker
+
+
+def remove_containers_by_label(label: str = "psrl=episode", run=None) -> int:
+    """Force-remove every Docker container carrying ``label`` (episode
+    containers a crashed worker left behind).  Returns how many were
+    removed; 0 when Docker is not installed.  ``run`` replaces
+    ``subprocess.run`` (tests)."""
+    import shutil
+    import subprocess
+    run = run or subprocess.run
+    if run is subprocess.run and shutil.which("docker") is None:
+        return 0
+    ps = run(["docker", "ps", "-aq", "--filter", f"label={label}"], capture_output=True, text=True, timeout=60)
+    ids = [x for x in (ps.stdout or "").split() if x]
+    if ids:
+        run(["docker", "rm", "-f", *ids], capture_output=True, text=True, timeout=120)
+    return len(ids)

@@ -94,3 +94,18 @@ def test_reward_from_user_module(tmp_path):
     rm = RewardManager(cfg)
     t = Trajectory(uid=0, request_id=1, prompt_ids=[1], response_ids=[2], rollout_logprobs=[0.0])
     assert rm.score(t)["score"] == 0.25
+
+
+def test_remove_containers_by_label_with_fake_docker():
+    from types import SimpleNamespace
+
+    from psrl_b200.utils.common import remove_containers_by_label
+    calls = []
+
+    def run(argv, **kw):
+        calls.append(argv)
+        return SimpleNamespace(stdout="abc123\ndef456\n" if argv[1] == "ps" else "", returncode=0)
+
+    assert remove_containers_by_label("psrl=episode", run=run) == 2
+    assert calls[0][:4] == ["docker", "ps", "-aq", "--filter"] and calls[0][4] == "label=psrl=episode"
+    assert calls[1] == ["docker", "rm", "-f", "abc123", "def456"]
