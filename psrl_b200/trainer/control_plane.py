@@ -158,6 +158,8 @@ class ControlPlane:
         log-probs, values) computed on trainer ranks before the buffer was
         consumed; :meth:`_build` attaches them to the trajectories."""
         with self._cv:
+            if int(b) in self._batches:
+                return          # already built: the step computes what is missing
             self._pre.setdefault(int(b), {}).update(fields)
 
     def _build(self, b: int, dp_world: int, timeout_s: float) -> dict:

@@ -212,6 +212,9 @@ def overlap_per_sample(cfg, cp, b: int, compute, *, group=None, src: int = 0, dp
             chunks += 1
             t0 = time.monotonic()
         elif ready:
+            if group is not None:
+                # every rank has posted before any rank makes the control plane build the batch
+                dist.barrier(group=group)
             return chunks
         else:
             if time.monotonic() - t0 > timeout_s:
