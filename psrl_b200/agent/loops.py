@@ -7,6 +7,10 @@
   (turn output + observation) and the next turn is resubmitted with a sticky
   hint so the rollout engine reuses the cached prefix KV; when the environment
   ends the episode the TITO builder assembles the sample (env tokens masked).
+* ``SessionAgentLoop`` — the agent drives: a user agent function runs per
+  task against a session of the session router (the same calls an external
+  agent makes over its HTTP API), and the closed session's TITO record is
+  the sample (reference ``loops/session_agent_loop.py``).
 
 The registry mirrors the reference's Hydra-registered loop names
 (``psrl/workers/agent_loop/loops/``).
@@ -102,6 +106,47 @@ class MultiTurnAgentLoop:
             s = self.sessions.pop(request_id, None)
         if s:
             s["env"].close()
+
+
+@register_agent_loop("session")
+class SessionAgentLoop:
+    """Runs ``agent_fn(client, task)`` for each task on ``workers`` threads;
+    ``client.complete(prompt_ids, max_tokens)`` goes through ``router`` (a
+    :class:`SessionRouter`, e.g. over :func:`engine_generate_fn`).  Returns
+    one sample per task: the TITO fields plus ``version_tag`` and the task,
+    or ``error`` when the agent raised (its session is closed either way)."""
+
+    multi_turn = True
+
+    def __init__(self, router, agent_fn, workers: int = 8):
+        self.router = router
+        self.agent_fn = agent_fn
+        self.workers = max(1, int(workers))
+
+    def run(self, tasks: list[dict]) -> list[dict]:
+        from concurrent.futures import ThreadPoolExecutor
+
+        from ..rollout.session_router import LocalSessionClient
+
+        def one(i_task):
+            i, task = i_task
+            sid = str(task.get("session_id", f"task-{i}"))
+            client = LocalSessionClient(self.router, sid)
+            err = None
+            try:
+                self.agent_fn(client, task)
+            except Exception as exc:       # the agent's failure ends its episode only
+                err = f"{type(exc).__name__}: {exc}"
+            if sid not in self.router.sessions:
+                return {"task": task, "error": err or "agent made no request"}
+            smp = client.close()
+            smp["task"] = task
+            if err:
+                smp["error"] = err
+            return smp
+
+        with ThreadPoolExecutor(self.workers, thread_name_prefix="session-agent") as ex:
+            return list(ex.map(one, enumerate(tasks)))
 
 
 def build_agent_loop(cfg, vocab_size: int, tokenizer=None):

@@ -19,6 +19,7 @@ Reference: ``psrl/workers/gen/session_router.py:36-360``.
 
 from __future__ import annotations
 
+import itertools
 import threading
 from dataclasses import asdict, dataclass, field
 
@@ -115,3 +116,52 @@ class SessionRouter:
             return self.states()
 
         return api
+
+
+def engine_generate_fn(engines: list, temperature: float = 1.0):
+    """A ``generate_fn`` for :class:`SessionRouter` over this framework's
+    rollout engines: a session sticks to the engine that served its first
+    turn (its KV prefix stays there), new sessions go round-robin, and each
+    request carries the session's pinned version tag (the engine's current
+    weight version for a first turn).  One lock per engine; the calling
+    thread steps the engine until its request finishes."""
+    from .engine import GenRequest, SamplingParams
+    locks = [threading.Lock() for _ in engines]
+    rr = itertools.count()
+    ids = itertools.count(1 << 41)
+
+    def generate(prompt_ids, max_tokens, version_tag, instance_hint):
+        k = int(instance_hint[0]) if instance_hint is not None else next(rr) % len(engines)
+        eng = engines[k]
+        rid = next(ids)
+        with locks[k]:
+            tag = int(version_tag) if version_tag is not None and version_tag >= 0 else int(eng.version)
+            params = SamplingParams(temperature=temperature, max_tokens=int(max_tokens), seed=rid & 0xFFFFF)
+            eng.add_request(GenRequest(rid, list(prompt_ids), params, tag, {}))
+            while True:
+                for o in eng.step():
+                    if o.request_id == rid:
+                        return list(o.output_ids), list(o.logprobs), list(o.versions), tag, (k, 0)
+                if not eng.has_unfinished():
+                    raise RuntimeError("engine dropped the session request")
+
+    return generate
+
+
+class LocalSessionClient:
+    """In-process client of one session (what an external agent would do
+    over HTTP): ``complete(prompt_ids, max_tokens)`` returns the output ids,
+    ``close()`` the session's TITO training sample."""
+
+    def __init__(self, router: SessionRouter, sid: str):
+        self.router = router
+        self.sid = sid
+
+    def complete(self, prompt_ids: list[int], max_tokens: int) -> list[int]:
+        r = self.router.complete(self.sid, list(prompt_ids), int(max_tokens))
+        if "error" in r:
+            raise RuntimeError(r["error"])
+        return list(r["output_ids"])
+
+    def close(self) -> dict:
+        return self.router.close(self.sid)

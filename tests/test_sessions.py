@@ -31,3 +31,38 @@ def test_thunder_agent_hang_and_continue():
           SessionInfo("d", 300, "hung")]
     hang, cont = sch.decide(ss)
     assert hang == [] and cont == ["b"]               # best fit decreasing: 500 fits 600 free
+
+
+def test_session_agent_loop_on_engines():
+    import torch
+
+    from psrl_b200.agent.loops import SessionAgentLoop
+    from psrl_b200.models import PRESETS, build_model
+    from psrl_b200.rollout import EngineWeights, RolloutEngine
+    from psrl_b200.rollout.session_router import engine_generate_fn
+    a = PRESETS["tiny"]
+    engines = []
+    for v in (4, 5):
+        m = build_model(a, "cpu", torch.float32, seed=v)
+        e = RolloutEngine(a, EngineWeights.from_model(m, "cpu", torch.float32), max_num_seqs=4, max_model_len=512,
+                          block_size=16, kv_cache_gb=0.05, use_cuda_graph=False)
+        e.version = v
+        engines.append(e)
+    router = SessionRouter(engine_generate_fn(engines))
+
+    def agent(client, task):
+        ctx = list(task["prompt"])
+        for turn in range(3):
+            out = client.complete(ctx, 4)
+            ctx = ctx + out + [9, 9]          # tool observation between turns
+        if task.get("fail"):
+            raise ValueError("agent crashed")
+
+    loop = SessionAgentLoop(router, agent, workers=3)
+    res = loop.run([{"prompt": [5, 6, 7]}, {"prompt": [8, 8]}, {"prompt": [3], "fail": True}])
+    assert len(res) == 3 and not router.sessions
+    for r in res:
+        assert len(r["response_ids"]) == 3 * 4 + 2 * 2
+        assert r["response_mask"] == [1] * 4 + [0, 0] + [1] * 4 + [0, 0] + [1] * 4
+        assert r["version_tag"] in (4, 5)           # pinned to the first turn's engine version
+    assert res[2]["error"].startswith("ValueError")
