@@ -103,6 +103,30 @@ def validate_config(cfg: ConfigNode) -> None:
     if rs not in ("random", "round_robin", "request_num_balance", "throughput_optimal",
                   "throughput_optimal_with_budget", "cache_aware", "cache_aware_v1"):
         raise ConfigError(f"unknown routing_strategy.method {rs!r}")
+    alg = cfg.algorithm
+    if alg.get("use_kl_in_reward"):
+        if str(alg.get("kl_penalty", "kl")) not in ("kl", "k1", "abs", "mse", "k2", "low_var_kl", "k3"):
+            raise ConfigError(f"unknown algorithm.kl_penalty {alg.kl_penalty!r}")
+        kc = alg.get("kl_ctrl") or {}
+        if str(kc.get("type", "fixed")) not in ("fixed", "adaptive"):
+            raise ConfigError("algorithm.kl_ctrl.type must be fixed|adaptive")
+        if str(kc.get("type", "fixed")) == "adaptive" and float(kc.get("target_kl", 0.1)) <= 0:
+            raise ConfigError("algorithm.kl_ctrl.target_kl must be > 0")
+    rc = alg.get("rollout_correction") or {}
+    if rc.get("rollout_is") not in (None, "token", "sequence"):
+        raise ConfigError("algorithm.rollout_correction.rollout_is must be null|token|sequence")
+    if rc.get("rollout_rs") not in (None, "token", "sequence", "geometric"):
+        raise ConfigError("algorithm.rollout_correction.rollout_rs must be null|token|sequence|geometric")
+    d = cfg.data
+    if d.kind in ("parquet", "jsonl", "files") and not d.get("train_files"):
+        raise ConfigError(f"data.kind={d.kind} needs data.train_files")
+    r = cfg.reward
+    g = r.get("gen_rm") or {}
+    if r.kind == "gen" and g.get("backend") == "http" and not g.get("url"):
+        raise ConfigError("reward.gen_rm.backend=http needs reward.gen_rm.url")
+    env = str(p.agentic_rl.get("env", "synthetic_tokens"))
+    if env not in ("synthetic_tokens", "shell_env", "tool_env"):
+        raise ConfigError(f"unknown psrl.agentic_rl.env {env!r}")
 
 
 __all__ = [

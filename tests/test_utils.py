@@ -109,3 +109,16 @@ def test_remove_containers_by_label_with_fake_docker():
     assert remove_containers_by_label("psrl=episode", run=run) == 2
     assert calls[0][:4] == ["docker", "ps", "-aq", "--filter"] and calls[0][4] == "label=psrl=episode"
     assert calls[1] == ["docker", "rm", "-f", "abc123", "def456"]
+
+
+def test_config_validation_of_new_groups():
+    import pytest
+
+    from psrl_b200.config import ConfigError, load_config
+    for bad in (["algorithm.use_kl_in_reward=true", "algorithm.kl_ctrl.type=pid"],
+                ["algorithm.rollout_correction.rollout_rs=banana"],
+                ["data.kind=parquet"],
+                ["reward.kind=gen", "reward.gen_rm.backend=http"],
+                ["psrl.agentic_rl.env=moon"]):
+        with pytest.raises(ConfigError):
+            load_config(preset="cpu_tiny_grpo", overrides=bad)
