@@ -31,8 +31,7 @@ from __future__ import annotations
 import itertools
 import re
 import threading
-from concurrent.futures import ProcessPoolExecutor
-from concurrent.futures import TimeoutError as FutureTimeout
+from multiprocessing import TimeoutError as mp_TimeoutError
 from typing import Callable
 
 # ------------------------------------------------------------------ scoring
@@ -105,30 +104,45 @@ def _inputs(ctx, traj) -> tuple:
 
 class ProcessScorer:
     """Scores in worker processes with a per-sample timeout (the scorer must
-    be importable by name, i.e. a module-level function)."""
+    be importable by name, i.e. a module-level function).  A timed-out
+    scorer may never return, so its pool is terminated and replaced: a stuck
+    worker neither blocks later samples nor the process's exit."""
 
     def __init__(self, fn: Callable, num_processes: int, timeout_s: float):
         self.fn = fn
         self.timeout = float(timeout_s)
+        self.n = max(1, int(num_processes))
+        self.stats = {"timeouts": 0, "errors": 0}
+        self.lock = threading.Lock()
+        self.pool = self._new_pool()
+
+    def _new_pool(self):
         # spawned workers: the scoring process is multi-threaded (fork would copy held locks)
         import multiprocessing as mp
-        self.pool = ProcessPoolExecutor(max_workers=max(1, int(num_processes)), mp_context=mp.get_context("spawn"))
-        self.stats = {"timeouts": 0, "errors": 0}
+        return mp.get_context("spawn").Pool(self.n)
 
     def __call__(self, *args) -> dict:
-        fut = self.pool.submit(self.fn, *args)
+        with self.lock:
+            pool = self.pool
+        res = pool.apply_async(self.fn, args)
         try:
-            return _as_result(fut.result(timeout=self.timeout))
-        except FutureTimeout:
-            fut.cancel()
-            self.stats["timeouts"] += 1
+            return _as_result(res.get(timeout=self.timeout))
+        except mp_TimeoutError:
+            with self.lock:
+                self.stats["timeouts"] += 1
+                if self.pool is pool:
+                    pool.terminate()
+                    self.pool = self._new_pool()
             return {"score": 0.0, "timeout": 1.0}
         except Exception:       # a failing scorer scores 0, as a timeout does
-            self.stats["errors"] += 1
+            with self.lock:
+                self.stats["errors"] += 1
             return {"score": 0.0, "error": 1.0}
 
     def close(self) -> None:
-        self.pool.shutdown(wait=False, cancel_futures=True)
+        with self.lock:
+            self.pool.terminate()
+            self.pool.join()
 
 
 def prime_loop(ctx, traj) -> dict:

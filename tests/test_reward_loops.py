@@ -56,6 +56,10 @@ def test_prime_scores_in_processes_and_times_out():
                 "reward.compute_score=tests.test_reward_loops:slow_score")
     r = slow.score(_traj("#### 42", 42))
     assert r["score"] == 0.0 and r["timeout"] == 1.0
+    scorer = slow.ctx["_prime"]
+    first_pool = scorer.pool
+    r = slow.score(_traj("#### 42", 42))            # the stuck worker was replaced
+    assert r["timeout"] == 1.0 and scorer.stats["timeouts"] == 2 and scorer.pool is not first_pool
     slow.close()
 
 
