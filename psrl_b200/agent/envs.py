@@ -114,7 +114,9 @@ class ShellTaskEnv(Environment):
     command runs with ``timeout_s``; its output is cut to ``max_obs_chars``.
     With ``docker_image`` the workspace is bind-mounted into a container that
     lives for the episode (``docker run -d`` at reset, ``docker rm -f`` at
-    close); without it commands run as local processes in the workspace."""
+    close); without it commands run as local processes of the current user
+    in the workspace, with no isolation beyond the working directory, so the
+    container backend is the one for untrusted model output."""
 
     def __init__(self, tokenizer, max_turns: int = 8, timeout_s: float = 30.0, max_obs_chars: int = 4000,
                  submit_marker: str = "COMPLETE_TASK_AND_SUBMIT", docker_image: str | None = None,
@@ -146,15 +148,23 @@ class ShellTaskEnv(Environment):
                            check=True, capture_output=True, timeout=120)
 
     def run(self, cmd: str) -> tuple[int, str]:
+        """Run one command; on timeout its whole process group is killed
+        (commands may start background children)."""
+        import signal
         argv = (["docker", "exec", "-w", "/workspace", self.container, "bash", "-lc", cmd] if self.container
                 else ["bash", "-c", cmd])
+        p = subprocess.Popen(argv, cwd=None if self.container else self.ws, stdout=subprocess.PIPE,
+                             stderr=subprocess.STDOUT, text=True, start_new_session=True)
         try:
-            p = subprocess.run(argv, cwd=None if self.container else self.ws, capture_output=True, text=True,
-                               timeout=self.timeout)
-            out, code = (p.stdout + p.stderr), p.returncode
-        except subprocess.TimeoutExpired as e:
-            out = (e.stdout or b"").decode(errors="replace") if isinstance(e.stdout, bytes) else (e.stdout or "")
-            out, code = out + f"\n[timed out after {self.timeout:g} s]", 124
+            out, _ = p.communicate(timeout=self.timeout)
+            code = p.returncode
+        except subprocess.TimeoutExpired:
+            try:
+                os.killpg(p.pid, signal.SIGKILL)
+            except ProcessLookupError:
+                pass
+            out, _ = p.communicate()
+            out, code = (out or "") + f"\n[timed out after {self.timeout:g} s]", 124
         if len(out) > self.max_obs:
             half = self.max_obs // 2
             out = out[:half] + "\n[... output truncated ...]\n" + out[-half:]
