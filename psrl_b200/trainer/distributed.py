@@ -38,7 +38,8 @@ from ..utils.rpc import RPCClient
 from . import algos
 from .actor import PolicyWorker
 from .control_plane import ExchangeMailbox, spawn_control_plane
-from .strategies import overlap_per_sample, per_sample_missing, sharded_overlap_enabled
+from .strategies import (overlap_per_sample, per_sample_missing, pre_step_train, sharded_overlap_enabled,
+                         sharded_overlap_mode)
 
 
 def log(msg: str) -> None:
@@ -160,6 +161,7 @@ class DisaggregatedRun:
                                     dp_world=self.dp_world, tp_group=self.tp_group)
         self.kl_ctrl = algos.kl_controller(cfg.algorithm) if cfg.algorithm.use_kl_in_reward else None
         self.sharded_overlap = sharded_overlap_enabled(cfg)
+        self.pre_step = sharded_overlap_mode(cfg) == "pre_step"
         mode = "hbm" if (cfg.psrl.ps_mode == "hbm" and self.device.type == "cuda") else "cpu"
         self.store = WeightStore(self.layout, self.device, mode)
         self.store.publish(self.pub_flat, 0)
@@ -179,19 +181,28 @@ class DisaggregatedRun:
                 self.cfg, self.cp, b, lambda ts: per_sample_missing(self.cfg, ts, self.actor, self.ref, self.critic),
                 group=self.train_cpu_group, src=0, dp_rank=self.dp_rank, dp_world=self.dp_world,
                 post=self.rank % self.tp_size == 0, timeout_s=self.buffer_timeout_s)
+        pre_metrics = None
+        if self.pre_step:
+            # train each committed mini-batch as it arrives; the batch below is only consumed
+            pre_metrics, chunks = pre_step_train(
+                self.cfg, self.cp, b, self.actor, self.ref, group=self.train_cpu_group, src=0, dp_rank=self.dp_rank,
+                dp_world=self.dp_world, timeout_s=self.buffer_timeout_s)
         batch = self.cp.get_batch(b, self.dp_rank, self.dp_world, self.buffer_timeout_s, self.rank % self.tp_size,
                                   self.tp_size)
         trajs, plan = batch["trajs"], batch["plan"]
         t1 = time.perf_counter()
         pre = sum(1 for t in trajs if t.ref_logprobs is not None or t.old_values is not None
                   or (t.old_logprobs is not None and t.old_logprobs is not t.rollout_logprobs))
-        per_sample_missing(self.cfg, trajs, self.actor, self.ref, self.critic)
-        critic_metrics = algos.shard_advantages(self.cfg, trajs, self.train_cpu_group, self.kl_ctrl, self.tp_size,
-                                                critic=self.critic is not None)
-        critic_metrics.update(algos.apply_rollout_correction(self.cfg.algorithm.rollout_correction, trajs))
-        if self.critic is not None:
-            critic_metrics.update(self.critic.update_critic(trajs, plan=plan))
-        metrics = self.actor.update_policy(trajs, float(self.cfg.rollout.temperature), plan=plan)
+        if pre_metrics is not None:
+            metrics, critic_metrics = dict(pre_metrics), {}
+        else:
+            per_sample_missing(self.cfg, trajs, self.actor, self.ref, self.critic)
+            critic_metrics = algos.shard_advantages(self.cfg, trajs, self.train_cpu_group, self.kl_ctrl,
+                                                    self.tp_size, critic=self.critic is not None)
+            critic_metrics.update(algos.apply_rollout_correction(self.cfg.algorithm.rollout_correction, trajs))
+            if self.critic is not None:
+                critic_metrics.update(self.critic.update_critic(trajs, plan=plan))
+            metrics = self.actor.update_policy(trajs, float(self.cfg.rollout.temperature), plan=plan)
         metrics.update(critic_metrics)
         if self.assembler is not None:
             self.assembler.gather()                  # collective over the trainer shards

@@ -49,7 +49,8 @@ from . import algos
 from .actor import PolicyWorker
 from .control_plane import ExchangeMailbox, spawn_control_plane
 from .driver import _apply_switch_interval, train_stream_ctx, trainer_stream_for
-from .strategies import overlap_per_sample, per_sample_missing, sharded_overlap_enabled
+from .strategies import (overlap_per_sample, per_sample_missing, pre_step_train, sharded_overlap_enabled,
+                         sharded_overlap_mode)
 
 
 def log(msg: str) -> None:
@@ -145,6 +146,7 @@ class HybridRun:
                                     dp_rank=self.dp_rank, dp_world=self.dp_world, tp_group=tp_group)
         self.kl_ctrl = algos.kl_controller(cfg.algorithm) if cfg.algorithm.use_kl_in_reward else None
         self.sharded_overlap = sharded_overlap_enabled(cfg)
+        self.pre_step = sharded_overlap_mode(cfg) == "pre_step"
         self.wlock = RWLock()
         self.eng_sources = None
         if self.eng_tp is not None:
@@ -334,6 +336,14 @@ class HybridRun:
                     self.cfg, self.cp, b, lambda ts: per_sample_missing(self.cfg, ts, self.actor, self.ref, self.critic),
                     group=self.cpu_group, src=0, dp_rank=self.dp_rank, dp_world=self.dp_world,
                     post=self.rank % self.tp_size == 0, timeout_s=self.buffer_timeout_s)
+        pre_metrics = None
+        if self.pre_step:
+            # train each committed mini-batch as it arrives; the batch below is only consumed
+            with train_stream_ctx(self.train_stream):
+                pre_metrics, chunks = pre_step_train(
+                    self.cfg, self.cp, b, self.actor, self.ref, group=self.cpu_group, src=0, dp_rank=self.dp_rank,
+                    dp_world=self.dp_world, step_guard=lambda: self.wlock.exclusive(600),
+                    sync_every_micro_batch=self.is_cuda, timeout_s=self.buffer_timeout_s)
         batch = self.cp.get_batch(b, self.dp_rank, self.dp_world, self.buffer_timeout_s, self.rank % self.tp_size,
                                   self.tp_size)
         trajs, plan = batch["trajs"], batch["plan"]
@@ -341,15 +351,18 @@ class HybridRun:
         pre = sum(1 for t in trajs if t.ref_logprobs is not None or t.old_values is not None
                   or (t.old_logprobs is not None and t.old_logprobs is not t.rollout_logprobs))
         with train_stream_ctx(self.train_stream):
-            per_sample_missing(self.cfg, trajs, self.actor, self.ref, self.critic)
-            critic_metrics = algos.shard_advantages(self.cfg, trajs, self.cpu_group, self.kl_ctrl, self.tp_size,
-                                                    critic=self.critic is not None)
-            critic_metrics.update(algos.apply_rollout_correction(self.cfg.algorithm.rollout_correction, trajs))
-            if self.critic is not None:
-                critic_metrics.update(self.critic.update_critic(trajs, plan=plan))
-            metrics = self.actor.update_policy(trajs, float(self.cfg.rollout.temperature),
-                                               step_guard=lambda: self.wlock.exclusive(600),
-                                               sync_every_micro_batch=self.is_cuda, plan=plan)
+            if pre_metrics is not None:
+                metrics, critic_metrics = dict(pre_metrics), {}
+            else:
+                per_sample_missing(self.cfg, trajs, self.actor, self.ref, self.critic)
+                critic_metrics = algos.shard_advantages(self.cfg, trajs, self.cpu_group, self.kl_ctrl, self.tp_size,
+                                                        critic=self.critic is not None)
+                critic_metrics.update(algos.apply_rollout_correction(self.cfg.algorithm.rollout_correction, trajs))
+                if self.critic is not None:
+                    critic_metrics.update(self.critic.update_critic(trajs, plan=plan))
+                metrics = self.actor.update_policy(trajs, float(self.cfg.rollout.temperature),
+                                                   step_guard=lambda: self.wlock.exclusive(600),
+                                                   sync_every_micro_batch=self.is_cuda, plan=plan)
             if self.assembler is not None:
                 # all ranks: gather the sharded weights for the full-model engines
                 with self.wlock.exclusive(600):

@@ -160,14 +160,86 @@ def per_sample_missing(cfg, trajs, actor, ref=None, critic=None) -> None:
         critic.compute_values(trajs, [i for i, t in enumerate(trajs) if t.old_values is None])
 
 
-def sharded_overlap_enabled(cfg) -> bool:
+def sharded_overlap_mode(cfg) -> str | None:
+    """None, ``"recompute"`` or ``"pre_step"`` for the multi-GPU placements.
+    ``pre_step`` trains each mini-batch as soon as it is committed, so it
+    needs ``mini_batch`` granularity and batch-free advantages: no critic
+    and no in-reward KL (both need the whole batch's statistics)."""
     fgo = cfg.psrl.fine_grain_overlap
     if fgo.granularity == "none":
-        return False
-    if fgo.overlap_scope != "recompute":
-        raise ValueError("the multi-GPU placements overlap the per-sample stages only "
-                         "(psrl.fine_grain_overlap.overlap_scope=recompute); pre_step runs colocated")
-    return True
+        return None
+    if fgo.overlap_scope == "pre_step":
+        if fgo.granularity != "mini_batch":
+            raise ValueError("pre_step overlap needs psrl.fine_grain_overlap.granularity=mini_batch")
+        if cfg.critic.enable or cfg.algorithm.get("use_kl_in_reward"):
+            raise ValueError("pre_step overlap in the multi-GPU placements takes outcome estimators without "
+                             "a critic or in-reward KL")
+        return "pre_step"
+    return "recompute"
+
+
+def pre_step_train(cfg, cp, b: int, actor, ref=None, *, group=None, src: int = 0, dp_rank: int = 0,
+                   dp_world: int = 1, step_guard=None, sync_every_micro_batch: bool = False,
+                   poll_s: float = 0.01, timeout_s: float = 1800.0) -> tuple[dict, int]:
+    """``overlap_scope=pre_step`` in the multi-GPU placements: each committed
+    mini-batch of buffer ``b`` is trained (one optimizer step) as soon as it
+    arrives, while the rest of the buffer is still being generated.
+
+    Every trainer rank takes the same chunk (rank ``src`` broadcasts the
+    buffer's progress over ``group``) and computes its advantages over the
+    whole chunk (the chunk holds complete prompt groups); the chunk is split
+    into token-balanced data-parallel shares as a full batch would be, and
+    each rank computes the per-sample stages and the update on its share.
+    The caller consumes the buffer afterwards (its batch is not trained
+    again).  Returns (averaged actor metrics, chunks)."""
+    import torch.distributed as dist
+
+    from .actor import plan_update
+    from .driver import compute_batch_advantages
+    _, chunk = resolve_fine_grain_chunk_size(cfg)
+    use_rl = bool(cfg.psrl.log_prob.enable_rollout_engine_log_prob)
+    sums: dict = {}
+    t0 = time.monotonic()
+    done = chunks = 0
+    while True:
+        lead = group is None or dist.get_rank() == src
+        msg = [cp.progress(b) if lead else None]
+        if group is not None:
+            dist.broadcast_object_list(msg, src=src, group=group)
+        avail, ready, _need = msg[0]
+        if avail - done >= chunk or (ready and avail > done):
+            hi = min(int(avail), done + chunk)
+            trajs = cp.peek_chunk(b, done, hi)
+            for t in trajs:
+                t.old_logprobs = t.rollout_logprobs if use_rl else None
+            adv_m = compute_batch_advantages(cfg, trajs)
+            plans = plan_update(trajs, len(trajs) + 1, dp_world)
+            need = sorted({i for mine, _, _ in plans[dp_rank] for i in mine})
+            local = {g: j for j, g in enumerate(need)}
+            mine = [trajs[i] for i in need]
+            plan = [([local[i] for i in idx], gt, ns) for idx, gt, ns in plans[dp_rank]]
+            per_sample_missing(cfg, mine, actor, ref, None)
+            m = dict(adv_m)
+            m.update(algos.apply_rollout_correction(cfg.algorithm.rollout_correction, mine))
+            m.update(actor.update_policy(mine, float(cfg.rollout.temperature), step_guard=step_guard,
+                                         sync_every_micro_batch=sync_every_micro_batch, plan=plan))
+            for k, v in m.items():
+                sums.setdefault(k, []).append(float(v))
+            done = hi
+            chunks += 1
+            t0 = time.monotonic()
+        elif ready:
+            if group is not None:
+                dist.barrier(group=group)
+            return {k: sum(v) / len(v) for k, v in sums.items()}, chunks
+        else:
+            if time.monotonic() - t0 > timeout_s:
+                raise TimeoutError(f"buffer {b}: no progress for the pre_step overlap")
+            time.sleep(poll_s)
+
+
+def sharded_overlap_enabled(cfg) -> bool:
+    return sharded_overlap_mode(cfg) == "recompute"
 
 
 def overlap_per_sample(cfg, cp, b: int, compute, *, group=None, src: int = 0, dp_rank: int = 0, dp_world: int = 1,

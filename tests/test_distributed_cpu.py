@@ -285,6 +285,18 @@ def test_gloo_world2_hybrid_fine_grain_per_sample_overlap():
     assert abs(res[0]["engine"] - res[1]["engine"]) < 1e-6 * max(1.0, abs(res[0]["engine"]))
 
 
+def test_gloo_world2_hybrid_pre_step_overlap():
+    """Each committed mini-batch is trained (its own optimizer step) while
+    the buffer fills, with trainer-side old log-probs; both engines end with
+    the same weights."""
+    res = _run_sharded(["psrl.log_prob.enable_rollout_engine_log_prob=false",
+                        "psrl.fine_grain_overlap.granularity=mini_batch", "psrl.fine_grain_overlap.overlap_scope=pre_step",
+                        "actor.ppo_mini_batch_size=4", "psrl.staleness_buffer_entries=8"])
+    assert res[0]["steps"] == [32, 32]
+    assert all(c is not None and c >= 2 for c in res[0]["chunks"]), res[0]["chunks"]
+    assert abs(res[0]["engine"] - res[1]["engine"]) < 1e-6 * max(1.0, abs(res[0]["engine"]))
+
+
 def test_gloo_world2_hybrid_tensor_parallel():
     """Dense trainer at TP=2 (one data-parallel rank); both engines hold the
     assembled full weights."""
@@ -308,7 +320,8 @@ def _worker_disagg_sharded(rank, world, port, q, overrides):
     if rank == 0:
         q.put({"steps": [m["num_trajectories"] for m in res["metrics"]], "pulls": res["sync"]["pulls"],
                "pre": [m.get("fine_grain/precomputed") for m in res["metrics"]],
-               "kl": [m.get("actor/reward_kl_penalty") for m in res["metrics"]]})
+               "kl": [m.get("actor/reward_kl_penalty") for m in res["metrics"]],
+               "chunks": [m.get("fine_grain/chunks") for m in res["metrics"]]})
     import torch.distributed as dist
     dist.destroy_process_group()
 
@@ -375,6 +388,39 @@ def test_gloo_world3_disaggregated_critic_kl_in_reward_fine_grain():
     assert res["steps"] == [32, 32]
     assert all(p is not None and p > 0 for p in res["pre"]), res
     assert all(k is not None for k in res["kl"]), res
+
+
+def test_gloo_world3_disaggregated_pre_step_overlap():
+    """Two trainer ranks train each committed mini-batch while the rollout
+    rank keeps filling the buffer."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ov = ["psrl.fine_grain_overlap.granularity=mini_batch", "psrl.fine_grain_overlap.overlap_scope=pre_step",
+          "actor.ppo_mini_batch_size=4"]
+    procs = [ctx.Process(target=_worker_disagg_sharded, args=(r, 3, port, q, ov)) for r in range(3)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(900)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0, 0], codes
+    res = q.get(timeout=5)
+    assert res["steps"] == [32, 32] and all(c == 2 for c in res["chunks"]), res
+
+
+def test_multi_gpu_pre_step_rejects_batch_statistics():
+    import pytest
+
+    from psrl_b200.config import load_config
+    from psrl_b200.trainer.strategies import sharded_overlap_mode
+    base = ["psrl.fine_grain_overlap.granularity=mini_batch", "psrl.fine_grain_overlap.overlap_scope=pre_step"]
+    assert sharded_overlap_mode(load_config(preset="cpu_tiny_grpo", overrides=base)) == "pre_step"
+    with pytest.raises(ValueError):
+        sharded_overlap_mode(load_config(preset="cpu_tiny_grpo", overrides=base + ["algorithm.use_kl_in_reward=true"]))
 
 
 def test_gloo_world2_hybrid_multiturn_agentic():
