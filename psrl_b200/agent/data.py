@@ -15,7 +15,7 @@ reference's row layout: ``prompt`` (chat messages or a string),
 chat template (``data.tokenizer``: an HF tokenizer directory; the byte-level
 tokenizer with ChatML otherwise); rows longer than
 ``rollout.max_prompt_length`` are dropped at load time.  Each epoch visits
-the rows in a fresh seeded permutation.
+the rows in a fresh seeded permutation (file order with ``data.shuffle=false``).
 
 ``DataProcessor`` hands out prompt *groups* (``rollout_n`` samples share a
 ``uid`` / parent id), is seeded, and can save/load its cursor for resume
@@ -131,9 +131,11 @@ def _read_rows(path: str) -> list[dict]:
 class FileSource:
     """Prompt rows from parquet / jsonl files (reference row layout)."""
 
-    def __init__(self, files, tokenizer, max_prompt_len: int, seed: int, filter_overlong: bool = True):
+    def __init__(self, files, tokenizer, max_prompt_len: int, seed: int, filter_overlong: bool = True,
+                 shuffle: bool = True):
         from ..utils.common import apply_chat_template
         self.tok = tokenizer
+        self.shuffle = bool(shuffle)
         self.seed = int(seed)
         self.vocab = getattr(tokenizer, "vocab_size", 1024)
         self.items: list[tuple[list[int], dict]] = []
@@ -168,7 +170,8 @@ class FileSource:
             return PromptItem(uid, list(ids), None, None, dict(meta))
         epoch, k = divmod(int(uid), n)
         if epoch != self._perm_epoch:
-            self._perm = np.random.default_rng([self.seed, epoch]).permutation(n).tolist()
+            self._perm = (np.random.default_rng([self.seed, epoch]).permutation(n).tolist() if self.shuffle
+                          else list(range(n)))
             self._perm_epoch = epoch
         ids, meta = self.items[self._perm[k]]
         return PromptItem(uid, list(ids), None, None, dict(meta))
@@ -192,7 +195,7 @@ class DataProcessor:
             self.src = AdditionSource(self.tokenizer, int(d.seed))
         elif d.kind in ("parquet", "jsonl", "files"):
             self.src = FileSource(d.train_files, self.tokenizer, int(cfg.rollout.max_prompt_length), int(d.seed),
-                                  bool(d.get("filter_overlong_prompts", True)))
+                                  bool(d.get("filter_overlong_prompts", True)), bool(d.get("shuffle", True)))
             if d.get("val_files"):
                 self.val_src = FileSource(d.val_files, self.tokenizer, int(cfg.rollout.max_prompt_length),
                                           int(d.seed), bool(d.get("filter_overlong_prompts", True)))

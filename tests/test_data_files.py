@@ -67,3 +67,10 @@ def test_training_on_a_parquet_dataset(tmp_path):
     out = t.fit(1)
     t.stop_rollout()
     assert out[0]["num_trajectories"] == 32
+
+
+def test_unshuffled_file_order(tmp_path):
+    cfg = _cfg(tmp_path, "jsonl", None, "data.shuffle=false")
+    dp = DataProcessor(cfg, 1024, 2)
+    got = [dp.next_group().meta["extra_info"]["index"] for _ in range(8)]
+    assert got == [0, 1, 2, 3, 4, 5, 0, 1]
