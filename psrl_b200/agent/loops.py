@@ -148,6 +148,25 @@ class SessionAgentLoop:
         with ThreadPoolExecutor(self.workers, thread_name_prefix="session-agent") as ex:
             return list(ex.map(one, enumerate(tasks)))
 
+    @staticmethod
+    def to_trajectories(samples: list[dict], uid: int, request_id_base: int = 0) -> list:
+        """Trajectories of one prompt group (``uid``) from finished session
+        samples (failed sessions are skipped); ``reward`` is taken from the
+        task's ``reward`` field when the agent left one there."""
+        from ..trainer.batch import Trajectory
+        out = []
+        for j, smp in enumerate(samples):
+            if "response_ids" not in smp or smp.get("error"):
+                continue
+            task = smp.get("task") or {}
+            out.append(Trajectory(uid=uid, request_id=request_id_base + j, prompt_ids=list(smp["prompt_ids"]),
+                                  response_ids=list(smp["response_ids"]),
+                                  rollout_logprobs=list(smp["rollout_logprobs"]), reward=float(task.get("reward", 0.0)),
+                                  versions=list(smp.get("versions") or []), version_tag=int(smp["version_tag"]),
+                                  response_mask=list(smp["response_mask"]),
+                                  meta={k: v for k, v in task.items() if k != "reward"}))
+        return out
+
 
 def build_agent_loop(cfg, vocab_size: int, tokenizer=None):
     """``psrl.agentic_rl.env`` picks the environment of multi-turn episodes:

@@ -66,3 +66,7 @@ def test_session_agent_loop_on_engines():
         assert r["response_mask"] == [1] * 4 + [0, 0] + [1] * 4 + [0, 0] + [1] * 4
         assert r["version_tag"] in (4, 5)           # pinned to the first turn's engine version
     assert res[2]["error"].startswith("ValueError")
+
+    trajs = SessionAgentLoop.to_trajectories(res, uid=3, request_id_base=30)
+    assert len(trajs) == 2 and [t.request_id for t in trajs] == [30, 31]
+    assert all(t.uid == 3 and t.response_len == 16 and len(t.rollout_logprobs) == 16 for t in trajs)
