@@ -54,23 +54,10 @@ def reference_arm(args) -> None:
         print(json.dumps({"impl": "reference", "metric": METRIC, "unavailable": why or "unknown"}), flush=True)
 
 
-def build_cfg(args, n_gpus: int):
-    from psrl_b200.config import load_config
-    per_gpu = args.prompts_per_gpu
-    ov = [
-        f"psrl.staleness_buffer_entries={per_gpu * n_gpus}",
-        "trainer.device=cuda",
-        f"rollout.max_num_seqs={args.max_num_seqs}",
-        f"++rollout.kv_cache_gb={args.kv_cache_gb}",
-        "rollout.block_size=64",
-        f"model.enable_gradient_checkpointing={'true' if args.recompute else 'false'}",
-    ] + list(args.override)
-    return load_config(preset=args.preset, overrides=ov)
-
-
 def run_colocated(args) -> dict:
     import torch
 
+    from psrl_b200.bench.rl_bench import build_cfg
     from psrl_b200.ops import _ext
     from psrl_b200.trainer import RLTrainer
     from psrl_b200.utils import transfer
@@ -104,7 +91,9 @@ def run_colocated(args) -> dict:
     return {
         "ms": ms, "wall_s": wall, "tokens": tokens, "launches": _ext.launches() - l0, "clocks": clocks,
         "h2d": (b1 - b0) / args.steps, "d2h": (o1 - o0) / args.steps, "metrics": metrics,
-        "global_batch": cfg.psrl.staleness_buffer_entries * cfg.psrl.rollout_n, "parallelism": "colocated-1gpu",
+        "prompts_per_step": cfg.psrl.staleness_buffer_entries,
+        "trajectories_per_step": cfg.psrl.staleness_buffer_entries * cfg.psrl.rollout_n,
+        "parallelism": "colocated-1gpu", "api": "RLTrainer.step",
         "sync": {"pulls": int(t.instance.sync_count), "pull_s": float(t.instance.sync_time),
                  "path": "in-HBM copy trainer -> engine weights (same GPU)"},
     }
@@ -122,6 +111,14 @@ def _sync_summary(res: dict) -> dict | None:
     return out
 
 
+def _breakdown(metrics: list) -> dict:
+    """Mean per timed step of every stage timer (``timing_s/*``) the trainer
+    reports: waiting for generation, log-prob passes, the update, the push."""
+    keys = sorted({k for m in metrics for k in m if k.startswith("timing_s/")})
+    return {k.split("/", 1)[1]: round(sum(float(m.get(k, 0.0)) for m in metrics) / max(1, len(metrics)), 3)
+            for k in keys}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -137,7 +134,11 @@ def main():
                          "10k-token micro-batch fit in HBM next to the KV cache)")
     ap.add_argument("--override", action="append", default=[])
     ap.add_argument("--placement", default="auto", choices=["auto", "colocated", "hybrid", "disaggregated"],
-                    help="auto: colocated on one GPU, hybrid (every GPU trains and serves rollout) on several")
+                    help="auto: colocated on one GPU; on several, disaggregated (half the GPUs train with "
+                         "sharded data parallelism, half serve rollout), the 4 + 4 split of the 8-GPU "
+                         "DAPO recipe")
+    ap.add_argument("--stack-dump-s", type=float, default=0.0,
+                    help="print every thread's stack each this many seconds (debugging stalls; 0 = off)")
     ap.add_argument("--verbose", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -146,11 +147,12 @@ def main():
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     world = int(os.environ.get("WORLD_SIZE", 1))
-    import faulthandler
-    faulthandler.dump_traceback_later(240, repeat=True)   # all-thread stacks if a run stalls
+    if args.stack_dump_s > 0:
+        import faulthandler
+        faulthandler.dump_traceback_later(args.stack_dump_s, repeat=True)
     placement = args.placement
     if placement == "auto":
-        placement = "hybrid" if (args.gpus > 1 or world > 1) else "colocated"
+        placement = "disaggregated" if (args.gpus > 1 or world > 1) else "colocated"
     if placement != "colocated":
         from psrl_b200.trainer.distributed import run_disaggregated_bench
         res = run_disaggregated_bench(args, placement)
@@ -180,16 +182,19 @@ def main():
         "config": {
             "model": "Qwen2.5-3B architecture (36L, h2048, 16Q/2KV, I11008, V151936)",
             "algorithm": "DAPO, staleness=3, 8 responses/prompt",
-            "global_batch": res["global_batch"],
+            "global_batch": res["prompts_per_step"],
+            "prompts_per_step": res["prompts_per_step"],
+            "trajectories_per_step": res["trajectories_per_step"],
             "seq_len": "prompt U[64,512] + response lognormal(7.0,0.8) cap 8192",
             "parallelism": res["parallelism"],
             "l2": "inputs larger than L2 (weights 6.2 GB, KV cache tens of GB)",
             "activation_recompute": bool(args.recompute),
         },
         "clocks": res["clocks"],
-        "e2e": {"value": round(e2e, 1), "unit": "trained tokens/s (wall clock, public API RLTrainer.step)",
+        "e2e": {"value": round(e2e, 1), "unit": f"trained tokens/s (wall clock, public API {res['api']})",
                 "h2d_bytes_per_step": int(res["h2d"]), "d2h_bytes_per_step": int(res["d2h"])},
         "gpu_launches": int(res["launches"]),
+        "breakdown_s_per_step": _breakdown(res["metrics"]),
         "weight_sync": _sync_summary(res),
     }
     print(json.dumps(line), flush=True)

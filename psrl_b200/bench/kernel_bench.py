@@ -78,17 +78,38 @@ def bench_decode(pk):
 
 
 def bench_gemm(pk):
-    from psrl_b200.ops.gemm import tc_linear
+    """Projection GEMMs of a Qwen2.5-3B training micro-batch (10240 tokens):
+    the paired-CTA tcgen05 kernel in all three roles (forward x W^T, data
+    gradient dy W, weight gradient dy^T x) against cuBLAS through torch on the
+    same operands, plus the fused gate_up + SwiGLU epilogue."""
+    from psrl_b200.ops import ext
+    from psrl_b200.ops.gemm import check_errors
+    from psrl_b200.ops.linear import gate_up_swiglu, matmul_nt, weight_grad
     out = []
-    for M, N, K in ((10240, 2560, 2048), (10240, 22016, 2048), (10240, 2048, 11008), (8192, 151936, 2048)):
+    M = 10240
+    for name, N, K in (("qkv", 2560, 2048), ("o", 2048, 2048), ("gate_up", 22016, 2048), ("down", 2048, 11008)):
         x = torch.randn(M, K, device="cuda").bfloat16()
-        w = torch.randn(N, K, device="cuda").bfloat16()
+        w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+        dy = torch.randn(M, N, device="cuda").bfloat16()
         fl = 2.0 * M * N * K
-        ms_tc = timeit(lambda: tc_linear(x, w), iters=10)
-        ms_cb = timeit(lambda: x @ w.t(), iters=10)
-        out.append({"case": f"gemm {M}x{N}x{K}", "tcgen05_ms": round(ms_tc, 3), "cublas_ms": round(ms_cb, 3),
-                    "tcgen05_tflops": round(fl / ms_tc / 1e9, 1), "cublas_tflops": round(fl / ms_cb / 1e9, 1),
-                    "frac_peak_tcgen05": round(fl / ms_tc / 1e9 / pk["bf16_tflops"], 3)})
+        rows = {}
+        for role, tc, cb in (("fwd", lambda: matmul_nt(x, w), lambda: x @ w.t()),
+                             ("dgrad", lambda: matmul_nt(dy, w, b_mn=True), lambda: dy @ w),
+                             ("wgrad", lambda: weight_grad(dy, x), lambda: dy.t() @ x)):
+            ms_tc = timeit(tc, iters=10)
+            ms_cb = timeit(cb, iters=10)
+            rows[role] = {"tcgen05_ms": round(ms_tc, 3), "cublas_ms": round(ms_cb, 3),
+                          "tcgen05_tflops": round(fl / ms_tc / 1e9, 1), "cublas_tflops": round(fl / ms_cb / 1e9, 1),
+                          "frac_peak_tcgen05": round(fl / ms_tc / 1e9 / pk["bf16_tflops"], 3),
+                          "vs_cublas": round(ms_cb / ms_tc, 3)}
+        if name == "gate_up":
+            ms_f = timeit(lambda: gate_up_swiglu(x, w), iters=10)
+            ms_u = timeit(lambda: ext().swiglu_fwd(x @ w.t()), iters=10)
+            rows["fwd+swiglu"] = {"fused_ms": round(ms_f, 3), "cublas_then_swiglu_ms": round(ms_u, 3),
+                                  "vs_unfused": round(ms_u / ms_f, 3)}
+        check_errors()
+        out.append({"case": f"{name} M={M} N={N} K={K}", **rows})
+        del x, w, dy
     return out
 
 

@@ -898,11 +898,7 @@ std::vector<at::Tensor> attn_varlen_fwd(at::Tensor q, at::Tensor k, at::Tensor v
   p.nkv = nkv;
   p.scale = scale;
   const size_t sm = fwd_smem();
-  static bool attr = false;
-  if (!attr) {
-    PSRL_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
-    attr = true;
-  }
+  ensure_smem_attr(attn_fwd_kernel<false>, (int)sm);
   dim3 grid((max_seqlen + BM - 1) / BM, nq, B);
   attn_fwd_kernel<false><<<grid, NTHREADS, sm, stream()>>>(p);
   PSRL_CHECK_LAUNCH();
@@ -939,11 +935,7 @@ at::Tensor attn_paged_prefill(at::Tensor q, at::Tensor k_cache, at::Tensor v_cac
   p.nkv = nkv;
   p.scale = scale;
   const size_t sm = fwd_smem();
-  static bool attr = false;
-  if (!attr) {
-    PSRL_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
-    attr = true;
-  }
+  ensure_smem_attr(attn_fwd_kernel<true>, (int)sm);
   dim3 grid((max_q_len + BM - 1) / BM, nq, B);
   attn_fwd_kernel<true><<<grid, NTHREADS, sm, stream()>>>(p);
   PSRL_CHECK_LAUNCH();
@@ -1000,11 +992,7 @@ std::vector<at::Tensor> attn_varlen_bwd(at::Tensor dO, at::Tensor q, at::Tensor 
   bp.T = T;
   bp.B = B;
   const size_t sm = bwd_smem();
-  static bool attr = false;
-  if (!attr) {
-    PSRL_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
-    attr = true;
-  }
+  ensure_smem_attr(attn_bwd_kernel, (int)sm);
   const int64_t nblk = (int64_t)((max_seqlen + BN - 1) / BN) * BWD_HSPLIT * nkv * B;
   attn_bwd_kernel<<<(unsigned)nblk, NTHREADS, sm, stream()>>>(bp);
   PSRL_CHECK_LAUNCH();
@@ -1069,12 +1057,7 @@ at::Tensor attn_decode(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at:
   // rollout shapes) or 2 stages x 3 CTAs/SM (stages == 2)
   const int st = stages == 2 ? 2 : 3;
   const size_t sm = dec_smem(st);
-  static bool attr[2] = {false, false};
-  if (!attr[st == 3]) {
-    PSRL_CHECK_CUDA(cudaFuncSetAttribute(st == 3 ? decode_kernel_s3 : decode_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
-    attr[st == 3] = true;
-  }
+  ensure_smem_attr(st == 3 ? decode_kernel_s3 : decode_kernel, (int)sm);
   dim3 grid(B, nkv, splits);
   if (st == 3)
     decode_kernel_s3<<<grid, NTHREADS, sm, stream()>>>(p);
@@ -1118,7 +1101,7 @@ static int noalloc_setup(int dev, float** out) {
   if (g_noalloc_ptr[dev] == nullptr) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return PSRL_NOALLOC_ECUDA;
-    if (cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dec_smem()) !=
+    if (cudaFuncSetAttribute(decode_kernel_s3, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dec_smem(3)) !=
         cudaSuccess)
       return PSRL_NOALLOC_ECUDA;
     g_noalloc_ptr[dev] = static_cast<float*>(p);
@@ -1137,7 +1120,11 @@ extern "C" __attribute__((visibility("default"))) int psrl_decode_attention_noal
   using namespace psrl;
   using namespace psrl::attn;
   if (!q || !k_cache || !v_cache || !block_table || !kv_lens || !out) return PSRL_NOALLOC_EBADARG;
-  if (head_dim != D || batch < 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0 ||
+  // the kernel moves q, K, V and out in 16-byte vectors
+  const uintptr_t misalign = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_cache) |
+                             reinterpret_cast<uintptr_t>(v_cache) | reinterpret_cast<uintptr_t>(out);
+  if (misalign % 16 != 0) return PSRL_NOALLOC_EBADARG;
+  if (head_dim != D || batch < 0 || num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0 ||
       num_heads / num_kv_heads > 16 || block_size <= 0 || max_blocks <= 0 || splits < 1 || splits > 32)
     return PSRL_NOALLOC_EBADARG;
   const long long need = splits > 1 ? (long long)batch * num_heads * splits * (D + 1) : 0;
@@ -1167,7 +1154,7 @@ extern "C" __attribute__((visibility("default"))) int psrl_decode_attention_noal
     p.part_lse = scratch + (long long)batch * num_heads * splits * D;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  decode_kernel<<<dim3(batch, num_kv_heads, splits), NTHREADS, dec_smem(), st>>>(p);
+  decode_kernel_s3<<<dim3(batch, num_kv_heads, splits), NTHREADS, dec_smem(3), st>>>(p);
   if (cudaPeekAtLastError() != cudaSuccess) return PSRL_NOALLOC_ECUDA;
   if (splits > 1) {
     decode_combine_kernel<<<batch * num_heads, D, 0, st>>>(p.part_o, p.part_lse, p.o, splits);

@@ -38,6 +38,9 @@ void copy_segments(at::Tensor dst, std::vector<at::Tensor> srcs, std::vector<int
                    std::vector<int64_t> src_offsets_bytes, std::vector<int64_t> lengths_bytes);
 at::Tensor tc_gemm(at::Tensor a, at::Tensor b, at::Tensor err);
 at::Tensor tc_grouped_gemm(at::Tensor a, at::Tensor w, at::Tensor seg, at::Tensor err);
+at::Tensor tc_gemm2(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, c10::optional<at::Tensor> out, int64_t splits,
+                    int64_t group_m, c10::optional<at::Tensor> bias, at::Tensor err);
+std::vector<at::Tensor> tc_gemm2_swiglu(at::Tensor x, at::Tensor w, int64_t group_m, at::Tensor err);
 std::vector<at::Tensor> moe_route(at::Tensor logits, c10::optional<at::Tensor> prior, int64_t k, bool renorm);
 std::vector<at::Tensor> moe_permute(at::Tensor ids, at::Tensor counts, int64_t bm, int64_t tiles_n);
 at::Tensor moe_gather(at::Tensor x, at::Tensor token_of_row);
@@ -82,6 +85,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("copy_segments", &psrl::copy_segments);
   m.def("tc_gemm", &psrl::tc_gemm);
   m.def("tc_grouped_gemm", &psrl::tc_grouped_gemm);
+  m.def("tc_gemm2", &psrl::tc_gemm2);
+  m.def("tc_gemm2_swiglu", &psrl::tc_gemm2_swiglu);
   m.def("moe_route", &psrl::moe_route);
   m.def("moe_permute", &psrl::moe_permute);
   m.def("moe_gather", &psrl::moe_gather);

@@ -7,6 +7,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <set>
+#include <utility>
+
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -39,6 +43,22 @@ inline int num_sms() {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   }
   return n;
+}
+
+// Raise a kernel's dynamic shared-memory limit on the current device, once
+// per (kernel, device): the attribute is per device, so a process that
+// launches the kernel on several GPUs sets it on each of them.
+template <typename Kernel>
+inline void ensure_smem_attr(Kernel* fn, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  PSRL_CHECK_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_pair(reinterpret_cast<const void*>(fn), dev);
+  if (done.count(key)) return;
+  PSRL_CHECK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.insert(key);
 }
 
 __device__ __forceinline__ float to_f(bf16 x) { return __bfloat162float(x); }

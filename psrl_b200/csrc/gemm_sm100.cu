@@ -450,11 +450,7 @@ static CUtensorMap make_tmap(const at::Tensor& t, uint32_t box_rows) {
 
 template <int EPI>
 static void launch(const at::Tensor& a, const at::Tensor& b, Args& args) {
-  static bool attr = false;
-  if (!attr) {
-    PSRL_CHECK_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    attr = true;
-  }
+  ensure_smem_attr(tc_gemm_kernel<EPI>, SMEM_BYTES);
   CUtensorMap ta = make_tmap(a, BM), tb = make_tmap(b, BN);
   // grouped: the tile count lives on the device; one persistent CTA per SM
   const int grid = args.grouped ? num_sms() : std::min(args.num_tiles, num_sms());

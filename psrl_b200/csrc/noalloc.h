@@ -11,11 +11,20 @@
 // loading the library holds until the process exits.
 //
 // Contract:
+//  * q, k_cache, v_cache and out start on 16-byte boundaries (the kernel moves
+//    them in 16-byte vectors); a misaligned pointer is rejected with
+//    PSRL_NOALLOC_EBADARG.  num_heads > 0, num_kv_heads > 0 and divides it, at
+//    most 16 query heads per KV head.
 //  * q          [batch, num_heads, 128] bf16, contiguous
 //  * k_cache,
 //    v_cache    [num_blocks, num_kv_heads, block_size, 128] bf16
 //  * block_table[batch, max_blocks] int32;  kv_lens [batch] int32 (context length
 //               including the current token)
+//  * The caller guarantees, for every b, 1 <= kv_lens[b] <= max_blocks * block_size
+//    and that the first ceil(kv_lens[b] / block_size) entries of block_table row b
+//    are valid block indices of the caches.  These arrays live on the device and
+//    are not read by the host, so the call cannot check them; a longer context
+//    or a bad block index reads outside the caches.
 //  * out        [batch, num_heads, 128] bf16 (written)
 //  * splits     number of KV splits (1..32); with splits > 1 the call needs
 //               batch * num_heads * splits * 129 floats of scratch, which must

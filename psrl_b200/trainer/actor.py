@@ -15,6 +15,8 @@ Reference: ``PSRL_EngineTrainWorker`` (``psrl/workers/train/engine_train_worker.
 
 from __future__ import annotations
 
+import time
+
 import torch
 
 from ..models import ModelArgs, build_model
@@ -206,6 +208,7 @@ class PolicyWorker:
         ac = self.cfg.actor
         self.model.train()
         stats: dict[str, list] = {}
+        opt_s = 0.0
         use_tis = bool(self.cfg.algorithm.rollout_correction.tis)
         if plan is None:
             plan = [(self.my_share(trajs, mini), float(sum(loss_tokens(trajs[i]) for i in mini)), len(mini))
@@ -250,16 +253,19 @@ class PolicyWorker:
                     if sync_every_micro_batch and self.device.type == "cuda":
                         # bounded launch queue: the host thread releases the GIL here
                         torch.cuda.current_stream().synchronize()
+                t_opt = time.perf_counter()
                 with guard():
                     st = self.dp.step(partners=[self.dp_partner] if self.dp_partner else None)
                     if self.device.type == "cuda":
                         torch.cuda.current_stream().synchronize()
+                opt_s += time.perf_counter() - t_opt
                 stats.setdefault("grad_norm", []).append(st["grad_norm"])
                 stats.setdefault("lr", []).append(torch.tensor(st["lr"]))
         out = {}
         for k, vs in stats.items():
             t = torch.stack([v.reshape(()).float().to(self.device) for v in vs])
             out[f"actor/{k}"] = float(t.sum()) if k in ("pg_loss", "entropy") else float(t.mean())
+        out["timing_s/optimizer"] = opt_s
         return out
 
     def update_critic(self, trajs: list[Trajectory], plan: list[tuple] | None = None) -> dict:

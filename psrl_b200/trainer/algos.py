@@ -92,18 +92,34 @@ def gdpo_advantage(score_components: torch.Tensor, uids, eps: float = 1e-6) -> t
 
 def reinforce_pp_returns(token_rewards: torch.Tensor, mask: torch.Tensor, gamma: float = 1.0) -> torch.Tensor:
     """token_rewards/mask [N, L] -> whitened discounted returns [N, L]."""
+    return masked_whiten(discounted_returns(token_rewards, mask, gamma), mask)
+
+
+def discounted_returns(token_rewards: torch.Tensor, mask: torch.Tensor, gamma: float = 1.0) -> torch.Tensor:
+    """Discounted reward-to-go over the action tokens only: a token with
+    mask 0 (padding, or an environment observation inside a multi-turn
+    response) takes no discount step and passes the running return through
+    unchanged, so a trajectory gives the same returns on its action tokens
+    with or without its observation spans."""
     ret = torch.zeros_like(token_rewards, dtype=torch.float32)
     run = torch.zeros(token_rewards.shape[0], dtype=torch.float32)
     for t in reversed(range(token_rewards.shape[1])):
-        run = token_rewards[:, t].float() + gamma * run * mask[:, t]
+        m = mask[:, t].float()
+        run = m * (token_rewards[:, t].float() + gamma * run) + (1.0 - m) * run
         ret[:, t] = run
-    return masked_whiten(ret, mask)
+    return ret
 
 
 def gae_advantage(token_rewards: torch.Tensor, values: torch.Tensor, mask: torch.Tensor, gamma: float, lam: float,
                   whiten: bool = True):
     """[N, L] tensors -> (advantages [N, L] (whitened over the batch unless
-    ``whiten`` is False), returns [N, L])."""
+    ``whiten`` is False), returns [N, L]).
+
+    Tokens with mask 0 (padding, environment observations of a multi-turn
+    response) take no TD step: the next value and the running lambda-return
+    are carried across them unchanged, as veRL's
+    ``compute_gae_advantage_return`` does with its response mask
+    (``psrl/trainer/ppo/utils.py:167-172`` passes it)."""
     N, L = token_rewards.shape
     adv = torch.zeros(N, L, dtype=torch.float32)
     last = torch.zeros(N, dtype=torch.float32)
@@ -111,10 +127,9 @@ def gae_advantage(token_rewards: torch.Tensor, values: torch.Tensor, mask: torch
     for t in reversed(range(L)):
         m = mask[:, t].float()
         delta = token_rewards[:, t].float() + gamma * nextv - values[:, t].float()
-        last = delta + gamma * lam * last
-        last = last * m
+        last = m * (delta + gamma * lam * last) + (1.0 - m) * last
         adv[:, t] = last
-        nextv = torch.where(m > 0, values[:, t].float(), nextv)
+        nextv = m * values[:, t].float() + (1.0 - m) * nextv
     returns = adv + values.float()
     return (masked_whiten(adv, mask) if whiten else adv * mask), returns * mask
 
@@ -497,6 +512,19 @@ def shard_advantages(cfg, trajs, group=None, kl_ctrl=None, replicas: int = 1, cr
     return out
 
 
+def response_mask_row(t) -> torch.Tensor:
+    """[response_len] float mask of the tokens the policy produced: the
+    trajectory's ``response_mask`` when set (0 on environment observations
+    of a multi-turn response), else all ones."""
+    n = t.response_len
+    if t.response_mask is None:
+        return torch.ones(n)
+    m = torch.zeros(n)
+    src = torch.tensor(t.response_mask[:n], dtype=torch.float32)
+    m[: src.numel()] = src
+    return m
+
+
 def gae_with_global_whitening(cfg, trajs, group=None) -> None:
     """GAE (``old_values`` set) or, with no critic, REINFORCE++ returns on
     this rank's trajectories, whitened with the mean and variance of all
@@ -510,7 +538,7 @@ def gae_with_global_whitening(cfg, trajs, group=None) -> None:
     use_values = all(t.old_values is not None for t in trajs)
     for i, t in enumerate(trajs):
         n = t.response_len
-        mask[i, :n] = 1
+        mask[i, :n] = response_mask_row(t)
         rew[i, :n] = torch.tensor(token_reward_row(t), dtype=torch.float32)
         if use_values:
             vals[i, :n] = torch.tensor(t.old_values[:n])
@@ -518,12 +546,7 @@ def gae_with_global_whitening(cfg, trajs, group=None) -> None:
         adv, ret = gae_advantage(rew, vals, mask, float(cfg.algorithm.gamma), float(cfg.algorithm.lam),
                                  whiten=False)
     else:
-        g = float(cfg.algorithm.gamma)
-        ret = torch.zeros(N, L)
-        run = torch.zeros(N)
-        for j in reversed(range(L)):
-            run = rew[:, j] + g * run * mask[:, j]
-            ret[:, j] = run
+        ret = discounted_returns(rew, mask, float(cfg.algorithm.gamma))
         adv = ret * mask
     st = torch.tensor([float((adv * mask).sum()), float((adv * adv * mask).sum()), float(mask.sum())],
                       dtype=torch.float64)

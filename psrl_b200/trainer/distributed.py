@@ -34,6 +34,7 @@ from ..parallel import dist as pdist
 from ..parallel.weight_sync import WeightLayout, WeightPuller, WeightStore
 from ..rollout.engine import EngineWeights, RolloutEngine
 from ..rollout.instance import SyncPolicy
+from ..utils import transfer
 from ..utils.rpc import RPCClient
 from . import algos
 from .actor import PolicyWorker
@@ -232,6 +233,7 @@ class DisaggregatedRun:
                         "response_length/mean": batch["response_length/mean"],
                         "staleness/max": batch["staleness/max"],
                         "timing_s/gen_wait": t1 - t0, "timing_s/train": t2 - t1,
+                        "timing_s/publish": time.perf_counter() - t2,
                         "timing_s/step": time.perf_counter() - t0})
         return metrics
 
@@ -347,6 +349,7 @@ def run_disaggregated(cfg, steps: int, warmup: int, info: pdist.DistInfo | None 
             ev.record()
             t_evt[p] = ev
         t_evt[f"wall{p}"] = time.perf_counter()
+        t_evt[f"xfer{p}"] = transfer.snapshot()
 
     metrics = []
     try:
@@ -381,9 +384,12 @@ def run_disaggregated(cfg, steps: int, warmup: int, info: pdist.DistInfo | None 
         else:
             ms = (t_evt["wall2"] - t_evt["wall1"]) * 1000.0
         wall = t_evt["wall2"] - t_evt["wall1"]
+        # host<->device bytes of this rank inside the timed region
+        xfer = [b - a for a, b in zip(t_evt["xfer1"], t_evt["xfer2"])]
         ms_max = pdist.all_reduce_max(ms, info.device)
         wall_max = pdist.all_reduce_max(wall, info.device)
         out = {"ms": ms_max, "wall_s": wall_max, "rank": run.rank, "metrics": metrics,
+               "h2d": xfer[0], "d2h": xfer[1],
                "n_train": run.n_train, "world": run.world}
         if run.rank == 0:
             out["tokens"] = sum(int(m["trained_tokens"]) for m in metrics)
@@ -401,16 +407,14 @@ def run_disaggregated_bench(args, placement: str = "disaggregated"):
     """bench.py entry for torch.distributed.run launches (N >= 1 ranks):
     ``placement`` is ``disaggregated`` (trainer ranks + rollout ranks) or
     ``hybrid`` (every rank trains and serves rollout, :mod:`.hybrid`)."""
-    from bench import build_cfg
+    from ..bench.rl_bench import build_cfg
     from ..ops import _ext
-    from ..utils import transfer
     from ..utils.clocks import ClockSampler
 
     info = pdist.init_distributed("cuda", timeout_s=900)
     cfg = build_cfg(args, info.world_size)
     sampler = ClockSampler(list(range(info.world_size))).start() if info.rank == 0 else None
     l0 = _ext.launches()
-    b0, o0 = transfer.snapshot()
     if placement == "hybrid":
         from .hybrid import run_hybrid
         res = run_hybrid(cfg, args.steps, args.warmup, info)
@@ -419,19 +423,21 @@ def run_disaggregated_bench(args, placement: str = "disaggregated"):
     else:
         res = run_disaggregated(cfg, args.steps, args.warmup, info)
         n_train = res["n_train"]
-        par = f"train dp{n_train} + rollout dp{res['world'] - n_train} (tp1)"
+        par = f"train dp{n_train} (sharded) + rollout dp{res['world'] - n_train} (tp1), NVLink weight pull"
     launches = pdist.all_reduce_sum(float(_ext.launches() - l0), info.device)
-    b1, o1 = transfer.snapshot()
-    h2d = pdist.all_reduce_sum(float(b1 - b0), info.device)
-    d2h = pdist.all_reduce_sum(float(o1 - o0), info.device)
+    # bytes copied host<->device inside the timed region, all ranks
+    h2d = pdist.all_reduce_sum(float(res["h2d"]), info.device)
+    d2h = pdist.all_reduce_sum(float(res["d2h"]), info.device)
     clocks = sampler.stop() if sampler else None
     pdist.destroy()
     if info.rank != 0:
         return None
     res.update({
         "launches": launches, "clocks": clocks,
-        "h2d": h2d / max(1, args.steps + args.warmup), "d2h": d2h / max(1, args.steps + args.warmup),
-        "global_batch": cfg.psrl.staleness_buffer_entries * cfg.psrl.rollout_n,
+        "h2d": h2d / max(1, args.steps), "d2h": d2h / max(1, args.steps),
+        "prompts_per_step": cfg.psrl.staleness_buffer_entries,
+        "trajectories_per_step": cfg.psrl.staleness_buffer_entries * cfg.psrl.rollout_n,
         "parallelism": par,
+        "api": "HybridRun.step" if placement == "hybrid" else "DisaggregatedRun.trainer_step",
     })
     return res

@@ -104,7 +104,7 @@ def compute_batch_advantages(cfg, trajs, kl_ctrl=None) -> dict:
         vals = torch.zeros(N, L)
         for i, t in enumerate(trajs):
             n = t.response_len
-            mask[i, :n] = 1
+            mask[i, :n] = algos.response_mask_row(t)
             rew[i, :n] = torch.tensor(algos.token_reward_row(t), dtype=torch.float32)
             if t.old_values is not None:
                 vals[i, :n] = torch.tensor(t.old_values[:n])

@@ -43,6 +43,7 @@ from ..parallel import dist as pdist
 from ..parallel.weight_sync import WeightLayout
 from ..rollout.engine import EngineWeights, RolloutEngine
 from ..rollout.instance import SyncPolicy
+from ..utils import transfer
 from ..utils.locks import RWLock
 from ..utils.rpc import RPCClient
 from . import algos
@@ -419,6 +420,7 @@ def run_hybrid(cfg, steps: int, warmup: int, info: pdist.DistInfo | None = None,
             ev.record()
             t_evt[p] = ev
         t_evt[f"wall{p}"] = time.perf_counter()
+        t_evt[f"xfer{p}"] = transfer.snapshot()
 
     metrics = []
     try:
@@ -441,10 +443,13 @@ def run_hybrid(cfg, steps: int, warmup: int, info: pdist.DistInfo | None = None,
         else:
             ms = (t_evt["wall2"] - t_evt["wall1"]) * 1000.0
         wall = t_evt["wall2"] - t_evt["wall1"]
+        # host<->device bytes of this rank inside the timed region
+        xfer = [b - a for a, b in zip(t_evt["xfer1"], t_evt["xfer2"])]
         run.stop_rollout()
         ms_max = pdist.all_reduce_max(ms, info.device)
         wall_max = pdist.all_reduce_max(wall, info.device)
         out = {"ms": ms_max, "wall_s": wall_max, "rank": run.rank, "metrics": metrics, "world": run.world,
+               "h2d": xfer[0], "d2h": xfer[1],
                "tokens": sum(int(m["trained_tokens"]) for m in metrics),
                "param_checksum": float(run.actor.dp.flat.double().sum()),
                "engine_checksum": float(sum(t.double().sum() for k, t in run.engine_weights.tensors.items()

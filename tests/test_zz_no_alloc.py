@@ -53,6 +53,7 @@ def _call(fn, q, kc, vc, bt, lens, out, splits):
 @pytest.mark.parametrize("splits", [1, 4])
 def test_noalloc_matches_regular_entry_point_twice(splits):
     from psrl_b200.ops import paged_decode_attention
+    from psrl_b200.ops.attention import paged_attention_ref
     fn = _entry()
     # two calls in a row with different inputs: the shared scratch must not leak
     for seed, ctx in ((1, [1, 70, 300, 1500, 64]), (2, [900, 5, 128, 2000, 33, 260, 1])):
@@ -62,6 +63,11 @@ def test_noalloc_matches_regular_entry_point_twice(splits):
         torch.cuda.synchronize()
         ref = paged_decode_attention(q, kc, vc, bt, lens, splits=splits)
         torch.testing.assert_close(out.float(), ref.float(), atol=2e-2, rtol=2e-2)
+        # and directly against the plain fp32 PyTorch attention over the same pages
+        B = q.shape[0]
+        cu = torch.arange(B + 1, dtype=torch.int32, device="cuda")
+        oracle = paged_attention_ref(q.float(), kc.float(), vc.float(), cu, lens, bt, 1.0 / math.sqrt(q.shape[-1]))
+        torch.testing.assert_close(out.float(), oracle, atol=2e-2, rtol=2e-2)
 
 
 def test_noalloc_rejects_oversize_and_bad_args():
@@ -78,5 +84,14 @@ def test_noalloc_rejects_oversize_and_bad_args():
     big_out = torch.zeros_like(big_q)
     assert _call(fn, big_q, kc, vc, big_bt, big_lens, big_out, 8) == ETOOBIG
     assert fn(None, None, None, None, None, None, 1, 16, 2, 128, 64, 1, 1, 1.0, None) == EBADARG
+    # no query heads, and a q pointer off its 16-byte boundary
+    B, nq, d = q.shape
+    args = (bt.data_ptr(), lens.data_ptr(), out.data_ptr())
+    assert fn(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), *args, B, 0, 2, d, kc.shape[2], bt.shape[1], 1, 1.0,
+              None) == EBADARG
+    assert fn(q.data_ptr() + 2, kc.data_ptr(), vc.data_ptr(), *args, B, nq, 2, d, kc.shape[2], bt.shape[1], 1, 1.0,
+              None) == EBADARG
+    assert fn(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), bt.data_ptr(), lens.data_ptr(), out.data_ptr() + 8, B, nq,
+              2, d, kc.shape[2], bt.shape[1], 1, 1.0, None) == EBADARG
     torch.cuda.synchronize()
     assert torch.count_nonzero(out) == 0 and torch.count_nonzero(big_out) == 0
