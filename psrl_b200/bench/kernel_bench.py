@@ -141,11 +141,18 @@ def bench_attn_train(pk):
         cu = torch.arange(0, T + 1, L, dtype=torch.int32, device="cuda")   # nseq sequences of L tokens
         fl = 4.0 * nseq * (L * L / 2) * d * nq
         ms_f = timeit(lambda: varlen_attention(qkv, cu, L, nq, nkv, d), iters=10)
+        from psrl_b200.ops import ext
+        q = qkv.detach()[:, : nq * d].view(T, nq, d)
+        k = qkv.detach()[:, nq * d:(nq + nkv) * d].view(T, nkv, d)
+        v = qkv.detach()[:, (nq + nkv) * d:].view(T, nkv, d)
+        ms_f_old = timeit(lambda: ext().attn_varlen_fwd(q, k, v, cu, L, 1 / math.sqrt(d), True), iters=10)
         o = varlen_attention(qkv, cu, L, nq, nkv, d)
         g = torch.randn_like(o)
         ms_b = timeit(lambda: torch.autograd.grad(o, qkv, g, retain_graph=True), iters=10)
         out.append({"case": f"varlen attn L={L}x{nseq} 16/2", "fwd_ms": round(ms_f, 3), "bwd_ms": round(ms_b, 3),
-                    "fwd_tflops": round(fl / ms_f / 1e9, 1), "bwd_tflops": round(2.5 * fl / ms_b / 1e9, 1)})
+                    "fwd_tflops": round(fl / ms_f / 1e9, 1), "bwd_tflops": round(2.5 * fl / ms_b / 1e9, 1),
+                    "fwd_frac_peak": round(fl / ms_f / 1e9 / pk["bf16_tflops"], 3),
+                    "fwd_mma_sync_ms": round(ms_f_old, 3), "fwd_vs_mma_sync": round(ms_f_old / ms_f, 2)})
     return out
 
 

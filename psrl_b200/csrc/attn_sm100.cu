@@ -1,0 +1,882 @@
+// Causal varlen attention forward for sm_100a on the 5th-generation tensor
+// cores (head_dim 128, bf16 in, fp32 softmax and accumulation).
+//
+// One CTA per (query head, sequence, 256-row query block).  The block is two
+// 128-row query tiles A and B that share every K/V tile, so each K/V byte
+// loaded by TMA serves two MMAs, and the tensor core alternates between the
+// tiles while the softmax of the other one runs ("ping-pong"):
+//
+//   TMEM (512 columns): S_A | S_B | O_A | O_B, 128 fp32 columns each; P (bf16
+//   probabilities, two per 32-bit column) overwrites the first 64 columns of
+//   its S once S has been read.
+//
+//   warp 0      TMA producer: Q_A, Q_B once, then K_j and V_j per 128-key tile
+//               into a 2-stage ring (128-byte swizzle).
+//   warp 1      MMA issuer (one thread): S_g = Q_g K_j^T (both operands from
+//               shared memory), O_g += P_g V_j (P from tensor memory, V read
+//               MN-major from shared memory); tcgen05.commit signals S ready,
+//               the K/V slot free, and O final.
+//   warps 2..5  softmax of tile A, warps 6..9 of tile B: one thread per row,
+//               online softmax in base 2 with lazy rescaling (O in TMEM is
+//               rescaled only when the running maximum grows by more than 2^8),
+//               P written back to TMEM with tcgen05.st; at the end O / l and the
+//               row's log-sum-exp.
+//
+// Work per block: tile A needs key tiles 0 .. 2t (t = block index), tile B
+// 0 .. 2t+1; only the diagonal tile of each is masked.  Blocks are launched
+// largest first.  Every wait is bounded; on timeout the kernel records an
+// error code and leaves.  TMA loads are plain per-CTA copies.
+#include <cuda.h>
+
+#include "driver_api.h"
+
+#include "common.cuh"
+#include "tcgen05.cuh"
+
+namespace psrl {
+namespace fa5 {
+
+using namespace tc5;
+
+constexpr int D = 128;
+constexpr int BQ = 128, BKV = 128;
+constexpr int NS = 2;                    // K/V ring depth
+constexpr int ATOM = 128 * 64 * 2;       // 128 rows x 64 bf16 (one 128-byte swizzle atom column)
+constexpr int Q_BYTES = 2 * ATOM;        // 32 KB
+constexpr int KV_TILE = 2 * ATOM;        // 32 KB
+constexpr int STAGE = 2 * KV_TILE;       // K + V
+constexpr int OFF_KV = 2 * Q_BYTES;
+constexpr int OFF_BAR = OFF_KV + NS * STAGE;  // 192 KB
+constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr int NTHREADS = 320;
+constexpr float RESCALE_LOG2 = 8.0f;
+
+struct FwdArgs {
+  const int* cu;     // [B + 1]
+  int nq, nkv, T;
+  int blocks_z;      // grid.z = max 256-row blocks per sequence
+  float scale_log2;  // softmax scale * log2(e)
+  bf16* o;           // [T, nq * D]
+  int64_t o_row;
+  float* lse;        // [nq, T] natural log, or null
+  int* err;
+};
+
+// First failure of the launch: code, then (block x, y, z, warp, iteration) in err[1..5].
+__device__ __forceinline__ void set_err(int* err, int code, int it = -1) {
+  if (err && atomicCAS(err, 0, code) == 0) {
+    err[1] = blockIdx.x;
+    err[2] = blockIdx.y;
+    err[3] = blockIdx.z;
+    err[4] = threadIdx.x >> 5;
+    err[5] = it;
+  }
+}
+
+__global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_constant__ CUtensorMap tm, FwdArgs a) {
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int blk = a.blocks_z - 1 - (int)blockIdx.z;  // largest blocks first
+  const int s0 = a.cu[b], L = a.cu[b + 1] - s0;
+  const int q0 = blk * 2 * BQ;
+  if (q0 >= L) return;  // uniform for the whole CTA, before any barrier
+  const int rowsB = max(0, min(BQ, L - q0 - BQ));
+  const int nA = 2 * blk + 1, nB = rowsB > 0 ? 2 * blk + 2 : 0;
+  const int nK = max(nA, nB);
+  const int hk = h / (a.nq / a.nkv);
+  const int xq = h * D, xk = (a.nq + hk) * D, xv = (a.nq + a.nkv + hk) * D;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  // bars: q_full, kv_full[NS], kv_empty[NS], s_full[2], p_full[2], o_full; then the TMEM slot
+  const uint32_t bq = smem_u32(bars), bkf = bq + 8, bke = bkf + 8 * NS, bsf = bke + 8 * NS, bpf = bsf + 16,
+                 bof = bpf + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 + 2 * NS + 4 + 1);
+  __shared__ volatile int s_abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    mbar_init(bq, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(bkf + 8 * i, 1);
+      mbar_init(bke + 8 * i, 1);
+    }
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(bsf + 8 * g, 1);
+      mbar_init(bpf + 8 * g, 4);  // one arrive per softmax warp
+    }
+    mbar_init(bof, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) tmem_alloc_1cta(smem_u32(tmem_slot), 512);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM columns: S_A 0..127, S_B 128..255, O_A 256..383, O_B 384..511
+  auto tS = [&](int g) { return tmem + 128u * (uint32_t)g; };
+  auto tO = [&](int g) { return tmem + 256u + 128u * (uint32_t)g; };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm);
+      mbar_expect_tx(bq, (nB ? 2 : 1) * Q_BYTES);
+      const uint32_t sq = smem_u32(smem);
+      tma_load_2d(sq, &tm, xq, s0 + q0, bq);
+      tma_load_2d(sq + ATOM, &tm, xq + 64, s0 + q0, bq);
+      if (nB) {
+        tma_load_2d(sq + Q_BYTES, &tm, xq, s0 + q0 + BQ, bq);
+        tma_load_2d(sq + Q_BYTES + ATOM, &tm, xq + 64, s0 + q0 + BQ, bq);
+      }
+      for (int j = 0; j < nK && !s_abort; ++j) {
+        const int st = j % NS;
+        const uint32_t ph = (j / NS) & 1;
+        if (!mbar_wait(bke + 8 * st, ph ^ 1)) {
+          set_err(a.err, 11);
+          s_abort = 1;
+          break;
+        }
+        const uint32_t fb = bkf + 8 * st;
+        mbar_expect_tx(fb, STAGE);
+        const uint32_t sk = smem_u32(smem + OFF_KV + st * STAGE), sv = sk + KV_TILE;
+        const int y = s0 + j * BKV;
+        tma_load_2d(sk, &tm, xk, y, fb);
+        tma_load_2d(sk + ATOM, &tm, xk + 64, y, fb);
+        tma_load_2d(sv, &tm, xv, y, fb);
+        tma_load_2d(sv + ATOM, &tm, xv + 64, y, fb);
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_bf16_f32(BQ, BKV, false, false);
+      constexpr uint32_t idesc_pv = idesc_bf16_f32(BQ, D, false, true);
+      bool ok = mbar_wait(bq, 0);
+      int kv_ready = -1;
+      auto wait_kv = [&](int j) {
+        if (!ok || j <= kv_ready) return;
+        if (!mbar_wait(bkf + 8 * (j % NS), (j / NS) & 1)) {
+          ok = false;
+          return;
+        }
+        kv_ready = j;
+      };
+      auto issue_s = [&](int g, int j) {
+        fence_after();
+        const uint32_t sq = smem_u32(smem + g * Q_BYTES), sk = smem_u32(smem + OFF_KV + (j % NS) * STAGE);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k >> 2) * ATOM + (k & 3) * 32;
+          mma_1cta(tS(g), desc_sw128(sq + off, 16, 1024), desc_sw128(sk + off, 16, 1024), idesc_qk, k > 0);
+        }
+        commit_1cta(bsf + 8 * g);
+      };
+      auto issue_pv = [&](int g, int j) {
+        fence_after();
+        const uint32_t sv = smem_u32(smem + OFF_KV + (j % NS) * STAGE + KV_TILE);
+#pragma unroll
+        for (int k = 0; k < BKV / 16; ++k)
+          mma_1cta_ts(tO(g), tS(g) + k * 8, desc_sw128(sv + k * 2048, ATOM, 1024), idesc_pv, (j > 0 || k > 0));
+      };
+      wait_kv(0);
+      if (ok) {
+        issue_s(0, 0);
+        if (nB) issue_s(1, 0);
+      }
+      int where = ok ? 0 : 120;
+      for (int j = 0; j < nK && ok && !s_abort; ++j) {
+        if (j < nA) {
+          if (!mbar_wait(bpf, j & 1)) { ok = false; where = 121 + 1000 * j; break; }
+          issue_pv(0, j);
+        }
+        if (j + 1 < nA) {
+          wait_kv(j + 1);
+          if (!ok) { where = 122 + 1000 * j; break; }
+          issue_s(0, j + 1);
+        }
+        if (j < nB) {
+          if (!mbar_wait(bpf + 8, j & 1)) { ok = false; where = 123 + 1000 * j; break; }
+          issue_pv(1, j);
+        }
+        commit_1cta(bke + 8 * (j % NS));  // K_j / V_j no longer read
+        if (j + 1 < nB) {
+          wait_kv(j + 1);
+          if (!ok) { where = 124 + 1000 * j; break; }
+          issue_s(1, j + 1);
+        }
+      }
+      if (!ok) {
+        set_err(a.err, 12, where);
+        s_abort = 1;
+      }
+      commit_1cta(bof);
+    }
+  } else {
+    // -------------------------------------------------------------- softmax
+    const int g = (warp - 2) >> 2;  // 0: tile A (warps 2..5), 1: tile B (warps 6..9)
+    const int n = g == 0 ? nA : nB;
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;           // row within the tile
+    const int row_pos = q0 + g * BQ + r;      // position within the sequence
+    const uint32_t ts = tS(g) + ((uint32_t)(quad * 32) << 16), to = tO(g) + ((uint32_t)(quad * 32) << 16);
+    const int diag = 2 * blk + g;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      if (!mbar_wait(bsf + 8 * g, j & 1) || s_abort) {
+        if (!s_abort) set_err(a.err, 14, j);
+        ok = false;
+        break;
+      }
+      fence_after();
+      const bool masked_tile = (j == diag);
+      // pass 1: row maximum of this key tile (scaled, base 2)
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(ts + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const bool dead = masked_tile && (c * 32 + i > r);
+          mx = fmaxf(mx, dead ? -INFINITY : __uint_as_float(v[i]) * a.scale_log2);
+        }
+      }
+      const float m_new = fmaxf(m, mx);
+      // tcgen05.ld / st are warp-collective (.sync.aligned): the decision to
+      // rescale O is taken for the whole warp, every lane moves to its m_new
+      const bool grow = __any_sync(0xffffffffu, j > 0 && m != -INFINITY && m_new > m + RESCALE_LOG2);
+      if (j == 0 || (!grow && m == -INFINITY)) {
+        m = m_new;
+      } else if (grow) {
+        // grow the reference maximum: O (complete up to P_{j-1} V_{j-1}) and l by 2^(m - m_new)
+        const float alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(to + c * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+          tmem_st32(to + c * 32, v);
+        }
+        l *= alpha;
+        m = m_new;
+      }
+      const float ref = (m == -INFINITY) ? 0.f : m;
+      // pass 2: P = 2^(x - ref) in bf16, packed two per column over S's first 64 columns
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32], pk[16];
+        tmem_ld32(ts + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int c0 = c * 32 + 2 * i;
+          const float x0 = (masked_tile && c0 > r) ? -INFINITY : __uint_as_float(v[2 * i]) * a.scale_log2;
+          const float x1 = (masked_tile && c0 + 1 > r) ? -INFINITY : __uint_as_float(v[2 * i + 1]) * a.scale_log2;
+          const float p0 = ex2(x0 - ref), p1 = ex2(x1 - ref);
+          l += p0 + p1;
+          const bf162 pp = __floats2bfloat162_rn(p0, p1);
+          pk[i] = *reinterpret_cast<const uint32_t*>(&pp);
+        }
+        tmem_st16(ts + c * 16, pk);
+      }
+      tmem_wait_st();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bpf + 8 * g);
+    }
+    if (n > 0) {
+      if (!mbar_wait(bof, 0)) ok = false;
+      fence_after();
+      if (ok && !s_abort) {
+        const bool valid = row_pos < L;
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        bf16* orow = a.o + (int64_t)(s0 + row_pos) * a.o_row + (int64_t)h * D;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(to + c * 32, v);
+          tmem_wait_ld();
+          if (valid) {
+            float f[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]) * inv;
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) *reinterpret_cast<bf16x8*>(orow + c * 32 + i) = pack8(f + i);
+          }
+        }
+        if (valid && a.lse != nullptr)
+          a.lse[(int64_t)h * a.T + s0 + row_pos] = (m + __log2f(l)) * 0.69314718055994531f;
+      } else {
+        set_err(a.err, 13);
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after();
+    tmem_free_1cta(tmem, 512);
+  }
+}
+
+
+// ---------------------------------------------------------------- backward
+//
+// Two kernels, no atomics:
+//   fa_bwd_dkdv  one CTA per (kv head, sequence, 128-key tile j): K_j and V_j
+//                stay in shared memory; for every query head of the GQA
+//                group and every query tile i >= j it recomputes
+//                S^T = K_j Q_i^T and dP^T = V_j dO_i^T into TMEM, forms
+//                P^T = exp(S^T - lse) and dS^T = P^T (dP^T - D) (bf16, back
+//                into TMEM) and accumulates dV += P^T dO_i and
+//                dK += dS^T Q_i in TMEM (A operands from TMEM, B read MN-major).
+//   fa_bwd_dq    one CTA per (query head, sequence, 128-row tile i): Q_i and
+//                dO_i stay in shared memory; for every key tile j <= i it
+//                recomputes S = Q_i K_j^T and dP = dO_i V_j^T, forms dS and
+//                accumulates dQ += dS K_j.
+// D = rowsum(dO * O) comes from fa_bwd_dot.  Softmax work uses eight warps,
+// two per TMEM lane quadrant, each on one 64-column half of the tile; the
+// bf16 results of half h are packed into columns [64 h, 64 h + 32) of the
+// tile they were computed from, so no warp overwrites columns another warp
+// still reads.
+constexpr int NT_BWD = 320;
+constexpr int OFF_B_STAGE = 2 * KV_TILE;             // after the two resident tiles
+constexpr int B_STAGE = 2 * KV_TILE + 1024;          // two streamed tiles + 128 lse + 128 D (dK/dV kernel)
+constexpr int OFF_B_BAR = OFF_B_STAGE + NS * B_STAGE;
+constexpr int SMEM_BWD = OFF_B_BAR + 256 + 1024;
+
+struct BwdArgs {
+  const int* cu;
+  int nq, nkv, T;
+  int blocks_z;
+  float scale, scale_log2;
+  const float* lse;  // [nq, T] natural log
+  const float* dd;   // [nq, T] rowsum(dO * O)
+  bf16* dqkv;        // [T, (nq + 2 nkv) * D]
+  int64_t dqkv_row;
+  int* err;
+};
+
+__global__ void fa_bwd_dot(const bf16* __restrict__ o, const bf16* __restrict__ dout, int64_t T, int nq,
+                           float* __restrict__ dd) {
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= T * nq) return;
+  const int64_t t = w / nq;
+  const int h = (int)(w - t * nq);
+  const bf16* po = o + w * D + lane * 4;
+  const bf16* pd = dout + w * D + lane * 4;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) s += __bfloat162float(po[i]) * __bfloat162float(pd[i]);
+  s = warp_sum(s);
+  if (lane == 0) dd[(int64_t)h * T + t] = s;
+}
+
+// MMA of a 128 x 128 x 128 tile with both operands K-major in shared memory
+// (two 64-wide swizzle atoms each).
+__device__ __forceinline__ void mma_tile_ss(uint32_t d, uint32_t sa, uint32_t sb, uint32_t idesc) {
+#pragma unroll
+  for (int k = 0; k < D / 16; ++k) {
+    const uint32_t off = (k >> 2) * ATOM + (k & 3) * 32;
+    mma_1cta(d, desc_sw128(sa + off, 16, 1024), desc_sw128(sb + off, 16, 1024), idesc, k > 0);
+  }
+}
+// D (+)= A (tensor memory, bf16 packed in columns [0, 32) and [64, 96)) x B
+// (MN-major tile in shared memory), K = 128.
+__device__ __forceinline__ void mma_tile_ts(uint32_t d, uint32_t a_tmem, uint32_t sb, uint32_t idesc, bool acc) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t acol = (k < 4) ? k * 8 : 64 + (k - 4) * 8;
+    mma_1cta_ts(d, a_tmem + acol, desc_sw128(sb + k * 2048, ATOM, 1024), idesc, (acc || k > 0) ? 1u : 0u);
+  }
+}
+
+__global__ void __launch_bounds__(NT_BWD, 1)
+    fa_bwd_dkdv(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do, BwdArgs a) {
+  const int hk = blockIdx.x, b = blockIdx.y, j = blockIdx.z;  // small j: most work, launched first
+  const int s0 = a.cu[b], L = a.cu[b + 1] - s0;
+  if (j * BKV >= L) return;
+  const int G = a.nq / a.nkv;
+  const int nqt = (L + BQ - 1) / BQ;
+  const int per_head = nqt - j;
+  const int iters = G * per_head;
+  const int xk = (a.nq + hk) * D, xv = (a.nq + a.nkv + hk) * D;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_B_BAR);
+  // kv_full, st_full[NS] (count 2: TMA bytes + the lse/D copy), st_empty[NS], s_full, p_full, done
+  const uint32_t bkv = smem_u32(bars), bsf0 = bkv + 8, bse0 = bsf0 + 8 * NS, bs = bse0 + 8 * NS, bp = bs + 8,
+                 bdone = bp + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 2 * NS + 3);
+  __shared__ volatile int s_abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    mbar_init(bkv, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(bsf0 + 8 * i, 2);
+      mbar_init(bse0 + 8 * i, 1);
+    }
+    mbar_init(bs, 1);
+    mbar_init(bp, 8);
+    mbar_init(bdone, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) tmem_alloc_1cta(smem_u32(tmem_slot), 512);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tP2 = tmem + 128, tdV = tmem + 256, tdK = tmem + 384;
+
+  if (warp == 0) {
+    // producer: K_j, V_j once; then per iteration Q_i, dO_i (TMA) and lse_i, D_i (warp copy)
+    const uint32_t sk = smem_u32(smem), sv = sk + KV_TILE;
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_qkv);
+      tma_prefetch_desc(&tm_do);
+      mbar_expect_tx(bkv, 2 * KV_TILE);
+      tma_load_2d(sk, &tm_qkv, xk, s0 + j * BKV, bkv);
+      tma_load_2d(sk + ATOM, &tm_qkv, xk + 64, s0 + j * BKV, bkv);
+      tma_load_2d(sv, &tm_qkv, xv, s0 + j * BKV, bkv);
+      tma_load_2d(sv + ATOM, &tm_qkv, xv + 64, s0 + j * BKV, bkv);
+    }
+    for (int it = 0; it < iters && !s_abort; ++it) {
+      const int hq = hk * G + it / per_head, i = j + it % per_head;
+      const int st = it % NS;
+      const uint32_t ph = (it / NS) & 1;
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(bse0 + 8 * st, ph ^ 1);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) {
+          set_err(a.err, 21);
+          s_abort = 1;
+        }
+        break;
+      }
+      uint8_t* stg = smem + OFF_B_STAGE + st * B_STAGE;
+      const uint32_t sq = smem_u32(stg), sdo = sq + KV_TILE;
+      const uint32_t fb = bsf0 + 8 * st;
+      if (lane == 0) {
+        mbar_expect_tx(fb, 2 * KV_TILE);
+        const int y = s0 + i * BQ;
+        tma_load_2d(sq, &tm_qkv, hq * D, y, fb);
+        tma_load_2d(sq + ATOM, &tm_qkv, hq * D + 64, y, fb);
+        tma_load_2d(sdo, &tm_do, hq * D, y, fb);
+        tma_load_2d(sdo + ATOM, &tm_do, hq * D + 64, y, fb);
+      }
+      float* lse_s = reinterpret_cast<float*>(stg + 2 * KV_TILE);
+      float* dd_s = lse_s + BQ;
+#pragma unroll
+      for (int c = lane; c < BQ; c += 32) {
+        const int q = i * BQ + c;
+        const bool in = q < L;
+        lse_s[c] = in ? a.lse[(int64_t)hq * a.T + s0 + q] * 1.4426950408889634f : 0.f;
+        dd_s[c] = in ? a.dd[(int64_t)hq * a.T + s0 + q] : 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(fb);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_ss = idesc_bf16_f32(BKV, BQ, false, false);  // M = keys, N = queries
+      constexpr uint32_t id_ts = idesc_bf16_f32(BKV, D, false, true);    // M = keys, N = d
+      const uint32_t sk = smem_u32(smem), sv = sk + KV_TILE;
+      bool ok = mbar_wait(bkv, 0);
+      for (int it = 0; it < iters && ok && !s_abort; ++it) {
+        const int st = it % NS;
+        const uint32_t ph = (it / NS) & 1;
+        if (!mbar_wait(bsf0 + 8 * st, ph)) { ok = false; break; }
+        fence_after();
+        const uint32_t sq = smem_u32(smem + OFF_B_STAGE + st * B_STAGE), sdo = sq + KV_TILE;
+        mma_tile_ss(tS, sk, sq, id_ss);    // S^T = K Q^T
+        mma_tile_ss(tP2, sv, sdo, id_ss);  // dP^T = V dO^T
+        commit_1cta(bs);
+        if (!mbar_wait(bp, it & 1)) { ok = false; break; }
+        fence_after();
+        mma_tile_ts(tdV, tS, sdo, id_ts, it > 0);   // dV += P^T dO
+        mma_tile_ts(tdK, tP2, sq, id_ts, it > 0);   // dK += dS^T Q
+        commit_1cta(bse0 + 8 * st);
+      }
+      if (!ok) {
+        set_err(a.err, 22);
+        s_abort = 1;
+      }
+      commit_1cta(bdone);
+    }
+  } else {
+    // softmax-gradient warps: thread = key row r, half = which 64 queries
+    const int quad = warp & 3, half = (warp - 2) >> 2;
+    const int r = quad * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    bool ok = true;
+    for (int it = 0; it < iters; ++it) {
+      const int i = j + it % per_head;
+      const int st = it % NS;
+      if (!mbar_wait(bs, it & 1) || s_abort) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      const float* lse_s = reinterpret_cast<const float*>(smem + OFF_B_STAGE + st * B_STAGE + 2 * KV_TILE);
+      const float* dd_s = lse_s + BQ;
+      const int key = j * BKV + r;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        const int col0 = half * 64 + c * 32;
+        uint32_t vs[32], vp[32], pk[16], dk[16];
+        tmem_ld32(tS + lane_off + col0, vs);
+        tmem_ld32(tP2 + lane_off + col0, vp);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int cc = col0 + 2 * e + u;
+            const int q = i * BQ + cc;
+            const bool live = (q < L) && (key <= q);
+            const float p = live ? ex2(__uint_as_float(vs[2 * e + u]) * a.scale_log2 - lse_s[cc]) : 0.f;
+            pv[u] = p;
+            dv[u] = live ? p * (__uint_as_float(vp[2 * e + u]) - dd_s[cc]) : 0.f;
+          }
+          const bf162 pp = __floats2bfloat162_rn(pv[0], pv[1]);
+          const bf162 dp = __floats2bfloat162_rn(dv[0], dv[1]);
+          pk[e] = *reinterpret_cast<const uint32_t*>(&pp);
+          dk[e] = *reinterpret_cast<const uint32_t*>(&dp);
+        }
+        tmem_st16(tS + lane_off + half * 64 + c * 16, pk);
+        tmem_st16(tP2 + lane_off + half * 64 + c * 16, dk);
+      }
+      tmem_wait_st();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bp);
+    }
+    // epilogue: dV and dK (x scale) rows of this thread's key, half the columns each
+    if (!mbar_wait(bdone, 0)) ok = false;
+    fence_after();
+    if (ok && !s_abort) {
+      const int key = j * BKV + r;
+      const bool valid = key < L;
+      bf16* rowp = a.dqkv + (int64_t)(s0 + key) * a.dqkv_row;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        const int col0 = half * 64 + c * 32;
+        uint32_t vdv[32], vdk[32];
+        tmem_ld32(tdV + lane_off + col0, vdv);
+        tmem_ld32(tdK + lane_off + col0, vdk);
+        tmem_wait_ld();
+        if (valid) {
+          float f[32], g[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            f[e] = __uint_as_float(vdv[e]);
+            g[e] = __uint_as_float(vdk[e]) * a.scale;
+          }
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            *reinterpret_cast<bf16x8*>(rowp + xv + col0 + e) = pack8(f + e);
+            *reinterpret_cast<bf16x8*>(rowp + xk + col0 + e) = pack8(g + e);
+          }
+        }
+      }
+    } else {
+      set_err(a.err, 23);
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after();
+    tmem_free_1cta(tmem, 512);
+  }
+}
+
+__global__ void __launch_bounds__(NT_BWD, 1)
+    fa_bwd_dq(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do, BwdArgs a) {
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int i = a.blocks_z - 1 - (int)blockIdx.z;  // large query tiles (most key tiles) first
+  const int s0 = a.cu[b], L = a.cu[b + 1] - s0;
+  if (i * BQ >= L) return;
+  const int n = i + 1;
+  const int hk = h / (a.nq / a.nkv);
+  const int xk = (a.nq + hk) * D, xv = (a.nq + a.nkv + hk) * D;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_B_BAR);
+  const uint32_t bqd = smem_u32(bars), bkf0 = bqd + 8, bke0 = bkf0 + 8 * NS, bs = bke0 + 8 * NS, bp = bs + 8,
+                 bdone = bp + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 2 * NS + 3);
+  __shared__ volatile int s_abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    mbar_init(bqd, 1);
+    for (int k = 0; k < NS; ++k) {
+      mbar_init(bkf0 + 8 * k, 1);
+      mbar_init(bke0 + 8 * k, 1);
+    }
+    mbar_init(bs, 1);
+    mbar_init(bp, 8);
+    mbar_init(bdone, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) tmem_alloc_1cta(smem_u32(tmem_slot), 512);
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tP2 = tmem + 128, tdQ = tmem + 256;
+  const uint32_t sq = smem_u32(smem), sdo = sq + KV_TILE;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_qkv);
+      tma_prefetch_desc(&tm_do);
+      mbar_expect_tx(bqd, 2 * KV_TILE);
+      const int y = s0 + i * BQ;
+      tma_load_2d(sq, &tm_qkv, h * D, y, bqd);
+      tma_load_2d(sq + ATOM, &tm_qkv, h * D + 64, y, bqd);
+      tma_load_2d(sdo, &tm_do, h * D, y, bqd);
+      tma_load_2d(sdo + ATOM, &tm_do, h * D + 64, y, bqd);
+      for (int jj = 0; jj < n && !s_abort; ++jj) {
+        const int st = jj % NS;
+        const uint32_t ph = (jj / NS) & 1;
+        if (!mbar_wait(bke0 + 8 * st, ph ^ 1)) {
+          set_err(a.err, 31);
+          s_abort = 1;
+          break;
+        }
+        const uint32_t fb = bkf0 + 8 * st;
+        mbar_expect_tx(fb, 2 * KV_TILE);
+        const uint32_t sk = smem_u32(smem + OFF_B_STAGE + st * B_STAGE), sv = sk + KV_TILE;
+        const int y2 = s0 + jj * BKV;
+        tma_load_2d(sk, &tm_qkv, xk, y2, fb);
+        tma_load_2d(sk + ATOM, &tm_qkv, xk + 64, y2, fb);
+        tma_load_2d(sv, &tm_qkv, xv, y2, fb);
+        tma_load_2d(sv + ATOM, &tm_qkv, xv + 64, y2, fb);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_ss = idesc_bf16_f32(BQ, BKV, false, false);
+      constexpr uint32_t id_ts = idesc_bf16_f32(BQ, D, false, true);
+      bool ok = mbar_wait(bqd, 0);
+      for (int jj = 0; jj < n && ok && !s_abort; ++jj) {
+        const int st = jj % NS;
+        if (!mbar_wait(bkf0 + 8 * st, (jj / NS) & 1)) { ok = false; break; }
+        fence_after();
+        const uint32_t sk = smem_u32(smem + OFF_B_STAGE + st * B_STAGE), sv = sk + KV_TILE;
+        mma_tile_ss(tS, sq, sk, id_ss);    // S = Q K^T
+        mma_tile_ss(tP2, sdo, sv, id_ss);  // dP = dO V^T
+        commit_1cta(bs);
+        if (!mbar_wait(bp, jj & 1)) { ok = false; break; }
+        fence_after();
+        mma_tile_ts(tdQ, tS, sk, id_ts, jj > 0);  // dQ += dS K
+        commit_1cta(bke0 + 8 * st);
+      }
+      if (!ok) {
+        set_err(a.err, 32);
+        s_abort = 1;
+      }
+      commit_1cta(bdone);
+    }
+  } else {
+    const int quad = warp & 3, half = (warp - 2) >> 2;
+    const int r = quad * 32 + lane;
+    const int q = i * BQ + r;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const bool qin = q < L;
+    const float lse2 = qin ? a.lse[(int64_t)h * a.T + s0 + q] * 1.4426950408889634f : 0.f;
+    const float dd = qin ? a.dd[(int64_t)h * a.T + s0 + q] : 0.f;
+    bool ok = true;
+    for (int jj = 0; jj < n; ++jj) {
+      if (!mbar_wait(bs, jj & 1) || s_abort) {
+        ok = false;
+        break;
+      }
+      fence_after();
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        const int col0 = half * 64 + c * 32;
+        uint32_t vs[32], vp[32], dk[16];
+        tmem_ld32(tS + lane_off + col0, vs);
+        tmem_ld32(tP2 + lane_off + col0, vp);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float dv[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int key = jj * BKV + col0 + 2 * e + u;
+            const bool live = qin && key <= q;
+            const float p = live ? ex2(__uint_as_float(vs[2 * e + u]) * a.scale_log2 - lse2) : 0.f;
+            dv[u] = live ? p * (__uint_as_float(vp[2 * e + u]) - dd) : 0.f;
+          }
+          const bf162 dp = __floats2bfloat162_rn(dv[0], dv[1]);
+          dk[e] = *reinterpret_cast<const uint32_t*>(&dp);
+        }
+        tmem_st16(tS + lane_off + half * 64 + c * 16, dk);
+      }
+      tmem_wait_st();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bp);
+    }
+    if (!mbar_wait(bdone, 0)) ok = false;
+    fence_after();
+    if (ok && !s_abort) {
+      bf16* rowp = a.dqkv + (int64_t)(s0 + q) * a.dqkv_row + (int64_t)h * D;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        const int col0 = half * 64 + c * 32;
+        uint32_t v[32];
+        tmem_ld32(tdQ + lane_off + col0, v);
+        tmem_wait_ld();
+        if (qin) {
+          float f[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(v[e]) * a.scale;
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) *reinterpret_cast<bf16x8*>(rowp + col0 + e) = pack8(f + e);
+        }
+      }
+    } else {
+      set_err(a.err, 33);
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after();
+    tmem_free_1cta(tmem, 512);
+  }
+}
+
+}  // namespace fa5
+
+using namespace fa5;
+
+// qkv: [T, (nq + 2 nkv) * 128] bf16 (q heads, then k heads, then v heads per
+// token, unit inner stride, rows on 16-byte boundaries).  Returns
+// {o [T, nq * 128] bf16, lse [nq, T] fp32 (natural log; empty unless want_lse)}.
+std::vector<at::Tensor> attn_fwd_sm100(at::Tensor qkv, at::Tensor cu_seqlens, int64_t max_seqlen, int64_t nq,
+                                       int64_t nkv, double scale, bool want_lse, at::Tensor err) {
+  CHECK_CUDA_TENSOR(qkv);
+  CHECK_DTYPE(qkv, at::kBFloat16);
+  TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1 && qkv.size(1) == (nq + 2 * nkv) * D,
+              "qkv must be [T, (nq + 2 nkv) * 128] with unit inner stride");
+  TORCH_CHECK(nq % nkv == 0, "nq must be a multiple of nkv");
+  TORCH_CHECK(cu_seqlens.scalar_type() == at::kInt && cu_seqlens.is_contiguous(), "cu_seqlens int32");
+  const int64_t T = qkv.size(0);
+  const int B = (int)cu_seqlens.numel() - 1;
+  at::cuda::CUDAGuard g(qkv.device());
+  auto o = at::empty({T, nq * D}, qkv.options());
+  auto lse = want_lse ? at::empty({nq, T}, qkv.options().dtype(at::kFloat)) : at::Tensor();
+  if (T == 0 || B <= 0 || max_seqlen <= 0) return {o, lse};
+  TORCH_CHECK((qkv.stride(0) * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(qkv.data_ptr()) % 16 == 0,
+              "qkv rows must start on 16-byte boundaries");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)qkv.size(1), (cuuint64_t)T};
+  cuuint64_t strides[1] = {(cuuint64_t)qkv.stride(0) * 2};
+  cuuint32_t box[2] = {64u, 128u};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = PSRL_DRV(cuTensorMapEncodeTiled)(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv.data_ptr(), dims, strides,
+                                                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (", (int)r, ")");
+  FwdArgs a{};
+  a.cu = cu_seqlens.data_ptr<int>();
+  a.nq = (int)nq;
+  a.nkv = (int)nkv;
+  a.T = (int)T;
+  a.blocks_z = (int)((max_seqlen + 2 * BQ - 1) / (2 * BQ));
+  a.scale_log2 = (float)(scale * 1.4426950408889634);
+  a.o = reinterpret_cast<bf16*>(o.data_ptr());
+  a.o_row = nq * D;
+  a.lse = want_lse ? lse.data_ptr<float>() : nullptr;
+  a.err = err.data_ptr<int>();
+  ensure_smem_attr(fa_fwd_kernel, SMEM_BYTES);
+  dim3 grid((unsigned)nq, (unsigned)B, (unsigned)a.blocks_z);
+  fa_fwd_kernel<<<grid, NTHREADS, SMEM_BYTES, stream()>>>(m, a);
+  PSRL_CHECK_LAUNCH();
+  return {o, lse};
+}
+
+static CUtensorMap map_rows_64x128(const at::Tensor& t) {
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1 && (t.stride(0) * 2) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+              "operand rows must start on 16-byte boundaries with unit inner stride");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)t.size(1), (cuuint64_t)t.size(0)};
+  cuuint64_t strides[1] = {(cuuint64_t)t.stride(0) * 2};
+  cuuint32_t box[2] = {64u, 128u};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = PSRL_DRV(cuTensorMapEncodeTiled)(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, t.data_ptr(), dims, strides,
+                                                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (", (int)r, ")");
+  return m;
+}
+
+// Backward of attn_fwd_sm100: qkv [T, (nq + 2 nkv) * 128], o and dout
+// [T, nq * 128] (bf16), lse [nq, T].  Returns dqkv [T, (nq + 2 nkv) * 128] bf16.
+at::Tensor attn_bwd_sm100(at::Tensor qkv, at::Tensor o, at::Tensor dout, at::Tensor lse, at::Tensor cu_seqlens,
+                          int64_t max_seqlen, int64_t nq, int64_t nkv, double scale, at::Tensor err) {
+  CHECK_CUDA_TENSOR(qkv);
+  CHECK_DTYPE(qkv, at::kBFloat16);
+  CHECK_DTYPE(o, at::kBFloat16);
+  CHECK_DTYPE(dout, at::kBFloat16);
+  CHECK_DTYPE(lse, at::kFloat);
+  const int64_t T = qkv.size(0);
+  TORCH_CHECK(qkv.dim() == 2 && qkv.size(1) == (nq + 2 * nkv) * D && nq % nkv == 0, "qkv layout");
+  TORCH_CHECK(o.is_contiguous() && dout.is_contiguous() && o.numel() == T * nq * D && dout.numel() == T * nq * D,
+              "o / dout must be contiguous [T, nq * 128]");
+  TORCH_CHECK(lse.is_contiguous() && lse.numel() == nq * T, "lse must be contiguous [nq, T]");
+  const int B = (int)cu_seqlens.numel() - 1;
+  at::cuda::CUDAGuard g(qkv.device());
+  auto dqkv = at::empty({T, (nq + 2 * nkv) * D}, qkv.options());
+  if (T == 0 || B <= 0 || max_seqlen <= 0) return dqkv.zero_();
+  auto dd = at::empty({nq, T}, qkv.options().dtype(at::kFloat));
+  {
+    const int64_t warps = T * nq;
+    fa_bwd_dot<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, stream()>>>(
+        reinterpret_cast<const bf16*>(o.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()), T, (int)nq,
+        dd.data_ptr<float>());
+    PSRL_CHECK_LAUNCH();
+  }
+  const CUtensorMap tq = map_rows_64x128(qkv), tdo = map_rows_64x128(dout.view({T, nq * D}));
+  BwdArgs a{};
+  a.cu = cu_seqlens.data_ptr<int>();
+  a.nq = (int)nq;
+  a.nkv = (int)nkv;
+  a.T = (int)T;
+  a.blocks_z = (int)((max_seqlen + BQ - 1) / BQ);
+  a.scale = (float)scale;
+  a.scale_log2 = (float)(scale * 1.4426950408889634);
+  a.lse = lse.data_ptr<float>();
+  a.dd = dd.data_ptr<float>();
+  a.dqkv = reinterpret_cast<bf16*>(dqkv.data_ptr());
+  a.dqkv_row = (nq + 2 * nkv) * D;
+  a.err = err.data_ptr<int>();
+  ensure_smem_attr(fa_bwd_dkdv, SMEM_BWD);
+  ensure_smem_attr(fa_bwd_dq, SMEM_BWD);
+  fa_bwd_dkdv<<<dim3((unsigned)nkv, (unsigned)B, (unsigned)a.blocks_z), NT_BWD, SMEM_BWD, stream()>>>(tq, tdo, a);
+  PSRL_CHECK_LAUNCH();
+  fa_bwd_dq<<<dim3((unsigned)nq, (unsigned)B, (unsigned)a.blocks_z), NT_BWD, SMEM_BWD, stream()>>>(tq, tdo, a);
+  PSRL_CHECK_LAUNCH();
+  return dqkv;
+}
+
+}  // namespace psrl

@@ -41,6 +41,10 @@ at::Tensor tc_grouped_gemm(at::Tensor a, at::Tensor w, at::Tensor seg, at::Tenso
 at::Tensor tc_gemm2(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, c10::optional<at::Tensor> out, int64_t splits,
                     int64_t group_m, c10::optional<at::Tensor> bias, at::Tensor err);
 std::vector<at::Tensor> tc_gemm2_swiglu(at::Tensor x, at::Tensor w, int64_t group_m, at::Tensor err);
+std::vector<at::Tensor> attn_fwd_sm100(at::Tensor qkv, at::Tensor cu_seqlens, int64_t max_seqlen, int64_t nq,
+                                       int64_t nkv, double scale, bool want_lse, at::Tensor err);
+at::Tensor attn_bwd_sm100(at::Tensor qkv, at::Tensor o, at::Tensor dout, at::Tensor lse, at::Tensor cu_seqlens,
+                          int64_t max_seqlen, int64_t nq, int64_t nkv, double scale, at::Tensor err);
 std::vector<at::Tensor> moe_route(at::Tensor logits, c10::optional<at::Tensor> prior, int64_t k, bool renorm);
 std::vector<at::Tensor> moe_permute(at::Tensor ids, at::Tensor counts, int64_t bm, int64_t tiles_n);
 at::Tensor moe_gather(at::Tensor x, at::Tensor token_of_row);
@@ -87,6 +91,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_grouped_gemm", &psrl::tc_grouped_gemm);
   m.def("tc_gemm2", &psrl::tc_gemm2);
   m.def("tc_gemm2_swiglu", &psrl::tc_gemm2_swiglu);
+  m.def("attn_fwd_sm100", &psrl::attn_fwd_sm100);
+  m.def("attn_bwd_sm100", &psrl::attn_bwd_sm100);
   m.def("moe_route", &psrl::moe_route);
   m.def("moe_permute", &psrl::moe_permute);
   m.def("moe_gather", &psrl::moe_gather);

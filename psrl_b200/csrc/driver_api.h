@@ -26,6 +26,23 @@ inline void* entry(const char* name) {
   return fn;
 }
 
+// Driver-API calls act on the calling thread's current context, which the
+// runtime binds to a host thread only lazily.  A thread that has not made a
+// runtime call needing the context yet (a fresh worker thread, the autograd
+// engine's device thread) would call the driver with no current context, and
+// some entry points (cuTensorMapEncodeTiled among them) do not survive that.
+// cudaFree(nullptr) binds the current device's primary context; once per
+// thread and device.
+inline void bind_thread_context() {
+  thread_local int bound_dev = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
+  if (dev != bound_dev) {
+    cudaFree(nullptr);
+    bound_dev = dev;
+  }
+}
+
 }  // namespace drv
 }  // namespace psrl
 
@@ -34,6 +51,7 @@ inline void* entry(const char* name) {
 // pointer type follows cuda.h's (possibly versioned) declaration.
 #define PSRL_DRV(name)                                                                   \
   ([]() {                                                                                \
+    ::psrl::drv::bind_thread_context();                                                  \
     static const auto fn_ = reinterpret_cast<decltype(&::name)>(::psrl::drv::entry(#name)); \
     return fn_;                                                                          \
   }())

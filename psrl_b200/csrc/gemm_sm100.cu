@@ -38,7 +38,7 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr int NTHREADS = 192;
 constexpr int TMEM_COLS = 512;
-constexpr uint32_t WAIT_LIMIT = 1u << 26;  // bounded spins (seconds)
+constexpr uint64_t WAIT_NS = 2000000000ull;  // bound of every barrier wait (global timer ns)
 
 enum { EPI_STORE = 0, EPI_LSE = 1 };
 
@@ -113,9 +113,10 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint32_t a) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
 }
-// Bounded wait for the phase with the given parity; false on timeout.
+// Bounded wait for the phase with the given parity (at most WAIT_NS); false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity) {
-  for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
     uint32_t ok;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
@@ -123,8 +124,13 @@ __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity) {
         : "r"(a), "r"(parity)
         : "memory");
     if (ok) return true;
+    if ((i & 63) == 0) {
+      uint64_t t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t0 == 0) t0 = t;
+      else if (t - t0 > WAIT_NS) return false;
+    }
   }
-  return false;
 }
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t mbar) {

@@ -4,8 +4,8 @@
 // (cta_group::2) kernels use.
 //
 // Rules these helpers keep:
-//  * every wait is bounded (WAIT_LIMIT polls) and reports failure to the
-//    caller instead of spinning forever;
+//  * every wait is bounded (WAIT_NS of the global timer) and reports failure
+//    to the caller instead of spinning forever;
 //  * tile loads are plain per-CTA copies: each CTA fetches its own tiles, and
 //    a paired MMA reads the peer's half through the pair's shared tensor-core
 //    datapath, so no copy is ever broadcast to several CTAs.
@@ -17,7 +17,16 @@
 namespace psrl {
 namespace tc5 {
 
-constexpr uint32_t WAIT_LIMIT = 1u << 26;  // bounded polls (on the order of seconds)
+// Bound of every wait on a pipeline barrier, in nanoseconds of %globaltimer:
+// far above any legitimate wait inside one CTA's pipeline (microseconds), short
+// enough that a kernel whose producer died returns an error quickly.
+constexpr uint64_t WAIT_NS = 2000000000ull;
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -46,25 +55,16 @@ __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase with the given parity; false on timeout.
+// Bounded wait for the phase with the given parity (at most WAIT_NS); false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity) {
-  for (uint32_t i = 0; i < WAIT_LIMIT; ++i)
-    if (mbar_try(a, parity)) return true;
-  return false;
-}
-// Same, with acquire at cluster scope (the phase was completed by the peer CTA).
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t a, uint32_t parity) {
-  for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (ok) return true;
+  if (mbar_try(a, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try(a, parity)) return true;
+    if (global_ns() - t0 > WAIT_NS) return false;
   }
-  return false;
 }
 
 // ----------------------------------------------------------------- cluster
@@ -220,7 +220,32 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
                ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
                : "memory");
 }
+// 32 lanes x 16 / 32 consecutive 32-bit TMEM columns from registers
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+        "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+        "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 2^x on the special-function unit (PTX ex2.approx; 2^-inf = +0)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ void tmem_alloc_1cta(uint32_t slot_smem, uint32_t cols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot_smem), "r"(cols));

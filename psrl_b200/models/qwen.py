@@ -14,7 +14,9 @@ are split/merged by :mod:`psrl_b200.models.hf_io`.
 
 The forward runs over a packed (remove-padding) batch: ``input_ids`` [T],
 ``positions`` [T], ``cu_seqlens`` [B+1].  Hot ops go through
-:mod:`psrl_b200.ops` (sm_100a kernels on GPU).
+:mod:`psrl_b200.ops` (sm_100a kernels on GPU): the projections run on the
+paired-CTA tcgen05 GEMM (:mod:`psrl_b200.ops.linear`, SwiGLU fused into the
+gate_up epilogue), the ``nn.Linear`` modules only hold the parameters.
 """
 
 from __future__ import annotations
@@ -27,6 +29,7 @@ import torch.nn.functional as F
 from torch.utils.checkpoint import checkpoint
 
 from .. import ops
+from ..ops.linear import gate_up_swiglu, linear
 from .config import ModelArgs
 
 
@@ -42,7 +45,7 @@ class Attention(nn.Module):
 
     def forward(self, x, positions, cu_seqlens, max_seqlen):
         a = self.a
-        qkv = self.qkv(x)
+        qkv = linear(x, self.qkv.weight, self.qkv.bias)
         if a.qk_norm:
             T = qkv.shape[0]
             q, k, v = qkv.split([a.q_size, a.kv_size, a.kv_size], dim=-1)
@@ -51,7 +54,7 @@ class Attention(nn.Module):
             qkv = torch.cat([q, k, v], dim=-1)
         qkv = ops.rope_qkv(qkv.contiguous(), positions, a.num_heads, a.num_kv_heads, a.head_dim, a.rope_theta)
         o = ops.varlen_attention(qkv, cu_seqlens, max_seqlen, a.num_heads, a.num_kv_heads, a.head_dim)
-        return self.o(o)
+        return linear(o, self.o.weight)
 
 
 class MLP(nn.Module):
@@ -61,7 +64,7 @@ class MLP(nn.Module):
         self.down = nn.Linear(a.intermediate_size, a.hidden_size, bias=False)
 
     def forward(self, x):
-        return self.down(ops.swiglu(self.gate_up(x)))
+        return linear(gate_up_swiglu(x, self.gate_up.weight), self.down.weight)
 
 
 def zipf_prior(num_experts: int, alpha: float, seed: int = 1234) -> torch.Tensor:

@@ -1,7 +1,8 @@
 """Attention ops (K1, K2, K3).
 
 * :func:`varlen_attention` — causal attention over a packed batch (training,
-  remove-padding), autograd-enabled.  CUDA: ``attn_varlen_fwd/bwd``.
+  remove-padding), autograd-enabled.  CUDA: forward on the tcgen05 / TMEM
+  kernels ``attn_fwd_sm100`` / ``attn_bwd_sm100`` (``csrc/attn_sm100.cu``).
 * :func:`paged_prefill_attention` — chunked prefill against the paged KV cache.
 * :func:`paged_decode_attention` — one query token per sequence, split-KV.
 
@@ -80,26 +81,36 @@ class _VarlenAttnFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, qkv, cu_seqlens, max_seqlen, nq, nkv, d, scale):
         T = qkv.shape[0]
-        q = qkv[:, : nq * d].view(T, nq, d)
-        k = qkv[:, nq * d: (nq + nkv) * d].view(T, nkv, d)
-        v = qkv[:, (nq + nkv) * d:].view(T, nkv, d)
-        o, lse = ext().attn_varlen_fwd(q, k, v, cu_seqlens, max_seqlen, scale, True)
+        o, lse = varlen_attention_fwd(qkv, cu_seqlens, max_seqlen, nq, nkv, scale, want_lse=True)
+        o = o.view(T, nq, d)
         ctx.save_for_backward(qkv, o, lse, cu_seqlens)
         ctx.cfg = (max_seqlen, nq, nkv, d, scale)
         return o.view(T, nq * d)
 
     @staticmethod
     def backward(ctx, do):
+        from .gemm import _err
         qkv, o, lse, cu = ctx.saved_tensors
         max_seqlen, nq, nkv, d, scale = ctx.cfg
-        T = qkv.shape[0]
-        q = qkv[:, : nq * d].view(T, nq, d)
-        k = qkv[:, nq * d: (nq + nkv) * d].view(T, nkv, d)
-        v = qkv[:, (nq + nkv) * d:].view(T, nkv, d)
-        do = do.contiguous().view(T, nq, d)
-        dq, dk, dv = ext().attn_varlen_bwd(do, q, k, v, o, lse, cu, max_seqlen, scale)
-        dqkv = torch.cat([dq.view(T, -1), dk.view(T, -1), dv.view(T, -1)], dim=1)
+        if qkv.stride(1) != 1 or qkv.stride(0) % 8 or qkv.data_ptr() % 16:
+            qkv = qkv.contiguous()
+        # tcgen05 backward (csrc/attn_sm100.cu): dK/dV per key tile and dQ per
+        # query tile, written straight into one [T, (nq + 2 nkv) * d] gradient
+        dqkv = ext().attn_bwd_sm100(qkv, o.reshape(qkv.shape[0], nq * d), do.contiguous(), lse, cu, max_seqlen,
+                                    nq, nkv, scale, _err(qkv.device))
         return dqkv, None, None, None, None, None, None
+
+
+def varlen_attention_fwd(qkv: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int, nq: int, nkv: int,
+                         scale: float, want_lse: bool = True):
+    """Forward of causal varlen attention on the tcgen05 kernel
+    (``csrc/attn_sm100.cu``): ``qkv`` [T, (nq + 2 nkv) * 128] bf16 ->
+    (o [T, nq * 128] bf16, lse [nq, T] fp32 natural log)."""
+    from .gemm import _err
+    if qkv.stride(1) != 1 or qkv.stride(0) % 8 or qkv.data_ptr() % 16:
+        qkv = qkv.contiguous()
+    return ext().attn_fwd_sm100(qkv, cu_seqlens, int(max_seqlen), int(nq), int(nkv), float(scale), bool(want_lse),
+                                _err(qkv.device))
 
 
 def varlen_attention(qkv: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int, nq: int, nkv: int, d: int,
@@ -107,6 +118,8 @@ def varlen_attention(qkv: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: in
     """Causal attention over a packed batch; ``qkv`` [T, (nq+2nkv)*d] -> [T, nq*d]."""
     scale = scale if scale is not None else 1.0 / math.sqrt(d)
     if qkv.is_cuda and qkv.dtype == torch.bfloat16 and d == 128:
+        if not torch.is_grad_enabled() or not qkv.requires_grad:
+            return varlen_attention_fwd(qkv, cu_seqlens, max_seqlen, nq, nkv, scale, want_lse=False)[0]
         return _VarlenAttnFn.apply(qkv, cu_seqlens, int(max_seqlen), nq, nkv, d, scale)
     T = qkv.shape[0]
     q = qkv[:, : nq * d].view(T, nq, d)

@@ -21,7 +21,8 @@ _ERR: dict = {}
 def _err(device) -> torch.Tensor:
     e = _ERR.get(device)
     if e is None:
-        e = torch.zeros(1, dtype=torch.int32, device=device)
+        # [code, block x, block y, block z, warp, iteration, -, -] of the first failure
+        e = torch.zeros(8, dtype=torch.int32, device=device)
         _ERR[device] = e
     return e
 
@@ -30,10 +31,11 @@ def check_errors(device=None) -> None:
     for dev, e in _ERR.items():
         if device is not None and dev != device:
             continue
-        v = int(e.item())
-        if v:
+        rec = e.tolist()
+        if rec[0]:
             e.zero_()
-            raise RuntimeError(f"tcgen05 GEMM kernel reported error code {v} (bounded wait expired)")
+            raise RuntimeError(f"tcgen05 kernel reported error code {rec[0]} (a bounded wait expired; "
+                               f"block ({rec[1]}, {rec[2]}, {rec[3]}), warp {rec[4]}, iteration {rec[5]})")
 
 
 def supported(x: torch.Tensor, w: torch.Tensor) -> bool:

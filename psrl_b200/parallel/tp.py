@@ -31,9 +31,9 @@ from dataclasses import dataclass, replace
 import torch
 import torch.distributed as dist
 import torch.nn as nn
-import torch.nn.functional as F
 
 from .. import ops
+from ..ops.linear import gate_up_swiglu, linear
 
 
 @dataclass
@@ -107,7 +107,7 @@ class TPAttention(nn.Module):
     def forward(self, x, positions, cu_seqlens, max_seqlen):
         la = self.la
         x = copy_to_tp(x, self.tp)
-        qkv = F.linear(x, self.qkv_weight, self.qkv_bias)
+        qkv = linear(x, self.qkv_weight, self.qkv_bias)
         if la.qk_norm:
             T = qkv.shape[0]
             q, k, v = qkv.split([la.q_size, la.kv_size, la.kv_size], dim=-1)
@@ -116,7 +116,7 @@ class TPAttention(nn.Module):
             qkv = torch.cat([q, k, v], dim=-1)
         qkv = ops.rope_qkv(qkv.contiguous(), positions, la.num_heads, la.num_kv_heads, la.head_dim, la.rope_theta)
         o = ops.varlen_attention(qkv, cu_seqlens, max_seqlen, la.num_heads, la.num_kv_heads, la.head_dim)
-        return reduce_from_tp(F.linear(o, self.o_weight), self.tp)
+        return reduce_from_tp(linear(o, self.o_weight), self.tp)
 
 
 class TPMLP(nn.Module):
@@ -133,7 +133,7 @@ class TPMLP(nn.Module):
 
     def forward(self, x):
         x = copy_to_tp(x, self.tp)
-        return reduce_from_tp(F.linear(ops.swiglu(F.linear(x, self.gate_up_weight)), self.down_weight), self.tp)
+        return reduce_from_tp(linear(gate_up_swiglu(x, self.gate_up_weight), self.down_weight), self.tp)
 
 
 @torch.no_grad()

@@ -132,10 +132,14 @@ class ControlPlane:
     # --------------------------------------------------------------- trainer
     def _wait_ready(self, b: int, timeout_s: float) -> None:
         t0 = time.monotonic()
+        t_act = t0
         while not self.manager.buffer_ready(b):
             if self.failed:
                 raise RuntimeError(f"rollout instance failed: {self.failed}")
             now = time.monotonic()
+            if now - t_act > self.manager.filter_patience_s:
+                t_act = now
+                self.manager.handle_waiting_buffer(b)
             silent = [i for i, t in self.last_seen.items() if now - t > self.liveness_s]
             if silent or now - t0 > timeout_s:
                 raise TimeoutError(f"buffer {b} not ready: silent instances {silent}, {self.manager.snapshot()}")

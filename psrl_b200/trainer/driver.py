@@ -249,9 +249,13 @@ class RLTrainer:
     # -------------------------------------------------------------- step
     def wait_for_buffer(self, b: int, timeout_s: float = 3600.0) -> None:
         t0 = time.monotonic()
+        t_act = t0
         if self.overlap:
             self.start_rollout()
         while not self.manager.buffer_ready(b):
+            if time.monotonic() - t_act > self.manager.filter_patience_s:
+                t_act = time.monotonic()
+                self.manager.handle_waiting_buffer(b)
             if self.overlap:
                 if self._rollout_error is not None:
                     raise RuntimeError("rollout thread failed") from self._rollout_error
