@@ -195,6 +195,7 @@ def main():
                 "h2d_bytes_per_step": int(res["h2d"]), "d2h_bytes_per_step": int(res["d2h"])},
         "gpu_launches": int(res["launches"]),
         "breakdown_s_per_step": _breakdown(res["metrics"]),
+        "rollout_engines": (res.get("cp") or {}).get("rollout"),
         "weight_sync": _sync_summary(res),
     }
     print(json.dumps(line), flush=True)

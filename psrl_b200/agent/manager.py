@@ -107,6 +107,7 @@ class AgentLoopManager:
         self.started_at: dict[int, float] = {}      # request id -> time handed to an instance
         self.timed_out: set[int] = set()
         self.last_error: str | None = None
+        self.migration_target: dict[int, tuple] = {}   # request id -> instance it is moving to
         ps.on_abort_rollout = self._on_abort_rollout
 
     # ------------------------------------------------------------ dispatch
@@ -150,9 +151,15 @@ class AgentLoopManager:
             self.fill()
             self._check_trajectory_timeouts()
             out: list[GenRequest] = []
+            held: list[GenRequest] = []       # migrating to another instance: not for this one
             while self.queue and len(out) < max_n:
                 req = self.queue[0]
                 rid = req.request_id
+                tgt = self.migration_target.get(rid)
+                if tgt is not None and tgt != instance_id:
+                    held.append(self.queue.popleft())
+                    continue
+                self.migration_target.pop(rid, None)
                 if self.ps.check_aborted_requests(rid, remove=True):
                     self.queue.popleft()
                     self._member_dropped(rid)
@@ -172,7 +179,26 @@ class AgentLoopManager:
                         self.ps.update_request_version_tag(rid, instance_version)
                 self.started_at.setdefault(rid, time.monotonic())
                 out.append(req)
+            self.queue.extendleft(reversed(held))
             return out
+
+    def migrate(self, src, dst, n: int) -> int:
+        """Move up to ``n`` requests running on instance ``src`` to ``dst``
+        (load-balanced migration, reference ``sync_and_migrate/greedy.py``): the
+        source is told to interrupt them; their partial outputs come back as
+        ``abort`` results, are re-queued with the tokens generated so far and
+        are handed only to ``dst``, which resumes them after a re-prefill."""
+        with self.lock:
+            running = sorted(r for r in self.ps.get_dispatched_requests_of_instance(src)
+                             if self.ps.get_request_status(r)[0] is RequestStatus.ROLLOUT_RUNNING)
+            pending = self.pending_aborts.get(src, set())
+            pick = [r for r in running if r not in pending and r not in self.timed_out][-int(n):] if n > 0 else []
+            for rid in pick:
+                self.migration_target[rid] = dst
+            if pick:
+                self.pending_aborts.setdefault(src, set()).update(pick)
+                self.stats["migrated_requests"] = self.stats.get("migrated_requests", 0) + len(pick)
+            return len(pick)
 
     def _check_trajectory_timeouts(self) -> None:
         """Abort requests that have run longer than the trajectory timeout; their

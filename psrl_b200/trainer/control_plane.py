@@ -55,6 +55,17 @@ class ControlPlane:
         self.exchange_stats = {"calls": 0, "outputs": 0, "requests": 0}
         self.stores: dict[int, dict] = {}
         self.layout = None
+        # rollout coordination (C16): weight-sync gating and load-balanced
+        # migration over the instances' reported states
+        from ..rollout.coordinator import CoordinatorConfig, RolloutCoordinator
+        self.coord = RolloutCoordinator(CoordinatorConfig.from_cfg(cfg), self.ps.get_ps_model_version)
+        self.states: dict = {}
+        sm = cfg.psrl.rollout_coordination.sync_and_mig_strategy
+        self.coord_interval_s = float(sm.get("check_interval_in_ms", 100)) / 1000.0
+        self._last_mig = 0.0
+        self._granted: dict = {}
+        self.engine_stats: dict = {}     # instance -> phase -> engine counters
+        self.mig_stats = {"rounds": 0, "requests": 0}
         self._cv = threading.Condition()
         self._batches: dict[int, dict] = {}
         self._batch_locks: dict[int, threading.Lock] = {}
@@ -90,6 +101,16 @@ class ControlPlane:
         self.ps.register_rollout_instance(iid, int(version))
         self.last_seen[iid] = time.monotonic()
 
+    def report_sync_failure(self, instance_id, message: str) -> None:
+        """A weight pull failed on an instance: quarantine it (no more requests);
+        the rest of the run continues on the healthy instances."""
+        from ..rollout.router import InstanceState
+        iid = tuple(instance_id)
+        s = self.states.setdefault(iid, InstanceState(iid))
+        self.coord.syncing.discard(iid)
+        self.coord.quarantine(s)
+        self.sync_stats.setdefault("failures", []).append(f"{iid}: {message}")
+
     def report_failure(self, instance_id, message: str) -> None:
         self.failed[tuple(instance_id)] = message
 
@@ -100,18 +121,56 @@ class ControlPlane:
         self._done.set()
 
     # --------------------------------------------------------------- rollout
-    def exchange(self, instance_id, version: int, free_slots: int, outputs: list):
+    def exchange(self, instance_id, version: int, free_slots: int, outputs: list, state: dict | None = None):
+        """One round trip of a rollout instance: finished trajectories in; new
+        requests, aborts (staleness aborts and migration moves), the PS version,
+        the run phase and the coordinator's sync decision out."""
         iid = tuple(instance_id)
-        self.last_seen[iid] = time.monotonic()
+        now = time.monotonic()
+        self.last_seen[iid] = now
         if outputs:
             self.manager.on_complete(outputs, iid)
-        reqs = self.manager.take_work(iid, int(version), int(free_slots)) if free_slots > 0 else []
+        sync = self._coordinate(iid, int(version), state, now)
+        quarantined = iid in self.coord.quarantined
+        reqs = self.manager.take_work(iid, int(version), int(free_slots)) if free_slots > 0 and not quarantined \
+            else []
         aborts = self.manager.take_aborts(iid)
         st = self.exchange_stats
         st["calls"] += 1
         st["outputs"] += len(outputs)
         st["requests"] += len(reqs)
-        return reqs, aborts, self.ps.get_ps_model_version(), self.phase
+        return reqs, aborts, self.ps.get_ps_model_version(), self.phase, sync
+
+    def _coordinate(self, iid, version: int, state: dict | None, now: float) -> bool:
+        """Update the instance's state; decide whether it syncs now and, every
+        check interval, plan a migration round between instances."""
+        from ..rollout.router import InstanceState
+        s = self.states.get(iid)
+        if s is None:
+            s = self.states[iid] = InstanceState(iid)
+        s.version = version
+        if state:
+            s.num_running = int(state.get("running", 0))
+            s.num_waiting = int(state.get("waiting", 0))
+            s.kv_usage = float(state.get("kv_usage", 0.0))
+            s.throughput = float(state.get("throughput", 0.0))
+        if iid in self.coord.syncing and (version >= self.ps.get_ps_model_version()
+                                          or now - self._granted.get(iid, now) > 60.0):
+            self.coord.syncing.discard(iid)        # the instance reports the new version (or the grant lapsed)
+            s.paused = False
+        sync = self.coord.should_sync(s)
+        if sync:
+            self.coord.syncing.add(iid)
+            self._granted[iid] = now
+            s.paused = True
+        if self.coord.cfg.mig_enable and now - self._last_mig >= self.coord_interval_s:
+            self._last_mig = now
+            for src, dst, n in self.coord.plan_migration(list(self.states.values())):
+                moved = self.manager.migrate(src, dst, n)
+                if moved:
+                    self.mig_stats["rounds"] += 1
+                    self.mig_stats["requests"] += moved
+        return sync
 
     def acquire_pull(self, timeout: float = 600.0) -> bool:
         return self.ps.acquire_shared_pull(timeout)
@@ -125,9 +184,38 @@ class ControlPlane:
             self.report_pull(seconds)
         return v
 
-    def report_pull(self, seconds: float) -> None:
+    def report_engine(self, instance_id, phase: int, stats: dict) -> None:
+        """Engine counters of a rollout instance at a phase boundary of the run."""
+        self.engine_stats.setdefault(tuple(instance_id), {})[int(phase)] = dict(stats)
+
+    def rollout_summary(self) -> dict | None:
+        """Rollout engines over the timed region (between phase 1 and 2 reports),
+        summed over instances: generated tokens, decode / prefill time and rate,
+        idle time, preemptions."""
+        keys = ("decode_tokens", "decode_steps", "decode_time", "prefill_tokens", "prefill_time", "idle_time",
+                "preemptions", "cached_tokens")
+        tot = {k: 0.0 for k in keys}
+        n = 0
+        for per in self.engine_stats.values():
+            if 1 in per and 2 in per:
+                n += 1
+                for k in keys:
+                    tot[k] += per[2].get(k, 0.0) - per[1].get(k, 0.0)
+        if not n:
+            return None
+        out = {"instances": n, **{k: round(v, 3) for k, v in tot.items()}}
+        out["decode_tok_per_s_per_instance"] = round(tot["decode_tokens"] / max(tot["decode_time"], 1e-9), 1)
+        out["prefill_tok_per_s_per_instance"] = round(tot["prefill_tokens"] / max(tot["prefill_time"], 1e-9), 1)
+        return out
+
+    def report_pull(self, seconds: float, instance_id=None, from_version: int = -1, to_version: int = -1,
+                    interrupted: int = 0) -> None:
         self.sync_stats["pulls"] += 1
         self.sync_stats["pull_s"] += float(seconds)
+        if instance_id is not None:
+            from ..rollout.coordinator import SyncRecord
+            self.coord.history.append(SyncRecord(tuple(instance_id), int(from_version), int(to_version),
+                                                 float(seconds), int(interrupted), True))
 
     # --------------------------------------------------------------- trainer
     def _wait_ready(self, b: int, timeout_s: float) -> None:
@@ -248,7 +336,9 @@ class ControlPlane:
 
     def stats(self) -> dict:
         return {"sync": dict(self.sync_stats), "exchange": dict(self.exchange_stats),
-                "manager": self.manager.snapshot(), "ps_version": self.ps.get_ps_model_version()}
+                "manager": self.manager.snapshot(), "ps_version": self.ps.get_ps_model_version(),
+                "rollout": self.rollout_summary(), "migration": dict(self.mig_stats),
+                "quarantined": sorted(map(list, self.coord.quarantined))}
 
 
 def _control_plane_main(cfg, vocab_size: int, n_train: int, port: int, liveness_s: float, ready=None) -> None:
@@ -314,6 +404,8 @@ class ExchangeMailbox:
         self.idle_interval = float(idle_interval)
         self.ps_version = int(engine.version)
         self.phase = 0
+        self.sync_granted = False   # the coordinator's go-ahead for a weight pull
+        self._tp_mark = (time.monotonic(), 0)
         self.error: BaseException | None = None
         self._lock = threading.Lock()
         self._outputs: list = []
@@ -341,6 +433,18 @@ class ExchangeMailbox:
     def kick(self) -> None:
         self._wake.set()
 
+    def take_sync_grant(self) -> bool:
+        with self._lock:
+            g, self.sync_granted = self.sync_granted, False
+        return g
+
+    def _throughput(self) -> float:
+        """Generated tokens per second since the previous report."""
+        t0, n0 = self._tp_mark
+        now, n = time.monotonic(), int(self.engine.stats.get("decode_tokens", 0))
+        self._tp_mark = (now, n)
+        return (n - n0) / max(now - t0, 1e-6)
+
     def _loop(self) -> None:
         last = 0.0
         eng = self.engine
@@ -357,11 +461,15 @@ class ExchangeMailbox:
                     outs, self._outputs = self._outputs, []
                     queued = len(self._reqs)
                 free = max(0, eng.max_num_seqs - eng.num_unfinished() - queued)
-                reqs, aborts, v, phase = self.proxy.exchange(self.instance_id, eng.version, free, outs)
+                state = {"running": len(eng.running), "waiting": len(eng.waiting) + queued,
+                         "kv_usage": float(eng.bm.usage()), "throughput": self._throughput()}
+                reqs, aborts, v, phase, sync = self.proxy.exchange(self.instance_id, eng.version, free, outs, state)
                 last = time.monotonic()
                 with self._lock:
                     self._reqs.extend(reqs)
                     self._aborts.extend(aborts)
+                    if sync:
+                        self.sync_granted = True
                 self.ps_version = int(v)
                 self.phase = int(phase)
         except BaseException as exc:     # surfaced to the engine loop by collect()

@@ -286,8 +286,19 @@ class DisaggregatedRun:
                 torch.cuda.current_stream().synchronize()
         finally:
             self.cp.release_pull()
+        from_v = self.engine.version
+        in_flight = self.engine.num_unfinished()
         self.engine.load_weights(None, v)
-        self.cp.report_pull(time.perf_counter() - t0)
+        self.cp.report_pull(time.perf_counter() - t0, self.instance_id, from_v, v,
+                            0 if self.engine.keep_kv_on_update else in_flight)
+
+    def _coordinated_pull(self) -> None:
+        """Pull granted by the control plane's coordinator; a failure quarantines
+        this instance (it gets no more work) instead of ending the run."""
+        try:
+            self._pull()
+        except Exception as exc:
+            self.cp.report_sync_failure(self.instance_id, f"{type(exc).__name__}: {exc}")
 
     def rollout_loop(self, on_phase) -> None:
         """Serve until the driver reaches the final phase; ``on_phase(p)`` runs the
@@ -297,6 +308,7 @@ class DisaggregatedRun:
             eng.capture_all()
         self.mailbox = mb = ExchangeMailbox(self.cp, self.instance_id, eng)
         seen = 0
+        idle_s = 0.0
         try:
             while True:
                 reqs, aborts = mb.collect()
@@ -306,18 +318,23 @@ class DisaggregatedRun:
                     eng.abort(rid)
                 while seen < mb.phase:
                     seen += 1
+                    # engine counters at the start / end of the timed region
+                    self.cp.report_engine(self.instance_id, seen,
+                                          {**{k: float(v) for k, v in eng.stats.items()}, "idle_time": idle_s})
                     on_phase(seen)
                 if seen >= 2:
                     return
-                if self.policy.should_sync(eng, mb.ps_version):
-                    self._pull()
+                if mb.take_sync_grant() and mb.ps_version > eng.version:
+                    self._coordinated_pull()
                 if eng.has_unfinished():
                     outs = eng.step()
                     if outs:
                         mb.post(outs)
                 else:
                     mb.kick()
+                    t_idle = time.perf_counter()
                     time.sleep(0.0005)
+                    idle_s += time.perf_counter() - t_idle
         finally:
             mb.close()
             self.mailbox = None
