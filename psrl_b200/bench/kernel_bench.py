@@ -113,6 +113,33 @@ def bench_gemm(pk):
     return out
 
 
+def bench_decode_gemm(pk):
+    """Decode-step projections of the Qwen2.5-3B engine (B rows = sequences in
+    the batch): the weight-streaming tcgen05 kernel against cuBLAS through
+    torch.  Reported as weight bandwidth (the bytes a decode step must stream)
+    and FLOP rate."""
+    from psrl_b200.ops.linear import decode_linear, decode_splits
+    out = []
+    shapes = (("qkv", 2560, 2048), ("o", 2048, 2048), ("gate_up", 22016, 2048), ("down", 2048, 11008),
+              ("lm_head", 151936, 2048))
+    ws = torch.zeros(512 * 22016, device="cuda")
+    for B in (16, 64, 128, 256):
+        for name, N, K in shapes:
+            x = torch.randn(B, K, device="cuda").bfloat16()
+            w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+            use_ws = ws if name != "lm_head" else None
+            ms_tc = timeit(lambda: decode_linear(x, w, None, use_ws), iters=20)
+            ms_cb = timeit(lambda: x @ w.t(), iters=20)
+            wb = N * K * 2
+            out.append({"case": f"decode {name} B={B} N={N} K={K}", "tcgen05_us": round(ms_tc * 1e3, 1),
+                        "cublas_us": round(ms_cb * 1e3, 1), "vs_cublas": round(ms_cb / ms_tc, 3),
+                        "splits": decode_splits(N, K) if use_ws is not None else 1,
+                        "weight_GB/s_tcgen05": round(wb / ms_tc / 1e6, 1),
+                        "frac_hbm_tcgen05": round(wb / ms_tc / 1e6 / pk["hbm_gbs"], 3)})
+            del x, w
+    return out
+
+
 def bench_logprob(pk):
     from psrl_b200.ops.gemm import tc_linear_logprob
     from psrl_b200.ops.logprob import linear_logprob
@@ -262,7 +289,7 @@ def bench_train_mb(pk):
              "frac_bf16": round(fl / ms / 1e9 / pk["bf16_tflops"], 3)}]
 
 
-CASES = {"train_mb": bench_train_mb, "sample": bench_sample, "decode": bench_decode, "gemm": bench_gemm, "logprob": bench_logprob, "attn": bench_attn_train,
+CASES = {"decode_gemm": bench_decode_gemm, "train_mb": bench_train_mb, "sample": bench_sample, "decode": bench_decode, "gemm": bench_gemm, "logprob": bench_logprob, "attn": bench_attn_train,
          "elementwise": bench_elementwise, "sync": bench_sync}
 
 

@@ -27,6 +27,7 @@ def main(argv=None):
     ap.add_argument("--block-size", type=int, default=64)
     ap.add_argument("--kv-cache-gb", type=float, default=40.0)
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--decode-gemm", default="library", choices=["library", "tcgen05"])
     args = ap.parse_args(argv)
     from psrl_b200.models import PRESETS, build_model
     from psrl_b200.rollout import EngineWeights, GenRequest, RolloutEngine, SamplingParams
@@ -39,7 +40,7 @@ def main(argv=None):
     torch.cuda.empty_cache()
     eng = RolloutEngine(a, w, max_num_seqs=args.max_num_seqs, max_model_len=args.prompt_len + args.output_len + 64,
                         block_size=args.block_size, kv_cache_gb=args.kv_cache_gb, use_cuda_graph=not args.no_graph,
-                        enable_prefix_caching=False)
+                        enable_prefix_caching=False, decode_gemm=args.decode_gemm)
     g = torch.Generator().manual_seed(0)
 
     def submit(base, n):

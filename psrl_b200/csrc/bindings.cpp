@@ -41,6 +41,13 @@ at::Tensor tc_grouped_gemm(at::Tensor a, at::Tensor w, at::Tensor seg, at::Tenso
 at::Tensor tc_gemm2(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, c10::optional<at::Tensor> out, int64_t splits,
                     int64_t group_m, c10::optional<at::Tensor> bias, at::Tensor err);
 std::vector<at::Tensor> tc_gemm2_swiglu(at::Tensor x, at::Tensor w, int64_t group_m, at::Tensor err);
+void tc_gemm2_allreduce2(at::Tensor a, at::Tensor b, bool b_mn, at::Tensor acc_local, at::Tensor acc_peer,
+                         int64_t group_m, at::Tensor err);
+void peer_barrier(std::vector<at::Tensor> flags_in_peer, std::vector<at::Tensor> own_slots, int64_t epoch,
+                  double timeout_s, at::Tensor err);
+void acc_finalize(at::Tensor acc, at::Tensor out, c10::optional<at::Tensor> bias);
+at::Tensor tc_gemm_skinny(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias, int64_t splits,
+                          c10::optional<at::Tensor> ws, at::Tensor err);
 std::vector<at::Tensor> attn_fwd_sm100(at::Tensor qkv, at::Tensor cu_seqlens, int64_t max_seqlen, int64_t nq,
                                        int64_t nkv, double scale, bool want_lse, at::Tensor err);
 at::Tensor attn_bwd_sm100(at::Tensor qkv, at::Tensor o, at::Tensor dout, at::Tensor lse, at::Tensor cu_seqlens,
@@ -91,6 +98,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_grouped_gemm", &psrl::tc_grouped_gemm);
   m.def("tc_gemm2", &psrl::tc_gemm2);
   m.def("tc_gemm2_swiglu", &psrl::tc_gemm2_swiglu);
+  m.def("tc_gemm_skinny", &psrl::tc_gemm_skinny);
+  m.def("tc_gemm2_allreduce2", &psrl::tc_gemm2_allreduce2);
+  m.def("peer_barrier", &psrl::peer_barrier);
+  m.def("acc_finalize", &psrl::acc_finalize);
   m.def("attn_fwd_sm100", &psrl::attn_fwd_sm100);
   m.def("attn_bwd_sm100", &psrl::attn_bwd_sm100);
   m.def("moe_route", &psrl::moe_route);

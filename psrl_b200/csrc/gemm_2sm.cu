@@ -31,6 +31,10 @@
 //   OUT_BF16    C (bf16) = acc.
 //   OUT_F32_ADD C (fp32) += acc with TMA reduce-add tiles: split-K partial
 //               sums and accumulation into an existing fp32 buffer.
+//   OUT_F32_ADD2 the same tile added into two fp32 buffers, this GPU's and the
+//               tensor-parallel peer's (a mapping of its memory over NVLink):
+//               a row-parallel GEMM whose all-reduce happens in the epilogue,
+//               tile by tile, while later tiles are still being computed.
 //   OUT_SWIGLU  gate_up projection: the B half of CTA 0 is gate rows
 //               [128 j, 128 j + 128) and that of CTA 1 the matching up rows
 //               I + 128 j ..., so every accumulator row holds gate and up side
@@ -68,7 +72,7 @@ constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
 constexpr int NTHREADS = 192;
 constexpr int TMEM_COLS = 512;
 
-enum { OUT_BF16 = 0, OUT_F32_ADD = 1, OUT_SWIGLU = 2 };
+enum { OUT_BF16 = 0, OUT_F32_ADD = 1, OUT_SWIGLU = 2, OUT_F32_ADD2 = 3 };
 
 struct Args {
   int M, N, K;
@@ -133,6 +137,18 @@ struct StoreRing {
       const uint32_t src = smem_u32(base + next * STG_BYTES);
       if (reduce_add) tma_reduce_add_2d(map, src, x, y);
       else tma_store_2d(map, src, x, y);
+      bulk_commit();
+    }
+    next ^= 1;
+  }
+  // the same staged tile added into two tensors (this GPU's and a peer's)
+  __device__ __forceinline__ void reduce2(int lane, const CUtensorMap* m0, const CUtensorMap* m1, int x, int y) {
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      const uint32_t src = smem_u32(base + next * STG_BYTES);
+      tma_reduce_add_2d(m0, src, x, y);
+      tma_reduce_add_2d(m1, src, x, y);
       bulk_commit();
     }
     next ^= 1;
@@ -346,7 +362,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
           tmem_ld32(taddr + c * 32, r);
           tmem_wait_ld();
           stage_row_f32(ring.acquire(lane), lane, r);
-          ring.store(lane, &tmC, cb, row0, true);
+          if constexpr (OUT == OUT_F32_ADD2) ring.reduce2(lane, &tmC, &tmH, cb, row0);
+          else ring.store(lane, &tmC, cb, row0, true);
         }
       }
       fence_before();
@@ -513,6 +530,46 @@ at::Tensor tc_gemm2(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, c10::optio
   if (out.has_value()) dispatch2<OUT_F32_ADD>(a_mn, b_mn, ta, tb, tc, args);
   else dispatch2<OUT_BF16>(a_mn, b_mn, ta, tb, tc, args);
   return c;
+}
+
+// Tensor-parallel row-parallel GEMM with the all-reduce in the epilogue (two
+// ranks): every output tile of A B^T is added, with TMA reduce-add, into
+// `acc_local` (this GPU) and `acc_peer` (the peer's accumulator, mapped into
+// this process over NVLink).  Both accumulators are fp32 [M, N] and zero on
+// entry on both ranks; once both ranks' kernels have finished (the caller's
+// cross-GPU barrier) each holds the full sum.  The two fp32 additions into a
+// zero commute exactly, so both ranks hold bit-identical sums.
+void tc_gemm2_allreduce2(at::Tensor a, at::Tensor b, bool b_mn, at::Tensor acc_local, at::Tensor acc_peer,
+                         int64_t group_m, at::Tensor err) {
+  CHECK_CUDA_TENSOR(a);
+  CHECK_DTYPE(a, at::kBFloat16);
+  CHECK_DTYPE(b, at::kBFloat16);
+  CHECK_DTYPE(acc_local, at::kFloat);
+  CHECK_DTYPE(acc_peer, at::kFloat);
+  const int64_t M = a.size(0), K = a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0), Kb = b_mn ? b.size(0) : b.size(1);
+  TORCH_CHECK(K == Kb, "K mismatch");
+  TORCH_CHECK(acc_local.dim() == 2 && acc_local.size(0) == M && acc_local.size(1) == N &&
+                  acc_peer.dim() == 2 && acc_peer.size(0) == M && acc_peer.size(1) == N,
+              "accumulators must be fp32 [M, N]");
+  at::cuda::CUDAGuard g(a.device());
+  if (M == 0 || N == 0) return;
+  Args args{};
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.tiles_m = (int)((M + TM - 1) / TM);
+  args.tiles_n = (int)((N + TN - 1) / TN);
+  args.kblocks = (int)((K + BK - 1) / BK);
+  args.splits = 1;
+  args.num_tiles = args.tiles_m * args.tiles_n;
+  args.num_units = args.num_tiles;
+  args.group_m = (int)std::max<int64_t>(1, group_m);
+  args.err = err.data_ptr<int>();
+  const CUtensorMap ta = make_map_2d(a, HM), tb = make_map_2d(b, b_mn ? 64 : HN);
+  const CUtensorMap tl = make_store_map(acc_local), tp = make_store_map(acc_peer);
+  if (b_mn) launch2<OUT_F32_ADD2, false, true>(ta, tb, tl, tp, args);
+  else launch2<OUT_F32_ADD2, false, false>(ta, tb, tl, tp, args);
 }
 
 // Fused gate_up projection + SwiGLU: x [M, K] (bf16), w [2 I, K] (gate rows

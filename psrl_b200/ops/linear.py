@@ -115,8 +115,60 @@ def gate_up_swiglu(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """``silu(x Wg^T) * (x Wu^T)`` for the fused ``w = [Wg; Wu]``."""
     if x.is_cuda and x.dtype == torch.bfloat16:
         x2 = x.reshape(-1, x.shape[-1]).contiguous()
-        if not supported(x2, w) or (w.shape[0] // 2) % 128:
+        if not supported(x2, w):
             raise RuntimeError(f"tcgen05 gate_up: unsupported operands x{tuple(x2.shape)} w{tuple(w.shape)}")
+        if (w.shape[0] // 2) % 128:
+            # the fused epilogue pairs 128-row gate and up blocks; other widths
+            # run the projection and the activation as two kernels
+            from .activation import swiglu
+            return swiglu(linear(x2, w)).reshape(*x.shape[:-1], w.shape[0] // 2)
         return _GateUpSwiGLUFn.apply(x2, w).reshape(*x.shape[:-1], w.shape[0] // 2)
     from .activation import swiglu_ref
     return swiglu_ref(F.linear(x, w))
+
+
+# ------------------------------------------------------------------- decode
+def decode_splits(n: int, k: int, sms: int = 148) -> int:
+    """K-splits for the weight-streaming decode GEMM: enough (weight slab,
+    split) units to cover every SM, each streaming at least two 64-deep
+    k-blocks."""
+    tiles = -(-n // 128)
+    kblocks = -(-k // 64)
+    if tiles >= sms:
+        return 1
+    return max(1, min(-(-sms // tiles), kblocks // 2))
+
+
+# above this many rows a decode GEMM is compute-bound: the paired 256 x 256 tile
+# kernel with split-K replaces the weight-streaming kernel
+SKINNY_MAX_ROWS = 64
+
+
+def decode_linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None,
+                  ws: torch.Tensor | None = None) -> torch.Tensor:
+    """``x W^T + b`` for a decode step's ``x`` ([B, K], one row per sequence).
+
+    * B <= 64: weight-streaming tcgen05 kernel (``csrc/gemm_skinny.cu``): the
+      weight fills the MMA's M dimension, the K loop is split over CTAs.
+    * larger B: the paired-CTA tcgen05 GEMM (``csrc/gemm_2sm.cu``) with split-K
+      partial sums added into ``ws``, then one pass converts to bf16, adds the
+      bias and zeroes ``ws``.
+    ``ws``: fp32 workspace of at least ``B * N`` zeros (kept zero); without it
+    the K loop is not split."""
+    n, k = w.shape
+    B = x.shape[0]
+    if B <= SKINNY_MAX_ROWS or ws is None:
+        splits = decode_splits(n, k) if ws is not None else 1
+        if B <= 256:
+            return ext().tc_gemm_skinny(x, w, b, splits, ws, _err(x.device))
+        return torch.cat([ext().tc_gemm_skinny(x[i:i + 256], w, b, splits, ws, _err(x.device))
+                          for i in range(0, B, 256)], 0)
+    if ws.numel() < B * n:
+        raise ValueError(f"decode workspace of {ws.numel()} floats is smaller than {B} x {n}")
+    tiles = -(-B // 256) * -(-n // 256)
+    splits = max(1, min(-(-2 * _PAIRS // tiles), -(-k // 64) // 4))
+    acc = ws[: B * n].view(B, n)
+    ext().tc_gemm2(x, w, False, False, acc, splits, GROUP_M, None, _err(x.device))
+    y = torch.empty(B, n, dtype=x.dtype, device=x.device)
+    ext().acc_finalize(acc, y, b)
+    return y

@@ -1,10 +1,10 @@
 """Fused LM-head log-probability (K8) and its backward.
 
 ``linear_logprob(h, W, labels)`` returns per-token log pi(label) and entropy
-without ever materialising fp32 logits for the whole batch: logits are
-produced one token chunk at a time (bf16 GEMM), reduced by a single-pass
-online log-sum-exp kernel (``csrc/logprob.cu``), and recomputed in backward
-where the softmax gradient is written in place before the two backward GEMMs.
+without materialising logits in the forward (fused tcgen05 GEMM + log-sum-exp
+epilogue); the backward recomputes bf16 logits one token chunk at a time on
+the tcgen05 GEMM, writes the softmax gradient in place (``csrc/logprob.cu``)
+and runs the two backward GEMMs on tcgen05 as well.
 """
 
 from __future__ import annotations
@@ -28,45 +28,46 @@ def linear_logprob_ref(h, W, labels, temperature: float = 1.0, want_entropy: boo
 
 
 class _LinearLogprobFn(torch.autograd.Function):
+    """Training LM head on the tcgen05 kernels.
+
+    Forward: the fused GEMM + log-sum-exp kernel (``csrc/gemm_sm100.cu``
+    EPI_LSE) over all T rows at once; no logits reach memory.  Backward, per
+    chunk of rows: logits recomputed by the paired tcgen05 GEMM (bf16), their
+    log-sum-exp and entropy re-derived from those same bf16 logits (so the
+    softmax gradient sums to zero over the vocabulary), the softmax gradient
+    written in place, then dH = dZ W and dW += dZ^T H as tcgen05 GEMMs reading
+    dZ and H in place (MN-major), dW accumulated in fp32 by TMA reduce-add."""
+
     @staticmethod
     def forward(ctx, h, W, labels, temperature, chunk):
-        T = h.shape[0]
-        lps, ents, lses = [], [], []
-        for s in range(0, T, chunk):
-            logits = h[s: s + chunk] @ W.t()
-            lp, ent, lse = ext().logprob_fwd(logits, labels[s: s + chunk], temperature, True)
-            lps.append(lp)
-            ents.append(ent)
-            lses.append(lse)
-        lp = torch.cat(lps) if len(lps) > 1 else lps[0]
-        ent = torch.cat(ents) if len(ents) > 1 else ents[0]
-        lse = torch.cat(lses) if len(lses) > 1 else lses[0]
-        ctx.save_for_backward(h, W, labels, lse, ent)
+        from . import gemm as tc
+        lp, ent, _ = tc.tc_linear_logprob(h, W, labels, temperature)
+        ctx.save_for_backward(h, W, labels)
         ctx.cfg = (temperature, chunk)
         return lp, ent
 
     @staticmethod
     def backward(ctx, glp, gent):
-        h, W, labels, lse, ent = ctx.saved_tensors
+        from .linear import matmul_nt
+        h, W, labels = ctx.saved_tensors
         temperature, chunk = ctx.cfg
         T = h.shape[0]
         dh = torch.empty_like(h)
-        dW = None
+        dW32 = torch.zeros(W.shape, dtype=torch.float32, device=W.device)
         for s in range(0, T, chunk):
             hc = h[s: s + chunk]
-            logits = hc @ W.t()
+            lab = labels[s: s + chunk]
+            logits = matmul_nt(hc, W)
+            _, ent_c, lse_c = ext().logprob_fwd(logits, lab, temperature, True)
             ext().logprob_bwd_(
-                logits, labels[s: s + chunk], temperature,
+                logits, lab, temperature,
                 glp[s: s + chunk].contiguous().float() if glp is not None else None,
                 gent[s: s + chunk].contiguous().float() if gent is not None else None,
-                lse[s: s + chunk], ent[s: s + chunk])
-            dh[s: s + chunk] = logits @ W
-            part = logits.t() @ hc
-            if T <= chunk:
-                dW = part
-            else:
-                dW = part.float() if dW is None else dW.add_(part.float())
-        return dh, dW.to(W.dtype), None, None, None
+                lse_c, ent_c)
+            dh[s: s + chunk] = matmul_nt(logits, W, b_mn=True)
+            matmul_nt(logits, hc, a_mn=True, b_mn=True, out=dW32)
+            del logits
+        return dh, dW32.to(W.dtype), None, None, None
 
 
 def linear_logprob(h: torch.Tensor, W: torch.Tensor, labels: torch.Tensor, temperature: float = 1.0,
@@ -76,13 +77,13 @@ def linear_logprob(h: torch.Tensor, W: torch.Tensor, labels: torch.Tensor, tempe
     if h.is_cuda and h.dtype == torch.bfloat16:
         needs_grad = torch.is_grad_enabled() and (h.requires_grad or W.requires_grad)
         from . import gemm as tc
-        if not needs_grad and USE_TCGEN05 and tc.supported(h, W):
+        if not (USE_TCGEN05 and tc.supported(h, W)):
+            raise RuntimeError(f"tcgen05 LM head: unsupported operands h{tuple(h.shape)} W{tuple(W.shape)}")
+        if not needs_grad:
             # inference (old / reference log-probs): fused tcgen05 GEMM + log-sum-exp
             # epilogue, the [T, V] logits never leave tensor memory
             lp, ent, _ = tc.tc_linear_logprob(h, W, labels, temperature)
             return lp, ent
-        # training: chunked logits in bf16, recomputed in backward (one consistent
-        # rounding of the logits in both directions)
         return _LinearLogprobFn.apply(h, W, labels, float(temperature), int(chunk))
     return linear_logprob_ref(h, W, labels, temperature)
 

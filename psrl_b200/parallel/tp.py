@@ -41,10 +41,24 @@ class TPGroup:
     group: object
     world: int
     rank: int
+    # fused GEMM + all-reduce over NVLink (parallel/tp_fused.py) for CUDA pairs;
+    # None: local GEMM then an NCCL (or gloo) all-reduce
+    fused: object = None
+
+    def fused_fits(self, x, n_out: int) -> bool:
+        f = self.fused
+        return f is not None and x.is_cuda and x.reshape(-1, x.shape[-1]).shape[0] * n_out <= f.max_elems
 
 
-def make_tp_group(group) -> TPGroup:
-    return TPGroup(group, dist.get_world_size(group), dist.get_rank(group))
+def make_tp_group(group, device=None, fused_max_elems: int = 0) -> TPGroup:
+    """TP group handle; with ``fused_max_elems`` > 0, a CUDA device and two
+    ranks, the row-parallel GEMMs (and the column-parallel data gradients)
+    run as fused GEMM + all-reduce kernels with accumulators of that size."""
+    tp = TPGroup(group, dist.get_world_size(group), dist.get_rank(group))
+    if fused_max_elems > 0 and tp.world == 2 and device is not None and torch.device(device).type == "cuda":
+        from .tp_fused import FusedTP
+        tp.fused = FusedTP(group, device, fused_max_elems)
+    return tp
 
 
 class _CopyToTP(torch.autograd.Function):
@@ -106,8 +120,13 @@ class TPAttention(nn.Module):
 
     def forward(self, x, positions, cu_seqlens, max_seqlen):
         la = self.la
-        x = copy_to_tp(x, self.tp)
-        qkv = linear(x, self.qkv_weight, self.qkv_bias)
+        T = x.shape[0]
+        if self.tp.fused_fits(x, self.a.hidden_size):
+            from .tp_fused import column_parallel
+            qkv = column_parallel(x, self.qkv_weight, self.qkv_bias, self.tp.fused)
+        else:
+            x = copy_to_tp(x, self.tp)
+            qkv = linear(x, self.qkv_weight, self.qkv_bias)
         if la.qk_norm:
             T = qkv.shape[0]
             q, k, v = qkv.split([la.q_size, la.kv_size, la.kv_size], dim=-1)
@@ -116,6 +135,9 @@ class TPAttention(nn.Module):
             qkv = torch.cat([q, k, v], dim=-1)
         qkv = ops.rope_qkv(qkv.contiguous(), positions, la.num_heads, la.num_kv_heads, la.head_dim, la.rope_theta)
         o = ops.varlen_attention(qkv, cu_seqlens, max_seqlen, la.num_heads, la.num_kv_heads, la.head_dim)
+        if self.tp.fused_fits(o, self.a.hidden_size) and T == o.shape[0]:
+            from .tp_fused import row_parallel
+            return row_parallel(o, self.o_weight, self.tp.fused)
         return reduce_from_tp(linear(o, self.o_weight), self.tp)
 
 
@@ -132,6 +154,11 @@ class TPMLP(nn.Module):
         self.down_weight = nn.Parameter(full.down.weight.data[:, r * il:(r + 1) * il].clone())
 
     def forward(self, x):
+        hidden = self.down_weight.shape[0]
+        if self.tp.fused_fits(x, hidden):
+            from .tp_fused import column_parallel, row_parallel
+            h = ops.swiglu(column_parallel(x, self.gate_up_weight, None, self.tp.fused))
+            return row_parallel(h, self.down_weight, self.tp.fused)
         x = copy_to_tp(x, self.tp)
         return reduce_from_tp(linear(gate_up_swiglu(x, self.gate_up_weight), self.down_weight), self.tp)
 

@@ -33,6 +33,8 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from .. import ops
+from ..ops.linear import decode_linear, gate_up_swiglu
+from ..ops.linear import linear as linear_tc
 from ..utils import transfer
 from ..models.config import ModelArgs
 from .kv_cache import BlockManager, allocate_kv_tensors
@@ -136,13 +138,31 @@ class EngineWeights:
     def lm_head(self) -> torch.Tensor:
         return self.tensors["embed.weight"] if self.args.tie_word_embeddings else self.tensors["lm_head.weight"]
 
+    @torch.no_grad()
+    def move_to_pool(self, pool, tag: str = "weights") -> None:
+        """Re-home every tensor in a virtual-memory region of ``pool`` (same
+        values, new addresses) so the engine's weights can be released and
+        restored around a sleep."""
+        items = [(k, t) for k, t in self.tensors.items() if t.is_cuda]
+        offs, total = [], 0
+        for _, t in items:
+            total = (total + 255) // 256 * 256            # 256-byte aligned views
+            offs.append(total)
+            total += t.numel() * t.element_size()
+        flat = pool.tensor(tag, (total,), torch.uint8)    # one region for every tensor
+        for (k, t), off in zip(items, offs):
+            nb = t.numel() * t.element_size()
+            dst = flat[off:off + nb].view(t.dtype).view(t.shape)
+            dst.copy_(t)
+            self.tensors[k] = dst
+
 
 class RolloutEngine:
     def __init__(self, args: ModelArgs, weights: EngineWeights, *, max_num_seqs: int = 256,
                  max_model_len: int = 8192 + 1024, block_size: int = 64, max_num_batched_tokens: int = 10240,
                  kv_cache_gb: float | None = None, num_blocks: int | None = None, enable_prefix_caching: bool = True,
                  use_cuda_graph: bool = True, keep_kv_on_update: bool = False, version: int = 0,
-                 eos_token_id: int | None = None, tp=None):
+                 eos_token_id: int | None = None, tp=None, memory_pool=None, decode_gemm: str = "library"):
         # tensor parallelism (``tp``: parallel.tp.TPGroup): this engine holds query heads,
         # KV heads and MLP columns [r/P, (r+1)/P) of every layer (weights in the same
         # layout as the TP trainer's shards) and its KV cache for its own KV heads; the
@@ -180,8 +200,21 @@ class RolloutEngine:
         self.num_blocks = int(num_blocks)
         self.bm = BlockManager(self.num_blocks, self.block_size)
         self.bm.set_version(self.version)
+        # memory_pool (parallel.memory.MemoryPool): KV cache and weights in
+        # virtual-memory regions ("kv", "weights") so sleep() can release them
+        self.pool = memory_pool
+        self.asleep = False
+        # decode-step projections: "library" (cuBLAS through torch; faster on
+        # B200 at every batch size measured so far) or "tcgen05" (the
+        # weight-streaming / split-K kernels of csrc/gemm_skinny.cu, gemm_2sm.cu)
+        if decode_gemm not in ("library", "tcgen05"):
+            raise ValueError(f"decode_gemm must be 'library' or 'tcgen05', not {decode_gemm!r}")
+        self.decode_gemm = decode_gemm
+        if memory_pool is not None:
+            weights.move_to_pool(memory_pool, "weights")
         self.k_cache, self.v_cache = allocate_kv_tensors(a.num_layers, self.num_blocks, a.num_kv_heads,
-                                                         self.block_size, a.head_dim, self.dtype, self.device)
+                                                         self.block_size, a.head_dim, self.dtype, self.device,
+                                                         pool=memory_pool)
         self.waiting: deque[_Seq] = deque()
         self.running: list[_Seq] = []
         self.by_id: dict[int, _Seq] = {}
@@ -226,9 +259,15 @@ class RolloutEngine:
             self.max_splits = 32
             self.decode_scratch = torch.empty(B * a.num_heads * self.max_splits * (a.head_dim + 1),
                                               dtype=torch.float32, device=dev)
+            # split-K workspace of the decode projections: 256 rows x the widest
+            # projection, zero between uses (each GEMM's finalize re-zeroes it)
+            widest = max(a.qkv_size, a.hidden_size, 2 * a.intermediate_size)
+            self.decode_ws = torch.zeros(B * widest, dtype=torch.float32, device=dev)
 
     # ----------------------------------------------------------- requests
     def add_request(self, req: GenRequest) -> None:
+        if self.asleep:
+            raise RuntimeError("engine is asleep: wake() it before adding requests")
         if req.request_id in self.by_id:
             raise ValueError(f"duplicate request id {req.request_id}")
         total = len(req.prompt_ids) + len(req.prev_output_ids)
@@ -281,6 +320,39 @@ class RolloutEngine:
 
     def abort_all(self) -> list[RequestOutput]:
         return [o for o in (self.abort(r) for r in list(self.by_id)) if o is not None]
+
+    # ------------------------------------------------------- sleep / wake
+    def sleep(self, keep_weights: bool = True) -> tuple[list[RequestOutput], int]:
+        """Release this engine's GPU memory for another role (elastic time
+        sharing; the reference's vLLM sleep levels 1 and 2).  In-flight requests
+        are interrupted and returned (their partial outputs can resume elsewhere
+        or after wake).  The KV cache's physical memory is released and its
+        contents dropped (the prefix cache is cleared); the weights' memory is
+        released too, with a pinned host copy if ``keep_weights`` (level 1),
+        else dropped (level 2: load weights after :meth:`wake`).  Addresses are
+        kept, so captured decode graphs stay valid.  Returns (interrupted
+        outputs, bytes released)."""
+        if self.pool is None:
+            raise RuntimeError("sleep needs an engine built with a memory_pool")
+        if self.asleep:
+            return [], 0
+        outs = self.abort_all()
+        if self.is_cuda:
+            torch.cuda.synchronize(self.device)
+        freed = self.pool.sleep("kv", backup=False) + self.pool.sleep("weights", backup=keep_weights)
+        self.bm = BlockManager(self.num_blocks, self.block_size)
+        self.bm.set_version(self.version)
+        self.asleep = True
+        return outs, freed
+
+    def wake(self) -> int:
+        """Map memory back at the same addresses (weights restored from the
+        host copy when one was kept; the KV cache starts empty)."""
+        if not self.asleep:
+            return 0
+        n = self.pool.wake("weights") + self.pool.wake("kv")
+        self.asleep = False
+        return n
 
     # ------------------------------------------------------------- weights
     @torch.no_grad()
@@ -537,7 +609,8 @@ class RolloutEngine:
             splits = min(splits, self.max_splits)
         h = self._forward(self.s_tokens[:nb], self.s_pos[:nb], self.s_slots[:nb], mode="decode",
                           kv_lens=self.s_lens[:nb], block_table=self.s_bt[:nb], splits=splits)
-        logits = F.linear(h, self.w.lm_head())
+        use_tc = self.is_cuda and self.tp is None and self.decode_gemm == "tcgen05"
+        logits = decode_linear(h, self.w.lm_head()) if use_tc else F.linear(h, self.w.lm_head())
         tok, lp = ops.sample(logits, self.s_temps[:nb], self.s_seeds[:nb], self.s_pos[:nb] + 1)
         self.s_out_tok[:nb].copy_(tok)
         self.s_out_lp[:nb].copy_(lp)
@@ -581,6 +654,30 @@ class RolloutEngine:
     # ------------------------------------------------------------- forward
     def _forward(self, ids, pos, slots, *, mode, cu_q=None, kv_lens=None, block_table=None, max_q=0, splits=1):
         a, W = self.args, self.w
+        # prefill chunks (hundreds to thousands of rows) run on the paired
+        # tcgen05 GEMM with SwiGLU fused into the gate_up epilogue; decode
+        # steps (one row per sequence) keep the batched library GEMM
+        big = mode == "prefill" and self.is_cuda and ids.shape[0] >= 256 and self.tp is None
+        if big:
+            def proj(x, w, b=None):
+                return linear_tc(x, w, b)
+
+            def mlp_act(x, w):
+                return gate_up_swiglu(x, w)
+        elif mode == "decode" and self.is_cuda and self.tp is None and self.decode_gemm == "tcgen05":
+            # one row per sequence: the weight-streaming tcgen05 kernel, split-K
+            # partial sums through the engine's zeroed fp32 workspace
+            def proj(x, w, b=None):
+                return decode_linear(x.contiguous(), w, b, self.decode_ws)
+
+            def mlp_act(x, w):
+                return ops.swiglu(decode_linear(x.contiguous(), w, None, self.decode_ws))
+        else:
+            def proj(x, w, b=None):
+                return F.linear(x, w, b)
+
+            def mlp_act(x, w):
+                return ops.swiglu(F.linear(x, w))
         x = F.embedding(ids, W["embed.weight"])
         resid = None
         T = ids.shape[0]
@@ -588,7 +685,7 @@ class RolloutEngine:
             pre = f"layers.{l}."
             h, r2 = ops.rms_norm(x, W[pre + "ln1"], a.rms_eps, residual=resid)
             resid = x if resid is None else r2
-            qkv = F.linear(h, W[pre + "attn.qkv.weight"], W.get(pre + "attn.qkv.bias"))
+            qkv = proj(h, W[pre + "attn.qkv.weight"], W.get(pre + "attn.qkv.bias"))
             if a.qk_norm:
                 q = qkv[:, : a.q_size].view(T, a.num_heads, a.head_dim)
                 k = qkv[:, a.q_size: a.q_size + a.kv_size].view(T, a.num_kv_heads, a.head_dim)
@@ -607,14 +704,14 @@ class RolloutEngine:
                 o = ops.paged_decode_attention(q, self.k_cache[l], self.v_cache[l], block_table, kv_lens,
                                                splits=splits if self.is_cuda else None,
                                                scratch=self.decode_scratch if self.is_cuda else None)
-            attn = F.linear(o.reshape(T, a.q_size), W[pre + "attn.o.weight"])
+            attn = proj(o.reshape(T, a.q_size), W[pre + "attn.o.weight"])
             if self.tp is not None:
                 dist.all_reduce(attn, group=self.tp.group)
             h2, resid = ops.rms_norm(attn, W[pre + "ln2"], a.rms_eps, residual=resid)
             if a.is_moe:
                 x = self._moe(h2, pre)
             else:
-                x = F.linear(ops.swiglu(F.linear(h2, W[pre + "mlp.gate_up.weight"])), W[pre + "mlp.down.weight"])
+                x = proj(mlp_act(h2, W[pre + "mlp.gate_up.weight"]), W[pre + "mlp.down.weight"])
                 if self.tp is not None:
                     dist.all_reduce(x, group=self.tp.group)
         hN, _ = ops.rms_norm(x, W["norm"], a.rms_eps, residual=resid)

@@ -119,8 +119,19 @@ class BlockManager:
             self.block_of[h] = b
 
 
-def allocate_kv_tensors(num_layers: int, num_blocks: int, nkv: int, block_size: int, head_dim: int, dtype, device):
-    """Two lists (K, V) of per-layer [num_blocks, nkv, block_size, head_dim] tensors."""
-    k = [torch.zeros(num_blocks, nkv, block_size, head_dim, dtype=dtype, device=device) for _ in range(num_layers)]
-    v = [torch.zeros(num_blocks, nkv, block_size, head_dim, dtype=dtype, device=device) for _ in range(num_layers)]
+def allocate_kv_tensors(num_layers: int, num_blocks: int, nkv: int, block_size: int, head_dim: int, dtype, device,
+                        pool=None, tag: str = "kv"):
+    """Two lists (K, V) of per-layer [num_blocks, nkv, block_size, head_dim] tensors.
+    With ``pool`` (:class:`psrl_b200.parallel.memory.MemoryPool`) the cache lives
+    in one driver virtual-memory region per tensor under ``tag``, so the engine
+    can release its physical memory while asleep and keep the addresses."""
+    shape = (num_blocks, nkv, block_size, head_dim)
+    if pool is not None:
+        k = [pool.tensor(tag, shape, dtype) for _ in range(num_layers)]
+        v = [pool.tensor(tag, shape, dtype) for _ in range(num_layers)]
+        for t in k + v:
+            t.zero_()
+        return k, v
+    k = [torch.zeros(*shape, dtype=dtype, device=device) for _ in range(num_layers)]
+    v = [torch.zeros(*shape, dtype=dtype, device=device) for _ in range(num_layers)]
     return k, v

@@ -84,7 +84,13 @@ class PolicyWorker:
         if tp_group is not None and dist_world(tp_group) > 1:
             # tensor parallelism inside tp_group (data parallelism across dp_group)
             from ..parallel.tp import apply_tensor_parallel, make_tp_group
-            self.tp = make_tp_group(tp_group)
+            fused = 0
+            if bool(cfg.actor.get("tp_fused_collectives", True)):
+                # accumulators for the widest fused all-reduce: one micro-batch x hidden
+                rows = max(int(cfg.actor.get("ppo_max_token_len_per_gpu", 10240)),
+                           int(cfg.rollout.max_prompt_length) + int(cfg.rollout.max_response_length))
+                fused = rows * args.hidden_size
+            self.tp = make_tp_group(tp_group, device, fused)
             self.tp_sharded = set(apply_tensor_parallel(self.model, self.tp))
         ep_size = int(cfg.actor.get("expert_parallel_size", 1) or 1)
         if args.is_moe and ep_size > 1:

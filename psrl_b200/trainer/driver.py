@@ -152,12 +152,19 @@ class RLTrainer:
         rc = cfg.rollout
         self.engine_weights = EngineWeights.from_model(self.actor.model, self.device, dtype=self.actor.dtype)
         max_len = int(rc.max_prompt_length) + int(rc.max_response_length) + 64
+        # time sharing without overlap (rollout.enable_sleep_mode): the engine's
+        # KV cache and weights live in virtual-memory regions, released while
+        # the trainer trains and mapped back before the next generation phase
+        pool = None
+        if bool(rc.get("enable_sleep_mode", False)) and self.device.type == "cuda":
+            from ..parallel.memory import MemoryPool
+            pool = MemoryPool(self.device)
         self.engine = RolloutEngine(
-            self.args, self.engine_weights, max_num_seqs=int(rc.max_num_seqs), max_model_len=max_len,
+            self.args, self.engine_weights, memory_pool=pool, max_num_seqs=int(rc.max_num_seqs), max_model_len=max_len,
             block_size=int(rc.block_size), max_num_batched_tokens=int(rc.max_num_batched_tokens),
             kv_cache_gb=float(rc.get("kv_cache_gb", 4.0)), enable_prefix_caching=bool(rc.enable_prefix_caching),
             use_cuda_graph=bool(rc.cuda_graph), keep_kv_on_update=bool(cfg.psrl.rollout_coordination.partial_rollout.get("keep_kv", False)),
-            eos_token_id=self.data.tokenizer.eos_id if not rc.ignore_eos else None)
+            eos_token_id=self.data.tokenizer.eos_id if not rc.ignore_eos else None, decode_gemm=str(cfg.rollout.get("decode_gemm", "library")))
         sm = cfg.psrl.rollout_coordination.sync_and_mig_strategy
         policy = SyncPolicy(sm.method, bool(cfg.psrl.rollout_coordination.partial_rollout.enable),
                             sm.sync.get("threshold"), sm.sync.get("indicator", "request_num"))
@@ -187,6 +194,7 @@ class RLTrainer:
         try:
             v, _ = self.ps.pull_model(self.instance_id)
             src = dict(self.actor.model.named_parameters())
+            src.update(dict(self.actor.model.named_buffers()))
             for k, t in self.engine_weights.tensors.items():
                 if k in src:
                     t.copy_(src[k].detach(), non_blocking=True)
@@ -264,6 +272,13 @@ class RLTrainer:
                 self.instance.pump()
             if time.monotonic() - t0 > timeout_s:
                 raise TimeoutError(f"buffer {b} not ready after {timeout_s}s: {self.manager.snapshot()}")
+        if not self.overlap and self.engine.pool is not None:
+            # generation phase over: hand the GPU memory to the trainer; in-flight
+            # requests go back to the dispatcher as partial rollouts
+            outs, freed = self.engine.sleep(keep_weights=False)
+            if outs:
+                self.manager.on_complete(outs, self.instance_id)
+            self.log.emit("engine sleep", "SWITCH", freed_bytes=int(freed))
 
     def step(self) -> dict:
         b = self.global_step
@@ -273,6 +288,9 @@ class RLTrainer:
             trajs = self.strategy.run_step(b, metrics)
         with self.log.span("PUSH", step=b):
             self._publish(b + 1)
+        if self.engine.asleep:
+            self.engine.wake()
+            self._pull_weights(b + 1)    # the weights were dropped while asleep
         self.global_step += 1
         ntok = sum(len(t.prompt_ids) + t.response_len for t in trajs)
         self.trained_tokens += ntok

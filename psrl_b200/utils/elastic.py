@@ -138,3 +138,54 @@ class ElasticExecutor:
         self._stop.set()
         if self._thread is not None:
             self._thread.join(timeout=5)
+
+
+class EngineFleet:
+    """The executor's view of real rollout engines: signals from each engine's
+    scheduler state, ``sleep`` / ``wake`` through the engines' virtual-memory
+    pools (:meth:`psrl_b200.rollout.engine.RolloutEngine.sleep`).
+
+    ``engines``: instance id -> engine (built with a ``memory_pool``).
+    ``on_interrupted(outputs)``: receives the in-flight requests an engine
+    interrupted when it went to sleep (the agent-loop manager's ``on_complete``
+    re-queues them with their partial outputs).  ``reload(instance_id, engine)``:
+    called after a wake when the engine dropped its weights while asleep (sleep
+    level 2), e.g. a weight pull from the parameter server.
+    Reference: ``psrl/utils/elastic_rm/elastic_executor.py:517,645``.
+    """
+
+    def __init__(self, engines: dict, on_interrupted=None, keep_weights: bool = True, reload=None):
+        self.engines = dict(engines)
+        self.on_interrupted = on_interrupted
+        self.keep_weights = keep_weights
+        self.reload = reload
+        self.released_bytes = 0
+        self.lock = threading.Lock()
+
+    def signals(self) -> list[InstanceSignal]:
+        out = []
+        for iid, e in self.engines.items():
+            out.append(InstanceSignal(iid, not e.asleep, float(e.bm.usage()) if not e.asleep else 0.0,
+                                      len(e.waiting), len(e.running),
+                                      float(e.stats.get("decode_tokens", 0))))
+        return out
+
+    def sleep(self, instance_id) -> int:
+        with self.lock:
+            e = self.engines[instance_id]
+            outs, freed = e.sleep(keep_weights=self.keep_weights)
+            self.released_bytes += freed
+        if outs and self.on_interrupted is not None:
+            self.on_interrupted(outs)
+        return freed
+
+    def wake(self, instance_id) -> int:
+        with self.lock:
+            e = self.engines[instance_id]
+            n = e.wake()
+        if not self.keep_weights and self.reload is not None:
+            self.reload(instance_id, e)
+        return n
+
+    def executor(self, policy: ScalingPolicy, interval_ms: float = 1000) -> ElasticExecutor:
+        return ElasticExecutor(policy, self.signals, self.sleep, self.wake, interval_ms)

@@ -162,6 +162,32 @@ def test_linear_logprob_fwd_bwd(temp):
         torch.testing.assert_close(got, ref, atol=0.3, rtol=0.1)
 
 
+def test_linear_logprob_full_vocab_gradients():
+    """Training LM head at the Qwen vocabulary (V = 151936): forward through the
+    fused log-sum-exp kernel, backward through chunked tcgen05 GEMMs, against
+    fp32 autograd."""
+    from psrl_b200.ops import linear_logprob
+    torch.manual_seed(1)
+    T, H, V = 1024, 2048, 151936
+    h = (0.5 * torch.randn(T, H, device=DEV)).bfloat16().requires_grad_(True)
+    W = (0.02 * torch.randn(V, H, device=DEV)).bfloat16().requires_grad_(True)
+    lab = torch.randint(0, V, (T,), device=DEV)
+    lp, ent = linear_logprob(h, W, lab, 1.0, chunk=512)
+    hf = h.detach().float().requires_grad_(True)
+    Wf = W.detach().float().requires_grad_(True)
+    logp = (hf @ Wf.t()).log_softmax(-1)
+    lpr = logp.gather(-1, lab[:, None])[:, 0]
+    entr = -(logp.exp() * logp).sum(-1)
+    torch.testing.assert_close(lp, lpr, atol=3e-2, rtol=1e-2)
+    torch.testing.assert_close(ent, entr, atol=3e-2, rtol=1e-2)
+    g = torch.randn(T, device=DEV)
+    (lp * g).sum().backward()
+    (lpr * g).sum().backward()
+    for got, ref in ((h.grad.float(), hf.grad), (W.grad.float(), Wf.grad)):
+        rel = (got - ref).norm() / ref.norm()
+        assert rel < 2e-2, float(rel)
+
+
 # ----------------------------------------------------------------- sampling
 def test_sampler_greedy_and_logprob():
     from psrl_b200.ops import sample
@@ -270,16 +296,19 @@ def test_paged_decode(splits, nq, nkv):
 
 
 # -------------------------------------------------------------- end to end
-def test_engine_greedy_matches_recompute_gpu():
+@pytest.mark.parametrize("chunk,decode_gemm", [(96, "library"), (1024, "library"), (1024, "tcgen05")])
+def test_engine_greedy_matches_recompute_gpu(chunk, decode_gemm):
+    # chunk 96: every prefill chunk on the library GEMM path; 1024: prefill
+    # chunks of >= 256 rows run on the paired tcgen05 GEMM and fused SwiGLU
     from psrl_b200.models import PRESETS, build_model, packed_positions
     from psrl_b200.rollout import EngineWeights, GenRequest, RolloutEngine, SamplingParams
     a = PRESETS["tiny128"]
     m = build_model(a, DEV, torch.bfloat16, seed=1)
     w = EngineWeights.from_model(m)
-    eng = RolloutEngine(a, w, max_num_seqs=8, max_model_len=512, block_size=64, max_num_batched_tokens=96,
-                        num_blocks=64, use_cuda_graph=True)
+    eng = RolloutEngine(a, w, max_num_seqs=8, max_model_len=1024, block_size=64, max_num_batched_tokens=chunk,
+                        num_blocks=96, use_cuda_graph=True, decode_gemm=decode_gemm)
     g = torch.Generator().manual_seed(0)
-    prompts = [torch.randint(3, a.vocab_size, (n,), generator=g).tolist() for n in (5, 70, 130, 9)]
+    prompts = [torch.randint(3, a.vocab_size, (n,), generator=g).tolist() for n in (5, 70, 330, 9)]
     for i, p in enumerate(prompts):
         eng.add_request(GenRequest(i, p, SamplingParams(temperature=0.0, max_tokens=20, ignore_eos=True)))
     outs = {}
