@@ -13,8 +13,8 @@ Cases:
   gate_up    fused gate_up + SwiGLU epilogue, x [16384, 2048], W [22016, 2048]
   attn       tcgen05 varlen causal attention fwd + bwd, 6 x 1700 tokens, 16/2 heads
   decode     paged decode attention, B=256, context 1024, 16/2 heads
-  skinny     weight-streaming decode GEMM, 16 rows: gate_up (22016 x 2048) and
-             QKV (2560 x 2048, split-K)
+  skinny     stream-K decode GEMM, 128 rows: gate_up + SwiGLU (22016 x 2048) and
+             QKV (2560 x 2048)
 """
 
 from __future__ import annotations
@@ -71,13 +71,13 @@ def _decode(iters: int) -> None:
 
 
 def _skinny(iters: int) -> None:
-    from psrl_b200.ops.linear import decode_linear
-    x = torch.randn(16, 2048, device="cuda").bfloat16()
+    from psrl_b200.ops.linear import DecodeWorkspace, decode_gate_up_swiglu, decode_linear
+    x = torch.randn(128, 2048, device="cuda").bfloat16()
     w = (torch.randn(22016, 2048, device="cuda") * 0.02).bfloat16()
     wq = (torch.randn(2560, 2048, device="cuda") * 0.02).bfloat16()
-    ws = torch.zeros(16 * 22016, device="cuda")
+    ws = DecodeWorkspace(22016, "cuda")
     for _ in range(iters):
-        decode_linear(x, w, None, ws)
+        decode_gate_up_swiglu(x, w, ws)
         decode_linear(x, wq, None, ws)
 
 

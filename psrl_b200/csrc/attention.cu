@@ -15,6 +15,7 @@
 // Tiles are staged in shared memory with cp.async (16 B chunks, XOR-swizzled so
 // ldmatrix is bank-conflict free) and double-buffered; the math uses
 // mma.sync.m16n8k16 bf16 tensor-core instructions.
+#include "checks.cuh"
 #include "common.cuh"
 
 namespace psrl {
@@ -119,6 +120,7 @@ struct Params {
   const int* kv_lens;    // paged mode: [B]
   const int* block_table;  // paged mode: [B, max_blocks]
   int max_blocks;
+  int num_blocks;        // paged mode: blocks in the cache (bounds checks)
   int block_size;
   int nq, nkv;
   float scale;
@@ -131,6 +133,7 @@ __device__ __forceinline__ const bf16* krow(const Params& p, const bf16* base, i
                                             int key) {
   if constexpr (PAGED) {
     const int blk = p.block_table[(int64_t)b * p.max_blocks + key / p.block_size];
+    if (!chk::in_range(blk, p.num_blocks, 62, b, key / p.block_size)) return nullptr;
     return base + (((int64_t)blk * p.nkv + kvh) * p.block_size + key % p.block_size) * D;
   } else {
     return base + ((int64_t)p.cu_k[b] + key) * row_stride + (int64_t)kvh * p.kv_head;
@@ -150,7 +153,8 @@ __global__ void __launch_bounds__(NTHREADS) attn_fwd_kernel(Params p) {
   const int q0 = p.cu_q[b];
   const int q_len = p.cu_q[b + 1] - q0;
   if (mb * BM >= q_len) return;
-  const int kv_len = PAGED ? p.kv_lens[b] : (p.cu_k[b + 1] - p.cu_k[b]);
+  const int kv_len =
+      PAGED ? chk::clamp_to(p.kv_lens[b], p.max_blocks * p.block_size, 61, b) : (p.cu_k[b + 1] - p.cu_k[b]);
   const int kvh = h / (p.nq / p.nkv);
   const int ctx_off = kv_len - q_len;  // absolute position of query 0
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -177,9 +181,10 @@ __global__ void __launch_bounds__(NTHREADS) attn_fwd_kernel(Params p) {
       if (p.block_size % BN == 0) {
         // the tile sits in one cache block: one block-table lookup
         const int key0 = t * BN;
-        const int blk = p.block_table[(int64_t)b * p.max_blocks + key0 / p.block_size];
+        int blk = p.block_table[(int64_t)b * p.max_blocks + key0 / p.block_size];
+        int nk = min(BN, k_end - key0);
+        if (!chk::in_range(blk, p.num_blocks, 62, b, key0 / p.block_size)) blk = nk = 0;
         const int64_t off = (((int64_t)blk * p.nkv + kvh) * p.block_size + key0 % p.block_size) * D;
-        const int nk = min(BN, k_end - key0);
         load_rows<BN>(sK + stage * BN * D, p.k + off, D, nk);
         load_rows<BN>(sV + stage * BN * D, p.v + off, D, nk);
         return;
@@ -601,6 +606,7 @@ struct DecodeParams {
   const int* block_table;
   const int* kv_lens;
   int max_blocks, block_size, nq, nkv, splits;
+  int num_blocks;     // blocks in the cache (bounds checks)
   float scale;
   bf16* o;            // [B, nq, D]
   float* part_o;      // [B, nq, splits, D]  (splits > 1)
@@ -615,18 +621,19 @@ struct DecodeParams {
 constexpr int DEC_STAGES = 2;   // default ring depth (x 3 resident CTAs per SM)
 
 __device__ __forceinline__ void dec_load_tile(bf16* sm, const bf16* cache, const int* bt_row, int block_size,
-                                              int nkv, int kvh, int key0, int k_end) {
+                                              int nkv, int kvh, int key0, int k_end, int b, int num_blocks) {
   // BN rows x 16 chunks of 16 B; 128 threads -> 8 chunks each
   if (block_size % BN == 0) {
     // tiles start on multiples of BN, so the whole tile sits in one cache
     // block: one block-table lookup and no per-chunk division
-    const int blk = bt_row[key0 / block_size];
-    const bf16* base = cache + (((int64_t)blk * nkv + kvh) * block_size + key0 % block_size) * D;
+    int blk = bt_row[key0 / block_size];
+    if (!chk::in_range(blk, num_blocks, 64, b, key0 / block_size)) blk = -1;
+    const bf16* base = cache + (((int64_t)(blk < 0 ? 0 : blk) * nkv + kvh) * block_size + key0 % block_size) * D;
 #pragma unroll
     for (int i = 0; i < BN * 16 / NTHREADS; ++i) {
       const int idx = threadIdx.x + i * NTHREADS;
       const int r = idx >> 4, c = idx & 15;
-      const bool ok = key0 + r < k_end;
+      const bool ok = key0 + r < k_end && blk >= 0;
       cp_async16(sm + swz(r, c * 8), ok ? base + r * D + c * 8 : cache, ok);
     }
     return;
@@ -636,11 +643,12 @@ __device__ __forceinline__ void dec_load_tile(bf16* sm, const bf16* cache, const
     const int idx = threadIdx.x + i * NTHREADS;
     const int r = idx >> 4, c = idx & 15;
     const int key = key0 + r;
-    const bool ok = key < k_end;
+    bool ok = key < k_end;
     const bf16* src = cache;
     if (ok) {
       const int blk = bt_row[key / block_size];
-      src = cache + (((int64_t)blk * nkv + kvh) * block_size + key % block_size) * D + c * 8;
+      ok = chk::in_range(blk, num_blocks, 64, b, key / block_size);
+      if (ok) src = cache + (((int64_t)blk * nkv + kvh) * block_size + key % block_size) * D + c * 8;
     }
     cp_async16(sm + swz(r, c * 8), src, ok);
   }
@@ -657,7 +665,7 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p) {
 
   const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
   const int grp = p.nq / p.nkv;
-  const int kv_len = p.kv_lens[b];
+  const int kv_len = chk::clamp_to(p.kv_lens[b], p.max_blocks * p.block_size, 63, b);
   const int per = (((kv_len + p.splits - 1) / p.splits) + BN - 1) / BN * BN;
   const int k_begin = split * per;
   const int k_end = min(kv_len, k_begin + per);
@@ -679,8 +687,10 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p) {
 #pragma unroll
   for (int st = 0; st < STAGES - 1; ++st) {
     if (st < n_tiles) {
-      dec_load_tile(sK + st * BN * D, p.kc, bt_row, p.block_size, p.nkv, kvh, k_begin + st * BN, k_end);
-      dec_load_tile(sV + st * BN * D, p.vc, bt_row, p.block_size, p.nkv, kvh, k_begin + st * BN, k_end);
+      dec_load_tile(sK + st * BN * D, p.kc, bt_row, p.block_size, p.nkv, kvh, k_begin + st * BN, k_end, b,
+                    p.num_blocks);
+      dec_load_tile(sV + st * BN * D, p.vc, bt_row, p.block_size, p.nkv, kvh, k_begin + st * BN, k_end, b,
+                    p.num_blocks);
     }
     cp_async_commit();
   }
@@ -706,8 +716,10 @@ __device__ __forceinline__ void decode_body(const DecodeParams& p) {
       const int tn = t + STAGES - 1;
       if (tn < n_tiles) {
         const int sn = tn % STAGES;
-        dec_load_tile(sK + sn * BN * D, p.kc, bt_row, p.block_size, p.nkv, kvh, k_begin + tn * BN, k_end);
-        dec_load_tile(sV + sn * BN * D, p.vc, bt_row, p.block_size, p.nkv, kvh, k_begin + tn * BN, k_end);
+        dec_load_tile(sK + sn * BN * D, p.kc, bt_row, p.block_size, p.nkv, kvh, k_begin + tn * BN, k_end, b,
+                      p.num_blocks);
+        dec_load_tile(sV + sn * BN * D, p.vc, bt_row, p.block_size, p.nkv, kvh, k_begin + tn * BN, k_end, b,
+                      p.num_blocks);
       }
       cp_async_commit();
     }
@@ -930,6 +942,7 @@ at::Tensor attn_paged_prefill(at::Tensor q, at::Tensor k_cache, at::Tensor v_cac
   p.kv_lens = kv_lens.data_ptr<int>();
   p.block_table = block_table.data_ptr<int>();
   p.max_blocks = block_table.size(1);
+  p.num_blocks = k_cache.size(0);
   p.block_size = k_cache.size(2);
   p.nq = nq;
   p.nkv = nkv;
@@ -1036,6 +1049,7 @@ at::Tensor attn_decode(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at:
   p.block_table = block_table.data_ptr<int>();
   p.kv_lens = kv_lens.data_ptr<int>();
   p.max_blocks = block_table.size(1);
+  p.num_blocks = k_cache.size(0);
   p.block_size = k_cache.size(2);
   p.nq = nq;
   p.nkv = nkv;
@@ -1143,6 +1157,7 @@ extern "C" __attribute__((visibility("default"))) int psrl_decode_attention_noal
   p.block_table = block_table;
   p.kv_lens = kv_lens;
   p.max_blocks = max_blocks;
+  p.num_blocks = 0x7fffffff;  // the C entry point does not take the cache's size
   p.block_size = block_size;
   p.nq = num_heads;
   p.nkv = num_kv_heads;

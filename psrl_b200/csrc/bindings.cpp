@@ -46,8 +46,8 @@ void tc_gemm2_allreduce2(at::Tensor a, at::Tensor b, bool b_mn, at::Tensor acc_l
 void peer_barrier(std::vector<at::Tensor> flags_in_peer, std::vector<at::Tensor> own_slots, int64_t epoch,
                   double timeout_s, at::Tensor err);
 void acc_finalize(at::Tensor acc, at::Tensor out, c10::optional<at::Tensor> bias);
-at::Tensor tc_gemm_skinny(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias, int64_t splits,
-                          c10::optional<at::Tensor> ws, at::Tensor err);
+at::Tensor tc_gemm_skinny(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias, bool swiglu, at::Tensor ws,
+                          at::Tensor tickets, int64_t grid, at::Tensor err);
 std::vector<at::Tensor> attn_fwd_sm100(at::Tensor qkv, at::Tensor cu_seqlens, int64_t max_seqlen, int64_t nq,
                                        int64_t nkv, double scale, bool want_lse, at::Tensor err);
 at::Tensor attn_bwd_sm100(at::Tensor qkv, at::Tensor o, at::Tensor dout, at::Tensor lse, at::Tensor cu_seqlens,
@@ -64,7 +64,9 @@ void peer_adamw(std::vector<at::Tensor> grads, std::vector<at::Tensor> flats, at
 std::vector<at::Tensor> tc_linear_logprob(at::Tensor h, at::Tensor w, at::Tensor labels, double temperature,
                                           at::Tensor err);
 void kv_copy_blocks(at::Tensor src_layers, at::Tensor dst_layers, at::Tensor src_blk, at::Tensor dst_blk,
-                    int64_t block_bytes);
+                    int64_t block_bytes, int64_t src_blocks, int64_t dst_blocks);
+bool kernel_checks_enabled();
+std::vector<int64_t> kernel_check_status(bool clear);
 void register_vmm(pybind11::module& m);
 pybind11::dict green_partition(int64_t device, int64_t reserve_sms, int64_t priority);
 }  // namespace psrl
@@ -111,7 +113,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_reduce", &psrl::peer_reduce);
   m.def("peer_adamw", &psrl::peer_adamw);
   m.def("tc_linear_logprob", &psrl::tc_linear_logprob);
-  m.def("kv_copy_blocks", &psrl::kv_copy_blocks);
+  m.def("kv_copy_blocks", &psrl::kv_copy_blocks, py::arg("src_layers"), py::arg("dst_layers"), py::arg("src_blk"),
+        py::arg("dst_blk"), py::arg("block_bytes"), py::arg("src_blocks") = 0, py::arg("dst_blocks") = 0);
+  m.def("kernel_checks_enabled", &psrl::kernel_checks_enabled);
+  m.def("kernel_check_status", &psrl::kernel_check_status, py::arg("clear") = true);
   psrl::register_vmm(m);
   m.def("green_partition", &psrl::green_partition);
 }

@@ -17,6 +17,7 @@
 #include <mutex>
 #include <string>
 
+#include "checks.cuh"
 #include "common.cuh"
 
 namespace py = pybind11;
@@ -86,6 +87,7 @@ struct SegTable {
   int64_t dst_off[MAX_SEG];  // in 16 B units
   int64_t len[MAX_SEG];      // in 16 B units
   int64_t start[MAX_SEG + 1];  // prefix sums of len
+  int64_t dst_total;           // destination size in 16 B units (bounds checks)
   int n;
 };
 
@@ -104,11 +106,12 @@ __global__ void __launch_bounds__(512) copy_segments_kernel(uint4* __restrict__ 
         while (seg > 0 && idx[u] < t.start[seg]) --seg;
         v[u] = t.src[seg][idx[u] - t.start[seg]];
         idx[u] = t.dst_off[seg] + (idx[u] - t.start[seg]);
+        if (!chk::in_range(idx[u], t.dst_total, 65, seg, 0)) idx[u] = -1;
       }
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u)
-      if (i + u * stride < total) dst[idx[u]] = v[u];
+      if (i + u * stride < total && (!chk::kOn || idx[u] >= 0)) dst[idx[u]] = v[u];
   }
 }
 
@@ -125,6 +128,7 @@ void copy_segments(at::Tensor dst, std::vector<at::Tensor> srcs, std::vector<int
   SegTable t{};
   t.n = n;
   t.start[0] = 0;
+  t.dst_total = dst.numel() * dst.element_size() / 16;
   const int64_t dst_bytes = dst.numel() * dst.element_size();
   for (int i = 0; i < n; ++i) {
     const char* sp = static_cast<const char*>(srcs[i].data_ptr()) + src_offsets_bytes[i];

@@ -20,6 +20,7 @@
 // the norm all-reduce between the kernels, a one-element all-reduce after the
 // update), so every peer buffer a kernel touches is quiescent while it runs.
 // No TMA and no multicast: plain loads and stores through the IPC mappings.
+#include "checks.cuh"
 #include "common.cuh"
 
 namespace psrl {
@@ -29,6 +30,7 @@ constexpr int MAX_PEERS = 16;
 struct PeerSet {
   const float* grad[MAX_PEERS];   // each rank's flat fp32 gradient (local pointer for this rank)
   bf16* flat[MAX_PEERS];          // each rank's flat bf16 parameters
+  int64_t numel;                  // elements in each flat buffer (bounds checks)
   int n;
 };
 
@@ -54,6 +56,7 @@ __global__ void __launch_bounds__(256) peer_reduce_kernel(PeerSet ps, const int6
     const int64_t i = v << 2;
     const int b = seg_of(start, nb, i);
     const int64_t g = src_off[b] + (i - start[b]);
+    if (!chk::in_range(g + 3, ps.numel, 66, b, 0)) continue;
     float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int r = 0; r < ps.n; ++r) {   // fixed rank order: the sum does not depend on timing
       const float4 t = *reinterpret_cast<const float4*>(ps.grad[r] + g);
@@ -110,6 +113,7 @@ __global__ void __launch_bounds__(256) peer_adamw_kernel(PeerSet ps, const int64
     const int64_t i = q << 2;
     const int b = seg_of(start, nb, i);
     const int64_t dst = src_off[b] + (i - start[b]);
+    if (!chk::in_range(dst + 3, ps.numel, 66, b, 1)) continue;
     for (int r = 0; r < ps.n; ++r) *reinterpret_cast<uint2*>(ps.flat[r] + dst) = word;
   }
   // make the peer stores visible system-wide before the kernel retires
@@ -120,7 +124,9 @@ static PeerSet make_set(const std::vector<at::Tensor>& grads, const std::vector<
   TORCH_CHECK(grads.size() == flats.size() && !grads.empty() && (int)grads.size() <= MAX_PEERS, "bad peer lists");
   PeerSet ps{};
   ps.n = (int)grads.size();
+  ps.numel = grads[0].numel();
   for (int r = 0; r < ps.n; ++r) {
+    TORCH_CHECK(grads[r].numel() == ps.numel && flats[r].numel() == ps.numel, "peer buffers differ in size");
     TORCH_CHECK(grads[r].scalar_type() == at::kFloat && flats[r].scalar_type() == at::kBFloat16, "peer dtypes");
     TORCH_CHECK(reinterpret_cast<uintptr_t>(grads[r].data_ptr()) % 16 == 0 &&
                     reinterpret_cast<uintptr_t>(flats[r].data_ptr()) % 16 == 0,

@@ -34,6 +34,9 @@ def check_errors(device=None) -> None:
         rec = e.tolist()
         if rec[0]:
             e.zero_()
+            if rec[0] == 51:
+                raise RuntimeError(f"cross-GPU flag barrier timed out: rank {rec[1]} last published epoch "
+                                   f"{rec[2]}, this rank waited for {rec[3]}")
             raise RuntimeError(f"tcgen05 kernel reported error code {rec[0]} (a bounded wait expired; "
                                f"block ({rec[1]}, {rec[2]}, {rec[3]}), warp {rec[4]}, iteration {rec[5]})")
 

@@ -128,47 +128,70 @@ def gate_up_swiglu(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------- decode
-def decode_splits(n: int, k: int, sms: int = 148) -> int:
-    """K-splits for the weight-streaming decode GEMM: enough (weight slab,
-    split) units to cover every SM, each streaming at least two 64-deep
-    k-blocks."""
-    tiles = -(-n // 128)
-    kblocks = -(-k // 64)
-    if tiles >= sms:
-        return 1
-    return max(1, min(-(-sms // tiles), kblocks // 2))
+class DecodeWorkspace:
+    """Scratch of the stream-K decode GEMM (``csrc/gemm_skinny.cu``): an fp32
+    accumulator for tiles shared by several CTAs and one arrival ticket per
+    128-row tile.  Both are all zero between calls (the kernel re-zeroes what it
+    used); after a reported kernel error call :meth:`reset`."""
+
+    ROWS = 256   # rows per launch; larger batches run in 256-row pieces
+
+    def __init__(self, max_cols: int, device):
+        self.max_cols = int(max_cols)
+        self.acc = torch.zeros(self.ROWS * self.max_cols, dtype=torch.float32, device=device)
+        self.tickets = torch.zeros(-(-self.max_cols // 128), dtype=torch.int32, device=device)
+
+    def reset(self) -> None:
+        self.acc.zero_()
+        self.tickets.zero_()
+
+    def fits(self, cols: int) -> bool:
+        return cols <= self.max_cols
 
 
-# above this many rows a decode GEMM is compute-bound: the paired 256 x 256 tile
-# kernel with split-K replaces the weight-streaming kernel
-SKINNY_MAX_ROWS = 64
+_DEFAULT_WS: dict = {}
+
+
+def _workspace(ws: "DecodeWorkspace | None", cols: int, device) -> DecodeWorkspace:
+    if ws is not None:
+        if not ws.fits(cols):
+            raise ValueError(f"decode workspace holds {ws.max_cols} columns, the GEMM needs {cols}")
+        return ws
+    key = (device.type, device.index)
+    cur = _DEFAULT_WS.get(key)
+    if cur is None or not cur.fits(cols):
+        cur = _DEFAULT_WS[key] = DecodeWorkspace(cols, device)
+    return cur
+
+
+def _skinny(x, w, b, swiglu: bool, ws: DecodeWorkspace, grid: int) -> torch.Tensor:
+    B = x.shape[0]
+    if B <= DecodeWorkspace.ROWS:
+        return ext().tc_gemm_skinny(x, w, b, swiglu, ws.acc, ws.tickets, int(grid), _err(x.device))
+    step = DecodeWorkspace.ROWS
+    return torch.cat([ext().tc_gemm_skinny(x[i:i + step], w, b, swiglu, ws.acc, ws.tickets, int(grid),
+                                           _err(x.device)) for i in range(0, B, step)], 0)
 
 
 def decode_linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None,
-                  ws: torch.Tensor | None = None) -> torch.Tensor:
-    """``x W^T + b`` for a decode step's ``x`` ([B, K], one row per sequence).
+                  ws: DecodeWorkspace | None = None, grid: int = 0) -> torch.Tensor:
+    """``x W^T + b`` for a decode step's ``x`` ([B, K], one row per sequence),
+    one launch of the weight-streaming stream-K tcgen05 kernel per 256 rows:
+    the weight fills the MMA's M dimension and its (128-row tile, 64-deep k
+    block) units are dealt out evenly to one CTA per SM (``grid`` overrides the
+    CTA count).  ``ws``: the caller's :class:`DecodeWorkspace` (a per-device
+    default is used without one)."""
+    ws = _workspace(ws, w.shape[0], x.device)
+    return _skinny(x.contiguous(), w, b, False, ws, grid)
 
-    * B <= 64: weight-streaming tcgen05 kernel (``csrc/gemm_skinny.cu``): the
-      weight fills the MMA's M dimension, the K loop is split over CTAs.
-    * larger B: the paired-CTA tcgen05 GEMM (``csrc/gemm_2sm.cu``) with split-K
-      partial sums added into ``ws``, then one pass converts to bf16, adds the
-      bias and zeroes ``ws``.
-    ``ws``: fp32 workspace of at least ``B * N`` zeros (kept zero); without it
-    the K loop is not split."""
-    n, k = w.shape
-    B = x.shape[0]
-    if B <= SKINNY_MAX_ROWS or ws is None:
-        splits = decode_splits(n, k) if ws is not None else 1
-        if B <= 256:
-            return ext().tc_gemm_skinny(x, w, b, splits, ws, _err(x.device))
-        return torch.cat([ext().tc_gemm_skinny(x[i:i + 256], w, b, splits, ws, _err(x.device))
-                          for i in range(0, B, 256)], 0)
-    if ws.numel() < B * n:
-        raise ValueError(f"decode workspace of {ws.numel()} floats is smaller than {B} x {n}")
-    tiles = -(-B // 256) * -(-n // 256)
-    splits = max(1, min(-(-2 * _PAIRS // tiles), -(-k // 64) // 4))
-    acc = ws[: B * n].view(B, n)
-    ext().tc_gemm2(x, w, False, False, acc, splits, GROUP_M, None, _err(x.device))
-    y = torch.empty(B, n, dtype=x.dtype, device=x.device)
-    ext().acc_finalize(acc, y, b)
-    return y
+
+def decode_gate_up_swiglu(x: torch.Tensor, w: torch.Tensor, ws: DecodeWorkspace | None = None,
+                          grid: int = 0) -> torch.Tensor:
+    """``silu(x W_gate^T) * (x W_up^T)`` for a decode step, with ``w`` the fused
+    [2I, K] gate_up weight (gate rows first): one launch whose epilogue applies
+    the activation, so the [B, 2I] projection never reaches HBM."""
+    ws = _workspace(ws, w.shape[0], x.device)
+    if (w.shape[0] // 2) % 128:
+        from .activation import swiglu
+        return swiglu(_skinny(x.contiguous(), w, None, False, ws, grid))
+    return _skinny(x.contiguous(), w, None, True, ws, grid)

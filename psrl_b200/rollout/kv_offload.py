@@ -37,7 +37,8 @@ def copy_blocks(src_k, src_v, dst_k, dst_v, src_blocks, dst_blocks, device=None)
     if dev.type == "cuda":
         ops.ext().kv_copy_blocks(layer_ptrs(src_k, src_v, dev), layer_ptrs(dst_k, dst_v, dev),
                                  torch.tensor(src_blocks, dtype=torch.int32, device=dev),
-                                 torch.tensor(dst_blocks, dtype=torch.int32, device=dev), block_bytes(src_k))
+                                 torch.tensor(dst_blocks, dtype=torch.int32, device=dev), block_bytes(src_k),
+                                 src_k[0].shape[0], dst_k[0].shape[0])
         return
     for s, d in zip(list(src_k) + list(src_v), list(dst_k) + list(dst_v)):
         d[torch.tensor(dst_blocks)] = s[torch.tensor(src_blocks)].to(d.device)
