@@ -1,4 +1,7 @@
-"""Model architecture arguments and presets (Qwen2 / Qwen2.5 / Qwen3 / Qwen3-MoE)."""
+"""Model architecture arguments and presets.
+
+One fused decoder covers every supported family; :class:`ModelArgs` holds the
+switches (``models/families.py`` maps HF configs onto them)."""
 
 from __future__ import annotations
 
@@ -9,7 +12,7 @@ from pathlib import Path
 
 @dataclass
 class ModelArgs:
-    arch: str = "qwen2"                 # qwen2 | qwen3 | qwen3_moe
+    arch: str = "qwen2"                 # HF model_type of a registered family (models/families.py)
     vocab_size: int = 151936
     hidden_size: int = 2048
     num_layers: int = 36
@@ -30,6 +33,13 @@ class ModelArgs:
     norm_topk_prob: bool = True
     router_zipf_alpha: float = 0.0      # >0: add log Zipf(alpha) prior to router logits (skewed load)
     value_head: bool = False            # critic: scalar head instead of the LM head
+    # family switches
+    rope_scaling: dict | None = None    # {"rope_type": "llama3" | "linear", "factor": ..., ...}
+    qk_norm_full: bool = False          # OLMoE: RMSNorm over the whole q / k projection
+    shared_expert_intermediate_size: int = 0   # Qwen2-MoE: always-on expert with a sigmoid gate
+    hidden_act: str = "silu"            # silu (SwiGLU) | gelu_tanh (GeGLU, Gemma)
+    embed_scale: float = 0.0            # Gemma: embeddings multiplied by sqrt(hidden)
+    sliding_window: int | None = None   # Mistral: attention window (must cover the whole context)
     extra: dict = field(default_factory=dict)
 
     @property
@@ -48,14 +58,32 @@ class ModelArgs:
     def qkv_size(self) -> int:
         return self.q_size + 2 * self.kv_size
 
+    @property
+    def rope_spec(self):
+        """Hashable RoPE description for the cos/sin table cache: the base, or
+        (base, scaling items) when the family rescales frequencies."""
+        if not self.rope_scaling:
+            return float(self.rope_theta)
+        return (float(self.rope_theta),) + tuple(sorted((k, v) for k, v in self.rope_scaling.items()
+                                                        if not isinstance(v, (list, dict))))
+
+    def check_context(self, length: int) -> None:
+        """Sliding-window attention is implemented only as full attention, which
+        is exact while the window covers the whole context."""
+        if self.sliding_window is not None and length > self.sliding_window:
+            raise NotImplementedError(f"context of {length} tokens exceeds the {self.sliding_window}-token "
+                                      "sliding window; windowed attention is not implemented")
+
     def num_params(self) -> int:
         h, L = self.hidden_size, self.num_layers
         attn = h * self.qkv_size + (self.qkv_size if self.qkv_bias else 0) + self.q_size * h
         if self.is_moe:
             mlp = self.num_experts * 3 * h * self.moe_intermediate_size + self.num_experts * h
+            mlp += 3 * h * self.shared_expert_intermediate_size + (h if self.shared_expert_intermediate_size else 0)
         else:
             mlp = 3 * h * self.intermediate_size
-        norms = 2 * h + (2 * self.head_dim if self.qk_norm else 0)
+        norms = 2 * h + (2 * self.head_dim if self.qk_norm else 0) + (self.q_size + self.kv_size
+                                                                       if self.qk_norm_full else 0)
         emb = self.vocab_size * h * (1 if self.tie_word_embeddings else 2)
         return L * (attn + mlp + norms) + emb + h
 
@@ -65,6 +93,7 @@ class ModelArgs:
         attn = h * self.qkv_size + self.q_size * h
         if self.is_moe:
             mlp = self.num_experts_per_tok * 3 * h * self.moe_intermediate_size + self.num_experts * h
+            mlp += 3 * h * self.shared_expert_intermediate_size
         else:
             mlp = 3 * h * self.intermediate_size
         return L * (attn + mlp) + self.vocab_size * h
@@ -74,54 +103,12 @@ class ModelArgs:
 
     @classmethod
     def from_hf_config(cls, cfg: dict) -> "ModelArgs":
-        mt = cfg.get("model_type", "qwen2")
-        arch = {"qwen2": "qwen2", "qwen3": "qwen3", "qwen3_moe": "qwen3_moe", "qwen2_moe": "qwen3_moe"}.get(mt, "qwen2")
-        heads = cfg["num_attention_heads"]
-        return cls(
-            arch=arch,
-            vocab_size=cfg["vocab_size"],
-            hidden_size=cfg["hidden_size"],
-            num_layers=cfg["num_hidden_layers"],
-            num_heads=heads,
-            num_kv_heads=cfg.get("num_key_value_heads", heads),
-            head_dim=cfg.get("head_dim", cfg["hidden_size"] // heads),
-            intermediate_size=cfg.get("intermediate_size", 0),
-            rope_theta=cfg.get("rope_theta", 1e6),
-            rms_eps=cfg.get("rms_norm_eps", 1e-6),
-            tie_word_embeddings=cfg.get("tie_word_embeddings", False),
-            qkv_bias=(arch == "qwen2") or cfg.get("attention_bias", False),
-            qk_norm=arch in ("qwen3", "qwen3_moe"),
-            max_position=cfg.get("max_position_embeddings", 32768),
-            num_experts=cfg.get("num_experts", 0),
-            num_experts_per_tok=cfg.get("num_experts_per_tok", 0),
-            moe_intermediate_size=cfg.get("moe_intermediate_size", 0),
-            norm_topk_prob=cfg.get("norm_topk_prob", True),
-        )
+        from .families import args_from_hf_config
+        return args_from_hf_config(cfg)
 
     def to_hf_config(self) -> dict:
-        mt = {"qwen2": "qwen2", "qwen3": "qwen3", "qwen3_moe": "qwen3_moe"}[self.arch]
-        d = {
-            "model_type": mt,
-            "architectures": [{"qwen2": "Qwen2ForCausalLM", "qwen3": "Qwen3ForCausalLM",
-                               "qwen3_moe": "Qwen3MoeForCausalLM"}[self.arch]],
-            "vocab_size": self.vocab_size,
-            "hidden_size": self.hidden_size,
-            "num_hidden_layers": self.num_layers,
-            "num_attention_heads": self.num_heads,
-            "num_key_value_heads": self.num_kv_heads,
-            "head_dim": self.head_dim,
-            "intermediate_size": self.intermediate_size,
-            "rope_theta": self.rope_theta,
-            "rms_norm_eps": self.rms_eps,
-            "tie_word_embeddings": self.tie_word_embeddings,
-            "max_position_embeddings": self.max_position,
-            "hidden_act": "silu",
-            "torch_dtype": "bfloat16",
-        }
-        if self.is_moe:
-            d.update(num_experts=self.num_experts, num_experts_per_tok=self.num_experts_per_tok,
-                     moe_intermediate_size=self.moe_intermediate_size, norm_topk_prob=self.norm_topk_prob)
-        return d
+        from .families import hf_config_from_args
+        return hf_config_from_args(self)
 
 
 PRESETS: dict[str, ModelArgs] = {

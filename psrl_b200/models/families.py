@@ -92,6 +92,9 @@ def _rope(cfg: dict, default_theta: float) -> tuple[float, dict | None]:
     return float(theta), scaling
 
 
+_TOKEN_KEYS = ("bos_token_id", "eos_token_id", "pad_token_id")
+
+
 def args_from_hf_config(cfg: dict) -> ModelArgs:
     mt = cfg.get("model_type", "qwen2")
     if mt not in FAMILIES:
@@ -138,6 +141,7 @@ def args_from_hf_config(cfg: dict) -> ModelArgs:
         hidden_act=act,
         embed_scale=float(cfg["hidden_size"]) ** 0.5 if mt == "gemma" else 0.0,
         sliding_window=window,
+        extra={"hf_tokens": {k: cfg[k] for k in _TOKEN_KEYS if cfg.get(k) is not None}},
     )
     return a
 
@@ -182,4 +186,5 @@ def hf_config_from_args(a: ModelArgs) -> dict:
         d["decoder_sparse_step"] = 1
         d["mlp_only_layers"] = []
     d.update(f.extra_hf)
+    d.update((a.extra or {}).get("hf_tokens", {}))
     return d

@@ -1,10 +1,14 @@
 """HF ↔ fused-layout parameter conversion and safetensors I/O (C18 converters).
 
-HF Qwen2/Qwen3(-MoE) checkpoints store separate ``q_proj``/``k_proj``/``v_proj``
-and ``gate_proj``/``up_proj`` (and per-expert matrices); this framework stacks
-them (``attn.qkv``, ``mlp.gate_up``, ``experts_w13``/``experts_w2``).  The
-conversion is a row split/concat along dim 0; the HF key names are the public
-checkpoint format and must match exactly.
+HF checkpoints store separate ``q_proj``/``k_proj``/``v_proj`` and
+``gate_proj``/``up_proj`` (Phi-3 stores them fused) and per-expert matrices
+(under ``block_sparse_moe`` with ``w1``/``w3``/``w2`` for Mixtral); this
+framework stacks them (``attn.qkv``, ``mlp.gate_up``, ``experts_w13`` /
+``experts_w2``).  The conversion is a row split/concat along dim 0 plus the
+family's names (``models/families.py``); the HF key names are the public
+checkpoint format and must match exactly.  Gemma checkpoints store RMSNorm
+weights as ``w - 1`` (the norm multiplies by ``1 + w``); they are shifted on
+the way in and out.
 """
 
 from __future__ import annotations
@@ -16,18 +20,23 @@ import re
 import torch
 
 from .config import ModelArgs
+from .families import family_of
 
 _LAYER = re.compile(r"^layers\.(\d+)\.(.+)$")
+_NORMS = ("ln1", "ln2", "attn.q_norm", "attn.k_norm")
 
 
 def to_hf_state_dict(state: dict[str, torch.Tensor], a: ModelArgs) -> dict[str, torch.Tensor]:
+    f = family_of(a)
+    g_name, u_name, d_name = f.expert_names
+    mp = f.moe_prefix
     out: dict[str, torch.Tensor] = {}
     for k, t in state.items():
         m = _LAYER.match(k)
         if k == "embed.weight":
             out["model.embed_tokens.weight"] = t
         elif k == "norm":
-            out["model.norm.weight"] = t
+            out["model.norm.weight"] = t - f.norm_offset if f.norm_offset else t
         elif k == "lm_head.weight":
             out["lm_head.weight"] = t
         elif k.startswith("value."):
@@ -35,16 +44,21 @@ def to_hf_state_dict(state: dict[str, torch.Tensor], a: ModelArgs) -> dict[str, 
         elif m:
             i, rest = m.group(1), m.group(2)
             p = f"model.layers.{i}."
+            if rest in _NORMS and f.norm_offset:
+                t = t - f.norm_offset
             if rest == "ln1":
                 out[p + "input_layernorm.weight"] = t
             elif rest == "ln2":
                 out[p + "post_attention_layernorm.weight"] = t
             elif rest in ("attn.qkv.weight", "attn.qkv.bias"):
                 kind = rest.rsplit(".", 1)[1]
-                q, kk, v = t.split([a.q_size, a.kv_size, a.kv_size], dim=0)
-                out[p + f"self_attn.q_proj.{kind}"] = q
-                out[p + f"self_attn.k_proj.{kind}"] = kk
-                out[p + f"self_attn.v_proj.{kind}"] = v
+                if f.fused_qkv:
+                    out[p + f"self_attn.qkv_proj.{kind}"] = t
+                else:
+                    q, kk, v = t.split([a.q_size, a.kv_size, a.kv_size], dim=0)
+                    out[p + f"self_attn.q_proj.{kind}"] = q
+                    out[p + f"self_attn.k_proj.{kind}"] = kk
+                    out[p + f"self_attn.v_proj.{kind}"] = v
             elif rest == "attn.o.weight":
                 out[p + "self_attn.o_proj.weight"] = t
             elif rest == "attn.q_norm":
@@ -52,21 +66,32 @@ def to_hf_state_dict(state: dict[str, torch.Tensor], a: ModelArgs) -> dict[str, 
             elif rest == "attn.k_norm":
                 out[p + "self_attn.k_norm.weight"] = t
             elif rest == "mlp.gate_up.weight":
-                g, u = t.chunk(2, dim=0)
-                out[p + "mlp.gate_proj.weight"] = g
-                out[p + "mlp.up_proj.weight"] = u
+                if f.fused_gate_up:
+                    out[p + "mlp.gate_up_proj.weight"] = t
+                else:
+                    g, u = t.chunk(2, dim=0)
+                    out[p + "mlp.gate_proj.weight"] = g
+                    out[p + "mlp.up_proj.weight"] = u
             elif rest == "mlp.down.weight":
                 out[p + "mlp.down_proj.weight"] = t
             elif rest == "mlp.router.weight":
-                out[p + "mlp.gate.weight"] = t
+                out[p + f"{mp}.gate.weight"] = t
             elif rest == "mlp.experts_w13":
                 for e in range(t.shape[0]):
                     g, u = t[e].chunk(2, dim=0)
-                    out[p + f"mlp.experts.{e}.gate_proj.weight"] = g
-                    out[p + f"mlp.experts.{e}.up_proj.weight"] = u
+                    out[p + f"{mp}.experts.{e}.{g_name}.weight"] = g
+                    out[p + f"{mp}.experts.{e}.{u_name}.weight"] = u
             elif rest == "mlp.experts_w2":
                 for e in range(t.shape[0]):
-                    out[p + f"mlp.experts.{e}.down_proj.weight"] = t[e]
+                    out[p + f"{mp}.experts.{e}.{d_name}.weight"] = t[e]
+            elif rest == "mlp.shared_gate_up.weight":
+                g, u = t.chunk(2, dim=0)
+                out[p + "mlp.shared_expert.gate_proj.weight"] = g
+                out[p + "mlp.shared_expert.up_proj.weight"] = u
+            elif rest == "mlp.shared_down.weight":
+                out[p + "mlp.shared_expert.down_proj.weight"] = t
+            elif rest == "mlp.shared_gate.weight":
+                out[p + "mlp.shared_expert_gate.weight"] = t
             else:
                 raise KeyError(f"no HF mapping for {k}")
         else:
@@ -75,11 +100,18 @@ def to_hf_state_dict(state: dict[str, torch.Tensor], a: ModelArgs) -> dict[str, 
 
 
 def from_hf_state_dict(hf: dict[str, torch.Tensor], a: ModelArgs) -> dict[str, torch.Tensor]:
+    f = family_of(a)
+    g_name, u_name, d_name = f.expert_names
+    mp = f.moe_prefix
+
+    def norm(t):
+        return t + f.norm_offset if f.norm_offset else t
+
     out: dict[str, torch.Tensor] = {}
     if "model.embed_tokens.weight" in hf:
         out["embed.weight"] = hf["model.embed_tokens.weight"]
     if "model.norm.weight" in hf:
-        out["norm"] = hf["model.norm.weight"]
+        out["norm"] = norm(hf["model.norm.weight"])
     if "lm_head.weight" in hf and not a.tie_word_embeddings:
         out["lm_head.weight"] = hf["lm_head.weight"]
     for k in ("score.weight", "score.bias"):
@@ -88,24 +120,33 @@ def from_hf_state_dict(hf: dict[str, torch.Tensor], a: ModelArgs) -> dict[str, t
     for i in range(a.num_layers):
         p = f"model.layers.{i}."
         q = f"layers.{i}."
-        out[q + "ln1"] = hf[p + "input_layernorm.weight"]
-        out[q + "ln2"] = hf[p + "post_attention_layernorm.weight"]
-        out[q + "attn.qkv.weight"] = torch.cat([hf[p + "self_attn.q_proj.weight"], hf[p + "self_attn.k_proj.weight"],
-                                                hf[p + "self_attn.v_proj.weight"]], 0)
-        if (p + "self_attn.q_proj.bias") in hf:
-            out[q + "attn.qkv.bias"] = torch.cat([hf[p + "self_attn.q_proj.bias"], hf[p + "self_attn.k_proj.bias"],
-                                                  hf[p + "self_attn.v_proj.bias"]], 0)
+        out[q + "ln1"] = norm(hf[p + "input_layernorm.weight"])
+        out[q + "ln2"] = norm(hf[p + "post_attention_layernorm.weight"])
+        for kind in ("weight", "bias"):
+            if f.fused_qkv:
+                if (p + f"self_attn.qkv_proj.{kind}") in hf:
+                    out[q + f"attn.qkv.{kind}"] = hf[p + f"self_attn.qkv_proj.{kind}"]
+            elif (p + f"self_attn.q_proj.{kind}") in hf:
+                out[q + f"attn.qkv.{kind}"] = torch.cat([hf[p + f"self_attn.{n}_proj.{kind}"] for n in "qkv"], 0)
         out[q + "attn.o.weight"] = hf[p + "self_attn.o_proj.weight"]
-        if a.qk_norm:
-            out[q + "attn.q_norm"] = hf[p + "self_attn.q_norm.weight"]
-            out[q + "attn.k_norm"] = hf[p + "self_attn.k_norm.weight"]
+        if a.qk_norm or a.qk_norm_full:
+            out[q + "attn.q_norm"] = norm(hf[p + "self_attn.q_norm.weight"])
+            out[q + "attn.k_norm"] = norm(hf[p + "self_attn.k_norm.weight"])
         if a.is_moe:
-            out[q + "mlp.router.weight"] = hf[p + "mlp.gate.weight"]
+            out[q + "mlp.router.weight"] = hf[p + f"{mp}.gate.weight"]
             out[q + "mlp.experts_w13"] = torch.stack([
-                torch.cat([hf[p + f"mlp.experts.{e}.gate_proj.weight"], hf[p + f"mlp.experts.{e}.up_proj.weight"]], 0)
+                torch.cat([hf[p + f"{mp}.experts.{e}.{g_name}.weight"], hf[p + f"{mp}.experts.{e}.{u_name}.weight"]], 0)
                 for e in range(a.num_experts)])
-            out[q + "mlp.experts_w2"] = torch.stack([hf[p + f"mlp.experts.{e}.down_proj.weight"]
+            out[q + "mlp.experts_w2"] = torch.stack([hf[p + f"{mp}.experts.{e}.{d_name}.weight"]
                                                      for e in range(a.num_experts)])
+            if a.shared_expert_intermediate_size:
+                out[q + "mlp.shared_gate_up.weight"] = torch.cat([hf[p + "mlp.shared_expert.gate_proj.weight"],
+                                                                  hf[p + "mlp.shared_expert.up_proj.weight"]], 0)
+                out[q + "mlp.shared_down.weight"] = hf[p + "mlp.shared_expert.down_proj.weight"]
+                out[q + "mlp.shared_gate.weight"] = hf[p + "mlp.shared_expert_gate.weight"]
+        elif f.fused_gate_up:
+            out[q + "mlp.gate_up.weight"] = hf[p + "mlp.gate_up_proj.weight"]
+            out[q + "mlp.down.weight"] = hf[p + "mlp.down_proj.weight"]
         else:
             out[q + "mlp.gate_up.weight"] = torch.cat([hf[p + "mlp.gate_proj.weight"], hf[p + "mlp.up_proj.weight"]], 0)
             out[q + "mlp.down.weight"] = hf[p + "mlp.down_proj.weight"]

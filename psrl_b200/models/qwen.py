@@ -1,4 +1,7 @@
-"""Qwen2 / Qwen2.5 / Qwen3 dense and Qwen3-MoE decoders for training.
+"""The fused decoder for training: Qwen2 / Qwen2.5 / Qwen3 / Qwen3-MoE /
+Qwen2-MoE / Llama / Mistral / Mixtral / OLMoE / Phi-3 / Gemma (the family
+switches are in :class:`ModelArgs`, the checkpoint names in
+``models/families.py`` and ``models/hf_io.py``).
 
 Parameter layout (shared with the rollout engine at TP=1):
 
@@ -42,6 +45,9 @@ class Attention(nn.Module):
         if a.qk_norm:
             self.q_norm = nn.Parameter(torch.ones(a.head_dim))
             self.k_norm = nn.Parameter(torch.ones(a.head_dim))
+        elif a.qk_norm_full:
+            self.q_norm = nn.Parameter(torch.ones(a.q_size))
+            self.k_norm = nn.Parameter(torch.ones(a.kv_size))
 
     def forward(self, x, positions, cu_seqlens, max_seqlen):
         a = self.a
@@ -52,19 +58,34 @@ class Attention(nn.Module):
             q = ops.head_rms_norm(q.reshape(T, a.num_heads, a.head_dim), self.q_norm, a.rms_eps).reshape(T, -1)
             k = ops.head_rms_norm(k.reshape(T, a.num_kv_heads, a.head_dim), self.k_norm, a.rms_eps).reshape(T, -1)
             qkv = torch.cat([q, k, v], dim=-1)
-        qkv = ops.rope_qkv(qkv.contiguous(), positions, a.num_heads, a.num_kv_heads, a.head_dim, a.rope_theta)
+        elif a.qk_norm_full:
+            q, k, v = qkv.split([a.q_size, a.kv_size, a.kv_size], dim=-1)
+            q, _ = ops.rms_norm(q.contiguous(), self.q_norm, a.rms_eps)
+            k, _ = ops.rms_norm(k.contiguous(), self.k_norm, a.rms_eps)
+            qkv = torch.cat([q, k, v], dim=-1)
+        qkv = ops.rope_qkv(qkv.contiguous(), positions, a.num_heads, a.num_kv_heads, a.head_dim, a.rope_spec)
         o = ops.varlen_attention(qkv, cu_seqlens, max_seqlen, a.num_heads, a.num_kv_heads, a.head_dim)
         return linear(o, self.o.weight)
+
+
+def gated_act(x: torch.Tensor, w_gate_up: torch.Tensor, act: str) -> torch.Tensor:
+    """act(x W_gate^T) * (x W_up^T) for the fused [2I, h] gate_up weight:
+    SwiGLU in the GEMM epilogue, GeGLU (tanh GELU, Gemma) after it."""
+    if act == "silu":
+        return gate_up_swiglu(x, w_gate_up)
+    g, u = linear(x, w_gate_up).chunk(2, dim=-1)
+    return F.gelu(g.float(), approximate="tanh").to(g.dtype) * u
 
 
 class MLP(nn.Module):
     def __init__(self, a: ModelArgs):
         super().__init__()
+        self.act = a.hidden_act
         self.gate_up = nn.Linear(a.hidden_size, 2 * a.intermediate_size, bias=False)
         self.down = nn.Linear(a.intermediate_size, a.hidden_size, bias=False)
 
     def forward(self, x):
-        return linear(gate_up_swiglu(x, self.gate_up.weight), self.down.weight)
+        return linear(gated_act(x, self.gate_up.weight, self.act), self.down.weight)
 
 
 def zipf_prior(num_experts: int, alpha: float, seed: int = 1234) -> torch.Tensor:
@@ -89,6 +110,16 @@ class MoE(nn.Module):
         self.experts_w2 = nn.Parameter(torch.empty(E, h, I))
         prior = zipf_prior(E, a.router_zipf_alpha) if a.router_zipf_alpha > 0 else torch.zeros(E)
         self.register_buffer("router_prior", prior, persistent=False)
+        Is = a.shared_expert_intermediate_size
+        if Is:
+            # Qwen2-MoE: an always-on SwiGLU expert scaled by sigmoid(x w_gate)
+            self.shared_gate_up = nn.Linear(h, 2 * Is, bias=False)
+            self.shared_down = nn.Linear(Is, h, bias=False)
+            self.shared_gate = nn.Linear(h, 1, bias=False)
+
+    def shared(self, x):
+        y = linear(gate_up_swiglu(x, self.shared_gate_up.weight), self.shared_down.weight)
+        return torch.sigmoid(F.linear(x, self.shared_gate.weight).float()).to(y.dtype) * y
 
     def route(self, x):
         logits = self.router(x).float() + self.router_prior
@@ -99,6 +130,10 @@ class MoE(nn.Module):
         return w, idx
 
     def forward(self, x):
+        y = self.routed(x)
+        return y + self.shared(x) if self.a.shared_expert_intermediate_size else y
+
+    def routed(self, x):
         from ..ops import moe as moe_ops
         ep = getattr(self, "ep", None)
         if ep is not None:
@@ -168,7 +203,12 @@ class QwenModel(nn.Module):
 
     # --------------------------------------------------------------- forward
     def hidden_states(self, input_ids, positions, cu_seqlens, max_seqlen):
+        a = self.args
+        if a.sliding_window is not None:
+            a.check_context(int(max_seqlen))
         x = self.embed(input_ids)
+        if a.embed_scale:
+            x = x * torch.tensor(a.embed_scale, dtype=x.dtype)
         resid = None
         for layer in self.layers:
             if self.gradient_checkpointing and torch.is_grad_enabled():

@@ -4,6 +4,8 @@ optionally fused with the paged KV-cache write)."""
 
 from __future__ import annotations
 
+import math
+
 import torch
 
 from ._ext import ext
@@ -11,14 +13,45 @@ from ._ext import ext
 _TABLES: dict = {}
 
 
-def rope_tables(theta: float, dim: int, max_pos: int, device) -> tuple[torch.Tensor, torch.Tensor]:
-    """fp32 cos/sin tables of shape [max_pos, dim/2] computed in float64."""
-    key = (float(theta), int(dim), str(device))
+def inv_frequencies(spec, dim: int) -> torch.Tensor:
+    """float64 [dim/2] rotary frequencies.  ``spec`` is the base, or
+    ``(base, (key, value), ...)`` with a scaling rule (``ModelArgs.rope_spec``):
+
+    * ``linear``: every frequency divided by ``factor`` (positions stretched);
+    * ``llama3``: wavelengths shorter than ``original / high_freq_factor`` kept,
+      longer than ``original / low_freq_factor`` divided by ``factor``, and a
+      linear blend (in ``original / wavelength``) between the two bands.
+    """
+    if isinstance(spec, tuple):
+        theta, opts = float(spec[0]), dict(spec[1:])
+    else:
+        theta, opts = float(spec), {}
+    inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.float64) / dim))
+    kind = opts.get("rope_type", "default")
+    if kind == "linear":
+        inv = inv / float(opts["factor"])
+    elif kind == "llama3":
+        factor = float(opts["factor"])
+        lo, hi = float(opts.get("low_freq_factor", 1.0)), float(opts.get("high_freq_factor", 4.0))
+        orig = float(opts.get("original_max_position_embeddings", 8192))
+        wavelen = 2 * math.pi / inv
+        smooth = ((orig / wavelen - lo) / (hi - lo)).clamp(0.0, 1.0)
+        blended = (1.0 - smooth) * inv / factor + smooth * inv
+        inv = torch.where(wavelen < orig / hi, inv, torch.where(wavelen > orig / lo, inv / factor, blended))
+    elif kind != "default":
+        raise NotImplementedError(f"RoPE scaling {kind!r}")
+    return inv
+
+
+def rope_tables(theta, dim: int, max_pos: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp32 cos/sin tables of shape [max_pos, dim/2] computed in float64;
+    ``theta`` is a base or a ``ModelArgs.rope_spec``."""
+    key = (theta if isinstance(theta, tuple) else float(theta), int(dim), str(device))
     have = _TABLES.get(key)
     if have is not None and have[0].shape[0] >= max_pos:
         return have
     n = max(int(max_pos), 4096)
-    inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.float64) / dim))
+    inv = inv_frequencies(theta, dim)
     ang = torch.arange(n, dtype=torch.float64)[:, None] * inv[None, :]
     tabs = (ang.cos().float().to(device), ang.sin().float().to(device))
     _TABLES[key] = tabs

@@ -133,7 +133,7 @@ class TPAttention(nn.Module):
             q = ops.head_rms_norm(q.reshape(T, la.num_heads, la.head_dim), self.q_norm, la.rms_eps).reshape(T, -1)
             k = ops.head_rms_norm(k.reshape(T, la.num_kv_heads, la.head_dim), self.k_norm, la.rms_eps).reshape(T, -1)
             qkv = torch.cat([q, k, v], dim=-1)
-        qkv = ops.rope_qkv(qkv.contiguous(), positions, la.num_heads, la.num_kv_heads, la.head_dim, la.rope_theta)
+        qkv = ops.rope_qkv(qkv.contiguous(), positions, la.num_heads, la.num_kv_heads, la.head_dim, la.rope_spec)
         o = ops.varlen_attention(qkv, cu_seqlens, max_seqlen, la.num_heads, la.num_kv_heads, la.head_dim)
         if self.tp.fused_fits(o, self.a.hidden_size) and T == o.shape[0]:
             from .tp_fused import row_parallel
@@ -170,6 +170,8 @@ def apply_tensor_parallel(model, tp: TPGroup) -> list[str]:
     a = model.args
     if a.is_moe:
         raise ValueError("tensor parallelism here covers dense decoders; MoE layers use expert parallelism")
+    if a.qk_norm_full or a.hidden_act != "silu":
+        raise NotImplementedError("tensor parallelism of full-width q/k norms or GeGLU is not implemented")
     names = []
     for i, layer in enumerate(model.layers):
         layer.attn = TPAttention(layer.attn, tp)

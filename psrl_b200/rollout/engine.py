@@ -174,6 +174,8 @@ class RolloutEngine:
         if tp is not None and tp.world > 1:
             if args.is_moe:
                 raise ValueError("tensor-parallel rollout covers dense decoders")
+            if args.qk_norm_full or args.hidden_act != "silu":
+                raise NotImplementedError("tensor-parallel rollout of full-width q/k norms or GeGLU is not implemented")
             from dataclasses import replace
             args = replace(args, num_heads=args.num_heads // tp.world, num_kv_heads=args.num_kv_heads // tp.world,
                            intermediate_size=args.intermediate_size // tp.world)
@@ -185,6 +187,7 @@ class RolloutEngine:
         self.dtype = weights.dtype
         self.max_num_seqs = int(max_num_seqs)
         self.max_model_len = int(max_model_len)
+        args.check_context(self.max_model_len)
         self.block_size = int(block_size)
         self.max_blocks_per_seq = math.ceil(self.max_model_len / self.block_size)
         self.max_num_batched_tokens = int(max_num_batched_tokens)
@@ -681,7 +684,14 @@ class RolloutEngine:
 
             def mlp_act(x, w):
                 return ops.swiglu(F.linear(x, w))
+        if a.hidden_act != "silu":
+            # GeGLU families: the projection, then the tanh-GELU gate
+            def mlp_act(x, w, _proj=proj):
+                g, u = _proj(x, w).chunk(2, dim=-1)
+                return F.gelu(g.float(), approximate="tanh").to(g.dtype) * u
         x = F.embedding(ids, W["embed.weight"])
+        if a.embed_scale:
+            x = x * torch.tensor(a.embed_scale, dtype=x.dtype)
         resid = None
         T = ids.shape[0]
         for l in range(a.num_layers):
@@ -698,7 +708,12 @@ class RolloutEngine:
                 else:
                     q.copy_(ops.head_rms_norm(q, W[pre + "attn.q_norm"], a.rms_eps))
                     k.copy_(ops.head_rms_norm(k, W[pre + "attn.k_norm"], a.rms_eps))
-            ops.rope_qkv_(qkv, pos, a.num_heads, a.num_kv_heads, a.head_dim, a.rope_theta,
+            if a.qk_norm_full:
+                q = qkv[:, : a.q_size]
+                k = qkv[:, a.q_size: a.q_size + a.kv_size]
+                q.copy_(ops.rms_norm(q.contiguous(), W[pre + "attn.q_norm"], a.rms_eps)[0])
+                k.copy_(ops.rms_norm(k.contiguous(), W[pre + "attn.k_norm"], a.rms_eps)[0])
+            ops.rope_qkv_(qkv, pos, a.num_heads, a.num_kv_heads, a.head_dim, a.rope_spec,
                           k_cache=self.k_cache[l], v_cache=self.v_cache[l], slots=slots)
             q = qkv[:, : a.q_size].view(T, a.num_heads, a.head_dim)
             if mode == "prefill":
@@ -721,6 +736,14 @@ class RolloutEngine:
         return hN
 
     def _moe(self, h, pre):
+        y = self._moe_routed(h, pre)
+        if self.args.shared_expert_intermediate_size:
+            W = self.w
+            sh = F.linear(ops.swiglu(F.linear(h, W[pre + "mlp.shared_gate_up.weight"])), W[pre + "mlp.shared_down.weight"])
+            y = y + torch.sigmoid(F.linear(h, W[pre + "mlp.shared_gate.weight"]).float()).to(sh.dtype) * sh
+        return y
+
+    def _moe_routed(self, h, pre):
         from ..ops import moe as moe_ops
         from ..parallel.moe import moe_forward_local
         a, W = self.args, self.w
