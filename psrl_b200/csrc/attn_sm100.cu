@@ -22,8 +22,14 @@
 //               P written back to TMEM with tcgen05.st; at the end O / l and the
 //               row's log-sum-exp.
 //
-// Work per block: tile A needs key tiles 0 .. 2t (t = block index), tile B
-// 0 .. 2t+1; only the diagonal tile of each is masked.  Blocks are launched
+// Queries and keys may come from different tensors with their own row
+// offsets (cu_q / cu_k): sequence b's queries are the LAST Lq of its Lk key
+// positions (Lk >= Lq; self-attention has Lk = Lq), so query row p sees keys
+// 0 .. p + Lk - Lq.  Context-parallel attention uses this for a rank's query
+// chunks against the gathered keys of the sequence prefix.
+//
+// Work per block: tile A needs the key tiles up to its last row's limit,
+// tile B one more or two; only tiles that cross a row's limit are masked.  Blocks are launched
 // largest first.  Every wait is bounded; on timeout the kernel records an
 // error code and leaves.  TMA loads are plain per-CTA copies.
 #include <cuda.h>
@@ -52,7 +58,9 @@ constexpr int NTHREADS = 320;
 constexpr float RESCALE_LOG2 = 8.0f;
 
 struct FwdArgs {
-  const int* cu;     // [B + 1]
+  const int* cu;     // [B + 1] query rows
+  const int* cu_k;   // [B + 1] key / value rows
+  int q_col, k_col, v_col;  // column of head 0 in the query / key / value tensors
   int nq, nkv, T;
   int blocks_z;      // grid.z = max 256-row blocks per sequence
   float scale_log2;  // softmax scale * log2(e)
@@ -73,17 +81,22 @@ __device__ __forceinline__ void set_err(int* err, int code, int it = -1) {
   }
 }
 
-__global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_constant__ CUtensorMap tm, FwdArgs a) {
+__global__ void __launch_bounds__(NTHREADS, 1)
+    fa_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV, FwdArgs a) {
   const int h = blockIdx.x, b = blockIdx.y;
   const int blk = a.blocks_z - 1 - (int)blockIdx.z;  // largest blocks first
   const int s0 = a.cu[b], L = a.cu[b + 1] - s0;
+  const int sk0 = a.cu_k[b], Lk = a.cu_k[b + 1] - sk0;
+  const int off = Lk - L;  // query row p sees keys 0 .. p + off
   const int q0 = blk * 2 * BQ;
   if (q0 >= L) return;  // uniform for the whole CTA, before any barrier
   const int rowsB = max(0, min(BQ, L - q0 - BQ));
-  const int nA = 2 * blk + 1, nB = rowsB > 0 ? 2 * blk + 2 : 0;
+  const int nKt = (Lk + BKV - 1) / BKV;
+  const int nA = min(nKt, (min(q0 + BQ, L) - 1 + off) / BKV + 1);
+  const int nB = rowsB > 0 ? min(nKt, (q0 + BQ + rowsB - 1 + off) / BKV + 1) : 0;
   const int nK = max(nA, nB);
   const int hk = h / (a.nq / a.nkv);
-  const int xq = h * D, xk = (a.nq + hk) * D, xv = (a.nq + a.nkv + hk) * D;
+  const int xq = a.q_col + h * D, xk = a.k_col + hk * D, xv = a.v_col + hk * D;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -121,14 +134,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      tma_prefetch_desc(&tm);
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmKV);
       mbar_expect_tx(bq, (nB ? 2 : 1) * Q_BYTES);
       const uint32_t sq = smem_u32(smem);
-      tma_load_2d(sq, &tm, xq, s0 + q0, bq);
-      tma_load_2d(sq + ATOM, &tm, xq + 64, s0 + q0, bq);
+      tma_load_2d(sq, &tmQ, xq, s0 + q0, bq);
+      tma_load_2d(sq + ATOM, &tmQ, xq + 64, s0 + q0, bq);
       if (nB) {
-        tma_load_2d(sq + Q_BYTES, &tm, xq, s0 + q0 + BQ, bq);
-        tma_load_2d(sq + Q_BYTES + ATOM, &tm, xq + 64, s0 + q0 + BQ, bq);
+        tma_load_2d(sq + Q_BYTES, &tmQ, xq, s0 + q0 + BQ, bq);
+        tma_load_2d(sq + Q_BYTES + ATOM, &tmQ, xq + 64, s0 + q0 + BQ, bq);
       }
       for (int j = 0; j < nK && !s_abort; ++j) {
         const int st = j % NS;
@@ -141,11 +155,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
         const uint32_t fb = bkf + 8 * st;
         mbar_expect_tx(fb, STAGE);
         const uint32_t sk = smem_u32(smem + OFF_KV + st * STAGE), sv = sk + KV_TILE;
-        const int y = s0 + j * BKV;
-        tma_load_2d(sk, &tm, xk, y, fb);
-        tma_load_2d(sk + ATOM, &tm, xk + 64, y, fb);
-        tma_load_2d(sv, &tm, xv, y, fb);
-        tma_load_2d(sv + ATOM, &tm, xv + 64, y, fb);
+        const int y = sk0 + j * BKV;
+        tma_load_2d(sk, &tmKV, xk, y, fb);
+        tma_load_2d(sk + ATOM, &tmKV, xk + 64, y, fb);
+        tma_load_2d(sv, &tmKV, xv, y, fb);
+        tma_load_2d(sv + ATOM, &tmKV, xv + 64, y, fb);
       }
     }
   } else if (warp == 1) {
@@ -221,7 +235,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
     const int r = quad * 32 + lane;           // row within the tile
     const int row_pos = q0 + g * BQ + r;      // position within the sequence
     const uint32_t ts = tS(g) + ((uint32_t)(quad * 32) << 16), to = tO(g) + ((uint32_t)(quad * 32) << 16);
-    const int diag = 2 * blk + g;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n; ++j) {
@@ -231,7 +244,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
         break;
       }
       fence_after();
-      const bool masked_tile = (j == diag);
+      const int lim = row_pos + off - j * BKV;  // last key column of tile j this row sees
+      const bool masked_tile = __any_sync(0xffffffffu, lim < BKV - 1);
       // pass 1: row maximum of this key tile (scaled, base 2)
       float mx = -INFINITY;
 #pragma unroll 1
@@ -241,7 +255,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const bool dead = masked_tile && (c * 32 + i > r);
+          const bool dead = masked_tile && (c * 32 + i > lim);
           mx = fmaxf(mx, dead ? -INFINITY : __uint_as_float(v[i]) * a.scale_log2);
         }
       }
@@ -276,8 +290,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) fa_fwd_kernel(const __grid_consta
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int c0 = c * 32 + 2 * i;
-          const float x0 = (masked_tile && c0 > r) ? -INFINITY : __uint_as_float(v[2 * i]) * a.scale_log2;
-          const float x1 = (masked_tile && c0 + 1 > r) ? -INFINITY : __uint_as_float(v[2 * i + 1]) * a.scale_log2;
+          const float x0 = (masked_tile && c0 > lim) ? -INFINITY : __uint_as_float(v[2 * i]) * a.scale_log2;
+          const float x1 = (masked_tile && c0 + 1 > lim) ? -INFINITY : __uint_as_float(v[2 * i + 1]) * a.scale_log2;
           const float p0 = ex2(x0 - ref), p1 = ex2(x1 - ref);
           l += p0 + p1;
           const bf162 pp = __floats2bfloat162_rn(p0, p1);
@@ -352,14 +366,20 @@ constexpr int OFF_B_BAR = OFF_B_STAGE + NS * B_STAGE;
 constexpr int SMEM_BWD = OFF_B_BAR + 256 + 1024;
 
 struct BwdArgs {
-  const int* cu;
+  const int* cu;     // [B + 1] query rows
+  const int* cu_k;   // [B + 1] key / value rows
+  int q_col, k_col, v_col;
   int nq, nkv, T;
-  int blocks_z;
+  int blocks_z;      // query tiles of the longest sequence (dQ grid)
   float scale, scale_log2;
   const float* lse;  // [nq, T] natural log
   const float* dd;   // [nq, T] rowsum(dO * O)
-  bf16* dqkv;        // [T, (nq + 2 nkv) * D]
-  int64_t dqkv_row;
+  bf16* dq;          // query-gradient rows (dq_row apart), head 0 at column dq_col
+  int64_t dq_row;
+  int dq_col;
+  bf16* dkv;         // key / value-gradient rows (dkv_row apart), heads at dk_col / dv_col
+  int64_t dkv_row;
+  int dk_col, dv_col;
   int* err;
 };
 
@@ -399,15 +419,19 @@ __device__ __forceinline__ void mma_tile_ts(uint32_t d, uint32_t a_tmem, uint32_
 }
 
 __global__ void __launch_bounds__(NT_BWD, 1)
-    fa_bwd_dkdv(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do, BwdArgs a) {
+    fa_bwd_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
+                const __grid_constant__ CUtensorMap tm_do, BwdArgs a) {
   const int hk = blockIdx.x, b = blockIdx.y, j = blockIdx.z;  // small j: most work, launched first
   const int s0 = a.cu[b], L = a.cu[b + 1] - s0;
-  if (j * BKV >= L) return;
+  const int sk0 = a.cu_k[b], Lk = a.cu_k[b + 1] - sk0;
+  const int off = Lk - L;
+  if (j * BKV >= Lk) return;
   const int G = a.nq / a.nkv;
   const int nqt = (L + BQ - 1) / BQ;
-  const int per_head = nqt - j;
+  const int i0 = max(0, j * BKV - off) / BQ;  // first query tile that sees key tile j
+  const int per_head = nqt - i0;
   const int iters = G * per_head;
-  const int xk = (a.nq + hk) * D, xv = (a.nq + a.nkv + hk) * D;
+  const int xk = a.k_col + hk * D, xv = a.v_col + hk * D;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -441,16 +465,17 @@ __global__ void __launch_bounds__(NT_BWD, 1)
     // producer: K_j, V_j once; then per iteration Q_i, dO_i (TMA) and lse_i, D_i (warp copy)
     const uint32_t sk = smem_u32(smem), sv = sk + KV_TILE;
     if (lane == 0) {
-      tma_prefetch_desc(&tm_qkv);
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmKV);
       tma_prefetch_desc(&tm_do);
       mbar_expect_tx(bkv, 2 * KV_TILE);
-      tma_load_2d(sk, &tm_qkv, xk, s0 + j * BKV, bkv);
-      tma_load_2d(sk + ATOM, &tm_qkv, xk + 64, s0 + j * BKV, bkv);
-      tma_load_2d(sv, &tm_qkv, xv, s0 + j * BKV, bkv);
-      tma_load_2d(sv + ATOM, &tm_qkv, xv + 64, s0 + j * BKV, bkv);
+      tma_load_2d(sk, &tmKV, xk, sk0 + j * BKV, bkv);
+      tma_load_2d(sk + ATOM, &tmKV, xk + 64, sk0 + j * BKV, bkv);
+      tma_load_2d(sv, &tmKV, xv, sk0 + j * BKV, bkv);
+      tma_load_2d(sv + ATOM, &tmKV, xv + 64, sk0 + j * BKV, bkv);
     }
     for (int it = 0; it < iters && !s_abort; ++it) {
-      const int hq = hk * G + it / per_head, i = j + it % per_head;
+      const int hq = hk * G + it / per_head, i = i0 + it % per_head;
       const int st = it % NS;
       const uint32_t ph = (it / NS) & 1;
       bool ok = true;
@@ -469,8 +494,8 @@ __global__ void __launch_bounds__(NT_BWD, 1)
       if (lane == 0) {
         mbar_expect_tx(fb, 2 * KV_TILE);
         const int y = s0 + i * BQ;
-        tma_load_2d(sq, &tm_qkv, hq * D, y, fb);
-        tma_load_2d(sq + ATOM, &tm_qkv, hq * D + 64, y, fb);
+        tma_load_2d(sq, &tmQ, a.q_col + hq * D, y, fb);
+        tma_load_2d(sq + ATOM, &tmQ, a.q_col + hq * D + 64, y, fb);
         tma_load_2d(sdo, &tm_do, hq * D, y, fb);
         tma_load_2d(sdo + ATOM, &tm_do, hq * D + 64, y, fb);
       }
@@ -520,7 +545,7 @@ __global__ void __launch_bounds__(NT_BWD, 1)
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     bool ok = true;
     for (int it = 0; it < iters; ++it) {
-      const int i = j + it % per_head;
+      const int i = i0 + it % per_head;
       const int st = it % NS;
       if (!mbar_wait(bs, it & 1) || s_abort) {
         ok = false;
@@ -544,7 +569,7 @@ __global__ void __launch_bounds__(NT_BWD, 1)
           for (int u = 0; u < 2; ++u) {
             const int cc = col0 + 2 * e + u;
             const int q = i * BQ + cc;
-            const bool live = (q < L) && (key <= q);
+            const bool live = (q < L) && (key <= q + off);
             const float p = live ? ex2(__uint_as_float(vs[2 * e + u]) * a.scale_log2 - lse_s[cc]) : 0.f;
             pv[u] = p;
             dv[u] = live ? p * (__uint_as_float(vp[2 * e + u]) - dd_s[cc]) : 0.f;
@@ -567,8 +592,9 @@ __global__ void __launch_bounds__(NT_BWD, 1)
     fence_after();
     if (ok && !s_abort) {
       const int key = j * BKV + r;
-      const bool valid = key < L;
-      bf16* rowp = a.dqkv + (int64_t)(s0 + key) * a.dqkv_row;
+      const bool valid = key < Lk;
+      bf16* rowp = a.dkv + (int64_t)(sk0 + key) * a.dkv_row;
+      const int ok_col = a.dk_col + hk * D, ov_col = a.dv_col + hk * D;
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
         const int col0 = half * 64 + c * 32;
@@ -585,8 +611,8 @@ __global__ void __launch_bounds__(NT_BWD, 1)
           }
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
-            *reinterpret_cast<bf16x8*>(rowp + xv + col0 + e) = pack8(f + e);
-            *reinterpret_cast<bf16x8*>(rowp + xk + col0 + e) = pack8(g + e);
+            *reinterpret_cast<bf16x8*>(rowp + ov_col + col0 + e) = pack8(f + e);
+            *reinterpret_cast<bf16x8*>(rowp + ok_col + col0 + e) = pack8(g + e);
           }
         }
       }
@@ -603,14 +629,17 @@ __global__ void __launch_bounds__(NT_BWD, 1)
 }
 
 __global__ void __launch_bounds__(NT_BWD, 1)
-    fa_bwd_dq(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do, BwdArgs a) {
+    fa_bwd_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
+              const __grid_constant__ CUtensorMap tm_do, BwdArgs a) {
   const int h = blockIdx.x, b = blockIdx.y;
   const int i = a.blocks_z - 1 - (int)blockIdx.z;  // large query tiles (most key tiles) first
   const int s0 = a.cu[b], L = a.cu[b + 1] - s0;
+  const int sk0 = a.cu_k[b], Lk = a.cu_k[b + 1] - sk0;
+  const int off = Lk - L;
   if (i * BQ >= L) return;
-  const int n = i + 1;
+  const int n = min((Lk + BKV - 1) / BKV, (min((i + 1) * BQ, L) - 1 + off) / BKV + 1);
   const int hk = h / (a.nq / a.nkv);
-  const int xk = (a.nq + hk) * D, xv = (a.nq + a.nkv + hk) * D;
+  const int xk = a.k_col + hk * D, xv = a.v_col + hk * D;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -642,12 +671,13 @@ __global__ void __launch_bounds__(NT_BWD, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      tma_prefetch_desc(&tm_qkv);
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmKV);
       tma_prefetch_desc(&tm_do);
       mbar_expect_tx(bqd, 2 * KV_TILE);
       const int y = s0 + i * BQ;
-      tma_load_2d(sq, &tm_qkv, h * D, y, bqd);
-      tma_load_2d(sq + ATOM, &tm_qkv, h * D + 64, y, bqd);
+      tma_load_2d(sq, &tmQ, a.q_col + h * D, y, bqd);
+      tma_load_2d(sq + ATOM, &tmQ, a.q_col + h * D + 64, y, bqd);
       tma_load_2d(sdo, &tm_do, h * D, y, bqd);
       tma_load_2d(sdo + ATOM, &tm_do, h * D + 64, y, bqd);
       for (int jj = 0; jj < n && !s_abort; ++jj) {
@@ -661,11 +691,11 @@ __global__ void __launch_bounds__(NT_BWD, 1)
         const uint32_t fb = bkf0 + 8 * st;
         mbar_expect_tx(fb, 2 * KV_TILE);
         const uint32_t sk = smem_u32(smem + OFF_B_STAGE + st * B_STAGE), sv = sk + KV_TILE;
-        const int y2 = s0 + jj * BKV;
-        tma_load_2d(sk, &tm_qkv, xk, y2, fb);
-        tma_load_2d(sk + ATOM, &tm_qkv, xk + 64, y2, fb);
-        tma_load_2d(sv, &tm_qkv, xv, y2, fb);
-        tma_load_2d(sv + ATOM, &tm_qkv, xv + 64, y2, fb);
+        const int y2 = sk0 + jj * BKV;
+        tma_load_2d(sk, &tmKV, xk, y2, fb);
+        tma_load_2d(sk + ATOM, &tmKV, xk + 64, y2, fb);
+        tma_load_2d(sv, &tmKV, xv, y2, fb);
+        tma_load_2d(sv + ATOM, &tmKV, xv + 64, y2, fb);
       }
     }
   } else if (warp == 1) {
@@ -720,7 +750,7 @@ __global__ void __launch_bounds__(NT_BWD, 1)
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int key = jj * BKV + col0 + 2 * e + u;
-            const bool live = qin && key <= q;
+            const bool live = qin && key <= q + off;
             const float p = live ? ex2(__uint_as_float(vs[2 * e + u]) * a.scale_log2 - lse2) : 0.f;
             dv[u] = live ? p * (__uint_as_float(vp[2 * e + u]) - dd) : 0.f;
           }
@@ -737,7 +767,7 @@ __global__ void __launch_bounds__(NT_BWD, 1)
     if (!mbar_wait(bdone, 0)) ok = false;
     fence_after();
     if (ok && !s_abort) {
-      bf16* rowp = a.dqkv + (int64_t)(s0 + q) * a.dqkv_row + (int64_t)h * D;
+      bf16* rowp = a.dq + (int64_t)(s0 + q) * a.dq_row + a.dq_col + (int64_t)h * D;
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
         const int col0 = half * 64 + c * 32;
@@ -768,52 +798,6 @@ __global__ void __launch_bounds__(NT_BWD, 1)
 
 using namespace fa5;
 
-// qkv: [T, (nq + 2 nkv) * 128] bf16 (q heads, then k heads, then v heads per
-// token, unit inner stride, rows on 16-byte boundaries).  Returns
-// {o [T, nq * 128] bf16, lse [nq, T] fp32 (natural log; empty unless want_lse)}.
-std::vector<at::Tensor> attn_fwd_sm100(at::Tensor qkv, at::Tensor cu_seqlens, int64_t max_seqlen, int64_t nq,
-                                       int64_t nkv, double scale, bool want_lse, at::Tensor err) {
-  CHECK_CUDA_TENSOR(qkv);
-  CHECK_DTYPE(qkv, at::kBFloat16);
-  TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1 && qkv.size(1) == (nq + 2 * nkv) * D,
-              "qkv must be [T, (nq + 2 nkv) * 128] with unit inner stride");
-  TORCH_CHECK(nq % nkv == 0, "nq must be a multiple of nkv");
-  TORCH_CHECK(cu_seqlens.scalar_type() == at::kInt && cu_seqlens.is_contiguous(), "cu_seqlens int32");
-  const int64_t T = qkv.size(0);
-  const int B = (int)cu_seqlens.numel() - 1;
-  at::cuda::CUDAGuard g(qkv.device());
-  auto o = at::empty({T, nq * D}, qkv.options());
-  auto lse = want_lse ? at::empty({nq, T}, qkv.options().dtype(at::kFloat)) : at::Tensor();
-  if (T == 0 || B <= 0 || max_seqlen <= 0) return {o, lse};
-  TORCH_CHECK((qkv.stride(0) * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(qkv.data_ptr()) % 16 == 0,
-              "qkv rows must start on 16-byte boundaries");
-  CUtensorMap m;
-  cuuint64_t dims[2] = {(cuuint64_t)qkv.size(1), (cuuint64_t)T};
-  cuuint64_t strides[1] = {(cuuint64_t)qkv.stride(0) * 2};
-  cuuint32_t box[2] = {64u, 128u};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = PSRL_DRV(cuTensorMapEncodeTiled)(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv.data_ptr(), dims, strides,
-                                                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (", (int)r, ")");
-  FwdArgs a{};
-  a.cu = cu_seqlens.data_ptr<int>();
-  a.nq = (int)nq;
-  a.nkv = (int)nkv;
-  a.T = (int)T;
-  a.blocks_z = (int)((max_seqlen + 2 * BQ - 1) / (2 * BQ));
-  a.scale_log2 = (float)(scale * 1.4426950408889634);
-  a.o = reinterpret_cast<bf16*>(o.data_ptr());
-  a.o_row = nq * D;
-  a.lse = want_lse ? lse.data_ptr<float>() : nullptr;
-  a.err = err.data_ptr<int>();
-  ensure_smem_attr(fa_fwd_kernel, SMEM_BYTES);
-  dim3 grid((unsigned)nq, (unsigned)B, (unsigned)a.blocks_z);
-  fa_fwd_kernel<<<grid, NTHREADS, SMEM_BYTES, stream()>>>(m, a);
-  PSRL_CHECK_LAUNCH();
-  return {o, lse};
-}
-
 static CUtensorMap map_rows_64x128(const at::Tensor& t) {
   TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1 && (t.stride(0) * 2) % 16 == 0 &&
                   reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
@@ -830,25 +814,90 @@ static CUtensorMap map_rows_64x128(const at::Tensor& t) {
   return m;
 }
 
-// Backward of attn_fwd_sm100: qkv [T, (nq + 2 nkv) * 128], o and dout
-// [T, nq * 128] (bf16), lse [nq, T].  Returns dqkv [T, (nq + 2 nkv) * 128] bf16.
-at::Tensor attn_bwd_sm100(at::Tensor qkv, at::Tensor o, at::Tensor dout, at::Tensor lse, at::Tensor cu_seqlens,
-                          int64_t max_seqlen, int64_t nq, int64_t nkv, double scale, at::Tensor err) {
+// Shared launcher: queries in q (columns q_col + h * 128), keys and values in
+// kv (k_col / v_col + hk * 128); sequence b's query rows [cu_q[b], cu_q[b+1])
+// are the last of its key rows [cu_k[b], cu_k[b+1]).
+static std::vector<at::Tensor> fwd_launch(const at::Tensor& q, const at::Tensor& kv, const at::Tensor& cu_q,
+                                          const at::Tensor& cu_k, int64_t max_q, int64_t nq, int64_t nkv, int q_col,
+                                          int k_col, int v_col, double scale, bool want_lse, const at::Tensor& err) {
+  CHECK_DTYPE(q, at::kBFloat16);
+  CHECK_DTYPE(kv, at::kBFloat16);
+  TORCH_CHECK(nq % nkv == 0, "nq must be a multiple of nkv");
+  TORCH_CHECK(cu_q.scalar_type() == at::kInt && cu_q.is_contiguous() && cu_k.scalar_type() == at::kInt &&
+                  cu_k.is_contiguous() && cu_q.numel() == cu_k.numel(),
+              "cu_q / cu_k: int32 [B + 1]");
+  const int64_t T = q.size(0);
+  const int B = (int)cu_q.numel() - 1;
+  at::cuda::CUDAGuard g(q.device());
+  auto o = at::empty({T, nq * D}, q.options());
+  auto lse = want_lse ? at::empty({nq, T}, q.options().dtype(at::kFloat)) : at::Tensor();
+  if (T == 0 || B <= 0 || max_q <= 0) return {o, lse};
+  const CUtensorMap tq = map_rows_64x128(q), tkv = map_rows_64x128(kv);
+  FwdArgs a{};
+  a.cu = cu_q.data_ptr<int>();
+  a.cu_k = cu_k.data_ptr<int>();
+  a.q_col = q_col;
+  a.k_col = k_col;
+  a.v_col = v_col;
+  a.nq = (int)nq;
+  a.nkv = (int)nkv;
+  a.T = (int)T;
+  a.blocks_z = (int)((max_q + 2 * BQ - 1) / (2 * BQ));
+  a.scale_log2 = (float)(scale * 1.4426950408889634);
+  a.o = reinterpret_cast<bf16*>(o.data_ptr());
+  a.o_row = nq * D;
+  a.lse = want_lse ? lse.data_ptr<float>() : nullptr;
+  a.err = err.data_ptr<int>();
+  ensure_smem_attr(fa_fwd_kernel, SMEM_BYTES);
+  dim3 grid((unsigned)nq, (unsigned)B, (unsigned)a.blocks_z);
+  fa_fwd_kernel<<<grid, NTHREADS, SMEM_BYTES, stream()>>>(tq, tkv, a);
+  PSRL_CHECK_LAUNCH();
+  return {o, lse};
+}
+
+// qkv: [T, (nq + 2 nkv) * 128] bf16 (q heads, then k heads, then v heads per
+// token, unit inner stride, rows on 16-byte boundaries).  Returns
+// {o [T, nq * 128] bf16, lse [nq, T] fp32 (natural log; empty unless want_lse)}.
+std::vector<at::Tensor> attn_fwd_sm100(at::Tensor qkv, at::Tensor cu_seqlens, int64_t max_seqlen, int64_t nq,
+                                       int64_t nkv, double scale, bool want_lse, at::Tensor err) {
   CHECK_CUDA_TENSOR(qkv);
-  CHECK_DTYPE(qkv, at::kBFloat16);
+  TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1 && qkv.size(1) == (nq + 2 * nkv) * D,
+              "qkv must be [T, (nq + 2 nkv) * 128] with unit inner stride");
+  return fwd_launch(qkv, qkv, cu_seqlens, cu_seqlens, max_seqlen, nq, nkv, 0, (int)(nq * D), (int)((nq + nkv) * D),
+                    scale, want_lse, err);
+}
+
+// Queries against separately stored keys / values (context parallelism):
+// q [Tq, >= nq * 128] (a row-strided view is fine), kv [Tk, 2 nkv * 128]
+// (k heads then v heads); sequence b has cu_q[b+1] - cu_q[b] queries that are
+// the last of its cu_k[b+1] - cu_k[b] (>=) key positions.
+std::vector<at::Tensor> attn_fwd_sm100_kv(at::Tensor q, at::Tensor kv, at::Tensor cu_q, at::Tensor cu_k,
+                                          int64_t max_q, int64_t nq, int64_t nkv, double scale, bool want_lse,
+                                          at::Tensor err) {
+  CHECK_CUDA_TENSOR(q);
+  TORCH_CHECK(q.dim() == 2 && q.size(1) >= nq * D && kv.dim() == 2 && kv.size(1) == 2 * nkv * D,
+              "q [Tq, nq * 128], kv [Tk, 2 nkv * 128]");
+  return fwd_launch(q, kv, cu_q, cu_k, max_q, nq, nkv, 0, 0, (int)(nkv * D), scale, want_lse, err);
+}
+
+// Shared backward launcher (see fwd_launch); writes dq rows into `dq` and dk /
+// dv rows into `dkv` (which may be the same tensor as dq).
+static void bwd_launch(const at::Tensor& q, const at::Tensor& kv, const at::Tensor& o, const at::Tensor& dout,
+                       const at::Tensor& lse, const at::Tensor& cu_q, const at::Tensor& cu_k, int64_t max_q,
+                       int64_t max_k, int64_t nq, int64_t nkv, int q_col, int k_col, int v_col, double scale,
+                       at::Tensor& dq, int dq_col, at::Tensor& dkv, int dk_col, int dv_col, const at::Tensor& err) {
+  CHECK_DTYPE(q, at::kBFloat16);
+  CHECK_DTYPE(kv, at::kBFloat16);
   CHECK_DTYPE(o, at::kBFloat16);
   CHECK_DTYPE(dout, at::kBFloat16);
   CHECK_DTYPE(lse, at::kFloat);
-  const int64_t T = qkv.size(0);
-  TORCH_CHECK(qkv.dim() == 2 && qkv.size(1) == (nq + 2 * nkv) * D && nq % nkv == 0, "qkv layout");
+  const int64_t T = q.size(0);
   TORCH_CHECK(o.is_contiguous() && dout.is_contiguous() && o.numel() == T * nq * D && dout.numel() == T * nq * D,
-              "o / dout must be contiguous [T, nq * 128]");
-  TORCH_CHECK(lse.is_contiguous() && lse.numel() == nq * T, "lse must be contiguous [nq, T]");
-  const int B = (int)cu_seqlens.numel() - 1;
-  at::cuda::CUDAGuard g(qkv.device());
-  auto dqkv = at::empty({T, (nq + 2 * nkv) * D}, qkv.options());
-  if (T == 0 || B <= 0 || max_seqlen <= 0) return dqkv.zero_();
-  auto dd = at::empty({nq, T}, qkv.options().dtype(at::kFloat));
+              "o / dout must be contiguous [Tq, nq * 128]");
+  TORCH_CHECK(lse.is_contiguous() && lse.numel() == nq * T, "lse must be contiguous [nq, Tq]");
+  const int B = (int)cu_q.numel() - 1;
+  if (T == 0 || B <= 0 || max_q <= 0) return;
+  auto dd = at::empty({nq, T}, q.options().dtype(at::kFloat));
   {
     const int64_t warps = T * nq;
     fa_bwd_dot<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, stream()>>>(
@@ -856,27 +905,68 @@ at::Tensor attn_bwd_sm100(at::Tensor qkv, at::Tensor o, at::Tensor dout, at::Ten
         dd.data_ptr<float>());
     PSRL_CHECK_LAUNCH();
   }
-  const CUtensorMap tq = map_rows_64x128(qkv), tdo = map_rows_64x128(dout.view({T, nq * D}));
+  const CUtensorMap tq = map_rows_64x128(q), tkv = map_rows_64x128(kv), tdo = map_rows_64x128(dout.view({T, nq * D}));
   BwdArgs a{};
-  a.cu = cu_seqlens.data_ptr<int>();
+  a.cu = cu_q.data_ptr<int>();
+  a.cu_k = cu_k.data_ptr<int>();
+  a.q_col = q_col;
+  a.k_col = k_col;
+  a.v_col = v_col;
   a.nq = (int)nq;
   a.nkv = (int)nkv;
   a.T = (int)T;
-  a.blocks_z = (int)((max_seqlen + BQ - 1) / BQ);
+  a.blocks_z = (int)((max_q + BQ - 1) / BQ);
   a.scale = (float)scale;
   a.scale_log2 = (float)(scale * 1.4426950408889634);
   a.lse = lse.data_ptr<float>();
   a.dd = dd.data_ptr<float>();
-  a.dqkv = reinterpret_cast<bf16*>(dqkv.data_ptr());
-  a.dqkv_row = (nq + 2 * nkv) * D;
+  a.dq = reinterpret_cast<bf16*>(dq.data_ptr());
+  a.dq_row = dq.stride(0);
+  a.dq_col = dq_col;
+  a.dkv = reinterpret_cast<bf16*>(dkv.data_ptr());
+  a.dkv_row = dkv.stride(0);
+  a.dk_col = dk_col;
+  a.dv_col = dv_col;
   a.err = err.data_ptr<int>();
   ensure_smem_attr(fa_bwd_dkdv, SMEM_BWD);
   ensure_smem_attr(fa_bwd_dq, SMEM_BWD);
-  fa_bwd_dkdv<<<dim3((unsigned)nkv, (unsigned)B, (unsigned)a.blocks_z), NT_BWD, SMEM_BWD, stream()>>>(tq, tdo, a);
+  const unsigned kz = (unsigned)((max_k + BKV - 1) / BKV);
+  fa_bwd_dkdv<<<dim3((unsigned)nkv, (unsigned)B, kz), NT_BWD, SMEM_BWD, stream()>>>(tq, tkv, tdo, a);
   PSRL_CHECK_LAUNCH();
-  fa_bwd_dq<<<dim3((unsigned)nq, (unsigned)B, (unsigned)a.blocks_z), NT_BWD, SMEM_BWD, stream()>>>(tq, tdo, a);
+  fa_bwd_dq<<<dim3((unsigned)nq, (unsigned)B, (unsigned)a.blocks_z), NT_BWD, SMEM_BWD, stream()>>>(tq, tkv, tdo, a);
   PSRL_CHECK_LAUNCH();
+}
+
+// Backward of attn_fwd_sm100: qkv [T, (nq + 2 nkv) * 128], o and dout
+// [T, nq * 128] (bf16), lse [nq, T].  Returns dqkv [T, (nq + 2 nkv) * 128] bf16.
+at::Tensor attn_bwd_sm100(at::Tensor qkv, at::Tensor o, at::Tensor dout, at::Tensor lse, at::Tensor cu_seqlens,
+                          int64_t max_seqlen, int64_t nq, int64_t nkv, double scale, at::Tensor err) {
+  CHECK_CUDA_TENSOR(qkv);
+  TORCH_CHECK(qkv.dim() == 2 && qkv.size(1) == (nq + 2 * nkv) * D && nq % nkv == 0, "qkv layout");
+  at::cuda::CUDAGuard g(qkv.device());
+  auto dqkv = at::empty({qkv.size(0), (nq + 2 * nkv) * D}, qkv.options());
+  if (qkv.size(0) == 0 || cu_seqlens.numel() < 2 || max_seqlen <= 0) return dqkv.zero_();
+  const int kc = (int)(nq * D), vc = (int)((nq + nkv) * D);
+  bwd_launch(qkv, qkv, o, dout, lse, cu_seqlens, cu_seqlens, max_seqlen, max_seqlen, nq, nkv, 0, kc, vc, scale, dqkv,
+             0, dqkv, kc, vc, err);
   return dqkv;
+}
+
+// Backward of attn_fwd_sm100_kv.  Returns {dq [Tq, nq * 128], dkv [Tk, 2 nkv * 128]}
+// (bf16; key rows that no query sees get zero gradients).
+std::vector<at::Tensor> attn_bwd_sm100_kv(at::Tensor q, at::Tensor kv, at::Tensor o, at::Tensor dout, at::Tensor lse,
+                                          at::Tensor cu_q, at::Tensor cu_k, int64_t max_q, int64_t max_k, int64_t nq,
+                                          int64_t nkv, double scale, at::Tensor err) {
+  CHECK_CUDA_TENSOR(q);
+  TORCH_CHECK(q.dim() == 2 && q.size(1) >= nq * D && kv.dim() == 2 && kv.size(1) == 2 * nkv * D && nq % nkv == 0,
+              "q [Tq, nq * 128], kv [Tk, 2 nkv * 128]");
+  at::cuda::CUDAGuard g(q.device());
+  auto dq = at::empty({q.size(0), nq * D}, q.options());
+  auto dkv = at::zeros({kv.size(0), 2 * nkv * D}, q.options());
+  if (q.size(0) == 0 || cu_q.numel() < 2 || max_q <= 0) return {dq.zero_(), dkv};
+  bwd_launch(q, kv, o, dout, lse, cu_q, cu_k, max_q, max_k, nq, nkv, 0, 0, (int)(nkv * D), scale, dq, 0, dkv, 0,
+             (int)(nkv * D), err);
+  return {dq, dkv};
 }
 
 }  // namespace psrl

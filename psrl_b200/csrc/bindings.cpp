@@ -48,6 +48,12 @@ void peer_barrier(std::vector<at::Tensor> flags_in_peer, std::vector<at::Tensor>
 void acc_finalize(at::Tensor acc, at::Tensor out, c10::optional<at::Tensor> bias);
 at::Tensor tc_gemm_skinny(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias, bool swiglu, at::Tensor ws,
                           at::Tensor tickets, int64_t grid, at::Tensor err);
+std::vector<at::Tensor> attn_fwd_sm100_kv(at::Tensor q, at::Tensor kv, at::Tensor cu_q, at::Tensor cu_k,
+                                          int64_t max_q, int64_t nq, int64_t nkv, double scale, bool want_lse,
+                                          at::Tensor err);
+std::vector<at::Tensor> attn_bwd_sm100_kv(at::Tensor q, at::Tensor kv, at::Tensor o, at::Tensor dout, at::Tensor lse,
+                                          at::Tensor cu_q, at::Tensor cu_k, int64_t max_q, int64_t max_k, int64_t nq,
+                                          int64_t nkv, double scale, at::Tensor err);
 std::vector<at::Tensor> attn_fwd_sm100(at::Tensor qkv, at::Tensor cu_seqlens, int64_t max_seqlen, int64_t nq,
                                        int64_t nkv, double scale, bool want_lse, at::Tensor err);
 at::Tensor attn_bwd_sm100(at::Tensor qkv, at::Tensor o, at::Tensor dout, at::Tensor lse, at::Tensor cu_seqlens,
@@ -105,6 +111,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_barrier", &psrl::peer_barrier);
   m.def("acc_finalize", &psrl::acc_finalize);
   m.def("attn_fwd_sm100", &psrl::attn_fwd_sm100);
+  m.def("attn_fwd_sm100_kv", &psrl::attn_fwd_sm100_kv);
+  m.def("attn_bwd_sm100_kv", &psrl::attn_bwd_sm100_kv);
   m.def("attn_bwd_sm100", &psrl::attn_bwd_sm100);
   m.def("moe_route", &psrl::moe_route);
   m.def("moe_permute", &psrl::moe_permute);

@@ -33,6 +33,7 @@ from torch.utils.checkpoint import checkpoint
 
 from .. import ops
 from ..ops.linear import gate_up_swiglu, linear
+from ..parallel.cp import CPPlan, cp_attention
 from .config import ModelArgs
 
 
@@ -64,7 +65,12 @@ class Attention(nn.Module):
             k, _ = ops.rms_norm(k.contiguous(), self.k_norm, a.rms_eps)
             qkv = torch.cat([q, k, v], dim=-1)
         qkv = ops.rope_qkv(qkv.contiguous(), positions, a.num_heads, a.num_kv_heads, a.head_dim, a.rope_spec)
-        o = ops.varlen_attention(qkv, cu_seqlens, max_seqlen, a.num_heads, a.num_kv_heads, a.head_dim)
+        if isinstance(cu_seqlens, CPPlan):
+            # context parallel: this rank's query chunks over the gathered keys
+            o = cp_attention(qkv[:, : a.q_size], qkv[:, a.q_size:], cu_seqlens, a.num_heads, a.num_kv_heads,
+                             a.head_dim)
+        else:
+            o = ops.varlen_attention(qkv, cu_seqlens, max_seqlen, a.num_heads, a.num_kv_heads, a.head_dim)
         return linear(o, self.o.weight)
 
 
@@ -204,7 +210,7 @@ class QwenModel(nn.Module):
     # --------------------------------------------------------------- forward
     def hidden_states(self, input_ids, positions, cu_seqlens, max_seqlen):
         a = self.args
-        if a.sliding_window is not None:
+        if a.sliding_window is not None and not isinstance(cu_seqlens, CPPlan):
             a.check_context(int(max_seqlen))
         x = self.embed(input_ids)
         if a.embed_scale:

@@ -176,3 +176,68 @@ def paged_decode_attention(q, k_cache, v_cache, block_table, kv_lens, scale=None
     B = q.shape[0]
     cu = torch.arange(B + 1, dtype=torch.int32, device=q.device)
     return paged_attention_ref(q, k_cache, v_cache, cu, kv_lens, block_table, scale)
+
+
+# ------------------------------------------- queries against separate keys
+def attention_kv_ref(q, k, v, cu_q, cu_k, scale):
+    """q [Tq, nq, d]; k / v [Tk, nkv, d]; sequence b's queries
+    [cu_q[b], cu_q[b+1]) are the last of its key positions [cu_k[b], cu_k[b+1]),
+    so query row p sees keys 0 .. p + Lk - Lq.  Differentiable, fp32 math."""
+    Tq, nq, d = q.shape
+    g = nq // k.shape[1]
+    outs = []
+    cq, ck = cu_q.tolist(), cu_k.tolist()
+    for b in range(len(cq) - 1):
+        qs, qe, ks, ke = cq[b], cq[b + 1], ck[b], ck[b + 1]
+        Lq, Lk = qe - qs, ke - ks
+        if Lq <= 0:
+            continue
+        qq = q[qs:qe].float().transpose(0, 1)
+        kk = k[ks:ke].float().transpose(0, 1).repeat_interleave(g, 0)
+        vv = v[ks:ke].float().transpose(0, 1).repeat_interleave(g, 0)
+        rows = torch.arange(Lq, device=q.device)[:, None] + (Lk - Lq)
+        mask = torch.arange(Lk, device=q.device)[None, :] > rows
+        att = ((qq @ kk.transpose(1, 2)) * scale).masked_fill(mask, float("-inf")).softmax(-1)
+        outs.append((att @ vv).transpose(0, 1).to(q.dtype))
+    return torch.cat(outs, 0) if outs else q.new_zeros(0, nq, d)
+
+
+class _AttnKVFn(torch.autograd.Function):
+    """tcgen05 forward / backward of queries against separately stored keys
+    (``attn_fwd_sm100_kv`` / ``attn_bwd_sm100_kv``)."""
+
+    @staticmethod
+    def forward(ctx, q, kv, cu_q, cu_k, max_q, max_k, nq, nkv, scale):
+        from .gemm import _err
+        o, lse = ext().attn_fwd_sm100_kv(q, kv, cu_q, cu_k, int(max_q), int(nq), int(nkv), float(scale), True,
+                                         _err(q.device))
+        ctx.save_for_backward(q, kv, o, lse, cu_q, cu_k)
+        ctx.cfg = (max_q, max_k, nq, nkv, scale)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        from .gemm import _err
+        q, kv, o, lse, cu_q, cu_k = ctx.saved_tensors
+        max_q, max_k, nq, nkv, scale = ctx.cfg
+        dq, dkv = ext().attn_bwd_sm100_kv(q, kv, o, do.contiguous(), lse, cu_q, cu_k, int(max_q), int(max_k),
+                                          int(nq), int(nkv), float(scale), _err(q.device))
+        return dq, dkv, None, None, None, None, None, None, None
+
+
+def attention_kv(q: torch.Tensor, kv: torch.Tensor, cu_q: torch.Tensor, cu_k: torch.Tensor, max_q: int, max_k: int,
+                 nq: int, nkv: int, d: int, scale: float | None = None) -> torch.Tensor:
+    """Causal attention of queries ``q`` [Tq, nq * d] against keys / values
+    ``kv`` [Tk, 2 nkv * d] (k heads, then v heads) where each sequence's queries
+    are the last ``Lq`` of its ``Lk >= Lq`` key positions; returns [Tq, nq * d].
+    Context-parallel attention runs a rank's query chunks through this against
+    the gathered key prefix."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(d)
+    if q.is_cuda and q.dtype == torch.bfloat16 and d == 128:
+        if q.stride(1) != 1 or q.stride(0) % 8 or q.data_ptr() % 16:
+            q = q.contiguous()
+        return _AttnKVFn.apply(q, kv.contiguous(), cu_q, cu_k, int(max_q), int(max_k), nq, nkv, scale)
+    Tq, Tk = q.shape[0], kv.shape[0]
+    o = attention_kv_ref(q.reshape(Tq, -1)[:, : nq * d].reshape(Tq, nq, d), kv[:, : nkv * d].reshape(Tk, nkv, d),
+                         kv[:, nkv * d:].reshape(Tk, nkv, d), cu_q, cu_k, scale)
+    return o.reshape(Tq, nq * d)

@@ -105,3 +105,37 @@ def test_bwd_matches_fp32(lens, nq, nkv):
         got, want = dqkv[:, sl].float(), ref[:, sl]
         err = (got - want).abs().max().item()
         assert err <= 5e-2 * max(1.0, want.abs().max().item()), f"{name}: max abs err {err}"
+
+
+@pytest.mark.parametrize("pairs,nq,nkv", [
+    ([(128, 128), (100, 300), (257, 257)], 16, 2),
+    ([(64, 1000), (200, 1700), (130, 131), (1, 77)], 16, 2),
+    ([(300, 812)], 28, 4),
+])
+def test_attention_kv_matches_fp32(pairs, nq, nkv):
+    """Queries that are the last Lq of Lk key positions (context-parallel
+    chunks): forward, log-sum-exp and the q / kv gradients against fp32."""
+    from psrl_b200.ops.attention import attention_kv, attention_kv_ref
+    from psrl_b200.ops.gemm import check_errors
+    d = 128
+    Tq, Tk = sum(p[0] for p in pairs), sum(p[1] for p in pairs)
+    g = torch.Generator(device="cuda").manual_seed(len(pairs))
+    q = torch.randn(Tq, nq * d, device="cuda", generator=g).bfloat16().requires_grad_(True)
+    kv = torch.randn(Tk, 2 * nkv * d, device="cuda", generator=g).bfloat16().requires_grad_(True)
+    cu_q = torch.tensor([0] + list(torch.tensor([p[0] for p in pairs]).cumsum(0)), dtype=torch.int32, device="cuda")
+    cu_k = torch.tensor([0] + list(torch.tensor([p[1] for p in pairs]).cumsum(0)), dtype=torch.int32, device="cuda")
+    scale = 1.0 / math.sqrt(d)
+    o = attention_kv(q, kv, cu_q, cu_k, max(p[0] for p in pairs), max(p[1] for p in pairs), nq, nkv, d, scale)
+    dout = torch.randn(Tq, nq * d, device="cuda", generator=g).bfloat16()
+    o.backward(dout)
+    torch.cuda.synchronize()
+    check_errors()
+    qf = q.detach().float().requires_grad_(True)
+    kvf = kv.detach().float().requires_grad_(True)
+    ref = attention_kv_ref(qf.view(Tq, nq, d), kvf[:, : nkv * d].reshape(Tk, nkv, d),
+                           kvf[:, nkv * d:].reshape(Tk, nkv, d), cu_q, cu_k, scale).reshape(Tq, nq * d)
+    torch.testing.assert_close(o.float(), ref, atol=2e-2, rtol=2e-2)
+    ref.backward(dout.float())
+    for name, got, want in (("dq", q.grad, qf.grad), ("dkv", kv.grad, kvf.grad)):
+        err = (got.float() - want).abs().max().item()
+        assert err <= 5e-2 * max(1.0, want.abs().max().item()), f"{name}: max abs err {err}"
