@@ -106,6 +106,14 @@ def _sync_summary(res: dict) -> dict | None:
     if not sync or not sync.get("pulls"):
         return None
     out = {"pulls": int(sync["pulls"]), "mean_ms": round(1000.0 * float(sync["pull_s"]) / int(sync["pulls"]), 2)}
+    if sync.get("copies"):
+        # device time of the copy kernel alone, against 770 GB/s (measured peer copy per direction)
+        # and 900 GB/s (NVLink 5 nominal per direction) per receiving GPU
+        copy_ms = 1000.0 * float(sync["copy_s"]) / int(sync["copies"])
+        gb = float(sync.get("bytes", 0)) / 1e9
+        out.update(copy_ms=round(copy_ms, 2), bytes_per_pull=int(sync.get("bytes", 0)),
+                   frac_measured_link=round(gb / 770.0 * 1000.0 / copy_ms, 3) if copy_ms else None,
+                   frac_nominal_link=round(gb / 900.0 * 1000.0 / copy_ms, 3) if copy_ms else None)
     out["path"] = sync.get("path", "NVLink peer loads from the trainers' HBM stores" if "n_train" in res
                            else "in-HBM copy from the local trainer replica")
     return out

@@ -1,0 +1,172 @@
+"""Pipeline parallelism for the trainer: contiguous layer ranges per stage and a
+1F1B micro-batch schedule over point-to-point sends (NCCL p2p on GPUs, gloo
+on CPU).  The reference gets PP / VPP from Megatron's pipeline schedules
+(``psrl/utils/config.py:119-126`` sizes the groups); pipeline send / recv stays
+on NCCL p2p, overlapped with compute by the schedule.
+
+Stage ``s`` of ``n`` owns decoder layers ``[s L / n, (s + 1) L / n)``; the first
+stage also owns the embedding, the last the final norm and the LM head.  The
+activations crossing a stage boundary are the residual stream pair
+``(x, resid)`` of the packed micro-batch ([T, hidden] each); their gradients
+come back the same way.  With tied embeddings the first and last stage both
+hold the embedding matrix and :meth:`PipelineStage.reduce_tied_grads` adds
+their two gradients (Megatron's embedding group).
+
+Schedule per stage (``M`` micro-batches): ``n - s - 1`` warm-up forwards,
+then one forward + one backward per step, then the remaining backwards; a
+forward's send to the next stage and the matching backward's receive from it
+are posted together (``batch_isend_irecv``) so neighbouring stages never wait
+on each other's sends.  At most ``n - s`` micro-batches' activations are alive
+on stage ``s``.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from .. import ops
+
+
+class PipelineStage:
+    def __init__(self, model, group=None):
+        self.model = model
+        self.group = group
+        self.n = dist.get_world_size(group)
+        self.s = dist.get_rank(group)
+        self.ranks = [dist.get_global_rank(group, i) for i in range(self.n)] if group is not None else \
+            list(range(self.n))
+        a = model.args
+        if a.num_layers < self.n:
+            raise ValueError(f"{a.num_layers} layers cannot fill {self.n} pipeline stages")
+        bounds = [round(i * a.num_layers / self.n) for i in range(self.n + 1)]
+        self.lo, self.hi = bounds[self.s], bounds[self.s + 1]
+        self.first, self.last = self.s == 0, self.s == self.n - 1
+        # release what this stage does not run (names of the kept parameters are unchanged)
+        for i in range(a.num_layers):
+            if not self.lo <= i < self.hi:
+                model.layers[i] = nn.Module()
+        if not self.first and not (self.last and a.tie_word_embeddings):
+            model.embed = None
+        if not self.last:
+            model.norm = None
+            if hasattr(model, "lm_head"):
+                model.lm_head = None
+        self.dtype = next(p for p in model.parameters()).dtype
+        self.device = next(p for p in model.parameters()).device
+        # first + last stage group for the tied embedding (created on every rank: new_group is collective)
+        self._tie_group = None
+        if a.tie_word_embeddings and self.n > 1:
+            self._tie_group = dist.new_group([self.ranks[0], self.ranks[-1]])
+
+    def parameters(self):
+        return [p for p in self.model.parameters()]
+
+    # ------------------------------------------------------------------ p2p
+    def _p2p(self, send_next=None, send_prev=None, recv_next=None, recv_prev=None):
+        """Post the given sends / receives together and wait for them.
+        recv_* are the number of rows T of a [T, hidden] (x, resid) pair."""
+        h = self.model.args.hidden_size
+        ops_, got_next, got_prev = [], None, None
+        if recv_prev is not None:
+            got_prev = [torch.empty(recv_prev, h, dtype=self.dtype, device=self.device) for _ in range(2)]
+            ops_ += [dist.P2POp(dist.irecv, t, self.ranks[self.s - 1], self.group) for t in got_prev]
+        if send_next is not None:
+            ops_ += [dist.P2POp(dist.isend, t.contiguous(), self.ranks[self.s + 1], self.group) for t in send_next]
+        if recv_next is not None:
+            got_next = [torch.empty(recv_next, h, dtype=self.dtype, device=self.device) for _ in range(2)]
+            ops_ += [dist.P2POp(dist.irecv, t, self.ranks[self.s + 1], self.group) for t in got_next]
+        if send_prev is not None:
+            ops_ += [dist.P2POp(dist.isend, t.contiguous(), self.ranks[self.s - 1], self.group) for t in send_prev]
+        if ops_:
+            for w in dist.batch_isend_irecv(ops_):
+                w.wait()
+        return got_next, got_prev
+
+    # -------------------------------------------------------------- compute
+    def _forward(self, mb, inputs):
+        """Run this stage on micro-batch ``mb``.  Returns (outputs, loss):
+        outputs = (x, resid) for a non-last stage, loss for the last."""
+        m, a = self.model, self.model.args
+        if self.first:
+            x = m.embed(mb["ids"])
+            if a.embed_scale:
+                x = x * torch.tensor(a.embed_scale, dtype=x.dtype)
+            resid = None
+        else:
+            x, resid = inputs
+        for i in range(self.lo, self.hi):
+            x, resid = m.layers[i](x, resid, mb["pos"], mb["cu"], mb["max"])
+        if not self.last:
+            return (x, resid), None
+        h, _ = ops.rms_norm(x, m.norm, a.rms_eps, residual=resid)
+        lp, ent = ops.linear_logprob(h, m.lm_head_weight(), mb["labels"], mb.get("temperature", 1.0))
+        return None, self.loss_fn(lp, ent, mb)
+
+    def train_step(self, micro_batches: list[dict], loss_fn) -> list[float]:
+        """Forward + backward of every micro-batch (gradients accumulate in
+        ``.grad``).  Each micro-batch dict holds ``ids``, ``pos``, ``cu``,
+        ``max`` and ``labels`` (the same on every stage); ``loss_fn(logprobs,
+        entropy, mb)`` gives the scalar loss on the last stage.  Returns the
+        last stage's losses (empty elsewhere)."""
+        self.loss_fn = loss_fn
+        M = len(micro_batches)
+        warm = min(self.n - self.s - 1, M)
+        saved: dict[int, tuple] = {}
+        losses: list[float] = []
+        T = [int(mb["ids"].shape[0]) for mb in micro_batches]
+
+        def run_fwd(k, inputs):
+            if inputs is not None:
+                inputs = [t.requires_grad_(True) for t in inputs]
+            out, loss = self._forward(micro_batches[k], inputs)
+            saved[k] = (inputs, out, loss)
+            if loss is not None:
+                losses.append(float(loss.detach()))
+            return out
+
+        def run_bwd(k, grads):
+            inputs, out, loss = saved.pop(k)
+            if self.last:
+                loss.backward()
+            else:
+                torch.autograd.backward([t for t in out], [g for g in grads])
+            return [t.grad for t in inputs] if inputs is not None else None
+
+        # warm-up forwards
+        for k in range(warm):
+            _, prev = self._p2p(recv_prev=None if self.first else T[k])
+            out = run_fwd(k, prev)
+            self._p2p(send_next=out)
+        # steady state: forward k + warm, backward k
+        for k in range(M - warm):
+            f = k + warm
+            _, prev = self._p2p(recv_prev=None if self.first else T[f])
+            out = run_fwd(f, prev)
+            if self.last:
+                gin = run_bwd(k, None)
+            else:
+                nxt, _ = self._p2p(send_next=out, recv_next=T[k])
+                gin = run_bwd(k, nxt)
+            if not self.first:
+                self._p2p(send_prev=gin)
+        # cool-down backwards
+        for k in range(M - warm, M):
+            nxt, _ = self._p2p(recv_next=T[k])
+            gin = run_bwd(k, nxt)
+            if not self.first:
+                self._p2p(send_prev=gin)
+        return losses
+
+    def reduce_tied_grads(self) -> None:
+        """Tied embeddings: first and last stage add their gradients of the
+        shared matrix (a two-rank all-reduce; every stage calls this)."""
+        if self._tie_group is None:
+            return
+        if self.first or self.last:
+            g = self.model.embed.weight.grad
+            if g is None:
+                g = torch.zeros_like(self.model.embed.weight)
+                self.model.embed.weight.grad = g
+            dist.all_reduce(g, group=self._tie_group)

@@ -51,7 +51,7 @@ class ControlPlane:
         self.phase = 0
         self.last_seen: dict = {}
         self.failed: dict = {}
-        self.sync_stats = {"pulls": 0, "pull_s": 0.0}
+        self.sync_stats = {"pulls": 0, "pull_s": 0.0, "copies": 0, "copy_s": 0.0, "bytes": 0}
         self.exchange_stats = {"calls": 0, "outputs": 0, "requests": 0}
         self.stores: dict[int, dict] = {}
         self.layout = None
@@ -209,9 +209,16 @@ class ControlPlane:
         return out
 
     def report_pull(self, seconds: float, instance_id=None, from_version: int = -1, to_version: int = -1,
-                    interrupted: int = 0) -> None:
+                    interrupted: int = 0, copy_seconds: float | None = None, nbytes: int = 0) -> None:
+        """One weight pull of a rollout instance: wall time (lock, version RPC,
+        copy, engine swap) and, when known, the device time of the copy kernel
+        and the bytes it moved."""
         self.sync_stats["pulls"] += 1
         self.sync_stats["pull_s"] += float(seconds)
+        if copy_seconds is not None:
+            self.sync_stats["copies"] += 1
+            self.sync_stats["copy_s"] += float(copy_seconds)
+            self.sync_stats["bytes"] = int(nbytes)
         if instance_id is not None:
             from ..rollout.coordinator import SyncRecord
             self.coord.history.append(SyncRecord(tuple(instance_id), int(from_version), int(to_version),

@@ -279,18 +279,25 @@ class DisaggregatedRun:
         t0 = time.perf_counter()
         if not self.cp.acquire_pull():
             raise TimeoutError("shared pull lock")
+        copy_s = None
         try:
             v = self.cp.pull_model(self.instance_id)
-            self.puller.pull()
             if self.device.type == "cuda":
-                torch.cuda.current_stream().synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                nbytes = self.puller.pull()
+                e1.record()
+                e1.synchronize()
+                copy_s = e0.elapsed_time(e1) / 1e3      # device time of the peer-load kernel
+            else:
+                nbytes = self.puller.pull()
         finally:
             self.cp.release_pull()
         from_v = self.engine.version
         in_flight = self.engine.num_unfinished()
         self.engine.load_weights(None, v)
         self.cp.report_pull(time.perf_counter() - t0, self.instance_id, from_v, v,
-                            0 if self.engine.keep_kv_on_update else in_flight)
+                            0 if self.engine.keep_kv_on_update else in_flight, copy_s, int(nbytes))
 
     def _coordinated_pull(self) -> None:
         """Pull granted by the control plane's coordinator; a failure quarantines

@@ -1,0 +1,83 @@
+"""Pipeline parallelism (1F1B over gloo, 2 and 3 stages) against the unsplit
+decoder: every stage's parameter gradients after a multi-micro-batch step
+equal the single-rank gradients of the same parameters, and the last stage's
+losses equal the single-rank losses."""
+
+import os
+import socket
+from dataclasses import replace
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _loss(lp, ent, mb):
+    return -(lp * mb["w"]).sum() / mb["w"].numel()
+
+
+def _batches(a, seed=9):
+    from psrl_b200.models import packed_positions
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for lens in ([7, 12], [20], [3, 5, 9], [16, 4], [11]):
+        T = sum(lens)
+        pos, cu, mx = packed_positions(lens, "cpu")
+        out.append({"ids": torch.randint(0, a.vocab_size, (T,), generator=g), "pos": pos, "cu": cu, "max": mx,
+                    "labels": torch.randint(0, a.vocab_size, (T,), generator=g), "w": torch.randn(T, generator=g)})
+    return out
+
+
+def _worker(rank, world, port, tied, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    import torch.distributed as dist
+    torch.set_num_threads(1)
+    from psrl_b200.models import PRESETS, build_model
+    from psrl_b200.parallel.pp import PipelineStage
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    a = replace(PRESETS["tiny"], num_layers=4, tie_word_embeddings=tied)
+    mbs = _batches(a)
+    ref = build_model(a, "cpu", torch.float32, seed=2)
+    ref_losses = []
+    for mb in mbs:
+        lp, ent = ref.logprobs(mb["ids"], mb["pos"], mb["cu"], mb["max"], mb["labels"])
+        loss = _loss(lp, ent, mb)
+        loss.backward()
+        ref_losses.append(float(loss))
+    ref_grads = {n: p.grad for n, p in ref.named_parameters()}
+    stage = PipelineStage(build_model(a, "cpu", torch.float32, seed=2), dist.group.WORLD)
+    losses = stage.train_step(mbs, _loss)
+    stage.reduce_tied_grads()
+    worst, n_params = 0.0, 0
+    for n, p in stage.model.named_parameters():
+        n_params += 1
+        worst = max(worst, float((p.grad - ref_grads[n]).abs().max() / (ref_grads[n].abs().max() + 1e-12)))
+    loss_err = max((abs(x - y) for x, y in zip(losses, ref_losses)), default=0.0) if stage.last else 0.0
+    q.put({"rank": rank, "grad": worst, "params": n_params, "losses": len(losses), "loss_err": loss_err,
+           "layers": (stage.lo, stage.hi)})
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,tied", [(2, True), (3, False), (3, True)])
+def test_pipeline_matches_single_rank(world, tied):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, tied, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted((q.get(timeout=600) for _ in range(world)), key=lambda r: r["rank"])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    covered = sorted(r["layers"] for r in res)
+    assert covered[0][0] == 0 and covered[-1][1] == 4
+    for r in res:
+        assert r["grad"] < 1e-5, r
+    assert res[-1]["losses"] == 5 and res[-1]["loss_err"] < 1e-5
