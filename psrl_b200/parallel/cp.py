@@ -150,3 +150,46 @@ def gather_tokens(x: torch.Tensor, plan: CPPlan) -> torch.Tensor:
     out = torch.empty((world * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
     dist.all_gather_into_tensor(out, x.contiguous(), group=plan.group)
     return out[plan.perm]
+
+
+class CPShard:
+    """One packed micro-batch padded to CP-divisible sequence lengths and cut
+    to this rank's zigzag share.  ``local(t, pad)`` cuts any per-token tensor
+    of the micro-batch the same way (``pad`` fills the padding rows);
+    ``full(x)`` gathers per-token results of every rank back into the
+    micro-batch's original token order (padding dropped)."""
+
+    def __init__(self, cu_seqlens: torch.Tensor, group):
+        world = dist.get_world_size(group)
+        cu = [int(v) for v in cu_seqlens.tolist()]
+        lens = [cu[j + 1] - cu[j] for j in range(len(cu) - 1)]
+        padded = pad_lengths(lens, world)
+        dev = cu_seqlens.device
+        src, pad_pos, real = [], [], []
+        o = 0
+        for j, (n, m) in enumerate(zip(lens, padded)):
+            src.extend(range(cu[j], cu[j] + n))
+            src.extend([-1] * (m - n))
+            pad_pos.extend(range(m))
+            real.extend(range(o, o + n))
+            o += m
+        self.src = torch.tensor(src, dtype=torch.int64, device=dev)          # padded row -> source row (-1: pad)
+        self.pos = torch.tensor(pad_pos, dtype=torch.int32, device=dev)      # position within the sequence
+        self.real = torch.tensor(real, dtype=torch.int64, device=dev)        # padded rows holding real tokens
+        self.plan = make_plan(padded, group, dev)
+        self._li = self.plan.local_idx
+        self._lsrc = self.src[self._li]
+        self._lpad = self._lsrc < 0
+
+    def local(self, t: torch.Tensor, pad=0) -> torch.Tensor:
+        x = t[self._lsrc.clamp(min=0)]
+        if bool(self._lpad.any()):
+            x = x.clone()
+            x[self._lpad] = pad
+        return x
+
+    def positions(self) -> torch.Tensor:
+        return self.pos[self._li]
+
+    def full(self, x: torch.Tensor) -> torch.Tensor:
+        return gather_tokens(x, self.plan)[self.real]

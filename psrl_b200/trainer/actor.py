@@ -19,6 +19,7 @@ import time
 
 import torch
 
+from ..parallel.cp import CPShard
 from ..models import ModelArgs, build_model
 from ..parallel.fsdp import FlatShardedDP
 from . import algos
@@ -68,7 +69,7 @@ def plan_update(trajs: list[Trajectory], mini_batch_size: int, dp_world: int) ->
 
 class PolicyWorker:
     def __init__(self, cfg, args: ModelArgs, device, dp_group=None, seed: int = 0, trainable: bool = True,
-                 dp_rank: int = 0, dp_world: int = 1, tp_group=None):
+                 dp_rank: int = 0, dp_world: int = 1, tp_group=None, cp_group=None):
         self.cfg = cfg
         self.args = args
         self.device = torch.device(device)
@@ -81,6 +82,18 @@ class PolicyWorker:
         self.ep = None
         expert_names: set = set()
         self.tp = None
+        # context parallelism: the ranks of cp_group share each micro-batch along
+        # the sequence (dp_rank / dp_world index the CP groups; dp_group spans
+        # every rank, so gradients sum over data and context parallelism)
+        self.cp_group = cp_group if cp_group is not None and dist_world(cp_group) > 1 else None
+        if self.cp_group is not None:
+            if tp_group is not None and dist_world(tp_group) > 1:
+                raise ValueError("context parallelism together with tensor parallelism is not implemented")
+            modes = {cfg.actor.loss_agg_mode} | ({cfg.critic.get("loss_agg_mode", "token-mean")}
+                                                  if args.value_head else set())
+            if not modes <= {"token-mean", "seq-mean-token-sum"}:
+                raise ValueError("context parallelism needs a loss that is a sum over tokens "
+                                 "(loss_agg_mode token-mean or seq-mean-token-sum)")
         if tp_group is not None and dist_world(tp_group) > 1:
             # tensor parallelism inside tp_group (data parallelism across dp_group)
             from ..parallel.tp import apply_tensor_parallel, make_tp_group
@@ -163,6 +176,26 @@ class PolicyWorker:
             local = local.cpu()
         return [(mine, max(1.0, float(n)), ns) for (mine, _, ns), n in zip(plan, local.tolist())]
 
+    def _cp_shard(self, mb):
+        """Under context parallelism, replace ``mb``'s per-token tensors in place
+        by this rank's share (``cu_seqlens`` becomes the :class:`CPPlan`) and
+        return the function that cuts other per-token tensors the same way;
+        otherwise leave ``mb`` alone and return the identity."""
+        if self.cp_group is None:
+            return lambda t: t
+        sh = CPShard(mb.cu_seqlens, self.cp_group)
+        mb.input_ids = sh.local(mb.input_ids)
+        mb.labels = sh.local(mb.labels)
+        mb.loss_mask = sh.local(mb.loss_mask, 0.0)
+        mb.old_logprobs = sh.local(mb.old_logprobs, 0.0)
+        mb.advantages = sh.local(mb.advantages, 0.0)
+        mb.seq_ids = sh.local(mb.seq_ids)
+        if "is_weights" in mb.extra:
+            mb.extra["is_weights"] = sh.local(mb.extra["is_weights"], 1.0)
+        mb.positions = sh.positions()
+        mb.cu_seqlens, mb.max_seqlen = sh.plan, sh.plan.max_q
+        return sh.local
+
     def _placeholder(self):
         t = Trajectory(uid=-1, request_id=-1, prompt_ids=[0], response_ids=[0], rollout_logprobs=[0.0],
                        response_mask=[0])
@@ -179,8 +212,14 @@ class PolicyWorker:
                 self.model.logprobs(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen, mb.labels, temperature)
                 continue
             mb = build_micro_batch(trajs, bin_, self.device)
-            lp, _ = self.model.logprobs(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen, mb.labels,
-                                        temperature)
+            if self.cp_group is not None:
+                sh = CPShard(mb.cu_seqlens, self.cp_group)
+                lp, _ = self.model.logprobs(sh.local(mb.input_ids), sh.positions(), sh.plan, sh.plan.max_q,
+                                            sh.local(mb.labels), temperature)
+                lp = sh.full(lp.float())
+            else:
+                lp, _ = self.model.logprobs(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen, mb.labels,
+                                            temperature)
             lp = lp.float().cpu()
             for i, sl in response_slices(mb, trajs):
                 setattr(trajs[i], field, lp[sl].tolist())
@@ -193,7 +232,12 @@ class PolicyWorker:
                 self.model.values(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen)
                 continue
             mb = build_micro_batch(trajs, bin_, self.device)
-            v = self.model.values(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen).float().cpu()
+            if self.cp_group is not None:
+                sh = CPShard(mb.cu_seqlens, self.cp_group)
+                v = sh.full(self.model.values(sh.local(mb.input_ids), sh.positions(), sh.plan,
+                                              sh.plan.max_q).float()).cpu()
+            else:
+                v = self.model.values(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen).float().cpu()
             for i, sl in response_slices(mb, trajs):
                 trajs[i].old_values = v[sl].tolist()
 
@@ -231,11 +275,12 @@ class PolicyWorker:
                         ((lp * 0).sum() + (ent * 0).sum()).backward()
                         continue
                     mb = build_micro_batch(trajs, bin_, self.device)
+                    shard = self._cp_shard(mb)
                     lp, ent = self.model.logprobs(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen,
                                                   mb.labels, temperature)
                     tis = mb.extra.get("is_weights")
                     if use_tis:
-                        rl = build_micro_batch(trajs, bin_, self.device, field_old="rollout_logprobs").old_logprobs
+                        rl = shard(build_micro_batch(trajs, bin_, self.device, field_old="rollout_logprobs").old_logprobs)
                         w = algos.truncated_is_weight(mb.old_logprobs, rl, float(self.cfg.algorithm.rollout_correction.tis_cap))
                         tis = w if tis is None else tis * w
                     agg = dict(seq_ids=mb.seq_ids, num_seqs=num_seqs, global_tokens=global_tokens)
@@ -247,7 +292,7 @@ class PolicyWorker:
                         ent_loss = algos.agg_loss(ent, mb.loss_mask, ac.loss_agg_mode, **agg)
                         loss = loss - float(ac.entropy_coeff) * ent_loss
                     if ac.use_kl_loss:
-                        ref = build_micro_batch(trajs, bin_, self.device, field_old="ref_logprobs").old_logprobs
+                        ref = shard(build_micro_batch(trajs, bin_, self.device, field_old="ref_logprobs").old_logprobs)
                         kl = algos.kl_penalty(lp, ref, ac.kl_loss_type)
                         loss = loss + float(ac.kl_loss_coef) * algos.agg_loss(kl, mb.loss_mask, ac.loss_agg_mode, **agg)
                     loss.backward()
@@ -289,12 +334,15 @@ class PolicyWorker:
                     (self.model.values(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen) * 0).sum().backward()
                     continue
                 mb = build_micro_batch(trajs, bin_, self.device)
-                v = self.model.values(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen)
-                old_v = torch.zeros_like(v)
-                ret = torch.zeros_like(v)
+                old_v = torch.zeros(mb.num_tokens, dtype=torch.float32, device=self.device)
+                ret = torch.zeros_like(old_v)
                 for j, (i, sl) in enumerate(response_slices(mb, trajs)):
-                    old_v[sl] = torch.tensor(trajs[i].old_values, device=v.device)
-                    ret[sl] = torch.tensor(trajs[i].returns, device=v.device)
+                    old_v[sl] = torch.tensor(trajs[i].old_values, device=old_v.device)
+                    ret[sl] = torch.tensor(trajs[i].returns, device=old_v.device)
+                shard = self._cp_shard(mb)
+                old_v, ret = shard(old_v), shard(ret)
+                v = self.model.values(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen)
+                old_v, ret = old_v.to(v.dtype), ret.to(v.dtype)
                 loss, m = algos.value_loss(v, old_v, ret, mb.loss_mask, float(cc.cliprange_value),
                                            global_tokens=global_tokens)
                 loss.backward()

@@ -71,16 +71,29 @@ class DisaggregatedRun:
         # trainer layout: tensor-parallel groups of `tp` consecutive trainer ranks,
         # data parallelism across them
         tp = int(cfg.actor.get("tensor_parallel_size", 1) or 1)
-        if self.n_train % tp:
-            raise ValueError(f"{self.n_train} trainer ranks are not a multiple of tensor_parallel_size={tp}")
-        self.tp_size = tp
-        self.dp_rank, self.dp_world = self.rank // tp, self.n_train // tp
+        cpn = int(cfg.actor.get("context_parallel_size", 1) or 1)
+        if tp > 1 and cpn > 1:
+            raise ValueError("tensor_parallel_size and context_parallel_size cannot both exceed 1")
+        if self.n_train % (tp * cpn):
+            raise ValueError(f"{self.n_train} trainer ranks are not a multiple of tensor_parallel_size={tp} x "
+                             f"context_parallel_size={cpn}")
+        # ranks that share one micro-batch share (a TP or a CP group) get the same data
+        self.tp_size = tp * cpn
+        self.dp_rank, self.dp_world = self.rank // self.tp_size, self.n_train // self.tp_size
         self.tp_group = None
+        self.cp_group = None
         if self.is_trainer and self.n_train > 1:
             # created by the trainer ranks only (group-local synchronisation)
             self.train_cpu_group = pdist.new_subgroup(trainer_ranks, backend="gloo")
             if tp == 1:
+                # data (and context) parallel gradients sum over every trainer rank
                 self.train_group = pdist.new_subgroup(trainer_ranks, backend=backend)
+                if cpn > 1:
+                    for k in range(self.n_train // cpn):
+                        g = pdist.new_subgroup(list(range(k * cpn, (k + 1) * cpn)), backend=backend) \
+                            if k == self.rank // cpn else None
+                        if g is not None:
+                            self.cp_group = g
             else:
                 for k in range(self.dp_world):
                     g = pdist.new_subgroup(list(range(k * tp, (k + 1) * tp)), backend=backend) \
@@ -118,7 +131,7 @@ class DisaggregatedRun:
         cfg = self.cfg
         self.actor = PolicyWorker(cfg, self.args, self.device, dp_group=self.train_group,
                                   seed=int(cfg.trainer.seed), dp_rank=self.dp_rank, dp_world=self.dp_world,
-                                  tp_group=self.tp_group)
+                                  tp_group=self.tp_group, cp_group=self.cp_group)
         self.assembler = None
         if self.actor.ep is not None or self.actor.tp is not None:
             # sharded trainer: every trainer rank publishes the full model, assembled
@@ -153,13 +166,13 @@ class DisaggregatedRun:
             cargs = _replace(self.args, value_head=True, tie_word_embeddings=False)
             self.critic = PolicyWorker(cfg, cargs, self.device, dp_group=self.train_group,
                                        seed=int(cfg.trainer.seed) + 1, dp_rank=self.dp_rank, dp_world=self.dp_world,
-                                       tp_group=self.tp_group)
+                                       tp_group=self.tp_group, cp_group=self.cp_group)
         self.ref = None
         if cfg.actor.use_kl_loss or cfg.algorithm.use_kl_in_reward:
             # sharded like the actor (expert / tensor parallel forwards are collectives)
             self.ref = PolicyWorker(cfg, self.args, self.device, dp_group=self.train_group,
                                     seed=int(cfg.trainer.seed), trainable=False, dp_rank=self.dp_rank,
-                                    dp_world=self.dp_world, tp_group=self.tp_group)
+                                    dp_world=self.dp_world, tp_group=self.tp_group, cp_group=self.cp_group)
         self.kl_ctrl = algos.kl_controller(cfg.algorithm) if cfg.algorithm.use_kl_in_reward else None
         self.sharded_overlap = sharded_overlap_enabled(cfg)
         self.pre_step = sharded_overlap_mode(cfg) == "pre_step"

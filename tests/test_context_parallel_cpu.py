@@ -93,3 +93,60 @@ def test_attention_kv_ref_equals_causal_suffix():
     part = attention_kv_ref(q[12:], k, v, torch.tensor([0, 8], dtype=torch.int32),
                             torch.tensor([0, L], dtype=torch.int32), 0.25)
     torch.testing.assert_close(part, full[12:])
+
+
+def _worker_policy(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+    torch.set_num_threads(1)
+    from psrl_b200.config import load_config
+    from psrl_b200.models import PRESETS
+    from psrl_b200.parallel.dist import init_distributed
+    from psrl_b200.trainer.actor import PolicyWorker
+    from psrl_b200.trainer.batch import Trajectory
+    init_distributed("cpu", timeout_s=300)
+    a = PRESETS["tiny"]
+    # a large Adam eps makes the update linear in the gradient, so the check sees
+    # gradient differences instead of the sign of near-zero gradients
+    cfg = load_config(preset="cpu_tiny_grpo", overrides=["actor.optim.lr=1.0", "actor.optim.eps=1.0",
+                                                         "actor.ppo_mini_batch_size=4"])
+    g = torch.Generator().manual_seed(4)
+    trajs = []
+    for i, (P, R) in enumerate(((5, 9), (3, 14), (7, 4), (2, 11))):
+        trajs.append(Trajectory(uid=i, request_id=i, prompt_ids=torch.randint(0, a.vocab_size, (P,), generator=g).tolist(),
+                                response_ids=torch.randint(0, a.vocab_size, (R,), generator=g).tolist(),
+                                rollout_logprobs=(-torch.rand(R, generator=g)).tolist()))
+        trajs[-1].advantage = float(torch.randn(1, generator=g))
+    ref = PolicyWorker(cfg, a, "cpu", seed=3)                                       # one rank, whole sequences
+    cpw = PolicyWorker(cfg, a, "cpu", seed=3, dp_group=dist.group.WORLD, cp_group=dist.group.WORLD)
+    import copy
+    t_ref, t_cp = copy.deepcopy(trajs), copy.deepcopy(trajs)
+    ref.compute_log_prob(t_ref, list(range(4)))
+    cpw.compute_log_prob(t_cp, list(range(4)))
+    lp_err = max(abs(x - y) for a_, b_ in zip(t_ref, t_cp) for x, y in zip(a_.old_logprobs, b_.old_logprobs))
+    ref.update_policy(t_ref)
+    cpw.update_policy(t_cp)
+    pr, pc = dict(ref.model.named_parameters()), dict(cpw.model.named_parameters())
+    upd = max(float((pr[n] - pc[n]).detach().abs().max()) for n in pr)
+    q.put({"rank": rank, "lp": lp_err, "param": upd})
+    dist.destroy_process_group()
+
+
+def test_policy_worker_context_parallel_step_matches_single_rank():
+    """PolicyWorker with CP=2: old log-probs and the parameters after one PPO
+    step equal those of the single-rank worker on the same trajectories."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_policy, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in res:
+        assert r["lp"] < 1e-4, r
+        assert r["param"] < 1e-5, r
