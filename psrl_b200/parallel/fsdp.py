@@ -75,14 +75,18 @@ class _Bucket:
 class FlatShardedDP:
     def __init__(self, model: torch.nn.Module, group=None, *, lr: float = 1e-6, betas=(0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 0.0, max_grad_norm: float = 1.0, warmup_steps: int = 0,
-                 bucket_mode: str = "layer", param_filter=None, norm_group=None):
+                 bucket_mode: str = "layer", param_filter=None, norm_group=None, count_in_norm: bool = True):
         """``param_filter(name) -> bool`` selects the parameters this instance
         owns (default: all trainable ones).  ``norm_group``: ranks whose
         parameters are disjoint from this rank's (expert parallelism), summed
-        into the squared gradient norm in addition to ``group``'s shards."""
+        into the squared gradient norm in addition to ``group``'s shards.
+        ``count_in_norm=False``: the parameters are a copy of ones another rank
+        already counts (a tied embedding on the last pipeline stage): they are
+        reduced and updated but add nothing to the clip norm."""
         self.model = model
         self.group = group
         self.norm_group = norm_group
+        self.count_in_norm = bool(count_in_norm)
         # no group = this rank trains alone (even inside a larger job)
         self.world = dist.get_world_size(group) if (group is not None and dist.is_initialized()) else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
@@ -198,6 +202,8 @@ class FlatShardedDP:
             dist.all_reduce(self.norm.sq, group=self.group)
         if self.norm_group is not None:
             dist.all_reduce(self.norm.sq, group=self.norm_group)
+        if not self.count_in_norm:
+            return torch.zeros_like(self.norm.sq)
         return self.norm.sq.clone()
 
     @torch.no_grad()

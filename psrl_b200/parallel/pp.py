@@ -101,6 +101,8 @@ class PipelineStage:
         if not self.last:
             return (x, resid), None
         h, _ = ops.rms_norm(x, m.norm, a.rms_eps, residual=resid)
+        if a.value_head:
+            return None, self.loss_fn(m.value(h).float().squeeze(-1), None, mb)
         lp, ent = ops.linear_logprob(h, m.lm_head_weight(), mb["labels"], mb.get("temperature", 1.0))
         return None, self.loss_fn(lp, ent, mb)
 
@@ -159,14 +161,47 @@ class PipelineStage:
                 self._p2p(send_prev=gin)
         return losses
 
-    def reduce_tied_grads(self) -> None:
+    @torch.no_grad()
+    def forward_only(self, micro_batches: list[dict]) -> list[torch.Tensor]:
+        """Per-token outputs of every micro-batch (log-probs, or values for a
+        value head), computed on the last stage and broadcast to every stage."""
+        outs: list[torch.Tensor] = []
+        self.loss_fn = lambda y, ent, mb: y
+        for mb in micro_batches:
+            T = int(mb["ids"].shape[0])
+            _, prev = self._p2p(recv_prev=None if self.first else T)
+            out, y = self._forward(mb, prev)
+            if not self.last:
+                self._p2p(send_next=out)
+                y = torch.empty(T, dtype=torch.float32, device=self.device)
+            y = y.float().contiguous()
+            dist.broadcast(y, self.ranks[-1], group=self.group)
+            outs.append(y)
+        return outs
+
+    def broadcast_metrics(self, metrics: dict) -> dict:
+        """The last stage's loss metrics on every stage (the other stages see no loss)."""
+        box = [metrics]
+        dist.broadcast_object_list(box, src=self.ranks[-1], group=self.group)
+        out = dict(box[0])
+        for k, v in metrics.items():
+            if k not in out:
+                out[k] = v
+        return out
+
+    def reduce_tied_grads(self, grad_of=None) -> None:
         """Tied embeddings: first and last stage add their gradients of the
-        shared matrix (a two-rank all-reduce; every stage calls this)."""
+        shared matrix (a two-rank all-reduce; every stage calls this).
+        ``grad_of(param)`` returns the tensor holding a parameter's accumulated
+        gradient when that is not ``param.grad`` (an optimizer's main-grad
+        buffer)."""
         if self._tie_group is None:
             return
         if self.first or self.last:
-            g = self.model.embed.weight.grad
+            w = self.model.embed.weight
+            g = grad_of(w) if grad_of is not None else None
             if g is None:
-                g = torch.zeros_like(self.model.embed.weight)
-                self.model.embed.weight.grad = g
+                if w.grad is None:
+                    w.grad = torch.zeros_like(w)
+                g = w.grad
             dist.all_reduce(g, group=self._tie_group)

@@ -128,3 +128,64 @@ class WeightPuller:
                 a, b = lo // esz, (lo + n) // esz
                 self.dst[a:b].copy_(self.srcs[j][a:b])
         return self.layout.nbytes
+
+
+class ShardedWeightPuller:
+    """Rollout-side pull from trainers whose stores hold different parameter
+    sets (pipeline stages: each stage publishes only its layers).  Every
+    tensor of the engine's full layout is copied from a store that holds it
+    (round-robin over the data-parallel replicas of its stage, so the load
+    spreads over their NVLink links), straight into its place in the engine's
+    flat buffer: the store layout is transformed into the engine layout by the
+    copy itself, with no assembly on the trainers.  Runs of tensors that are
+    contiguous on both sides merge into one segment; the segments go through
+    ``copy_segments`` 16 per launch."""
+
+    MAX_SEG = 16
+
+    def __init__(self, layout: WeightLayout, descriptors: list[dict], dst_flat: torch.Tensor):
+        self.layout = layout
+        self.dst = dst_flat
+        self.srcs = [open_store(d) for d in descriptors]
+        self.gpu = dst_flat.is_cuda
+        if self.gpu:
+            me = dst_flat.device.index
+            for d in descriptors:
+                if d["kind"] == "ipc" and int(d["device"]) != me:
+                    ops.ext().enable_peer_access(int(d["device"]))
+        esz = torch.finfo(layout.dtype).bits // 8
+        owners: dict[str, list] = {}
+        for j, d in enumerate(descriptors):
+            for name, shape, off in d["entries"]:
+                owners.setdefault(name, []).append((j, int(off)))
+        segs, turn = [], {}
+        for name, shape, off in layout.entries:
+            if name not in owners:
+                raise KeyError(f"no trainer store holds {name}")
+            cands = owners[name]
+            k = turn.get(len(cands), 0)
+            turn[len(cands)] = k + 1
+            j, src = cands[k % len(cands)]
+            n = 1
+            for s in shape:
+                n *= s
+            seg = [j, src * esz, int(off) * esz, n * esz]
+            last = segs[-1] if segs else None
+            if last and last[0] == j and last[1] + last[3] == seg[1] and last[2] + last[3] == seg[2]:
+                last[3] += seg[3]
+            else:
+                segs.append(seg)
+        self.segments = [tuple(s) for s in segs]       # (store, src byte, dst byte, bytes)
+
+    @torch.no_grad()
+    def pull(self) -> int:
+        if self.gpu:
+            for i in range(0, len(self.segments), self.MAX_SEG):
+                part = self.segments[i:i + self.MAX_SEG]
+                ops.ext().copy_segments(self.dst, [self.srcs[j] for j, _, _, _ in part], [d for _, _, d, _ in part],
+                                        [s for _, s, _, _ in part], [n for _, _, _, n in part])
+        else:
+            esz = self.dst.element_size()
+            for j, s, d, n in self.segments:
+                self.dst[d // esz:(d + n) // esz].copy_(self.srcs[j][s // esz:(s + n) // esz])
+        return sum(n for _, _, _, n in self.segments)

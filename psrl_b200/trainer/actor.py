@@ -69,7 +69,7 @@ def plan_update(trajs: list[Trajectory], mini_batch_size: int, dp_world: int) ->
 
 class PolicyWorker:
     def __init__(self, cfg, args: ModelArgs, device, dp_group=None, seed: int = 0, trainable: bool = True,
-                 dp_rank: int = 0, dp_world: int = 1, tp_group=None, cp_group=None):
+                 dp_rank: int = 0, dp_world: int = 1, tp_group=None, cp_group=None, pp_group=None):
         self.cfg = cfg
         self.args = args
         self.device = torch.device(device)
@@ -86,6 +86,14 @@ class PolicyWorker:
         # the sequence (dp_rank / dp_world index the CP groups; dp_group spans
         # every rank, so gradients sum over data and context parallelism)
         self.cp_group = cp_group if cp_group is not None and dist_world(cp_group) > 1 else None
+        # pipeline parallelism: this rank runs one stage of the layers (dp_group
+        # then joins the same stage of every pipeline; the clip norm spans the stages)
+        self.pp = None
+        if pp_group is not None and dist_world(pp_group) > 1:
+            if (tp_group is not None and dist_world(tp_group) > 1) or self.cp_group is not None or args.is_moe:
+                raise ValueError("pipeline parallelism here combines with data parallelism only")
+            from ..parallel.pp import PipelineStage
+            self.pp = PipelineStage(self.model, pp_group)
         if self.cp_group is not None:
             if tp_group is not None and dist_world(tp_group) > 1:
                 raise ValueError("context parallelism together with tensor parallelism is not implemented")
@@ -126,13 +134,23 @@ class PolicyWorker:
                 self.dp = FlatShardedDP(self.model, dp_group, param_filter=lambda n: n not in sh, **kw)
                 self.dp_partner = FlatShardedDP(self.model, dp_group, param_filter=lambda n: n in sh,
                                                 norm_group=tp_group, **kw)
+            elif self.pp is not None:
+                if self.pp.last and not self.pp.first and args.tie_word_embeddings:
+                    # the tied embedding's other copy lives on the first stage, which counts it
+                    # in the clip norm; this copy is reduced and updated the same way
+                    self.dp = FlatShardedDP(self.model, dp_group, norm_group=pp_group,
+                                            param_filter=lambda n: n != "embed.weight", **kw)
+                    self.dp_partner = FlatShardedDP(self.model, dp_group, count_in_norm=False,
+                                                    param_filter=lambda n: n == "embed.weight", **kw)
+                else:
+                    self.dp = FlatShardedDP(self.model, dp_group, norm_group=pp_group, **kw)
             else:
                 self.dp = FlatShardedDP(self.model, dp_group, param_filter=lambda n: n not in expert_names, **kw)
             if self.tp is None and expert_names:
                 # each rank's experts are its own: no reduction, but the clip norm spans all ranks
                 self.dp_partner = FlatShardedDP(self.model, None, param_filter=lambda n: n in expert_names,
                                                 norm_group=dp_group, **kw)
-            elif self.tp is None and bool(cfg.actor.get("fsdp_peer_step", True)):
+            elif self.tp is None and self.pp is None and bool(cfg.actor.get("fsdp_peer_step", True)):
                 # fused peer-memory reduce-scatter + AdamW + all-gather (CUDA, world > 1)
                 self.dp.enable_peer_step()
         else:
@@ -196,6 +214,20 @@ class PolicyWorker:
         mb.cu_seqlens, mb.max_seqlen = sh.plan, sh.plan.max_q
         return sh.local
 
+    def _main_grad(self, p):
+        """The fp32 main-gradient view of parameter ``p`` in its optimizer's
+        flat buffer (None when no optimizer owns it)."""
+        for d in (self.dp, self.dp_partner):
+            if d is not None and p in d.param_to_bucket:
+                b, off = d.param_to_bucket[p]
+                return b.grad[off: off + p.numel()]
+        return None
+
+    def _pp_dict(self, mb, temperature: float = 1.0, bin_=None) -> dict:
+        """A micro-batch as the pipeline schedule takes it."""
+        return {"ids": mb.input_ids, "pos": mb.positions, "cu": mb.cu_seqlens, "max": mb.max_seqlen,
+                "labels": mb.labels, "temperature": temperature, "mb": mb, "bin": bin_}
+
     def _placeholder(self):
         t = Trajectory(uid=-1, request_id=-1, prompt_ids=[0], response_ids=[0], rollout_logprobs=[0.0],
                        response_mask=[0])
@@ -206,6 +238,14 @@ class PolicyWorker:
     def compute_log_prob(self, trajs: list[Trajectory], idx: list[int], field: str = "old_logprobs",
                          temperature: float = 1.0) -> None:
         self.model.eval()
+        if self.pp is not None:
+            bins = pack_micro_batches(idx, trajs, self.max_tokens)
+            mbs = [build_micro_batch(trajs, b, self.device) for b in bins]
+            for mb, lp in zip(mbs, self.pp.forward_only([self._pp_dict(mb, temperature) for mb in mbs])):
+                lp = lp.cpu()
+                for i, sl in response_slices(mb, trajs):
+                    setattr(trajs[i], field, lp[sl].tolist())
+            return
         for bin_ in self._lockstep(pack_micro_batches(idx, trajs, self.max_tokens)):
             if bin_ is None:
                 mb = self._placeholder()
@@ -226,6 +266,14 @@ class PolicyWorker:
 
     @torch.no_grad()
     def compute_values(self, trajs: list[Trajectory], idx: list[int]) -> None:
+        if self.pp is not None:
+            bins = pack_micro_batches(idx, trajs, self.max_tokens)
+            mbs = [build_micro_batch(trajs, b, self.device) for b in bins]
+            for mb, v in zip(mbs, self.pp.forward_only([self._pp_dict(mb) for mb in mbs])):
+                v = v.cpu()
+                for i, sl in response_slices(mb, trajs):
+                    trajs[i].old_values = v[sl].tolist()
+            return
         for bin_ in self._lockstep(pack_micro_batches(idx, trajs, self.max_tokens)):
             if bin_ is None:
                 mb = self._placeholder()
@@ -245,6 +293,34 @@ class PolicyWorker:
     def _mini_batches(self, trajs: list[Trajectory]) -> list[list[int]]:
         return mini_batch_groups(trajs, int(self.cfg.actor.ppo_mini_batch_size))
 
+    def _policy_loss(self, lp, ent, mb, shard, trajs, bin_, num_seqs, global_tokens, stats):
+        """DAPO / PPO loss of one micro-batch (clip-higher, dual clip, optional
+        entropy bonus, KL loss and truncated importance weights); appends the
+        micro-batch's metrics to ``stats``."""
+        ac = self.cfg.actor
+        tis = mb.extra.get("is_weights")
+        if bool(self.cfg.algorithm.rollout_correction.tis):
+            rl = shard(build_micro_batch(trajs, bin_, self.device, field_old="rollout_logprobs").old_logprobs)
+            w = algos.truncated_is_weight(mb.old_logprobs, rl, float(self.cfg.algorithm.rollout_correction.tis_cap))
+            tis = w if tis is None else tis * w
+        agg = dict(seq_ids=mb.seq_ids, num_seqs=num_seqs, global_tokens=global_tokens)
+        loss, m = algos.ppo_policy_loss(lp, mb.old_logprobs, mb.advantages, mb.loss_mask,
+                                        float(ac.clip_ratio_low), float(ac.clip_ratio_high),
+                                        float(ac.clip_ratio_c), ac.loss_agg_mode, tis_weight=tis, **agg)
+        pg_loss = loss.detach()
+        if float(ac.entropy_coeff) != 0.0:
+            loss = loss - float(ac.entropy_coeff) * algos.agg_loss(ent, mb.loss_mask, ac.loss_agg_mode, **agg)
+        if ac.use_kl_loss:
+            ref = shard(build_micro_batch(trajs, bin_, self.device, field_old="ref_logprobs").old_logprobs)
+            kl = algos.kl_penalty(lp, ref, ac.kl_loss_type)
+            loss = loss + float(ac.kl_loss_coef) * algos.agg_loss(kl, mb.loss_mask, ac.loss_agg_mode, **agg)
+        with torch.no_grad():
+            m["pg_loss"] = pg_loss
+            m["entropy"] = (ent.detach() * mb.loss_mask).sum() / global_tokens
+        for k, v in m.items():
+            stats.setdefault(k, []).append(v)
+        return loss
+
     def update_policy(self, trajs: list[Trajectory], temperature: float = 1.0, step_guard=None,
                       sync_every_micro_batch: bool = False, plan: list[tuple] | None = None) -> dict:
         """PPO-family update.  ``step_guard`` (a context manager) wraps each
@@ -259,7 +335,6 @@ class PolicyWorker:
         self.model.train()
         stats: dict[str, list] = {}
         opt_s = 0.0
-        use_tis = bool(self.cfg.algorithm.rollout_correction.tis)
         if plan is None:
             plan = [(self.my_share(trajs, mini), float(sum(loss_tokens(trajs[i]) for i in mini)), len(mini))
                     for mini in self._mini_batches(trajs)]
@@ -267,7 +342,15 @@ class PolicyWorker:
             plan = self._recount_plan(trajs, plan)
         for _epoch in range(int(ac.ppo_epochs)):
             for mine, global_tokens, num_seqs in plan:
-                for bin_ in self._lockstep(pack_micro_batches(mine, trajs, self.max_tokens)):
+                if self.pp is not None:
+                    bins = pack_micro_batches(mine, trajs, self.max_tokens)
+                    mbs = [self._pp_dict(build_micro_batch(trajs, b, self.device), temperature, bin_=b)
+                           for b in bins]
+                    self.pp.train_step(mbs, lambda lp, ent, d: self._policy_loss(
+                        lp, ent, d["mb"], lambda t: t, trajs, d["bin"], num_seqs, global_tokens, stats))
+                    self.pp.reduce_tied_grads(self._main_grad)
+                for bin_ in (self._lockstep(pack_micro_batches(mine, trajs, self.max_tokens))
+                             if self.pp is None else []):
                     if bin_ is None:
                         mb = self._placeholder()
                         lp, ent = self.model.logprobs(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen,
@@ -278,29 +361,7 @@ class PolicyWorker:
                     shard = self._cp_shard(mb)
                     lp, ent = self.model.logprobs(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen,
                                                   mb.labels, temperature)
-                    tis = mb.extra.get("is_weights")
-                    if use_tis:
-                        rl = shard(build_micro_batch(trajs, bin_, self.device, field_old="rollout_logprobs").old_logprobs)
-                        w = algos.truncated_is_weight(mb.old_logprobs, rl, float(self.cfg.algorithm.rollout_correction.tis_cap))
-                        tis = w if tis is None else tis * w
-                    agg = dict(seq_ids=mb.seq_ids, num_seqs=num_seqs, global_tokens=global_tokens)
-                    loss, m = algos.ppo_policy_loss(lp, mb.old_logprobs, mb.advantages, mb.loss_mask,
-                                                    float(ac.clip_ratio_low), float(ac.clip_ratio_high),
-                                                    float(ac.clip_ratio_c), ac.loss_agg_mode, tis_weight=tis, **agg)
-                    pg_loss = loss.detach()
-                    if float(ac.entropy_coeff) != 0.0:
-                        ent_loss = algos.agg_loss(ent, mb.loss_mask, ac.loss_agg_mode, **agg)
-                        loss = loss - float(ac.entropy_coeff) * ent_loss
-                    if ac.use_kl_loss:
-                        ref = shard(build_micro_batch(trajs, bin_, self.device, field_old="ref_logprobs").old_logprobs)
-                        kl = algos.kl_penalty(lp, ref, ac.kl_loss_type)
-                        loss = loss + float(ac.kl_loss_coef) * algos.agg_loss(kl, mb.loss_mask, ac.loss_agg_mode, **agg)
-                    loss.backward()
-                    with torch.no_grad():
-                        m["pg_loss"] = pg_loss
-                        m["entropy"] = (ent.detach() * mb.loss_mask).sum() / global_tokens
-                    for k, v in m.items():
-                        stats.setdefault(k, []).append(v)
+                    self._policy_loss(lp, ent, mb, shard, trajs, bin_, num_seqs, global_tokens, stats).backward()
                     if sync_every_micro_batch and self.device.type == "cuda":
                         # bounded launch queue: the host thread releases the GIL here
                         torch.cuda.current_stream().synchronize()
@@ -316,6 +377,8 @@ class PolicyWorker:
         for k, vs in stats.items():
             t = torch.stack([v.reshape(()).float().to(self.device) for v in vs])
             out[f"actor/{k}"] = float(t.sum()) if k in ("pg_loss", "entropy") else float(t.mean())
+        if self.pp is not None:
+            out = self.pp.broadcast_metrics(out)
         out["timing_s/optimizer"] = opt_s
         return out
 
@@ -327,31 +390,44 @@ class PolicyWorker:
         if plan is None:
             plan = [(self.my_share(trajs, mini), float(sum(loss_tokens(trajs[i]) for i in mini)), len(mini))
                     for mini in self._mini_batches(trajs)]
+        def targets(mb):
+            old_v = torch.zeros(mb.num_tokens, dtype=torch.float32, device=self.device)
+            ret = torch.zeros_like(old_v)
+            for j, (i, sl) in enumerate(response_slices(mb, trajs)):
+                old_v[sl] = torch.tensor(trajs[i].old_values, device=old_v.device)
+                ret[sl] = torch.tensor(trajs[i].returns, device=old_v.device)
+            return old_v, ret
+
+        def vloss(v, old_v, ret, mb, global_tokens):
+            old_v, ret = old_v.to(v.dtype), ret.to(v.dtype)
+            loss, m = algos.value_loss(v, old_v, ret, mb.loss_mask, float(cc.cliprange_value),
+                                       global_tokens=global_tokens)
+            m["vf_loss"] = loss.detach()
+            for k, val in m.items():
+                stats.setdefault(k, []).append(val)
+            return loss
+
         for mine, global_tokens, _ in plan:
-            for bin_ in self._lockstep(pack_micro_batches(mine, trajs, self.max_tokens)):
+            if self.pp is not None:
+                mbs = [self._pp_dict(build_micro_batch(trajs, b, self.device), bin_=b)
+                       for b in pack_micro_batches(mine, trajs, self.max_tokens)]
+                self.pp.train_step(mbs, lambda v, _e, d, gt=global_tokens: vloss(v, *targets(d["mb"]), d["mb"], gt))
+            for bin_ in (self._lockstep(pack_micro_batches(mine, trajs, self.max_tokens))
+                         if self.pp is None else []):
                 if bin_ is None:
                     mb = self._placeholder()
                     (self.model.values(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen) * 0).sum().backward()
                     continue
                 mb = build_micro_batch(trajs, bin_, self.device)
-                old_v = torch.zeros(mb.num_tokens, dtype=torch.float32, device=self.device)
-                ret = torch.zeros_like(old_v)
-                for j, (i, sl) in enumerate(response_slices(mb, trajs)):
-                    old_v[sl] = torch.tensor(trajs[i].old_values, device=old_v.device)
-                    ret[sl] = torch.tensor(trajs[i].returns, device=old_v.device)
+                old_v, ret = targets(mb)
                 shard = self._cp_shard(mb)
                 old_v, ret = shard(old_v), shard(ret)
                 v = self.model.values(mb.input_ids, mb.positions, mb.cu_seqlens, mb.max_seqlen)
-                old_v, ret = old_v.to(v.dtype), ret.to(v.dtype)
-                loss, m = algos.value_loss(v, old_v, ret, mb.loss_mask, float(cc.cliprange_value),
-                                           global_tokens=global_tokens)
-                loss.backward()
-                m["vf_loss"] = loss.detach()
-                for k, val in m.items():
-                    stats.setdefault(k, []).append(val)
+                vloss(v, old_v, ret, mb, global_tokens).backward()
             st = self.dp.step(partners=[self.dp_partner] if self.dp_partner else None)
             stats.setdefault("grad_norm", []).append(st["grad_norm"])
-        return {f"critic/{k}": float(torch.stack([x.reshape(()).float() for x in vs]).mean()) for k, vs in stats.items()}
+        out = {f"critic/{k}": float(torch.stack([x.reshape(()).float() for x in vs]).mean()) for k, vs in stats.items()}
+        return self.pp.broadcast_metrics(out) if self.pp is not None else out
 
     # --------------------------------------------------------------- state
     def named_parameters(self) -> dict[str, torch.Tensor]:

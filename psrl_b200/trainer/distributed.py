@@ -31,7 +31,7 @@ import torch.distributed as dist
 from ..models import model_args_from_config
 from ..models.qwen import zipf_prior
 from ..parallel import dist as pdist
-from ..parallel.weight_sync import WeightLayout, WeightPuller, WeightStore
+from ..parallel.weight_sync import ShardedWeightPuller, WeightLayout, WeightPuller, WeightStore
 from ..rollout.engine import EngineWeights, RolloutEngine
 from ..rollout.instance import SyncPolicy
 from ..utils import transfer
@@ -55,6 +55,22 @@ def _role_split(world: int, cfg) -> int:
     return t
 
 
+def full_model_layout(args, dtype) -> WeightLayout:
+    """Flat layout of the unsharded model's parameters (each tensor 64-element
+    aligned), the layout rollout engines hold their weights in."""
+    from ..models.qwen import QwenModel
+    with torch.device("meta"):
+        shapes = [(n, tuple(p.shape)) for n, p in QwenModel(args).named_parameters()]
+    entries, off = [], 0
+    for n, shp in shapes:
+        entries.append((n, shp, off))
+        k = 1
+        for d in shp:
+            k *= d
+        off += (k + 63) // 64 * 64
+    return WeightLayout(entries, off, dtype)
+
+
 class DisaggregatedRun:
     def __init__(self, cfg, info: pdist.DistInfo):
         self.cfg = cfg
@@ -70,39 +86,44 @@ class DisaggregatedRun:
         self.train_cpu_group = None
         # trainer layout: tensor-parallel groups of `tp` consecutive trainer ranks,
         # data parallelism across them
-        tp = int(cfg.actor.get("tensor_parallel_size", 1) or 1)
-        cpn = int(cfg.actor.get("context_parallel_size", 1) or 1)
-        if tp > 1 and cpn > 1:
-            raise ValueError("tensor_parallel_size and context_parallel_size cannot both exceed 1")
-        if self.n_train % (tp * cpn):
-            raise ValueError(f"{self.n_train} trainer ranks are not a multiple of tensor_parallel_size={tp} x "
-                             f"context_parallel_size={cpn}")
-        # ranks that share one micro-batch share (a TP or a CP group) get the same data
-        self.tp_size = tp * cpn
-        self.dp_rank, self.dp_world = self.rank // self.tp_size, self.n_train // self.tp_size
-        self.tp_group = None
-        self.cp_group = None
+        # sizes: this framework's keys, or the reference's Megatron-backend names
+        meg = cfg.actor.get("megatron", None) or {}
+        tp = max(int(cfg.actor.get("tensor_parallel_size", 1) or 1), int(meg.get("tensor_model_parallel_size", 1) or 1))
+        cpn = max(int(cfg.actor.get("context_parallel_size", 1) or 1), int(meg.get("context_parallel_size", 1) or 1))
+        ppn = max(int(cfg.actor.get("pipeline_parallel_size", 1) or 1),
+                  int(meg.get("pipeline_model_parallel_size", 1) or 1))
+        if sum(x > 1 for x in (tp, cpn, ppn)) > 1:
+            raise ValueError("tensor, context and pipeline parallelism combine with data parallelism only, "
+                             "not with each other")
+        gsize = tp * cpn * ppn
+        if self.n_train % gsize:
+            raise ValueError(f"{self.n_train} trainer ranks are not a multiple of the model-parallel size {gsize}")
+        # ranks of one TP / CP / PP group hold the same data share
+        self.tp_size = gsize
+        self.dp_rank, self.dp_world = self.rank // gsize, self.n_train // gsize
+        self.tp_group = self.cp_group = self.pp_group = None
+        self.pp_size = ppn
         if self.is_trainer and self.n_train > 1:
             # created by the trainer ranks only (group-local synchronisation)
             self.train_cpu_group = pdist.new_subgroup(trainer_ranks, backend="gloo")
-            if tp == 1:
+            if gsize == 1 or cpn > 1:
                 # data (and context) parallel gradients sum over every trainer rank
                 self.train_group = pdist.new_subgroup(trainer_ranks, backend=backend)
-                if cpn > 1:
-                    for k in range(self.n_train // cpn):
-                        g = pdist.new_subgroup(list(range(k * cpn, (k + 1) * cpn)), backend=backend) \
-                            if k == self.rank // cpn else None
-                        if g is not None:
-                            self.cp_group = g
-            else:
+            if gsize > 1:
                 for k in range(self.dp_world):
-                    g = pdist.new_subgroup(list(range(k * tp, (k + 1) * tp)), backend=backend) \
+                    g = pdist.new_subgroup(list(range(k * gsize, (k + 1) * gsize)), backend=backend) \
                         if k == self.dp_rank else None
                     if g is not None:
-                        self.tp_group = g
-                j = self.rank % tp
-                if self.dp_world > 1:
-                    self.train_group = pdist.new_subgroup(list(range(j, self.n_train, tp)), backend=backend)
+                        if tp > 1:
+                            self.tp_group = g
+                        elif cpn > 1:
+                            self.cp_group = g
+                        else:
+                            self.pp_group = g
+                if cpn == 1 and self.dp_world > 1:
+                    # TP shard / PP stage j of every replica reduce their gradients together
+                    self.train_group = pdist.new_subgroup(list(range(self.rank % gsize, self.n_train, gsize)),
+                                                          backend=backend)
         self.args = model_args_from_config(cfg.model)
         self.trained_tokens = 0
         self.global_step = 0
@@ -131,29 +152,20 @@ class DisaggregatedRun:
         cfg = self.cfg
         self.actor = PolicyWorker(cfg, self.args, self.device, dp_group=self.train_group,
                                   seed=int(cfg.trainer.seed), dp_rank=self.dp_rank, dp_world=self.dp_world,
-                                  tp_group=self.tp_group, cp_group=self.cp_group)
+                                  tp_group=self.tp_group, cp_group=self.cp_group,
+                                  pp_group=self.pp_group)
         self.assembler = None
         if self.actor.ep is not None or self.actor.tp is not None:
             # sharded trainer: every trainer rank publishes the full model, assembled
             # from the shards after each optimizer step (rollout ranks pull as usual)
-            from ..models.qwen import QwenModel
             from ..parallel.assemble import FullWeightAssembler
             m = self.actor.model
             self.assembler = FullWeightAssembler(
                 m, ep=self.actor.ep, tp=self.actor.tp,
                 ep_names=[n for n, _ in m.named_parameters() if "experts_w" in n] if self.actor.ep is not None else (),
                 tp_names=sorted(self.actor.tp_sharded) if self.actor.tp is not None else ())
-            with torch.device("meta"):        # parameter names and shapes of the unsharded model
-                shapes = [(n, tuple(p.shape)) for n, p in QwenModel(self.args).named_parameters()]
-            entries, off = [], 0
-            for n, shp in shapes:
-                entries.append((n, shp, off))
-                k = 1
-                for d in shp:
-                    k *= d
-                off += (k + 63) // 64 * 64          # 16-byte aligned segments
-            self.layout = WeightLayout(entries, off, self.actor.dtype)
-            self.pub_flat = torch.zeros(off, dtype=self.actor.dtype, device=self.device)
+            self.layout = full_model_layout(self.args, self.actor.dtype)
+            self.pub_flat = torch.zeros(self.layout.total, dtype=self.actor.dtype, device=self.device)
             self.pub_views = self.layout.views(self.pub_flat)
             self.assembler.gather()
             self.assembler.assemble_into(self.pub_views)
@@ -166,13 +178,15 @@ class DisaggregatedRun:
             cargs = _replace(self.args, value_head=True, tie_word_embeddings=False)
             self.critic = PolicyWorker(cfg, cargs, self.device, dp_group=self.train_group,
                                        seed=int(cfg.trainer.seed) + 1, dp_rank=self.dp_rank, dp_world=self.dp_world,
-                                       tp_group=self.tp_group, cp_group=self.cp_group)
+                                       tp_group=self.tp_group, cp_group=self.cp_group,
+                                       pp_group=self.pp_group)
         self.ref = None
         if cfg.actor.use_kl_loss or cfg.algorithm.use_kl_in_reward:
             # sharded like the actor (expert / tensor parallel forwards are collectives)
             self.ref = PolicyWorker(cfg, self.args, self.device, dp_group=self.train_group,
                                     seed=int(cfg.trainer.seed), trainable=False, dp_rank=self.dp_rank,
-                                    dp_world=self.dp_world, tp_group=self.tp_group, cp_group=self.cp_group)
+                                    dp_world=self.dp_world, tp_group=self.tp_group, cp_group=self.cp_group,
+                                    pp_group=self.pp_group)
         self.kl_ctrl = algos.kl_controller(cfg.algorithm) if cfg.algorithm.use_kl_in_reward else None
         self.sharded_overlap = sharded_overlap_enabled(cfg)
         self.pre_step = sharded_overlap_mode(cfg) == "pre_step"
@@ -181,9 +195,16 @@ class DisaggregatedRun:
         self.store.publish(self.pub_flat, 0)
         if self.device.type == "cuda":
             torch.cuda.synchronize()
+        desc = self.store.descriptor()
+        engine_layout = self.layout
+        if self.pp_size > 1:
+            # each stage publishes its own layers; rollout ranks pull every tensor from a
+            # stage that holds it, straight into the full engine layout
+            desc["entries"] = list(self.layout.entries)
+            engine_layout = full_model_layout(self.args, self.actor.dtype)
         if self.rank == 0:
-            self.cp.set_layout(self.layout)
-        self.cp.register_store(self.rank, self.store.descriptor())
+            self.cp.set_layout(engine_layout)
+        self.cp.register_store(self.rank, desc)
         log(f"trainer ready: {self.layout.nbytes / 2**30:.2f} GiB published store ({mode})")
 
     def trainer_step(self) -> dict:
@@ -269,7 +290,8 @@ class DisaggregatedRun:
             for i in range(a.num_layers):
                 w.tensors[f"layers.{i}.mlp.router_prior"] = prior.to(self.device)
         self.weights = w
-        self.puller = WeightPuller(layout, descs, flat)
+        self.puller = ShardedWeightPuller(layout, descs, flat) if any("entries" in d for d in descs) \
+            else WeightPuller(layout, descs, flat)
         max_len = int(rc.max_prompt_length) + int(rc.max_response_length) + 64
         # a rollout-only GPU can give the KV cache and the batch more room
         kv_gb = float(rc.get("kv_cache_gb_dedicated", 0) or rc.get("kv_cache_gb", 4.0))

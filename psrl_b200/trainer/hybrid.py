@@ -86,8 +86,9 @@ class HybridRun:
         self.cpu_group = pdist.new_subgroup(list(range(self.world)), backend="gloo") if self.world > 1 else None
         # trainer layout: tensor-parallel groups of `tp` consecutive ranks, data
         # parallelism across them (expert parallelism spans the data-parallel group)
-        if int(cfg.actor.get("context_parallel_size", 1) or 1) > 1:
-            raise ValueError("context parallelism runs in the disaggregated placement")
+        if int(cfg.actor.get("context_parallel_size", 1) or 1) > 1 or \
+                int(cfg.actor.get("pipeline_parallel_size", 1) or 1) > 1:
+            raise ValueError("context and pipeline parallelism run in the disaggregated placement")
         tp = int(cfg.actor.get("tensor_parallel_size", 1) or 1)
         if self.world % tp:
             raise ValueError(f"world size {self.world} is not a multiple of tensor_parallel_size={tp}")

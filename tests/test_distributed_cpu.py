@@ -442,3 +442,33 @@ def test_gloo_world2_hybrid_tensor_parallel_rollout():
     schedule."""
     res = _run_sharded(["++actor.tensor_parallel_size=2", "++rollout.tensor_parallel_size=2"])
     assert res[0]["steps"] == [32, 32]
+
+
+def _run_disagg(overrides):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_disagg_sharded, args=(r, 3, port, q, overrides)) for r in range(3)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(900)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0, 0], codes
+    return q.get(timeout=5)
+
+
+def test_gloo_world3_disaggregated_pipeline_parallel_trainer():
+    """Two trainer ranks as two pipeline stages, each publishing its own layers;
+    the rollout rank pulls every tensor from the stage that holds it."""
+    res = _run_disagg(["++actor.pipeline_parallel_size=2"])
+    assert res["steps"] == [32, 32] and res["pulls"] >= 2
+
+
+def test_gloo_world3_disaggregated_context_parallel_trainer():
+    """Two trainer ranks splitting every sequence (CP=2)."""
+    res = _run_disagg(["++actor.context_parallel_size=2"])
+    assert res["steps"] == [32, 32] and res["pulls"] >= 2

@@ -81,3 +81,62 @@ def test_pipeline_matches_single_rank(world, tied):
     for r in res:
         assert r["grad"] < 1e-5, r
     assert res[-1]["losses"] == 5 and res[-1]["loss_err"] < 1e-5
+
+
+def _worker_policy(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import copy
+    import torch.distributed as dist
+    torch.set_num_threads(1)
+    from psrl_b200.config import load_config
+    from psrl_b200.models import PRESETS
+    from psrl_b200.parallel.dist import init_distributed
+    from psrl_b200.trainer.actor import PolicyWorker
+    from psrl_b200.trainer.batch import Trajectory
+    init_distributed("cpu", timeout_s=300)
+    a = replace(PRESETS["tiny"], num_layers=4)
+    # a large Adam eps keeps the update linear in the gradient (see the CP test)
+    cfg = load_config(preset="cpu_tiny_grpo", overrides=["actor.optim.lr=1.0", "actor.optim.eps=1.0",
+                                                         "actor.ppo_mini_batch_size=4", "actor.ppo_max_token_len_per_gpu=24"])
+    g = torch.Generator().manual_seed(4)
+    trajs = []
+    for i, (P, R) in enumerate(((5, 9), (3, 14), (7, 4), (2, 11))):
+        trajs.append(Trajectory(uid=i, request_id=i, prompt_ids=torch.randint(0, a.vocab_size, (P,), generator=g).tolist(),
+                                response_ids=torch.randint(0, a.vocab_size, (R,), generator=g).tolist(),
+                                rollout_logprobs=(-torch.rand(R, generator=g)).tolist()))
+        trajs[-1].advantage = float(torch.randn(1, generator=g))
+    ref = PolicyWorker(cfg, a, "cpu", seed=3)
+    ppw = PolicyWorker(cfg, a, "cpu", seed=3, pp_group=dist.group.WORLD)
+    t_ref, t_pp = copy.deepcopy(trajs), copy.deepcopy(trajs)
+    ref.compute_log_prob(t_ref, list(range(4)))
+    ppw.compute_log_prob(t_pp, list(range(4)))
+    lp_err = max(abs(x - y) for a_, b_ in zip(t_ref, t_pp) for x, y in zip(a_.old_logprobs, b_.old_logprobs))
+    mr = ref.update_policy(t_ref)
+    mp_ = ppw.update_policy(t_pp)
+    pr, pp_ = dict(ref.model.named_parameters()), dict(ppw.model.named_parameters())
+    upd = max(float((pr[n] - pp_[n]).detach().abs().max()) for n in pp_)
+    q.put({"rank": rank, "lp": lp_err, "param": upd, "pg": abs(mr["actor/pg_loss"] - mp_["actor/pg_loss"]),
+           "owned": len(pp_)})
+    dist.destroy_process_group()
+
+
+def test_policy_worker_pipeline_step_matches_single_rank():
+    """PolicyWorker with PP=2 (several micro-batches per mini-batch): old
+    log-probs on every stage, the loss metric and each stage's parameters after
+    one PPO step equal the single-rank worker's."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_policy, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in res:
+        assert r["lp"] < 1e-4, r
+        assert r["param"] < 1e-5, r
+        assert r["pg"] < 1e-5, r
