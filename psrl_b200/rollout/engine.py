@@ -162,7 +162,8 @@ class RolloutEngine:
                  max_model_len: int = 8192 + 1024, block_size: int = 64, max_num_batched_tokens: int = 10240,
                  kv_cache_gb: float | None = None, num_blocks: int | None = None, enable_prefix_caching: bool = True,
                  use_cuda_graph: bool = True, keep_kv_on_update: bool = False, version: int = 0,
-                 eos_token_id: int | None = None, tp=None, memory_pool=None, decode_gemm: str = "library"):
+                 eos_token_id: int | None = None, tp=None, memory_pool=None, decode_gemm: str = "library",
+                 kv_offload_blocks: int = 0):
         # tensor parallelism (``tp``: parallel.tp.TPGroup): this engine holds query heads,
         # KV heads and MLP columns [r/P, (r+1)/P) of every layer (weights in the same
         # layout as the TP trainer's shards) and its KV cache for its own KV heads; the
@@ -213,11 +214,18 @@ class RolloutEngine:
         if decode_gemm not in ("library", "tcgen05"):
             raise ValueError(f"decode_gemm must be 'library' or 'tcgen05', not {decode_gemm!r}")
         self.decode_gemm = decode_gemm
+        # host KV store (C29): a preempted sequence's complete blocks are copied to
+        # pinned host memory (keyed by their chained content hashes) and copied
+        # back when it resumes, instead of being recomputed
+        self.offload = None
         if memory_pool is not None:
             weights.move_to_pool(memory_pool, "weights")
         self.k_cache, self.v_cache = allocate_kv_tensors(a.num_layers, self.num_blocks, a.num_kv_heads,
                                                          self.block_size, a.head_dim, self.dtype, self.device,
                                                          pool=memory_pool)
+        if int(kv_offload_blocks) > 0:
+            from .kv_offload import KVOffloadStore
+            self.offload = KVOffloadStore(self, int(kv_offload_blocks))
         self.waiting: deque[_Seq] = deque()
         self.running: list[_Seq] = []
         self.by_id: dict[int, _Seq] = {}
@@ -230,7 +238,8 @@ class RolloutEngine:
         self._alloc_static()
         # stats
         self.stats = {"prefill_tokens": 0, "decode_tokens": 0, "prefill_steps": 0, "decode_steps": 0,
-                      "preemptions": 0, "cached_tokens": 0, "prefill_time": 0.0, "decode_time": 0.0}
+                      "preemptions": 0, "cached_tokens": 0, "prefill_time": 0.0, "decode_time": 0.0,
+                      "offloaded_blocks": 0, "onloaded_blocks": 0}
 
     # ------------------------------------------------------------- buffers
     def _alloc_static(self):
@@ -347,6 +356,8 @@ class RolloutEngine:
         freed = self.pool.sleep("kv", backup=False) + self.pool.sleep("weights", backup=keep_weights)
         self.bm = BlockManager(self.num_blocks, self.block_size)
         self.bm.set_version(self.version)
+        if self.offload is not None:
+            self.offload.clear()
         self.asleep = True
         return outs, freed
 
@@ -380,6 +391,8 @@ class RolloutEngine:
                     self._free(s, register=False)
                     s.num_computed = 0
             self.bm.set_version(self.version)
+            if self.offload is not None:
+                self.offload.clear()            # host copies hold the old weights' KV
 
     # --------------------------------------------------------------- step
     def step(self) -> list[RequestOutput]:
@@ -436,6 +449,8 @@ class RolloutEngine:
                 s.cached_tokens = s.num_computed
                 s.registered_blocks = len(blocks)
                 self.stats["cached_tokens"] += s.num_computed
+            if self.offload is not None and s.num_computed == len(s.blocks) * bs:
+                self._onload(s)
             todo = len(s.tokens) - s.num_computed
             chunk = min(todo, budget)
             need = math.ceil((s.num_computed + chunk) / bs) - len(s.blocks)
@@ -534,8 +549,35 @@ class RolloutEngine:
                 s.blocks.extend(self.bm.allocate(1))
                 self.n_bt[s.row, len(s.blocks) - 1] = s.blocks[-1]
 
+    def _onload(self, s: _Seq) -> None:
+        """Resume from the host KV store: the complete blocks after the device
+        prefix whose content hashes the store holds are copied back (the last
+        token is always recomputed)."""
+        bs = self.block_size
+        hs = self.bm.chain_hashes(s.tokens)
+        i0 = len(s.blocks)
+        k = 0
+        while i0 + k < len(hs) and hs[i0 + k] in self.offload.index and (i0 + k + 1) * bs < len(s.tokens):
+            k += 1
+        if k == 0 or not self.bm.can_allocate(k + 1):
+            return
+        new = self.bm.allocate(k)
+        n = self.offload.onload(hs[i0: i0 + k], new)
+        if n < k:
+            self.bm.release(new[n:])
+            new = new[:n]
+        s.blocks.extend(new)
+        s.num_computed += n * bs
+        s.cached_tokens += n * bs
+        self.stats["onloaded_blocks"] += n
+
     def _preempt(self, s: _Seq) -> None:
         self._remove_running(s)
+        if self.offload is not None and s.blocks:
+            full = min(s.num_computed // self.block_size, len(s.blocks))
+            if full:
+                hs = self.bm.chain_hashes(s.tokens[: full * self.block_size])
+                self.stats["offloaded_blocks"] += self.offload.offload(hs, s.blocks[:full])
         self._free(s, register=False)
         s.num_computed = 0
         self.waiting.appendleft(s)

@@ -164,7 +164,8 @@ class RLTrainer:
             block_size=int(rc.block_size), max_num_batched_tokens=int(rc.max_num_batched_tokens),
             kv_cache_gb=float(rc.get("kv_cache_gb", 4.0)), enable_prefix_caching=bool(rc.enable_prefix_caching),
             use_cuda_graph=bool(rc.cuda_graph), keep_kv_on_update=bool(cfg.psrl.rollout_coordination.partial_rollout.get("keep_kv", False)),
-            eos_token_id=self.data.tokenizer.eos_id if not rc.ignore_eos else None, decode_gemm=str(cfg.rollout.get("decode_gemm", "library")))
+            eos_token_id=self.data.tokenizer.eos_id if not rc.ignore_eos else None, decode_gemm=str(cfg.rollout.get("decode_gemm", "library")),
+            kv_offload_blocks=int(cfg.rollout.get("kv_offload_blocks", 0) or 0))
         sm = cfg.psrl.rollout_coordination.sync_and_mig_strategy
         policy = SyncPolicy(sm.method, bool(cfg.psrl.rollout_coordination.partial_rollout.enable),
                             sm.sync.get("threshold"), sm.sync.get("indicator", "request_num"))

@@ -192,7 +192,8 @@ class HybridRun:
             max_num_batched_tokens=int(rc.max_num_batched_tokens), kv_cache_gb=float(rc.get("kv_cache_gb", 4.0)),
             enable_prefix_caching=bool(rc.enable_prefix_caching), use_cuda_graph=bool(rc.cuda_graph),
             keep_kv_on_update=bool(cfg.psrl.rollout_coordination.partial_rollout.get("keep_kv", False)),
-            eos_token_id=None if rc.ignore_eos else self.cp.eos_id(), tp=self.eng_tp, decode_gemm=str(cfg.rollout.get("decode_gemm", "library")))
+            eos_token_id=None if rc.ignore_eos else self.cp.eos_id(), tp=self.eng_tp, decode_gemm=str(cfg.rollout.get("decode_gemm", "library")),
+            kv_offload_blocks=int(cfg.rollout.get("kv_offload_blocks", 0) or 0))
         sm = cfg.psrl.rollout_coordination.sync_and_mig_strategy
         self.policy = SyncPolicy(sm.method, bool(cfg.psrl.rollout_coordination.partial_rollout.enable),
                                  sm.sync.get("threshold"), sm.sync.get("indicator", "request_num"))
