@@ -157,6 +157,11 @@ class EngineWeights:
             self.tensors[k] = dst
 
 
+def _nullctx():
+    import contextlib
+    return contextlib.nullcontext()
+
+
 class RolloutEngine:
     def __init__(self, args: ModelArgs, weights: EngineWeights, *, max_num_seqs: int = 256,
                  max_model_len: int = 8192 + 1024, block_size: int = 64, max_num_batched_tokens: int = 10240,
@@ -239,7 +244,7 @@ class RolloutEngine:
         # stats
         self.stats = {"prefill_tokens": 0, "decode_tokens": 0, "prefill_steps": 0, "decode_steps": 0,
                       "preemptions": 0, "cached_tokens": 0, "prefill_time": 0.0, "decode_time": 0.0,
-                      "offloaded_blocks": 0, "onloaded_blocks": 0}
+                      "offloaded_blocks": 0, "onloaded_blocks": 0, "migrated_out": 0, "migrated_in": 0}
 
     # ------------------------------------------------------------- buffers
     def _alloc_static(self):
@@ -331,6 +336,51 @@ class RolloutEngine:
                 pass
         self._free(s, register=False)
         return self._output(s, "abort")
+
+    def migrate_request(self, request_id: int, dst: "RolloutEngine") -> bool:
+        """Move a request to engine ``dst`` together with the KV of every token
+        computed so far (the KV block kernel copies the blocks: same GPU, a
+        peer GPU over NVLink, or host memory), so ``dst`` continues it with a
+        one-token prefill instead of recomputing the context.  Both engines must
+        hold the same weight version.  Returns False (and keeps the request) when
+        ``dst`` has no room."""
+        from .kv_offload import transfer_direct
+        s = self.by_id.get(request_id)
+        bs = self.block_size
+        if s is None or dst is self or dst.asleep or dst.version != self.version or dst.block_size != bs:
+            return False
+        need = -(-s.num_computed // bs)
+        if dst.num_unfinished() >= dst.max_num_seqs or not dst.bm.can_allocate(need + 1):
+            return False
+        new = dst.bm.allocate(need)
+        if need:
+            cross = self.is_cuda and dst.is_cuda and self.device != dst.device
+            if self.is_cuda:
+                ready = torch.cuda.Event()
+                ready.record(torch.cuda.current_stream(self.device))     # the source's KV writes
+                torch.cuda.current_stream(dst.device).wait_event(ready)
+            if cross:
+                with torch.cuda.device(dst.device):
+                    ops.ext().enable_peer_access(self.device.index)
+            with torch.cuda.device(dst.device) if dst.is_cuda else _nullctx():
+                transfer_direct(self, dst, s.blocks[:need], new)
+            if self.is_cuda:
+                done = torch.cuda.Event()
+                done.record(torch.cuda.current_stream(dst.device))       # before the source reuses its blocks
+                torch.cuda.current_stream(self.device).wait_event(done)
+        self.by_id.pop(request_id)
+        if s.row >= 0:
+            self._remove_running(s)
+        else:
+            self.waiting.remove(s)
+        self._free(s, register=False)
+        s.blocks = new
+        s.registered_blocks = 0
+        dst.by_id[request_id] = s
+        dst.waiting.appendleft(s)
+        self.stats["migrated_out"] += 1
+        dst.stats["migrated_in"] += 1
+        return True
 
     def abort_all(self) -> list[RequestOutput]:
         return [o for o in (self.abort(r) for r in list(self.by_id)) if o is not None]
