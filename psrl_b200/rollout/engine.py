@@ -267,8 +267,12 @@ class RolloutEngine:
         self.h_bt = torch.zeros(B, MB, dtype=torch.int32, pin_memory=pin)
         self.h_temps = torch.ones(B, dtype=torch.float32, pin_memory=pin)
         self.h_seeds = torch.zeros(B, dtype=torch.long, pin_memory=pin)
-        self.h_out_tok = torch.zeros(B, dtype=torch.long, pin_memory=pin)
-        self.h_out_lp = torch.zeros(B, dtype=torch.float32, pin_memory=pin)
+        # two output buffers: the host reads one step's samples while the next is copied
+        self._h_out = [(torch.zeros(B, dtype=torch.long, pin_memory=pin),
+                        torch.zeros(B, dtype=torch.float32, pin_memory=pin)) for _ in range(2)]
+        self._out_flip = 0
+        self._pending = None
+        self._h2d_done = None
         self.n_bt = self.h_bt.numpy()
         a = self.args
         self.max_splits = 1
@@ -324,6 +328,7 @@ class RolloutEngine:
 
     def abort(self, request_id: int) -> RequestOutput | None:
         """Stop a request and return its partial output (or None if unknown)."""
+        self._drain(self.finished_unreported)
         s = self.by_id.pop(request_id, None)
         if s is None:
             return None
@@ -345,6 +350,8 @@ class RolloutEngine:
         hold the same weight version.  Returns False (and keeps the request) when
         ``dst`` has no room."""
         from .kv_offload import transfer_direct
+        self._drain(self.finished_unreported)
+        dst._drain(dst.finished_unreported)
         s = self.by_id.get(request_id)
         bs = self.block_size
         if s is None or dst is self or dst.asleep or dst.version != self.version or dst.block_size != bs:
@@ -425,6 +432,7 @@ class RolloutEngine:
     def load_weights(self, state: dict | None, version: int) -> None:
         """Install new weights (``state`` may be None when the caller already
         wrote them in place) and advance the weight version."""
+        self._drain(self.finished_unreported)
         if state:
             self.w.copy_from_state(state)
         self.version = int(version)
@@ -446,14 +454,20 @@ class RolloutEngine:
 
     # --------------------------------------------------------------- step
     def step(self) -> list[RequestOutput]:
-        """Run one scheduling step; returns requests that finished in it."""
-        out: list[RequestOutput] = []
+        """Run one scheduling step; returns requests that finished in it (and
+        any that finished while an abort or a weight load completed the step in
+        flight)."""
+        out: list[RequestOutput] = self.finished_unreported
+        self.finished_unreported = []
         if self.waiting and len(self.running) < self.max_num_seqs:
+            self._drain(out)                  # admission changes the batch: finish the step in flight
             did = self._prefill_step(out)
             if did:
                 return out
         if self.running:
             self._decode_step(out)
+        else:
+            self._drain(out)
         return out
 
     def _finish_check(self, s: _Seq, tok: int) -> str | None:
@@ -639,20 +653,75 @@ class RolloutEngine:
                 return min(b, self.max_num_seqs)
         return self.max_num_seqs
 
-    @torch.no_grad()
-    def _decode_step(self, out: list) -> None:
-        t0 = time.perf_counter()
-        self._ensure_decode_slots()
+    # A decode step in flight (CUDA graphs only): its rows, batch sizes, output
+    # buffers and completion event.  When no running sequence can finish with the
+    # token it computes and nothing waits for admission, the next step is
+    # launched before this one's tokens reach the host (its input tokens are
+    # copied on the device from the sampler's output), and the host appends
+    # this step's tokens while the GPU runs the next: the host's per-step work
+    # hides behind the device's.
+    def _chainable(self) -> bool:
+        if self._pending is None or self.waiting:
+            return False
+        new_blocks = 0
+        bs = self.block_size
+        for s in self.running:
+            p = s.req.params
+            if len(s.out_ids) + 2 > p.max_tokens or len(s.tokens) + 2 > self.max_model_len:
+                return False
+            if not p.ignore_eos and (self.eos_token_id is not None or p.stop_token_ids):
+                return False
+            if len(s.tokens) // bs >= len(s.blocks):
+                new_blocks += 1
+        return self.bm.can_allocate(new_blocks)
+
+    def _drain(self, out: list) -> None:
+        """Append the tokens of the step in flight (if any)."""
+        if self._pending is not None:
+            pend, self._pending = self._pending, None
+            self._finish(pend, out)
+
+    def _finish(self, pend, out: list) -> None:
+        rows, B, nb, tok_buf, lp_buf, done = pend
+        if done is not None:
+            done.synchronize()
+            transfer.d2h(nb * 12)
+            tok = tok_buf.numpy()[:B].tolist()
+            lp = lp_buf.numpy()[:B].tolist()
+        else:
+            tok = self.s_out_tok[:B].tolist()
+            lp = self.s_out_lp[:B].tolist()
+        for s, t, l in zip(rows, tok, lp):
+            s.num_computed = len(s.tokens)
+            self._append(s, t, l, out)
+        self.stats["decode_tokens"] += B
+        self.stats["decode_steps"] += 1
+
+    def _launch(self, chained: bool):
+        """Prepare and launch one decode step over the running sequences;
+        ``chained``: the previous step's tokens are not appended yet (each
+        sequence is one position further than its token list says)."""
+        if self._h2d_done is not None:
+            self._h2d_done.synchronize()      # the last step's host->device copies read these buffers
+        shift = 1 if chained else 0
+        if not chained:
+            self._ensure_decode_slots()
+        else:
+            bs = self.block_size
+            for s in self.running:            # room checked by _chainable: no preemption here
+                if len(s.tokens) // bs >= len(s.blocks):
+                    s.blocks.extend(self.bm.allocate(1))
+                    self.n_bt[s.row, len(s.blocks) - 1] = s.blocks[-1]
         B = len(self.running)
         if B == 0:
-            return
+            return None
         bs = self.block_size
-        toks = np.fromiter((s.tokens[-1] for s in self.running), dtype=np.int64, count=B)
-        pos = np.fromiter((len(s.tokens) - 1 for s in self.running), dtype=np.int32, count=B)
+        pos = np.fromiter((len(s.tokens) - 1 + shift for s in self.running), dtype=np.int32, count=B)
         blk = np.fromiter((s.blocks[p // bs] for s, p in zip(self.running, pos)), dtype=np.int64, count=B)
         slots = (blk * bs + pos % bs).astype(np.int32)
         nb = self._bucket(B)
-        self.h_tokens.numpy()[:B] = toks
+        if not chained:
+            self.h_tokens.numpy()[:B] = np.fromiter((s.tokens[-1] for s in self.running), dtype=np.int64, count=B)
         self.h_pos.numpy()[:B] = pos
         self.h_slots.numpy()[:B] = slots
         self.h_lens.numpy()[:B] = pos + 1
@@ -665,13 +734,19 @@ class RolloutEngine:
             self.h_slots.numpy()[B:nb] = -1
             self.h_lens.numpy()[B:nb] = 1
             self.n_bt[B:nb, 0] = 0
-        for src, dst in ((self.h_tokens, self.s_tokens), (self.h_pos, self.s_pos), (self.h_slots, self.s_slots),
-                         (self.h_lens, self.s_lens), (self.h_temps, self.s_temps), (self.h_seeds, self.s_seeds)):
+        if chained:
+            self.s_tokens[:nb].copy_(self.s_out_tok[:nb])    # the previous step's samples, on the device
+        else:
+            self.s_tokens[:nb].copy_(self.h_tokens[:nb], non_blocking=True)
+        for src, dst in ((self.h_pos, self.s_pos), (self.h_slots, self.s_slots), (self.h_lens, self.s_lens),
+                         (self.h_temps, self.s_temps), (self.h_seeds, self.s_seeds)):
             dst[:nb].copy_(src[:nb], non_blocking=True)
         mb = max(len(s.blocks) for s in self.running)
         self.s_bt[:nb, :mb].copy_(self.h_bt[:nb, :mb], non_blocking=True)
-        transfer.h2d(nb * (8 + 4 + 4 + 4 + 4 + 8 + 4 * mb))
+        transfer.h2d(nb * (4 + 4 + 4 + 4 + 8 + 4 * mb) + (0 if chained else 8 * nb))
         if self.is_cuda:
+            self._h2d_done = torch.cuda.Event()
+            self._h2d_done.record()
             torch.cuda.nvtx.range_push("decode_step")
         if self.use_cuda_graph:
             g = self._graphs.get(nb)
@@ -681,22 +756,34 @@ class RolloutEngine:
             ops._ext.add_launches(self._graph_launches[nb])
         else:
             self._decode_forward(nb)
-        if self.is_cuda:
-            torch.cuda.nvtx.range_pop()
-            self.h_out_tok[:nb].copy_(self.s_out_tok[:nb], non_blocking=True)
-            self.h_out_lp[:nb].copy_(self.s_out_lp[:nb], non_blocking=True)
-            torch.cuda.current_stream().synchronize()
-            transfer.d2h(nb * 12)
-            tok = self.h_out_tok.numpy()[:B].tolist()
-            lp = self.h_out_lp.numpy()[:B].tolist()
+        rows = list(self.running)
+        if not self.is_cuda:
+            return rows, B, nb, None, None, None
+        torch.cuda.nvtx.range_pop()
+        self._out_flip ^= 1
+        tok_buf, lp_buf = self._h_out[self._out_flip]
+        tok_buf[:nb].copy_(self.s_out_tok[:nb], non_blocking=True)
+        lp_buf[:nb].copy_(self.s_out_lp[:nb], non_blocking=True)
+        done = torch.cuda.Event()
+        done.record()
+        return rows, B, nb, tok_buf, lp_buf, done
+
+    @torch.no_grad()
+    def _decode_step(self, out: list) -> None:
+        t0 = time.perf_counter()
+        if self.use_cuda_graph and self._chainable():
+            prev = self._pending
+            self._pending = self._launch(chained=True)     # the GPU runs it while the host appends prev
+            self._finish(prev, out)
         else:
-            tok = self.s_out_tok[:B].tolist()
-            lp = self.s_out_lp[:B].tolist()
-        for s, t, l in zip(list(self.running), tok, lp):
-            s.num_computed = len(s.tokens)
-            self._append(s, t, l, out)
-        self.stats["decode_tokens"] += B
-        self.stats["decode_steps"] += 1
+            self._drain(out)
+            if self.running:
+                pend = self._launch(chained=False)
+                if pend is not None:
+                    if self.use_cuda_graph:
+                        self._pending = pend
+                    else:
+                        self._finish(pend, out)
         self.stats["decode_time"] += time.perf_counter() - t0
 
     def _decode_forward(self, nb: int) -> None:

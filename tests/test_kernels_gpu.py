@@ -412,10 +412,19 @@ def test_policy_step_gpu_matches_cpu_fp32():
                                 rollout_logprobs=(-torch.rand(R, generator=g) - 7.0).tolist()))
         trajs[-1].advantage = float(torch.randn(1, generator=g))
     res = {}
+    init = None
     for dev, dt in (("cpu", "fp32"), ("cuda", "bf16")):
         cfg = load_config(preset="cpu_tiny_grpo", overrides=[f"model.dtype={dt}", "actor.optim.lr=1e-3",
                                                              "actor.ppo_mini_batch_size=4"])
         w = PolicyWorker(cfg, a, dev, seed=3)
+        # random init draws from the device's generator: give both workers the CPU weights
+        if init is None:
+            init = {n: p.detach().clone() for n, p in w.model.named_parameters()}
+        else:
+            with torch.no_grad():
+                for n, p in w.model.named_parameters():
+                    p.copy_(init[n])
+            w.dp.sync_master_from_params()
         ts = copy.deepcopy(trajs)
         w.compute_log_prob(ts, list(range(len(ts))))       # ratio 1: no token clipped
         before = {n: p.detach().float().cpu().clone() for n, p in w.model.named_parameters()}
