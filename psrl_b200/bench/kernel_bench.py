@@ -140,17 +140,16 @@ def _graph_time(fns, reps: int = 5) -> float:
 
 def bench_decode_gemm(pk):
     """Decode-step projections of the Qwen2.5-3B engine (B rows = sequences in
-    the batch): the stream-K tcgen05 kernel against cuBLAS through torch, both
+    the batch): the weight-streaming tcgen05 kernel against cuBLAS through torch, both
     replayed from CUDA graphs over enough weight copies that every call streams
     its weight from HBM (more than the 126 MB L2).  gate_up is timed with its
     activation: the fused SwiGLU epilogue against cuBLAS + the SwiGLU kernel.
     Reported as weight bandwidth (the bytes a decode step must stream)."""
     from psrl_b200.ops import swiglu
-    from psrl_b200.ops.linear import DecodeWorkspace, decode_gate_up_swiglu, decode_linear
+    from psrl_b200.ops.linear import decode_gate_up_swiglu, decode_linear
     out = []
     shapes = (("qkv", 2560, 2048), ("o", 2048, 2048), ("gate_up+swiglu", 22016, 2048), ("down", 2048, 11008),
               ("lm_head", 151936, 2048))
-    ws = DecodeWorkspace(151936, "cuda")
     for B in (16, 64, 128, 256):
         for name, N, K in shapes:
             wb = N * K * 2
@@ -158,10 +157,10 @@ def bench_decode_gemm(pk):
             x = torch.randn(B, K, device="cuda").bfloat16()
             ws_ = [(torch.randn(N, K, device="cuda") * 0.02).bfloat16() for _ in range(copies)]
             if name.startswith("gate_up"):
-                tc = [lambda w=w: decode_gate_up_swiglu(x, w, ws) for w in ws_]
+                tc = [lambda w=w: decode_gate_up_swiglu(x, w) for w in ws_]
                 cb = [lambda w=w: swiglu(x @ w.t()) for w in ws_]
             else:
-                tc = [lambda w=w: decode_linear(x, w, None, ws) for w in ws_]
+                tc = [lambda w=w: decode_linear(x, w) for w in ws_]
                 cb = [lambda w=w: x @ w.t() for w in ws_]
             ms_tc, ms_cb = _graph_time(tc), _graph_time(cb)
             out.append({"case": f"decode {name} B={B} N={N} K={K}", "tcgen05_us": round(ms_tc * 1e3, 1),

@@ -13,8 +13,8 @@ Cases:
   gate_up    fused gate_up + SwiGLU epilogue, x [16384, 2048], W [22016, 2048]
   attn       tcgen05 varlen causal attention fwd + bwd, 6 x 1700 tokens, 16/2 heads
   decode     paged decode attention, B=256, context 1024, 16/2 heads
-  skinny     stream-K decode GEMM, 128 rows: gate_up + SwiGLU (22016 x 2048) and
-             QKV (2560 x 2048)
+  skinny     weight-streaming decode GEMM, 128 rows: gate_up + SwiGLU (22016 x 2048)
+             and QKV (2560 x 2048, K split over a 4-CTA cluster)
 """
 
 from __future__ import annotations
@@ -71,14 +71,13 @@ def _decode(iters: int) -> None:
 
 
 def _skinny(iters: int) -> None:
-    from psrl_b200.ops.linear import DecodeWorkspace, decode_gate_up_swiglu, decode_linear
+    from psrl_b200.ops.linear import decode_gate_up_swiglu, decode_linear
     x = torch.randn(128, 2048, device="cuda").bfloat16()
     w = (torch.randn(22016, 2048, device="cuda") * 0.02).bfloat16()
     wq = (torch.randn(2560, 2048, device="cuda") * 0.02).bfloat16()
-    ws = DecodeWorkspace(22016, "cuda")
     for _ in range(iters):
-        decode_gate_up_swiglu(x, w, ws)
-        decode_linear(x, wq, None, ws)
+        decode_gate_up_swiglu(x, w)
+        decode_linear(x, wq)
 
 
 CASES = {"skinny": _skinny, "gemm_fwd": lambda n: _gemm("fwd", n), "gemm_wgrad": lambda n: _gemm("wgrad", n), "gate_up": _gate_up,

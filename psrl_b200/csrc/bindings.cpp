@@ -46,8 +46,8 @@ void tc_gemm2_allreduce2(at::Tensor a, at::Tensor b, bool b_mn, at::Tensor acc_l
 void peer_barrier(std::vector<at::Tensor> flags_in_peer, std::vector<at::Tensor> own_slots, int64_t epoch,
                   double timeout_s, at::Tensor err);
 void acc_finalize(at::Tensor acc, at::Tensor out, c10::optional<at::Tensor> bias);
-at::Tensor tc_gemm_skinny(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias, bool swiglu, at::Tensor ws,
-                          at::Tensor tickets, int64_t grid, at::Tensor err);
+at::Tensor tc_gemm_skinny(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias, bool swiglu, int64_t split,
+                          at::Tensor err);
 std::vector<at::Tensor> attn_fwd_sm100_kv(at::Tensor q, at::Tensor kv, at::Tensor cu_q, at::Tensor cu_k,
                                           int64_t max_q, int64_t nq, int64_t nkv, double scale, bool want_lse,
                                           at::Tensor err);

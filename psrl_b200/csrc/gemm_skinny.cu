@@ -1,4 +1,4 @@
-// Weight-streaming tcgen05 GEMM for decode (few rows, large weights), stream-K:
+// Weight-streaming tcgen05 GEMM for decode (few rows, large weights):
 //   Y[b, n] = sum_k X[b, k] W[n, k] (+ bias[n])                        (ACT_NONE)
 //   H[b, i] = silu(G[b, i]) * U[b, i],  G / U = X W[i] / X W[I + i]     (ACT_SWIGLU)
 // for b < B <= 256.
@@ -6,25 +6,23 @@
 // The roles of the operands are swapped so that the weight fills the MMA's M
 // dimension: a tile is 128 weight rows (output features) x NB tokens, computed
 // as D = W_tile X^T with tcgen05.mma (M = 128, N = NB, K = 16) into NB fp32 TMEM
-// columns (two accumulators, gate and up, for ACT_SWIGLU).  A decode step's
-// GEMMs have too few tiles to occupy 148 SMs with one CTA per tile (QKV of a
-// 3B model: 20 tiles; gate_up: 86 tile pairs) and, with whole tiles per CTA,
-// leave a partial last wave, so the kernel is persistent and stream-K: the
-// (tile, 64-wide k block) units are dealt out in equal contiguous ranges to
-// one CTA per SM.  A CTA whose range covers a whole tile finishes it in its
-// epilogue (bias or SwiGLU, bf16 TMA store); a tile shared by several CTAs is
-// accumulated in an fp32 workspace with TMA reduce-add, and the CTA that
-// arrives last on the tile's ticket (an atomic counter, reset by that CTA)
-// reads the sum back, applies the epilogue, stores bf16 and zeroes the
-// workspace, so no second launch is needed.
+// columns (two accumulators, gate and up, for ACT_SWIGLU), the weight slab
+// streaming through a TMA ring.  A decode step's GEMMs have too few tiles to
+// occupy 148 SMs (QKV of a 3B model: 20, O and down: 16), so the K loop of a
+// tile is split over the S CTAs of one thread-block cluster (S = 1, 2, 4 or 8,
+// chosen on the host so that tiles x S fits one wave): each CTA accumulates its
+// K slice in TMEM and writes the fp32 partial tile into its own shared memory
+// (the drained TMA ring), one cluster barrier publishes the partials, and CTA r
+// sums rows [r NB / S, (r + 1) NB / S) of all S partials with distributed
+// shared-memory loads, applies bias or SwiGLU and stores bf16 -- no global
+// workspace, no atomics, no second launch.  With S = 1 the epilogue stores the
+// tile from TMEM directly (TMA store of bf16 boxes).
 //
 // Per CTA: 192 threads: warp 0 TMA producer, warp 1 MMA issuer (one thread),
-// warps 2..5 epilogue (TMEM lane quadrant = 32 weight rows each; tiles are
-// transposed through shared memory so every store is a [tokens, features]
-// box).  Accumulators are double-buffered in TMEM when they fit, so the
-// epilogue of one tile overlaps the MMAs of the next.  Waits are bounded; a
-// timeout records an error code and the kernel leaves after releasing its
-// TMEM.  Tile loads are plain per-CTA TMA copies.
+// warps 2..5 epilogue (TMEM lane quadrant = 32 weight rows each).  Waits are
+// bounded; a timeout records an error code, and every thread still reaches
+// both cluster barriers, so the cluster's peers are never left waiting.  Tile
+// loads are plain per-CTA TMA copies (no multicast).
 #include <cuda.h>
 
 #include "driver_api.h"
@@ -39,8 +37,8 @@ using namespace tc5;
 
 constexpr int BM = 128, BK = 64;
 constexpr int NTHREADS = 192;
-constexpr int STG_BYTES = 4096;  // per warp and buffer: 32 tokens x 32 fp32 (or bf16) features
-constexpr int RING_BUDGET = 193 * 1024;  // 3 x 64 KB stages of the widest (NB 256, SwiGLU) case fit
+constexpr int STG_BYTES = 4096;  // per warp and buffer: 32 tokens x 32 bf16 features
+constexpr int RING_BUDGET = 193 * 1024;
 enum { ACT_NONE = 0, ACT_SWIGLU = 1 };
 
 template <int NB, int ACT>
@@ -51,9 +49,10 @@ struct Cfg {
   static constexpr int STAGE_BYTES = NACC * A_BYTES + B_BYTES;
   static constexpr int STAGES = RING_BUDGET / STAGE_BYTES > 8 ? 8 : RING_BUDGET / STAGE_BYTES;
   static constexpr int ACC_COLS = NACC * NB;                         // TMEM columns per tile
-  static constexpr int ACC_STAGES = 2 * ACC_COLS <= 512 ? 2 : 1;
-  static constexpr int TMEM_COLS = ACC_STAGES * ACC_COLS < 32 ? 32 : ACC_STAGES * ACC_COLS;
+  static constexpr int TMEM_COLS = ACC_COLS < 32 ? 32 : ACC_COLS;
+  static constexpr int PART_BYTES = NACC * NB * BM * 4;              // fp32 partial tile (split K)
   static constexpr int STG_OFF = STAGES * STAGE_BYTES;
+  static constexpr bool CAN_SPLIT = PART_BYTES <= STG_OFF;           // partials fit the drained ring
   static constexpr int BAR_OFF = STG_OFF + 4 * 2 * STG_BYTES;
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
 };
@@ -61,12 +60,9 @@ struct Cfg {
 struct Args {
   int B, N, K;          // N: output features (I for ACT_SWIGLU)
   int up_off;           // ACT_SWIGLU: row of W where the up half starts (= I)
-  int tiles, kblocks;   // work units = tiles * kblocks
-  int grid;
+  int kblocks;
+  int S;                // CTAs per cluster splitting one tile's K loop
   const bf16* bias;     // ACT_NONE only (may be null)
-  float* ws;            // fp32 [B, ws_cols] accumulator of shared tiles (zero between calls)
-  int ws_cols;
-  int* tickets;         // [tiles] arrival counters (zero between calls)
   bf16* y;              // [B, N]
   int* err;
 };
@@ -75,77 +71,35 @@ __device__ __forceinline__ void set_err(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
-// CTA whose unit range [c U / G, (c + 1) U / G) holds unit u
-__device__ __forceinline__ int owner_of(int64_t u, int64_t U, int G) { return (int)(((u + 1) * G + U - 1) / U) - 1; }
-
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + __expf(-g)) * u; }
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
-// The last CTA on a shared tile: y = epilogue(ws) for the tile's 128 features,
-// then ws = 0.  Run by the 128 epilogue threads, eight independent 16-byte
-// loads in flight per thread (a load-store-load chain would pay the L2
-// latency once per vector).
-template <int ACT>
-__device__ __forceinline__ void finalize_tile(const Args& a, int tile) {
-  constexpr int V = 8;
-  const int tid = threadIdx.x - 64;
-  const int f0 = tile * BM;
-  const int total = a.B * (BM / 4);
-  for (int base = tid; base < total; base += 128 * V) {
-    float4 g[V], u[V];
-    int off[V];
-#pragma unroll
-    for (int j = 0; j < V; ++j) {
-      const int idx = base + j * 128;
-      const int t = idx / (BM / 4), f = f0 + (idx % (BM / 4)) * 4;
-      off[j] = (idx < total && f < a.N) ? t * a.ws_cols + f : -1;
-      g[j] = off[j] >= 0 ? __ldcg(reinterpret_cast<const float4*>(a.ws + off[j])) : make_float4(0.f, 0.f, 0.f, 0.f);
-      if constexpr (ACT == ACT_SWIGLU)
-        u[j] = off[j] >= 0 ? __ldcg(reinterpret_cast<const float4*>(a.ws + off[j] + a.up_off))
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int j = 0; j < V; ++j) {
-      if (off[j] < 0) continue;
-      const int idx = base + j * 128;
-      const int t = idx / (BM / 4), f = f0 + (idx % (BM / 4)) * 4;
-      float o[4] = {g[j].x, g[j].y, g[j].z, g[j].w};
-      if constexpr (ACT == ACT_SWIGLU) {
-        o[0] = silu_mul(o[0], u[j].x);
-        o[1] = silu_mul(o[1], u[j].y);
-        o[2] = silu_mul(o[2], u[j].z);
-        o[3] = silu_mul(o[3], u[j].w);
-        __stcg(reinterpret_cast<float4*>(a.ws + off[j] + a.up_off), make_float4(0.f, 0.f, 0.f, 0.f));
-      } else if (a.bias != nullptr) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) o[q] += __bfloat162float(a.bias[f + q]);
-      }
-      __stcg(reinterpret_cast<float4*>(a.ws + off[j]), make_float4(0.f, 0.f, 0.f, 0.f));
-      bf162 p[2] = {__floats2bfloat162_rn(o[0], o[1]), __floats2bfloat162_rn(o[2], o[3])};
-      *reinterpret_cast<uint2*>(a.y + (int64_t)t * a.N + f) = *reinterpret_cast<const uint2*>(p);
-    }
-  }
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
 }
 
 template <int NB, int ACT>
 __global__ void __launch_bounds__(NTHREADS, 1)
     skinny_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-                  const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmWS, Args a) {
+                  const __grid_constant__ CUtensorMap tmY, Args a) {
   using C = Cfg<NB, ACT>;
-  constexpr int STAGES = C::STAGES, ACCS = C::ACC_STAGES;
+  constexpr int STAGES = C::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2 * ACCS);
-  const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * STAGES;
-  const uint32_t accf0 = empty0 + 8 * STAGES, acce0 = accf0 + 8 * ACCS;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
+  const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * STAGES, accf = empty0 + 8 * STAGES;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int KB = a.kblocks, G = a.grid;
-  const int64_t U = (int64_t)a.tiles * KB;
-  const int64_t u0 = (int64_t)blockIdx.x * U / G, u1 = (int64_t)(blockIdx.x + 1) * U / G;
+  const int S = a.S;
+  const int rank = S > 1 ? (int)cluster_ctarank() : 0;
+  const int tile = blockIdx.x / S;
+  const int n0 = tile * BM;
+  const int kb_lo = (int)((int64_t)rank * a.kblocks / S), kb_hi = (int)((int64_t)(rank + 1) * a.kblocks / S);
   __shared__ volatile int s_abort;
-  __shared__ volatile int s_last;
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -153,10 +107,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       mbar_init(full0 + 8 * i, 1);
       mbar_init(empty0 + 8 * i, 1);
     }
-    for (int i = 0; i < ACCS; ++i) {
-      mbar_init(accf0 + 8 * i, 1);
-      mbar_init(acce0 + 8 * i, 4);   // one arrival per epilogue warp
-    }
+    mbar_init(accf, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) tmem_alloc_1cta(smem_u32(tmem_slot), C::TMEM_COLS);
@@ -171,100 +122,74 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tma_prefetch_desc(&tmX);
       int stage = 0;
       uint32_t phase = 0;
-      for (int64_t u = u0; u < u1 && !s_abort;) {
-        const int tile = (int)(u / KB);
-        const int kb_lo = (int)(u - (int64_t)tile * KB);
-        const int64_t end = u1 < (int64_t)(tile + 1) * KB ? u1 : (int64_t)(tile + 1) * KB;
-        const int kb_hi = kb_lo + (int)(end - u);
-        for (int kb = kb_lo; kb < kb_hi; ++kb) {
-          if (!mbar_wait(empty0 + 8 * stage, phase ^ 1)) {
-            set_err(a.err, 41);
-            s_abort = 1;
-            break;
-          }
-          const uint32_t fb = full0 + 8 * stage;
-          mbar_expect_tx(fb, C::STAGE_BYTES);
-          const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
-          tma_load_2d(sa, &tmW, kb * BK, tile * BM, fb);
-          if constexpr (ACT == ACT_SWIGLU) tma_load_2d(sa + C::A_BYTES, &tmW, kb * BK, a.up_off + tile * BM, fb);
-          tma_load_2d(sa + C::NACC * C::A_BYTES, &tmX, kb * BK, 0, fb);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
+      for (int kb = kb_lo; kb < kb_hi; ++kb) {
+        if (!mbar_wait(empty0 + 8 * stage, phase ^ 1)) {
+          set_err(a.err, 41);
+          s_abort = 1;
+          break;
         }
-        u = end;
+        const uint32_t fb = full0 + 8 * stage;
+        mbar_expect_tx(fb, C::STAGE_BYTES);
+        const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
+        tma_load_2d(sa, &tmW, kb * BK, n0, fb);
+        if constexpr (ACT == ACT_SWIGLU) tma_load_2d(sa + C::A_BYTES, &tmW, kb * BK, a.up_off + n0, fb);
+        tma_load_2d(sa + C::NACC * C::A_BYTES, &tmX, kb * BK, 0, fb);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(BM, NB, false, false);
-      int stage = 0, s = 0;
+      int stage = 0;
       uint32_t phase = 0;
-      for (int64_t u = u0; u < u1; ++s) {
-        const int tile = (int)(u / KB);
-        const int kb_lo = (int)(u - (int64_t)tile * KB);
-        const int64_t end = u1 < (int64_t)(tile + 1) * KB ? u1 : (int64_t)(tile + 1) * KB;
-        const int kb_hi = kb_lo + (int)(end - u);
-        u = end;
-        const int acc = s % ACCS;
-        const uint32_t tacc = tmem + acc * C::ACC_COLS;
-        bool ok = !s_abort && mbar_wait(acce0 + 8 * acc, ((s / ACCS) & 1) ^ 1);
+      bool ok = true;
+      for (int kb = kb_lo; kb < kb_hi; ++kb) {
+        if (!mbar_wait(full0 + 8 * stage, phase) || s_abort) {
+          ok = false;
+          break;
+        }
         fence_after();
-        for (int kb = kb_lo; ok && kb < kb_hi; ++kb) {
-          if (!mbar_wait(full0 + 8 * stage, phase) || s_abort) {
-            ok = false;
-            break;
-          }
-          fence_after();
-          const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES), sb = sa + C::NACC * C::A_BYTES;
+        const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES), sb = sa + C::NACC * C::A_BYTES;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint32_t accum = (kb > kb_lo || k > 0) ? 1u : 0u;
-            const uint64_t db = desc_sw128(sb + k * 32, 16, 1024);
-            mma_1cta(tacc, desc_sw128(sa + k * 32, 16, 1024), db, idesc, accum);
-            if constexpr (ACT == ACT_SWIGLU)
-              mma_1cta(tacc + NB, desc_sw128(sa + C::A_BYTES + k * 32, 16, 1024), db, idesc, accum);
-          }
-          commit_1cta(empty0 + 8 * stage);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint32_t accum = (kb > kb_lo || k > 0) ? 1u : 0u;
+          const uint64_t db = desc_sw128(sb + k * 32, 16, 1024);
+          mma_1cta(tmem, desc_sw128(sa + k * 32, 16, 1024), db, idesc, accum);
+          if constexpr (ACT == ACT_SWIGLU)
+            mma_1cta(tmem + NB, desc_sw128(sa + C::A_BYTES + k * 32, 16, 1024), db, idesc, accum);
         }
-        if (!ok) {
-          set_err(a.err, 42);
-          s_abort = 1;
+        commit_1cta(empty0 + 8 * stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
         }
-        commit_1cta(accf0 + 8 * acc);   // the epilogue sees s_abort if the tile is incomplete
-        if (!ok) break;
       }
+      if (!ok) {
+        set_err(a.err, 42);
+        s_abort = 1;
+      }
+      commit_1cta(accf);   // the epilogue sees s_abort if the tile is incomplete
     }
   } else {
     // epilogue: this warp's 32 weight rows (output features) x NB tokens
     const int quad = warp & 3;
-    uint8_t* stg = smem + C::STG_OFF + (warp - 2) * 2 * STG_BYTES;
-    int next = 0, s = 0;
-    for (int64_t u = u0; u < u1; ++s) {
-      const int tile = (int)(u / KB);
-      const int kb_lo = (int)(u - (int64_t)tile * KB);
-      const int64_t end = u1 < (int64_t)(tile + 1) * KB ? u1 : (int64_t)(tile + 1) * KB;
-      const int kb_hi = kb_lo + (int)(end - u);
-      u = end;
-      const int acc = s % ACCS;
-      bool ok = mbar_wait(accf0 + 8 * acc, (s / ACCS) & 1);
-      if (!ok) {
-        set_err(a.err, 43);
-        s_abort = 1;
-      }
-      fence_after();
-      ok = ok && !s_abort;
-      const bool whole = kb_lo == 0 && kb_hi == KB;
-      const int feat0 = tile * BM + quad * 32;
-      const uint32_t tacc = tmem + ((uint32_t)(quad * 32) << 16) + acc * C::ACC_COLS;
-      float bias = 0.f;
-      if constexpr (ACT == ACT_NONE)
-        if (whole && a.bias != nullptr && feat0 + lane < a.N) bias = __bfloat162float(a.bias[feat0 + lane]);
+    const int feat0 = n0 + quad * 32;
+    bool ok = mbar_wait(accf, 0);
+    if (!ok) {
+      set_err(a.err, 43);
+      s_abort = 1;
+    }
+    fence_after();
+    ok = ok && !s_abort;
+    const uint32_t tacc = tmem + ((uint32_t)(quad * 32) << 16);
+    if (S == 1) {
+      uint8_t* stg = smem + C::STG_OFF + (warp - 2) * 2 * STG_BYTES;
+      int next = 0;
+      const float bias =
+          (ACT == ACT_NONE && a.bias != nullptr && feat0 + lane < a.N) ? __bfloat162float(a.bias[feat0 + lane]) : 0.f;
 #pragma unroll 1
       for (int c = 0; c < NB / 32; ++c) {
         uint32_t r[32], ru[ACT == ACT_SWIGLU ? 32 : 1];
@@ -272,80 +197,82 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if constexpr (ACT == ACT_SWIGLU) tmem_ld32(tacc + NB + c * 32, ru);
         tmem_wait_ld();
         if (!ok || c * 32 >= a.B) continue;
-        if (whole) {
-          if (lane == 0) bulk_wait_read<1>();
-          __syncwarp();
-          bf16* t = reinterpret_cast<bf16*>(stg + next * STG_BYTES);   // [32 tokens][32 features]
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float v;
-            if constexpr (ACT == ACT_SWIGLU) v = silu_mul(__uint_as_float(r[i]), __uint_as_float(ru[i]));
-            else v = __uint_as_float(r[i]) + bias;
-            t[i * 32 + lane] = __float2bfloat16(v);
-          }
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&tmY, smem_u32(t), feat0, c * 32);
-            bulk_commit();
-          }
-          next ^= 1;
-        } else {
-          if (lane == 0) bulk_wait_read<0>();
-          __syncwarp();
-          float* t0 = reinterpret_cast<float*>(stg);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) t0[i * 32 + lane] = __uint_as_float(r[i]);
-          if constexpr (ACT == ACT_SWIGLU) {
-            float* t1 = reinterpret_cast<float*>(stg + STG_BYTES);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) t1[i * 32 + lane] = __uint_as_float(ru[i]);
-          }
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_reduce_add_2d(&tmWS, smem_u32(t0), feat0, c * 32);
-            if constexpr (ACT == ACT_SWIGLU) tma_reduce_add_2d(&tmWS, smem_u32(stg + STG_BYTES), a.up_off + feat0, c * 32);
-            bulk_commit();
-          }
-        }
-      }
-      // the accumulator is free for the tile after next
-      fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acce0 + 8 * acc);
-      if (!whole) {
-        // tile shared with other CTAs: the last to arrive finishes it
-        if (lane == 0) {
-          bulk_wait_all();
-          asm volatile("fence.proxy.async.global;" ::: "memory");
-          __threadfence();
-        }
+        if (lane == 0) bulk_wait_read<1>();
         __syncwarp();
-        epi_bar();
-        if (threadIdx.x == 64) {
-          int last = 0;
-          if (!s_abort) {
-            const int parts = owner_of((int64_t)(tile + 1) * KB - 1, U, G) - owner_of((int64_t)tile * KB, U, G) + 1;
-            const int old = atomicAdd(&a.tickets[tile], 1);
-            last = old == parts - 1;
-            if (last) a.tickets[tile] = 0;
-          }
-          s_last = last;
+        bf16* t = reinterpret_cast<bf16*>(stg + next * STG_BYTES);   // [32 tokens][32 features]
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float v;
+          if constexpr (ACT == ACT_SWIGLU) v = silu_mul(__uint_as_float(r[i]), __uint_as_float(ru[i]));
+          else v = __uint_as_float(r[i]) + bias;
+          t[i * 32 + lane] = __float2bfloat16(v);
         }
-        epi_bar();
-        if (s_last) {
-          __threadfence();
-          asm volatile("fence.proxy.async.global;" ::: "memory");
-          finalize_tile<ACT>(a, tile);
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmY, smem_u32(t), feat0, c * 32);
+          bulk_commit();
         }
-        epi_bar();   // s_last is rewritten for the next shared tile
+        next ^= 1;
+      }
+      if (lane == 0) bulk_wait_all();
+    } else if constexpr (C::CAN_SPLIT) {
+      // fp32 partial [acc][token][feature] in the drained TMA ring
+      float* part = reinterpret_cast<float*>(smem);
+#pragma unroll 1
+      for (int c = 0; c < NB / 32; ++c) {
+        uint32_t r[32], ru[ACT == ACT_SWIGLU ? 32 : 1];
+        tmem_ld32(tacc + c * 32, r);
+        if constexpr (ACT == ACT_SWIGLU) tmem_ld32(tacc + NB + c * 32, ru);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int o = (c * 32 + i) * BM + quad * 32 + lane;
+          part[o] = ok ? __uint_as_float(r[i]) : 0.f;
+          if constexpr (ACT == ACT_SWIGLU) part[NB * BM + o] = ok ? __uint_as_float(ru[i]) : 0.f;
+        }
       }
     }
-    if (lane == 0) bulk_wait_all();
   }
   fence_before();
   __syncthreads();
+  if constexpr (C::CAN_SPLIT) {
+    if (S > 1) {
+      cluster_sync();   // every CTA's partial is complete and visible to the cluster
+      // this CTA's share of the tokens, all 128 features, summed over the cluster
+      const int t_lo = rank * NB / S, t_hi = min((rank + 1) * NB / S, a.B);
+      const int total = (t_hi > t_lo ? t_hi - t_lo : 0) * (BM / 4);
+      const uint32_t base = smem_u32(smem);
+      for (int idx = threadIdx.x; idx < total; idx += NTHREADS) {
+        const int t = t_lo + idx / (BM / 4), f = (idx % (BM / 4)) * 4;
+        if (n0 + f >= a.N) continue;
+        const uint32_t off = (uint32_t)((t * BM + f) * 4);
+        float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
+        for (int q = 0; q < S; ++q) {
+          const uint32_t pa = mapa(base + off, (uint32_t)q);
+          const float4 v = ld_cluster_f4(pa);
+          g.x += v.x; g.y += v.y; g.z += v.z; g.w += v.w;
+          if constexpr (ACT == ACT_SWIGLU) {
+            const float4 w = ld_cluster_f4(pa + NB * BM * 4);
+            u.x += w.x; u.y += w.y; u.z += w.z; u.w += w.w;
+          }
+        }
+        float o[4] = {g.x, g.y, g.z, g.w};
+        if constexpr (ACT == ACT_SWIGLU) {
+          o[0] = silu_mul(o[0], u.x);
+          o[1] = silu_mul(o[1], u.y);
+          o[2] = silu_mul(o[2], u.z);
+          o[3] = silu_mul(o[3], u.w);
+        } else if (a.bias != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) o[j] += __bfloat162float(a.bias[n0 + f + j]);
+        }
+        bf162 pk[2] = {__floats2bfloat162_rn(o[0], o[1]), __floats2bfloat162_rn(o[2], o[3])};
+        *reinterpret_cast<uint2*>(a.y + (int64_t)t * a.N + n0 + f) = *reinterpret_cast<const uint2*>(pk);
+      }
+      cluster_sync();   // no CTA leaves while a peer still reads its shared memory
+    }
+  }
   if (warp == 0) {
     fence_after();
     tmem_free_1cta(tmem, C::TMEM_COLS);
@@ -376,21 +303,41 @@ static CUtensorMap skinny_map(const at::Tensor& t, uint32_t box_cols, uint32_t b
 }
 
 template <int NB, int ACT>
-static void skinny_launch(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& ty, const CUtensorMap& tws,
-                          const Args& a) {
+static void skinny_launch(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& ty, const Args& a,
+                          int tiles) {
   ensure_smem_attr(skinny_kernel<NB, ACT>, Cfg<NB, ACT>::SMEM_BYTES);
-  skinny_kernel<NB, ACT><<<a.grid, NTHREADS, Cfg<NB, ACT>::SMEM_BYTES, stream()>>>(tw, tx, ty, tws, a);
-  PSRL_CHECK_LAUNCH();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(tiles * a.S), 1, 1);
+  cfg.blockDim = dim3(NTHREADS, 1, 1);
+  cfg.dynamicSmemBytes = Cfg<NB, ACT>::SMEM_BYTES;
+  cfg.stream = stream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)a.S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  PSRL_CHECK_CUDA(cudaLaunchKernelEx(&cfg, skinny_kernel<NB, ACT>, tw, tx, ty, a));
 }
 
 template <int ACT>
 static void skinny_dispatch(int nb, const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& ty,
-                            const CUtensorMap& tws, const Args& a) {
+                            const Args& a, int tiles) {
   switch (nb) {
-    case 32: skinny_launch<32, ACT>(tw, tx, ty, tws, a); break;
-    case 64: skinny_launch<64, ACT>(tw, tx, ty, tws, a); break;
-    case 128: skinny_launch<128, ACT>(tw, tx, ty, tws, a); break;
-    default: skinny_launch<256, ACT>(tw, tx, ty, tws, a); break;
+    case 32: skinny_launch<32, ACT>(tw, tx, ty, a, tiles); break;
+    case 64: skinny_launch<64, ACT>(tw, tx, ty, a, tiles); break;
+    case 128: skinny_launch<128, ACT>(tw, tx, ty, a, tiles); break;
+    default: skinny_launch<256, ACT>(tw, tx, ty, a, tiles); break;
+  }
+}
+
+static bool can_split(int nb, bool swiglu) {
+  switch (nb) {
+    case 32: return swiglu ? Cfg<32, ACT_SWIGLU>::CAN_SPLIT : Cfg<32, ACT_NONE>::CAN_SPLIT;
+    case 64: return swiglu ? Cfg<64, ACT_SWIGLU>::CAN_SPLIT : Cfg<64, ACT_NONE>::CAN_SPLIT;
+    case 128: return swiglu ? Cfg<128, ACT_SWIGLU>::CAN_SPLIT : Cfg<128, ACT_NONE>::CAN_SPLIT;
+    default: return swiglu ? Cfg<256, ACT_SWIGLU>::CAN_SPLIT : Cfg<256, ACT_NONE>::CAN_SPLIT;
   }
 }
 
@@ -398,12 +345,11 @@ static void skinny_dispatch(int nb, const CUtensorMap& tw, const CUtensorMap& tx
 //   swiglu = false: y [B, R] = x w^T (+ bias [R]);
 //   swiglu = true:  w holds gate rows [0, I) then up rows [I, 2I) (R = 2I,
 //                   I % 128 == 0): y [B, I] = silu(x w_gate^T) * (x w_up^T).
-// ws: fp32 workspace of at least B * R elements and tickets: int32 of at least
-// ceil(R / 128) elements, both all zero on entry and zero again on return
-// (after an error report their contents are undefined: zero them).
-// grid: CTAs (<= 0: one per SM).
-at::Tensor tc_gemm_skinny(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias, bool swiglu, at::Tensor ws,
-                          at::Tensor tickets, int64_t grid, at::Tensor err) {
+// split: CTAs per 128-row tile sharing its K loop (1, 2, 4 or 8; <= 0: the
+// largest that keeps tiles x split within one wave of the SMs and at least two
+// 64-deep k blocks per CTA).
+at::Tensor tc_gemm_skinny(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> bias, bool swiglu, int64_t split,
+                          at::Tensor err) {
   CHECK_CUDA_TENSOR(x);
   CHECK_DTYPE(x, at::kBFloat16);
   CHECK_DTYPE(w, at::kBFloat16);
@@ -416,36 +362,38 @@ at::Tensor tc_gemm_skinny(at::Tensor x, at::Tensor w, c10::optional<at::Tensor> 
   at::cuda::CUDAGuard g(x.device());
   auto y = at::empty({B, N}, x.options());
   if (B == 0 || N == 0) return y;
-  TORCH_CHECK(ws.scalar_type() == at::kFloat && ws.is_contiguous() && ws.numel() >= B * R,
-              "ws must be a zeroed contiguous fp32 workspace of at least B * R elements");
-  const int64_t tiles = (N + BM - 1) / BM;
-  TORCH_CHECK(tickets.scalar_type() == at::kInt && tickets.is_contiguous() && tickets.numel() >= tiles,
-              "tickets must be a zeroed int32 tensor of at least ceil(N / 128) elements");
   const int nb = B <= 32 ? 32 : B <= 64 ? 64 : B <= 128 ? 128 : 256;
+  const int tiles = (int)((N + BM - 1) / BM);
   Args a{};
   a.B = (int)B;
   a.N = (int)N;
   a.K = (int)K;
   a.up_off = swiglu ? (int)N : 0;
-  a.tiles = (int)tiles;
   a.kblocks = (int)((K + BK - 1) / BK);
-  const int64_t units = tiles * a.kblocks;
-  a.grid = (int)std::min<int64_t>(grid > 0 ? grid : num_sms(), units);
+  int S = (int)split;
+  if (S <= 0) {
+    S = 1;
+    for (int c : {8, 4, 2})
+      if ((int64_t)tiles * c <= num_sms() && a.kblocks >= 2 * c) {
+        S = c;
+        break;
+      }
+  }
+  TORCH_CHECK(S == 1 || S == 2 || S == 4 || S == 8, "split must be 1, 2, 4 or 8");
+  if (!can_split(nb, swiglu) || S > a.kblocks) S = 1;
+  a.S = S;
   a.err = err.data_ptr<int>();
-  a.ws = ws.data_ptr<float>();
-  a.ws_cols = (int)R;
-  a.tickets = tickets.data_ptr<int>();
   a.y = reinterpret_cast<bf16*>(y.data_ptr());
   if (bias.has_value()) {
     CHECK_DTYPE((*bias), at::kBFloat16);
     TORCH_CHECK(bias->numel() == N && bias->is_contiguous(), "bias must be a contiguous bf16 [N]");
     a.bias = reinterpret_cast<const bf16*>(bias->data_ptr());
   }
-  auto acc = ws.narrow(0, 0, B * R).view({B, R});
+  TORCH_CHECK(y.stride(0) == N, "y must be contiguous");
   const CUtensorMap tw = skinny_map(w, 64, BM, true), tx = skinny_map(x, 64, (uint32_t)nb, true);
-  const CUtensorMap ty = skinny_map(y, 32, 32, false), tws = skinny_map(acc, 32, 32, false);
-  if (swiglu) skinny_dispatch<ACT_SWIGLU>(nb, tw, tx, ty, tws, a);
-  else skinny_dispatch<ACT_NONE>(nb, tw, tx, ty, tws, a);
+  const CUtensorMap ty = skinny_map(y, 32, 32, false);
+  if (swiglu) skinny_dispatch<ACT_SWIGLU>(nb, tw, tx, ty, a, tiles);
+  else skinny_dispatch<ACT_NONE>(nb, tw, tx, ty, a, tiles);
   return y;
 }
 

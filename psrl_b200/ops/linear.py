@@ -128,70 +128,29 @@ def gate_up_swiglu(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------- decode
-class DecodeWorkspace:
-    """Scratch of the stream-K decode GEMM (``csrc/gemm_skinny.cu``): an fp32
-    accumulator for tiles shared by several CTAs and one arrival ticket per
-    128-row tile.  Both are all zero between calls (the kernel re-zeroes what it
-    used); after a reported kernel error call :meth:`reset`."""
-
-    ROWS = 256   # rows per launch; larger batches run in 256-row pieces
-
-    def __init__(self, max_cols: int, device):
-        self.max_cols = int(max_cols)
-        self.acc = torch.zeros(self.ROWS * self.max_cols, dtype=torch.float32, device=device)
-        self.tickets = torch.zeros(-(-self.max_cols // 128), dtype=torch.int32, device=device)
-
-    def reset(self) -> None:
-        self.acc.zero_()
-        self.tickets.zero_()
-
-    def fits(self, cols: int) -> bool:
-        return cols <= self.max_cols
-
-
-_DEFAULT_WS: dict = {}
-
-
-def _workspace(ws: "DecodeWorkspace | None", cols: int, device) -> DecodeWorkspace:
-    if ws is not None:
-        if not ws.fits(cols):
-            raise ValueError(f"decode workspace holds {ws.max_cols} columns, the GEMM needs {cols}")
-        return ws
-    key = (device.type, device.index)
-    cur = _DEFAULT_WS.get(key)
-    if cur is None or not cur.fits(cols):
-        cur = _DEFAULT_WS[key] = DecodeWorkspace(cols, device)
-    return cur
-
-
-def _skinny(x, w, b, swiglu: bool, ws: DecodeWorkspace, grid: int) -> torch.Tensor:
+def _skinny(x, w, b, swiglu: bool, split: int) -> torch.Tensor:
     B = x.shape[0]
-    if B <= DecodeWorkspace.ROWS:
-        return ext().tc_gemm_skinny(x, w, b, swiglu, ws.acc, ws.tickets, int(grid), _err(x.device))
-    step = DecodeWorkspace.ROWS
-    return torch.cat([ext().tc_gemm_skinny(x[i:i + step], w, b, swiglu, ws.acc, ws.tickets, int(grid),
-                                           _err(x.device)) for i in range(0, B, step)], 0)
+    if B <= 256:
+        return ext().tc_gemm_skinny(x, w, b, swiglu, int(split), _err(x.device))
+    return torch.cat([ext().tc_gemm_skinny(x[i:i + 256], w, b, swiglu, int(split), _err(x.device))
+                      for i in range(0, B, 256)], 0)
 
 
-def decode_linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None,
-                  ws: DecodeWorkspace | None = None, grid: int = 0) -> torch.Tensor:
+def decode_linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None, split: int = 0) -> torch.Tensor:
     """``x W^T + b`` for a decode step's ``x`` ([B, K], one row per sequence),
-    one launch of the weight-streaming stream-K tcgen05 kernel per 256 rows:
-    the weight fills the MMA's M dimension and its (128-row tile, 64-deep k
-    block) units are dealt out evenly to one CTA per SM (``grid`` overrides the
-    CTA count).  ``ws``: the caller's :class:`DecodeWorkspace` (a per-device
-    default is used without one)."""
-    ws = _workspace(ws, w.shape[0], x.device)
-    return _skinny(x.contiguous(), w, b, False, ws, grid)
+    one launch of the weight-streaming tcgen05 kernel per 256 rows
+    (``csrc/gemm_skinny.cu``): the weight fills the MMA's M dimension, and when
+    the 128-row tiles do not fill the GPU a cluster of ``split`` CTAs (1, 2, 4
+    or 8; 0 = chosen from the shape) shares each tile's K loop and reduces the
+    partial tiles through distributed shared memory."""
+    return _skinny(x.contiguous(), w, b, False, split)
 
 
-def decode_gate_up_swiglu(x: torch.Tensor, w: torch.Tensor, ws: DecodeWorkspace | None = None,
-                          grid: int = 0) -> torch.Tensor:
+def decode_gate_up_swiglu(x: torch.Tensor, w: torch.Tensor, split: int = 0) -> torch.Tensor:
     """``silu(x W_gate^T) * (x W_up^T)`` for a decode step, with ``w`` the fused
     [2I, K] gate_up weight (gate rows first): one launch whose epilogue applies
     the activation, so the [B, 2I] projection never reaches HBM."""
-    ws = _workspace(ws, w.shape[0], x.device)
     if (w.shape[0] // 2) % 128:
         from .activation import swiglu
-        return swiglu(_skinny(x.contiguous(), w, None, False, ws, grid))
-    return _skinny(x.contiguous(), w, None, True, ws, grid)
+        return swiglu(_skinny(x.contiguous(), w, None, False, split))
+    return _skinny(x.contiguous(), w, None, True, split)

@@ -33,7 +33,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from .. import ops
-from ..ops.linear import DecodeWorkspace, decode_gate_up_swiglu, decode_linear, gate_up_swiglu
+from ..ops.linear import decode_gate_up_swiglu, decode_linear, gate_up_swiglu
 from ..ops.linear import linear as linear_tc
 from ..utils import transfer
 from ..models.config import ModelArgs
@@ -276,16 +276,10 @@ class RolloutEngine:
         self.n_bt = self.h_bt.numpy()
         a = self.args
         self.max_splits = 1
-        self.decode_ws = None
         if self.is_cuda:
             self.max_splits = 32
             self.decode_scratch = torch.empty(B * a.num_heads * self.max_splits * (a.head_dim + 1),
                                               dtype=torch.float32, device=dev)
-            # stream-K workspace of the decode projections and the LM head:
-            # 256 rows x the widest weight, zero between uses
-            if self.decode_gemm == "tcgen05":
-                widest = max(a.qkv_size, a.hidden_size, 2 * a.intermediate_size, a.vocab_size)
-                self.decode_ws = DecodeWorkspace(widest, dev)
 
     # ----------------------------------------------------------- requests
     def add_request(self, req: GenRequest) -> None:
@@ -795,7 +789,7 @@ class RolloutEngine:
                           kv_lens=self.s_lens[:nb], block_table=self.s_bt[:nb], splits=splits)
         use_tc = self.is_cuda and self.tp is None and self.decode_gemm == "tcgen05"
         w_head = self.w.lm_head()
-        logits = decode_linear(h, w_head, None, self.decode_ws) if use_tc else F.linear(h, w_head)
+        logits = decode_linear(h, w_head) if use_tc else F.linear(h, w_head)
         tok, lp = ops.sample(logits, self.s_temps[:nb], self.s_seeds[:nb], self.s_pos[:nb] + 1)
         self.s_out_tok[:nb].copy_(tok)
         self.s_out_lp[:nb].copy_(lp)
@@ -850,13 +844,13 @@ class RolloutEngine:
             def mlp_act(x, w):
                 return gate_up_swiglu(x, w)
         elif mode == "decode" and self.is_cuda and self.tp is None and self.decode_gemm == "tcgen05":
-            # one row per sequence: the weight-streaming stream-K tcgen05
-            # kernel, SwiGLU fused into the gate_up epilogue
+            # one row per sequence: the weight-streaming tcgen05 kernel (split K
+            # reduced in-cluster), SwiGLU fused into the gate_up epilogue
             def proj(x, w, b=None):
-                return decode_linear(x, w, b, self.decode_ws)
+                return decode_linear(x, w, b)
 
             def mlp_act(x, w):
-                return decode_gate_up_swiglu(x, w, self.decode_ws)
+                return decode_gate_up_swiglu(x, w)
         else:
             def proj(x, w, b=None):
                 return F.linear(x, w, b)
