@@ -34,6 +34,8 @@ at::Tensor attn_decode(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at:
 std::tuple<pybind11::bytes, int64_t> ipc_handle(at::Tensor t);
 at::Tensor ipc_open(pybind11::bytes handle, int64_t offset, int64_t numel, at::ScalarType dtype, int64_t src_device);
 void enable_peer_access(int64_t peer);
+void scatter_segments(at::Tensor src, std::vector<at::Tensor> dsts, std::vector<int64_t> src_offsets_bytes,
+                      std::vector<int64_t> lengths_bytes);
 void copy_segments(at::Tensor dst, std::vector<at::Tensor> srcs, std::vector<int64_t> dst_offsets_bytes,
                    std::vector<int64_t> src_offsets_bytes, std::vector<int64_t> lengths_bytes);
 at::Tensor tc_gemm(at::Tensor a, at::Tensor b, at::Tensor err);
@@ -102,6 +104,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_open", &psrl::ipc_open);
   m.def("enable_peer_access", &psrl::enable_peer_access);
   m.def("copy_segments", &psrl::copy_segments);
+  m.def("scatter_segments", &psrl::scatter_segments);
   m.def("tc_gemm", &psrl::tc_gemm);
   m.def("tc_grouped_gemm", &psrl::tc_grouped_gemm);
   m.def("tc_gemm2", &psrl::tc_gemm2);

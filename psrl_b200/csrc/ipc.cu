@@ -150,3 +150,82 @@ void copy_segments(at::Tensor dst, std::vector<at::Tensor> srcs, std::vector<int
 }
 
 }  // namespace psrl
+
+// ---------------------------------------------------------------------------
+// scatter_segments: the mirror of copy_segments for one source and up to 16
+// destinations (local or peer device pointers): segment i copies len[i] bytes
+// from src + src_off[i] to dsts[i] + dst_off[i] with 16-byte vector loads and
+// stores.  The peer all-to-all of expert parallelism (parallel/ep_p2p.py)
+// writes each destination rank's rows straight into that rank's receive
+// buffer this way: the stores travel over NVLink, no copy engine, no staging.
+namespace psrl {
+
+struct ScatterTable {
+  uint4* dst[MAX_SEG];
+  int64_t src_off[MAX_SEG];    // in 16 B units
+  int64_t start[MAX_SEG + 1];  // prefix sums of lengths (16 B units)
+  int64_t dst_total[MAX_SEG];  // destination size in 16 B units (bounds checks)
+  int n;
+};
+
+__global__ void __launch_bounds__(512) scatter_segments_kernel(const uint4* __restrict__ src, ScatterTable t) {
+  const int64_t total = t.start[t.n];
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int seg = 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride * 4) {
+    uint4 v[4];
+    int64_t at[4];
+    int sg[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t idx = i + u * stride;
+      sg[u] = -1;
+      if (idx < total) {
+        while (seg + 1 < t.n && idx >= t.start[seg + 1]) ++seg;
+        while (seg > 0 && idx < t.start[seg]) --seg;
+        const int64_t w = idx - t.start[seg];
+        v[u] = src[t.src_off[seg] + w];
+        at[u] = w;
+        sg[u] = chk::in_range(w, t.dst_total[seg], 65, seg, 1) ? seg : -1;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (sg[u] >= 0) t.dst[sg[u]][at[u]] = v[u];
+  }
+  __threadfence_system();  // peer stores visible before the barrier that follows
+}
+
+// src: source tensor; dsts: destination views (each segment writes from the
+// start of its view, so pass the view at the destination offset); src offsets
+// and lengths in bytes (multiples of 16).
+void scatter_segments(at::Tensor src, std::vector<at::Tensor> dsts, std::vector<int64_t> src_offsets_bytes,
+                      std::vector<int64_t> lengths_bytes) {
+  CHECK_CUDA_TENSOR(src);
+  const int n = dsts.size();
+  TORCH_CHECK(n <= MAX_SEG && n == (int)src_offsets_bytes.size() && n == (int)lengths_bytes.size(),
+              "bad segment lists");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(src.data_ptr()) % 16 == 0, "src must be 16-byte aligned");
+  const int64_t src_bytes = src.numel() * src.element_size();
+  ScatterTable t{};
+  t.n = n;
+  t.start[0] = 0;
+  for (int i = 0; i < n; ++i) {
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(dsts[i].data_ptr()) % 16 == 0, "destination ", i, " not 16-byte aligned");
+    TORCH_CHECK(lengths_bytes[i] % 16 == 0 && src_offsets_bytes[i] % 16 == 0, "lengths/offsets must be x16");
+    TORCH_CHECK(src_offsets_bytes[i] + lengths_bytes[i] <= src_bytes, "segment ", i, " overflows the source");
+    const int64_t db = dsts[i].numel() * dsts[i].element_size();
+    TORCH_CHECK(lengths_bytes[i] <= db, "segment ", i, " overflows its destination");
+    t.dst[i] = reinterpret_cast<uint4*>(dsts[i].data_ptr());
+    t.src_off[i] = src_offsets_bytes[i] / 16;
+    t.dst_total[i] = db / 16;
+    t.start[i + 1] = t.start[i] + lengths_bytes[i] / 16;
+  }
+  if (t.start[n] == 0) return;
+  at::cuda::CUDAGuard g(src.device());
+  const int grid = std::min<int64_t>(num_sms() * 4, (t.start[n] + 511) / 512);
+  scatter_segments_kernel<<<grid, 512, 0, stream()>>>(reinterpret_cast<const uint4*>(src.data_ptr()), t);
+  PSRL_CHECK_LAUNCH();
+}
+
+}  // namespace psrl

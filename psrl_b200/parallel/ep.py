@@ -36,6 +36,7 @@ class EPGroup:
     world: int
     rank: int
     num_experts: int
+    p2p: object = None       # parallel.ep_p2p.PeerAllToAll: dispatch / combine over NVLink peer memory
 
     @property
     def local(self) -> int:
@@ -46,11 +47,18 @@ class EPGroup:
         return self.rank * self.local
 
 
-def make_ep_group(group, num_experts: int) -> EPGroup:
+def make_ep_group(group, num_experts: int, device=None, p2p_bytes: int = 0) -> EPGroup:
+    """``p2p_bytes`` > 0 on CUDA: dispatch and combine rows move through
+    symmetric receive buffers of that size in peer memory (``ep_p2p``)
+    instead of NCCL."""
     world = dist.get_world_size(group)
     if num_experts % world:
         raise ValueError(f"{num_experts} experts do not split over {world} expert-parallel ranks")
-    return EPGroup(group, world, dist.get_rank(group), num_experts)
+    p2p = None
+    if p2p_bytes > 0 and device is not None and torch.device(device).type == "cuda" and world > 1:
+        from .ep_p2p import PeerAllToAll
+        p2p = PeerAllToAll(group, device, int(p2p_bytes))
+    return EPGroup(group, world, dist.get_rank(group), num_experts, p2p)
 
 
 class _AllToAll(torch.autograd.Function):
@@ -102,16 +110,27 @@ def moe_forward_ep(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, w13_loca
     token_of = order // k
     dest = flat.index_select(0, order) // ep.local
     send = torch.bincount(dest, minlength=ep.world)
-    recv = torch.empty_like(send)
-    dist.all_to_all_single(recv, send, group=ep.group)
-    send_l, recv_l = send.tolist(), recv.tolist()
     xs = x.index_select(0, token_of)
     local_ids = (flat.index_select(0, order) - dest * ep.local).to(torch.int64)
-    rx = all_to_all(xs, recv_l, send_l, ep.group)
+    if ep.p2p is not None:
+        # rows over NVLink peer memory; the count matrix (P x P ints) and the
+        # expert ids (8 bytes a row) stay on NCCL
+        from .ep_p2p import peer_all_to_all
+        M = ep.p2p.counts(send.tolist())
+        send_l, recv_l = list(M[ep.rank]), [M[s][ep.rank] for s in range(ep.world)]
+        rx = peer_all_to_all(xs, M, ep.p2p)
+    else:
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=ep.group)
+        send_l, recv_l = send.tolist(), recv.tolist()
+        rx = all_to_all(xs, recv_l, send_l, ep.group)
     rids = torch.empty(sum(recv_l), dtype=torch.int64, device=x.device)
     dist.all_to_all_single(rids, local_ids.contiguous(), recv_l, send_l, group=ep.group)
     ry = _local_experts(rx, rids, w13_local, w2_local)
-    back = all_to_all(ry, send_l, recv_l, ep.group)
+    if ep.p2p is not None:
+        back = peer_all_to_all(ry, [list(c) for c in zip(*M)], ep.p2p)
+    else:
+        back = all_to_all(ry, send_l, recv_l, ep.group)
     wts = w.reshape(-1).index_select(0, order).to(torch.float32)
     y = torch.zeros(T, x.shape[1], dtype=torch.float32, device=x.device)
     y = y.index_add(0, token_of, back.float() * wts[:, None])

@@ -120,7 +120,12 @@ class PolicyWorker:
             from ..parallel.ep import make_ep_group, shard_experts
             if dp_group is None or dp_world != ep_size:
                 raise ValueError("expert_parallel_size must equal the data-parallel world size")
-            self.ep = make_ep_group(dp_group, args.num_experts)
+            p2p_bytes = 0
+            if bool(cfg.actor.get("ep_peer_all_to_all", True)):
+                # receive buffers for twice a micro-batch's routed rows (rows beyond go through NCCL)
+                p2p_bytes = 2 * int(cfg.actor.ppo_max_token_len_per_gpu) * args.num_experts_per_tok * \
+                    args.hidden_size * torch.finfo(self.dtype).bits // 8
+            self.ep = make_ep_group(dp_group, args.num_experts, device=self.device, p2p_bytes=p2p_bytes)
             expert_names = set(shard_experts(self.model, self.ep))
         if trainable:
             oc = cfg.actor.optim if not args.value_head else cfg.critic.optim
