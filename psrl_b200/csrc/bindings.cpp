@@ -36,6 +36,7 @@ at::Tensor ipc_open(pybind11::bytes handle, int64_t offset, int64_t numel, at::S
 void enable_peer_access(int64_t peer);
 void scatter_segments(at::Tensor src, std::vector<at::Tensor> dsts, std::vector<int64_t> src_offsets_bytes,
                       std::vector<int64_t> lengths_bytes);
+void copy_rows(at::Tensor dst, at::Tensor table, at::Tensor start);
 void copy_segments(at::Tensor dst, std::vector<at::Tensor> srcs, std::vector<int64_t> dst_offsets_bytes,
                    std::vector<int64_t> src_offsets_bytes, std::vector<int64_t> lengths_bytes);
 at::Tensor tc_gemm(at::Tensor a, at::Tensor b, at::Tensor err);
@@ -105,6 +106,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("enable_peer_access", &psrl::enable_peer_access);
   m.def("copy_segments", &psrl::copy_segments);
   m.def("scatter_segments", &psrl::scatter_segments);
+  m.def("copy_rows", &psrl::copy_rows);
   m.def("tc_gemm", &psrl::tc_gemm);
   m.def("tc_grouped_gemm", &psrl::tc_grouped_gemm);
   m.def("tc_gemm2", &psrl::tc_gemm2);

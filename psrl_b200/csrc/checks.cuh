@@ -15,7 +15,8 @@
 //   62  paged prefill: block id out of range                  (b, slot, blk, num_blocks)
 //   63  decode: kv_len above max_blocks * block_size          (b, kv_len, cap, 0)
 //   64  decode: block id out of range                         (b, slot, blk, num_blocks)
-//   65  copy_segments: destination vector out of range        (seg, 0, idx, dst_total)
+//   65  peer copies: destination out of range                 (segment, 0 copy_segments | 1 scatter_segments
+//                                                              | 2 copy_rows, index, bound)
 //   66  peer optimizer: shard offset out of range             (bucket, 0 reduce | 1 update, off, numel)
 //   67  kv_copy_blocks: block id out of range                 (pair, 0 src | 1 dst, blk, blocks)
 // (values above 2^31 - 1 are reported truncated)

@@ -229,3 +229,54 @@ void scatter_segments(at::Tensor src, std::vector<at::Tensor> dsts, std::vector<
 }
 
 }  // namespace psrl
+
+// ---------------------------------------------------------------------------
+// copy_rows: one kernel for any number of 2-D byte blocks gathered into one
+// destination buffer (the layout-transforming weight pull): block k copies
+// `rows` rows of `row_vecs` 16-byte vectors from src_ptr (local or peer device
+// memory; row stride src_stride bytes) to dst + dst_off (row stride dst_stride
+// bytes).  A tensor-parallel shard of a row-parallel weight (columns of the
+// full matrix) is one block; a contiguous range is a block of one row.  The
+// table (int64 [n, 6]) and the prefix sums of rows * row_vecs (int64 [n + 1])
+// live on the device, built once per pull plan.
+namespace psrl {
+
+__global__ void __launch_bounds__(512) copy_rows_kernel(uint8_t* __restrict__ dst, const int64_t* __restrict__ tab,
+                                                        const int64_t* __restrict__ start, int n, int64_t dst_bytes) {
+  const int64_t total = start[n];
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += stride) {
+    int lo = 0, hi = n;  // block k holds vectors [start[k], start[k + 1])
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (start[mid] <= v) lo = mid;
+      else hi = mid;
+    }
+    const int64_t* t = tab + 6 * lo;
+    const int64_t local = v - start[lo];
+    const int64_t rv = t[3];
+    const int64_t row = local / rv, col = local - row * rv;
+    const uint4* s = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(t[0]) + row * t[4]) + col;
+    const int64_t d = t[1] + row * t[5] + col * 16;
+    if (!chk::in_range(d + 15, dst_bytes, 65, lo, 2)) continue;
+    *reinterpret_cast<uint4*>(dst + d) = *s;
+  }
+}
+
+void copy_rows(at::Tensor dst, at::Tensor table, at::Tensor start) {
+  CHECK_CUDA_TENSOR(dst);
+  TORCH_CHECK(table.is_cuda() && start.is_cuda() && table.scalar_type() == at::kLong &&
+                  start.scalar_type() == at::kLong && table.dim() == 2 && table.size(1) == 6 &&
+                  start.numel() == table.size(0) + 1 && table.is_contiguous() && start.is_contiguous(),
+              "table: int64 [n, 6] and start: int64 [n + 1] on the device");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(dst.data_ptr()) % 16 == 0, "dst must be 16-byte aligned");
+  const int n = (int)table.size(0);
+  if (n == 0) return;
+  at::cuda::CUDAGuard g(dst.device());
+  const int grid = num_sms() * 4;
+  copy_rows_kernel<<<grid, 512, 0, stream()>>>(reinterpret_cast<uint8_t*>(dst.data_ptr()), table.data_ptr<int64_t>(),
+                                               start.data_ptr<int64_t>(), n, dst.numel() * dst.element_size());
+  PSRL_CHECK_LAUNCH();
+}
+
+}  // namespace psrl

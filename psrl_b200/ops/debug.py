@@ -17,7 +17,7 @@ CODES = {
     62: "paged prefill: block id out of range",
     63: "decode attention: kv_len above max_blocks * block_size",
     64: "decode attention: block id out of range",
-    65: "copy_segments: destination offset out of range",
+    65: "peer copy (copy_segments / scatter_segments / copy_rows): destination offset out of range",
     66: "peer optimizer: shard offset out of range",
     67: "kv_copy_blocks: block id out of range",
 }

@@ -76,6 +76,22 @@ class WeightStore:
             self.flat.copy_(src_flat.to("cpu", non_blocking=False))
         self.version = int(version)
 
+    @torch.no_grad()
+    def publish_parts(self, parts: list[torch.Tensor], version: int) -> None:
+        """Publish several flat buffers back to back (a tensor-parallel rank's
+        replicated and sharded parameters)."""
+        esz = torch.finfo(self.layout.dtype).bits // 8
+        offs, o = [], 0
+        for t in parts:
+            offs.append(o)
+            o += t.numel() * esz
+        if self.mode == "hbm":
+            ops.ext().copy_segments(self.flat, list(parts), offs, [0] * len(parts), [t.numel() * esz for t in parts])
+        else:
+            for t, off in zip(parts, offs):
+                self.flat[off // esz: off // esz + t.numel()].copy_(t.to("cpu"))
+        self.version = int(version)
+
     def descriptor(self) -> dict:
         if self.mode == "hbm":
             handle, off = ops.ext().ipc_handle(self.flat)
@@ -132,18 +148,26 @@ class WeightPuller:
 
 class ShardedWeightPuller:
     """Rollout-side pull from trainers whose stores hold different parameter
-    sets (pipeline stages: each stage publishes only its layers).  Every
-    tensor of the engine's full layout is copied from a store that holds it
-    (round-robin over the data-parallel replicas of its stage, so the load
-    spreads over their NVLink links), straight into its place in the engine's
-    flat buffer: the store layout is transformed into the engine layout by the
-    copy itself, with no assembly on the trainers.  Runs of tensors that are
-    contiguous on both sides merge into one segment; the segments go through
-    ``copy_segments`` 16 per launch."""
+    sets, writing the engine's full layout directly (no assembly on the
+    trainers):
 
-    MAX_SEG = 16
+    * pipeline stages: a store holds whole tensors of its layers (descriptor
+      ``entries`` with the full names and shapes); each tensor is read from a
+      store that holds it, round-robin over the stage's data-parallel replicas;
+    * tensor-parallel ranks: a store holds this rank's shards (``entries`` with
+      the local names and shapes plus ``tp_rank`` / ``tp_world``); every
+      sharded tensor is assembled from all TP ranks' shards as it is copied:
+      column-parallel row ranges (q | k | v heads, gate | up halves) are
+      contiguous blocks, row-parallel column ranges (O, down) are 2-D blocks
+      with their own row strides (``models.converters.tp_slices`` gives the
+      pieces).  Replicated tensors come from any rank.
 
-    def __init__(self, layout: WeightLayout, descriptors: list[dict], dst_flat: torch.Tensor):
+    On CUDA the whole plan runs as ONE kernel (``copy_rows``: a device table of
+    2-D byte blocks, 16-byte loads from the trainers' HBM over NVLink)."""
+
+    def __init__(self, layout: WeightLayout, descriptors: list[dict], dst_flat: torch.Tensor, args=None):
+        from .assemble import engine_name
+        from ..models.converters import tp_slices
         self.layout = layout
         self.dst = dst_flat
         self.srcs = [open_store(d) for d in descriptors]
@@ -154,38 +178,85 @@ class ShardedWeightPuller:
                 if d["kind"] == "ipc" and int(d["device"]) != me:
                     ops.ext().enable_peer_access(int(d["device"]))
         esz = torch.finfo(layout.dtype).bits // 8
-        owners: dict[str, list] = {}
+        whole: dict[str, list] = {}        # engine name -> [(store, offset)]
+        shards: dict[str, dict] = {}       # engine name -> {tp rank: [(store, offset, local shape)]}
         for j, d in enumerate(descriptors):
+            tp = d.get("tp_world", 1)
             for name, shape, off in d["entries"]:
-                owners.setdefault(name, []).append((j, int(off)))
-        segs, turn = [], {}
+                en = engine_name(name)
+                if tp > 1 and en != name:
+                    shards.setdefault(en, {}).setdefault(int(d["tp_rank"]), []).append((j, int(off), tuple(shape)))
+                else:
+                    whole.setdefault(en, []).append((j, int(off)))
+        blocks, turn = [], {}
+
+        def pick(cands):
+            # rotate over the stores that hold the same set of tensors (a stage's or a
+            # TP rank's data-parallel replicas), so consecutive tensors use different links
+            key = tuple(c[0] for c in cands)
+            k = turn.get(key, 0)
+            turn[key] = k + 1
+            return cands[k % len(cands)]
+
         for name, shape, off in layout.entries:
-            if name not in owners:
-                raise KeyError(f"no trainer store holds {name}")
-            cands = owners[name]
-            k = turn.get(len(cands), 0)
-            turn[len(cands)] = k + 1
-            j, src = cands[k % len(cands)]
             n = 1
-            for s in shape:
-                n *= s
-            seg = [j, src * esz, int(off) * esz, n * esz]
-            last = segs[-1] if segs else None
-            if last and last[0] == j and last[1] + last[3] == seg[1] and last[2] + last[3] == seg[2]:
-                last[3] += seg[3]
+            for x in shape:
+                n *= x
+            dst0 = int(off) * esz
+            if name in shards:
+                per = shards[name]
+                P = len(per)
+                full = tuple(shape)
+                cols = full[1] if len(full) > 1 else 1
+                for r in range(P):
+                    j, loff, lshape = pick(per[r])
+                    lcols = lshape[1] if len(lshape) > 1 else 1
+                    acc = 0
+                    for dim, start, length in tp_slices(name, full, args, r, P):
+                        if dim == 0:
+                            blocks.append((j, (loff + acc * lcols) * esz, dst0 + start * cols * esz, 1,
+                                           length * cols * esz, 0, 0))
+                        else:
+                            blocks.append((j, (loff + acc) * esz, dst0 + start * esz, full[0], length * esz,
+                                           lcols * esz, cols * esz))
+                        acc += length
+            elif name in whole:
+                j, soff = pick(whole[name])
+                blocks.append((j, soff * esz, dst0, 1, n * esz, 0, 0))
             else:
-                segs.append(seg)
-        self.segments = [tuple(s) for s in segs]       # (store, src byte, dst byte, bytes)
+                raise KeyError(f"no trainer store holds {name}")
+        # merge contiguous one-row blocks (same store, adjacent on both sides)
+        merged = []
+        for b in blocks:
+            last = merged[-1] if merged else None
+            if last and b[3] == 1 and last[3] == 1 and last[0] == b[0] and last[1] + last[4] == b[1] \
+                    and last[2] + last[4] == b[2]:
+                merged[-1] = (last[0], last[1], last[2], 1, last[4] + b[4], 0, 0)
+            else:
+                merged.append(b)
+        for b in merged:
+            if b[4] % 16 or b[1] % 16 or b[2] % 16 or (b[3] > 1 and (b[5] % 16 or b[6] % 16)):
+                raise ValueError(f"weight pull block {b} is not 16-byte aligned")
+        self.blocks = merged          # (store, src byte, dst byte, rows, row bytes, src stride, dst stride)
+        if self.gpu:
+            tab = torch.tensor([[int(self.srcs[j].data_ptr()) + s, d, rows, rb // 16, ss, ds]
+                                for j, s, d, rows, rb, ss, ds in merged], dtype=torch.int64)
+            start = torch.zeros(len(merged) + 1, dtype=torch.int64)
+            start[1:] = torch.tensor([rows * (rb // 16) for _, _, _, rows, rb, _, _ in merged],
+                                     dtype=torch.int64).cumsum(0)
+            self.table = tab.to(dst_flat.device)
+            self.start = start.to(dst_flat.device)
 
     @torch.no_grad()
     def pull(self) -> int:
         if self.gpu:
-            for i in range(0, len(self.segments), self.MAX_SEG):
-                part = self.segments[i:i + self.MAX_SEG]
-                ops.ext().copy_segments(self.dst, [self.srcs[j] for j, _, _, _ in part], [d for _, _, d, _ in part],
-                                        [s for _, s, _, _ in part], [n for _, _, _, n in part])
+            ops.ext().copy_rows(self.dst, self.table, self.start)
         else:
-            esz = self.dst.element_size()
-            for j, s, d, n in self.segments:
-                self.dst[d // esz:(d + n) // esz].copy_(self.srcs[j][s // esz:(s + n) // esz])
-        return sum(n for _, _, _, n in self.segments)
+            dst = self.dst.view(torch.uint8)
+            for j, s, d, rows, rb, ss, ds in self.blocks:
+                src = self.srcs[j].view(torch.uint8)
+                if rows == 1:
+                    dst[d:d + rb].copy_(src[s:s + rb])
+                else:
+                    dst.as_strided((rows, rb), (ds, 1), d).copy_(src.as_strided((rows, rb), (ss, 1), s))
+        return sum(rows * rb for _, _, _, rows, rb, _, _ in self.blocks)

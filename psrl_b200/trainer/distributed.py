@@ -155,7 +155,17 @@ class DisaggregatedRun:
                                   tp_group=self.tp_group, cp_group=self.cp_group,
                                   pp_group=self.pp_group)
         self.assembler = None
-        if self.actor.ep is not None or self.actor.tp is not None:
+        self.pub_parts = None
+        if self.actor.tp is not None and self.actor.ep is None:
+            # tensor-parallel trainer: each rank publishes its own shards (replicated
+            # parameters, then sharded ones); rollout ranks put the full tensors
+            # together while they pull (parallel.weight_sync.ShardedWeightPuller)
+            dp, dpp = self.actor.dp, self.actor.dp_partner
+            entries = list(dp.layout) + [(n, shp, dp.total + off) for n, shp, off in dpp.layout]
+            self.layout = WeightLayout(entries, dp.total + dpp.total, self.actor.dtype)
+            self.pub_parts = [dp.flat, dpp.flat]
+            self.pub_flat = None
+        elif self.actor.ep is not None or self.actor.tp is not None:
             # sharded trainer: every trainer rank publishes the full model, assembled
             # from the shards after each optimizer step (rollout ranks pull as usual)
             from ..parallel.assemble import FullWeightAssembler
@@ -192,11 +202,14 @@ class DisaggregatedRun:
         self.pre_step = sharded_overlap_mode(cfg) == "pre_step"
         mode = "hbm" if (cfg.psrl.ps_mode == "hbm" and self.device.type == "cuda") else "cpu"
         self.store = WeightStore(self.layout, self.device, mode)
-        self.store.publish(self.pub_flat, 0)
+        self._publish(0)
         if self.device.type == "cuda":
             torch.cuda.synchronize()
         desc = self.store.descriptor()
         engine_layout = self.layout
+        if self.pub_parts is not None:
+            desc.update(entries=list(self.layout.entries), tp_rank=self.actor.tp.rank, tp_world=self.actor.tp.world)
+            engine_layout = full_model_layout(self.args, self.actor.dtype)
         if self.pp_size > 1:
             # each stage publishes its own layers; rollout ranks pull every tensor from a
             # stage that holds it, straight into the full engine layout
@@ -206,6 +219,12 @@ class DisaggregatedRun:
             self.cp.set_layout(engine_layout)
         self.cp.register_store(self.rank, desc)
         log(f"trainer ready: {self.layout.nbytes / 2**30:.2f} GiB published store ({mode})")
+
+    def _publish(self, version: int) -> None:
+        if self.pub_parts is not None:
+            self.store.publish_parts(self.pub_parts, version)
+        else:
+            self.store.publish(self.pub_flat, version)
 
     def trainer_step(self) -> dict:
         b = self.global_step
@@ -248,7 +267,7 @@ class DisaggregatedRun:
             raise TimeoutError("exclusive push lock")
         if self.n_train > 1:
             dist.barrier(group=self.train_cpu_group)
-        self.store.publish(self.pub_flat, b + 1)
+        self._publish(b + 1)
         if self.device.type == "cuda":
             torch.cuda.current_stream().synchronize()
         if self.n_train > 1:
@@ -290,7 +309,7 @@ class DisaggregatedRun:
             for i in range(a.num_layers):
                 w.tensors[f"layers.{i}.mlp.router_prior"] = prior.to(self.device)
         self.weights = w
-        self.puller = ShardedWeightPuller(layout, descs, flat) if any("entries" in d for d in descs) \
+        self.puller = ShardedWeightPuller(layout, descs, flat, a) if any("entries" in d for d in descs) \
             else WeightPuller(layout, descs, flat)
         max_len = int(rc.max_prompt_length) + int(rc.max_response_length) + 64
         # a rollout-only GPU can give the KV cache and the batch more room
