@@ -502,7 +502,17 @@ def run_disaggregated_bench(args, placement: str = "disaggregated"):
     else:
         res = run_disaggregated(cfg, args.steps, args.warmup, info)
         n_train = res["n_train"]
-        par = f"train dp{n_train} (sharded) + rollout dp{res['world'] - n_train} (tp1), NVLink weight pull"
+        ac = cfg.actor
+        mp = [f"{k}{int(ac.get(key, 1) or 1)}" for k, key in (("tp", "tensor_parallel_size"),
+                                                               ("cp", "context_parallel_size"),
+                                                               ("pp", "pipeline_parallel_size"),
+                                                               ("ep", "expert_parallel_size"))
+              if int(ac.get(key, 1) or 1) > 1]
+        g = 1
+        for m in mp:
+            g *= int(m[2:]) if not m.startswith("ep") else 1
+        train = f"dp{n_train // g} (sharded)" + ("".join(" x " + m for m in mp))
+        par = f"train {train} + rollout dp{res['world'] - n_train} (tp1), NVLink weight pull"
     launches = pdist.all_reduce_sum(float(_ext.launches() - l0), info.device)
     # bytes copied host<->device inside the timed region, all ranks
     h2d = pdist.all_reduce_sum(float(res["h2d"]), info.device)
