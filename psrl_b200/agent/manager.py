@@ -145,19 +145,28 @@ class AgentLoopManager:
                 n += 1
             return n
 
-    def take_work(self, instance_id, instance_version: int, max_n: int) -> list[GenRequest]:
-        """Admission: reserve each request at the instance's version and hand it out."""
+    def take_work(self, instance_id, instance_version: int, max_n: int, accept=None) -> list[GenRequest]:
+        """Admission: reserve each request at the instance's version and hand it
+        out.  ``accept(req) -> bool`` (the router's pull-mode policy) may pass
+        a request over for another instance; at most ``4 * max_n`` requests
+        are looked at per call."""
         with self.lock:
             self.fill()
             self._check_trajectory_timeouts()
             out: list[GenRequest] = []
-            held: list[GenRequest] = []       # migrating to another instance: not for this one
-            while self.queue and len(out) < max_n:
+            held: list[GenRequest] = []       # migrating elsewhere, or routed to another instance
+            looked = 0
+            while self.queue and len(out) < max_n and looked < 4 * max(1, max_n):
+                looked += 1
                 req = self.queue[0]
                 rid = req.request_id
                 tgt = self.migration_target.get(rid)
                 if tgt is not None and tgt != instance_id:
                     held.append(self.queue.popleft())
+                    continue
+                if tgt is None and accept is not None and not accept(req):
+                    held.append(self.queue.popleft())
+                    self.stats["routed_elsewhere"] = self.stats.get("routed_elsewhere", 0) + 1
                     continue
                 self.migration_target.pop(rid, None)
                 if self.ps.check_aborted_requests(rid, remove=True):

@@ -172,6 +172,26 @@ class Router:
                 list(req.prompt_ids) + list(getattr(req, "prev_output_ids", [])))
         return s
 
+    @classmethod
+    def from_cfg(cls, cfg, ps=None) -> "Router":
+        """Router of ``psrl.rollout_coordination.routing_strategy``."""
+        rs = cfg.psrl.rollout_coordination.routing_strategy
+        cap = rs.get("cache_aware_policy", {}) or {}
+        return cls(str(rs.method), ps, group_sticky=bool(rs.get("enable_group_sticky", False)),
+                   trajectory_sticky=bool(rs.get("enable_trajectory_sticky", False)),
+                   request_budget=int(rs.get("request_budget", 1024)), block_size=int(rs.get("block_size", 16)),
+                   balance_abs_threshold=int(cap.get("balance_abs_threshold", 16)),
+                   balance_rel_threshold=float(cap.get("balance_rel_threshold", 1.5)))
+
+    def assigned(self, req, s: InstanceState) -> None:
+        """Record that ``req`` went to ``s`` (pull mode): group home, the
+        instance's prefix index, its queued count."""
+        s.num_waiting += 1
+        self.group_home.setdefault(req.meta.get("uid"), s.instance_id)
+        if self.method.startswith("cache_aware"):
+            self.prefix.setdefault(s.instance_id, PrefixIndex(self.block_size)).insert(
+                list(req.prompt_ids) + list(getattr(req, "prev_output_ids", [])))
+
     def accepts(self, req, me: InstanceState, instances: list[InstanceState]) -> bool:
         """Pull-mode check: should instance ``me`` take ``req`` now?"""
         s = self.sticky(req, self.eligible(req, instances))

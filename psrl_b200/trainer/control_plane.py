@@ -59,6 +59,8 @@ class ControlPlane:
         # migration over the instances' reported states
         from ..rollout.coordinator import CoordinatorConfig, RolloutCoordinator
         self.coord = RolloutCoordinator(CoordinatorConfig.from_cfg(cfg), self.ps.get_ps_model_version)
+        from ..rollout.router import Router
+        self.router = Router.from_cfg(cfg)
         self.states: dict = {}
         sm = cfg.psrl.rollout_coordination.sync_and_mig_strategy
         self.coord_interval_s = float(sm.get("check_interval_in_ms", 100)) / 1000.0
@@ -132,8 +134,17 @@ class ControlPlane:
             self.manager.on_complete(outputs, iid)
         sync = self._coordinate(iid, int(version), state, now)
         quarantined = iid in self.coord.quarantined
-        reqs = self.manager.take_work(iid, int(version), int(free_slots)) if free_slots > 0 and not quarantined \
-            else []
+        reqs = []
+        if free_slots > 0 and not quarantined:
+            me = self.states[iid]
+            peers = [s for i, s in self.states.items() if i not in self.coord.quarantined]
+            accept = None
+            if len(peers) > 1:
+                # routing policy in pull mode (request balance, stickiness, cache affinity, ...)
+                accept = lambda req: self.router.accepts(req, me, peers)          # noqa: E731
+            reqs = self.manager.take_work(iid, int(version), int(free_slots), accept)
+            for r in reqs:
+                self.router.assigned(r, me)
         aborts = self.manager.take_aborts(iid)
         st = self.exchange_stats
         st["calls"] += 1

@@ -72,3 +72,24 @@ def test_migration_moves_running_requests_to_the_idle_instance():
     assert set(resumed) == moved
     assert all(r.prev_output_ids == [7, 7] for r in resumed.values())   # tokens so far kept
     cp.ps.staleness_inventory.check_invariants()
+
+
+def test_pull_dispatch_follows_routing_policy():
+    """Training dispatch goes through the router in pull mode: with request-count
+    balancing a loaded instance passes requests over for an idle one; with group
+    stickiness every member of a prompt group lands on the group's first instance."""
+    cfg, cp = _cp()
+    busy, idle = (0, 0), (1, 0)
+    cp.exchange(idle, 0, 0, [], _state(running=0))
+    reqs, *_ = cp.exchange(busy, 0, 8, [], _state(running=40))      # far more loaded than the idle one
+    assert reqs == [] and cp.manager.stats.get("routed_elsewhere", 0) > 0
+    got, *_ = cp.exchange(idle, 0, 8, [], _state(running=0))
+    assert len(got) == 8
+
+    cfg, cp = _cp(["psrl.rollout_coordination.routing_strategy.enable_group_sticky=true"])
+    a, b = (0, 0), (1, 0)
+    cp.exchange(b, 0, 0, [], _state())
+    first, *_ = cp.exchange(a, 0, 3, [], _state())                   # a takes part of the first group
+    rest, *_ = cp.exchange(b, 0, 16, [], _state())                   # b must leave that group to a
+    uids_a = {r.meta["uid"] for r in first}
+    assert not uids_a & {r.meta["uid"] for r in rest}
