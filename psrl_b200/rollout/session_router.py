@@ -32,6 +32,8 @@ class SessionState:
     version_tag: int = -1
     instance_id: tuple | None = None
     hung: bool = False
+    status: str = "env"          # gen (a turn is generating) | env (between turns)
+    pending_obs_tokens: int = 0  # expected observation tokens of the next turn
     turns: list = field(default_factory=list)
 
     def context_tokens(self) -> int:
@@ -42,27 +44,55 @@ class SessionRouter:
     """``generate_fn(prompt_ids, max_tokens, version_tag, instance_hint) ->
     (output_ids, logprobs, versions, version_tag, instance_id)``."""
 
-    def __init__(self, generate_fn):
+    def __init__(self, generate_fn, scheduler=None):
+        """``scheduler`` (``session_scheduler.ThunderAgentScheduler``): after
+        every turn boundary the sessions' KV footprints are checked against its
+        capacity and sessions are hung (their next turn refused with 409 until
+        continued) or continued."""
         self.generate = generate_fn
+        self.scheduler = scheduler
         self.sessions: dict[str, SessionState] = {}
         self.lock = threading.Lock()
+        self.sched_stats = {"hung": 0, "continued": 0}
+
+    def _schedule(self) -> None:
+        """Run the capacity scheduler over every open session (lock held)."""
+        if self.scheduler is None:
+            return
+        from .session_scheduler import SessionInfo
+        infos = [SessionInfo(k, v.context_tokens(), "hung" if v.hung else v.status, v.pending_obs_tokens)
+                 for k, v in self.sessions.items()]
+        to_hang, to_cont = self.scheduler.decide(infos)
+        for k in to_hang:
+            self.sessions[k].hung = True
+        for k in to_cont:
+            self.sessions[k].hung = False
+        self.sched_stats["hung"] += len(to_hang)
+        self.sched_stats["continued"] += len(to_cont)
 
     def complete(self, sid: str, prompt_ids: list[int], max_tokens: int) -> dict:
         with self.lock:
             s = self.sessions.setdefault(sid, SessionState(sid))
             if s.hung:
                 return {"error": "session is hung", "status": 409}
+            prev = s.context_tokens()
+            s.pending_obs_tokens = max(0, len(prompt_ids) - prev)
+            s.status = "gen"
+            self._schedule()
         out, lps, vers, tag, inst = self.generate(prompt_ids, max_tokens, s.version_tag, s.instance_id)
         with self.lock:
             if s.version_tag < 0:
                 s.version_tag = tag
             s.instance_id = inst
             s.turns.append(TurnRecord(list(prompt_ids), list(out), list(lps), list(vers)))
+            s.status = "env"                      # the environment acts before the next turn
+            self._schedule()
         return {"session_id": sid, "output_ids": out, "logprobs": lps, "version_tag": s.version_tag}
 
     def close(self, sid: str) -> dict:
         with self.lock:
             s = self.sessions.pop(sid)
+            self._schedule()                      # freed capacity may continue hung sessions
         smp = build_training_data(s.turns)
         return {"session_id": sid, "version_tag": s.version_tag, **asdict(smp)}
 
@@ -157,8 +187,18 @@ class LocalSessionClient:
         self.router = router
         self.sid = sid
 
-    def complete(self, prompt_ids: list[int], max_tokens: int) -> list[int]:
-        r = self.router.complete(self.sid, list(prompt_ids), int(max_tokens))
+    def complete(self, prompt_ids: list[int], max_tokens: int, wait_s: float = 600.0) -> list[int]:
+        """A hung session waits (polling, at most ``wait_s``) until the
+        scheduler continues it, as an HTTP client retrying on 409 would."""
+        import time
+        t0 = time.monotonic()
+        while True:
+            r = self.router.complete(self.sid, list(prompt_ids), int(max_tokens))
+            if r.get("status") != 409:
+                break
+            if time.monotonic() - t0 > wait_s:
+                raise TimeoutError(f"session {self.sid} stayed hung for {wait_s} s")
+            time.sleep(0.005)
         if "error" in r:
             raise RuntimeError(r["error"])
         return list(r["output_ids"])

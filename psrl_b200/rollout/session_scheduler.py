@@ -62,3 +62,14 @@ class ThunderAgentScheduler:
                 to_continue.append(s.session_id)
                 free -= need
         return [], to_continue
+
+
+def scheduler_from_cfg(cfg, capacity_tokens: int):
+    """The scheduler of ``psrl.rollout_coordination.session_strategy.thunder_agent``
+    (None unless enabled), for a pool whose KV cache holds ``capacity_tokens``
+    (the engines' blocks x block size)."""
+    ta = cfg.psrl.rollout_coordination.session_strategy.thunder_agent
+    if not bool(ta.get("enable", False)):
+        return None
+    return ThunderAgentScheduler(int(capacity_tokens), float(ta.get("env_token_weight", 1.0)),
+                                 int(ta.get("buffer_per_session", 100)))

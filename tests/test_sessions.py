@@ -70,3 +70,27 @@ def test_session_agent_loop_on_engines():
     trajs = SessionAgentLoop.to_trajectories(res, uid=3, request_id_base=30)
     assert len(trajs) == 2 and [t.request_id for t in trajs] == [30, 31]
     assert all(t.uid == 3 and t.response_len == 16 and len(t.rollout_logprobs) == 16 for t in trajs)
+
+
+def test_session_router_runs_the_capacity_scheduler():
+    """With a ThunderAgent scheduler in the router, a session over capacity is
+    hung at a turn boundary (its next turn answers 409), and closing another
+    session continues it; a local client waits through the hang."""
+    import threading
+    sch = ThunderAgentScheduler(capacity_tokens=50, env_token_weight=1.0, buffer_per_session=0)
+    r = SessionRouter(_gen, scheduler=sch)
+    r.complete("a", [1] * 20, 5)                       # a: 25 tokens, in env
+    r.complete("b", [1] * 20, 5)                       # b: 25 tokens -> 50 used, fits
+    out = r.complete("c", [1] * 10, 5)                 # c pushes the total over 50: an env session is hung
+    assert "output_ids" in out and r.sched_stats["hung"] >= 1
+    hung = [k for k, v in r.states().items() if v["hung"]]
+    assert hung
+    assert r.complete(hung[0], [1] * 30, 1).get("status") == 409
+    from psrl_b200.rollout.session_router import LocalSessionClient
+    got = {}
+    t = threading.Thread(target=lambda: got.update(ids=LocalSessionClient(r, hung[0]).complete([1] * 30, 1)))
+    t.start()
+    for k in [k for k in ("a", "b", "c") if k != hung[0]]:
+        r.close(k)                                     # frees capacity: the hung session continues
+    t.join(timeout=10)
+    assert got.get("ids") == [7] and r.sched_stats["continued"] >= 1
