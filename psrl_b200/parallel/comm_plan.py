@@ -73,6 +73,13 @@ def _row_bytes(shape: tuple, dim: int, itemsize: int) -> int:
     return inner * itemsize
 
 
+def least_loaded(cands: list[int], load: dict, link: dict | None = None) -> int:
+    """Sender for the next piece: the best link class first (NVLink before PCIe
+    before the network), then the fewest bytes assigned so far."""
+    link = link or {}
+    return min(cands, key=lambda c: (LINK_PRIORITY.get(link.get(c, "nvlink"), 9), load.get(c, 0), c))
+
+
 def plan_transfer(specs: list[TensorSpec], senders: dict[int, dict[str, Sharding]],
                   receiver: dict[str, Sharding], link: dict[int, str] | None = None) -> CommPlan:
     """Plan the segments one receiver must pull.
@@ -109,7 +116,8 @@ def plan_transfer(specs: list[TensorSpec], senders: dict[int, dict[str, Sharding
             if p * r.n // L != r.index:
                 continue                       # piece not owned by this receiver
             cands = [(sid, h) for sid, h in holders if h.n == 1 or p * h.n // L == h.index]
-            sid, h = min(cands, key=lambda c: (LINK_PRIORITY.get(link.get(c[0], "nvlink"), 9), load[c[0]], c[0]))
+            sid = least_loaded([c[0] for c in cands], load, link)
+            h = dict(cands)[sid]
             # piece p covers rows [p*piece, (p+1)*piece) along dim
             src_first = p * piece - (h.index * (extent // h.n) if h.n > 1 else 0)
             dst_first = p * piece - r.index * (extent // r.n)

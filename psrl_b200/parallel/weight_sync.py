@@ -160,7 +160,9 @@ class ShardedWeightPuller:
       column-parallel row ranges (q | k | v heads, gate | up halves) are
       contiguous blocks, row-parallel column ranges (O, down) are 2-D blocks
       with their own row strides (``models.converters.tp_slices`` gives the
-      pieces).  Replicated tensors come from any rank.
+      pieces).  Replicated tensors come from any rank.  Among the stores that
+    hold a piece, the comm plan's rule picks the sender (``comm_plan.least_loaded``:
+    best link, then fewest bytes so far).
 
     On CUDA the whole plan runs as ONE kernel (``copy_rows``: a device table of
     2-D byte blocks, 16-byte loads from the trainers' HBM over NVLink)."""
@@ -188,15 +190,18 @@ class ShardedWeightPuller:
                     shards.setdefault(en, {}).setdefault(int(d["tp_rank"]), []).append((j, int(off), tuple(shape)))
                 else:
                     whole.setdefault(en, []).append((j, int(off)))
-        blocks, turn = [], {}
+        from .comm_plan import least_loaded
+        blocks = []
+        load: dict[int, int] = {}          # bytes assigned to each store so far
+        link = {j: ("self" if d.get("device") == (dst_flat.device.index if self.gpu else None) else "nvlink")
+                for j, d in enumerate(descriptors)}
 
-        def pick(cands):
-            # rotate over the stores that hold the same set of tensors (a stage's or a
-            # TP rank's data-parallel replicas), so consecutive tensors use different links
-            key = tuple(c[0] for c in cands)
-            k = turn.get(key, 0)
-            turn[key] = k + 1
-            return cands[k % len(cands)]
+        def pick(cands, nbytes):
+            # the comm plan's rule: best link, then the least-loaded holder, so the
+            # egress of every trainer GPU holding a tensor is used evenly
+            j = least_loaded([c[0] for c in cands], load, link)
+            load[j] = load.get(j, 0) + nbytes
+            return next(c for c in cands if c[0] == j)
 
         for name, shape, off in layout.entries:
             n = 1
@@ -209,7 +214,7 @@ class ShardedWeightPuller:
                 full = tuple(shape)
                 cols = full[1] if len(full) > 1 else 1
                 for r in range(P):
-                    j, loff, lshape = pick(per[r])
+                    j, loff, lshape = pick(per[r], n * esz // P)
                     lcols = lshape[1] if len(lshape) > 1 else 1
                     acc = 0
                     for dim, start, length in tp_slices(name, full, args, r, P):
@@ -221,7 +226,7 @@ class ShardedWeightPuller:
                                            lcols * esz, cols * esz))
                         acc += length
             elif name in whole:
-                j, soff = pick(whole[name])
+                j, soff = pick(whole[name], n * esz)
                 blocks.append((j, soff * esz, dst0, 1, n * esz, 0, 0))
             else:
                 raise KeyError(f"no trainer store holds {name}")
