@@ -246,59 +246,70 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       fence_after();
       const int lim = row_pos + off - j * BKV;  // last key column of tile j this row sees
       const bool masked_tile = __any_sync(0xffffffffu, lim < BKV - 1);
-      // pass 1: row maximum of this key tile (scaled, base 2)
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(ts + c * 32, v);
-        tmem_wait_ld();
+      // the whole S row (128 fp32 columns) comes out of TMEM in four loads
+      // behind one wait and stays in registers for both passes
+      uint32_t v[128];
+      tmem_ld32(ts, v);
+      tmem_ld32(ts + 32, v + 32);
+      tmem_ld32(ts + 64, v + 64);
+      tmem_ld32(ts + 96, v + 96);
+      tmem_wait_ld();
+      if (masked_tile) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const bool dead = masked_tile && (c * 32 + i > lim);
-          mx = fmaxf(mx, dead ? -INFINITY : __uint_as_float(v[i]) * a.scale_log2);
-        }
+        for (int i = 0; i < 128; ++i)
+          if (i > lim) v[i] = 0xff800000u;  // -inf: key past this row's causal limit
       }
-      const float m_new = fmaxf(m, mx);
+      // pass 1: row maximum of the raw scores; the scale is positive, so it is
+      // applied once, to the maximum
+      float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int i = 0; i < 128; ++i) mq[i & 3] = fmaxf(mq[i & 3], __uint_as_float(v[i]));
+      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+      const float m_new = fmaxf(m, mx * a.scale_log2);
       // tcgen05.ld / st are warp-collective (.sync.aligned): the decision to
       // rescale O is taken for the whole warp, every lane moves to its m_new
       const bool grow = __any_sync(0xffffffffu, j > 0 && m != -INFINITY && m_new > m + RESCALE_LOG2);
+      float alpha = 1.f;
       if (j == 0 || (!grow && m == -INFINITY)) {
         m = m_new;
       } else if (grow) {
-        // grow the reference maximum: O (complete up to P_{j-1} V_{j-1}) and l by 2^(m - m_new)
-        const float alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld32(to + c * 32, v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-          tmem_st32(to + c * 32, v);
-        }
-        l *= alpha;
+        alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
         m = m_new;
       }
       const float ref = (m == -INFINITY) ? 0.f : m;
       // pass 2: P = 2^(x - ref) in bf16, packed two per column over S's first 64 columns
-#pragma unroll 1
+      float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t v[32], pk[16];
-        tmem_ld32(ts + c * 32, v);
-        tmem_wait_ld();
+        uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int c0 = c * 32 + 2 * i;
-          const float x0 = (masked_tile && c0 > lim) ? -INFINITY : __uint_as_float(v[2 * i]) * a.scale_log2;
-          const float x1 = (masked_tile && c0 + 1 > lim) ? -INFINITY : __uint_as_float(v[2 * i + 1]) * a.scale_log2;
-          const float p0 = ex2(x0 - ref), p1 = ex2(x1 - ref);
-          l += p0 + p1;
+          const float x0 = fmaf(__uint_as_float(v[c0]), a.scale_log2, -ref);
+          const float x1 = fmaf(__uint_as_float(v[c0 + 1]), a.scale_log2, -ref);
+          const float p0 = ex2(x0), p1 = ex2(x1);
+          ls0 += p0;
+          ls1 += p1;
           const bf162 pp = __floats2bfloat162_rn(p0, p1);
           pk[i] = *reinterpret_cast<const uint32_t*>(&pp);
         }
         tmem_st16(ts + c * 16, pk);
       }
+      if (grow) {
+        // grow the reference maximum: O (complete up to P_{j-1} V_{j-1}) and l by
+        // 2^(m_old - m_new); the PV MMA of tile j waits for this warp's arrive
+        // below, so nothing writes O meanwhile
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ov[32];
+          tmem_ld32(to + c * 32, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+          tmem_st32(to + c * 32, ov);
+        }
+      }
+      l = l * alpha + (ls0 + ls1);
       tmem_wait_st();
       fence_before();
       __syncwarp();
