@@ -391,6 +391,12 @@ struct BwdArgs {
   bf16* dkv;         // key / value-gradient rows (dkv_row apart), heads at dk_col / dv_col
   int64_t dkv_row;
   int dk_col, dv_col;
+  // dK/dV head split: hsplit CTAs share a key tile, each over nq / nkv / hsplit
+  // query heads; with hsplit > 1 they write fp32 partial sums, part[p][key row]
+  // [kv head][dK (unscaled) | dV], which fa_bwd_dkdv_reduce adds up
+  int hsplit;
+  float* part;
+  int64_t part_rows;
   int* err;
 };
 
@@ -408,6 +414,34 @@ __global__ void fa_bwd_dot(const bf16* __restrict__ o, const bf16* __restrict__ 
   for (int i = 0; i < 4; ++i) s += __bfloat162float(po[i]) * __bfloat162float(pd[i]);
   s = warp_sum(s);
   if (lane == 0) dd[(int64_t)h * T + t] = s;
+}
+
+// Adds the hsplit fp32 partial dK / dV rows of fa_bwd_dkdv and writes bf16
+// (dK times the softmax scale).  One thread per 8 columns of one key row and kv
+// head; rows outside every sequence (at or past cu_k[B]) are left alone.
+__global__ void fa_bwd_dkdv_reduce(const float* __restrict__ part, int hsplit, int64_t rows, int nkv,
+                                   const int* __restrict__ cu_k, int B, float scale, bf16* __restrict__ dkv,
+                                   int64_t dkv_row, int dk_col, int dv_col) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int per_row = nkv * 2 * D / 8;
+  const int64_t row = t / per_row;
+  if (row >= rows || row >= cu_k[B]) return;
+  const int c8 = (int)(t - row * per_row) * 8;  // column within [kv head][dK | dV]
+  const int hk = c8 / (2 * D), w = c8 - hk * 2 * D;
+  const bool is_k = w < D;
+  float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int p = 0; p < hsplit; ++p) {
+    const float4* src = reinterpret_cast<const float4*>(part + ((int64_t)p * rows + row) * (2 * nkv * D) + c8);
+    const float4 x = src[0], y = src[1];
+    f[0] += x.x; f[1] += x.y; f[2] += x.z; f[3] += x.w;
+    f[4] += y.x; f[5] += y.y; f[6] += y.z; f[7] += y.w;
+  }
+  if (is_k) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] *= scale;
+  }
+  bf16* dst = dkv + row * dkv_row + (is_k ? dk_col + hk * D + w : dv_col + hk * D + (w - D));
+  *reinterpret_cast<bf16x8*>(dst) = pack8(f);
 }
 
 // MMA of a 128 x 128 x 128 tile with both operands K-major in shared memory
@@ -432,16 +466,17 @@ __device__ __forceinline__ void mma_tile_ts(uint32_t d, uint32_t a_tmem, uint32_
 __global__ void __launch_bounds__(NT_BWD, 1)
     fa_bwd_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                 const __grid_constant__ CUtensorMap tm_do, BwdArgs a) {
-  const int hk = blockIdx.x, b = blockIdx.y, j = blockIdx.z;  // small j: most work, launched first
+  // small j: most work, launched first; the hsplit CTAs of one key tile are adjacent
+  const int hk = blockIdx.x, b = blockIdx.y, j = (int)blockIdx.z / a.hsplit, part = (int)blockIdx.z % a.hsplit;
   const int s0 = a.cu[b], L = a.cu[b + 1] - s0;
   const int sk0 = a.cu_k[b], Lk = a.cu_k[b + 1] - sk0;
   const int off = Lk - L;
   if (j * BKV >= Lk) return;
-  const int G = a.nq / a.nkv;
+  const int G = a.nq / a.nkv, Gc = G / a.hsplit;
   const int nqt = (L + BQ - 1) / BQ;
   const int i0 = max(0, j * BKV - off) / BQ;  // first query tile that sees key tile j
   const int per_head = nqt - i0;
-  const int iters = G * per_head;
+  const int iters = Gc * per_head;
   const int xk = a.k_col + hk * D, xv = a.v_col + hk * D;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -486,7 +521,7 @@ __global__ void __launch_bounds__(NT_BWD, 1)
       tma_load_2d(sv + ATOM, &tmKV, xv + 64, sk0 + j * BKV, bkv);
     }
     for (int it = 0; it < iters && !s_abort; ++it) {
-      const int hq = hk * G + it / per_head, i = i0 + it % per_head;
+      const int hq = hk * G + part * Gc + it / per_head, i = i0 + it % per_head;
       const int st = it % NS;
       const uint32_t ph = (it / NS) & 1;
       bool ok = true;
@@ -566,6 +601,9 @@ __global__ void __launch_bounds__(NT_BWD, 1)
       const float* lse_s = reinterpret_cast<const float*>(smem + OFF_B_STAGE + st * B_STAGE + 2 * KV_TILE);
       const float* dd_s = lse_s + BQ;
       const int key = j * BKV + r;
+      // every query of tile i is in the sequence and sees every key of tile j:
+      // no per-element mask
+      const bool full = (i + 1) * BQ <= L && (j + 1) * BKV - 1 <= i * BQ + off;
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
         const int col0 = half * 64 + c * 32;
@@ -573,22 +611,33 @@ __global__ void __launch_bounds__(NT_BWD, 1)
         tmem_ld32(tS + lane_off + col0, vs);
         tmem_ld32(tP2 + lane_off + col0, vp);
         tmem_wait_ld();
+        if (!full) {
+          // masked scores become -inf: P = 0 and dS = P (dP - D) = 0 (dP and D
+          // are finite; rows past the sequence were loaded as zeros)
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float pv[2], dv[2];
+          for (int e = 0; e < 32; ++e) {
+            const int q = i * BQ + col0 + e;
+            if (!(q < L && key <= q + off)) vs[e] = 0xff800000u;
+          }
+        }
+#pragma unroll
+        for (int e4 = 0; e4 < 8; ++e4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(lse_s + col0 + 4 * e4);
+          const float4 d4 = *reinterpret_cast<const float4*>(dd_s + col0 + 4 * e4);
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+          float pv[4], dv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            pv[u] = ex2(fmaf(__uint_as_float(vs[4 * e4 + u]), a.scale_log2, -lv[u]));
+            dv[u] = pv[u] * (__uint_as_float(vp[4 * e4 + u]) - dv4[u]);
+          }
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
-            const int cc = col0 + 2 * e + u;
-            const int q = i * BQ + cc;
-            const bool live = (q < L) && (key <= q + off);
-            const float p = live ? ex2(__uint_as_float(vs[2 * e + u]) * a.scale_log2 - lse_s[cc]) : 0.f;
-            pv[u] = p;
-            dv[u] = live ? p * (__uint_as_float(vp[2 * e + u]) - dd_s[cc]) : 0.f;
+            const bf162 pp = __floats2bfloat162_rn(pv[2 * u], pv[2 * u + 1]);
+            const bf162 dp = __floats2bfloat162_rn(dv[2 * u], dv[2 * u + 1]);
+            pk[2 * e4 + u] = *reinterpret_cast<const uint32_t*>(&pp);
+            dk[2 * e4 + u] = *reinterpret_cast<const uint32_t*>(&dp);
           }
-          const bf162 pp = __floats2bfloat162_rn(pv[0], pv[1]);
-          const bf162 dp = __floats2bfloat162_rn(dv[0], dv[1]);
-          pk[e] = *reinterpret_cast<const uint32_t*>(&pp);
-          dk[e] = *reinterpret_cast<const uint32_t*>(&dp);
         }
         tmem_st16(tS + lane_off + half * 64 + c * 16, pk);
         tmem_st16(tP2 + lane_off + half * 64 + c * 16, dk);
@@ -606,6 +655,7 @@ __global__ void __launch_bounds__(NT_BWD, 1)
       const bool valid = key < Lk;
       bf16* rowp = a.dkv + (int64_t)(sk0 + key) * a.dkv_row;
       const int ok_col = a.dk_col + hk * D, ov_col = a.dv_col + hk * D;
+      float* prow = a.part + ((int64_t)part * a.part_rows + sk0 + key) * (2 * a.nkv * D) + hk * 2 * D;
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
         const int col0 = half * 64 + c * 32;
@@ -613,7 +663,13 @@ __global__ void __launch_bounds__(NT_BWD, 1)
         tmem_ld32(tdV + lane_off + col0, vdv);
         tmem_ld32(tdK + lane_off + col0, vdk);
         tmem_wait_ld();
-        if (valid) {
+        if (valid && a.hsplit > 1) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            *reinterpret_cast<uint4*>(prow + col0 + e) = make_uint4(vdk[e], vdk[e + 1], vdk[e + 2], vdk[e + 3]);
+            *reinterpret_cast<uint4*>(prow + D + col0 + e) = make_uint4(vdv[e], vdv[e + 1], vdv[e + 2], vdv[e + 3]);
+          }
+        } else if (valid) {
           float f[32], g[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
@@ -748,6 +804,8 @@ __global__ void __launch_bounds__(NT_BWD, 1)
         break;
       }
       fence_after();
+      // every query of tile i is in the sequence and sees every key of tile jj
+      const bool full = (i + 1) * BQ <= L && (jj + 1) * BKV - 1 <= i * BQ + off;
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
         const int col0 = half * 64 + c * 32;
@@ -755,15 +813,21 @@ __global__ void __launch_bounds__(NT_BWD, 1)
         tmem_ld32(tS + lane_off + col0, vs);
         tmem_ld32(tP2 + lane_off + col0, vp);
         tmem_wait_ld();
+        if (!full) {
+          // masked scores become -inf, so P = 0 and dS = P (dP - D) = 0
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int key = jj * BKV + col0 + e;
+            if (!(qin && key <= q + off)) vs[e] = 0xff800000u;
+          }
+        }
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           float dv[2];
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
-            const int key = jj * BKV + col0 + 2 * e + u;
-            const bool live = qin && key <= q + off;
-            const float p = live ? ex2(__uint_as_float(vs[2 * e + u]) * a.scale_log2 - lse2) : 0.f;
-            dv[u] = live ? p * (__uint_as_float(vp[2 * e + u]) - dd) : 0.f;
+            const float p = ex2(fmaf(__uint_as_float(vs[2 * e + u]), a.scale_log2, -lse2));
+            dv[u] = p * (__uint_as_float(vp[2 * e + u]) - dd);
           }
           const bf162 dp = __floats2bfloat162_rn(dv[0], dv[1]);
           dk[e] = *reinterpret_cast<const uint32_t*>(&dp);
@@ -942,8 +1006,33 @@ static void bwd_launch(const at::Tensor& q, const at::Tensor& kv, const at::Tens
   ensure_smem_attr(fa_bwd_dkdv, SMEM_BWD);
   ensure_smem_attr(fa_bwd_dq, SMEM_BWD);
   const unsigned kz = (unsigned)((max_k + BKV - 1) / BKV);
-  fa_bwd_dkdv<<<dim3((unsigned)nkv, (unsigned)B, kz), NT_BWD, SMEM_BWD, stream()>>>(tq, tkv, tdo, a);
+  // Causal balance: the CTA of key tile 0 loops over every query tile of all
+  // G = nq / nkv heads, the last key tile over one.  Split the heads of each
+  // key tile over hsplit CTAs until the longest CTA holds at most half of an
+  // SM's average share (estimated for B sequences of the longest length),
+  // at the price of fp32 partials summed by a small second kernel.
+  const int G = (int)(nq / nkv);
+  const int64_t nqt = (max_q + BQ - 1) / BQ;
+  const int64_t total = (int64_t)B * nkv * G * nqt * (nqt + 1) / 2;
+  const int64_t share = total / std::max(1, num_sms());
+  int hsplit = 1;
+  while (hsplit < 4 && G % (2 * hsplit) == 0 && 2 * (int64_t)G * nqt / hsplit > share) hsplit *= 2;
+  a.hsplit = hsplit;
+  at::Tensor part;
+  if (hsplit > 1) {
+    part = at::empty({hsplit, kv.size(0), 2 * nkv * D}, q.options().dtype(at::kFloat));
+    a.part = part.data_ptr<float>();
+    a.part_rows = kv.size(0);
+  }
+  fa_bwd_dkdv<<<dim3((unsigned)nkv, (unsigned)B, kz * (unsigned)hsplit), NT_BWD, SMEM_BWD, stream()>>>(tq, tkv, tdo,
+                                                                                                       a);
   PSRL_CHECK_LAUNCH();
+  if (hsplit > 1) {
+    const int64_t threads = kv.size(0) * nkv * 2 * D / 8;
+    fa_bwd_dkdv_reduce<<<(unsigned)((threads + 255) / 256), 256, 0, stream()>>>(
+        a.part, hsplit, kv.size(0), (int)nkv, a.cu_k, B, a.scale, a.dkv, a.dkv_row, dk_col, dv_col);
+    PSRL_CHECK_LAUNCH();
+  }
   fa_bwd_dq<<<dim3((unsigned)nq, (unsigned)B, (unsigned)a.blocks_z), NT_BWD, SMEM_BWD, stream()>>>(tq, tkv, tdo, a);
   PSRL_CHECK_LAUNCH();
 }
