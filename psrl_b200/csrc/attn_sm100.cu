@@ -371,10 +371,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 // tile they were computed from, so no warp overwrites columns another warp
 // still reads.
 constexpr int NT_BWD = 320;
-constexpr int OFF_B_STAGE = 2 * KV_TILE;             // after the two resident tiles
-constexpr int B_STAGE = 2 * KV_TILE + 1024;          // two streamed tiles + 128 lse + 128 D (dK/dV kernel)
-constexpr int OFF_B_BAR = OFF_B_STAGE + NS * B_STAGE;
-constexpr int SMEM_BWD = OFF_B_BAR + 256 + 1024;
 
 struct BwdArgs {
   const int* cu;     // [B + 1] query rows
@@ -444,28 +440,31 @@ __global__ void fa_bwd_dkdv_reduce(const float* __restrict__ part, int hsplit, i
   *reinterpret_cast<bf16x8*>(dst) = pack8(f);
 }
 
-// MMA of a 128 x 128 x 128 tile with both operands K-major in shared memory
-// (two 64-wide swizzle atoms each).
-__device__ __forceinline__ void mma_tile_ss(uint32_t d, uint32_t sa, uint32_t sb, uint32_t idesc) {
-#pragma unroll
-  for (int k = 0; k < D / 16; ++k) {
-    const uint32_t off = (k >> 2) * ATOM + (k & 3) * 32;
-    mma_1cta(d, desc_sw128(sa + off, 16, 1024), desc_sw128(sb + off, 16, 1024), idesc, k > 0);
-  }
-}
-// D (+)= A (tensor memory, bf16 packed in columns [0, 32) and [64, 96)) x B
-// (MN-major tile in shared memory), K = 128.
-__device__ __forceinline__ void mma_tile_ts(uint32_t d, uint32_t a_tmem, uint32_t sb, uint32_t idesc, bool acc) {
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const uint32_t acol = (k < 4) ? k * 8 : 64 + (k - 4) * 8;
-    mma_1cta_ts(d, a_tmem + acol, desc_sw128(sb + k * 2048, ATOM, 1024), idesc, (acc || k > 0) ? 1u : 0u);
-  }
-}
+// dQ kernel tiles: 64 keys per step, so two S / dP buffers (64 TMEM columns
+// each) fit beside the 128-column dQ accumulator and the tensor core computes
+// S and dP of key tile jj+1 while the elementwise warps turn tile jj into dS.
+constexpr int BK2 = 64;
+constexpr int ATOM64 = 64 * 64 * 2;          // 64 rows x 64 bf16 (one 128-byte swizzle atom column)
+constexpr int KV64_TILE = 2 * ATOM64;        // 16 KB
+constexpr int NSQ = 4;                       // K/V ring depth of the dQ kernel
+constexpr int DQ_STAGE = 2 * KV64_TILE;      // K + V
+constexpr int OFF_DQ_KV = 2 * KV_TILE;       // after the resident Q and dO tiles
+constexpr int OFF_DQ_BAR = OFF_DQ_KV + NSQ * DQ_STAGE;
+constexpr int SMEM_DQ = OFF_DQ_BAR + 256 + 1024;
+
+// dK/dV kernel tiles: 64 queries per step, so two S^T / dP^T buffers (64 TMEM
+// columns each) fit beside the dV and dK accumulators and the tensor core
+// computes S^T and dP^T of step it+1 while the elementwise warps work on step it.
+constexpr int BQ2 = 64;
+constexpr int NSK = 4;                                  // Q / dO ring depth
+constexpr int DKV_STAGE = 2 * KV64_TILE + 1024;          // Q + dO (64 rows each) + 64 lse + 64 D, 1 KB aligned
+constexpr int OFF_DKV_STAGE = 2 * KV_TILE;               // after the resident K and V tiles
+constexpr int OFF_DKV_BAR = OFF_DKV_STAGE + NSK * DKV_STAGE;
+constexpr int SMEM_DKV = OFF_DKV_BAR + 256 + 1024;
 
 __global__ void __launch_bounds__(NT_BWD, 1)
-    fa_bwd_dkdv(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
-                const __grid_constant__ CUtensorMap tm_do, BwdArgs a) {
+    fa_bwd_dkdv(const __grid_constant__ CUtensorMap tmQ64, const __grid_constant__ CUtensorMap tmKV,
+                const __grid_constant__ CUtensorMap tm_do64, BwdArgs a) {
   // small j: most work, launched first; the hsplit CTAs of one key tile are adjacent
   const int hk = blockIdx.x, b = blockIdx.y, j = (int)blockIdx.z / a.hsplit, part = (int)blockIdx.z % a.hsplit;
   const int s0 = a.cu[b], L = a.cu[b + 1] - s0;
@@ -473,30 +472,33 @@ __global__ void __launch_bounds__(NT_BWD, 1)
   const int off = Lk - L;
   if (j * BKV >= Lk) return;
   const int G = a.nq / a.nkv, Gc = G / a.hsplit;
-  const int nqt = (L + BQ - 1) / BQ;
-  const int i0 = max(0, j * BKV - off) / BQ;  // first query tile that sees key tile j
+  const int nqt = (L + BQ2 - 1) / BQ2;
+  const int i0 = max(0, j * BKV - off) / BQ2;  // first 64-row query tile that sees key tile j
   const int per_head = nqt - i0;
   const int iters = Gc * per_head;
   const int xk = a.k_col + hk * D, xv = a.v_col + hk * D;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_B_BAR);
-  // kv_full, st_full[NS] (count 2: TMA bytes + the lse/D copy), st_empty[NS], s_full, p_full, done
-  const uint32_t bkv = smem_u32(bars), bsf0 = bkv + 8, bse0 = bsf0 + 8 * NS, bs = bse0 + 8 * NS, bp = bs + 8,
-                 bdone = bp + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 2 * NS + 3);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_DKV_BAR);
+  // kv_full, st_full[NSK] (count 2: TMA bytes + the lse/D copy), st_empty[NSK],
+  // s_full[2], p_full[2], done; then the TMEM slot
+  const uint32_t bkv = smem_u32(bars), bsf0 = bkv + 8, bse0 = bsf0 + 8 * NSK, bs0 = bse0 + 8 * NSK, bp0 = bs0 + 16,
+                 bdone = bp0 + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 2 * NSK + 5);
   __shared__ volatile int s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     s_abort = 0;
     mbar_init(bkv, 1);
-    for (int i = 0; i < NS; ++i) {
-      mbar_init(bsf0 + 8 * i, 2);
-      mbar_init(bse0 + 8 * i, 1);
+    for (int k = 0; k < NSK; ++k) {
+      mbar_init(bsf0 + 8 * k, 2);
+      mbar_init(bse0 + 8 * k, 1);
     }
-    mbar_init(bs, 1);
-    mbar_init(bp, 8);
+    for (int k = 0; k < 2; ++k) {
+      mbar_init(bs0 + 8 * k, 1);
+      mbar_init(bp0 + 8 * k, 8);  // one arrive per elementwise warp
+    }
     mbar_init(bdone, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -505,15 +507,18 @@ __global__ void __launch_bounds__(NT_BWD, 1)
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tP2 = tmem + 128, tdV = tmem + 256, tdK = tmem + 384;
+  // TMEM columns: S^T_0 0..63, dP^T_0 64..127, S^T_1 128..191, dP^T_1 192..255, dV 256..383, dK 384..511
+  auto tS = [&](int bb) { return tmem + 128u * (uint32_t)bb; };
+  auto tP = [&](int bb) { return tmem + 128u * (uint32_t)bb + 64u; };
+  const uint32_t tdV = tmem + 256, tdK = tmem + 384;
 
   if (warp == 0) {
-    // producer: K_j, V_j once; then per iteration Q_i, dO_i (TMA) and lse_i, D_i (warp copy)
+    // producer: K_j, V_j once; then per step Q, dO (64 rows, TMA) and lse, D (warp copy)
     const uint32_t sk = smem_u32(smem), sv = sk + KV_TILE;
     if (lane == 0) {
-      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmQ64);
       tma_prefetch_desc(&tmKV);
-      tma_prefetch_desc(&tm_do);
+      tma_prefetch_desc(&tm_do64);
       mbar_expect_tx(bkv, 2 * KV_TILE);
       tma_load_2d(sk, &tmKV, xk, sk0 + j * BKV, bkv);
       tma_load_2d(sk + ATOM, &tmKV, xk + 64, sk0 + j * BKV, bkv);
@@ -522,8 +527,8 @@ __global__ void __launch_bounds__(NT_BWD, 1)
     }
     for (int it = 0; it < iters && !s_abort; ++it) {
       const int hq = hk * G + part * Gc + it / per_head, i = i0 + it % per_head;
-      const int st = it % NS;
-      const uint32_t ph = (it / NS) & 1;
+      const int st = it % NSK;
+      const uint32_t ph = (it / NSK) & 1;
       bool ok = true;
       if (lane == 0) ok = mbar_wait(bse0 + 8 * st, ph ^ 1);
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -534,22 +539,22 @@ __global__ void __launch_bounds__(NT_BWD, 1)
         }
         break;
       }
-      uint8_t* stg = smem + OFF_B_STAGE + st * B_STAGE;
-      const uint32_t sq = smem_u32(stg), sdo = sq + KV_TILE;
+      uint8_t* stg = smem + OFF_DKV_STAGE + st * DKV_STAGE;
+      const uint32_t sq = smem_u32(stg), sdo = sq + KV64_TILE;
       const uint32_t fb = bsf0 + 8 * st;
       if (lane == 0) {
-        mbar_expect_tx(fb, 2 * KV_TILE);
-        const int y = s0 + i * BQ;
-        tma_load_2d(sq, &tmQ, a.q_col + hq * D, y, fb);
-        tma_load_2d(sq + ATOM, &tmQ, a.q_col + hq * D + 64, y, fb);
-        tma_load_2d(sdo, &tm_do, hq * D, y, fb);
-        tma_load_2d(sdo + ATOM, &tm_do, hq * D + 64, y, fb);
+        mbar_expect_tx(fb, 2 * KV64_TILE);
+        const int y = s0 + i * BQ2;
+        tma_load_2d(sq, &tmQ64, a.q_col + hq * D, y, fb);
+        tma_load_2d(sq + ATOM64, &tmQ64, a.q_col + hq * D + 64, y, fb);
+        tma_load_2d(sdo, &tm_do64, hq * D, y, fb);
+        tma_load_2d(sdo + ATOM64, &tm_do64, hq * D + 64, y, fb);
       }
-      float* lse_s = reinterpret_cast<float*>(stg + 2 * KV_TILE);
-      float* dd_s = lse_s + BQ;
+      float* lse_s = reinterpret_cast<float*>(stg + 2 * KV64_TILE);
+      float* dd_s = lse_s + BQ2;
 #pragma unroll
-      for (int c = lane; c < BQ; c += 32) {
-        const int q = i * BQ + c;
+      for (int c = lane; c < BQ2; c += 32) {
+        const int q = i * BQ2 + c;
         const bool in = q < L;
         lse_s[c] = in ? a.lse[(int64_t)hq * a.T + s0 + q] * 1.4426950408889634f : 0.f;
         dd_s[c] = in ? a.dd[(int64_t)hq * a.T + s0 + q] : 0.f;
@@ -559,93 +564,128 @@ __global__ void __launch_bounds__(NT_BWD, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t id_ss = idesc_bf16_f32(BKV, BQ, false, false);  // M = keys, N = queries
-      constexpr uint32_t id_ts = idesc_bf16_f32(BKV, D, false, true);    // M = keys, N = d
+      constexpr uint32_t id_ss = idesc_bf16_f32(BKV, BQ2, false, false);  // M = keys, N = 64 queries
+      constexpr uint32_t id_ts = idesc_bf16_f32(BKV, D, false, true);     // M = keys, N = d, K = 64 queries
       const uint32_t sk = smem_u32(smem), sv = sk + KV_TILE;
+      // S^T = K Q^T and dP^T = V dO^T of step it into buffer it & 1
+      auto issue_s = [&](int it) -> bool {
+        const int st = it % NSK;
+        if (!mbar_wait(bsf0 + 8 * st, (it / NSK) & 1)) return false;
+        fence_after();
+        const uint32_t sq = smem_u32(smem + OFF_DKV_STAGE + st * DKV_STAGE), sdo = sq + KV64_TILE;
+        const int bb = it & 1;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t oa = (k >> 2) * ATOM + (k & 3) * 32, ob = (k >> 2) * ATOM64 + (k & 3) * 32;
+          mma_1cta(tS(bb), desc_sw128(sk + oa, 16, 1024), desc_sw128(sq + ob, 16, 1024), id_ss, k > 0);
+        }
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t oa = (k >> 2) * ATOM + (k & 3) * 32, ob = (k >> 2) * ATOM64 + (k & 3) * 32;
+          mma_1cta(tP(bb), desc_sw128(sv + oa, 16, 1024), desc_sw128(sdo + ob, 16, 1024), id_ss, k > 0);
+        }
+        commit_1cta(bs0 + 8 * bb);
+        return true;
+      };
       bool ok = mbar_wait(bkv, 0);
+      int where = 0;
+      if (ok && iters > 0) {
+        ok = issue_s(0);
+        where = 1;
+      }
       for (int it = 0; it < iters && ok && !s_abort; ++it) {
-        const int st = it % NS;
-        const uint32_t ph = (it / NS) & 1;
-        if (!mbar_wait(bsf0 + 8 * st, ph)) { ok = false; break; }
+        // buffer (it + 1) & 1 was last read by the dV / dK MMAs of step it - 1,
+        // issued before (tcgen05 MMAs of one thread run in order)
+        if (it + 1 < iters && !issue_s(it + 1)) {
+          ok = false;
+          where = 2 + 10 * it;
+          break;
+        }
+        const int bb = it & 1;
+        if (!mbar_wait(bp0 + 8 * bb, (it >> 1) & 1)) {
+          ok = false;
+          where = 3 + 10 * it;
+          break;
+        }
         fence_after();
-        const uint32_t sq = smem_u32(smem + OFF_B_STAGE + st * B_STAGE), sdo = sq + KV_TILE;
-        mma_tile_ss(tS, sk, sq, id_ss);    // S^T = K Q^T
-        mma_tile_ss(tP2, sv, sdo, id_ss);  // dP^T = V dO^T
-        commit_1cta(bs);
-        if (!mbar_wait(bp, it & 1)) { ok = false; break; }
-        fence_after();
-        mma_tile_ts(tdV, tS, sdo, id_ts, it > 0);   // dV += P^T dO
-        mma_tile_ts(tdK, tP2, sq, id_ts, it > 0);   // dK += dS^T Q
-        commit_1cta(bse0 + 8 * st);
+        const int st = it % NSK;
+        const uint32_t sq = smem_u32(smem + OFF_DKV_STAGE + st * DKV_STAGE), sdo = sq + KV64_TILE;
+        // P^T and dS^T (bf16) sit packed in columns [0, 16) and [32, 48) of S^T_bb and dP^T_bb
+#pragma unroll
+        for (int k = 0; k < BQ2 / 16; ++k) {
+          const uint32_t acol = (k < 2) ? k * 8 : 32 + (k - 2) * 8;
+          const uint32_t acc = (it > 0 || k > 0) ? 1u : 0u;
+          mma_1cta_ts(tdV, tS(bb) + acol, desc_sw128(sdo + k * 2048, ATOM64, 1024), id_ts, acc);  // dV += P^T dO
+          mma_1cta_ts(tdK, tP(bb) + acol, desc_sw128(sq + k * 2048, ATOM64, 1024), id_ts, acc);   // dK += dS^T Q
+        }
+        commit_1cta(bse0 + 8 * st);  // Q / dO of this step no longer read
       }
       if (!ok) {
-        set_err(a.err, 22);
+        set_err(a.err, 22, where);
         s_abort = 1;
       }
       commit_1cta(bdone);
     }
   } else {
-    // softmax-gradient warps: thread = key row r, half = which 64 queries
+    // elementwise warps: thread = key row r, half = which 32 of the step's 64 queries
     const int quad = warp & 3, half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const int key = j * BKV + r;
+    const int col0 = half * 32;
     bool ok = true;
     for (int it = 0; it < iters; ++it) {
       const int i = i0 + it % per_head;
-      const int st = it % NS;
-      if (!mbar_wait(bs, it & 1) || s_abort) {
+      const int st = it % NSK, bb = it & 1;
+      if (!mbar_wait(bs0 + 8 * bb, (it >> 1) & 1) || s_abort) {
         ok = false;
         break;
       }
       fence_after();
-      const float* lse_s = reinterpret_cast<const float*>(smem + OFF_B_STAGE + st * B_STAGE + 2 * KV_TILE);
-      const float* dd_s = lse_s + BQ;
-      const int key = j * BKV + r;
+      const float* lse_s = reinterpret_cast<const float*>(smem + OFF_DKV_STAGE + st * DKV_STAGE + 2 * KV64_TILE);
+      const float* dd_s = lse_s + BQ2;
       // every query of tile i is in the sequence and sees every key of tile j:
       // no per-element mask
-      const bool full = (i + 1) * BQ <= L && (j + 1) * BKV - 1 <= i * BQ + off;
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        const int col0 = half * 64 + c * 32;
-        uint32_t vs[32], vp[32], pk[16], dk[16];
-        tmem_ld32(tS + lane_off + col0, vs);
-        tmem_ld32(tP2 + lane_off + col0, vp);
-        tmem_wait_ld();
-        if (!full) {
-          // masked scores become -inf: P = 0 and dS = P (dP - D) = 0 (dP and D
-          // are finite; rows past the sequence were loaded as zeros)
+      const bool full = (i + 1) * BQ2 <= L && (j + 1) * BKV - 1 <= i * BQ2 + off;
+      uint32_t vs[32], vp[32], pk[16], dk[16];
+      tmem_ld32(tS(bb) + lane_off + col0, vs);
+      tmem_ld32(tP(bb) + lane_off + col0, vp);
+      tmem_wait_ld();
+      if (!full) {
+        // masked scores become -inf: P = 0 and dS = P (dP - D) = 0 (dP and D
+        // are finite; rows past the sequence were loaded as zeros)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int q = i * BQ + col0 + e;
-            if (!(q < L && key <= q + off)) vs[e] = 0xff800000u;
-          }
+        for (int e = 0; e < 32; ++e) {
+          const int q = i * BQ2 + col0 + e;
+          if (!(q < L && key <= q + off)) vs[e] = 0xff800000u;
         }
-#pragma unroll
-        for (int e4 = 0; e4 < 8; ++e4) {
-          const float4 l4 = *reinterpret_cast<const float4*>(lse_s + col0 + 4 * e4);
-          const float4 d4 = *reinterpret_cast<const float4*>(dd_s + col0 + 4 * e4);
-          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
-          float pv[4], dv[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            pv[u] = ex2(fmaf(__uint_as_float(vs[4 * e4 + u]), a.scale_log2, -lv[u]));
-            dv[u] = pv[u] * (__uint_as_float(vp[4 * e4 + u]) - dv4[u]);
-          }
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const bf162 pp = __floats2bfloat162_rn(pv[2 * u], pv[2 * u + 1]);
-            const bf162 dp = __floats2bfloat162_rn(dv[2 * u], dv[2 * u + 1]);
-            pk[2 * e4 + u] = *reinterpret_cast<const uint32_t*>(&pp);
-            dk[2 * e4 + u] = *reinterpret_cast<const uint32_t*>(&dp);
-          }
-        }
-        tmem_st16(tS + lane_off + half * 64 + c * 16, pk);
-        tmem_st16(tP2 + lane_off + half * 64 + c * 16, dk);
       }
+#pragma unroll
+      for (int e4 = 0; e4 < 8; ++e4) {
+        const float4 l4 = *reinterpret_cast<const float4*>(lse_s + col0 + 4 * e4);
+        const float4 d4 = *reinterpret_cast<const float4*>(dd_s + col0 + 4 * e4);
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+        float pv[4], dv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          pv[u] = ex2(fmaf(__uint_as_float(vs[4 * e4 + u]), a.scale_log2, -lv[u]));
+          dv[u] = pv[u] * (__uint_as_float(vp[4 * e4 + u]) - dv4[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const bf162 pp = __floats2bfloat162_rn(pv[2 * u], pv[2 * u + 1]);
+          const bf162 dp = __floats2bfloat162_rn(dv[2 * u], dv[2 * u + 1]);
+          pk[2 * e4 + u] = *reinterpret_cast<const uint32_t*>(&pp);
+          dk[2 * e4 + u] = *reinterpret_cast<const uint32_t*>(&dp);
+        }
+      }
+      // P^T and dS^T of this half's 32 queries, packed into the first 16 of the 32 columns it read
+      tmem_st16(tS(bb) + lane_off + col0, pk);
+      tmem_st16(tP(bb) + lane_off + col0, dk);
       tmem_wait_st();
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bp);
+      if (lane == 0) mbar_arrive(bp0 + 8 * bb);
     }
     // epilogue: dV and dK (x scale) rows of this thread's key, half the columns each
     if (!mbar_wait(bdone, 0)) ok = false;
@@ -695,8 +735,9 @@ __global__ void __launch_bounds__(NT_BWD, 1)
   }
 }
 
+
 __global__ void __launch_bounds__(NT_BWD, 1)
-    fa_bwd_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
+    fa_bwd_dq(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV64,
               const __grid_constant__ CUtensorMap tm_do, BwdArgs a) {
   const int h = blockIdx.x, b = blockIdx.y;
   const int i = a.blocks_z - 1 - (int)blockIdx.z;  // large query tiles (most key tiles) first
@@ -704,27 +745,30 @@ __global__ void __launch_bounds__(NT_BWD, 1)
   const int sk0 = a.cu_k[b], Lk = a.cu_k[b + 1] - sk0;
   const int off = Lk - L;
   if (i * BQ >= L) return;
-  const int n = min((Lk + BKV - 1) / BKV, (min((i + 1) * BQ, L) - 1 + off) / BKV + 1);
+  const int n = min((Lk + BK2 - 1) / BK2, (min((i + 1) * BQ, L) - 1 + off) / BK2 + 1);
   const int hk = h / (a.nq / a.nkv);
   const int xk = a.k_col + hk * D, xv = a.v_col + hk * D;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_B_BAR);
-  const uint32_t bqd = smem_u32(bars), bkf0 = bqd + 8, bke0 = bkf0 + 8 * NS, bs = bke0 + 8 * NS, bp = bs + 8,
-                 bdone = bp + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 2 * NS + 3);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_DQ_BAR);
+  // q_full, kv_full[NSQ], kv_empty[NSQ], s_full[2], ds_full[2], done; then the TMEM slot
+  const uint32_t bqd = smem_u32(bars), bkf0 = bqd + 8, bke0 = bkf0 + 8 * NSQ, bs0 = bke0 + 8 * NSQ, bp0 = bs0 + 16,
+                 bdone = bp0 + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 1 + 2 * NSQ + 5);
   __shared__ volatile int s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     s_abort = 0;
     mbar_init(bqd, 1);
-    for (int k = 0; k < NS; ++k) {
+    for (int k = 0; k < NSQ; ++k) {
       mbar_init(bkf0 + 8 * k, 1);
       mbar_init(bke0 + 8 * k, 1);
     }
-    mbar_init(bs, 1);
-    mbar_init(bp, 8);
+    for (int k = 0; k < 2; ++k) {
+      mbar_init(bs0 + 8 * k, 1);
+      mbar_init(bp0 + 8 * k, 8);  // one arrive per elementwise warp
+    }
     mbar_init(bdone, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -733,13 +777,16 @@ __global__ void __launch_bounds__(NT_BWD, 1)
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tP2 = tmem + 128, tdQ = tmem + 256;
+  // TMEM columns: S_0 0..63, dP_0 64..127, S_1 128..191, dP_1 192..255, dQ 256..383
+  auto tS = [&](int bb) { return tmem + 128u * (uint32_t)bb; };
+  auto tP = [&](int bb) { return tmem + 128u * (uint32_t)bb + 64u; };
+  const uint32_t tdQ = tmem + 256;
   const uint32_t sq = smem_u32(smem), sdo = sq + KV_TILE;
 
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmKV);
+      tma_prefetch_desc(&tmKV64);
       tma_prefetch_desc(&tm_do);
       mbar_expect_tx(bqd, 2 * KV_TILE);
       const int y = s0 + i * BQ;
@@ -748,48 +795,85 @@ __global__ void __launch_bounds__(NT_BWD, 1)
       tma_load_2d(sdo, &tm_do, h * D, y, bqd);
       tma_load_2d(sdo + ATOM, &tm_do, h * D + 64, y, bqd);
       for (int jj = 0; jj < n && !s_abort; ++jj) {
-        const int st = jj % NS;
-        const uint32_t ph = (jj / NS) & 1;
+        const int st = jj % NSQ;
+        const uint32_t ph = (jj / NSQ) & 1;
         if (!mbar_wait(bke0 + 8 * st, ph ^ 1)) {
           set_err(a.err, 31);
           s_abort = 1;
           break;
         }
         const uint32_t fb = bkf0 + 8 * st;
-        mbar_expect_tx(fb, 2 * KV_TILE);
-        const uint32_t sk = smem_u32(smem + OFF_B_STAGE + st * B_STAGE), sv = sk + KV_TILE;
-        const int y2 = sk0 + jj * BKV;
-        tma_load_2d(sk, &tmKV, xk, y2, fb);
-        tma_load_2d(sk + ATOM, &tmKV, xk + 64, y2, fb);
-        tma_load_2d(sv, &tmKV, xv, y2, fb);
-        tma_load_2d(sv + ATOM, &tmKV, xv + 64, y2, fb);
+        mbar_expect_tx(fb, DQ_STAGE);
+        const uint32_t sk = smem_u32(smem + OFF_DQ_KV + st * DQ_STAGE), sv = sk + KV64_TILE;
+        const int y2 = sk0 + jj * BK2;
+        tma_load_2d(sk, &tmKV64, xk, y2, fb);
+        tma_load_2d(sk + ATOM64, &tmKV64, xk + 64, y2, fb);
+        tma_load_2d(sv, &tmKV64, xv, y2, fb);
+        tma_load_2d(sv + ATOM64, &tmKV64, xv + 64, y2, fb);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t id_ss = idesc_bf16_f32(BQ, BKV, false, false);
-      constexpr uint32_t id_ts = idesc_bf16_f32(BQ, D, false, true);
+      constexpr uint32_t id_s = idesc_bf16_f32(BQ, BK2, false, false);  // M = queries, N = 64 keys
+      constexpr uint32_t id_dq = idesc_bf16_f32(BQ, D, false, true);    // M = queries, N = d, K = 64 keys
+      // S = Q K^T and dP = dO V^T of key tile jj into buffer jj & 1
+      auto issue_sdp = [&](int jj) -> bool {
+        const int st = jj % NSQ;
+        if (!mbar_wait(bkf0 + 8 * st, (jj / NSQ) & 1)) return false;
+        fence_after();
+        const uint32_t sk = smem_u32(smem + OFF_DQ_KV + st * DQ_STAGE), sv = sk + KV64_TILE;
+        const int bb = jj & 1;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t oa = (k >> 2) * ATOM + (k & 3) * 32, ob = (k >> 2) * ATOM64 + (k & 3) * 32;
+          mma_1cta(tS(bb), desc_sw128(sq + oa, 16, 1024), desc_sw128(sk + ob, 16, 1024), id_s, k > 0);
+        }
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t oa = (k >> 2) * ATOM + (k & 3) * 32, ob = (k >> 2) * ATOM64 + (k & 3) * 32;
+          mma_1cta(tP(bb), desc_sw128(sdo + oa, 16, 1024), desc_sw128(sv + ob, 16, 1024), id_s, k > 0);
+        }
+        commit_1cta(bs0 + 8 * bb);
+        return true;
+      };
       bool ok = mbar_wait(bqd, 0);
+      int where = 0;
+      if (ok && n > 0) {
+        ok = issue_sdp(0);
+        where = 1;
+      }
       for (int jj = 0; jj < n && ok && !s_abort; ++jj) {
-        const int st = jj % NS;
-        if (!mbar_wait(bkf0 + 8 * st, (jj / NS) & 1)) { ok = false; break; }
+        // buffer (jj + 1) & 1 was last read by dQ of tile jj - 1, issued before
+        // (tcgen05 MMAs of one thread run in order)
+        if (jj + 1 < n && !issue_sdp(jj + 1)) {
+          ok = false;
+          where = 2 + 10 * jj;
+          break;
+        }
+        const int bb = jj & 1;
+        if (!mbar_wait(bp0 + 8 * bb, (jj >> 1) & 1)) {
+          ok = false;
+          where = 3 + 10 * jj;
+          break;
+        }
         fence_after();
-        const uint32_t sk = smem_u32(smem + OFF_B_STAGE + st * B_STAGE), sv = sk + KV_TILE;
-        mma_tile_ss(tS, sq, sk, id_ss);    // S = Q K^T
-        mma_tile_ss(tP2, sdo, sv, id_ss);  // dP = dO V^T
-        commit_1cta(bs);
-        if (!mbar_wait(bp, jj & 1)) { ok = false; break; }
-        fence_after();
-        mma_tile_ts(tdQ, tS, sk, id_ts, jj > 0);  // dQ += dS K
-        commit_1cta(bke0 + 8 * st);
+        const uint32_t sk = smem_u32(smem + OFF_DQ_KV + (jj % NSQ) * DQ_STAGE);
+        // dQ += dS K: dS (bf16) sits packed in columns [0, 16) and [32, 48) of S_bb
+#pragma unroll
+        for (int k = 0; k < BK2 / 16; ++k) {
+          const uint32_t acol = (k < 2) ? k * 8 : 32 + (k - 2) * 8;
+          mma_1cta_ts(tdQ, tS(bb) + acol, desc_sw128(sk + k * 2048, ATOM64, 1024), id_dq, (jj > 0 || k > 0) ? 1u : 0u);
+        }
+        commit_1cta(bke0 + 8 * (jj % NSQ));  // K_jj / V_jj no longer read
       }
       if (!ok) {
-        set_err(a.err, 32);
+        set_err(a.err, 32, where);
         s_abort = 1;
       }
       commit_1cta(bdone);
     }
   } else {
+    // elementwise warps: thread = query row r, half = which 32 of the tile's 64 keys
     const int quad = warp & 3, half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
     const int q = i * BQ + r;
@@ -797,47 +881,46 @@ __global__ void __launch_bounds__(NT_BWD, 1)
     const bool qin = q < L;
     const float lse2 = qin ? a.lse[(int64_t)h * a.T + s0 + q] * 1.4426950408889634f : 0.f;
     const float dd = qin ? a.dd[(int64_t)h * a.T + s0 + q] : 0.f;
+    const int col0 = half * 32;
     bool ok = true;
     for (int jj = 0; jj < n; ++jj) {
-      if (!mbar_wait(bs, jj & 1) || s_abort) {
+      const int bb = jj & 1;
+      if (!mbar_wait(bs0 + 8 * bb, (jj >> 1) & 1) || s_abort) {
         ok = false;
         break;
       }
       fence_after();
       // every query of tile i is in the sequence and sees every key of tile jj
-      const bool full = (i + 1) * BQ <= L && (jj + 1) * BKV - 1 <= i * BQ + off;
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        const int col0 = half * 64 + c * 32;
-        uint32_t vs[32], vp[32], dk[16];
-        tmem_ld32(tS + lane_off + col0, vs);
-        tmem_ld32(tP2 + lane_off + col0, vp);
-        tmem_wait_ld();
-        if (!full) {
-          // masked scores become -inf, so P = 0 and dS = P (dP - D) = 0
+      const bool full = (i + 1) * BQ <= L && (jj + 1) * BK2 - 1 <= i * BQ + off;
+      uint32_t vs[32], vp[32], dk[16];
+      tmem_ld32(tS(bb) + lane_off + col0, vs);
+      tmem_ld32(tP(bb) + lane_off + col0, vp);
+      tmem_wait_ld();
+      if (!full) {
+        // masked scores become -inf, so P = 0 and dS = P (dP - D) = 0
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int key = jj * BKV + col0 + e;
-            if (!(qin && key <= q + off)) vs[e] = 0xff800000u;
-          }
+        for (int e = 0; e < 32; ++e) {
+          const int key = jj * BK2 + col0 + e;
+          if (!(qin && key <= q + off)) vs[e] = 0xff800000u;
         }
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float dv[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const float p = ex2(fmaf(__uint_as_float(vs[2 * e + u]), a.scale_log2, -lse2));
-            dv[u] = p * (__uint_as_float(vp[2 * e + u]) - dd);
-          }
-          const bf162 dp = __floats2bfloat162_rn(dv[0], dv[1]);
-          dk[e] = *reinterpret_cast<const uint32_t*>(&dp);
-        }
-        tmem_st16(tS + lane_off + half * 64 + c * 16, dk);
       }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        float dv[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const float p = ex2(fmaf(__uint_as_float(vs[2 * e + u]), a.scale_log2, -lse2));
+          dv[u] = p * (__uint_as_float(vp[2 * e + u]) - dd);
+        }
+        const bf162 dp = __floats2bfloat162_rn(dv[0], dv[1]);
+        dk[e] = *reinterpret_cast<const uint32_t*>(&dp);
+      }
+      // dS of this half's 32 keys, packed into the first 16 of the 32 columns it read
+      tmem_st16(tS(bb) + lane_off + col0, dk);
       tmem_wait_st();
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bp);
+      if (lane == 0) mbar_arrive(bp0 + 8 * bb);
     }
     if (!mbar_wait(bdone, 0)) ok = false;
     fence_after();
@@ -845,16 +928,16 @@ __global__ void __launch_bounds__(NT_BWD, 1)
       bf16* rowp = a.dq + (int64_t)(s0 + q) * a.dq_row + a.dq_col + (int64_t)h * D;
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
-        const int col0 = half * 64 + c * 32;
+        const int dc = half * 64 + c * 32;
         uint32_t v[32];
-        tmem_ld32(tdQ + lane_off + col0, v);
+        tmem_ld32(tdQ + lane_off + dc, v);
         tmem_wait_ld();
         if (qin) {
           float f[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(v[e]) * a.scale;
 #pragma unroll
-          for (int e = 0; e < 32; e += 8) *reinterpret_cast<bf16x8*>(rowp + col0 + e) = pack8(f + e);
+          for (int e = 0; e < 32; e += 8) *reinterpret_cast<bf16x8*>(rowp + dc + e) = pack8(f + e);
         }
       }
     } else {
@@ -873,14 +956,14 @@ __global__ void __launch_bounds__(NT_BWD, 1)
 
 using namespace fa5;
 
-static CUtensorMap map_rows_64x128(const at::Tensor& t) {
+static CUtensorMap map_rows_64xR(const at::Tensor& t, uint32_t rows) {
   TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1 && (t.stride(0) * 2) % 16 == 0 &&
                   reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
               "operand rows must start on 16-byte boundaries with unit inner stride");
   CUtensorMap m;
   cuuint64_t dims[2] = {(cuuint64_t)t.size(1), (cuuint64_t)t.size(0)};
   cuuint64_t strides[1] = {(cuuint64_t)t.stride(0) * 2};
-  cuuint32_t box[2] = {64u, 128u};
+  cuuint32_t box[2] = {64u, rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = PSRL_DRV(cuTensorMapEncodeTiled)(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, t.data_ptr(), dims, strides,
                                                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -888,6 +971,7 @@ static CUtensorMap map_rows_64x128(const at::Tensor& t) {
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (", (int)r, ")");
   return m;
 }
+static CUtensorMap map_rows_64x128(const at::Tensor& t) { return map_rows_64xR(t, 128u); }
 
 // Shared launcher: queries in q (columns q_col + h * 128), keys and values in
 // kv (k_col / v_col + hk * 128); sequence b's query rows [cu_q[b], cu_q[b+1])
@@ -1003,8 +1087,8 @@ static void bwd_launch(const at::Tensor& q, const at::Tensor& kv, const at::Tens
   a.dk_col = dk_col;
   a.dv_col = dv_col;
   a.err = err.data_ptr<int>();
-  ensure_smem_attr(fa_bwd_dkdv, SMEM_BWD);
-  ensure_smem_attr(fa_bwd_dq, SMEM_BWD);
+  ensure_smem_attr(fa_bwd_dkdv, SMEM_DKV);
+  ensure_smem_attr(fa_bwd_dq, SMEM_DQ);
   const unsigned kz = (unsigned)((max_k + BKV - 1) / BKV);
   // Causal balance: the CTA of key tile 0 loops over every query tile of all
   // G = nq / nkv heads, the last key tile over one.  Split the heads of each
@@ -1024,8 +1108,9 @@ static void bwd_launch(const at::Tensor& q, const at::Tensor& kv, const at::Tens
     a.part = part.data_ptr<float>();
     a.part_rows = kv.size(0);
   }
-  fa_bwd_dkdv<<<dim3((unsigned)nkv, (unsigned)B, kz * (unsigned)hsplit), NT_BWD, SMEM_BWD, stream()>>>(tq, tkv, tdo,
-                                                                                                       a);
+  const CUtensorMap tq64 = map_rows_64xR(q, 64u), tdo64 = map_rows_64xR(dout.view({T, nq * D}), 64u);
+  fa_bwd_dkdv<<<dim3((unsigned)nkv, (unsigned)B, kz * (unsigned)hsplit), NT_BWD, SMEM_DKV, stream()>>>(tq64, tkv,
+                                                                                                       tdo64, a);
   PSRL_CHECK_LAUNCH();
   if (hsplit > 1) {
     const int64_t threads = kv.size(0) * nkv * 2 * D / 8;
@@ -1033,7 +1118,8 @@ static void bwd_launch(const at::Tensor& q, const at::Tensor& kv, const at::Tens
         a.part, hsplit, kv.size(0), (int)nkv, a.cu_k, B, a.scale, a.dkv, a.dkv_row, dk_col, dv_col);
     PSRL_CHECK_LAUNCH();
   }
-  fa_bwd_dq<<<dim3((unsigned)nq, (unsigned)B, (unsigned)a.blocks_z), NT_BWD, SMEM_BWD, stream()>>>(tq, tkv, tdo, a);
+  const CUtensorMap tkv64 = map_rows_64xR(kv, 64u);
+  fa_bwd_dq<<<dim3((unsigned)nq, (unsigned)B, (unsigned)a.blocks_z), NT_BWD, SMEM_DQ, stream()>>>(tq, tkv64, tdo, a);
   PSRL_CHECK_LAUNCH();
 }
 
