@@ -2,6 +2,7 @@
 disaggregated RL run (1 trainer rank + 1 rollout rank).  Processes are spawned
 per test; every collective has a short timeout."""
 
+import math
 import os
 import socket
 
@@ -173,6 +174,72 @@ def test_hybrid_rl_two_gpus():
     res = next(d for d in items if "steps" in d)
     assert sums[0] == sums[1]
     assert res["steps"] == [32, 32] and res["ps_version"] == 3 and res["ms"] > 0
+
+
+_GPU_TINY = ["model.dtype=bf16", "trainer.device=cuda", "rollout.cuda_graph=true", "data.kind=synthetic_tokens",
+             "data.prompt_len_min=16", "data.prompt_len_max=64", "data.response_len_mu=3.0",
+             "data.response_len_sigma=0.5", "data.response_len_cap=64", "reward.kind=bernoulli_hash",
+             "rollout.ignore_eos=true"]
+
+
+def _hybrid_cfg_worker(rank, world, port, q, overrides):
+    import faulthandler
+    faulthandler.dump_traceback_later(150, repeat=True)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    from psrl_b200.config import load_config
+    from psrl_b200.parallel.dist import init_distributed
+    from psrl_b200.trainer.hybrid import run_hybrid
+    cfg = load_config(preset="cpu_tiny_grpo", overrides=_GPU_TINY + list(overrides))
+    info = init_distributed("cuda", timeout_s=60)
+    res = run_hybrid(cfg, steps=2, warmup=0, info=info)
+    ms = res["metrics"]
+    q.put({"rank": rank, "engine": res["engine_checksum"], "steps": [m["num_trajectories"] for m in ms],
+           "vf": [m.get("critic/vf_loss") for m in ms], "kl": [m.get("actor/reward_kl_penalty") for m in ms],
+           "pg": [m.get("actor/pg_loss") for m in ms]})
+    dist.destroy_process_group()
+
+
+def _run_hybrid_cfg(overrides):
+    _need(2)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_hybrid_cfg_worker, args=(r, 2, port, q, overrides)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(300)
+    codes = [p.exitcode for p in ps]
+    for p in ps:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0], codes
+    return sorted([q.get(timeout=5) for _ in range(2)], key=lambda d: d["rank"])
+
+
+def test_hybrid_expert_parallel_moe_two_gpus():
+    """MoE training step with experts sharded over two GPUs (peer-memory
+    all-to-all for dispatch and combine), in-reward KL and the KL loss, both
+    ranks' engines ending with the same assembled weights."""
+    res = _run_hybrid_cfg(["model.preset=tiny-moe", "++actor.expert_parallel_size=2",
+                           "algorithm.use_kl_in_reward=true", "actor.use_kl_loss=true",
+                           "psrl.log_prob.enable_rollout_engine_log_prob=false"])
+    assert res[0]["steps"] == [32, 32]
+    assert all(math.isfinite(x) for x in res[0]["pg"]), res[0]["pg"]
+    assert res[0]["kl"][0] is not None and abs(res[0]["kl"][0]) < 1e-6
+    assert abs(res[0]["engine"] - res[1]["engine"]) <= 1e-6 * max(1.0, abs(res[0]["engine"]))
+
+
+def test_hybrid_ppo_with_critic_two_gpus():
+    """PPO with a critic over two GPUs: values on each rank's share, GAE
+    whitened with both ranks' statistics, critic and actor updates."""
+    res = _run_hybrid_cfg(["model.preset=tiny128", "critic.enable=true", "algorithm.adv_estimator=gae"])
+    assert res[0]["steps"] == [32, 32]
+    assert all(v is not None and math.isfinite(v) and v >= 0 for v in res[0]["vf"]), res[0]["vf"]
+    assert abs(res[0]["engine"] - res[1]["engine"]) <= 1e-6 * max(1.0, abs(res[0]["engine"]))
 
 
 def _peer_step_worker(rank, world, port, q):
