@@ -6,7 +6,7 @@ switches (``models/families.py`` maps HF configs onto them)."""
 from __future__ import annotations
 
 import json
-from dataclasses import asdict, dataclass, field, replace
+from dataclasses import asdict, dataclass, field, fields, replace
 from pathlib import Path
 
 
@@ -146,4 +146,13 @@ def model_args_from_config(model_cfg) -> ModelArgs:
     if preset not in PRESETS:
         raise KeyError(f"unknown model preset {preset!r}; have {sorted(PRESETS)}")
     args = replace(PRESETS[preset])
+    # ``model.overrides``: ModelArgs fields to change on the preset (a smaller
+    # layer count for a test run, a longer max_position, ...)
+    over = model_cfg.get("overrides", None) if hasattr(model_cfg, "get") else None
+    if over:
+        known = {f.name for f in fields(ModelArgs)}
+        bad = sorted(set(over) - known)
+        if bad:
+            raise KeyError(f"model.overrides names unknown ModelArgs fields {bad}")
+        args = replace(args, **{k: over[k] for k in over})
     return args

@@ -93,7 +93,10 @@ class PolicyWorker:
             if (tp_group is not None and dist_world(tp_group) > 1) or self.cp_group is not None or args.is_moe:
                 raise ValueError("pipeline parallelism here combines with data parallelism only")
             from ..parallel.pp import PipelineStage
-            self.pp = PipelineStage(self.model, pp_group)
+            meg = cfg.actor.get("megatron", None) or {}
+            vpp = max(int(cfg.actor.get("virtual_pipeline_parallel_size", 1) or 1),
+                      int(meg.get("virtual_pipeline_model_parallel_size", 1) or 1))
+            self.pp = PipelineStage(self.model, pp_group, virtual=vpp)
         if self.cp_group is not None:
             if tp_group is not None and dist_world(tp_group) > 1:
                 raise ValueError("context parallelism together with tensor parallelism is not implemented")

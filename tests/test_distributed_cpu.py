@@ -468,6 +468,15 @@ def test_gloo_world3_disaggregated_pipeline_parallel_trainer():
     assert res["steps"] == [32, 32] and res["pulls"] >= 2
 
 
+def test_gloo_world3_disaggregated_interleaved_pipeline_trainer():
+    """Two pipeline ranks with two virtual stages each (four 1-layer chunks,
+    interleaved schedule); the rollout rank pulls every tensor from the rank
+    that holds it."""
+    res = _run_disagg(["++model.overrides.num_layers=4", "++actor.pipeline_parallel_size=2",
+                       "++actor.virtual_pipeline_parallel_size=2"])
+    assert res["steps"] == [32, 32] and res["pulls"] >= 2
+
+
 def test_gloo_world3_disaggregated_context_parallel_trainer():
     """Two trainer ranks splitting every sequence (CP=2)."""
     res = _run_disagg(["++actor.context_parallel_size=2"])
