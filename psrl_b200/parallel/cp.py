@@ -1,6 +1,6 @@
 """Context parallelism for the trainer: one packed micro-batch split over ``P``
-ranks along the sequence (SURVEY §2.3 CP; the reference gets it from
-Megatron's context-parallel group, ``psrl/utils/config.py:119-126``).
+ranks along the sequence (the reference gets it from Megatron's
+context-parallel group, ``psrl/utils/config.py:119-126``).
 
 Layout (zigzag, so causal work is balanced): every sequence of length ``L``
 (a multiple of ``2P``) is cut into ``2P`` chunks of ``c = L / 2P`` tokens and

@@ -75,16 +75,23 @@ class _Bucket:
 class FlatShardedDP:
     def __init__(self, model: torch.nn.Module, group=None, *, lr: float = 1e-6, betas=(0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 0.0, max_grad_norm: float = 1.0, warmup_steps: int = 0,
-                 bucket_mode: str = "layer", param_filter=None, norm_group=None, count_in_norm: bool = True):
+                 bucket_mode: str = "layer", param_filter=None, norm_group=None, count_in_norm: bool = True,
+                 replicate_group=None):
         """``param_filter(name) -> bool`` selects the parameters this instance
         owns (default: all trainable ones).  ``norm_group``: ranks whose
         parameters are disjoint from this rank's (expert parallelism), summed
         into the squared gradient norm in addition to ``group``'s shards.
         ``count_in_norm=False``: the parameters are a copy of ones another rank
         already counts (a tied embedding on the last pipeline stage): they are
-        reduced and updated but add nothing to the clip norm."""
+        reduced and updated but add nothing to the clip norm.
+        ``replicate_group`` (hybrid sharding, HSDP): ``group`` is this rank's
+        shard group and ``replicate_group`` the ranks holding the same shard in
+        the other shard groups; the reduce-scattered shard is summed over it
+        before the update, so every replica applies the same step."""
         self.model = model
         self.group = group
+        self.replicate_group = replicate_group if (replicate_group is not None and dist.is_initialized()
+                                                   and dist.get_world_size(replicate_group) > 1) else None
         self.norm_group = norm_group
         self.count_in_norm = bool(count_in_norm)
         # no group = this rank trains alone (even inside a larger job)
@@ -145,7 +152,7 @@ class FlatShardedDP:
     def enable_peer_step(self) -> bool:
         """Use the fused peer-memory reduce-scatter + AdamW + all-gather kernels
         for the optimizer step (CUDA, world > 1).  Returns whether it is on."""
-        if self.world <= 1 or self.device.type != "cuda":
+        if self.world <= 1 or self.device.type != "cuda" or self.replicate_group is not None:
             return False
         from .peer import PeerShardedStep
         self.peer = PeerShardedStep(self)
@@ -197,6 +204,8 @@ class FlatShardedDP:
         for b in self.buckets:
             if self.world > 1:
                 dist.reduce_scatter_tensor(b.grad_shard, b.grad, op=dist.ReduceOp.SUM, group=self.group)
+            if self.replicate_group is not None:
+                dist.all_reduce(b.grad_shard, group=self.replicate_group)
             self.norm.add(b.grad_shard)
         if self.world > 1:
             dist.all_reduce(self.norm.sq, group=self.group)
@@ -249,3 +258,27 @@ class FlatShardedDP:
     def remove_hooks(self) -> None:
         for h in self._hooks:
             h.remove()
+
+
+def hybrid_shard_groups(group, shard_size: int):
+    """(shard group, replicate group) of this rank for hybrid sharding over
+    ``group``: shard groups of ``shard_size`` consecutive ranks of ``group``,
+    replicate groups of the ranks at the same position in each.  Only the
+    ranks of ``group`` take part (local synchronisation), so a trainer group
+    inside a larger job can call it alone."""
+    world = dist.get_world_size(group)
+    if shard_size <= 0 or shard_size >= world:
+        return group, None
+    if world % shard_size:
+        raise ValueError(f"{world} data-parallel ranks do not split into shard groups of {shard_size}")
+    ranks = dist.get_process_group_ranks(group)
+    me = dist.get_rank(group)
+    shard = rep = None
+    for i in range(world // shard_size):
+        g = dist.new_group(ranks[i * shard_size:(i + 1) * shard_size], use_local_synchronization=True) \
+            if me // shard_size == i else None
+        shard = g if g is not None else shard
+    for j in range(shard_size):
+        if me % shard_size == j:
+            rep = dist.new_group(ranks[j::shard_size], use_local_synchronization=True)
+    return shard, rep

@@ -153,7 +153,17 @@ class PolicyWorker:
                 else:
                     self.dp = FlatShardedDP(self.model, dp_group, norm_group=pp_group, **kw)
             else:
-                self.dp = FlatShardedDP(self.model, dp_group, param_filter=lambda n: n not in expert_names, **kw)
+                # hybrid sharding: optimizer state sharded over groups of fsdp_size ranks,
+                # replicated across them (veRL's fsdp_config.fsdp_size; -1: shard over all)
+                fc = cfg.actor.get("fsdp_config", None) or {}
+                fsdp_size = int(cfg.actor.get("fsdp_size", -1) or -1)
+                fsdp_size = fsdp_size if fsdp_size > 0 else int(fc.get("fsdp_size", -1) or -1)
+                shard_group, rep_group = dp_group, None
+                if fsdp_size > 0 and dp_group is not None and dist_world(dp_group) > fsdp_size:
+                    from ..parallel.fsdp import hybrid_shard_groups
+                    shard_group, rep_group = hybrid_shard_groups(dp_group, fsdp_size)
+                self.dp = FlatShardedDP(self.model, shard_group, param_filter=lambda n: n not in expert_names,
+                                        replicate_group=rep_group, **kw)
             if self.tp is None and expert_names:
                 # each rank's experts are its own: no reduction, but the clip norm spans all ranks
                 self.dp_partner = FlatShardedDP(self.model, None, param_filter=lambda n: n in expert_names,
