@@ -13,6 +13,16 @@ Layout (chosen for 180 GB of HBM per GPU):
   (one tiny all-reduce) → fused AdamW on the shard writing the bf16 shard in
   place → all-gather of the bf16 shard back into the full bucket.
 
+``shard_grads=True`` (gradient sharding, for models whose full fp32 main
+gradients would not fit beside the rest): there is no model-wide gradient
+buffer.  A bucket's gradients accumulate into a transient fp32 staging buffer
+of one bucket; when the backward has produced all of them the staging buffer
+is reduce-scattered and added into this rank's fp32 gradient shard, and
+freed.  One reduce-scatter per bucket per micro-batch (issued from the
+backward, in bucket-completion order, which is the same on every rank of a
+dense model) instead of one per step; the peer-memory step, which reads every
+peer's full gradient buffer, is off in this mode.
+
 The reference trains with FSDP2 full-shard (parameters re-gathered per layer
 in every forward and backward, ``engine_train_worker.py:80-85``); keeping
 parameters resident trades 2 bytes/param of HBM for one all-gather per
@@ -46,7 +56,9 @@ class _Bucket:
         self.rank = rank
         self.base = base                     # offset of this bucket in the model-wide flat buffer
         self.flat = flat[base: base + padded]
-        self.grad = grad[base: base + padded]
+        self.grad = grad[base: base + padded] if grad.numel() else None
+        self.stage = None                    # gradient sharding: this bucket's fp32 staging buffer
+        self.fired: set = set()
         off = 0
         self.offsets = []
         for p in params:
@@ -67,6 +79,7 @@ class _Bucket:
         self.m = m_all[sl]
         self.v = v_all[sl]
         self.grad_shard = self.grad[lo: self.hi] if world == 1 else gs_all[sl]
+        self.params_set = set(id(p) for p in params)
 
     def param_shard(self) -> torch.Tensor:
         return self.flat[self.lo: self.hi]
@@ -76,7 +89,7 @@ class FlatShardedDP:
     def __init__(self, model: torch.nn.Module, group=None, *, lr: float = 1e-6, betas=(0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 0.0, max_grad_norm: float = 1.0, warmup_steps: int = 0,
                  bucket_mode: str = "layer", param_filter=None, norm_group=None, count_in_norm: bool = True,
-                 replicate_group=None):
+                 replicate_group=None, shard_grads: bool = False):
         """``param_filter(name) -> bool`` selects the parameters this instance
         owns (default: all trainable ones).  ``norm_group``: ranks whose
         parameters are disjoint from this rank's (expert parallelism), summed
@@ -97,6 +110,7 @@ class FlatShardedDP:
         # no group = this rank trains alone (even inside a larger job)
         self.world = dist.get_world_size(group) if (group is not None and dist.is_initialized()) else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
+        self.shard_grads = bool(shard_grads) and self.world > 1
         self.device = next(model.parameters()).device
         self.lr, self.betas, self.eps, self.wd = lr, tuple(betas), eps, weight_decay
         self.max_grad_norm = max_grad_norm
@@ -122,7 +136,9 @@ class FlatShardedDP:
         dtype = next(model.parameters()).dtype
         self.num_params = sum(p.numel() for k in order for _, p in groups[k])
         self.flat = torch.zeros(self.total, dtype=dtype, device=self.device)
-        self.flat_grad = torch.zeros(self.total, dtype=torch.float32, device=self.device)
+        # the model-wide fp32 main-grad buffer (a placeholder when gradients are sharded)
+        self.flat_grad = torch.zeros(self.total if not self.shard_grads else 0, dtype=torch.float32,
+                                     device=self.device)
         self.shard_total = self.total // self.world
         f32 = dict(dtype=torch.float32, device=self.device)
         self.master_all = torch.zeros(self.shard_total, **f32)
@@ -152,7 +168,7 @@ class FlatShardedDP:
     def enable_peer_step(self) -> bool:
         """Use the fused peer-memory reduce-scatter + AdamW + all-gather kernels
         for the optimizer step (CUDA, world > 1).  Returns whether it is on."""
-        if self.world <= 1 or self.device.type != "cuda" or self.replicate_group is not None:
+        if self.world <= 1 or self.device.type != "cuda" or self.replicate_group is not None or self.shard_grads:
             return False
         from .peer import PeerShardedStep
         self.peer = PeerShardedStep(self)
@@ -161,11 +177,34 @@ class FlatShardedDP:
     # --------------------------------------------------------------- grads
     def _accumulate(self, p: torch.Tensor) -> None:
         b, off = self.param_to_bucket[p]
-        b.grad[off: off + p.numel()].add_(p.grad.reshape(-1))
+        if not self.shard_grads:
+            b.grad[off: off + p.numel()].add_(p.grad.reshape(-1))
+            p.grad = None
+            return
+        if b.stage is None:
+            b.stage = torch.zeros(b.padded, dtype=torch.float32, device=self.device)
+        b.stage[off: off + p.numel()].add_(p.grad.reshape(-1))
         p.grad = None
+        b.fired.add(id(p))
+        if len(b.fired) == len(b.params_set):
+            self._flush(b)
+
+    def _flush(self, b) -> None:
+        """Gradient sharding: reduce-scatter a bucket's staged gradients into
+        this rank's shard and free the staging buffer."""
+        part = torch.empty(b.shard, dtype=torch.float32, device=self.device)
+        dist.reduce_scatter_tensor(part, b.stage, op=dist.ReduceOp.SUM, group=self.group)
+        b.grad_shard.add_(part)
+        b.stage = None
+        b.fired = set()
 
     def zero_grad(self) -> None:
-        self.flat_grad.zero_()
+        if self.shard_grads:
+            self.grad_shard_all.zero_()
+            for b in self.buckets:
+                b.stage, b.fired = None, set()
+        else:
+            self.flat_grad.zero_()
 
     # ---------------------------------------------------------------- step
     def current_lr(self) -> float:
@@ -201,8 +240,14 @@ class FlatShardedDP:
         """Reduce-scatter the main grads into this rank's shards; returns the
         global squared norm of this instance's gradients (device scalar)."""
         self.norm.reset()
+        if self.shard_grads:
+            # buckets some of whose parameters got no gradient: flush in bucket
+            # order (the same set on every rank of a dense model)
+            for b in self.buckets:
+                if b.stage is not None:
+                    self._flush(b)
         for b in self.buckets:
-            if self.world > 1:
+            if self.world > 1 and not self.shard_grads:
                 dist.reduce_scatter_tensor(b.grad_shard, b.grad, op=dist.ReduceOp.SUM, group=self.group)
             if self.replicate_group is not None:
                 dist.all_reduce(b.grad_shard, group=self.replicate_group)

@@ -162,8 +162,10 @@ class PolicyWorker:
                 if fsdp_size > 0 and dp_group is not None and dist_world(dp_group) > fsdp_size:
                     from ..parallel.fsdp import hybrid_shard_groups
                     shard_group, rep_group = hybrid_shard_groups(dp_group, fsdp_size)
+                # gradient sharding: no model-wide fp32 main-grad buffer (large models)
                 self.dp = FlatShardedDP(self.model, shard_group, param_filter=lambda n: n not in expert_names,
-                                        replicate_group=rep_group, **kw)
+                                        replicate_group=rep_group,
+                                        shard_grads=bool(cfg.actor.get("fsdp_shard_grads", False)), **kw)
             if self.tp is None and expert_names:
                 # each rank's experts are its own: no reduction, but the clip norm spans all ranks
                 self.dp_partner = FlatShardedDP(self.model, None, param_filter=lambda n: n in expert_names,
@@ -188,13 +190,19 @@ class PolicyWorker:
         every rank runs the same number of micro-batches: this rank's list is
         padded with ``None`` up to the group maximum (one all-reduce of an
         int).  A ``None`` entry runs a one-token placeholder whose result is
-        discarded (its loss is multiplied by zero)."""
-        if self.ep is None:
+        discarded (its loss is multiplied by zero).  Gradient sharding needs
+        the same: every micro-batch's backward reduce-scatters each layer's
+        gradients over the shard group."""
+        if self.ep is not None:
+            grp = self.ep.group
+        elif self.dp is not None and getattr(self.dp, "shard_grads", False):
+            grp = self.dp.group
+        else:
             return list(bins)
         import torch.distributed as dist
         dev = self.device if self.device.type == "cuda" else torch.device("cpu")
         n = torch.tensor([len(bins)], dtype=torch.int64, device=dev)
-        dist.all_reduce(n, op=dist.ReduceOp.MAX, group=self.ep.group)
+        dist.all_reduce(n, op=dist.ReduceOp.MAX, group=grp)
         return list(bins) + [None] * (int(n.item()) - len(bins))
 
     def _recount_plan(self, trajs: list[Trajectory], plan: list[tuple]) -> list[tuple]:

@@ -77,17 +77,20 @@ def _worker_policy(rank, world, port, q):
     from psrl_b200.trainer.batch import Trajectory
     init_distributed("cpu", timeout_s=300)
     a = PRESETS["tiny"]
-    base = ["actor.optim.lr=1.0", "actor.optim.eps=1.0", "actor.ppo_mini_batch_size=8"]
+    # a small token budget: ranks pack different numbers of micro-batches, which
+    # gradient sharding must pad to the same count (its backward is collective)
+    base = ["actor.optim.lr=1.0", "actor.optim.eps=1.0", "actor.ppo_mini_batch_size=8",
+            "actor.ppo_max_token_len_per_gpu=20"]
     g = torch.Generator().manual_seed(4)
     trajs = []
     for i in range(8):
-        P, R = 3 + i % 4, 5 + (3 * i) % 7
+        P, R = 3 + i % 4, 5 + (3 * i) % 7 if i % 4 else 2
         trajs.append(Trajectory(uid=i, request_id=i, prompt_ids=torch.randint(0, a.vocab_size, (P,), generator=g).tolist(),
                                 response_ids=torch.randint(0, a.vocab_size, (R,), generator=g).tolist(),
                                 rollout_logprobs=(-torch.rand(R, generator=g)).tolist()))
         trajs[-1].advantage = float(torch.randn(1, generator=g))
     out = {}
-    for name, extra in (("full", []), ("hsdp", ["actor.fsdp_size=2"])):
+    for name, extra in (("full", []), ("hsdp", ["actor.fsdp_size=2", "actor.fsdp_shard_grads=true"])):
         cfg = load_config(preset="cpu_tiny_grpo", overrides=base + extra)
         w = PolicyWorker(cfg, a, "cpu", seed=3, dp_group=dist.group.WORLD, dp_rank=rank, dp_world=world)
         t = copy.deepcopy(trajs)
@@ -101,8 +104,9 @@ def _worker_policy(rank, world, port, q):
 
 
 def test_policy_worker_hybrid_sharding_step():
-    """PolicyWorker with actor.fsdp_size=2 on 4 ranks: the PPO step leaves the
-    same parameters as sharding over all 4 ranks."""
+    """PolicyWorker with actor.fsdp_size=2 and gradient sharding on 4 ranks:
+    the PPO step leaves the same parameters as sharding over all 4 ranks with
+    full gradient buffers."""
     world = 4
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -117,3 +121,62 @@ def test_policy_worker_hybrid_sharding_step():
     for r in res:
         assert r["shard_world"] == 2 and r["full_world"] == 4, r
         assert r["diff"] < 1e-5, r
+
+
+def _worker_shard_grads(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    import torch.distributed as dist
+    torch.set_num_threads(1)
+    from psrl_b200.models import PRESETS, build_model, packed_positions
+    from psrl_b200.parallel.fsdp import FlatShardedDP, hybrid_shard_groups
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    a = PRESETS["tiny"]
+    shard, rep = hybrid_shard_groups(dist.group.WORLD, 2)
+    kw = dict(lr=1e-2, eps=1.0, weight_decay=0.1, max_grad_norm=1.0)
+    runs = {}
+    for name, extra in (("full", dict(group=dist.group.WORLD)),
+                        ("sharded", dict(group=dist.group.WORLD, shard_grads=True)),
+                        ("hsdp_sharded", dict(group=shard, replicate_group=rep, shard_grads=True))):
+        model = build_model(a, "cpu", torch.float32, seed=1)
+        dp = FlatShardedDP(model, extra.pop("group"), **extra, **kw)
+        g = torch.Generator().manual_seed(70 + rank)
+        norms = []
+        for _ in range(2):                       # optimizer steps
+            for lens in ([5, 9], [12], [3, 4, 6]):   # micro-batches
+                T = sum(lens)
+                pos, cu, mx = packed_positions(lens, "cpu")
+                ids = torch.randint(0, a.vocab_size, (T,), generator=g)
+                lab = torch.randint(0, a.vocab_size, (T,), generator=g)
+                lp, _ = model.logprobs(ids, pos, cu, mx, lab)
+                (-lp.mean()).backward()
+            norms.append(float(dp.step()["grad_norm"]))
+        runs[name] = (dp, norms)
+    base = runs["full"][0].flat
+    out = {"rank": rank, "grad_buffer": runs["sharded"][0].flat_grad.numel()}
+    for name in ("sharded", "hsdp_sharded"):
+        out[name] = (float((runs[name][0].flat - base).abs().max()),
+                     max(abs(x - y) for x, y in zip(runs[name][1], runs["full"][1])))
+    q.put(out)
+    dist.destroy_process_group()
+
+
+def test_gradient_sharding_matches_full_gradients():
+    """shard_grads=True (no model-wide fp32 gradient buffer; each layer bucket
+    reduce-scattered as its backward completes), alone and with hybrid
+    sharding: same gradient norms and parameters as the full-buffer path
+    after two steps of three micro-batches each."""
+    world = 4
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_shard_grads, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in res:
+        assert r["grad_buffer"] == 0, r
+        for name in ("sharded", "hsdp_sharded"):
+            assert r[name][0] < 1e-6 and r[name][1] < 1e-4, (name, r)
