@@ -125,6 +125,27 @@ class DisaggregatedRun:
                     self.train_group = pdist.new_subgroup(list(range(self.rank % gsize, self.n_train, gsize)),
                                                           backend=backend)
         self.args = model_args_from_config(cfg.model)
+        # tensor-parallel rollout engines: groups of `rtp` consecutive rollout
+        # ranks serve one instance; the first rank of a group (the leader)
+        # talks to the control plane and broadcasts every round to the others
+        self.rtp = int(cfg.rollout.get("tensor_parallel_size", 1) or 1)
+        self.eng_tp = self.eng_tp_cpu = None
+        self.eng_leader = self.rank
+        if self.rtp > 1:
+            n_roll = self.world - self.n_train
+            if n_roll % self.rtp:
+                raise ValueError(f"{n_roll} rollout ranks are not a multiple of rollout.tensor_parallel_size "
+                                 f"{self.rtp}")
+            if self.args.is_moe:
+                raise ValueError("tensor-parallel rollout covers dense decoders")
+            if not self.is_trainer:
+                from ..parallel.tp import make_tp_group
+                j = (self.rank - self.n_train) // self.rtp
+                ranks = list(range(self.n_train + j * self.rtp, self.n_train + (j + 1) * self.rtp))
+                self.eng_tp = make_tp_group(pdist.new_subgroup(ranks, backend=backend))
+                self.eng_tp_cpu = pdist.new_subgroup(ranks, backend="gloo")
+                self.eng_leader = ranks[0]
+        self.is_leader = self.eng_tp is None or self.rank == self.eng_leader
         self.trained_tokens = 0
         self.global_step = 0
         self.liveness_s = float(cfg.trainer.get("liveness_timeout_s", 300))
@@ -294,7 +315,7 @@ class DisaggregatedRun:
     def _init_rollout(self):
         cfg, a = self.cfg, self.args
         rc = cfg.rollout
-        self.instance_id = (self.rank - self.n_train, 0)
+        self.instance_id = (self.eng_leader - self.n_train, 0)
         log("rollout: waiting for trainer stores")
         layout, descs = self.cp.get_stores()
         self.layout = layout
@@ -311,6 +332,17 @@ class DisaggregatedRun:
         self.weights = w
         self.puller = ShardedWeightPuller(layout, descs, flat, a) if any("entries" in d for d in descs) \
             else WeightPuller(layout, descs, flat)
+        if self.eng_tp is not None:
+            # every TP rank pulls the full model, then keeps its own shard of the
+            # column / row-parallel tensors (persistent copies, refreshed after each
+            # pull; replicated tensors stay views of the pulled buffer)
+            from ..parallel.tp import shard_engine_tensors
+            self.full_tensors = w.tensors
+            ew = EngineWeights(a, self.device, dtype)
+            ew.tensors = shard_engine_tensors(a, self.full_tensors, self.eng_tp)
+            self.sharded_names = [n for n, t in ew.tensors.items() if t is not self.full_tensors.get(n)]
+            self.weights_tp = ew.tensors
+            w = ew
         max_len = int(rc.max_prompt_length) + int(rc.max_response_length) + 64
         # a rollout-only GPU can give the KV cache and the batch more room
         kv_gb = float(rc.get("kv_cache_gb_dedicated", 0) or rc.get("kv_cache_gb", 4.0))
@@ -321,16 +353,19 @@ class DisaggregatedRun:
             enable_prefix_caching=bool(rc.enable_prefix_caching), use_cuda_graph=bool(rc.cuda_graph),
             keep_kv_on_update=bool(cfg.psrl.rollout_coordination.partial_rollout.get("keep_kv", False)),
             eos_token_id=None if rc.ignore_eos else self.cp.eos_id(), decode_gemm=str(cfg.rollout.get("decode_gemm", "library")),
-            kv_offload_blocks=int(cfg.rollout.get("kv_offload_blocks", 0) or 0))
+            kv_offload_blocks=int(cfg.rollout.get("kv_offload_blocks", 0) or 0), tp=self.eng_tp)
         sm = cfg.psrl.rollout_coordination.sync_and_mig_strategy
         self.policy = SyncPolicy(sm.method, bool(cfg.psrl.rollout_coordination.partial_rollout.enable),
                                  sm.sync.get("threshold"), sm.sync.get("indicator", "request_num"))
         self._pull()
-        self.cp.register_instance(self.instance_id, self.engine.version)
+        if self.is_leader:
+            self.cp.register_instance(self.instance_id, self.engine.version)
         log(f"rollout instance {self.instance_id} ready at version {self.engine.version} "
             f"({max_seqs} seqs, {kv_gb:.0f} GB KV)")
 
     def _pull(self) -> None:
+        if self.eng_tp is not None:
+            return self._tp_pull()
         t0 = time.perf_counter()
         if not self.cp.acquire_pull():
             raise TimeoutError("shared pull lock")
@@ -354,6 +389,39 @@ class DisaggregatedRun:
         self.cp.report_pull(time.perf_counter() - t0, self.instance_id, from_v, v,
                             0 if self.engine.keep_kv_on_update else in_flight, copy_s, int(nbytes))
 
+    def _tp_pull(self) -> None:
+        """A TP instance's pull: the leader takes the shared pull lock and the
+        version, every rank of the group copies the full model from the
+        trainer stores and re-slices its shard, and the leader releases the
+        lock once all of them are done (a gloo barrier of the group)."""
+        t0 = time.perf_counter()
+        box = [None]
+        if self.is_leader:
+            ok = bool(self.cp.acquire_pull())
+            box = [(ok, self.cp.pull_model(self.instance_id) if ok else None)]
+        dist.broadcast_object_list(box, src=self.eng_leader, group=self.eng_tp_cpu)
+        ok, v = box[0]
+        if not ok:
+            raise TimeoutError("shared pull lock")
+        try:
+            nbytes = self.puller.pull()
+            from ..parallel.tp import shard_engine_tensors
+            fresh = shard_engine_tensors(self.args, self.full_tensors, self.eng_tp)
+            for n in self.sharded_names:
+                self.weights_tp[n].copy_(fresh[n])
+            if self.device.type == "cuda":
+                torch.cuda.current_stream().synchronize()
+            dist.barrier(group=self.eng_tp_cpu)
+        finally:
+            if self.is_leader:
+                self.cp.release_pull()
+        from_v = self.engine.version
+        in_flight = self.engine.num_unfinished()
+        self.engine.load_weights(None, v)
+        if self.is_leader:
+            self.cp.report_pull(time.perf_counter() - t0, self.instance_id, from_v, v,
+                                0 if self.engine.keep_kv_on_update else in_flight, None, int(nbytes))
+
     def _coordinated_pull(self) -> None:
         """Pull granted by the control plane's coordinator; a failure quarantines
         this instance (it gets no more work) instead of ending the run."""
@@ -362,12 +430,68 @@ class DisaggregatedRun:
         except Exception as exc:
             self.cp.report_sync_failure(self.instance_id, f"{type(exc).__name__}: {exc}")
 
+    def _tp_rollout_loop(self, on_phase) -> None:
+        """A TP instance: the leader reads its mailbox and the driver phase and
+        broadcasts (requests, aborts, phase, pull decision) each round, so every
+        rank of the group applies the same operations and steps in lockstep."""
+        eng = self.engine
+        leader = self.is_leader
+        mb = None
+        if leader:
+            self.mailbox = mb = ExchangeMailbox(self.cp, self.instance_id, eng)
+        seen = 0
+        idle_s = 0.0
+        try:
+            while True:
+                msg = None
+                if leader:
+                    reqs, aborts = mb.collect()
+                    sync = bool(mb.take_sync_grant() and mb.ps_version > eng.version)
+                    msg = (reqs, aborts, mb.phase, sync)
+                box = [msg]
+                dist.broadcast_object_list(box, src=self.eng_leader, group=self.eng_tp_cpu)
+                reqs, aborts, phase, sync = box[0]
+                for r in reqs:
+                    eng.add_request(r)
+                for rid in aborts:
+                    eng.abort(rid)
+                while seen < phase:
+                    seen += 1
+                    if leader:
+                        self.cp.report_engine(self.instance_id, seen,
+                                              {**{k: float(v) for k, v in eng.stats.items()}, "idle_time": idle_s})
+                    on_phase(seen)
+                if seen >= 2:
+                    return
+                if sync:
+                    try:
+                        self._tp_pull()
+                    except Exception as exc:
+                        if leader:
+                            self.cp.report_sync_failure(self.instance_id, f"{type(exc).__name__}: {exc}")
+                if eng.has_unfinished():
+                    outs = eng.step()
+                    if outs and leader:
+                        mb.post(outs)
+                else:
+                    if leader:
+                        mb.kick()
+                    t_idle = time.perf_counter()
+                    time.sleep(0.0005)
+                    idle_s += time.perf_counter() - t_idle
+        finally:
+            if mb is not None:
+                mb.close()
+            self.mailbox = None
+
     def rollout_loop(self, on_phase) -> None:
         """Serve until the driver reaches the final phase; ``on_phase(p)`` runs the
         collective steps tied to phase ``p`` (same order as on the trainers)."""
         eng = self.engine
         if self.device.type == "cuda" and eng.use_cuda_graph:
             eng.capture_all()
+        if self.eng_tp is not None:
+            return self._tp_rollout_loop(on_phase)
         self.mailbox = mb = ExchangeMailbox(self.cp, self.instance_id, eng)
         seen = 0
         idle_s = 0.0

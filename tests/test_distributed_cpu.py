@@ -444,11 +444,11 @@ def test_gloo_world2_hybrid_tensor_parallel_rollout():
     assert res[0]["steps"] == [32, 32]
 
 
-def _run_disagg(overrides):
+def _run_disagg(overrides, world=3):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker_disagg_sharded, args=(r, 3, port, q, overrides)) for r in range(3)]
+    procs = [ctx.Process(target=_worker_disagg_sharded, args=(r, world, port, q, overrides)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -457,8 +457,25 @@ def _run_disagg(overrides):
     for p in procs:
         if p.is_alive():
             p.kill()
-    assert codes == [0, 0, 0], codes
+    assert codes == [0] * world, codes
     return q.get(timeout=5)
+
+
+def test_gloo_world4_disaggregated_tensor_parallel_rollout():
+    """Two trainer ranks (data parallel) and one rollout instance of two
+    tensor-parallel ranks: the leader takes the work and broadcasts each round,
+    both ranks pull the model and keep their shards, and both step in lockstep."""
+    res = _run_disagg(["rollout.tensor_parallel_size=2"], world=4)
+    assert res["steps"] == [32, 32] and res["pulls"] >= 2
+
+
+def test_gloo_world4_disaggregated_tp_trainer_and_tp_rollout():
+    """The PPO-7B layout in miniature: trainer TP=2 publishing its shards, one
+    TP=2 rollout instance pulling them and re-slicing its own shards, PPO with
+    a critic."""
+    res = _run_disagg(["++actor.tensor_parallel_size=2", "rollout.tensor_parallel_size=2", "critic.enable=true",
+                       "algorithm.adv_estimator=gae"], world=4)
+    assert res["steps"] == [32, 32] and res["pulls"] >= 2
 
 
 def test_gloo_world3_disaggregated_pipeline_parallel_trainer():
