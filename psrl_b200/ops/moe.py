@@ -118,6 +118,22 @@ def supported(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor) -> bool:
             and w2.shape[-1] % 64 == 0 and w13.shape[0] <= 256)
 
 
+def moe_mlp_routed(x: torch.Tensor, w: torch.Tensor, ids: torch.Tensor, w13: torch.Tensor,
+                   w2: torch.Tensor) -> torch.Tensor:
+    """SwiGLU experts for a given routing (``w`` [T, k] combine weights, ``ids``
+    [T, k] indices into ``w13`` / ``w2``), inference only.  The per-expert
+    counts come from a device scatter-add, so nothing waits on the host."""
+    from .activation import swiglu
+    ids = ids.to(torch.int32).contiguous()
+    counts = torch.zeros(w13.shape[0], dtype=torch.int32, device=x.device)
+    counts.scatter_add_(0, ids.reshape(-1).long(), torch.ones(ids.numel(), dtype=torch.int32, device=x.device))
+    pos, tor, seg, _ = ext().moe_permute(ids, counts, 128, 1)
+    xs = _GatherFn.apply(x.contiguous(), tor)
+    h = swiglu(grouped_linear(xs, w13, seg))
+    ys = grouped_linear(h, w2, seg)
+    return _CombineFn.apply(ys, pos, w.float())
+
+
 def moe_mlp(x: torch.Tensor, router_logits: torch.Tensor, prior: torch.Tensor | None, w13: torch.Tensor,
             w2: torch.Tensor, k: int, renorm: bool = True) -> torch.Tensor:
     """Top-k routed SwiGLU experts on CUDA (see module docstring)."""

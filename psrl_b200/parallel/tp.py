@@ -205,6 +205,17 @@ def shard_engine_tensors(args, tensors: dict, tp: TPGroup) -> dict:
             out[n] = torch.cat([t[r * il:(r + 1) * il], t[I + r * il:I + (r + 1) * il]]).contiguous()
         elif n.endswith("mlp.down.weight"):
             out[n] = t[:, r * il:(r + 1) * il].contiguous()
+        elif n.endswith("mlp.experts_w13") or n.endswith("mlp.experts_w2"):
+            # expert parallelism over the TP group: whole experts [r E/P, (r+1) E/P)
+            el = args.num_experts // P
+            out[n] = t[r * el:(r + 1) * el].contiguous()
+        elif n.endswith("mlp.shared_gate_up.weight"):
+            Is = args.shared_expert_intermediate_size
+            sl = Is // P
+            out[n] = torch.cat([t[r * sl:(r + 1) * sl], t[Is + r * sl:Is + (r + 1) * sl]]).contiguous()
+        elif n.endswith("mlp.shared_down.weight"):
+            sl = args.shared_expert_intermediate_size // P
+            out[n] = t[:, r * sl:(r + 1) * sl].contiguous()
         else:
             out[n] = t
     return out

@@ -178,13 +178,18 @@ class RolloutEngine:
         self.tp = tp
         self.full_args = args
         if tp is not None and tp.world > 1:
-            if args.is_moe:
-                raise ValueError("tensor-parallel rollout covers dense decoders")
             if args.qk_norm_full or args.hidden_act != "silu":
                 raise NotImplementedError("tensor-parallel rollout of full-width q/k norms or GeGLU is not implemented")
+            if args.is_moe and (args.num_experts % tp.world or args.shared_expert_intermediate_size % tp.world):
+                raise ValueError("expert parallelism over the TP group needs experts (and the shared expert's "
+                                 "width) divisible by the TP size")
             from dataclasses import replace
+            # MoE: expert parallelism follows TP: rank r holds experts [r E/P, (r+1) E/P)
+            # at full width (routing still spans all E experts) and 1/P of the
+            # shared expert's width; its partial output joins the MLP all-reduce
             args = replace(args, num_heads=args.num_heads // tp.world, num_kv_heads=args.num_kv_heads // tp.world,
-                           intermediate_size=args.intermediate_size // tp.world)
+                           intermediate_size=args.intermediate_size // tp.world,
+                           shared_expert_intermediate_size=args.shared_expert_intermediate_size // tp.world)
         else:
             self.tp = None
         self.args = args
@@ -901,6 +906,8 @@ class RolloutEngine:
             h2, resid = ops.rms_norm(attn, W[pre + "ln2"], a.rms_eps, residual=resid)
             if a.is_moe:
                 x = self._moe(h2, pre)
+                if self.tp is not None:
+                    dist.all_reduce(x, group=self.tp.group)
             else:
                 x = proj(mlp_act(h2, W[pre + "mlp.gate_up.weight"]), W[pre + "mlp.down.weight"])
                 if self.tp is not None:
@@ -916,9 +923,32 @@ class RolloutEngine:
             y = y + torch.sigmoid(F.linear(h, W[pre + "mlp.shared_gate.weight"]).float()).to(sh.dtype) * sh
         return y
 
+    def _moe_routed_ep(self, h, pre):
+        """Routed experts of a TP engine: top-k over all experts (identical on
+        every rank), then only this rank's experts; entries routed elsewhere
+        keep weight 0 (computed on local expert 0 and dropped by the combine),
+        so the step has no host synchronisation."""
+        from ..ops import moe as moe_ops
+        from ..parallel.moe import moe_forward_local
+        a, W = self.args, self.w
+        w13, w2 = W[pre + "mlp.experts_w13"], W[pre + "mlp.experts_w2"]
+        n_local = w13.shape[0]
+        lo = self.tp.rank * n_local
+        wt, ids, _ = moe_ops.route(F.linear(h, W[pre + "mlp.router.weight"]), W[pre + "mlp.router_prior"],
+                                   a.num_experts_per_tok, bool(a.norm_topk_prob))
+        ids = ids.long()
+        local = (ids >= lo) & (ids < lo + n_local)
+        wl = torch.where(local, wt, torch.zeros_like(wt))
+        il = torch.where(local, ids - lo, torch.zeros_like(ids))
+        if moe_ops.supported(h, w13, w2):
+            return moe_ops.moe_mlp_routed(h, wl, il, w13, w2)
+        return moe_forward_local(h, wl.to(h.dtype), il, w13, w2)
+
     def _moe_routed(self, h, pre):
         from ..ops import moe as moe_ops
         from ..parallel.moe import moe_forward_local
+        if self.tp is not None:
+            return self._moe_routed_ep(h, pre)
         a, W = self.args, self.w
         if moe_ops.supported(h, W[pre + "mlp.experts_w13"], W[pre + "mlp.experts_w2"]):
             return moe_ops.moe_mlp(h, F.linear(h, W[pre + "mlp.router.weight"]).float(), W[pre + "mlp.router_prior"],

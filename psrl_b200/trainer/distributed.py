@@ -136,8 +136,6 @@ class DisaggregatedRun:
             if n_roll % self.rtp:
                 raise ValueError(f"{n_roll} rollout ranks are not a multiple of rollout.tensor_parallel_size "
                                  f"{self.rtp}")
-            if self.args.is_moe:
-                raise ValueError("tensor-parallel rollout covers dense decoders")
             if not self.is_trainer:
                 from ..parallel.tp import make_tp_group
                 j = (self.rank - self.n_train) // self.rtp

@@ -469,6 +469,15 @@ def test_gloo_world4_disaggregated_tensor_parallel_rollout():
     assert res["steps"] == [32, 32] and res["pulls"] >= 2
 
 
+def test_gloo_world4_disaggregated_moe_expert_parallel_rollout():
+    """MoE: an expert-parallel trainer pair publishes its experts; one rollout
+    instance of two ranks splits the experts between them (expert parallelism
+    following rollout TP) after pulling the full model."""
+    res = _run_disagg(["model.preset=tiny-moe", "++actor.expert_parallel_size=2",
+                       "rollout.tensor_parallel_size=2"], world=4)
+    assert res["steps"] == [32, 32] and res["pulls"] >= 2
+
+
 def test_gloo_world4_disaggregated_tp_trainer_and_tp_rollout():
     """The PPO-7B layout in miniature: trainer TP=2 publishing its shards, one
     TP=2 rollout instance pulling them and re-slicing its own shards, PPO with

@@ -5,6 +5,7 @@ leave every shard equal to the matching slice of the unsharded model's update.""
 import os
 import socket
 
+import pytest
 import torch.multiprocessing as mp
 
 
@@ -154,7 +155,7 @@ def test_full_weight_assembly_from_tp_and_ep_shards():
         assert w["tiny"] == 0.0 and w["tiny-moe"] == 0.0, w
 
 
-def _engine_worker(rank, world, port, q):
+def _engine_worker(rank, world, port, q, preset="tiny", shared=0):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     import torch
@@ -165,7 +166,10 @@ def _engine_worker(rank, world, port, q):
     from psrl_b200.parallel.tp import make_tp_group, shard_engine_tensors
     from psrl_b200.rollout.engine import EngineWeights, GenRequest, RolloutEngine, SamplingParams
     init_distributed("cpu", timeout_s=300)
-    a = PRESETS["tiny"]
+    from dataclasses import replace
+    a = PRESETS[preset]
+    if shared:
+        a = replace(a, shared_expert_intermediate_size=shared)
     full = EngineWeights.from_model(build_model(a, "cpu", torch.float32, seed=4), "cpu", torch.float32)
     tp = make_tp_group(dist.group.WORLD)
     shard = EngineWeights(a, "cpu", torch.float32)
@@ -191,13 +195,16 @@ def _engine_worker(rank, world, port, q):
     dist.destroy_process_group()
 
 
-def test_tensor_parallel_rollout_engine_matches_single_rank():
+@pytest.mark.parametrize("preset,shared", [("tiny", 0), ("tiny-moe", 0), ("tiny-moe", 128)])
+def test_tensor_parallel_rollout_engine_matches_single_rank(preset, shared):
     """A TP=2 rollout engine (two gloo ranks, identical request streams) decodes
-    the same greedy tokens and log-probs as the unsharded engine."""
+    the same greedy tokens and log-probs as the unsharded engine; for MoE the
+    experts are split over the two ranks (expert parallelism follows TP), with
+    and without a TP-sharded shared expert."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_engine_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_engine_worker, args=(r, 2, port, q, preset, shared)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
