@@ -128,21 +128,32 @@ class DisaggregatedRun:
         # tensor-parallel rollout engines: groups of `rtp` consecutive rollout
         # ranks serve one instance; the first rank of a group (the leader)
         # talks to the control plane and broadcasts every round to the others
-        self.rtp = int(cfg.rollout.get("tensor_parallel_size", 1) or 1)
+        # (heterogeneous instances: rollout.tensor_parallel_sizes lists one TP size
+        # per instance, in rollout-rank order)
+        n_roll = self.world - self.n_train
+        sizes = list(cfg.rollout.get("tensor_parallel_sizes", None) or [])
+        if sizes:
+            sizes = [int(x) for x in sizes]
+            if sum(sizes) != n_roll or min(sizes) < 1:
+                raise ValueError(f"rollout.tensor_parallel_sizes {sizes} must add up to the {n_roll} rollout ranks")
+        else:
+            rtp = int(cfg.rollout.get("tensor_parallel_size", 1) or 1)
+            if n_roll % rtp:
+                raise ValueError(f"{n_roll} rollout ranks are not a multiple of rollout.tensor_parallel_size {rtp}")
+            sizes = [rtp] * (n_roll // rtp)
+        self.rollout_tp_sizes = sizes
         self.eng_tp = self.eng_tp_cpu = None
         self.eng_leader = self.rank
-        if self.rtp > 1:
-            n_roll = self.world - self.n_train
-            if n_roll % self.rtp:
-                raise ValueError(f"{n_roll} rollout ranks are not a multiple of rollout.tensor_parallel_size "
-                                 f"{self.rtp}")
-            if not self.is_trainer:
-                from ..parallel.tp import make_tp_group
-                j = (self.rank - self.n_train) // self.rtp
-                ranks = list(range(self.n_train + j * self.rtp, self.n_train + (j + 1) * self.rtp))
-                self.eng_tp = make_tp_group(pdist.new_subgroup(ranks, backend=backend))
-                self.eng_tp_cpu = pdist.new_subgroup(ranks, backend="gloo")
-                self.eng_leader = ranks[0]
+        if not self.is_trainer:
+            start = self.n_train
+            for sz in sizes:
+                if start <= self.rank < start + sz and sz > 1:
+                    from ..parallel.tp import make_tp_group
+                    ranks = list(range(start, start + sz))
+                    self.eng_tp = make_tp_group(pdist.new_subgroup(ranks, backend=backend))
+                    self.eng_tp_cpu = pdist.new_subgroup(ranks, backend="gloo")
+                    self.eng_leader = ranks[0]
+                start += sz
         self.is_leader = self.eng_tp is None or self.rank == self.eng_leader
         self.trained_tokens = 0
         self.global_step = 0

@@ -469,6 +469,13 @@ def test_gloo_world4_disaggregated_tensor_parallel_rollout():
     assert res["steps"] == [32, 32] and res["pulls"] >= 2
 
 
+def test_gloo_world5_disaggregated_heterogeneous_rollout():
+    """Rollout instances of different sizes in one job: a TP=2 instance and a
+    TP=1 instance serve the same run."""
+    res = _run_disagg(["++rollout.tensor_parallel_sizes=[2,1]"], world=5)
+    assert res["steps"] == [32, 32] and res["pulls"] >= 3
+
+
 def test_gloo_world4_disaggregated_moe_expert_parallel_rollout():
     """MoE: an expert-parallel trainer pair publishes its experts; one rollout
     instance of two ranks splits the experts between them (expert parallelism
