@@ -14,7 +14,9 @@ The trainer stores full fused tensors; a TP-``t`` rollout rank ``r`` holds
 
 ``tp_slices(name, shape, args, r, t)`` returns the (dim, start, length) pieces
 of the full tensor that make rank ``r``'s local tensor, in order; the weight
-sync turns them into copy segments.  MoE experts are split by expert (EP).
+sync turns them into copy segments.  MoE experts of a tensor-parallel trainer
+are split along their SwiGLU width (ETP: ``experts_w13`` like ``gate_up`` for
+every expert, ``experts_w2`` like ``down``), and so is a shared expert.
 """
 
 from __future__ import annotations
@@ -54,9 +56,21 @@ def tp_slices(name: str, shape: tuple, a: ModelArgs, r: int, t: int) -> list[tup
         per = -(-shape[0] // t)
         lo = r * per
         return [(0, lo, max(0, min(per, shape[0] - lo)))]
-    if name.endswith("experts_w13") or name.endswith("experts_w2"):
-        per = shape[0] // t
-        return [(0, r * per, per)]
+    if name.endswith("experts_w13"):
+        # [E, 2 I, h]: the same gate / up split as gate_up, for every expert
+        inter = shape[1] // 2
+        per = inter // t
+        return [(1, r * per, per), (1, inter + r * per, per)]
+    if name.endswith("experts_w2"):
+        per = shape[2] // t
+        return [(2, r * per, per)]
+    if name.endswith("mlp.shared_gate_up.weight"):
+        inter = shape[0] // 2
+        per = inter // t
+        return [(0, r * per, per), (0, inter + r * per, per)]
+    if name.endswith("mlp.shared_down.weight"):
+        per = shape[1] // t
+        return [(1, r * per, per)]
     return [(0, 0, shape[0])]      # replicated
 
 
@@ -82,18 +96,17 @@ def copy_segments_for(name: str, shape: tuple, itemsize: int, a: ModelArgs, r: i
     from the full row-major tensor stored at ``src_base`` into ``dst_base``."""
     out = []
     lshape = local_shape(name, shape, a, r, t)
-    dst = dst_base
+    acc = 0
     for dim, start, length in tp_slices(name, shape, a, r, t):
-        if dim == 0:
-            row = itemsize
-            for s in shape[1:]:
-                row *= s
-            out.append((src_base + start * row, dst, length * row))
-            dst += length * row
-        else:  # dim 1 of a 2-D matrix: one run per row
-            rows, cols = shape
-            lcols = lshape[1]
-            for i in range(rows):
-                out.append((src_base + (i * cols + start) * itemsize, dst_base + i * lcols * itemsize,
-                            length * itemsize))
+        inner = itemsize
+        for x in shape[dim + 1:]:
+            inner *= x
+        outer = 1
+        for x in shape[:dim]:
+            outer *= x
+        # one run per index of the leading dimensions
+        for i in range(outer):
+            out.append((src_base + (i * shape[dim] + start) * inner, dst_base + (i * lshape[dim] + acc) * inner,
+                        length * inner))
+        acc += length
     return out

@@ -14,7 +14,9 @@ intermediate slices), a rollout engine beside it still needs every weight.
   - experts are concatenated along the expert dimension;
   - QKV rows are put back in q | k | v order;
   - gate_up rows are put back in gate | up order;
-  - the O and down projections are concatenated along their input columns.
+  - the O and down projections are concatenated along their input columns;
+  - tensor-parallel experts (split along their width) get their gate, up and
+    down slices put back per expert.
 
 Engine tensor names are the unsharded model's (``layers.{i}.attn.qkv.weight``
 and so on).  The gathers are NCCL on GPU and gloo on CPU.
@@ -79,9 +81,19 @@ class FullWeightAssembler:
                 q, k, v = st.split([qn, kn, kn], dim=1)
                 dst.copy_(torch.cat([q.reshape(P * qn, *q.shape[2:]), k.reshape(P * kn, *k.shape[2:]),
                                      v.reshape(P * kn, *v.shape[2:])]), non_blocking=True)
-            elif n.endswith("mlp.gate_up_weight"):
-                il = a.intermediate_size // P
+            elif n.endswith("mlp.gate_up_weight") or n.endswith("mlp.shared_gate_up.weight"):
+                il = (a.intermediate_size if n.endswith("mlp.gate_up_weight") else a.shared_expert_intermediate_size) // P
                 g, u = st.split([il, il], dim=1)
                 dst.copy_(torch.cat([g.reshape(P * il, -1), u.reshape(P * il, -1)]), non_blocking=True)
-            else:   # row-parallel O / down: [P, h, cols] -> [h, P * cols]
+            elif n.endswith("experts_w13"):
+                # [P, E, 2 il, h] -> gate rows then up rows of every expert: [E, 2 P il, h]
+                il = st.shape[2] // 2
+                g, u = st.split([il, il], dim=2)
+                E, h = st.shape[1], st.shape[3]
+                dst.copy_(torch.cat([g.permute(1, 0, 2, 3).reshape(E, P * il, h),
+                                     u.permute(1, 0, 2, 3).reshape(E, P * il, h)], dim=1), non_blocking=True)
+            elif n.endswith("experts_w2"):
+                # [P, E, h, il] -> [E, h, P il]
+                dst.copy_(st.permute(1, 2, 0, 3).reshape(dst.shape), non_blocking=True)
+            else:   # row-parallel O / down (and the shared expert's down): [P, h, cols] -> [h, P * cols]
                 dst.copy_(st.permute(1, 0, 2).reshape(dst.shape), non_blocking=True)

@@ -9,6 +9,10 @@ With a tensor-parallel group of size P, rank r keeps
 * MLP: intermediate columns [r I/P, (r+1) I/P) of both the gate and the up
   halves of ``gate_up`` (column parallel, still [gate | up] per rank) and the
   matching input columns of ``down`` (row parallel);
+* MoE layers (expert tensor parallelism): the same column / row split of
+  every expert's SwiGLU width and of the shared expert's; router and
+  shared-expert gate replicated, their partial gradients summed over the
+  group (:func:`make_tp_moe`);
 * everything else (embedding, norms, q/k head norms, LM head) replicated.
 
 A layer's input enters the column-parallel projections through
@@ -163,21 +167,79 @@ class TPMLP(nn.Module):
         return reduce_from_tp(linear(gate_up_swiglu(x, self.gate_up_weight), self.down_weight), self.tp)
 
 
+def _sum_over_tp(tp: TPGroup):
+    def hook(g):
+        g = g.clone()
+        dist.all_reduce(g, group=tp.group)
+        return g
+    return hook
+
+
+def make_tp_moe(full, tp: TPGroup):
+    """Expert tensor parallelism (ETP = TP): every expert's SwiGLU width, and
+    the shared expert's, split over the TP ranks like a dense MLP (gate / up
+    rows and the matching down columns of each expert); the router and the
+    shared-expert gate are replicated.  Routing is identical on every rank, so
+    each rank computes every routed (token, expert) pair at 1/P of the width
+    and the partial outputs are summed by the layer's all-reduce.  The router
+    and shared-gate gradients come out partial (each rank sees its own
+    partial expert outputs) and are summed over the TP group by a gradient
+    hook, which keeps them identical, as replicated parameters must be.
+    Parameter names stay those of the unsharded MoE block."""
+    from ..models.qwen import MoE
+    a = full.a
+    I, Is, P, r = a.moe_intermediate_size, a.shared_expert_intermediate_size, tp.world, tp.rank
+    if I % P or Is % P:
+        raise ValueError(f"expert width {I} / shared width {Is} does not split over TP={P}")
+
+    class TPMoE(MoE):
+        def forward(self, x):
+            return reduce_from_tp(MoE.forward(self, copy_to_tp(x, self.tp)), self.tp)
+
+    m = TPMoE.__new__(TPMoE)
+    nn.Module.__init__(m)
+    m.a, m.tp = a, tp
+    il = I // P
+    m.router = full.router
+    w13, w2 = full.experts_w13.data, full.experts_w2.data
+    m.experts_w13 = nn.Parameter(torch.cat([w13[:, r * il:(r + 1) * il], w13[:, I + r * il:I + (r + 1) * il]],
+                                           dim=1).contiguous())
+    m.experts_w2 = nn.Parameter(w2[:, :, r * il:(r + 1) * il].contiguous())
+    m.register_buffer("router_prior", full.router_prior, persistent=False)
+    m.router.weight.register_hook(_sum_over_tp(tp))
+    names = ["experts_w13", "experts_w2"]
+    if Is:
+        sl = Is // P
+        g = full.shared_gate_up.weight.data
+        m.shared_gate_up = nn.Linear(a.hidden_size, 2 * sl, bias=False, device=g.device, dtype=g.dtype)
+        m.shared_gate_up.weight.data.copy_(torch.cat([g[r * sl:(r + 1) * sl], g[Is + r * sl:Is + (r + 1) * sl]]))
+        d = full.shared_down.weight.data
+        m.shared_down = nn.Linear(sl, a.hidden_size, bias=False, device=d.device, dtype=d.dtype)
+        m.shared_down.weight.data.copy_(d[:, r * sl:(r + 1) * sl])
+        m.shared_gate = full.shared_gate
+        m.shared_gate.weight.register_hook(_sum_over_tp(tp))
+        names += ["shared_gate_up.weight", "shared_down.weight"]
+    return m, names
+
+
 @torch.no_grad()
 def apply_tensor_parallel(model, tp: TPGroup) -> list[str]:
-    """Shard every dense decoder layer of ``model`` in place; returns the names
-    of the sharded parameters (the rest are replicated)."""
+    """Shard every decoder layer of ``model`` in place (attention heads, the
+    dense MLP's width, or each expert's width in a MoE layer); returns the
+    names of the sharded parameters (the rest are replicated)."""
     a = model.args
-    if a.is_moe:
-        raise ValueError("tensor parallelism here covers dense decoders; MoE layers use expert parallelism")
     if a.qk_norm_full or a.hidden_act != "silu":
         raise NotImplementedError("tensor parallelism of full-width q/k norms or GeGLU is not implemented")
     names = []
     for i, layer in enumerate(model.layers):
         layer.attn = TPAttention(layer.attn, tp)
-        layer.mlp = TPMLP(layer.mlp, tp, a.intermediate_size)
-        names += [f"layers.{i}.attn.qkv_weight", f"layers.{i}.attn.o_weight", f"layers.{i}.mlp.gate_up_weight",
-                  f"layers.{i}.mlp.down_weight"]
+        names += [f"layers.{i}.attn.qkv_weight", f"layers.{i}.attn.o_weight"]
+        if a.is_moe:
+            layer.mlp, mnames = make_tp_moe(layer.mlp, tp)
+            names += [f"layers.{i}.mlp.{n}" for n in mnames]
+        else:
+            layer.mlp = TPMLP(layer.mlp, tp, a.intermediate_size)
+            names += [f"layers.{i}.mlp.gate_up_weight", f"layers.{i}.mlp.down_weight"]
         if layer.attn.qkv_bias is not None:
             names.append(f"layers.{i}.attn.qkv_bias")
     model.tp = tp

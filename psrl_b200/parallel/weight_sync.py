@@ -182,11 +182,14 @@ class ShardedWeightPuller:
         esz = torch.finfo(layout.dtype).bits // 8
         whole: dict[str, list] = {}        # engine name -> [(store, offset)]
         shards: dict[str, dict] = {}       # engine name -> {tp rank: [(store, offset, local shape)]}
+        full_shape = {n: tuple(sh) for n, sh, _ in layout.entries}
         for j, d in enumerate(descriptors):
             tp = d.get("tp_world", 1)
             for name, shape, off in d["entries"]:
                 en = engine_name(name)
-                if tp > 1 and en != name:
+                # a TP shard: renamed (dense TP modules) or narrower than the full
+                # tensor under the same name (tensor-parallel experts)
+                if tp > 1 and (en != name or tuple(shape) != full_shape.get(en, tuple(shape))):
                     shards.setdefault(en, {}).setdefault(int(d["tp_rank"]), []).append((j, int(off), tuple(shape)))
                 else:
                     whole.setdefault(en, []).append((j, int(off)))
@@ -212,18 +215,24 @@ class ShardedWeightPuller:
                 per = shards[name]
                 P = len(per)
                 full = tuple(shape)
-                cols = full[1] if len(full) > 1 else 1
                 for r in range(P):
                     j, loff, lshape = pick(per[r], n * esz // P)
-                    lcols = lshape[1] if len(lshape) > 1 else 1
                     acc = 0
                     for dim, start, length in tp_slices(name, full, args, r, P):
-                        if dim == 0:
-                            blocks.append((j, (loff + acc * lcols) * esz, dst0 + start * cols * esz, 1,
-                                           length * cols * esz, 0, 0))
+                        # the piece is `outer` rows (one per index of the leading
+                        # dimensions) of length x inner contiguous elements
+                        inner = 1
+                        for x in full[dim + 1:]:
+                            inner *= x
+                        outer = 1
+                        for x in full[:dim]:
+                            outer *= x
+                        src, dst = (loff + acc * inner) * esz, dst0 + start * inner * esz
+                        if outer == 1:
+                            blocks.append((j, src, dst, 1, length * inner * esz, 0, 0))
                         else:
-                            blocks.append((j, (loff + acc) * esz, dst0 + start * esz, full[0], length * esz,
-                                           lcols * esz, cols * esz))
+                            blocks.append((j, src, dst, outer, length * inner * esz, lshape[dim] * inner * esz,
+                                           full[dim] * inner * esz))
                         acc += length
             elif name in whole:
                 j, soff = pick(whole[name], n * esz)

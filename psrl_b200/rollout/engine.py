@@ -947,8 +947,10 @@ class RolloutEngine:
     def _moe_routed(self, h, pre):
         from ..ops import moe as moe_ops
         from ..parallel.moe import moe_forward_local
-        if self.tp is not None:
+        if self.tp is not None and self.w[pre + "mlp.experts_w13"].shape[0] < self.args.num_experts:
             return self._moe_routed_ep(h, pre)
+        # (a TP engine holding every expert at 1/P of its width, from a TP trainer's
+        # shards, runs the plain path: its partial output joins the all-reduce)
         a, W = self.args, self.w
         if moe_ops.supported(h, W[pre + "mlp.experts_w13"], W[pre + "mlp.experts_w2"]):
             return moe_ops.moe_mlp(h, F.linear(h, W[pre + "mlp.router.weight"]).float(), W[pre + "mlp.router_prior"],

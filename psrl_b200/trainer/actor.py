@@ -117,6 +117,9 @@ class PolicyWorker:
             self.tp = make_tp_group(tp_group, device, fused)
             self.tp_sharded = set(apply_tensor_parallel(self.model, self.tp))
         ep_size = int(cfg.actor.get("expert_parallel_size", 1) or 1)
+        if args.is_moe and ep_size > 1 and self.tp is not None:
+            raise ValueError("tensor parallelism splits each expert's width (ETP); combining it with expert "
+                             "parallelism is not implemented")
         if args.is_moe and ep_size > 1:
             # expert parallelism over the data-parallel group: rank r keeps
             # experts [r E/P, (r+1) E/P) of every layer (K12)

@@ -54,13 +54,19 @@ def _full_model_from_shards(worker):
 def _shard_into(worker, full) -> None:
     """Copy this rank's shards of an unsharded model into a TP / EP worker."""
     fp = {n: p.detach() for n, p in full.named_parameters()}
-    if worker.tp is not None:
-        from ..parallel.assemble import engine_name
-        from ..parallel.tp import shard_engine_tensors
-        fp = shard_engine_tensors(worker.args, fp, worker.tp)
     with torch.no_grad():
         for n, p in worker.model.named_parameters():
-            src = fp[engine_name(n)] if worker.tp is not None else fp[n]
+            if worker.tp is not None:
+                # the trainer's TP layout (``models.converters.tp_slices``): heads,
+                # MLP width and, for MoE, every expert's width
+                from ..models.converters import shard_tensor
+                from ..parallel.assemble import engine_name
+                en = engine_name(n)
+                src = fp[en]
+                if n in worker.tp_sharded:
+                    src = shard_tensor(src, en, worker.args, worker.tp.rank, worker.tp.world)
+            else:
+                src = fp[n]
             if worker.ep is not None and "experts_w" in n:
                 src = src[worker.ep.first: worker.ep.first + worker.ep.local]
             p.copy_(src.to(p.dtype))

@@ -247,6 +247,17 @@ def test_gloo_world2_hybrid_expert_parallel_moe():
     assert abs(res[0]["engine"] - res[1]["engine"]) < 1e-6 * max(1.0, abs(res[0]["engine"]))
 
 
+@pytest.mark.parametrize("rollout_tp", [1, 2])
+def test_gloo_world2_hybrid_expert_tensor_parallel_moe(rollout_tp):
+    """MoE trainer at TP=2 with every expert split along its width; the
+    engines take the assembled full model (rollout TP 1) or the trainer's own
+    shards (rollout TP 2, the engine then runs width-split experts)."""
+    res = _run_sharded(["model.preset=tiny-moe", "++actor.tensor_parallel_size=2",
+                        f"rollout.tensor_parallel_size={rollout_tp}"])
+    assert res[0]["steps"] == [32, 32]
+    assert abs(res[0]["engine"] - res[1]["engine"]) < 1e-6 * max(1.0, abs(res[0]["engine"])) or rollout_tp > 1
+
+
 def test_gloo_world2_hybrid_expert_parallel_in_reward_kl():
     """MoE at EP=2 with in-reward KL (adaptive coefficient), the KL loss and
     trainer-side old log-probs, with a token budget small enough that the two
@@ -476,12 +487,21 @@ def test_gloo_world5_disaggregated_heterogeneous_rollout():
     assert res["steps"] == [32, 32] and res["pulls"] >= 3
 
 
-def test_gloo_world4_disaggregated_moe_expert_parallel_rollout():
-    """MoE: an expert-parallel trainer pair publishes its experts; one rollout
-    instance of two ranks splits the experts between them (expert parallelism
-    following rollout TP) after pulling the full model."""
-    res = _run_disagg(["model.preset=tiny-moe", "++actor.expert_parallel_size=2",
-                       "rollout.tensor_parallel_size=2"], world=4)
+@pytest.mark.parametrize("trainer", ["++actor.expert_parallel_size=2", "++actor.tensor_parallel_size=2"])
+def test_gloo_world4_disaggregated_moe_expert_parallel_rollout(trainer):
+    """MoE: an expert-parallel (or expert-tensor-parallel) trainer pair
+    publishes its experts; one rollout instance of two ranks splits the
+    experts between them (expert parallelism following rollout TP) after
+    pulling the full model."""
+    res = _run_disagg(["model.preset=tiny-moe", trainer, "rollout.tensor_parallel_size=2"], world=4)
+    assert res["steps"] == [32, 32] and res["pulls"] >= 2
+
+
+def test_gloo_world3_disaggregated_expert_tensor_parallel_trainer():
+    """MoE with trainer TP=2 (every expert split along its width): both ranks
+    publish their shards, the rollout rank assembles the full experts while
+    it pulls."""
+    res = _run_disagg(["model.preset=tiny-moe", "++actor.tensor_parallel_size=2"])
     assert res["steps"] == [32, 32] and res["pulls"] >= 2
 
 

@@ -1,5 +1,6 @@
 """Comm planning (finest shard mesh, balancing, merging) and TP layouts."""
 
+import pytest
 import torch
 
 from psrl_b200.models import PRESETS, build_model
@@ -43,8 +44,11 @@ def test_merge_contiguous():
     assert len(merge_contiguous(segs)) == 2
 
 
-def test_tp_slices_reconstruct_and_segments():
-    a = PRESETS["tiny128"]
+@pytest.mark.parametrize("preset", ["tiny128", "tiny-moe-shared"])
+def test_tp_slices_reconstruct_and_segments(preset):
+    from dataclasses import replace
+    a = PRESETS[preset] if preset != "tiny-moe-shared" else replace(PRESETS["tiny-moe"],
+                                                                     shared_expert_intermediate_size=128)
     m = build_model(a, "cpu", torch.float32)
     for name, p in m.named_parameters():
         t = 2

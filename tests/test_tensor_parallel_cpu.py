@@ -119,11 +119,13 @@ def _assemble_worker(rank, world, port, q):
     from psrl_b200.trainer.actor import PolicyWorker
     init_distributed("cpu", timeout_s=300)
     worst = {}
-    for preset, kw in (("tiny", {"tp_group": dist.group.WORLD}),
-                       ("tiny-moe", {"dp_group": dist.group.WORLD, "dp_rank": rank, "dp_world": world})):
+    for label, preset, kw, ep in (
+            ("tiny", "tiny", {"tp_group": dist.group.WORLD}, 2),
+            ("tiny-moe", "tiny-moe", {"dp_group": dist.group.WORLD, "dp_rank": rank, "dp_world": world}, 2),
+            ("tiny-moe-tp", "tiny-moe", {"tp_group": dist.group.WORLD}, 1)):
         a = PRESETS[preset]
         cfg = load_config(preset="cpu_tiny_grpo", overrides=[f"model.preset={preset}",
-                                                             "++actor.expert_parallel_size=2"])
+                                                             f"++actor.expert_parallel_size={ep}"])
         w = PolicyWorker(cfg, a, "cpu", seed=9, **kw)
         asm = FullWeightAssembler(w.model, ep=w.ep, tp=w.tp,
                                   ep_names=[n for n, _ in w.model.named_parameters() if "experts_w" in n]
@@ -133,14 +135,14 @@ def _assemble_worker(rank, world, port, q):
         asm.gather()
         asm.assemble_into(eng.tensors)
         ref = dict(build_model(a, "cpu", torch.float32, seed=9).named_parameters())
-        worst[preset] = max(float((eng.tensors[n] - p.detach()).abs().max()) for n, p in ref.items())
+        worst[label] = max(float((eng.tensors[n] - p.detach()).abs().max()) for n, p in ref.items())
     q.put(worst)
     dist.destroy_process_group()
 
 
 def test_full_weight_assembly_from_tp_and_ep_shards():
-    """The rollout engine's full weights assembled from TP / EP shards equal
-    the unsharded model's weights exactly."""
+    """The rollout engine's full weights assembled from TP / EP shards (and
+    from tensor-parallel experts) equal the unsharded model's weights exactly."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -152,7 +154,7 @@ def test_full_weight_assembly_from_tp_and_ep_shards():
     assert [p.exitcode for p in procs] == [0, 0]
     for _ in range(2):
         w = q.get(timeout=5)
-        assert w["tiny"] == 0.0 and w["tiny-moe"] == 0.0, w
+        assert w["tiny"] == 0.0 and w["tiny-moe"] == 0.0 and w["tiny-moe-tp"] == 0.0, w
 
 
 def _engine_worker(rank, world, port, q, preset="tiny", shared=0):
@@ -230,12 +232,14 @@ def _ckpt_worker(rank, world, port, q, path):
     from psrl_b200.utils.checkpoint import load_worker, save_worker
     init_distributed("cpu", timeout_s=300)
     out = {"rank": rank}
-    for preset, kw in (("tiny", {"tp_group": dist.group.WORLD}),
-                       ("tiny-moe", {"dp_group": dist.group.WORLD, "dp_rank": rank, "dp_world": world})):
+    for label, preset, kw, ep in (
+            ("tiny", "tiny", {"tp_group": dist.group.WORLD}, 2),
+            ("tiny-moe", "tiny-moe", {"dp_group": dist.group.WORLD, "dp_rank": rank, "dp_world": world}, 2),
+            ("tiny-moe-tp", "tiny-moe", {"tp_group": dist.group.WORLD}, 1)):
         a = PRESETS[preset]
         cfg = load_config(preset="cpu_tiny_grpo", overrides=[f"model.preset={preset}",
-                                                             "++actor.expert_parallel_size=2"])
-        d = os.path.join(path, preset)
+                                                             f"++actor.expert_parallel_size={ep}"])
+        d = os.path.join(path, label)
         w = PolicyWorker(cfg, a, "cpu", seed=21, **kw)
         save_worker(w, d, rank)
         dist.barrier()
@@ -244,12 +248,12 @@ def _ckpt_worker(rank, world, port, q, path):
         load_hf_into(full, d)
         ref = build_model(a, "cpu", torch.float32, seed=21)
         rp = dict(ref.named_parameters())
-        out[preset + "_hf"] = max(float((p.detach() - rp[n].detach()).abs().max()) for n, p in full.named_parameters())
+        out[label + "_hf"] = max(float((p.detach() - rp[n].detach()).abs().max()) for n, p in full.named_parameters())
         # a differently initialised sharded worker reloads the same shards
         w2 = PolicyWorker(cfg, a, "cpu", seed=99, **kw)
         load_worker(w2, d, rank)
         p1 = dict(w.model.named_parameters())
-        out[preset + "_reload"] = max(float((p.detach() - p1[n].detach()).abs().max())
+        out[label + "_reload"] = max(float((p.detach() - p1[n].detach()).abs().max())
                                       for n, p in w2.model.named_parameters())
     q.put(out)
     dist.destroy_process_group()
@@ -268,5 +272,85 @@ def test_sharded_worker_checkpoint_roundtrip(tmp_path):
     assert [p.exitcode for p in procs] == [0, 0]
     for _ in range(2):
         r = q.get(timeout=5)
-        for k in ("tiny_hf", "tiny_reload", "tiny-moe_hf", "tiny-moe_reload"):
+        for k in ("tiny_hf", "tiny_reload", "tiny-moe_hf", "tiny-moe_reload", "tiny-moe-tp_hf", "tiny-moe-tp_reload"):
             assert r[k] == 0.0, r
+
+
+def _etp_worker(rank, world, port, q, shared):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    from dataclasses import replace
+    import torch
+    import torch.distributed as dist
+    torch.set_num_threads(1)
+    from psrl_b200.config import load_config
+    from psrl_b200.models import PRESETS, packed_positions
+    from psrl_b200.parallel.dist import init_distributed
+    from psrl_b200.trainer.actor import PolicyWorker
+    init_distributed("cpu", timeout_s=300)
+    a = replace(PRESETS["tiny-moe"], shared_expert_intermediate_size=shared)
+    cfg = load_config(preset="cpu_tiny_grpo", overrides=["model.preset=tiny-moe", "actor.optim.lr=1e-2",
+                                                         "actor.optim.eps=1.0"])
+    ref = PolicyWorker(cfg, a, "cpu", seed=3)
+    tpw = PolicyWorker(cfg, a, "cpu", seed=3, tp_group=dist.group.WORLD)
+    g = torch.Generator().manual_seed(7)
+    lens = [11, 17, 6]
+    ids = torch.randint(0, a.vocab_size, (sum(lens),), generator=g)
+    pos, cu, mx = packed_positions(lens, "cpu")
+    coef = torch.randn(sum(lens), a.hidden_size, generator=g)
+    out = {"rank": rank}
+    hr = ref.model.hidden_states(ids, pos, cu, mx)
+    ht = tpw.model.hidden_states(ids, pos, cu, mx)
+    out["fwd"] = float((hr - ht).detach().abs().max() / hr.detach().abs().max())
+    (hr * coef).sum().backward()
+    (ht * coef).sum().backward()
+
+    def grad(dp, p):
+        b, off = dp.param_to_bucket[p]
+        return b.grad[off: off + p.numel()].view(p.shape)
+
+    I, il = a.moe_intermediate_size, a.moe_intermediate_size // 2
+    m_ref, m_tp = ref.model.layers[0].mlp, tpw.model.layers[0].mlp
+    g_w2 = grad(ref.dp, m_ref.experts_w2)[:, :, rank * il:(rank + 1) * il]
+    g_w13 = grad(ref.dp, m_ref.experts_w13)
+    g_w13 = torch.cat([g_w13[:, rank * il:(rank + 1) * il], g_w13[:, I + rank * il:I + (rank + 1) * il]], dim=1)
+    errs = [float((g_w2 - grad(tpw.dp_partner, m_tp.experts_w2)).abs().max() / g_w2.abs().max()),
+            float((g_w13 - grad(tpw.dp_partner, m_tp.experts_w13)).abs().max() / g_w13.abs().max())]
+    # replicated router: the summed partial gradients equal the unsharded gradient
+    g_r = grad(ref.dp, m_ref.router.weight)
+    errs.append(float((g_r - grad(tpw.dp, m_tp.router.weight)).abs().max() / g_r.abs().max()))
+    if shared:
+        g_s = grad(ref.dp, m_ref.shared_gate.weight)
+        errs.append(float((g_s - grad(tpw.dp, m_tp.shared_gate.weight)).abs().max() / g_s.abs().max()))
+    out["grad"] = max(errs)
+    sr = ref.dp.step()
+    st = tpw.dp.step(partners=[tpw.dp_partner])
+    out["norm"] = (float(sr["grad_norm"]), float(st["grad_norm"]))
+    w2_new = m_ref.experts_w2[:, :, rank * il:(rank + 1) * il]
+    out["param_diff"] = max(float((w2_new - m_tp.experts_w2).detach().abs().max()),
+                            float((m_ref.router.weight - m_tp.router.weight).detach().abs().max()))
+    q.put(out)
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("shared", [0, 128])
+def test_expert_tensor_parallel_matches_unsharded_moe(shared):
+    """TP=2 on a MoE decoder (each expert's width split, router replicated, its
+    partial gradients summed over the group): forward, gradients, grad norm
+    and the updated parameters equal the unsharded worker's, with and without
+    a shared expert."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_etp_worker, args=(r, 2, port, q, shared)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(900)
+    assert [p.exitcode for p in procs] == [0, 0]
+    for r in [q.get(timeout=5) for _ in range(2)]:
+        assert r["fwd"] < 1e-5, r
+        assert r["grad"] < 1e-5, r
+        nr, nt = r["norm"]
+        assert abs(nr - nt) < 1e-4 * max(1.0, nr), r
+        assert r["param_diff"] < 1e-5, r

@@ -27,13 +27,20 @@ def _store(entries_tensors):
     return {"kind": "shm", "tensor": flat, "entries": entries}
 
 
-@pytest.mark.parametrize("P,nkv", [(2, 2), (4, 2)])
-def test_tensor_parallel_shards_pull_into_full_layout(P, nkv):
+@pytest.mark.parametrize("P,nkv,moe", [(2, 2, False), (4, 2, False), (2, 2, True)])
+def test_tensor_parallel_shards_pull_into_full_layout(P, nkv, moe):
+    """TP trainer shards (for MoE: every expert, and the shared expert, split
+    along its width under the unsharded name) are copied into the full layout."""
     from psrl_b200.models import PRESETS, build_model
     from psrl_b200.models.converters import shard_tensor
     from psrl_b200.parallel.assemble import _TP_NAMES
     from psrl_b200.parallel.weight_sync import ShardedWeightPuller
-    a = replace(PRESETS["tiny"], num_heads=8, num_kv_heads=nkv, head_dim=16, hidden_size=128, intermediate_size=256)
+    if moe:
+        a = replace(PRESETS["tiny-moe"], num_heads=8, num_kv_heads=nkv, head_dim=16, hidden_size=128,
+                    moe_intermediate_size=64, shared_expert_intermediate_size=64)
+    else:
+        a = replace(PRESETS["tiny"], num_heads=8, num_kv_heads=nkv, head_dim=16, hidden_size=128,
+                    intermediate_size=256)
     m = build_model(a, "cpu", torch.float32, seed=1)
     full = dict(m.named_parameters())
     inv = {v: k for k, v in _TP_NAMES.items()}
@@ -44,6 +51,8 @@ def test_tensor_parallel_shards_pull_into_full_layout(P, nkv):
             suffix = next((k for k in inv if n.endswith(k)), None)
             if suffix is not None:                       # sharded: the TP trainer's local name
                 items.append((n[: -len(suffix)] + inv[suffix], shard_tensor(t.detach(), n, a, r, P)))
+            elif "experts_w" in n or "shared_gate_up" in n or "shared_down" in n:
+                items.append((n, shard_tensor(t.detach(), n, a, r, P)))   # expert TP: same name
             else:
                 items.append((n, t.detach()))
         d = _store(items)
