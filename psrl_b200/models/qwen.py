@@ -34,6 +34,7 @@ from torch.utils.checkpoint import checkpoint
 from .. import ops
 from ..ops.linear import gate_up_swiglu, linear
 from ..parallel.cp import CPPlan, cp_attention
+from ..parallel.ulysses import UlyssesPlan, ulysses_attention
 from .config import ModelArgs
 
 
@@ -69,6 +70,10 @@ class Attention(nn.Module):
             # context parallel: this rank's query chunks over the gathered keys
             o = cp_attention(qkv[:, : a.q_size], qkv[:, a.q_size:], cu_seqlens, a.num_heads, a.num_kv_heads,
                              a.head_dim)
+        elif isinstance(cu_seqlens, UlyssesPlan):
+            # Ulysses: all-to-all to head-parallel attention over the whole micro-batch and back
+            o = ulysses_attention(qkv[:, : a.q_size], qkv[:, a.q_size:], cu_seqlens, a.num_heads,
+                                  a.num_kv_heads, a.head_dim)
         else:
             o = ops.varlen_attention(qkv, cu_seqlens, max_seqlen, a.num_heads, a.num_kv_heads, a.head_dim)
         return linear(o, self.o.weight)
@@ -210,7 +215,7 @@ class QwenModel(nn.Module):
     # --------------------------------------------------------------- forward
     def hidden_states(self, input_ids, positions, cu_seqlens, max_seqlen):
         a = self.args
-        if a.sliding_window is not None and not isinstance(cu_seqlens, CPPlan):
+        if a.sliding_window is not None and not isinstance(cu_seqlens, (CPPlan, UlyssesPlan)):
             a.check_context(int(max_seqlen))
         x = self.embed(input_ids)
         if a.embed_scale:

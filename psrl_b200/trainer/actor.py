@@ -69,7 +69,8 @@ def plan_update(trajs: list[Trajectory], mini_batch_size: int, dp_world: int) ->
 
 class PolicyWorker:
     def __init__(self, cfg, args: ModelArgs, device, dp_group=None, seed: int = 0, trainable: bool = True,
-                 dp_rank: int = 0, dp_world: int = 1, tp_group=None, cp_group=None, pp_group=None):
+                 dp_rank: int = 0, dp_world: int = 1, tp_group=None, cp_group=None, pp_group=None,
+                 cp_mode: str = "zigzag"):
         self.cfg = cfg
         self.args = args
         self.device = torch.device(device)
@@ -86,6 +87,11 @@ class PolicyWorker:
         # the sequence (dp_rank / dp_world index the CP groups; dp_group spans
         # every rank, so gradients sum over data and context parallelism)
         self.cp_group = cp_group if cp_group is not None and dist_world(cp_group) > 1 else None
+        # "zigzag": context parallelism (keys / values all-gathered); "ulysses":
+        # contiguous token slices, head-parallel attention between two all-to-alls
+        if cp_mode not in ("zigzag", "ulysses"):
+            raise ValueError(f"unknown sequence-parallel mode {cp_mode!r}")
+        self.cp_mode = cp_mode
         # pipeline parallelism: this rank runs one stage of the layers (dp_group
         # then joins the same stage of every pipeline; the clip norm spans the stages)
         self.pp = None
@@ -223,6 +229,12 @@ class PolicyWorker:
             local = local.cpu()
         return [(mine, max(1.0, float(n)), ns) for (mine, _, ns), n in zip(plan, local.tolist())]
 
+    def _new_shard(self, cu_seqlens):
+        if self.cp_mode == "ulysses":
+            from ..parallel.ulysses import UlyssesShard
+            return UlyssesShard(cu_seqlens, self.cp_group)
+        return CPShard(cu_seqlens, self.cp_group)
+
     def _cp_shard(self, mb):
         """Under context parallelism, replace ``mb``'s per-token tensors in place
         by this rank's share (``cu_seqlens`` becomes the :class:`CPPlan`) and
@@ -230,7 +242,7 @@ class PolicyWorker:
         otherwise leave ``mb`` alone and return the identity."""
         if self.cp_group is None:
             return lambda t: t
-        sh = CPShard(mb.cu_seqlens, self.cp_group)
+        sh = self._new_shard(mb.cu_seqlens)
         mb.input_ids = sh.local(mb.input_ids)
         mb.labels = sh.local(mb.labels)
         mb.loss_mask = sh.local(mb.loss_mask, 0.0)
@@ -282,7 +294,7 @@ class PolicyWorker:
                 continue
             mb = build_micro_batch(trajs, bin_, self.device)
             if self.cp_group is not None:
-                sh = CPShard(mb.cu_seqlens, self.cp_group)
+                sh = self._new_shard(mb.cu_seqlens)
                 lp, _ = self.model.logprobs(sh.local(mb.input_ids), sh.positions(), sh.plan, sh.plan.max_q,
                                             sh.local(mb.labels), temperature)
                 lp = sh.full(lp.float())
@@ -310,7 +322,7 @@ class PolicyWorker:
                 continue
             mb = build_micro_batch(trajs, bin_, self.device)
             if self.cp_group is not None:
-                sh = CPShard(mb.cu_seqlens, self.cp_group)
+                sh = self._new_shard(mb.cu_seqlens)
                 v = sh.full(self.model.values(sh.local(mb.input_ids), sh.positions(), sh.plan,
                                               sh.plan.max_q).float()).cpu()
             else:

@@ -90,6 +90,13 @@ class DisaggregatedRun:
         meg = cfg.actor.get("megatron", None) or {}
         tp = max(int(cfg.actor.get("tensor_parallel_size", 1) or 1), int(meg.get("tensor_model_parallel_size", 1) or 1))
         cpn = max(int(cfg.actor.get("context_parallel_size", 1) or 1), int(meg.get("context_parallel_size", 1) or 1))
+        # Ulysses sequence parallelism (veRL's name) takes the context-parallel groups
+        usp = int(cfg.actor.get("ulysses_sequence_parallel_size", 1) or 1)
+        self.cp_mode = "zigzag"
+        if usp > 1:
+            if cpn > 1:
+                raise ValueError("context parallelism and Ulysses sequence parallelism are alternatives; set one")
+            cpn, self.cp_mode = usp, "ulysses"
         ppn = max(int(cfg.actor.get("pipeline_parallel_size", 1) or 1),
                   int(meg.get("pipeline_model_parallel_size", 1) or 1))
         if sum(x > 1 for x in (tp, cpn, ppn)) > 1:
@@ -182,7 +189,7 @@ class DisaggregatedRun:
         cfg = self.cfg
         self.actor = PolicyWorker(cfg, self.args, self.device, dp_group=self.train_group,
                                   seed=int(cfg.trainer.seed), dp_rank=self.dp_rank, dp_world=self.dp_world,
-                                  tp_group=self.tp_group, cp_group=self.cp_group,
+                                  tp_group=self.tp_group, cp_group=self.cp_group, cp_mode=self.cp_mode,
                                   pp_group=self.pp_group)
         self.assembler = None
         self.pub_parts = None
@@ -218,14 +225,14 @@ class DisaggregatedRun:
             cargs = _replace(self.args, value_head=True, tie_word_embeddings=False)
             self.critic = PolicyWorker(cfg, cargs, self.device, dp_group=self.train_group,
                                        seed=int(cfg.trainer.seed) + 1, dp_rank=self.dp_rank, dp_world=self.dp_world,
-                                       tp_group=self.tp_group, cp_group=self.cp_group,
+                                       tp_group=self.tp_group, cp_group=self.cp_group, cp_mode=self.cp_mode,
                                        pp_group=self.pp_group)
         self.ref = None
         if cfg.actor.use_kl_loss or cfg.algorithm.use_kl_in_reward:
             # sharded like the actor (expert / tensor parallel forwards are collectives)
             self.ref = PolicyWorker(cfg, self.args, self.device, dp_group=self.train_group,
                                     seed=int(cfg.trainer.seed), trainable=False, dp_rank=self.dp_rank,
-                                    dp_world=self.dp_world, tp_group=self.tp_group, cp_group=self.cp_group,
+                                    dp_world=self.dp_world, tp_group=self.tp_group, cp_group=self.cp_group, cp_mode=self.cp_mode,
                                     pp_group=self.pp_group)
         self.kl_ctrl = algos.kl_controller(cfg.algorithm) if cfg.algorithm.use_kl_in_reward else None
         self.sharded_overlap = sharded_overlap_enabled(cfg)

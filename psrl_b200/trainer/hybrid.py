@@ -87,8 +87,9 @@ class HybridRun:
         # trainer layout: tensor-parallel groups of `tp` consecutive ranks, data
         # parallelism across them (expert parallelism spans the data-parallel group)
         if int(cfg.actor.get("context_parallel_size", 1) or 1) > 1 or \
+                int(cfg.actor.get("ulysses_sequence_parallel_size", 1) or 1) > 1 or \
                 int(cfg.actor.get("pipeline_parallel_size", 1) or 1) > 1:
-            raise ValueError("context and pipeline parallelism run in the disaggregated placement")
+            raise ValueError("context / sequence and pipeline parallelism run in the disaggregated placement")
         tp = int(cfg.actor.get("tensor_parallel_size", 1) or 1)
         if self.world % tp:
             raise ValueError(f"world size {self.world} is not a multiple of tensor_parallel_size={tp}")

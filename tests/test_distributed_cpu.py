@@ -530,6 +530,12 @@ def test_gloo_world3_disaggregated_interleaved_pipeline_trainer():
     assert res["steps"] == [32, 32] and res["pulls"] >= 2
 
 
+def test_gloo_world3_disaggregated_ulysses_trainer():
+    """Two trainer ranks splitting every micro-batch's tokens (Ulysses SP=2)."""
+    res = _run_disagg(["++actor.ulysses_sequence_parallel_size=2"])
+    assert res["steps"] == [32, 32] and res["pulls"] >= 2
+
+
 def test_gloo_world3_disaggregated_context_parallel_trainer():
     """Two trainer ranks splitting every sequence (CP=2)."""
     res = _run_disagg(["++actor.context_parallel_size=2"])
