@@ -252,10 +252,15 @@ def shard_engine_tensors(args, tensors: dict, tp: TPGroup) -> dict:
     and so on), in the layout the TP trainer's shards and a TP rollout engine
     use; replicated tensors are shared, not copied."""
     d, r, P = args.head_dim, tp.rank, tp.world
-    qn, kn = args.num_heads // P * d, args.num_kv_heads // P * d
+    qn = args.num_heads // P * d
+    if args.num_kv_heads >= P:
+        kn, k0 = args.num_kv_heads // P * d, r * (args.num_kv_heads // P) * d
+    else:
+        # more ranks than KV heads: the KV head this rank's query heads read (replicated)
+        kn, k0 = d, (r * args.num_kv_heads // P) * d
     il = args.intermediate_size // P
-    rows = torch.cat([torch.arange(r * qn, (r + 1) * qn), args.q_size + torch.arange(r * kn, (r + 1) * kn),
-                      args.q_size + args.kv_size + torch.arange(r * kn, (r + 1) * kn)])
+    rows = torch.cat([torch.arange(r * qn, (r + 1) * qn), args.q_size + torch.arange(k0, k0 + kn),
+                      args.q_size + args.kv_size + torch.arange(k0, k0 + kn)])
     out = {}
     for n, t in tensors.items():
         if n.endswith("attn.qkv.weight") or n.endswith("attn.qkv.bias"):

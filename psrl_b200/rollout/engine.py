@@ -184,10 +184,16 @@ class RolloutEngine:
                 raise ValueError("expert parallelism over the TP group needs experts (and the shared expert's "
                                  "width) divisible by the TP size")
             from dataclasses import replace
+            if args.num_heads % tp.world or (args.num_kv_heads % tp.world and tp.world % args.num_kv_heads):
+                raise ValueError(f"{args.num_heads} query / {args.num_kv_heads} KV heads do not split over "
+                                 f"TP={tp.world}")
+            # more TP ranks than KV heads: each rank keeps the one KV head its query
+            # heads read (replicated over the tp.world / nkv ranks that share it)
             # MoE: expert parallelism follows TP: rank r holds experts [r E/P, (r+1) E/P)
             # at full width (routing still spans all E experts) and 1/P of the
             # shared expert's width; its partial output joins the MLP all-reduce
-            args = replace(args, num_heads=args.num_heads // tp.world, num_kv_heads=args.num_kv_heads // tp.world,
+            args = replace(args, num_heads=args.num_heads // tp.world,
+                           num_kv_heads=max(1, args.num_kv_heads // tp.world),
                            intermediate_size=args.intermediate_size // tp.world,
                            shared_expert_intermediate_size=args.shared_expert_intermediate_size // tp.world)
         else:

@@ -197,22 +197,24 @@ def _engine_worker(rank, world, port, q, preset="tiny", shared=0):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("preset,shared", [("tiny", 0), ("tiny-moe", 0), ("tiny-moe", 128)])
-def test_tensor_parallel_rollout_engine_matches_single_rank(preset, shared):
-    """A TP=2 rollout engine (two gloo ranks, identical request streams) decodes
-    the same greedy tokens and log-probs as the unsharded engine; for MoE the
-    experts are split over the two ranks (expert parallelism follows TP), with
-    and without a TP-sharded shared expert."""
+@pytest.mark.parametrize("preset,shared,world", [("tiny", 0, 2), ("tiny-moe", 0, 2), ("tiny-moe", 128, 2),
+                                                 ("tiny", 0, 4)])
+def test_tensor_parallel_rollout_engine_matches_single_rank(preset, shared, world):
+    """A TP rollout engine (gloo ranks, identical request streams) decodes the
+    same greedy tokens and log-probs as the unsharded engine; for MoE the
+    experts are split over the ranks (expert parallelism follows TP), with and
+    without a TP-sharded shared expert; at TP=4 over 2 KV heads each KV head
+    is replicated on the two ranks whose query heads read it."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_engine_worker, args=(r, 2, port, q, preset, shared)) for r in range(2)]
+    procs = [ctx.Process(target=_engine_worker, args=(r, world, port, q, preset, shared)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(900)
-    assert [p.exitcode for p in procs] == [0, 0]
-    for _ in range(2):
+    assert [p.exitcode for p in procs] == [0] * world
+    for _ in range(world):
         r = q.get(timeout=5)
         assert r["same_tokens"], r
         assert r["lp_diff"] < 1e-4, r
