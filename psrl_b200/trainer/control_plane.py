@@ -73,6 +73,12 @@ class ControlPlane:
         self._batch_locks: dict[int, threading.Lock] = {}
         self._pre: dict[int, dict] = {}     # buffer -> request id -> per-sample fields computed early
         self._done = threading.Event()
+        # validation (trainer.test_freq): requests handed to instances before
+        # training work, their completions kept out of the training buffers
+        self._val_queue: list = []
+        self._val_pending: dict = {}         # request id -> (prompt item, meta)
+        self._val_done: list = []
+        self._val_round = 0
 
     # ----------------------------------------------------------------- setup
     def ping(self) -> bool:
@@ -130,11 +136,24 @@ class ControlPlane:
         iid = tuple(instance_id)
         now = time.monotonic()
         self.last_seen[iid] = now
+        if outputs and any(o.request_id >= self.VAL_RID_BASE for o in outputs):
+            # validation samples (late ones, after a timed-out round, are dropped)
+            with self._cv:
+                for o in outputs:
+                    item = self._val_pending.pop(o.request_id, None) if o.request_id >= self.VAL_RID_BASE else None
+                    if item is not None:
+                        self._val_done.append((item, o))
+                self._cv.notify_all()
+            outputs = [o for o in outputs if o.request_id < self.VAL_RID_BASE]
         if outputs:
             self.manager.on_complete(outputs, iid)
         sync = self._coordinate(iid, int(version), state, now)
         quarantined = iid in self.coord.quarantined
         reqs = []
+        if free_slots > 0 and not quarantined and self._val_queue:
+            with self._cv:
+                reqs, self._val_queue = self._val_queue[:free_slots], self._val_queue[free_slots:]
+            free_slots -= len(reqs)
         if free_slots > 0 and not quarantined:
             me = self.states[iid]
             peers = [s for i, s in self.states.items() if i not in self.coord.quarantined]
@@ -142,9 +161,10 @@ class ControlPlane:
             if len(peers) > 1:
                 # routing policy in pull mode (request balance, stickiness, cache affinity, ...)
                 accept = lambda req: self.router.accepts(req, me, peers)          # noqa: E731
-            reqs = self.manager.take_work(iid, int(version), int(free_slots), accept)
-            for r in reqs:
+            work = self.manager.take_work(iid, int(version), int(free_slots), accept)
+            for r in work:
                 self.router.assigned(r, me)
+            reqs = reqs + work
         aborts = self.manager.take_aborts(iid)
         st = self.exchange_stats
         st["calls"] += 1
@@ -182,6 +202,57 @@ class ControlPlane:
                     self.mig_stats["rounds"] += 1
                     self.mig_stats["requests"] += moved
         return sync
+
+    VAL_RID_BASE = 1 << 50
+
+    def validate(self, num_prompts: int | None = None, timeout_s: float = 1800.0) -> dict:
+        """Generate on the validation prompts on the rollout instances and score
+        them (``val/score_mean``, ``val/response_length/mean``,
+        ``val/num_samples``).  The requests go out before any training work in
+        the instances' next exchanges and carry the current PS version; their
+        completions never reach the training buffers.  Sampling as in the
+        one-process trainer's validation: ``trainer.val_temperature`` (0 =
+        greedy), ``psrl.val_rollout_n`` samples per prompt (the reference's
+        ``test_freq`` validation, ``psrl/trainer/ppo/ray_trainer.py``)."""
+        from ..rollout.engine import GenRequest, SamplingParams
+        from .batch import Trajectory
+        cfg = self.cfg
+        n = int(num_prompts if num_prompts is not None else cfg.data.get("val_size", 32))
+        per = max(1, int(cfg.psrl.get("val_rollout_n", 1)))
+        temp = float(cfg.trainer.get("val_temperature", 0.0))
+        rc = cfg.rollout
+        v = self.ps.get_ps_model_version()
+        items = self.data.validation_items(n)
+        with self._cv:
+            self._val_round += 1
+            base = self.VAL_RID_BASE + self._val_round * (1 << 32)
+            for i, it in enumerate(items):
+                for j in range(per):
+                    rid = base + i * per + j
+                    mt = int(it.response_lens[j % len(it.response_lens)]) if it.response_lens \
+                        else int(rc.max_response_length)
+                    params = SamplingParams(temperature=temp, top_p=1.0, top_k=-1, max_tokens=mt,
+                                            ignore_eos=bool(rc.ignore_eos), seed=rid)
+                    meta = dict(it.meta)
+                    if it.answer is not None:
+                        meta["answer"] = it.answer
+                    self._val_queue.append(GenRequest(rid, list(it.prompt_ids), params, v, meta))
+                    self._val_pending[rid] = (it, meta)
+            ok = self._cv.wait_for(lambda: not self._val_pending, timeout_s)
+            done, self._val_done = self._val_done, []
+            if not ok:
+                self._val_queue.clear()
+                self._val_pending.clear()
+                raise TimeoutError(f"validation: {len(done)} of {n * per} samples in {timeout_s:.0f} s")
+        scores, lens = [], []
+        for (it, meta), o in done:
+            tr = Trajectory(uid=it.uid, request_id=o.request_id, prompt_ids=list(o.prompt_ids),
+                            response_ids=list(o.output_ids), rollout_logprobs=list(o.logprobs), meta=meta)
+            scores.append(float(self.reward.score(tr)["score"]))
+            lens.append(len(o.output_ids))
+        m = len(scores)
+        return {"val/score_mean": sum(scores) / max(1, m), "val/response_length/mean": sum(lens) / max(1, m),
+                "val/num_samples": m}
 
     def acquire_pull(self, timeout: float = 600.0) -> bool:
         return self.ps.acquire_shared_pull(timeout)

@@ -325,6 +325,12 @@ class DisaggregatedRun:
                         "timing_s/gen_wait": t1 - t0, "timing_s/train": t2 - t1,
                         "timing_s/publish": time.perf_counter() - t2,
                         "timing_s/step": time.perf_counter() - t0})
+        tf = int(self.cfg.trainer.get("test_freq", -1) or -1)
+        if tf > 0 and self.global_step % tf == 0 and self.rank == 0:
+            # validation on the rollout instances with the weights just pushed
+            t3 = time.perf_counter()
+            metrics.update(self.cp.validate())
+            metrics["timing_s/validate"] = time.perf_counter() - t3
         return metrics
 
     # ------------------------------------------------------------ rollout

@@ -392,6 +392,12 @@ class HybridRun:
             "fine_grain/precomputed": pre,
         })
         metrics.update({f"rollout/{k}": v for k, v in self.engine.engine_stats().items() if isinstance(v, (int, float))})
+        tf = int(self.cfg.trainer.get("test_freq", -1) or -1)
+        if tf > 0 and self.global_step % tf == 0 and self.rank == 0:
+            # validation on the rollout instances with the weights just pushed
+            t3 = time.perf_counter()
+            metrics.update(self.cp.validate())
+            metrics["timing_s/validate"] = time.perf_counter() - t3
         return metrics
 
     def close(self) -> None:

@@ -217,7 +217,8 @@ def _worker_hybrid_sharded(rank, world, port, q, overrides):
            "kl": [m.get("actor/reward_kl_penalty") for m in res["metrics"]] if rank == 0 else None,
            "kl_coef": [m.get("actor/reward_kl_penalty_coeff") for m in res["metrics"]] if rank == 0 else None,
            "chunks": [m.get("fine_grain/chunks") for m in res["metrics"]] if rank == 0 else None,
-           "pre": [m.get("fine_grain/precomputed") for m in res["metrics"]] if rank == 0 else None})
+           "pre": [m.get("fine_grain/precomputed") for m in res["metrics"]] if rank == 0 else None,
+           "val": [m.get("val/num_samples") for m in res["metrics"]] if rank == 0 else None})
     import torch.distributed as dist
     dist.destroy_process_group()
 
@@ -237,6 +238,14 @@ def _run_sharded(overrides):
             p.kill()
     assert codes == [0, 0], codes
     return sorted([q.get(timeout=5) for _ in range(2)], key=lambda d: d["rank"])
+
+
+def test_gloo_world2_hybrid_validation():
+    """trainer.test_freq=1 in the hybrid placement: validation samples run on
+    the ranks' engines between steps and stay out of the training buffers."""
+    res = _run_sharded(["trainer.test_freq=1", "++data.val_size=4"])
+    assert res[0]["steps"] == [32, 32]
+    assert res[0]["val"] == [4, 4], res[0]
 
 
 def test_gloo_world2_hybrid_expert_parallel_moe():
@@ -330,6 +339,7 @@ def _worker_disagg_sharded(rank, world, port, q, overrides):
     res = run_disaggregated(cfg, steps=2, warmup=0, info=info)
     if rank == 0:
         q.put({"steps": [m["num_trajectories"] for m in res["metrics"]], "pulls": res["sync"]["pulls"],
+               "val": [m.get("val/num_samples") for m in res["metrics"]],
                "pre": [m.get("fine_grain/precomputed") for m in res["metrics"]],
                "kl": [m.get("actor/reward_kl_penalty") for m in res["metrics"]],
                "chunks": [m.get("fine_grain/chunks") for m in res["metrics"]]})
@@ -528,6 +538,15 @@ def test_gloo_world3_disaggregated_interleaved_pipeline_trainer():
     res = _run_disagg(["++model.overrides.num_layers=4", "++actor.pipeline_parallel_size=2",
                        "++actor.virtual_pipeline_parallel_size=2"])
     assert res["steps"] == [32, 32] and res["pulls"] >= 2
+
+
+def test_gloo_world3_disaggregated_validation():
+    """trainer.test_freq=1 in the disaggregated placement: after each step the
+    rollout instance generates the validation prompts, which are scored and
+    never enter a training buffer."""
+    res = _run_disagg(["trainer.test_freq=1", "++data.val_size=4"])
+    assert res["steps"] == [32, 32]
+    assert res["val"] == [4, 4], res
 
 
 def test_gloo_world3_disaggregated_ulysses_trainer():
