@@ -79,6 +79,23 @@ class ControlPlane:
         self._val_pending: dict = {}         # request id -> (prompt item, meta)
         self._val_done: list = []
         self._val_round = 0
+        # resume (trainer.resume_mode): data cursor and PS version of the latest
+        # checkpoint, set before any instance takes work
+        self._resumed = None
+        if str(cfg.trainer.get("resume_mode", "disable")) != "disable":
+            import torch as _torch
+            from ..utils.checkpoint import find_latest, step_dir
+            root = cfg.trainer.get("resume_from_path") or cfg.trainer.default_local_dir
+            step = find_latest(root)
+            if step is not None:
+                import os as _os
+                meta = _torch.load(_os.path.join(step_dir(root, step), "data.pt"), weights_only=False)
+                if meta.get("data"):
+                    self.data.load_state_dict(meta["data"])
+                self.ps.init_model_version_for_resume(step + 1)
+                self.manager.initial_ps_version = step
+                self.manager.request_counter = 0
+                self._resumed = int(step)
 
     # ----------------------------------------------------------------- setup
     def ping(self) -> bool:
@@ -204,6 +221,14 @@ class ControlPlane:
         return sync
 
     VAL_RID_BASE = 1 << 50
+
+    def resumed_step(self):
+        """The checkpoint step this run resumed from (None: a fresh start)."""
+        return self._resumed
+
+    def checkpoint_meta(self) -> dict:
+        """What a checkpoint keeps of the control plane: the data cursor and the PS version."""
+        return {"data": self.data.state_dict(), "ps_version": self.ps.get_ps_model_version()}
 
     def validate(self, num_prompts: int | None = None, timeout_s: float = 1800.0) -> dict:
         """Generate on the validation prompts on the rollout instances and score

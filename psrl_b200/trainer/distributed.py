@@ -239,7 +239,19 @@ class DisaggregatedRun:
         self.pre_step = sharded_overlap_mode(cfg) == "pre_step"
         mode = "hbm" if (cfg.psrl.ps_mode == "hbm" and self.device.type == "cuda") else "cpu"
         self.store = WeightStore(self.layout, self.device, mode)
-        self._publish(0)
+        # resume: the control plane already re-seated the data cursor and the PS
+        # version; every trainer rank loads its part of the same step
+        self.resumed = self.cp.resumed_step()
+        if self.resumed is not None:
+            from ..utils.checkpoint import load_trainer_ranks
+            root = cfg.trainer.get("resume_from_path") or cfg.trainer.default_local_dir
+            extra = load_trainer_ranks(root, self.resumed, self.actor, self.critic, self.rank,
+                                       bool(cfg.psrl.checkpoint.use_dcp_save), self._ckpt_group())
+            if self.kl_ctrl is not None and "kl_coef" in extra:
+                self.kl_ctrl.value = float(extra["kl_coef"])
+            self.global_step = self.resumed
+            log(f"trainer rank {self.rank}: resumed from step {self.resumed}")
+        self._publish(self.resumed or 0)
         if self.device.type == "cuda":
             torch.cuda.synchronize()
         desc = self.store.descriptor()
@@ -256,6 +268,28 @@ class DisaggregatedRun:
             self.cp.set_layout(engine_layout)
         self.cp.register_store(self.rank, desc)
         log(f"trainer ready: {self.layout.nbytes / 2**30:.2f} GiB published store ({mode})")
+
+    def _ckpt_group(self):
+        """The trainer ranks' gloo group (DCP must not wait for rollout ranks)."""
+        if self.train_cpu_group is not None:
+            return self.train_cpu_group
+        if getattr(self, "_solo_group", None) is None and dist.is_initialized():
+            self._solo_group = pdist.new_subgroup([self.rank], backend="gloo")
+        return getattr(self, "_solo_group", None)
+
+    def _save_checkpoint(self) -> None:
+        """Every trainer rank saves its part of ``global_step``; rank 0 then
+        adds the control plane's data cursor and marks the step complete."""
+        from ..utils.checkpoint import finish_trainer_checkpoint, save_trainer_ranks
+        cfg = self.cfg
+        root = cfg.trainer.default_local_dir
+        save_trainer_ranks(root, self.global_step, self.actor, self.critic, self.rank, None,
+                           bool(cfg.psrl.checkpoint.use_dcp_save), group=self._ckpt_group())
+        if self.n_train > 1:
+            dist.barrier(group=self.train_cpu_group)
+        if self.rank == 0:
+            extra = {"kl_coef": self.kl_ctrl.value} if self.kl_ctrl is not None else {}
+            finish_trainer_checkpoint(root, self.global_step, self.cp.checkpoint_meta(), extra)
 
     def _publish(self, version: int) -> None:
         if self.pub_parts is not None:
@@ -325,6 +359,11 @@ class DisaggregatedRun:
                         "timing_s/gen_wait": t1 - t0, "timing_s/train": t2 - t1,
                         "timing_s/publish": time.perf_counter() - t2,
                         "timing_s/step": time.perf_counter() - t0})
+        sf = int(self.cfg.trainer.get("save_freq", -1) or -1)
+        if sf > 0 and self.global_step % sf == 0:
+            t3 = time.perf_counter()
+            self._save_checkpoint()
+            metrics["timing_s/checkpoint"] = time.perf_counter() - t3
         tf = int(self.cfg.trainer.get("test_freq", -1) or -1)
         if tf > 0 and self.global_step % tf == 0 and self.rank == 0:
             # validation on the rollout instances with the weights just pushed

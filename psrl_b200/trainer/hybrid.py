@@ -150,6 +150,17 @@ class HybridRun:
             self.ref = PolicyWorker(cfg, self.args, self.device, dp_group=dp_group, seed=seed, trainable=False,
                                     dp_rank=self.dp_rank, dp_world=self.dp_world, tp_group=tp_group)
         self.kl_ctrl = algos.kl_controller(cfg.algorithm) if cfg.algorithm.use_kl_in_reward else None
+        # resume: the control plane already re-seated the data cursor and the PS
+        # version; every rank loads its part before the engine copies its weights
+        self.resumed = self.cp.resumed_step()
+        if self.resumed is not None:
+            from ..utils.checkpoint import load_trainer_ranks
+            root = cfg.trainer.get("resume_from_path") or cfg.trainer.default_local_dir
+            extra = load_trainer_ranks(root, self.resumed, self.actor, self.critic, self.rank,
+                                       bool(cfg.psrl.checkpoint.use_dcp_save))
+            if self.kl_ctrl is not None and "kl_coef" in extra:
+                self.kl_ctrl.value = float(extra["kl_coef"])
+            self.global_step = self.resumed
         self.sharded_overlap = sharded_overlap_enabled(cfg)
         self.pre_step = sharded_overlap_mode(cfg) == "pre_step"
         self.wlock = RWLock()
@@ -213,6 +224,22 @@ class HybridRun:
         self.pulls = 0
         self.pull_s = 0.0
         log(f"hybrid rank ready: trainer dp{self.world} + rollout instance {self.instance_id}")
+
+    def _save_checkpoint(self) -> None:
+        """Every rank saves its part of ``global_step`` (under the shared weight
+        lock, so no optimizer step runs meanwhile); rank 0 then adds the control
+        plane's data cursor and marks the step complete."""
+        from ..utils.checkpoint import finish_trainer_checkpoint, save_trainer_ranks
+        cfg = self.cfg
+        root = cfg.trainer.default_local_dir
+        with self.wlock.shared(600):
+            save_trainer_ranks(root, self.global_step, self.actor, self.critic, self.rank, None,
+                               bool(cfg.psrl.checkpoint.use_dcp_save))
+        if self.cpu_group is not None:
+            dist.barrier(group=self.cpu_group)
+        if self.rank == 0:
+            extra = {"kl_coef": self.kl_ctrl.value} if self.kl_ctrl is not None else {}
+            finish_trainer_checkpoint(root, self.global_step, self.cp.checkpoint_meta(), extra)
 
     # -------------------------------------------------------------- rollout
     def _pull(self, v: int | None = None) -> None:
@@ -392,6 +419,11 @@ class HybridRun:
             "fine_grain/precomputed": pre,
         })
         metrics.update({f"rollout/{k}": v for k, v in self.engine.engine_stats().items() if isinstance(v, (int, float))})
+        sf = int(self.cfg.trainer.get("save_freq", -1) or -1)
+        if sf > 0 and self.global_step % sf == 0:
+            t3 = time.perf_counter()
+            self._save_checkpoint()
+            metrics["timing_s/checkpoint"] = time.perf_counter() - t3
         tf = int(self.cfg.trainer.get("test_freq", -1) or -1)
         if tf > 0 and self.global_step % tf == 0 and self.rank == 0:
             # validation on the rollout instances with the weights just pushed

@@ -72,9 +72,15 @@ def _shard_into(worker, full) -> None:
             p.copy_(src.to(p.dtype))
 
 
-def save_worker(worker, path: str, rank: int = 0, use_dcp: bool = False) -> None:
+def save_worker(worker, path: str, rank: int = 0, use_dcp: bool = False, group=None) -> None:
+    """``group``: the process group of the ranks that save together (DCP's
+    coordination; default: every rank of the job)."""
     os.makedirs(path, exist_ok=True)
-    if _is_sharded(worker):
+    if getattr(worker, "pp", None) is not None:
+        # a pipeline stage holds only its layers: every rank keeps its own file
+        torch.save({k: v.detach().cpu() for k, v in worker.model.state_dict().items()},
+                   os.path.join(path, f"model_rank{rank}.pt"))
+    elif _is_sharded(worker):
         # HF export of the whole model, assembled from the TP / EP shards (collective)
         full = _full_model_from_shards(worker)
         if rank == 0:
@@ -87,16 +93,22 @@ def save_worker(worker, path: str, rank: int = 0, use_dcp: bool = False) -> None
     if use_dcp:
         import torch.distributed.checkpoint as dcp
         sd = {k: v.detach() for k, v in worker.model.state_dict().items()}
-        dcp.save(sd, checkpoint_id=os.path.join(path, "dcp"))
+        dcp.save(sd, checkpoint_id=os.path.join(path, "dcp"), process_group=group)
     if worker.dp is not None:
         torch.save(worker.dp.optimizer_state(), os.path.join(path, f"optim_rank{rank}.pt"))
 
 
-def load_worker(worker, path: str, rank: int = 0, use_dcp: bool = False) -> None:
-    if use_dcp and os.path.isdir(os.path.join(path, "dcp")):
+def load_worker(worker, path: str, rank: int = 0, use_dcp: bool = False, group=None) -> None:
+    stage_file = os.path.join(path, f"model_rank{rank}.pt")
+    if getattr(worker, "pp", None) is not None:
+        sd = torch.load(stage_file, map_location="cpu", weights_only=False)
+        with torch.no_grad():
+            for k, v in worker.model.state_dict().items():
+                v.copy_(sd[k].to(v.dtype))
+    elif use_dcp and os.path.isdir(os.path.join(path, "dcp")):
         import torch.distributed.checkpoint as dcp
         sd = {k: v.detach() for k, v in worker.model.state_dict().items()}
-        dcp.load(sd, checkpoint_id=os.path.join(path, "dcp"))
+        dcp.load(sd, checkpoint_id=os.path.join(path, "dcp"), process_group=group)
     elif _is_sharded(worker):
         from ..models.qwen import QwenModel
         full = QwenModel(worker.args)
@@ -159,3 +171,37 @@ def load_checkpoint(root: str, actor, data=None, critic=None, step: int | None =
     if extra_out is not None:
         extra_out.update(meta.get("extra") or {})
     return int(meta["global_step"])
+
+
+# --------------------------------------------------- multi-GPU placements
+def save_trainer_ranks(root: str, step: int, actor, critic, rank: int, meta: dict | None, use_dcp: bool = False,
+                       extra: dict | None = None, group=None) -> str:
+    """Every trainer rank of a multi-GPU placement calls this (the HF export of
+    TP / EP shards is collective); rank 0 also writes ``data.pt`` from
+    ``meta`` (the control plane's data cursor and PS version) and, last, the
+    latest-step marker, so a half-written step is never the one resumed."""
+    d = step_dir(root, step)
+    save_worker(actor, os.path.join(d, "actor"), rank, use_dcp, group)
+    if critic is not None:
+        save_worker(critic, os.path.join(d, "critic"), rank, use_dcp, group)
+    return d
+
+
+def finish_trainer_checkpoint(root: str, step: int, meta: dict | None, extra: dict | None = None) -> None:
+    """Rank 0, after every trainer rank saved its part (a barrier in between)."""
+    d = step_dir(root, step)
+    torch.save({"data": (meta or {}).get("data"), "ps_version": (meta or {}).get("ps_version"),
+                "global_step": step, "extra": dict(extra or {})}, os.path.join(d, "data.pt"))
+    with open(os.path.join(os.path.expanduser(root), LATEST), "w") as fh:
+        fh.write(str(step))
+
+
+def load_trainer_ranks(root: str, step: int, actor, critic, rank: int, use_dcp: bool = False, group=None) -> dict:
+    """Every trainer rank loads its part of step ``step``; returns the extra
+    trainer state saved beside the data cursor."""
+    d = step_dir(root, step)
+    load_worker(actor, os.path.join(d, "actor"), rank, use_dcp, group)
+    if critic is not None:
+        load_worker(critic, os.path.join(d, "critic"), rank, use_dcp, group)
+    meta = torch.load(os.path.join(d, "data.pt"), weights_only=False)
+    return dict(meta.get("extra") or {})

@@ -218,7 +218,8 @@ def _worker_hybrid_sharded(rank, world, port, q, overrides):
            "kl_coef": [m.get("actor/reward_kl_penalty_coeff") for m in res["metrics"]] if rank == 0 else None,
            "chunks": [m.get("fine_grain/chunks") for m in res["metrics"]] if rank == 0 else None,
            "pre": [m.get("fine_grain/precomputed") for m in res["metrics"]] if rank == 0 else None,
-           "val": [m.get("val/num_samples") for m in res["metrics"]] if rank == 0 else None})
+           "val": [m.get("val/num_samples") for m in res["metrics"]] if rank == 0 else None,
+           "step_ids": [m.get("step") for m in res["metrics"]] if rank == 0 else None})
     import torch.distributed as dist
     dist.destroy_process_group()
 
@@ -238,6 +239,16 @@ def _run_sharded(overrides):
             p.kill()
     assert codes == [0, 0], codes
     return sorted([q.get(timeout=5) for _ in range(2)], key=lambda d: d["rank"])
+
+
+def test_gloo_world2_hybrid_checkpoint_resume(tmp_path):
+    """The hybrid placement saves every step and a new run resumes after the
+    last saved step."""
+    d = str(tmp_path / "ckpt")
+    first = _run_sharded([f"trainer.default_local_dir={d}", "trainer.save_freq=1"])
+    assert first[0]["step_ids"] == [0, 1]
+    again = _run_sharded([f"trainer.default_local_dir={d}", "trainer.resume_mode=auto"])
+    assert again[0]["step_ids"] == [2, 3] and again[0]["steps"] == [32, 32]
 
 
 def test_gloo_world2_hybrid_validation():
@@ -340,6 +351,7 @@ def _worker_disagg_sharded(rank, world, port, q, overrides):
     if rank == 0:
         q.put({"steps": [m["num_trajectories"] for m in res["metrics"]], "pulls": res["sync"]["pulls"],
                "val": [m.get("val/num_samples") for m in res["metrics"]],
+               "step_ids": [m.get("step") for m in res["metrics"]],
                "pre": [m.get("fine_grain/precomputed") for m in res["metrics"]],
                "kl": [m.get("actor/reward_kl_penalty") for m in res["metrics"]],
                "chunks": [m.get("fine_grain/chunks") for m in res["metrics"]]})
@@ -538,6 +550,20 @@ def test_gloo_world3_disaggregated_interleaved_pipeline_trainer():
     res = _run_disagg(["++model.overrides.num_layers=4", "++actor.pipeline_parallel_size=2",
                        "++actor.virtual_pipeline_parallel_size=2"])
     assert res["steps"] == [32, 32] and res["pulls"] >= 2
+
+
+@pytest.mark.parametrize("layout", [[], ["++actor.pipeline_parallel_size=2"]])
+def test_gloo_world3_disaggregated_checkpoint_resume(tmp_path, layout):
+    """Checkpoints every step (each trainer rank its part, a pipeline stage its
+    own layers; rank 0 the data cursor and the marker), then a new run resumes
+    at the last step: the PS version and the step counter continue."""
+    d = str(tmp_path / "ckpt")
+    first = _run_disagg([f"trainer.default_local_dir={d}", "trainer.save_freq=1"] + layout)
+    assert first["step_ids"] == [0, 1]
+    from psrl_b200.utils.checkpoint import find_latest
+    assert find_latest(d) == 2
+    again = _run_disagg([f"trainer.default_local_dir={d}", "trainer.resume_mode=auto"] + layout)
+    assert again["step_ids"] == [2, 3] and again["steps"] == [32, 32]
 
 
 def test_gloo_world3_disaggregated_validation():
