@@ -359,6 +359,10 @@ class DisaggregatedRun:
                         "timing_s/gen_wait": t1 - t0, "timing_s/train": t2 - t1,
                         "timing_s/publish": time.perf_counter() - t2,
                         "timing_s/step": time.perf_counter() - t0})
+        from .perf import perf_metrics
+        metrics.update(perf_metrics(self.cfg, self.args, int(batch["trained_tokens"]),
+                                    int(batch["num_trajectories"]), metrics["timing_s/step"], t2 - t1,
+                                    self.world, self.n_train))
         sf = int(self.cfg.trainer.get("save_freq", -1) or -1)
         if sf > 0 and self.global_step % sf == 0:
             t3 = time.perf_counter()

@@ -303,6 +303,9 @@ class RLTrainer:
             "staleness/max": max((b - t.version_tag) for t in trajs) if trajs else 0,
         })
         metrics.update({f"rollout/{k}": v for k, v in self.engine.engine_stats().items() if isinstance(v, (int, float))})
+        from .perf import perf_metrics
+        metrics.update(perf_metrics(self.cfg, self.args, ntok, len(trajs), metrics["timing_s/step"],
+                                    float(metrics.get("timing_s/train", 0.0)), 1, 1))
         return metrics
 
     def fit(self, num_steps: int | None = None) -> list[dict]:

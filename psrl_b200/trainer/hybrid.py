@@ -419,6 +419,9 @@ class HybridRun:
             "fine_grain/precomputed": pre,
         })
         metrics.update({f"rollout/{k}": v for k, v in self.engine.engine_stats().items() if isinstance(v, (int, float))})
+        from .perf import perf_metrics
+        metrics.update(perf_metrics(self.cfg, self.args, int(batch["trained_tokens"]), int(batch["num_trajectories"]),
+                                    metrics["timing_s/step"], t2 - t1, self.world, self.world))
         sf = int(self.cfg.trainer.get("save_freq", -1) or -1)
         if sf > 0 and self.global_step % sf == 0:
             t3 = time.perf_counter()

@@ -1,0 +1,27 @@
+"""Per-step perf metrics under the reference's names."""
+
+import torch
+
+
+def test_perf_metrics_formula():
+    from psrl_b200.config import load_config
+    from psrl_b200.models import PRESETS
+    from psrl_b200.models.qwen import flops_per_token
+    from psrl_b200.trainer.perf import perf_metrics
+    cfg = load_config(preset="cpu_tiny_grpo", overrides=["++trainer.peak_tflops=1000"])
+    a = PRESETS["tiny"]
+    m = perf_metrics(cfg, a, tokens=8000, num_trajectories=8, step_s=2.0, train_s=1.0, n_gpus=4, n_train_gpus=2)
+    assert m["perf/throughput"] == 8000 / 2.0 / 4
+    assert abs(m["perf/mfu/actor"] - 3 * flops_per_token(a, 1000) * 8000 / (1.0 * 2 * 1e15)) < 1e-12
+    assert m["perf/total_num_tokens"] == 8000 and m["perf/time_per_step"] == 2.0
+
+
+def test_trainer_step_reports_perf():
+    torch.set_num_threads(2)
+    from psrl_b200.config import load_config
+    from psrl_b200.trainer import RLTrainer
+    t = RLTrainer(load_config(preset="cpu_tiny_grpo", overrides=["rollout.max_response_length=12"]))
+    m = t.step()
+    t.stop_rollout()
+    assert m["perf/throughput"] > 0 and m["perf/mfu/actor"] > 0
+    assert m["perf/total_num_tokens"] == m["trained_tokens"]
