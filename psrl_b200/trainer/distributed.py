@@ -606,6 +606,9 @@ def run_disaggregated(cfg, steps: int, warmup: int, info: pdist.DistInfo | None 
     (rank 0 also gets metrics, token counts and control-plane stats)."""
     info = info or pdist.init_distributed(cfg.trainer.get("device", "auto"))
     run = DisaggregatedRun(cfg, info)
+    if steps is None:
+        # trainer.total_training_steps counts from step 0 (a resumed run does the rest)
+        steps = max(0, int(cfg.trainer.total_training_steps) - int(getattr(run, "global_step", 0)))
     is_cuda = info.device.type == "cuda"
     t_evt = {}
 

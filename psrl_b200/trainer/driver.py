@@ -309,9 +309,11 @@ class RLTrainer:
         return metrics
 
     def fit(self, num_steps: int | None = None) -> list[dict]:
-        n = int(num_steps if num_steps is not None else self.cfg.trainer.total_training_steps)
         if self.cfg.trainer.resume_mode != "disable" and self.global_step == 0:
             self.resume()
+        # trainer.total_training_steps counts from step 0: a resumed run does the rest
+        n = int(num_steps) if num_steps is not None else \
+            max(0, int(self.cfg.trainer.total_training_steps) - self.global_step)
         out = []
         for _ in range(n):
             out.append(self.step())

@@ -453,6 +453,9 @@ def run_hybrid(cfg, steps: int, warmup: int, info: pdist.DistInfo | None = None,
     (max over ranks) and, on rank 0, metrics, token counts and control-plane stats."""
     info = info or pdist.init_distributed(cfg.trainer.get("device", "auto"))
     run = HybridRun(cfg, info)
+    if steps is None:
+        # trainer.total_training_steps counts from step 0 (a resumed run does the rest)
+        steps = max(0, int(cfg.trainer.total_training_steps) - int(getattr(run, "global_step", 0)))
     is_cuda = info.device.type == "cuda"
     if capture and is_cuda and run.engine.use_cuda_graph:
         run.engine.capture_all()

@@ -31,7 +31,9 @@ def main(argv=None) -> int:
     if args.print_config:
         print(cfg.to_yaml())
         return 0
-    steps = args.steps if args.steps is not None else int(cfg.trainer.total_training_steps)
+    # without --steps: trainer.total_training_steps counts from step 0, so a
+    # resumed run does only the steps still missing
+    steps = args.steps
     world = int(os.environ.get("WORLD_SIZE", 1))
     if world > 1:
         from ..parallel.dist import destroy, init_distributed
