@@ -164,6 +164,8 @@ class DisaggregatedRun:
         self.is_leader = self.eng_tp is None or self.rank == self.eng_leader
         self.trained_tokens = 0
         self.global_step = 0
+        from ..utils.events import rank_event_log
+        self.log = rank_event_log(cfg, self.rank, "trainer" if self.is_trainer else "rollout")
         self.liveness_s = float(cfg.trainer.get("liveness_timeout_s", 300))
         self.buffer_timeout_s = float(cfg.trainer.get("buffer_timeout_s", 1800))
         log(f"role split: {self.n_train} trainer rank(s), {self.world - self.n_train} rollout rank(s)")
@@ -363,6 +365,7 @@ class DisaggregatedRun:
         metrics.update(perf_metrics(self.cfg, self.args, int(batch["trained_tokens"]),
                                     int(batch["num_trajectories"]), metrics["timing_s/step"], t2 - t1,
                                     self.world, self.n_train))
+        _log_step_spans(self.log, b, t0, t1, t2, metrics)
         sf = int(self.cfg.trainer.get("save_freq", -1) or -1)
         if sf > 0 and self.global_step % sf == 0:
             t3 = time.perf_counter()
@@ -453,6 +456,8 @@ class DisaggregatedRun:
         self.engine.load_weights(None, v)
         self.cp.report_pull(time.perf_counter() - t0, self.instance_id, from_v, v,
                             0 if self.engine.keep_kv_on_update else in_flight, copy_s, int(nbytes))
+        self.log.record_span("PULL", time.time() - (time.perf_counter() - t0), time.perf_counter() - t0,
+                             version=int(v), bytes=int(nbytes))
 
     def _tp_pull(self) -> None:
         """A TP instance's pull: the leader takes the shared pull lock and the
@@ -599,6 +604,17 @@ class DisaggregatedRun:
             self.cp_proc.join(timeout=30)
             if self.cp_proc.is_alive():
                 self.cp_proc.terminate()
+
+
+def _log_step_spans(log, step: int, t0: float, t1: float, t2: float, metrics: dict) -> None:
+    """WAIT (generation wait), TRAIN and PUSH spans of one trainer step from its
+    perf_counter marks; VAL / checkpoint spans from their timing metrics."""
+    off = time.time() - time.perf_counter()
+    log.record_span("WAIT", t0 + off, t1 - t0, step=step)
+    log.record_span("TRAIN", t1 + off, t2 - t1, step=step)
+    log.record_span("PUSH", t2 + off, float(metrics.get("timing_s/publish", 0.0)), step=step)
+    if "timing_s/validate" in metrics:
+        log.record_span("VAL", time.time() - metrics["timing_s/validate"], metrics["timing_s/validate"], step=step)
 
 
 def run_disaggregated(cfg, steps: int, warmup: int, info: pdist.DistInfo | None = None):

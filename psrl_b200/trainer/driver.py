@@ -132,6 +132,9 @@ class RLTrainer:
         self.cfg = cfg
         self.device = torch.device(device) if device is not None else resolve_device(cfg)
         self.seed = int(cfg.trainer.seed if seed is None else seed)
+        if log is None and cfg.trainer.get("event_log_dir", None):
+            from ..utils.events import rank_event_log
+            log = rank_event_log(cfg, 0, "driver")
         self.log = log or EventLog()
         self.args = model_args_from_config(cfg.model)
         rn, alg_rn, _, _ = redundant_settings(cfg)

@@ -69,6 +69,8 @@ class HybridRun:
         self.args = model_args_from_config(cfg.model)
         self.trained_tokens = 0
         self.global_step = 0
+        from ..utils.events import rank_event_log
+        self.log = rank_event_log(cfg, self.rank, "hybrid")
         self.liveness_s = float(cfg.trainer.get("liveness_timeout_s", 300))
         self.buffer_timeout_s = float(cfg.trainer.get("buffer_timeout_s", 1800))
         self.cp_proc = None
@@ -263,6 +265,7 @@ class HybridRun:
         dt = time.perf_counter() - t0
         self.pulls += 1
         self.pull_s += dt
+        self.log.record_span("PULL", time.time() - dt, dt, version=int(v))
         if self.is_leader:
             self.cp_roll.report_pull(dt)
 
@@ -422,6 +425,8 @@ class HybridRun:
         from .perf import perf_metrics
         metrics.update(perf_metrics(self.cfg, self.args, int(batch["trained_tokens"]), int(batch["num_trajectories"]),
                                     metrics["timing_s/step"], t2 - t1, self.world, self.world))
+        from .distributed import _log_step_spans
+        _log_step_spans(self.log, b, t0, t1, t2, metrics)
         sf = int(self.cfg.trainer.get("save_freq", -1) or -1)
         if sf > 0 and self.global_step % sf == 0:
             t3 = time.perf_counter()

@@ -566,6 +566,26 @@ def test_gloo_world3_disaggregated_checkpoint_resume(tmp_path, layout):
     assert again["step_ids"] == [2, 3] and again["steps"] == [32, 32]
 
 
+def test_gloo_world3_disaggregated_event_logs(tmp_path):
+    """trainer.event_log_dir: every rank writes its begin / end spans (trainer
+    ranks WAIT / TRAIN / PUSH per step, the rollout rank its PULLs) for the
+    timeline viewer."""
+    import json
+    d = str(tmp_path / "events")
+    res = _run_disagg([f"++trainer.event_log_dir={d}"])
+    assert res["steps"] == [32, 32]
+    kinds = {}
+    for r in range(3):
+        with open(os.path.join(d, f"events_rank{r}.jsonl")) as fh:
+            evs = [json.loads(line) for line in fh]
+        kinds[r] = {e["type"] for e in evs if e.get("phase") == "end"}
+    assert {"WAIT", "TRAIN", "PUSH"} <= kinds[0] and {"WAIT", "TRAIN", "PUSH"} <= kinds[1], kinds
+    assert "PULL" in kinds[2], kinds
+    from psrl_b200.utils.visualize import spans
+    with open(os.path.join(d, "events_rank0.jsonl")) as fh:
+        assert len(spans([json.loads(line) for line in fh])) >= 6
+
+
 def test_gloo_world3_disaggregated_validation():
     """trainer.test_freq=1 in the disaggregated placement: after each step the
     rollout instance generates the validation prompts, which are scored and
