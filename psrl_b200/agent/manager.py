@@ -232,6 +232,25 @@ class AgentLoopManager:
         with self.lock:
             for o in outputs:
                 self._complete_one(o, instance_id)
+            turns = self._turn_records()
+            if turns is not None:
+                for o in outputs:
+                    turns.from_output(o)
+                if len(turns.data) >= 256:
+                    turns.flush()
+
+    def _turn_records(self):
+        """Per-request turn records (``trainer.turn_records_path``, JSON lines;
+        written in batches of 256 requests), or None."""
+        if not hasattr(self, "_turns"):
+            path = self.cfg.trainer.get("turn_records_path", None) if hasattr(self.cfg, "trainer") else None
+            from ..utils.profiling import TurnProfilingCollector
+            self._turns = TurnProfilingCollector(str(path)) if path else None
+        return self._turns
+
+    def flush_turn_records(self) -> int:
+        t = self._turn_records()
+        return t.flush() if t is not None else 0
 
     def _complete_one(self, o: RequestOutput, instance_id=None) -> None:
         rid = o.request_id

@@ -143,6 +143,7 @@ class ControlPlane:
         self.phase = int(p)
 
     def shutdown(self) -> None:
+        self.manager.flush_turn_records()
         self._done.set()
 
     # --------------------------------------------------------------- rollout

@@ -166,6 +166,8 @@ class DisaggregatedRun:
         self.global_step = 0
         from ..utils.events import rank_event_log
         self.log = rank_event_log(cfg, self.rank, "trainer" if self.is_trainer else "rollout")
+        from ..utils.profiling import StepObserver
+        self.obs = StepObserver(cfg, self.device, self.rank)
         self.liveness_s = float(cfg.trainer.get("liveness_timeout_s", 300))
         self.buffer_timeout_s = float(cfg.trainer.get("buffer_timeout_s", 1800))
         log(f"role split: {self.n_train} trainer rank(s), {self.world - self.n_train} rollout rank(s)")
@@ -301,6 +303,7 @@ class DisaggregatedRun:
 
     def trainer_step(self) -> dict:
         b = self.global_step
+        self.obs.begin(b)
         t0 = time.perf_counter()
         chunks = 0
         if self.sharded_overlap:
@@ -366,6 +369,7 @@ class DisaggregatedRun:
                                     int(batch["num_trajectories"]), metrics["timing_s/step"], t2 - t1,
                                     self.world, self.n_train))
         _log_step_spans(self.log, b, t0, t1, t2, metrics)
+        self.obs.end(b, metrics)
         sf = int(self.cfg.trainer.get("save_freq", -1) or -1)
         if sf > 0 and self.global_step % sf == 0:
             t3 = time.perf_counter()

@@ -286,6 +286,10 @@ class RLTrainer:
 
     def step(self) -> dict:
         b = self.global_step
+        if not hasattr(self, "obs"):
+            from ..utils.profiling import StepObserver
+            self.obs = StepObserver(self.cfg, self.device, 0)
+        self.obs.begin(b)
         metrics: dict = {}
         t0 = time.perf_counter()
         with train_stream_ctx(self.train_stream):
@@ -309,6 +313,7 @@ class RLTrainer:
         from .perf import perf_metrics
         metrics.update(perf_metrics(self.cfg, self.args, ntok, len(trajs), metrics["timing_s/step"],
                                     float(metrics.get("timing_s/train", 0.0)), 1, 1))
+        self.obs.end(b, metrics)
         return metrics
 
     def fit(self, num_steps: int | None = None) -> list[dict]:
@@ -326,6 +331,7 @@ class RLTrainer:
             tf = int(self.cfg.trainer.get("test_freq", -1))
             if tf > 0 and self.global_step % tf == 0:
                 out[-1].update(self.validate())
+        self.manager.flush_turn_records()
         return out
 
     # --------------------------------------------------------- validation

@@ -71,6 +71,8 @@ class HybridRun:
         self.global_step = 0
         from ..utils.events import rank_event_log
         self.log = rank_event_log(cfg, self.rank, "hybrid")
+        from ..utils.profiling import StepObserver
+        self.obs = StepObserver(cfg, self.device, self.rank)
         self.liveness_s = float(cfg.trainer.get("liveness_timeout_s", 300))
         self.buffer_timeout_s = float(cfg.trainer.get("buffer_timeout_s", 1800))
         self.cp_proc = None
@@ -361,6 +363,7 @@ class HybridRun:
     # -------------------------------------------------------------- training
     def step(self) -> dict:
         b = self.global_step
+        self.obs.begin(b)
         if self._rollout_error is not None:
             raise RuntimeError("rollout thread failed") from self._rollout_error
         self.start_rollout()
@@ -427,6 +430,7 @@ class HybridRun:
                                     metrics["timing_s/step"], t2 - t1, self.world, self.world))
         from .distributed import _log_step_spans
         _log_step_spans(self.log, b, t0, t1, t2, metrics)
+        self.obs.end(b, metrics)
         sf = int(self.cfg.trainer.get("save_freq", -1) or -1)
         if sf > 0 and self.global_step % sf == 0:
             t3 = time.perf_counter()

@@ -148,3 +148,32 @@ class ProfilerWindow:
         self.prof.export_chrome_trace(path)
         self.prof = None
         return path
+
+
+class StepObserver:
+    """What every trainer step records besides its own metrics: allocator
+    statistics on CUDA (``memory/allocated_gb``, ``memory/reserved_gb``,
+    ``memory/max_allocated_gb``) and, for the steps listed in
+    ``trainer.profile_steps``, a torch-profiler trace under
+    ``trainer.profile_dir/rank{r}`` (the reference's ``global_profiler.steps``)."""
+
+    def __init__(self, cfg, device, rank: int = 0):
+        steps = list(cfg.trainer.get("profile_steps", None) or [])
+        out = os.path.join(str(cfg.trainer.get("profile_dir", "torch_traces")), f"rank{rank}")
+        self.window = ProfilerWindow(steps, out) if steps else None
+        dev = torch.device(device)
+        self.mem = MemoryLogger(dev) if dev.type == "cuda" else None
+
+    def begin(self, step: int) -> None:
+        if self.window is not None:
+            self.window.start(step)
+
+    def end(self, step: int, metrics: dict) -> None:
+        if self.window is not None:
+            path = self.window.stop(step)
+            if path:
+                metrics["profile/trace"] = path
+        if self.mem is not None:
+            r = self.mem.snapshot(f"step{step}")
+            metrics.update({"memory/allocated_gb": r["allocated_gb"], "memory/reserved_gb": r["reserved_gb"],
+                            "memory/max_allocated_gb": r["max_allocated_gb"]})

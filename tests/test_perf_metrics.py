@@ -25,3 +25,24 @@ def test_trainer_step_reports_perf():
     t.stop_rollout()
     assert m["perf/throughput"] > 0 and m["perf/mfu/actor"] > 0
     assert m["perf/total_num_tokens"] == m["trained_tokens"]
+
+
+def test_profiler_window_and_turn_records(tmp_path):
+    """trainer.profile_steps writes a torch-profiler trace for those steps only;
+    trainer.turn_records_path gets one JSON line per finished request."""
+    import json
+    import os
+    torch.set_num_threads(2)
+    from psrl_b200.config import load_config
+    from psrl_b200.trainer import RLTrainer
+    turns = str(tmp_path / "turns.jsonl")
+    cfg = load_config(preset="cpu_tiny_grpo", overrides=[
+        "rollout.max_response_length=12", "++trainer.profile_steps=[1]", f"++trainer.profile_dir={tmp_path}/tr",
+        f"++trainer.turn_records_path={turns}"])
+    t = RLTrainer(cfg)
+    out = t.fit(2)
+    t.stop_rollout()
+    assert "profile/trace" not in out[0] and os.path.exists(out[1]["profile/trace"])
+    with open(turns) as fh:
+        recs = [json.loads(line) for line in fh]
+    assert len(recs) >= 32 and all("turns" in r for r in recs)
