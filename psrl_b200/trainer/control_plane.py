@@ -81,6 +81,14 @@ class ControlPlane:
         self._val_round = 0
         # resume (trainer.resume_mode): data cursor and PS version of the latest
         # checkpoint, set before any instance takes work
+        # engine statistics as JSON lines (trainer.engine_stats_path), at most one
+        # snapshot per instance per trainer.engine_stats_interval_s
+        self._stats_rec = None
+        if cfg.trainer.get("engine_stats_path", None):
+            from ..rollout.stats import StatsRecorder
+            self._stats_rec = StatsRecorder(str(cfg.trainer.engine_stats_path))
+        self._stats_every = float(cfg.trainer.get("engine_stats_interval_s", 1.0) or 1.0)
+        self._stats_last: dict = {}
         self._resumed = None
         if str(cfg.trainer.get("resume_mode", "disable")) != "disable":
             import torch as _torch
@@ -166,6 +174,13 @@ class ControlPlane:
         if outputs:
             self.manager.on_complete(outputs, iid)
         sync = self._coordinate(iid, int(version), state, now)
+        if self._stats_rec is not None and state and now - self._stats_last.get(iid, -1e9) >= self._stats_every:
+            self._stats_last[iid] = now
+            self._stats_rec.record({"instance_id": list(iid), "version": int(version), "ts": time.time(),
+                                    "num_running": int(state.get("running", 0)),
+                                    "num_waiting": int(state.get("waiting", 0)),
+                                    "kv_usage": float(state.get("kv_usage", 0.0)),
+                                    "gen_throughput": float(state.get("throughput", 0.0))})
         quarantined = iid in self.coord.quarantined
         reqs = []
         if free_slots > 0 and not quarantined and self._val_queue:

@@ -314,6 +314,12 @@ class RLTrainer:
         metrics.update(perf_metrics(self.cfg, self.args, ntok, len(trajs), metrics["timing_s/step"],
                                     float(metrics.get("timing_s/train", 0.0)), 1, 1))
         self.obs.end(b, metrics)
+        path = self.cfg.trainer.get("engine_stats_path", None)
+        if path:
+            from ..rollout.stats import EngineStats, StatsRecorder, ThroughputWindow
+            if not hasattr(self, "_stats_rec"):
+                self._stats_rec, self._stats_win = StatsRecorder(str(path)), ThroughputWindow()
+            self._stats_rec.record(EngineStats.from_engine(self.instance_id, self.engine, self._stats_win))
         return metrics
 
     def fit(self, num_steps: int | None = None) -> list[dict]:

@@ -569,10 +569,13 @@ def test_gloo_world3_disaggregated_checkpoint_resume(tmp_path, layout):
 def test_gloo_world3_disaggregated_event_logs(tmp_path):
     """trainer.event_log_dir: every rank writes its begin / end spans (trainer
     ranks WAIT / TRAIN / PUSH per step, the rollout rank its PULLs) for the
-    timeline viewer."""
+    timeline viewer; trainer.engine_stats_path: the control plane records the
+    instances' engine snapshots."""
     import json
     d = str(tmp_path / "events")
-    res = _run_disagg([f"++trainer.event_log_dir={d}"])
+    stats = str(tmp_path / "engine_stats.jsonl")
+    res = _run_disagg([f"++trainer.event_log_dir={d}", f"++trainer.engine_stats_path={stats}",
+                       "++trainer.engine_stats_interval_s=0.05"])
     assert res["steps"] == [32, 32]
     kinds = {}
     for r in range(3):
@@ -584,6 +587,10 @@ def test_gloo_world3_disaggregated_event_logs(tmp_path):
     from psrl_b200.utils.visualize import spans
     with open(os.path.join(d, "events_rank0.jsonl")) as fh:
         assert len(spans([json.loads(line) for line in fh])) >= 6
+    # the control plane's engine snapshots of the rollout instance
+    from psrl_b200.rollout.stats import StatsRecorder
+    recs = StatsRecorder(stats).read()
+    assert recs and all(r["instance_id"] == [0, 0] for r in recs)
 
 
 def test_gloo_world3_disaggregated_validation():

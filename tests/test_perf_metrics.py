@@ -46,3 +46,19 @@ def test_profiler_window_and_turn_records(tmp_path):
     with open(turns) as fh:
         recs = [json.loads(line) for line in fh]
     assert len(recs) >= 32 and all("turns" in r for r in recs)
+
+
+def test_engine_stats_recorded(tmp_path):
+    """trainer.engine_stats_path: one engine snapshot per step (one-process
+    trainer), readable back through StatsRecorder."""
+    torch.set_num_threads(2)
+    from psrl_b200.config import load_config
+    from psrl_b200.rollout.stats import StatsRecorder
+    from psrl_b200.trainer import RLTrainer
+    path = str(tmp_path / "stats.jsonl")
+    t = RLTrainer(load_config(preset="cpu_tiny_grpo", overrides=["rollout.max_response_length=12",
+                                                                 f"++trainer.engine_stats_path={path}"]))
+    t.fit(2)
+    t.stop_rollout()
+    recs = StatsRecorder(path).read()
+    assert len(recs) == 2 and all("kv_usage" in r and "num_running" in r for r in recs)
