@@ -569,8 +569,14 @@ class DisaggregatedRun:
         self.mailbox = mb = ExchangeMailbox(self.cp, self.instance_id, eng)
         seen = 0
         idle_s = 0.0
+        # host-side fault injection for failure-detection tests: this rollout
+        # rank leaves abruptly (no exception, no goodbye) after that many seconds
+        exit_after = float(self.cfg.trainer.get("inject_rollout_exit_after_s", 0) or 0)
+        t_enter = time.monotonic()
         try:
             while True:
+                if exit_after > 0 and time.monotonic() - t_enter > exit_after:
+                    os._exit(3)
                 reqs, aborts = mb.collect()
                 for r in reqs:
                     eng.add_request(r)
