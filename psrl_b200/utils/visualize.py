@@ -59,10 +59,22 @@ def render(events: list[dict], title: str = "psrl_b200 timeline") -> str:
 
 
 def main(argv=None) -> int:
+    """``visualize SRC... OUT.html``: SRC is an events file (JSON lines) or a
+    directory of them (one per rank, as ``trainer.event_log_dir`` writes); all
+    ranks' spans go on one timeline."""
+    import os
     argv = argv if argv is not None else sys.argv[1:]
-    src, dst = argv[0], argv[1]
-    with open(src) as fh:
-        events = [json.loads(ln) for ln in fh if ln.strip()]
+    *srcs, dst = argv
+    files = []
+    for src in srcs:
+        if os.path.isdir(src):
+            files += sorted(os.path.join(src, f) for f in os.listdir(src) if f.endswith(".jsonl"))
+        else:
+            files.append(src)
+    events = []
+    for f in files:
+        with open(f) as fh:
+            events += [json.loads(ln) for ln in fh if ln.strip()]
     with open(dst, "w") as fh:
         fh.write(render(events))
     return 0

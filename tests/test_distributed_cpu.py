@@ -584,9 +584,14 @@ def test_gloo_world3_disaggregated_event_logs(tmp_path):
         kinds[r] = {e["type"] for e in evs if e.get("phase") == "end"}
     assert {"WAIT", "TRAIN", "PUSH"} <= kinds[0] and {"WAIT", "TRAIN", "PUSH"} <= kinds[1], kinds
     assert "PULL" in kinds[2], kinds
-    from psrl_b200.utils.visualize import spans
+    from psrl_b200.utils.visualize import main as render_timeline, spans
     with open(os.path.join(d, "events_rank0.jsonl")) as fh:
         assert len(spans([json.loads(line) for line in fh])) >= 6
+    html = str(tmp_path / "timeline.html")
+    assert render_timeline([d, html]) == 0
+    with open(html) as fh:
+        page = fh.read()
+    assert "trainer0" in page and "rollout2" in page
     # the control plane's engine snapshots of the rollout instance
     from psrl_b200.rollout.stats import StatsRecorder
     recs = StatsRecorder(stats).read()
