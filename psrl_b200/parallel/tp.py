@@ -247,6 +247,22 @@ def apply_tensor_parallel(model, tp: TPGroup) -> list[str]:
 
 
 @torch.no_grad()
+def engine_slices(name: str, shape: tuple, args, r: int, P: int) -> list[tuple[int, int, int]]:
+    """(dim, start, length) pieces of the full tensor that make TP engine rank
+    ``r``'s tensor, in :func:`shard_engine_tensors`'s layout: the trainer's TP
+    layout (``models.converters.tp_slices``) for attention and the (shared)
+    MLP, whole experts [r E/P, (r+1) E/P) for MoE, embeddings and everything
+    else replicated."""
+    from ..models.converters import tp_slices
+    if name.endswith("experts_w13") or name.endswith("experts_w2"):
+        per = shape[0] // P
+        return [(0, r * per, per)]
+    if name.endswith(("attn.qkv.weight", "attn.qkv.bias", "attn.o.weight", "mlp.gate_up.weight", "mlp.down.weight",
+                      "mlp.shared_gate_up.weight", "mlp.shared_down.weight")):
+        return tp_slices(name, shape, args, r, P)
+    return [(0, 0, shape[0])]
+
+
 def shard_engine_tensors(args, tensors: dict, tp: TPGroup) -> dict:
     """This TP rank's shard of full engine tensors (``layers.{i}.attn.qkv.weight``
     and so on), in the layout the TP trainer's shards and a TP rollout engine

@@ -239,6 +239,11 @@ class ShardedWeightPuller:
                 blocks.append((j, soff * esz, dst0, 1, n * esz, 0, 0))
             else:
                 raise KeyError(f"no trainer store holds {name}")
+        self._set_blocks(blocks)
+
+    def _set_blocks(self, blocks: list) -> None:
+        """Merge contiguous one-row blocks, check alignment and build the
+        device table of the copy kernel."""
         # merge contiguous one-row blocks (same store, adjacent on both sides)
         merged = []
         for b in blocks:
@@ -258,8 +263,8 @@ class ShardedWeightPuller:
             start = torch.zeros(len(merged) + 1, dtype=torch.int64)
             start[1:] = torch.tensor([rows * (rb // 16) for _, _, _, rows, rb, _, _ in merged],
                                      dtype=torch.int64).cumsum(0)
-            self.table = tab.to(dst_flat.device)
-            self.start = start.to(dst_flat.device)
+            self.table = tab.to(self.dst.device)
+            self.start = start.to(self.dst.device)
 
     @torch.no_grad()
     def pull(self) -> int:
@@ -274,3 +279,76 @@ class ShardedWeightPuller:
                 else:
                     dst.as_strided((rows, rb), (ds, 1), d).copy_(src.as_strided((rows, rb), (ss, 1), s))
         return sum(rows * rb for _, _, _, rows, rb, _, _ in self.blocks)
+
+
+class EngineShardPuller(ShardedWeightPuller):
+    """A tensor-parallel rollout rank's pull from whole-tensor trainer stores
+    (data-parallel trainers): only this rank's slices of every tensor
+    (``parallel.tp.engine_slices``: heads, MLP width, whole experts, the KV head
+    it reads when there are more ranks than KV heads; replicated tensors whole)
+    are copied, straight into the engine's shard tensors, in one kernel on
+    CUDA.  ``tensors`` maps each name to its view of the shard flat buffer."""
+
+    def __init__(self, layout: WeightLayout, descriptors: list[dict], args, tp_rank: int, tp_world: int,
+                 device=None):
+        from ..parallel.tp import engine_slices
+        from .comm_plan import least_loaded
+        esz = torch.finfo(layout.dtype).bits // 8
+        pieces, local, total = {}, {}, 0
+        for name, shape, _ in layout.entries:
+            sl = engine_slices(name, tuple(shape), args, tp_rank, tp_world)
+            lshape = list(shape)
+            lshape[sl[0][0]] = sum(x[2] for x in sl)
+            pieces[name], local[name] = sl, (tuple(lshape), total)
+            n = 1
+            for x in lshape:
+                n *= x
+            total += -(-n * esz // 16) * 16 // esz          # every shard starts on 16 bytes
+        self.layout = layout
+        self.srcs = [open_store(d) for d in descriptors]
+        self.dst = torch.empty(total, dtype=layout.dtype,
+                               device=device if device is not None else self._device_for(descriptors))
+        self.gpu = self.dst.is_cuda
+        if self.gpu:
+            me = self.dst.device.index
+            for d in descriptors:
+                if d["kind"] == "ipc" and int(d["device"]) != me:
+                    ops.ext().enable_peer_access(int(d["device"]))
+        self.tensors = {}
+        for name, (lshape, off) in local.items():
+            n = 1
+            for x in lshape:
+                n *= x
+            self.tensors[name] = self.dst[off:off + n].view(lshape)
+        link = {j: ("self" if d.get("device") == (self.dst.device.index if self.gpu else None) else "nvlink")
+                for j, d in enumerate(descriptors)}
+        load: dict[int, int] = {}
+        blocks = []
+        for name, shape, off in layout.entries:
+            full = tuple(shape)
+            lshape, loff = local[name]
+            acc = 0
+            for dim, start, length in pieces[name]:
+                inner = 1
+                for x in full[dim + 1:]:
+                    inner *= x
+                outer = 1
+                for x in full[:dim]:
+                    outer *= x
+                nbytes = outer * length * inner * esz
+                j = least_loaded(list(range(len(descriptors))), load, link)
+                load[j] = load.get(j, 0) + nbytes
+                src, dst = (int(off) + start * inner) * esz, (loff + acc * inner) * esz
+                if outer == 1:
+                    blocks.append((j, src, dst, 1, length * inner * esz, 0, 0))
+                else:
+                    blocks.append((j, src, dst, outer, length * inner * esz, full[dim] * inner * esz,
+                                   lshape[dim] * inner * esz))
+                acc += length
+        self._set_blocks(blocks)
+
+    @staticmethod
+    def _device_for(descriptors):
+        if torch.cuda.is_available() and any(d.get("kind") == "ipc" for d in descriptors):
+            return torch.device("cuda", torch.cuda.current_device())
+        return torch.device("cpu")

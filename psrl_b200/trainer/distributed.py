@@ -392,22 +392,38 @@ class DisaggregatedRun:
         layout, descs = self.cp.get_stores()
         self.layout = layout
         dtype = layout.dtype
-        flat = torch.empty(layout.total, dtype=dtype, device=self.device)
+        shard_mode = self.eng_tp is not None and not any("entries" in d for d in descs)
+        # (a TP rank pulling its shards directly needs no full-model buffer)
+        flat = torch.empty(layout.total if not shard_mode else 0, dtype=dtype, device=self.device)
         w = EngineWeights(a, self.device, dtype)
         w.flat = flat
-        w.tensors = layout.views(flat)
+        w.tensors = layout.views(flat) if not shard_mode else {}
         if a.is_moe:
             prior = zipf_prior(a.num_experts, a.router_zipf_alpha) if a.router_zipf_alpha > 0 \
                 else torch.zeros(a.num_experts)
             for i in range(a.num_layers):
                 w.tensors[f"layers.{i}.mlp.router_prior"] = prior.to(self.device)
         self.weights = w
-        self.puller = ShardedWeightPuller(layout, descs, flat, a) if any("entries" in d for d in descs) \
-            else WeightPuller(layout, descs, flat)
-        if self.eng_tp is not None:
-            # every TP rank pulls the full model, then keeps its own shard of the
-            # column / row-parallel tensors (persistent copies, refreshed after each
-            # pull; replicated tensors stay views of the pulled buffer)
+        self.shard_pull = False
+        if not shard_mode:
+            self.puller = ShardedWeightPuller(layout, descs, flat, a) if any("entries" in d for d in descs) \
+                else WeightPuller(layout, descs, flat)
+        if shard_mode:
+            # whole-tensor trainer stores (data-parallel trainers): each TP rank
+            # copies only its own slices, straight into its shard buffers
+            from ..parallel.weight_sync import EngineShardPuller
+            self.puller = EngineShardPuller(layout, descs, a, self.eng_tp.rank, self.eng_tp.world, self.device)
+            ew = EngineWeights(a, self.device, dtype)
+            ew.tensors = dict(self.puller.tensors)
+            if a.is_moe:
+                for i in range(a.num_layers):
+                    ew.tensors[f"layers.{i}.mlp.router_prior"] = w.tensors[f"layers.{i}.mlp.router_prior"]
+            self.shard_pull = True
+            w = ew
+        elif self.eng_tp is not None:
+            # sharded trainer stores: every TP rank pulls the full model, then keeps
+            # its own shard of the column / row-parallel tensors (persistent copies,
+            # refreshed after each pull; replicated tensors stay views of the pulled buffer)
             from ..parallel.tp import shard_engine_tensors
             self.full_tensors = w.tensors
             ew = EngineWeights(a, self.device, dtype)
@@ -479,10 +495,11 @@ class DisaggregatedRun:
             raise TimeoutError("shared pull lock")
         try:
             nbytes = self.puller.pull()
-            from ..parallel.tp import shard_engine_tensors
-            fresh = shard_engine_tensors(self.args, self.full_tensors, self.eng_tp)
-            for n in self.sharded_names:
-                self.weights_tp[n].copy_(fresh[n])
+            if not self.shard_pull:
+                from ..parallel.tp import shard_engine_tensors
+                fresh = shard_engine_tensors(self.args, self.full_tensors, self.eng_tp)
+                for n in self.sharded_names:
+                    self.weights_tp[n].copy_(fresh[n])
             if self.device.type == "cuda":
                 torch.cuda.current_stream().synchronize()
             dist.barrier(group=self.eng_tp_cpu)

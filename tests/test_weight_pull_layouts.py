@@ -123,3 +123,28 @@ def test_tensor_parallel_pull_kernel_gpu():
     for name, t in full.items():
         torch.testing.assert_close(views[name], t.detach(), rtol=0, atol=0)
     assert n >= sum(t.numel() * 2 for t in full.values())
+
+
+@pytest.mark.parametrize("preset,P", [("tiny", 2), ("tiny", 4), ("tiny-moe", 2)])
+def test_engine_shard_pull_from_whole_tensor_stores(preset, P):
+    """A TP rollout rank's direct shard pull from data-parallel trainer stores
+    equals slicing the full model (shard_engine_tensors), for every rank, also
+    with more ranks than KV heads and with experts split by expert."""
+    from psrl_b200.models import PRESETS, build_model
+    from psrl_b200.parallel.tp import TPGroup, shard_engine_tensors
+    from psrl_b200.parallel.weight_sync import EngineShardPuller
+    a = PRESETS[preset]
+    m = build_model(a, "cpu", torch.float32, seed=3)
+    full = {n: p.detach() for n, p in m.named_parameters()}
+    lay = _full_layout(a)
+    flat = torch.zeros(lay.total)
+    views = lay.views(flat)
+    for n, t in full.items():
+        views[n].copy_(t)
+    stores = [{"kind": "shm", "tensor": flat}, {"kind": "shm", "tensor": flat.clone()}]
+    for r in range(P):
+        pl = EngineShardPuller(lay, stores, a, r, P)
+        pl.pull()
+        want = shard_engine_tensors(a, full, TPGroup(None, P, r))
+        for n, t in want.items():
+            torch.testing.assert_close(pl.tensors[n], t, rtol=0, atol=0)
