@@ -283,7 +283,9 @@ class ShardedWeightPuller:
 
 class EngineShardPuller(ShardedWeightPuller):
     """A tensor-parallel rollout rank's pull from whole-tensor trainer stores
-    (data-parallel trainers): only this rank's slices of every tensor
+    (data-parallel trainers), or from the stores of a dense tensor-parallel
+    trainer of the same TP size (whole shards of the same rank): only this
+    rank's slices of every tensor
     (``parallel.tp.engine_slices``: heads, MLP width, whole experts, the KV head
     it reads when there are more ranks than KV heads; replicated tensors whole)
     are copied, straight into the engine's shard tensors, in one kernel on
@@ -324,6 +326,29 @@ class EngineShardPuller(ShardedWeightPuller):
                 for j, d in enumerate(descriptors)}
         load: dict[int, int] = {}
         blocks = []
+        if any("entries" in d for d in descriptors):
+            # tensor-parallel trainer stores of the same TP size (dense model):
+            # engine rank r's shard of every tensor is trainer rank r's, copied whole;
+            # replicated tensors come from the least-loaded store
+            from .assemble import engine_name
+            held: dict[str, list] = {}
+            for j, d in enumerate(descriptors):
+                for nm, shp, o in d["entries"]:
+                    held.setdefault(engine_name(nm), []).append((j, int(d.get("tp_rank", 0)), tuple(shp), int(o)))
+            for name, shape, _ in layout.entries:
+                lshape, loff = local[name]
+                n = 1
+                for x in lshape:
+                    n *= x
+                cands = [c for c in held.get(name, []) if c[2] == lshape and (c[2] == tuple(shape) or c[1] == tp_rank)]
+                if not cands:
+                    raise KeyError(f"no trainer store holds rank {tp_rank}'s {name} {lshape}")
+                j = least_loaded([c[0] for c in cands], load, link)
+                load[j] = load.get(j, 0) + n * esz
+                o = next(c[3] for c in cands if c[0] == j)
+                blocks.append((j, o * esz, loff * esz, 1, n * esz, 0, 0))
+            self._set_blocks(blocks)
+            return
         for name, shape, off in layout.entries:
             full = tuple(shape)
             lshape, loff = local[name]

@@ -392,7 +392,11 @@ class DisaggregatedRun:
         layout, descs = self.cp.get_stores()
         self.layout = layout
         dtype = layout.dtype
-        shard_mode = self.eng_tp is not None and not any("entries" in d for d in descs)
+        # a TP instance pulls its shards directly from whole-tensor stores, or from a
+        # dense TP trainer's stores of the same TP size (rank r's shards whole)
+        same_tp = self.eng_tp is not None and not a.is_moe and bool(descs) and \
+            all(int(d.get("tp_world", 1)) == self.eng_tp.world for d in descs)
+        shard_mode = self.eng_tp is not None and (not any("entries" in d for d in descs) or same_tp)
         # (a TP rank pulling its shards directly needs no full-model buffer)
         flat = torch.empty(layout.total if not shard_mode else 0, dtype=dtype, device=self.device)
         w = EngineWeights(a, self.device, dtype)

@@ -148,3 +148,32 @@ def test_engine_shard_pull_from_whole_tensor_stores(preset, P):
         want = shard_engine_tensors(a, full, TPGroup(None, P, r))
         for n, t in want.items():
             torch.testing.assert_close(pl.tensors[n], t, rtol=0, atol=0)
+
+
+def test_engine_shard_pull_from_same_size_tp_stores():
+    """Trainer TP=2 stores (local names, own shards) feed a TP=2 engine rank
+    directly: rank r copies trainer rank r's shards whole."""
+    from psrl_b200.models import PRESETS, build_model
+    from psrl_b200.models.converters import shard_tensor
+    from psrl_b200.parallel.assemble import _TP_NAMES
+    from psrl_b200.parallel.tp import TPGroup, shard_engine_tensors
+    from psrl_b200.parallel.weight_sync import EngineShardPuller
+    a = PRESETS["tiny"]
+    P = 2
+    full = {n: p.detach() for n, p in build_model(a, "cpu", torch.float32, seed=4).named_parameters()}
+    inv = {v: k for k, v in _TP_NAMES.items()}
+    stores = []
+    for r in range(P):
+        items = []
+        for n, t in full.items():
+            suffix = next((k for k in inv if n.endswith(k)), None)
+            items.append((n[: -len(suffix)] + inv[suffix], shard_tensor(t, n, a, r, P)) if suffix else (n, t))
+        d = _store(items)
+        d.update(tp_rank=r, tp_world=P)
+        stores.append(d)
+    lay = _full_layout(a)
+    for r in range(P):
+        pl = EngineShardPuller(lay, stores, a, r, P)
+        pl.pull()
+        for n, t in shard_engine_tensors(a, full, TPGroup(None, P, r)).items():
+            torch.testing.assert_close(pl.tensors[n], t, rtol=0, atol=0)
